@@ -1,0 +1,432 @@
+#!/usr/bin/env python
+"""Q4_K decode-matvec HBM throughput on B200 (BASELINE.json metric).
+
+Workload (the Q4_K leg of the per-format sweep):
+batch-1 matvecs y = W x with W a random Q4_K matrix of shape (rows x K)
+4096x4096, 14336x4096 and 4096x14336, x ~ N(0,1) f32 quantized to Q8_K. One
+step streams every weight copy of every shape once: each shape rotates
+through distinct device copies totalling >= 4x the L2 size, so no step reads
+weights from L2.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Under torchrun each rank runs the same sweep on its own GPU (independent
+replicas, weak scaling; there is no data-path collective). Rank 0 prints one
+JSON line. value = algorithmic bytes of all ranks' steps / max-over-ranks
+device time. e2e = the same metric through sicu_gemv_host, the call shape of
+the reference's backend gemv slot: pinned host x in, host y out, per matvec.
+--impl reference times the reference's own CPU matvec (si_backend_cpu()->gemv,
+AVX2, all host threads) on host copies of the same sweep.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+from siphon_b200 import quant as Q  # noqa: E402
+from siphon_b200 import synth  # noqa: E402
+
+METRIC = "Q4_K matvec HBM GB/s (% of peak)"
+UNIT = "GB/s"
+SHAPES = [(4096, 4096), (14336, 4096), (4096, 14336)]   # rows x K
+WTYPE = Q.Q4_K
+PEAKS = ROOT / "MEASURED_PEAKS.json"
+FALLBACK_HBM = 6650.0
+# DRAM bytes per launch from the ncu capture summarised in
+# profiles/gemv_q4k_launches.md (null until a capture exists)
+NCU_TRAFFIC = {}
+
+
+def peak_hbm() -> tuple[float, str]:
+    try:
+        return float(json.loads(PEAKS.read_text())["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM, "fallback"
+
+
+def workload_config(copies: dict | None, extra: dict | None = None) -> dict:
+    cfg = {
+        "workload": "configs[1] Q4_K matvec sweep: 4096x4096, 14336x4096, 4096x14336 (rows x K), batch 1, "
+                    "f32 activation quantized to Q8_K inside the matvec kernel",
+        "weights": "seeded random Q4_K blocks (f16 d,dmin U[1e-4,1e-2]; other bits uniform); x ~ N(0,1)",
+        "l2": "inputs larger than L2: each shape rotates through distinct weight copies totalling >= 4x L2",
+        "parallelism": "replicas",
+    }
+    if copies:
+        cfg["copies_per_shape"] = copies
+    if extra:
+        cfg.update(extra)
+    return cfg
+
+
+# ---- clocks during the timed region -------------------------------------------------
+class ClockSampler:
+    """Polls NVML for SM clock and throttle reasons on a background thread."""
+
+    REASONS = {0x8: "hw_slowdown", 0x40: "hw_thermal_slowdown", 0x20: "sw_thermal_slowdown",
+               0x4: "sw_power_cap", 0x80: "hw_power_brake_slowdown"}
+
+    def __init__(self, device: int):
+        self.samples: list[int] = []
+        self.reasons: int = 0
+        self.ok = False
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(device)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception:
+            self.max_mhz = None
+        self._stop = threading.Event()
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+                self.reasons |= self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+            except Exception:
+                pass
+            time.sleep(0.0005)
+
+    def __enter__(self):
+        if self.ok:
+            self.t = threading.Thread(target=self._run, daemon=True)
+            self.t.start()
+        return self
+
+    def __exit__(self, *a):
+        if self.ok:
+            self._stop.set()
+            self.t.join()
+
+    def summary(self) -> dict:
+        if not self.ok:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvml unavailable"]}
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
+                "sm_max_mhz": self.max_mhz, "samples": len(self.samples),
+                "reasons": [n for bit, n in self.REASONS.items() if self.reasons & bit]}
+
+
+# ---- distributed plumbing ----------------------------------------------------------------
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def max_over_ranks(v: float, world: int, device) -> float:
+    if world == 1:
+        return v
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world: int):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+# ---- the reference's CPU matvec ------------------------------------------------------------
+def cpu_sweep_setup(copies: dict):
+    """Host copies of the sweep for the reference's CPU gemv."""
+    mats = []
+    for (n_out, n_in) in SHAPES:
+        w = synth.weights(WTYPE, n_out, n_in, seed=n_out + n_in)
+        x = synth.activations(n_in, 1, seed=7)[0]
+        c = copies[f"{n_out}x{n_in}"]
+        mats.append((n_out, n_in, [w] + [w.copy() for _ in range(c - 1)], x, np.zeros(n_out, np.float32)))
+    return mats
+
+
+def cpu_run_pass(gemv, mats) -> int:
+    done = 0
+    for n_out, n_in, ws, x, y in mats:
+        for w in ws:
+            gemv(gemv.tensor(WTYPE, w, n_in, n_out), x, y)
+            done += Q.matvec_bytes(WTYPE, n_out, n_in)
+    return done
+
+
+def cpu_gemv_handle():
+    from oracle.oracle import RefCpuGemv, Reference, have_reference
+    threads = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+    if have_reference():
+        return RefCpuGemv(Reference(), threads), "reference", threads
+    return None, "port", 1
+
+
+def cpu_baseline(copies: dict, budget_s: float = 12.0) -> dict:
+    """The reference's AVX2 matvec on the host cores over a bounded sample of
+    the sweep (whole passes until ~budget_s)."""
+    gemv, kind, threads = cpu_gemv_handle()
+    if gemv is None:
+        return port_baseline(budget_s)
+    mats = cpu_sweep_setup(copies)
+    cpu_run_pass(gemv, mats)   # warm
+    t0 = time.perf_counter()
+    nbytes = 0
+    passes = 0
+    while True:
+        nbytes += cpu_run_pass(gemv, mats)
+        passes += 1
+        if time.perf_counter() - t0 > budget_s:
+            break
+    dt = time.perf_counter() - t0
+    gemv.close()
+    return {"value": round(nbytes / dt / 1e9, 3), "unit": UNIT, "cores": threads, "kind": kind,
+            "sample": f"{passes} pass(es) over the sweep ({sum(copies.values())} matvecs each), "
+                      f"si_backend_cpu()->gemv ({'AVX2' if kind == 'reference' else 'scalar'}), {threads} threads, "
+                      f"{dt:.1f} s", "cpu": cpu_model()}
+
+
+def port_baseline(budget_s: float) -> dict:
+    from oracle.oracle import Oracle
+    o = Oracle()
+    n_out, n_in = SHAPES[0]
+    w = synth.weights(WTYPE, n_out, n_in, seed=1)
+    x = synth.activations(n_in, 1, seed=7)
+    t0 = time.perf_counter()
+    nbytes = reps = 0
+    while time.perf_counter() - t0 < budget_s:
+        o.gemv(WTYPE, w, n_in, n_out, o.quantize_pair(WTYPE, x)[0])
+        nbytes += Q.matvec_bytes(WTYPE, n_out, n_in)
+        reps += 1
+    dt = time.perf_counter() - t0
+    return {"value": round(nbytes / dt / 1e9, 3), "unit": UNIT, "cores": 1, "kind": "port",
+            "sample": f"{reps} x 4096x4096 matvec, oracle restatement, 1 thread", "cpu": cpu_model()}
+
+
+def cpu_model() -> str:
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except Exception:
+        pass
+    return "unknown"
+
+
+def copies_for(l2_bytes: int) -> dict:
+    out = {}
+    for n_out, n_in in SHAPES:
+        wb = n_out * Q.row_bytes(WTYPE, n_in)
+        out[f"{n_out}x{n_in}"] = max(2, math.ceil(4 * l2_bytes / wb))
+    return out
+
+
+def run_reference(args, world, rank) -> None:
+    if rank != 0:
+        return
+    gemv, kind, threads = cpu_gemv_handle()
+    copies = copies_for(126 * 2 ** 20)
+    if gemv is None:
+        bl = port_baseline(5.0)
+        line = {"impl": "reference", "metric": METRIC, "value": bl["value"], "unit": UNIT, "n_gpus": args.gpus,
+                "steps": 0, "warmup": 0, "higher_is_better": True, "note": "oracle port: reference build absent",
+                "cpu_baseline": bl, "e2e": {"value": bl["value"], "unit": UNIT, "h2d_bytes_per_step": 0,
+                                            "d2h_bytes_per_step": 0}}
+        print(json.dumps(line))
+        return
+    mats = cpu_sweep_setup(copies)
+    for _ in range(args.warmup):
+        cpu_run_pass(gemv, mats)
+    t0 = time.perf_counter()
+    nbytes = 0
+    for _ in range(args.steps):
+        nbytes += cpu_run_pass(gemv, mats)
+    dt = time.perf_counter() - t0
+    gemv.close()
+    value = nbytes / dt / 1e9
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3 / args.steps, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+        "config": workload_config(copies),
+        "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": threads, "kind": kind,
+                         "sample": f"{args.steps} timed passes over the sweep, si_backend_cpu()->gemv (AVX2), "
+                                   f"{threads} threads", "cpu": cpu_model()},
+        "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line))
+
+
+# ---- our arm ----------------------------------------------------------------------------------
+def run_ours(args, world, rank, local) -> None:
+    import torch
+
+    from siphon_b200 import lib
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    s = lib.load()
+    s.init(local)
+    props = torch.cuda.get_device_properties(dev)
+    l2 = int(getattr(props, "L2_cache_size", 126 * 2 ** 20))
+    copies = copies_for(l2)
+
+    stream = torch.cuda.Stream(device=dev)
+    mats = []
+    for (n_out, n_in) in SHAPES:
+        w = torch.from_numpy(synth.weights(WTYPE, n_out, n_in, seed=n_out + n_in)).to(dev)
+        c = copies[f"{n_out}x{n_in}"]
+        ws = [w] + [w.clone() for _ in range(c - 1)]
+        x = torch.from_numpy(synth.activations(n_in, 1, seed=7)[0]).to(dev)
+        ys = [torch.empty(n_out, dtype=torch.float32, device=dev) for _ in range(c)]
+        mats.append((n_out, n_in, ws, x, ys))
+    torch.cuda.synchronize()
+    step_bytes = sum(len(ws) * Q.matvec_bytes(WTYPE, n_out, n_in) for n_out, n_in, ws, _, _ in mats)
+    launches_per_step = sum(len(ws) for _, _, ws, _, _ in mats)
+
+    def step(st, evs=None):
+        h = st.cuda_stream
+        for si, (n_out, n_in, ws, x, ys) in enumerate(mats):
+            if evs is not None:
+                evs[si][0].record(st)
+            for w, y in zip(ws, ys):
+                s.gemv_f32(WTYPE, w, n_in, n_out, x, y, stream=h)
+            if evs is not None:
+                evs[si][1].record(st)
+
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            step(stream)
+    torch.cuda.synchronize()
+    for n_out, n_in, ws, x, ys in mats:
+        assert torch.isfinite(ys[-1]).all(), "non-finite matvec output"
+
+    # the K timed steps as one CUDA graph, with timing events around each
+    # shape's group of launches
+    evs = [[[torch.cuda.Event(enable_timing=True, external=True) for _ in range(2)] for _ in SHAPES]
+           for _ in range(args.steps)]
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        for k in range(args.steps):
+            step(stream, evs[k])
+    g.replay()                       # graph upload + K more warm-up steps
+    torch.cuda.synchronize()
+
+    barrier(world)
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        e0.record(stream)
+        g.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+    barrier(world)
+    ms = e0.elapsed_time(e1)
+    ms_max = max_over_ranks(ms, world, dev)
+    value = world * args.steps * step_bytes / (ms_max * 1e-3) / 1e9
+
+    # dominant kernel: gemv_kernel<Q4_K>, per-shape groups of back-to-back launches
+    per_shape_ms = [0.0] * len(SHAPES)
+    for k in range(args.steps):
+        for si in range(len(SHAPES)):
+            per_shape_ms[si] += evs[k][si][0].elapsed_time(evs[k][si][1])
+    kern_bytes = args.steps * step_bytes
+    achieved = kern_bytes / (sum(per_shape_ms) * 1e-3) / 1e9
+    peak, peak_kind = peak_hbm()
+    traffic = NCU_TRAFFIC.get("per_launch_bytes")
+    shape_detail = {}
+    for si, (n_out, n_in, ws, _, _) in enumerate(mats):
+        b = Q.matvec_bytes(WTYPE, n_out, n_in)
+        us = per_shape_ms[si] * 1e3 / (args.steps * len(ws))
+        shape_detail[f"{n_out}x{n_in}"] = {"us_per_launch": round(us, 3), "bytes_per_launch": b,
+                                           "GBps": round(b / (us * 1e-6) / 1e9, 1)}
+
+    # e2e through the host-buffer entry point (reference backend call shape)
+    hx = [torch.from_numpy(synth.activations(n_in, 1, seed=7)[0]).pin_memory() for _, n_in, _, _, _ in mats]
+    hy = [[torch.empty(n_out, dtype=torch.float32).pin_memory() for _ in ws] for n_out, _, ws, _, _ in mats]
+
+    def e2e_step():
+        for si, (n_out, n_in, ws, _, _) in enumerate(mats):
+            for ci, w in enumerate(ws):
+                s.gemv_host(WTYPE, w, n_in, n_out, hx[si], hy[si][ci], stream=stream.cuda_stream)
+
+    for _ in range(max(1, min(args.warmup, 3))):
+        e2e_step()
+    e2e_steps = max(3, min(args.steps, 20))
+    barrier(world)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        e2e_step()
+    e2e_s = max_over_ranks(time.perf_counter() - t0, world, dev)
+    e2e_value = world * e2e_steps * step_bytes / e2e_s / 1e9
+    h2d = sum(len(ws) * 4 * n_in for _, n_in, ws, _, _ in mats)
+    d2h = sum(len(ws) * 4 * n_out for n_out, _, ws, _, _ in mats)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(copies)
+
+    del g
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    line = {
+        "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+        "config": workload_config(copies, {"parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                                           "per_shape": shape_detail}),
+        "roofline": {"bound": "hbm", "kernel": "gemv_kernel<Q4_K>", "achieved": round(achieved, 1),
+                     "peak": peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),
+                     "traffic": traffic},
+        "e2e": {"value": round(e2e_value, 1), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "path": "sicu_gemv_host per matvec (pinned host x in, host y out, stream sync per call)"},
+        "gpu_launches": args.steps * launches_per_step,
+        "clocks": clk.summary(),
+    }
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    print(json.dumps(line))
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    world, rank, local = dist_setup()
+    if args.impl == "reference":
+        run_reference(args, world, rank)
+    else:
+        run_ours(args, world, rank, local)
+
+
+if __name__ == "__main__":
+    main()

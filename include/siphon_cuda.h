@@ -1,0 +1,146 @@
+/* libsiphon_cuda: the quantized-weight matrix path of Siphon on NVIDIA B200
+ * (sm_100a), as a plain C ABI.
+ *
+ * Every entry point takes raw GGUF block bytes exactly as they sit in the
+ * model file (block layouts of the reference's include/siphon/quant.h:31-100)
+ * and plain device pointers. No torch or CUDA types cross the boundary: a
+ * cudaStream_t travels as void* (NULL = the legacy default stream).
+ *
+ * Results are bit-identical with the reference's CPU code:
+ *   - quantized activations byte-for-byte with si_quant_row_q8_K
+ *     (src/kernels.c:561-595) and the AVX2 si_quant_row_q8_0 that x86 hosts
+ *     dispatch to (src/kernels_avx2.c:594-645);
+ *   - matvec outputs bit-for-bit with the scalar dot products
+ *     si_dot_<fmt>_<pair> (src/kernels.c:189-523) applied row by row.
+ *
+ * Return values follow the reference's convention (include/siphon/common.h:
+ * 25-34): 0 on success, a negative SICU_E* code on failure, with a message
+ * for the calling thread from sicu_last_error(). Argument checks run on the
+ * host before any CUDA call. All device memory handed in is owned by the
+ * caller; the library allocates device memory only in sicu_init, sicu_upload
+ * / sicu_malloc and the growable staging buffers of sicu_gemv_host.
+ */
+#ifndef SIPHON_CUDA_H
+#define SIPHON_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define SICU_API __attribute__((visibility("default")))
+#else
+#define SICU_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* error codes: the same values as the reference's SI_* (common.h:25-34) */
+#define SICU_OK        0
+#define SICU_ENOMEM   (-1)
+#define SICU_EIO      (-2)   /* CUDA runtime / launch failure */
+#define SICU_EFORMAT  (-3)
+#define SICU_ENOTSUP  (-4)   /* type or device not supported */
+#define SICU_EINVAL   (-5)   /* bad argument (size, alignment, null, state) */
+
+/* ggml type ids (reference include/siphon/quant.h:103-119) */
+#define SICU_T_F32   0
+#define SICU_T_F16   1
+#define SICU_T_Q4_0  2
+#define SICU_T_Q5_0  6
+#define SICU_T_Q8_0  8
+#define SICU_T_Q2_K 10
+#define SICU_T_Q3_K 11
+#define SICU_T_Q4_K 12
+#define SICU_T_Q5_K 13
+#define SICU_T_Q6_K 14
+#define SICU_T_Q8_K 15
+
+/* ---- lifecycle ----------------------------------------------------------- */
+
+/* Select and prepare a device (compute capability 10.0 required). Makes it
+ * current for the calling thread. Replaces the reference's implicit CPU
+ * backend singleton si_backend_cpu() (src/backend.c:133-142). */
+SICU_API int sicu_init(int device);
+/* Release library state on every initialised device. */
+SICU_API int sicu_shutdown(void);
+/* Copy the calling thread's last error message into buf (always
+ * NUL-terminated). Returns the message length. Replaces si_errstr()
+ * (include/siphon/common.h:37-38) with per-thread state. */
+SICU_API int sicu_last_error(char *buf, size_t len);
+/* Read and clear the device status word of the current device: bit 0 set
+ * means a kernel's bounded wait on its own copies gave up (outputs of that
+ * launch are invalid). Synchronises the device. */
+SICU_API int sicu_status(int *flags);
+
+/* ---- memory ------------------------------------------------------------- */
+
+SICU_API int sicu_malloc(void **dev, size_t bytes);
+SICU_API int sicu_free(void *dev);
+/* Make weight bytes device-resident once at load: allocate and copy. The
+ * returned pointer is 256-byte aligned. Replaces the mmap'd host view of
+ * si_tensor_from_gguf (src/backend.c:144-176). */
+SICU_API int sicu_upload(const void *host, size_t bytes, void **dev);
+SICU_API int sicu_memcpy_h2d(void *dev, const void *host, size_t bytes, void *stream);
+SICU_API int sicu_memcpy_d2h(void *host, const void *dev, size_t bytes, void *stream);
+SICU_API int sicu_stream_sync(void *stream);
+
+/* ---- geometry ------------------------------------------------------------ */
+
+/* Elements per block and bytes per block of a type.
+ * Replaces si_quant_geometry (src/kernels.c:904-919). */
+SICU_API int sicu_quant_geometry(uint32_t type, uint32_t *blck_size, uint32_t *type_size);
+/* Activation format a weight type's dot product consumes.
+ * Replaces si_quant_vec_dot_pair (src/kernels.c:946-960). */
+SICU_API int sicu_vec_dot_pair(uint32_t wtype, uint32_t *pair_type);
+
+/* ---- activation conversion ------------------------------------------------
+ * m rows of n contiguous f32 (dx, 16-byte aligned) into m rows of the pair
+ * format, each row quantized on its own. */
+
+/* Replaces si_quant_row_q8_K (src/kernels.c:561-595). n % 256 == 0.
+ * All-zero blocks get bsums = 0 (the reference leaves them unwritten). */
+SICU_API int sicu_quantize_q8_K(const float *dx, void *dy, int64_t n, int64_t m, void *stream);
+/* Replaces si_quant_row_q8_0 as dispatched on x86 (si_avx2_quant_row_q8_0,
+ * src/kernels_avx2.c:594-645). n % 32 == 0. */
+SICU_API int sicu_quantize_q8_0(const float *dx, void *dy, int64_t n, int64_t m, void *stream);
+/* F16 pair: element-wise round-to-nearest-even (src/backend.c:19-27). */
+SICU_API int sicu_convert_f16(const float *dx, void *dy, int64_t n, int64_t m, void *stream);
+/* Dispatch on the weight type's pair format. Replaces conv_task_fn
+ * (src/backend.c:17-47). */
+SICU_API int sicu_quantize_pair(uint32_t wtype, const float *dx, void *dxq, int64_t n, int64_t m, void *stream);
+
+/* ---- matrix-vector products ----------------------------------------------
+ * dw: [n_out rows][row bytes] of wtype blocks, row-major, 16-byte aligned.
+ * dy: [m][n_out] f32. Supported wtype: F16, Q4_0, Q5_0, Q8_0, Q2_K..Q6_K. */
+
+/* y_i = dot(W, xq_i) for m pair-format activation rows (dxq: m rows, each
+ * sicu pair-row bytes long). Replaces dot_task_fn (src/backend.c:61-71) with
+ * si_vec_dot_for(wtype) (src/kernels.c:1058-1072), scalar semantics. */
+SICU_API int sicu_gemv(uint32_t wtype, const void *dw, int64_t n_in, int64_t n_out,
+              const void *dxq, float *dy, int64_t m, void *stream);
+/* y = W x from f32 activations: the activation conversion happens inside
+ * the matvec kernel (each CTA quantizes into shared memory), exactly once
+ * per row as far as results go. Replaces the si_backend gemv vtable slot
+ * cpu_gemv (src/backend.c:85-120; include/siphon/tensor.h:43-55). */
+SICU_API int sicu_gemv_f32(uint32_t wtype, const void *dw, int64_t n_in, int64_t n_out,
+                  const float *dx, float *dy, int64_t m, void *stream);
+/* Same, with host input and output buffers (one activation row): copies x
+ * in, runs sicu_gemv_f32, copies y out and waits. This is the exact call
+ * shape of the reference's backend gemv slot. */
+SICU_API int sicu_gemv_host(uint32_t wtype, const void *dw, int64_t n_in, int64_t n_out,
+                   const float *hx, float *hy, void *stream);
+
+/* ---- dequantisation --------------------------------------------------------
+ * Rows rows[0..nrows) (host array) of W into dout[nrows][n_in] f32, reference
+ * semantics. Replaces cpu_row_to_f32 (src/backend.c:122-131) with
+ * si_dequant_row (src/kernels.c:803-817). */
+SICU_API int sicu_row_to_f32(uint32_t wtype, const void *dw, int64_t n_in, const int64_t *rows,
+                    int64_t nrows, float *dout, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SIPHON_CUDA_H */

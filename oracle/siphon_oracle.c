@@ -1,0 +1,581 @@
+/* siphon oracle: CPU restatement of the reference's quantized matrix path.
+ *
+ * TEST INFRASTRUCTURE ONLY. This file is the checker the CUDA library is
+ * compared against; nothing in siphon_b200/ links, loads or calls it. It is
+ * loaded by tests/, by __graft_entry__.smoke() and by bench.py's CPU
+ * baseline leg, and nowhere else.
+ *
+ * What it restates (all paths relative to the reference project root):
+ *   - f16 <-> f32 conversion ............ src/kernels.c:98-176
+ *   - Q8_K activation quantizer ......... src/kernels.c:527-533, 561-595
+ *   - Q8_0 activation quantizer, the
+ *     AVX2 form x86 hosts dispatch to ... src/kernels_avx2.c:594-645
+ *     and the scalar form ............... src/kernels.c:542-558
+ *   - scalar dot products ............... src/kernels.c:189-523
+ *   - row dequantisation ................ src/kernels.c:599-817
+ *   - block geometry / dot pairing ...... src/kernels.c:904-919, 946-960
+ *
+ * Integer partial sums are order-free, so they are written here in whatever
+ * order reads best. Every floating-point operation is written one rounding
+ * at a time in exactly the order the reference's scalar code performs it;
+ * the file must be compiled with -ffp-contract=off (oracle/Makefile does)
+ * so no multiply-add is fused.
+ *
+ * Parity pin: tests/test_oracle_pin.py compares every function here with
+ * the reference built from its own sources (oracle/_ref), and
+ * tests/test_oracle_golden.py against fixtures that reference produced
+ * (tests/golden/gen_golden.py).
+ */
+#include <math.h>
+#include <stdint.h>
+#include <string.h>
+
+#define ORC_API __attribute__((visibility("default")))
+
+/* ggml type ids as stored in GGUF (include/siphon/quant.h:103-119) */
+enum {
+    T_F32 = 0, T_F16 = 1, T_Q4_0 = 2, T_Q5_0 = 6, T_Q8_0 = 8,
+    T_Q2_K = 10, T_Q3_K = 11, T_Q4_K = 12, T_Q5_K = 13, T_Q6_K = 14,
+    T_Q8_K = 15,
+};
+
+/* on-disk block sizes (include/siphon/quant.h:92-100) */
+enum {
+    B_Q4_0 = 18, B_Q5_0 = 22, B_Q8_0 = 34, B_Q2_K = 84, B_Q3_K = 110,
+    B_Q4_K = 144, B_Q5_K = 176, B_Q6_K = 210, B_Q8_K = 292,
+};
+
+static inline uint16_t ld16(const uint8_t *p) { return (uint16_t)(p[0] | (p[1] << 8)); }
+static inline uint32_t ld32(const uint8_t *p) {
+    return (uint32_t)p[0] | ((uint32_t)p[1] << 8) | ((uint32_t)p[2] << 16) | ((uint32_t)p[3] << 24);
+}
+static inline float bits_f32(uint32_t u) { float f; memcpy(&f, &u, 4); return f; }
+static inline uint32_t f32_bits(float f) { uint32_t u; memcpy(&u, &f, 4); return u; }
+static inline float ldf32(const uint8_t *p) { return bits_f32(ld32(p)); }
+
+/* ---- half precision ------------------------------------------------------
+ * kernels.c:98-122 widens exactly (NaN payloads kept, not quieted). A half
+ * with a zero exponent field is man * 2^-24, which a float holds exactly. */
+ORC_API float orc_f16_to_f32(uint16_t h) {
+    const uint32_t sign = (uint32_t)(h >> 15) << 31;
+    const uint32_t e = (h >> 10) & 31u, m = h & 1023u;
+    if (e == 31) return bits_f32(sign | 0x7f800000u | (m << 13));
+    if (e == 0) {
+        const float mag = ldexpf((float)m, -24);
+        return sign ? -mag : mag;
+    }
+    return bits_f32(sign | ((e + 112u) << 23) | (m << 13));
+}
+
+/* kernels.c:124-176: IEEE round-to-nearest-even narrowing; a NaN becomes
+ * sign|0x7c00|0x0200|payload>>13 (payload forced non-zero). */
+ORC_API uint16_t orc_f32_to_f16(float f) {
+    const uint32_t u = f32_bits(f);
+    const uint16_t sign = (uint16_t)((u >> 16) & 0x8000u);
+    const uint32_t ef = (u >> 23) & 0xffu, m = u & 0x7fffffu;
+    if (ef == 0xff) {
+        if (m == 0) return (uint16_t)(sign | 0x7c00u);
+        uint32_t p = m >> 13;
+        if (p == 0) p = 1;
+        return (uint16_t)(sign | 0x7c00u | 0x0200u | p);
+    }
+    const int e = (int)ef - 112;               /* biased half exponent */
+    if (e >= 31) return (uint16_t)(sign | 0x7c00u);
+    if (e <= 0) {
+        if (e < -10) return sign;              /* below half the smallest subnormal */
+        const uint32_t full = m | 0x800000u;   /* implicit bit made explicit */
+        const int drop = 14 - e;               /* 14..24 bits go away */
+        uint32_t q = full >> drop;
+        const uint32_t rest = full & ((1u << drop) - 1u), mid = 1u << (drop - 1);
+        if (rest > mid || (rest == mid && (q & 1u))) q++;
+        return (uint16_t)(sign | q);
+    }
+    uint32_t q = ((uint32_t)e << 10) | (m >> 13);
+    const uint32_t rest = m & 0x1fffu;
+    if (rest > 0x1000u || (rest == 0x1000u && (q & 1u))) q++;   /* may carry into inf */
+    return (uint16_t)(sign | q);
+}
+
+/* ---- geometry (kernels.c:904-919) and dot pairing (kernels.c:946-960) ---- */
+ORC_API int orc_geometry(uint32_t t, uint32_t *blck, uint32_t *bytes) {
+    static const struct { uint32_t t, n, b; } g[] = {
+        {T_F32, 1, 4}, {T_F16, 1, 2}, {T_Q4_0, 32, B_Q4_0}, {T_Q5_0, 32, B_Q5_0},
+        {T_Q8_0, 32, B_Q8_0}, {T_Q2_K, 256, B_Q2_K}, {T_Q3_K, 256, B_Q3_K},
+        {T_Q4_K, 256, B_Q4_K}, {T_Q5_K, 256, B_Q5_K}, {T_Q6_K, 256, B_Q6_K},
+        {T_Q8_K, 256, B_Q8_K},
+    };
+    for (unsigned i = 0; i < sizeof g / sizeof g[0]; i++) {
+        if (g[i].t == t) { *blck = g[i].n; *bytes = g[i].b; return 1; }
+    }
+    return 0;
+}
+
+ORC_API int orc_pair_type(uint32_t wt, uint32_t *pair) {
+    switch (wt) {
+        case T_F32: case T_F16: *pair = wt; return 1;
+        case T_Q4_0: case T_Q5_0: case T_Q8_0: *pair = T_Q8_0; return 1;
+        case T_Q2_K: case T_Q3_K: case T_Q4_K: case T_Q5_K: case T_Q6_K: *pair = T_Q8_K; return 1;
+        default: return 0;
+    }
+}
+
+/* ---- activation quantizers ------------------------------------------------ */
+
+/* Q8_K, kernels.c:561-595. Per 256: the first element of largest magnitude
+ * (strict > scan) fixes iscale = -127/max; quants are nearest_int(iscale*x)
+ * capped at +127, bsums are the 16-element group sums, d = 1/iscale.
+ * nearest_int (kernels.c:528-533) is the 1.5*2^23 magic add: round half to
+ * even for every product that can occur here. On x86 a NaN product is the
+ * NaN operand itself, so the magic add leaves its low 22 payload bits as
+ * the "integer"; that is reproduced for NaN inputs. An all-zero block sets
+ * d = 0 and qs = 0 and leaves bsums as they were (kernels.c:574-579). */
+ORC_API void orc_quant_q8_K(const float *x, uint8_t *y, int n) {
+    for (int b = 0; b < n / 256; b++, x += 256, y += B_Q8_K) {
+        float peak = 0.0f, lead = 0.0f;
+        for (int j = 0; j < 256; j++) {
+            const float a = fabsf(x[j]);
+            if (a > peak) { peak = a; lead = x[j]; }
+        }
+        int8_t *qs = (int8_t *)(y + 4);
+        if (peak == 0.0f) {
+            const float zero = 0.0f;
+            memcpy(y, &zero, 4);
+            memset(qs, 0, 256);
+            continue;
+        }
+        const float iscale = -127.f / lead;
+        for (int j = 0; j < 256; j++) {
+            int v;
+            if (isnan(x[j])) {
+                v = (int)(f32_bits(x[j]) & 0x3fffffu);
+            } else {
+                const float p = iscale * x[j];
+                v = (int)((f32_bits(p + 12582912.f) & 0x7fffffu)) - 0x400000;
+            }
+            qs[j] = (int8_t)(v < 127 ? v : 127);
+        }
+        for (int g = 0; g < 16; g++) {
+            int s = 0;
+            for (int k = 0; k < 16; k++) s += qs[16 * g + k];
+            const int16_t s16 = (int16_t)s;
+            memcpy(y + 260 + 2 * g, &s16, 2);
+        }
+        const float d = 1.0f / iscale;
+        memcpy(y, &d, 4);
+    }
+}
+
+/* vmaxps semantics: first operand if it compares greater, else the second
+ * (so a NaN in either slot yields the second operand). */
+static inline float vmax(float a, float b) { return a > b ? a : b; }
+
+/* int32 -> int16 -> int8 with saturation at each step, as packs_epi32 then
+ * packs_epi16 do; a NaN / out-of-range cvtps_epi32 gives INT32_MIN. */
+static inline int8_t sat8_from_rounded(float r) {
+    int32_t i;
+    if (!(r >= -2147483648.0f && r < 2147483648.0f)) i = INT32_MIN;
+    else i = (int32_t)r;
+    if (i > 127) i = 127;
+    if (i < -128) i = -128;
+    return (int8_t)i;
+}
+
+/* Q8_0 in the AVX2 form that x86 hosts run (kernels_avx2.c:594-645): the
+ * lane-wise max tree of |x|, d = max/127 stored as f16, id = 127/max,
+ * quants = round-half-even(x*id) with saturating packs. */
+ORC_API void orc_quant_q8_0(const float *x, uint8_t *y, int n) {
+    for (int b = 0; b < n / 32; b++, x += 32, y += B_Q8_0) {
+        float lane[8];
+        for (int i = 0; i < 8; i++) {
+            float m = fabsf(x[i]);
+            m = vmax(m, fabsf(x[8 + i]));
+            m = vmax(m, fabsf(x[16 + i]));
+            m = vmax(m, fabsf(x[24 + i]));
+            lane[i] = m;
+        }
+        float q4[4];
+        for (int i = 0; i < 4; i++) q4[i] = vmax(lane[4 + i], lane[i]);
+        const float q2a = vmax(q4[0], q4[2]), q2b = vmax(q4[1], q4[3]);
+        const float top = vmax(q2a, q2b);
+        const uint16_t dh = orc_f32_to_f16(top / 127.f);
+        y[0] = (uint8_t)dh; y[1] = (uint8_t)(dh >> 8);
+        const float id = (top != 0.0f) ? 127.f / top : 0.0f;
+        for (int j = 0; j < 32; j++) y[2 + j] = (uint8_t)sat8_from_rounded(nearbyintf(x[j] * id));
+    }
+}
+
+/* Q8_0 in the portable scalar form (kernels.c:542-558): id = 1/(amax/127)
+ * and roundf (half away from zero). Kept to report how often the two forms
+ * disagree; the CUDA quantizer follows the AVX2 form above. */
+ORC_API void orc_quant_q8_0_scalar(const float *x, uint8_t *y, int n) {
+    for (int b = 0; b < n / 32; b++, x += 32, y += B_Q8_0) {
+        float amax = 0.0f;
+        for (int j = 0; j < 32; j++) amax = amax > fabsf(x[j]) ? amax : fabsf(x[j]);
+        const float d = amax / 127.0f;
+        const float id = d != 0.0f ? 1.0f / d : 0.0f;
+        const uint16_t dh = orc_f32_to_f16(d);
+        y[0] = (uint8_t)dh; y[1] = (uint8_t)(dh >> 8);
+        for (int j = 0; j < 32; j++) y[2 + j] = (uint8_t)(int8_t)roundf(x[j] * id);
+    }
+}
+
+/* F16 pair: element-wise RNE narrowing (src/backend.c:19-27) */
+ORC_API void orc_convert_f16(const float *x, uint16_t *y, int n) {
+    for (int i = 0; i < n; i++) y[i] = orc_f32_to_f16(x[i]);
+}
+
+/* ---- weight element decoders ----------------------------------------------
+ * One function per format returning the signed integer quant of element e
+ * (0..255 within a super-block, 0..31 within a classic block) and, for the
+ * K formats, the scale (and min) of the sub-block e falls in. */
+
+/* Q4_K/Q5_K 6-bit scale/min unpack (kernels.c:648-656, identical to the
+ * utmp shuffle at kernels.c:377-382) */
+static void k4_scales(const uint8_t *s, int sc[8], int mn[8]) {
+    for (int j = 0; j < 4; j++) {
+        sc[j] = s[j] & 63;
+        mn[j] = s[j + 4] & 63;
+        sc[j + 4] = (s[j + 8] & 15) | ((s[j] >> 6) << 4);
+        mn[j + 4] = (s[j + 8] >> 4) | ((s[j + 4] >> 6) << 4);
+    }
+}
+
+/* Q4_K element (kernels.c:371-376): chunk c = e/64 of 32 bytes; low nibble
+ * for e%64 < 32, high nibble otherwise */
+static int q4k_elem(const uint8_t *blk, int e) {
+    const uint8_t byte = blk[16 + 32 * (e / 64) + (e % 32)];
+    return (e % 64) < 32 ? (byte & 15) : (byte >> 4);
+}
+
+/* Q5_K element (kernels.c:436-444): Q4_K nibble + 16 * bit (e/32) of qh[e%32] */
+static int q5k_elem(const uint8_t *blk, int e) {
+    const uint8_t byte = blk[48 + 32 * (e / 64) + (e % 32)];
+    const int nib = (e % 64) < 32 ? (byte & 15) : (byte >> 4);
+    return nib + (((blk[16 + e % 32] >> (e / 32)) & 1) ? 16 : 0);
+}
+
+/* Q6_K element (kernels.c:496-506): half h, group g of 32, lane i */
+static int q6k_elem(const uint8_t *blk, int e) {
+    const int h = e / 128, g = (e % 128) / 32, i = e % 32;
+    const uint8_t lo = blk[64 * h + i + ((g & 1) ? 32 : 0)];
+    const uint8_t hi = blk[128 + 32 * h + i];
+    const int nib = g < 2 ? (lo & 15) : (lo >> 4);
+    return (nib | (((hi >> (2 * g)) & 3) << 4)) - 32;
+}
+
+/* Q3_K element (kernels.c:311-325): 2-bit quant, minus 4 when the hmask bit
+ * (4h + g) of hmask[i] is clear */
+static int q3k_elem(const uint8_t *blk, int e) {
+    const int h = e / 128, g = (e % 128) / 32, i = e % 32;
+    const int q = (blk[32 + 32 * h + i] >> (2 * g)) & 3;
+    return q - ((blk[i] >> (4 * h + g)) & 1 ? 0 : 4);
+}
+
+/* Q3_K 6-bit scales (kernels.c:328-333): low nibble from byte j (j<8) or
+ * the high nibble of byte j-8, top two bits from byte 8 + j%4 at 2*(j/4) */
+static void q3k_scales(const uint8_t *blk, int sc[16]) {
+    const uint8_t *s = blk + 96;
+    for (int j = 0; j < 16; j++) {
+        const int lo = j < 8 ? (s[j] & 15) : (s[j - 8] >> 4);
+        const int hi = (s[8 + j % 4] >> (2 * (j / 4))) & 3;
+        sc[j] = (lo | (hi << 4)) - 32;
+    }
+}
+
+/* Q2_K element (kernels.c:268-283): half k, shift group jj, 16-lane half */
+static int q2k_elem(const uint8_t *blk, int e) {
+    const int k = e / 128, r = e % 128, jj = r / 32, i = r % 32;
+    return (blk[16 + 32 * k + i] >> (2 * jj)) & 3;
+}
+
+/* ---- dot products (scalar reference semantics) ------------------------------ */
+
+/* Shared tail of the K formats with eight lane accumulators
+ * (kernels.c:343-345, 403-408, 471-476, 518-521): per super-block
+ * sums[l] += d * aux[l]; after the row, sumf += sums[l] for l = 0..7. */
+typedef struct { float sums[8]; float sumf; } lanes8;
+
+static void lanes8_add(lanes8 *st, float d, const int32_t aux[8]) {
+    for (int l = 0; l < 8; l++) st->sums[l] = st->sums[l] + d * (float)aux[l];
+}
+static float lanes8_finish(lanes8 *st) {
+    float s = st->sumf;
+    for (int l = 0; l < 8; l++) s = s + st->sums[l];
+    return s;
+}
+
+/* kernels.c:349-410 */
+ORC_API float orc_dot_q4_K(int n, const uint8_t *x, const uint8_t *y) {
+    lanes8 st = {{0}, 0.0f};
+    for (int i = 0; i < n / 256; i++, x += B_Q4_K, y += B_Q8_K) {
+        int sc[8], mn[8];
+        k4_scales(x + 4, sc, mn);
+        const int8_t *a = (const int8_t *)(y + 4);
+        int32_t aux[8] = {0};
+        for (int e = 0; e < 256; e++) aux[e % 8] += sc[e / 32] * (q4k_elem(x, e) * a[e]);
+        int mins = 0;
+        for (int g = 0; g < 16; g++) {
+            int16_t bs; memcpy(&bs, y + 260 + 2 * g, 2);
+            mins += bs * mn[g / 2];
+        }
+        const float yd = ldf32(y);
+        lanes8_add(&st, orc_f16_to_f32(ld16(x)) * yd, aux);
+        st.sumf = st.sumf - (orc_f16_to_f32(ld16(x + 2)) * yd) * (float)mins;
+    }
+    return lanes8_finish(&st);
+}
+
+/* kernels.c:412-478 */
+ORC_API float orc_dot_q5_K(int n, const uint8_t *x, const uint8_t *y) {
+    lanes8 st = {{0}, 0.0f};
+    for (int i = 0; i < n / 256; i++, x += B_Q5_K, y += B_Q8_K) {
+        int sc[8], mn[8];
+        k4_scales(x + 4, sc, mn);
+        const int8_t *a = (const int8_t *)(y + 4);
+        int32_t aux[8] = {0};
+        for (int e = 0; e < 256; e++) aux[e % 8] += sc[e / 32] * (q5k_elem(x, e) * a[e]);
+        int mins = 0;
+        for (int g = 0; g < 16; g++) {
+            int16_t bs; memcpy(&bs, y + 260 + 2 * g, 2);
+            mins += bs * mn[g / 2];
+        }
+        const float yd = ldf32(y);
+        lanes8_add(&st, orc_f16_to_f32(ld16(x)) * yd, aux);
+        st.sumf = st.sumf - (orc_f16_to_f32(ld16(x + 2)) * yd) * (float)mins;
+    }
+    return lanes8_finish(&st);
+}
+
+/* kernels.c:480-523 */
+ORC_API float orc_dot_q6_K(int n, const uint8_t *x, const uint8_t *y) {
+    lanes8 st = {{0}, 0.0f};
+    for (int i = 0; i < n / 256; i++, x += B_Q6_K, y += B_Q8_K) {
+        const int8_t *sc = (const int8_t *)(x + 192);
+        const int8_t *a = (const int8_t *)(y + 4);
+        int32_t aux[8] = {0};
+        for (int e = 0; e < 256; e++) aux[e % 8] += sc[e / 16] * (q6k_elem(x, e) * a[e]);
+        lanes8_add(&st, orc_f16_to_f32(ld16(x + 208)) * ldf32(y), aux);
+    }
+    return lanes8_finish(&st);
+}
+
+/* kernels.c:289-347 */
+ORC_API float orc_dot_q3_K(int n, const uint8_t *x, const uint8_t *y) {
+    lanes8 st = {{0}, 0.0f};
+    for (int i = 0; i < n / 256; i++, x += B_Q3_K, y += B_Q8_K) {
+        int sc[16];
+        q3k_scales(x, sc);
+        const int8_t *a = (const int8_t *)(y + 4);
+        int32_t aux[8] = {0};
+        for (int e = 0; e < 256; e++) aux[e % 8] += sc[e / 16] * (q3k_elem(x, e) * a[e]);
+        lanes8_add(&st, orc_f16_to_f32(ld16(x + 108)) * ldf32(y), aux);
+    }
+    return lanes8_finish(&st);
+}
+
+/* kernels.c:249-287: one integer sum per super-block, then
+ * sumf += dall*isum - dmin*summs */
+ORC_API float orc_dot_q2_K(int n, const uint8_t *x, const uint8_t *y) {
+    float sumf = 0.0f;
+    for (int i = 0; i < n / 256; i++, x += B_Q2_K, y += B_Q8_K) {
+        const int8_t *a = (const int8_t *)(y + 4);
+        int isum = 0, summs = 0;
+        for (int e = 0; e < 256; e++) isum += (x[e / 16] & 15) * (q2k_elem(x, e) * a[e]);
+        for (int g = 0; g < 16; g++) {
+            int16_t bs; memcpy(&bs, y + 260 + 2 * g, 2);
+            summs += bs * (x[g] >> 4);
+        }
+        const float yd = ldf32(y);
+        const float dall = yd * orc_f16_to_f32(ld16(x + 80));
+        const float dmin = yd * orc_f16_to_f32(ld16(x + 82));
+        sumf = sumf + (dall * (float)isum - dmin * (float)summs);
+    }
+    return sumf;
+}
+
+/* kernels.c:197-213: sumf += sumi * dx * dy, left to right */
+ORC_API float orc_dot_q4_0(int n, const uint8_t *x, const uint8_t *y) {
+    float sumf = 0.0f;
+    for (int b = 0; b < n / 32; b++, x += B_Q4_0, y += B_Q8_0) {
+        const int8_t *a = (const int8_t *)(y + 2);
+        int s = 0;
+        for (int j = 0; j < 16; j++) s += ((x[2 + j] & 15) - 8) * a[j] + ((x[2 + j] >> 4) - 8) * a[j + 16];
+        sumf = sumf + ((float)s * orc_f16_to_f32(ld16(x))) * orc_f16_to_f32(ld16(y));
+    }
+    return sumf;
+}
+
+/* kernels.c:215-233: bit j of qh tops element j, bit j+16 element j+16 */
+ORC_API float orc_dot_q5_0(int n, const uint8_t *x, const uint8_t *y) {
+    float sumf = 0.0f;
+    for (int b = 0; b < n / 32; b++, x += B_Q5_0, y += B_Q8_0) {
+        const int8_t *a = (const int8_t *)(y + 2);
+        const uint32_t qh = ld32(x + 2);
+        int s = 0;
+        for (int j = 0; j < 16; j++) {
+            const int v0 = ((x[6 + j] & 15) | (int)(((qh >> j) & 1) << 4)) - 16;
+            const int v1 = ((x[6 + j] >> 4) | (int)(((qh >> (j + 16)) & 1) << 4)) - 16;
+            s += v0 * a[j] + v1 * a[j + 16];
+        }
+        sumf = sumf + ((float)s * orc_f16_to_f32(ld16(x))) * orc_f16_to_f32(ld16(y));
+    }
+    return sumf;
+}
+
+/* kernels.c:235-247: sumf += sumi * (dx * dy) */
+ORC_API float orc_dot_q8_0(int n, const uint8_t *x, const uint8_t *y) {
+    float sumf = 0.0f;
+    for (int b = 0; b < n / 32; b++, x += B_Q8_0, y += B_Q8_0) {
+        const int8_t *w = (const int8_t *)(x + 2), *a = (const int8_t *)(y + 2);
+        int s = 0;
+        for (int j = 0; j < 32; j++) s += w[j] * a[j];
+        sumf = sumf + (float)s * (orc_f16_to_f32(ld16(x)) * orc_f16_to_f32(ld16(y)));
+    }
+    return sumf;
+}
+
+/* kernels.c:189-195: float products summed into a double, left to right */
+ORC_API float orc_dot_f16(int n, const uint8_t *x, const uint8_t *y) {
+    double acc = 0.0;
+    for (int i = 0; i < n; i++) {
+        acc += (double)(orc_f16_to_f32(ld16(x + 2 * i)) * orc_f16_to_f32(ld16(y + 2 * i)));
+    }
+    return (float)acc;
+}
+
+/* kernels.c:180-187 (F32 rows are not on the quantized path; kept so the
+ * gemv below accepts every type the reference's cpu_gemv does) */
+ORC_API float orc_dot_f32(int n, const uint8_t *x, const uint8_t *y) {
+    double acc = 0.0;
+    for (int i = 0; i < n; i++) acc += (double)(ldf32(x + 4 * i) * ldf32(y + 4 * i));
+    return (float)acc;
+}
+
+typedef float (*dot_fn)(int, const uint8_t *, const uint8_t *);
+
+static dot_fn dot_for(uint32_t wt) {
+    switch (wt) {
+        case T_F32: return orc_dot_f32;
+        case T_F16: return orc_dot_f16;
+        case T_Q4_0: return orc_dot_q4_0;
+        case T_Q5_0: return orc_dot_q5_0;
+        case T_Q8_0: return orc_dot_q8_0;
+        case T_Q2_K: return orc_dot_q2_K;
+        case T_Q3_K: return orc_dot_q3_K;
+        case T_Q4_K: return orc_dot_q4_K;
+        case T_Q5_K: return orc_dot_q5_K;
+        case T_Q6_K: return orc_dot_q6_K;
+        default: return 0;
+    }
+}
+
+/* One dot of a weight row against an already converted activation. */
+ORC_API int orc_vec_dot(uint32_t wt, int n, const void *x, const void *y, float *s) {
+    dot_fn f = dot_for(wt);
+    if (!f) return -4;
+    *s = f(n, (const uint8_t *)x, (const uint8_t *)y);
+    return 0;
+}
+
+/* Convert an f32 activation row into wt's pair format (src/backend.c:17-47). */
+ORC_API int orc_quantize_pair(uint32_t wt, const float *x, void *out, int n) {
+    uint32_t pair;
+    if (!orc_pair_type(wt, &pair)) return -4;
+    switch (pair) {
+        case T_F32: memcpy(out, x, (size_t)n * 4); return 0;
+        case T_F16: orc_convert_f16(x, (uint16_t *)out, n); return 0;
+        case T_Q8_0: orc_quant_q8_0(x, (uint8_t *)out, n); return 0;
+        default: orc_quant_q8_K(x, (uint8_t *)out, n); return 0;
+    }
+}
+
+/* Rows [r0, r1) of y = W xq, W row-major [n_out, n_in] of wt blocks,
+ * xq already in the pair format (src/backend.c:61-71). */
+ORC_API int orc_gemv_rows(uint32_t wt, const void *w, int64_t row_bytes, int n_in,
+                          int64_t r0, int64_t r1, const void *xq, float *y) {
+    dot_fn f = dot_for(wt);
+    if (!f) return -4;
+    const uint8_t *base = (const uint8_t *)w;
+    for (int64_t r = r0; r < r1; r++) y[r] = f(n_in, base + r * row_bytes, (const uint8_t *)xq);
+    return 0;
+}
+
+/* ---- dequantisation (kernels.c:599-817), the row_to_f32 leg ------------------ */
+
+ORC_API int orc_dequant_row(uint32_t t, const void *xv, float *y, int n) {
+    const uint8_t *x = (const uint8_t *)xv;
+    switch (t) {
+        case T_F32: memcpy(y, x, (size_t)n * 4); return 0;
+        case T_F16:
+            for (int i = 0; i < n; i++) y[i] = orc_f16_to_f32(ld16(x + 2 * i));
+            return 0;
+        case T_Q4_0:
+            for (int b = 0; b < n / 32; b++, x += B_Q4_0) {
+                const float d = orc_f16_to_f32(ld16(x));
+                for (int j = 0; j < 16; j++) {
+                    y[32 * b + j] = (float)((x[2 + j] & 15) - 8) * d;
+                    y[32 * b + j + 16] = (float)((x[2 + j] >> 4) - 8) * d;
+                }
+            }
+            return 0;
+        case T_Q5_0:
+            for (int b = 0; b < n / 32; b++, x += B_Q5_0) {
+                const float d = orc_f16_to_f32(ld16(x));
+                const uint32_t qh = ld32(x + 2);
+                for (int j = 0; j < 16; j++) {
+                    y[32 * b + j] = (float)(((x[6 + j] & 15) | (int)(((qh >> j) & 1) << 4)) - 16) * d;
+                    y[32 * b + j + 16] = (float)(((x[6 + j] >> 4) | (int)(((qh >> (j + 16)) & 1) << 4)) - 16) * d;
+                }
+            }
+            return 0;
+        case T_Q8_0:
+            for (int b = 0; b < n / 32; b++, x += B_Q8_0) {
+                const float d = orc_f16_to_f32(ld16(x));
+                for (int j = 0; j < 32; j++) y[32 * b + j] = (float)(int8_t)x[2 + j] * d;
+            }
+            return 0;
+        case T_Q2_K:
+            /* kernels.c:658-682: dl * q - ml per 16 elements */
+            for (int b = 0; b < n / 256; b++, x += B_Q2_K) {
+                const float d = orc_f16_to_f32(ld16(x + 80)), mn = orc_f16_to_f32(ld16(x + 82));
+                for (int e = 0; e < 256; e++) {
+                    const uint8_t s = x[e / 16];
+                    const float dl = d * (float)(s & 15), ml = mn * (float)(s >> 4);
+                    y[256 * b + e] = dl * (float)q2k_elem(x, e) - ml;
+                }
+            }
+            return 0;
+        case T_Q3_K:
+            for (int b = 0; b < n / 256; b++, x += B_Q3_K) {
+                int sc[16];
+                q3k_scales(x, sc);
+                const float d = orc_f16_to_f32(ld16(x + 108));
+                for (int e = 0; e < 256; e++) y[256 * b + e] = (d * (float)sc[e / 16]) * (float)q3k_elem(x, e);
+            }
+            return 0;
+        case T_Q4_K:
+        case T_Q5_K:
+            /* kernels.c:726-774: d*sc * q - dmin*m */
+            for (int b = 0; b < n / 256; b++) {
+                int sc[8], mn[8];
+                k4_scales(x + 4, sc, mn);
+                const float d = orc_f16_to_f32(ld16(x)), dm = orc_f16_to_f32(ld16(x + 2));
+                for (int e = 0; e < 256; e++) {
+                    const int q = t == T_Q4_K ? q4k_elem(x, e) : q5k_elem(x, e);
+                    y[256 * b + e] = (d * (float)sc[e / 32]) * (float)q - dm * (float)mn[e / 32];
+                }
+                x += t == T_Q4_K ? B_Q4_K : B_Q5_K;
+            }
+            return 0;
+        case T_Q6_K:
+            /* kernels.c:776-801: y = d * sc * q (left to right) */
+            for (int b = 0; b < n / 256; b++, x += B_Q6_K) {
+                const float d = orc_f16_to_f32(ld16(x + 208));
+                const int8_t *sc = (const int8_t *)(x + 192);
+                for (int e = 0; e < 256; e++) y[256 * b + e] = (d * (float)sc[e / 16]) * (float)q6k_elem(x, e);
+            }
+            return 0;
+        default:
+            return -4;
+    }
+}

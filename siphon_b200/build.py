@@ -1,0 +1,59 @@
+"""Build libsiphon_cuda.so in-tree with nvcc for sm_100a.
+
+    python -m siphon_b200.build            # builds siphon_b200/libsiphon_cuda.so
+
+The library links the CUDA runtime statically, so it only needs the driver at
+run time and shares the device's primary context with anything else in the
+process (torch included).
+"""
+
+from __future__ import annotations
+
+import os
+import shutil
+import subprocess
+import sys
+from pathlib import Path
+
+PKG = Path(__file__).resolve().parent
+CSRC = PKG / "csrc"
+ROOT = PKG.parent
+LIB = PKG / "libsiphon_cuda.so"
+
+SOURCES = ["abi.cu", "gemv.cu", "gemv_f16.cu", "quantize.cu"]
+HEADERS = ["common.cuh", "gemv.cuh", "quantize.cuh", "launch.h"]
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+
+
+def nvcc() -> str:
+    cand = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
+    if not Path(cand).exists():
+        raise RuntimeError("nvcc not found")
+    return cand
+
+
+def stale() -> bool:
+    if not LIB.exists():
+        return True
+    t = LIB.stat().st_mtime
+    deps = [CSRC / s for s in SOURCES + HEADERS] + [ROOT / "include" / "siphon_cuda.h"]
+    return any(d.stat().st_mtime > t for d in deps)
+
+
+def build(force: bool = False, verbose: bool = False) -> Path:
+    if not force and not stale():
+        return LIB
+    cmd = [nvcc(), *ARCH, "-O3", "-lineinfo", "-std=c++17", "-shared", "-Xcompiler", "-fPIC,-fvisibility=hidden",
+           "-I", str(ROOT / "include"), "-o", str(LIB) + ".tmp", *[str(CSRC / s) for s in SOURCES]]
+    if os.environ.get("SICU_PTXAS_VERBOSE"):
+        cmd.insert(1, "-Xptxas=-v")
+    if verbose:
+        print(" ".join(cmd))
+    subprocess.run(cmd, check=True)
+    os.replace(str(LIB) + ".tmp", LIB)
+    return LIB
+
+
+if __name__ == "__main__":
+    build(force="--force" in sys.argv, verbose=True)
+    print(LIB)

@@ -1,0 +1,402 @@
+// The extern "C" boundary of libsiphon_cuda (declared in include/siphon_cuda.h).
+// Argument checks happen on the host before any CUDA call, so they behave the
+// same on a machine without a GPU.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "../../include/siphon_cuda.h"
+#include "common.cuh"
+#include "launch.h"
+
+using namespace sicu;
+
+namespace {
+
+thread_local char g_err[512] = "";
+
+int fail(int code, const char *fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_err, sizeof g_err, fmt, ap);
+    va_end(ap);
+    return code;
+}
+
+struct DevState {
+    bool ready = false;
+    int sms = 0;
+    int smem_optin = 0;
+    int *status = nullptr;      // device status word
+    // growable staging for the host-buffer entry points
+    void *stage = nullptr;
+    size_t stage_bytes = 0;
+};
+
+constexpr int MAX_DEV = 64;
+DevState g_dev[MAX_DEV];
+std::mutex g_mu;
+
+bool geometry(uint32_t t, uint32_t &blck, uint32_t &bytes) {
+    switch (t) {
+        case T_F32: blck = 1; bytes = 4; return true;
+        case T_F16: blck = 1; bytes = 2; return true;
+        case T_Q4_0: blck = 32; bytes = B_Q4_0; return true;
+        case T_Q5_0: blck = 32; bytes = B_Q5_0; return true;
+        case T_Q8_0: blck = 32; bytes = B_Q8_0; return true;
+        case T_Q2_K: blck = 256; bytes = B_Q2_K; return true;
+        case T_Q3_K: blck = 256; bytes = B_Q3_K; return true;
+        case T_Q4_K: blck = 256; bytes = B_Q4_K; return true;
+        case T_Q5_K: blck = 256; bytes = B_Q5_K; return true;
+        case T_Q6_K: blck = 256; bytes = B_Q6_K; return true;
+        case T_Q8_K: blck = 256; bytes = B_Q8_K; return true;
+        default: return false;
+    }
+}
+
+bool pair_of(uint32_t wt, uint32_t &pair) {
+    switch (wt) {
+        case T_F16: pair = T_F16; return true;
+        case T_Q4_0: case T_Q5_0: case T_Q8_0: pair = T_Q8_0; return true;
+        case T_Q2_K: case T_Q3_K: case T_Q4_K: case T_Q5_K: case T_Q6_K: pair = T_Q8_K; return true;
+        default: return false;
+    }
+}
+
+const char *tname(uint32_t t) {
+    switch (t) {
+        case T_F32: return "F32"; case T_F16: return "F16"; case T_Q4_0: return "Q4_0";
+        case T_Q5_0: return "Q5_0"; case T_Q8_0: return "Q8_0"; case T_Q2_K: return "Q2_K";
+        case T_Q3_K: return "Q3_K"; case T_Q4_K: return "Q4_K"; case T_Q5_K: return "Q5_K";
+        case T_Q6_K: return "Q6_K"; case T_Q8_K: return "Q8_K"; default: return "unknown";
+    }
+}
+
+bool aligned(const void *p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
+
+int cuda_fail(cudaError_t e, const char *what) {
+    return fail(SICU_EIO, "%s: %s", what, cudaGetErrorString(e));
+}
+
+// Current device's state, or an error when sicu_init was not called for it.
+bool any_ready();
+
+int current(DevState *&ds) {
+    if (!any_ready()) return fail(SICU_EINVAL, "no device initialised (call sicu_init first)");
+    int dev = -1;
+    const cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    if (dev < 0 || dev >= MAX_DEV || !g_dev[dev].ready)
+        return fail(SICU_EINVAL, "device %d not initialised (call sicu_init first)", dev);
+    ds = &g_dev[dev];
+    return SICU_OK;
+}
+
+bool any_ready() {
+    for (auto &d : g_dev) if (d.ready) return true;
+    return false;
+}
+
+int check_activation(uint32_t pair, const float *dx, const void *dy, int64_t n, int64_t m) {
+    uint32_t blck, bytes;
+    if (!geometry(pair, blck, bytes)) return fail(SICU_ENOTSUP, "no activation format %u", pair);
+    if (n <= 0 || m <= 0) return fail(SICU_EINVAL, "empty activation (n=%lld, m=%lld)", (long long)n, (long long)m);
+    if (n % blck) return fail(SICU_EINVAL, "%s activation length %lld is not a multiple of %u", tname(pair), (long long)n, blck);
+    if (n > (int64_t)1 << 30) return fail(SICU_EINVAL, "activation length %lld too large", (long long)n);
+    if (!dx || !dy) return fail(SICU_EINVAL, "null activation pointer");
+    if (!aligned(dx, 16)) return fail(SICU_EINVAL, "f32 activation must be 16-byte aligned");
+    if (!aligned(dy, pair == T_Q8_K ? 4 : 2)) return fail(SICU_EINVAL, "%s output misaligned", tname(pair));
+    return SICU_OK;
+}
+
+int check_matvec(uint32_t wt, const void *dw, int64_t n_in, int64_t n_out, const void *dx, const float *dy,
+                 int64_t m, uint32_t &pair) {
+    if (!pair_of(wt, pair)) return fail(SICU_ENOTSUP, "matvec: unsupported weight type %s (%u)", tname(wt), wt);
+    uint32_t blck, bytes;
+    geometry(wt, blck, bytes);
+    if (n_in <= 0 || n_out < 0 || m <= 0)
+        return fail(SICU_EINVAL, "matvec: bad shape n_in=%lld n_out=%lld m=%lld", (long long)n_in, (long long)n_out, (long long)m);
+    if (n_in % blck) return fail(SICU_EINVAL, "matvec: row length %lld of %s is not a multiple of %u", (long long)n_in, tname(wt), blck);
+    if (n_in > (int64_t)1 << 24) return fail(SICU_EINVAL, "matvec: row length %lld too large", (long long)n_in);
+    if (!dw || !dx || !dy) return fail(SICU_EINVAL, "matvec: null pointer");
+    if (!aligned(dw, 16)) return fail(SICU_EINVAL, "matvec: weight pointer must be 16-byte aligned");
+    if (!aligned(dy, 4)) return fail(SICU_EINVAL, "matvec: output must be 4-byte aligned");
+    return SICU_OK;
+}
+
+int64_t pair_row_bytes(uint32_t pair, int64_t n) {
+    uint32_t blck, bytes;
+    geometry(pair, blck, bytes);
+    return n / blck * bytes;
+}
+
+GemvLaunch make_launch(const DevState &ds, const void *dw, int64_t n_in, int64_t n_out, float *dy) {
+    GemvLaunch L{};
+    L.w = dw;
+    L.y = dy;
+    L.n_out = n_out;
+    L.n_in = (int)n_in;
+    L.num_sms = ds.sms;
+    L.smem_limit = ds.smem_optin;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    L.device = dev;
+    L.status = ds.status;
+    return L;
+}
+
+int run_gemv(uint32_t wt, GemvLaunch &L, cudaStream_t st) {
+    const int rc = (wt == T_F16) ? launch_gemv_f16(L, st) : launch_gemv(wt, L, st);
+    if (rc == -1) return fail(SICU_ENOTSUP, "matvec: %s row of %d elements does not fit the kernel's shared memory", tname(wt), L.n_in);
+    if (rc == -3) return fail(SICU_ENOTSUP, "matvec: no kernel for %s", tname(wt));
+    if (rc != 0) return cuda_fail(cudaGetLastError(), "matvec launch");
+    return SICU_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int sicu_init(int device) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (device < 0 || device >= MAX_DEV) return fail(SICU_EINVAL, "device %d out of range", device);
+    int count = 0;
+    cudaError_t e = cudaGetDeviceCount(&count);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDeviceCount");
+    if (device >= count) return fail(SICU_EINVAL, "device %d not present (%d devices)", device, count);
+    if ((e = cudaSetDevice(device)) != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+    DevState &ds = g_dev[device];
+    if (ds.ready) return SICU_OK;
+    cudaDeviceProp prop;
+    if ((e = cudaGetDeviceProperties(&prop, device)) != cudaSuccess) return cuda_fail(e, "cudaGetDeviceProperties");
+    if (prop.major != 10 || prop.minor != 0)
+        return fail(SICU_ENOTSUP, "device %d is sm_%d%d; this library is built for sm_100a only", device, prop.major, prop.minor);
+    ds.sms = prop.multiProcessorCount;
+    ds.smem_optin = (int)prop.sharedMemPerBlockOptin;
+    if ((e = cudaMalloc(&ds.status, sizeof(int))) != cudaSuccess) return cuda_fail(e, "cudaMalloc(status)");
+    if ((e = cudaMemset(ds.status, 0, sizeof(int))) != cudaSuccess) return cuda_fail(e, "cudaMemset(status)");
+    ds.ready = true;
+    return SICU_OK;
+}
+
+int sicu_shutdown(void) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    int cur = -1;
+    const bool have = cudaGetDevice(&cur) == cudaSuccess;
+    for (int d = 0; d < MAX_DEV; ++d) {
+        DevState &ds = g_dev[d];
+        if (!ds.ready) continue;
+        cudaSetDevice(d);
+        cudaFree(ds.status);
+        if (ds.stage) cudaFree(ds.stage);
+        ds = DevState{};
+    }
+    if (have && cur >= 0) cudaSetDevice(cur);
+    return SICU_OK;
+}
+
+int sicu_last_error(char *buf, size_t len) {
+    const size_t n = strlen(g_err);
+    if (buf && len) {
+        const size_t c = n < len - 1 ? n : len - 1;
+        memcpy(buf, g_err, c);
+        buf[c] = '\0';
+    }
+    return (int)n;
+}
+
+int sicu_status(int *flags) {
+    if (!flags) return fail(SICU_EINVAL, "null flags");
+    DevState *ds;
+    if (int rc = current(ds)) return rc;
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceSynchronize");
+    if ((e = cudaMemcpy(flags, ds->status, sizeof(int), cudaMemcpyDeviceToHost)) != cudaSuccess)
+        return cuda_fail(e, "read status");
+    if ((e = cudaMemset(ds->status, 0, sizeof(int))) != cudaSuccess) return cuda_fail(e, "clear status");
+    return SICU_OK;
+}
+
+int sicu_malloc(void **dev, size_t bytes) {
+    if (!dev) return fail(SICU_EINVAL, "null out pointer");
+    if (!any_ready()) return fail(SICU_EINVAL, "no device initialised (call sicu_init first)");
+    const cudaError_t e = cudaMalloc(dev, bytes ? bytes : 1);
+    if (e != cudaSuccess) return e == cudaErrorMemoryAllocation ? fail(SICU_ENOMEM, "cudaMalloc(%zu) failed", bytes)
+                                                                : cuda_fail(e, "cudaMalloc");
+    return SICU_OK;
+}
+
+int sicu_free(void *dev) {
+    if (!dev) return SICU_OK;
+    const cudaError_t e = cudaFree(dev);
+    return e == cudaSuccess ? SICU_OK : cuda_fail(e, "cudaFree");
+}
+
+int sicu_upload(const void *host, size_t bytes, void **dev) {
+    if (!host || !dev) return fail(SICU_EINVAL, "upload: null pointer");
+    if (int rc = sicu_malloc(dev, bytes)) return rc;
+    const cudaError_t e = cudaMemcpy(*dev, host, bytes, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+        cudaFree(*dev);
+        *dev = nullptr;
+        return cuda_fail(e, "upload copy");
+    }
+    return SICU_OK;
+}
+
+int sicu_memcpy_h2d(void *dev, const void *host, size_t bytes, void *stream) {
+    if ((!dev || !host) && bytes) return fail(SICU_EINVAL, "memcpy: null pointer");
+    const cudaError_t e = cudaMemcpyAsync(dev, host, bytes, cudaMemcpyHostToDevice, (cudaStream_t)stream);
+    return e == cudaSuccess ? SICU_OK : cuda_fail(e, "memcpy h2d");
+}
+
+int sicu_memcpy_d2h(void *host, const void *dev, size_t bytes, void *stream) {
+    if ((!dev || !host) && bytes) return fail(SICU_EINVAL, "memcpy: null pointer");
+    const cudaError_t e = cudaMemcpyAsync(host, dev, bytes, cudaMemcpyDeviceToHost, (cudaStream_t)stream);
+    return e == cudaSuccess ? SICU_OK : cuda_fail(e, "memcpy d2h");
+}
+
+int sicu_stream_sync(void *stream) {
+    const cudaError_t e = cudaStreamSynchronize((cudaStream_t)stream);
+    return e == cudaSuccess ? SICU_OK : cuda_fail(e, "stream sync");
+}
+
+int sicu_quant_geometry(uint32_t type, uint32_t *blck_size, uint32_t *type_size) {
+    if (!blck_size || !type_size) return fail(SICU_EINVAL, "null out pointer");
+    uint32_t b, s;
+    if (!geometry(type, b, s)) return fail(SICU_ENOTSUP, "unsupported type %u", type);
+    *blck_size = b;
+    *type_size = s;
+    return SICU_OK;
+}
+
+int sicu_vec_dot_pair(uint32_t wtype, uint32_t *pair_type) {
+    if (!pair_type) return fail(SICU_EINVAL, "null out pointer");
+    uint32_t p;
+    if (!pair_of(wtype, p)) return fail(SICU_ENOTSUP, "no dot product for type %s (%u)", tname(wtype), wtype);
+    *pair_type = p;
+    return SICU_OK;
+}
+
+static int quantize_common(uint32_t pair, const float *dx, void *dy, int64_t n, int64_t m, void *stream) {
+    if (int rc = check_activation(pair, dx, dy, n, m)) return rc;
+    DevState *ds;
+    if (int rc = current(ds)) return rc;
+    const int rc = launch_quantize(pair, dx, dy, n, m, (cudaStream_t)stream);
+    if (rc) return cuda_fail(cudaGetLastError(), "quantize launch");
+    return SICU_OK;
+}
+
+int sicu_quantize_q8_K(const float *dx, void *dy, int64_t n, int64_t m, void *stream) {
+    return quantize_common(T_Q8_K, dx, dy, n, m, stream);
+}
+int sicu_quantize_q8_0(const float *dx, void *dy, int64_t n, int64_t m, void *stream) {
+    return quantize_common(T_Q8_0, dx, dy, n, m, stream);
+}
+int sicu_convert_f16(const float *dx, void *dy, int64_t n, int64_t m, void *stream) {
+    return quantize_common(T_F16, dx, dy, n, m, stream);
+}
+int sicu_quantize_pair(uint32_t wtype, const float *dx, void *dxq, int64_t n, int64_t m, void *stream) {
+    uint32_t pair;
+    if (!pair_of(wtype, pair)) return fail(SICU_ENOTSUP, "no dot product for type %s (%u)", tname(wtype), wtype);
+    return quantize_common(pair, dx, dxq, n, m, stream);
+}
+
+int sicu_gemv(uint32_t wtype, const void *dw, int64_t n_in, int64_t n_out, const void *dxq, float *dy, int64_t m,
+              void *stream) {
+    uint32_t pair;
+    if (int rc = check_matvec(wtype, dw, n_in, n_out, dxq, dy, m, pair)) return rc;
+    if (!aligned(dxq, pair == T_Q8_K ? 4 : 2)) return fail(SICU_EINVAL, "matvec: activation misaligned");
+    DevState *ds;
+    if (int rc = current(ds)) return rc;
+    if (n_out == 0) return SICU_OK;
+    const int64_t prb = pair_row_bytes(pair, n_in);
+    for (int64_t i = 0; i < m; ++i) {
+        GemvLaunch L = make_launch(*ds, dw, n_in, n_out, dy + i * n_out);
+        L.xq = static_cast<const uint8_t *>(dxq) + i * prb;
+        if (int rc = run_gemv(wtype, L, (cudaStream_t)stream)) return rc;
+    }
+    return SICU_OK;
+}
+
+int sicu_gemv_f32(uint32_t wtype, const void *dw, int64_t n_in, int64_t n_out, const float *dx, float *dy, int64_t m,
+                  void *stream) {
+    uint32_t pair;
+    if (int rc = check_matvec(wtype, dw, n_in, n_out, dx, dy, m, pair)) return rc;
+    if (!aligned(dx, 16)) return fail(SICU_EINVAL, "matvec: f32 activation must be 16-byte aligned");
+    DevState *ds;
+    if (int rc = current(ds)) return rc;
+    if (n_out == 0) return SICU_OK;
+    for (int64_t i = 0; i < m; ++i) {
+        GemvLaunch L = make_launch(*ds, dw, n_in, n_out, dy + i * n_out);
+        L.xf = dx + i * n_in;
+        if (int rc = run_gemv(wtype, L, (cudaStream_t)stream)) return rc;
+    }
+    return SICU_OK;
+}
+
+int sicu_gemv_host(uint32_t wtype, const void *dw, int64_t n_in, int64_t n_out, const float *hx, float *hy,
+                   void *stream) {
+    uint32_t pair;
+    if (int rc = check_matvec(wtype, dw, n_in, n_out, hx, hy, 1, pair)) return rc;
+    DevState *ds;
+    if (int rc = current(ds)) return rc;
+    const size_t xb = ((size_t)n_in * 4 + 255) & ~size_t(255);
+    const size_t need = xb + (size_t)n_out * 4;
+    cudaError_t e;
+    if (ds->stage_bytes < need) {
+        if (ds->stage) cudaFree(ds->stage);
+        ds->stage = nullptr;
+        ds->stage_bytes = 0;
+        if ((e = cudaMalloc(&ds->stage, need)) != cudaSuccess) return fail(SICU_ENOMEM, "staging alloc of %zu bytes", need);
+        ds->stage_bytes = need;
+    }
+    float *dx = static_cast<float *>(ds->stage);
+    float *dy = reinterpret_cast<float *>(static_cast<uint8_t *>(ds->stage) + xb);
+    const cudaStream_t st = (cudaStream_t)stream;
+    if ((e = cudaMemcpyAsync(dx, hx, (size_t)n_in * 4, cudaMemcpyHostToDevice, st)) != cudaSuccess)
+        return cuda_fail(e, "gemv_host h2d");
+    if (n_out > 0) {
+        GemvLaunch L = make_launch(*ds, dw, n_in, n_out, dy);
+        L.xf = dx;
+        if (int rc = run_gemv(wtype, L, st)) return rc;
+        if ((e = cudaMemcpyAsync(hy, dy, (size_t)n_out * 4, cudaMemcpyDeviceToHost, st)) != cudaSuccess)
+            return cuda_fail(e, "gemv_host d2h");
+    }
+    if ((e = cudaStreamSynchronize(st)) != cudaSuccess) return cuda_fail(e, "gemv_host sync");
+    return SICU_OK;
+}
+
+int sicu_row_to_f32(uint32_t wtype, const void *dw, int64_t n_in, const int64_t *rows, int64_t nrows, float *dout,
+                    void *stream) {
+    uint32_t blck, bytes;
+    if (!geometry(wtype, blck, bytes) || wtype == T_F32 || wtype == T_Q8_K)
+        return fail(SICU_ENOTSUP, "row_to_f32: unsupported type %s (%u)", tname(wtype), wtype);
+    if (n_in <= 0 || nrows < 0 || n_in % blck) return fail(SICU_EINVAL, "row_to_f32: bad shape");
+    if (nrows > 65535) return fail(SICU_EINVAL, "row_to_f32: at most 65535 rows per call");
+    if (!dw || !dout || (nrows && !rows)) return fail(SICU_EINVAL, "row_to_f32: null pointer");
+    DevState *ds;
+    if (int rc = current(ds)) return rc;
+    if (nrows == 0) return SICU_OK;
+    const size_t need = (size_t)nrows * sizeof(int64_t);
+    cudaError_t e;
+    // the row list rides in the staging buffer's tail-free head
+    if (ds->stage_bytes < need) {
+        if (ds->stage) cudaFree(ds->stage);
+        ds->stage = nullptr;
+        ds->stage_bytes = 0;
+        if ((e = cudaMalloc(&ds->stage, need)) != cudaSuccess) return fail(SICU_ENOMEM, "staging alloc");
+        ds->stage_bytes = need;
+    }
+    const cudaStream_t st = (cudaStream_t)stream;
+    if ((e = cudaMemcpyAsync(ds->stage, rows, need, cudaMemcpyHostToDevice, st)) != cudaSuccess)
+        return cuda_fail(e, "row list copy");
+    const int rc = launch_dequant(wtype, dw, n_in, static_cast<const int64_t *>(ds->stage), nrows, dout, st);
+    if (rc) return cuda_fail(cudaGetLastError(), "dequant launch");
+    // the row list must stay put until the kernel read it
+    if ((e = cudaStreamSynchronize(st)) != cudaSuccess) return cuda_fail(e, "row_to_f32 sync");
+    return SICU_OK;
+}
+
+}  // extern "C"

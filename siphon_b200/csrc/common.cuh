@@ -1,0 +1,171 @@
+// Shared device helpers for libsiphon_cuda: block geometry, exact f16
+// conversions, and thin inline-PTX wrappers (integer dot products, byte
+// permutes, mbarriers, 1-D bulk TMA copies). sm_100a only.
+#pragma once
+
+#include <cstdint>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+namespace sicu {
+
+// ggml type ids as stored in GGUF (reference include/siphon/quant.h:103-119)
+enum : uint32_t {
+    T_F32 = 0, T_F16 = 1, T_Q4_0 = 2, T_Q5_0 = 6, T_Q8_0 = 8,
+    T_Q2_K = 10, T_Q3_K = 11, T_Q4_K = 12, T_Q5_K = 13, T_Q6_K = 14, T_Q8_K = 15,
+};
+
+// on-disk block sizes (reference include/siphon/quant.h:92-100)
+constexpr int QK_K = 256, QK8_0 = 32;
+constexpr int B_Q4_0 = 18, B_Q5_0 = 22, B_Q8_0 = 34, B_Q2_K = 84, B_Q3_K = 110;
+constexpr int B_Q4_K = 144, B_Q5_K = 176, B_Q6_K = 210, B_Q8_K = 292;
+
+// device status word: set by a kernel whose bounded wait gave up
+constexpr int STATUS_WAIT_TIMEOUT = 1;
+
+// ---- f16 ---------------------------------------------------------------------
+// f16 -> f32 is exact in hardware for every finite half and inf.
+__device__ __forceinline__ float h2f(uint32_t h16) {
+    return __half2float(__ushort_as_half(static_cast<unsigned short>(h16)));
+}
+
+// f32 -> f16, round to nearest even. Finite values and inf go through the
+// hardware conversion (IEEE RNE, overflow to inf); a NaN maps to
+// sign|0x7c00|0x0200|payload>>13 with the payload forced non-zero, which is
+// what the reference's software conversion produces (src/kernels.c:133-142).
+__device__ __forceinline__ uint16_t f2h(float f) {
+    const uint32_t u = __float_as_uint(f);
+    if ((u & 0x7f800000u) == 0x7f800000u && (u & 0x7fffffu)) {
+        uint32_t p = (u & 0x7fffffu) >> 13;
+        if (p == 0) p = 1;
+        return static_cast<uint16_t>(((u >> 16) & 0x8000u) | 0x7c00u | 0x0200u | p);
+    }
+    return __half_as_ushort(__float2half_rn(f));
+}
+
+// ---- integer SIMD ------------------------------------------------------------
+__device__ __forceinline__ int dp4a(uint32_t a, uint32_t b, int c) {  // u8 x s8
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+__device__ __forceinline__ int dp4a_ss(uint32_t a, uint32_t b, int c) {  // s8 x s8
+    int d;
+    asm("dp4a.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+// a: two s16, b: four s8; .lo pairs a with bytes 0,1 of b, .hi with bytes 2,3
+__device__ __forceinline__ int dp2a_lo(uint32_t a, uint32_t b, int c) {
+    int d;
+    asm("dp2a.lo.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+__device__ __forceinline__ int dp2a_hi(uint32_t a, uint32_t b, int c) {
+    int d;
+    asm("dp2a.hi.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+    uint32_t d;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+    return d;
+}
+// (a & b) | c
+__device__ __forceinline__ uint32_t and_or(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t d;
+    asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+// (a & b) ^ c
+__device__ __forceinline__ uint32_t and_xor(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t d;
+    asm("lop3.b32 %0, %1, %2, %3, 0x6A;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+// 4x4 byte transpose: out[c] byte k = in[k] byte c.
+__device__ __forceinline__ void transpose4(uint32_t r0, uint32_t r1, uint32_t r2, uint32_t r3,
+                                           uint32_t &t0, uint32_t &t1, uint32_t &t2, uint32_t &t3) {
+    const uint32_t a = prmt(r0, r1, 0x5140), b = prmt(r0, r1, 0x7362);
+    const uint32_t c = prmt(r2, r3, 0x5140), d = prmt(r2, r3, 0x7362);
+    t0 = prmt(a, c, 0x5410);
+    t1 = prmt(a, c, 0x7632);
+    t2 = prmt(b, d, 0x5410);
+    t3 = prmt(b, d, 0x7632);
+}
+
+__device__ __forceinline__ uint32_t funnel(uint32_t lo, uint32_t hi, uint32_t sh) {
+    return __funnelshift_r(lo, hi, sh);
+}
+
+// ---- shared memory / async copies -------------------------------------------
+__device__ __forceinline__ uint32_t smem_addr(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ uint32_t lds32(uint32_t a) {
+    uint32_t v;
+    asm volatile("ld.shared.b32 %0, [%1];" : "=r"(v) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ uint4 lds128(uint32_t a) {
+    uint4 v;
+    asm volatile("ld.shared.v4.b32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+    return v;
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" :: "r"(bar), "r"(count));
+}
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void fence_proxy_async() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" :: "r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
+    return ok != 0;
+}
+// Bounded wait: gives up after `limit` polls (each try_wait itself suspends
+// for a hardware-defined slice) and reports false.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, uint32_t limit = 1u << 24) {
+    for (uint32_t i = 0; i < limit; ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+    }
+    return false;
+}
+// 1-D bulk copy global -> this CTA's shared memory, completion counted in
+// bytes on `bar`. dst, src and bytes must be multiples of 16.
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+        :: "r"(dst), "l"(src), "r"(bytes), "r"(bar) : "memory");
+}
+__device__ __forceinline__ void bulk_g2s_hint(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar,
+                                              uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;"
+        :: "r"(dst), "l"(src), "r"(bytes), "r"(bar), "l"(policy) : "memory");
+}
+__device__ __forceinline__ uint64_t policy_evict_first() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
+__device__ __forceinline__ uint32_t ldg_u8(const uint8_t *p) {
+    uint16_t v;
+    asm volatile("ld.global.nc.u8 %0, [%1];" : "=h"(v) : "l"(p));
+    return v;
+}
+
+}  // namespace sicu

@@ -1,0 +1,456 @@
+// Batch-1 decode matvec y = W x for GGUF block formats, bit-exact with the
+// reference's scalar dot products (src/kernels.c:197-523).
+//
+// Structure (one persistent CTA per SM, 8 warps):
+//   * Work is split into tasks of R consecutive rows; long rows are streamed
+//     in chunks of CU "units" (a unit is one K super-block, or eight classic
+//     32-blocks = 256 elements). Tasks are dealt to CTAs in balanced
+//     contiguous ranges and to warps round-robin.
+//   * Each warp owns an S-slot ring in shared memory. Lane 0 fills slots with
+//     1-D bulk TMA copies (cp.async.bulk + mbarrier transaction counts); the
+//     raw GGUF bytes are never re-laid-out in HBM.
+//   * Phase 1: lanes decode one unit each (nibbles, high bits, 6-bit scales in
+//     registers), run int8 dot products (dp4a / dp2a), and emit the float
+//     terms the reference's scalar loop adds per block.
+//   * Phase 2: one lane per float chain adds those terms in the reference's
+//     order with __fadd_rn / __fsub_rn, so every output is bit-identical.
+//
+// Exactness: the reference keeps, for the K formats with int8 lane
+// accumulators, eight per-lane integer sums aux32[l] over elements l mod 8
+// (src/kernels.c:384-409). Integer sums are order-free, so the kernel forms
+// them with byte transposes (prmt) that gather same-l elements into one
+// dp4a / dp2a operand; only the float chain is order-bound.
+#pragma once
+
+#include "common.cuh"
+
+namespace sicu {
+
+constexpr int GEMV_WARPS = 8;
+constexpr int ACT_STRIDE = 272;    // bytes per prepared 256-element activation unit (17 x 16 B)
+constexpr int MAX_CHAINS = 9;
+constexpr int TERM_FLOATS = 32 * MAX_CHAINS;   // >= 32 units x 9 chains, >= 32 units x 8 blocks
+constexpr int WARP_HDR = 64 + 4 * (TERM_FLOATS + 64) + 64;   // barriers, terms, chain results (128-aligned)
+
+struct GemvParams {
+    const uint8_t *w;      // weight blocks, row-major, 16-byte aligned base
+    const uint8_t *xq;     // pair-format activation (Q8_K / Q8_0 blocks), or null
+    const float *xf;       // f32 activation for the fused quantize variant, or null
+    float *y;
+    int64_t row_bytes;
+    int64_t n_out;
+    int n_in;
+    int nu;                // units per row
+    int cu;                // units per chunk
+    int nchunks;           // chunks per row (1 unless R == 1)
+    int rows_per_task;     // R
+    int64_t ntasks;
+    int slot_bytes;
+    int nslots;
+    int act_bytes;         // prepared-activation region
+    int warp_bytes;        // per-warp region (barriers, terms, ring)
+    int *status;
+};
+
+// ---------------------------------------------------------------------------
+// Prepared activation layout (shared memory, one record per 256-element unit)
+//   aq : 64 words of int8 quants in the order the format's unit decoder wants
+//   ad : K formats: Q8_K d; classic: 8 per-block f32 scales
+//   ax : K formats: extra integer sums; classic: 8 per-block quant sums
+// ---------------------------------------------------------------------------
+struct ActView {
+    uint8_t *base;
+    int nu;
+    __device__ uint8_t *aq(int u) const { return base + (size_t)u * ACT_STRIDE; }
+    __device__ float *ad(int u) const { return reinterpret_cast<float *>(base + (size_t)nu * ACT_STRIDE) + u * 8; }
+    __device__ int *ax(int u) const {
+        return reinterpret_cast<int *>(base + (size_t)nu * ACT_STRIDE + (size_t)nu * 32) + u * 16;
+    }
+    static __host__ __device__ int bytes(int nu) { return nu * (ACT_STRIDE + 32 + 64); }
+};
+
+// ---- format traits ----------------------------------------------------------
+// kind: 0 = K format, lane sums (9 chains: 8 lanes + dmin), 1 = K format,
+// lane sums without mins (8 chains), 2 = one chain per super-block (Q2_K),
+// 3 = classic 32-blocks (one chain, eight terms per unit)
+template <uint32_t T> struct Fmt;
+template <> struct Fmt<T_Q4_K> { static constexpr int kind = 0, unit_bytes = B_Q4_K, chains = 9, tpu = 1, act = 0; };
+template <> struct Fmt<T_Q5_K> { static constexpr int kind = 0, unit_bytes = B_Q5_K, chains = 9, tpu = 1, act = 0; };
+template <> struct Fmt<T_Q6_K> { static constexpr int kind = 1, unit_bytes = B_Q6_K, chains = 8, tpu = 1, act = 1; };
+template <> struct Fmt<T_Q3_K> { static constexpr int kind = 1, unit_bytes = B_Q3_K, chains = 8, tpu = 1, act = 1; };
+template <> struct Fmt<T_Q2_K> { static constexpr int kind = 2, unit_bytes = B_Q2_K, chains = 1, tpu = 1, act = 2; };
+template <> struct Fmt<T_Q4_0> { static constexpr int kind = 3, unit_bytes = 8 * B_Q4_0, chains = 1, tpu = 8, act = 3; };
+template <> struct Fmt<T_Q5_0> { static constexpr int kind = 3, unit_bytes = 8 * B_Q5_0, chains = 1, tpu = 8, act = 3; };
+template <> struct Fmt<T_Q8_0> { static constexpr int kind = 3, unit_bytes = 8 * B_Q8_0, chains = 1, tpu = 8, act = 3; };
+
+// ---------------------------------------------------------------------------
+// Activation preparation (every CTA builds its own copy in shared memory).
+//   act 0 (Q4_K, Q5_K): per 32-element sub-block j, word l holds the quants of
+//         elements l, l+8, l+16, l+24 (the reference's lane-l elements);
+//         ax[k] = bsums[2k] + bsums[2k+1] (the per-32 sums the mins use).
+//   act 1 (Q3_K, Q6_K): per 16-element sub-block j, word q holds elements
+//         q, q+8 (dp2a.lo half) and q+4, q+12 (dp2a.hi half).
+//   act 2 (Q2_K): natural order; ax = the 16 bsums.
+//   act 3 (classic): natural order, ad = f16 block scale as f32, ax = sum of
+//         the block's 32 quants.
+// src points at the raw pair-format row (global or shared memory).
+// ---------------------------------------------------------------------------
+// K formats: prepare 32-element piece j of super-block u from a raw Q8_K block.
+template <int ACT>
+__device__ __forceinline__ void prep_piece(const ActView av, const uint8_t *blk, int u, int j) {
+    const uint32_t *qs = reinterpret_cast<const uint32_t *>(blk + 4 + 32 * j);
+    uint32_t v[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) v[k] = qs[k];
+    uint32_t *dst = reinterpret_cast<uint32_t *>(av.aq(u)) + 8 * j;
+    if constexpr (ACT == 0) {
+        transpose4(v[0], v[2], v[4], v[6], dst[0], dst[1], dst[2], dst[3]);
+        transpose4(v[1], v[3], v[5], v[7], dst[4], dst[5], dst[6], dst[7]);
+    } else if constexpr (ACT == 1) {
+        // two 16-element sub-blocks: words (v0,v1,v2,v3) = elements 0..15
+        transpose4(v[0], v[2], v[1], v[3], dst[0], dst[1], dst[2], dst[3]);
+        transpose4(v[4], v[6], v[5], v[7], dst[4], dst[5], dst[6], dst[7]);
+    } else {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) dst[k] = v[k];
+    }
+    if (j == 0) {
+        av.ad(u)[0] = *reinterpret_cast<const float *>(blk);
+        const int16_t *bs = reinterpret_cast<const int16_t *>(blk + 260);
+        if constexpr (ACT == 0) {
+#pragma unroll
+            for (int k = 0; k < 8; ++k) av.ax(u)[k] = (int)bs[2 * k] + (int)bs[2 * k + 1];
+        } else if constexpr (ACT == 2) {
+#pragma unroll
+            for (int k = 0; k < 16; ++k) av.ax(u)[k] = bs[k];
+        }
+    }
+}
+
+// Build the prepared layout from the caller's pair-format row (global memory).
+template <int ACT>
+__device__ void prep_activation(const ActView av, const uint8_t *src, int n_in) {
+    const int tid = threadIdx.x, nt = blockDim.x;
+    if constexpr (ACT == 3) {
+        const int nblk = n_in / 32;
+        for (int b = tid; b < nblk; b += nt) {
+            // qs start at byte 2 of a 34-byte block: read halves and rejoin
+            const uint16_t *h = reinterpret_cast<const uint16_t *>(src + (size_t)b * B_Q8_0);
+            uint32_t wv[8];
+            int s = 0;
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                wv[k] = (uint32_t)h[1 + 2 * k] | ((uint32_t)h[2 + 2 * k] << 16);
+                s = dp4a_ss(wv[k], 0x01010101u, s);
+            }
+            const int u = b >> 3, bi = b & 7;
+            uint32_t *dst = reinterpret_cast<uint32_t *>(av.aq(u)) + bi * 8;
+#pragma unroll
+            for (int k = 0; k < 8; ++k) dst[k] = wv[k];
+            av.ad(u)[bi] = h2f(h[0]);
+            av.ax(u)[bi] = s;
+        }
+    } else {
+        for (int p = tid; p < (n_in / 256) * 8; p += nt) {
+            const int u = p >> 3;
+            prep_piece<ACT>(av, src + (size_t)u * B_Q8_K, u, p & 7);
+        }
+    }
+}
+
+// ---- unit decoders ------------------------------------------------------------
+// Each computes the float term(s) one super-block (or eight 32-blocks) of one
+// weight row contributes, exactly as the reference computes them before the
+// running sums: t[0..chains-1] (K formats) or t[0..7] (classic, per block).
+
+__device__ __forceinline__ uint32_t byte_of(uint32_t w, int i) { return (w >> (8 * i)) & 0xffu; }
+__device__ __forceinline__ int sbyte_of(uint32_t w, int i) { return ((int)(w << (24 - 8 * i))) >> 24; }
+
+// Q4_K (src/kernels.c:349-410): 16-byte aligned in shared memory.
+template <bool Q5>
+__device__ __forceinline__ void unit_q45k(const uint8_t *wb, const uint8_t *aq, float yd, const int *pb, float *t) {
+    const uint4 h = *reinterpret_cast<const uint4 *>(wb);
+    // 6-bit scales/mins (src/kernels.c:377-382 / 648-656), four per word
+    const uint32_t sc_lo = h.y & 0x3f3f3f3fu;
+    const uint32_t mn_lo = h.z & 0x3f3f3f3fu;
+    const uint32_t sc_hi = (h.w & 0x0f0f0f0fu) | ((h.y >> 2) & 0x30303030u);
+    const uint32_t mn_hi = ((h.w >> 4) & 0x0f0f0f0fu) | ((h.z >> 2) & 0x30303030u);
+
+    constexpr int QS = Q5 ? 48 : 16;
+    uint32_t ht[8];
+    if constexpr (Q5) {
+        const uint4 h0 = *reinterpret_cast<const uint4 *>(wb + 16);
+        const uint4 h1 = *reinterpret_cast<const uint4 *>(wb + 32);
+        transpose4(h0.x, h0.z, h1.x, h1.z, ht[0], ht[1], ht[2], ht[3]);
+        transpose4(h0.y, h0.w, h1.y, h1.w, ht[4], ht[5], ht[6], ht[7]);
+    }
+    int aux[8];
+#pragma unroll
+    for (int l = 0; l < 8; ++l) aux[l] = 0;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        const uint4 qa = *reinterpret_cast<const uint4 *>(wb + QS + 32 * c);
+        const uint4 qb = *reinterpret_cast<const uint4 *>(wb + QS + 32 * c + 16);
+        uint32_t tq[8];
+        transpose4(qa.x, qa.z, qb.x, qb.z, tq[0], tq[1], tq[2], tq[3]);
+        transpose4(qa.y, qa.w, qb.y, qb.w, tq[4], tq[5], tq[6], tq[7]);
+        const uint4 a0 = *reinterpret_cast<const uint4 *>(aq + 64 * c);
+        const uint4 a1 = *reinterpret_cast<const uint4 *>(aq + 64 * c + 16);
+        const uint4 a2 = *reinterpret_cast<const uint4 *>(aq + 64 * c + 32);
+        const uint4 a3 = *reinterpret_cast<const uint4 *>(aq + 64 * c + 48);
+        const uint32_t alo[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+        const uint32_t ahi[8] = {a2.x, a2.y, a2.z, a2.w, a3.x, a3.y, a3.z, a3.w};
+        const uint32_t scw = c < 2 ? sc_lo : sc_hi;
+        const int s0 = (int)byte_of(scw, (2 * c) & 3), s1 = (int)byte_of(scw, (2 * c + 1) & 3);
+#pragma unroll
+        for (int l = 0; l < 8; ++l) {
+            uint32_t lo = tq[l] & 0x0f0f0f0fu;
+            uint32_t hi = (tq[l] >> 4) & 0x0f0f0f0fu;
+            if constexpr (Q5) {
+                // fifth bit of sub-block 2c / 2c+1 is bit 2c / 2c+1 of qh[b]
+                const uint32_t b0 = (c <= 2 ? (ht[l] << (4 - 2 * c)) : (ht[l] >> (2 * c - 4))) & 0x10101010u;
+                const uint32_t b1 = (c <= 1 ? (ht[l] << (3 - 2 * c)) : (ht[l] >> (2 * c - 3))) & 0x10101010u;
+                lo |= b0;
+                hi |= b1;
+            }
+            aux[l] += dp4a(lo, alo[l], 0) * s0 + dp4a(hi, ahi[l], 0) * s1;
+        }
+    }
+    const int mins = (int)byte_of(mn_lo, 0) * pb[0] + (int)byte_of(mn_lo, 1) * pb[1] +
+                     (int)byte_of(mn_lo, 2) * pb[2] + (int)byte_of(mn_lo, 3) * pb[3] +
+                     (int)byte_of(mn_hi, 0) * pb[4] + (int)byte_of(mn_hi, 1) * pb[5] +
+                     (int)byte_of(mn_hi, 2) * pb[6] + (int)byte_of(mn_hi, 3) * pb[7];
+    const float d = __fmul_rn(h2f(h.x & 0xffffu), yd);
+#pragma unroll
+    for (int l = 0; l < 8; ++l) t[l] = __fmul_rn(d, __int2float_rn(aux[l]));
+    t[8] = __fmul_rn(__fmul_rn(h2f(h.x >> 16), yd), __int2float_rn(mins));
+}
+
+// Realigned 32-bit reads from a 2-byte aligned shared address.
+struct Words {
+    const uint32_t *p;
+    uint32_t sh;
+    __device__ Words(const uint8_t *addr) {
+        const uintptr_t a = reinterpret_cast<uintptr_t>(addr);
+        p = reinterpret_cast<const uint32_t *>(a & ~uintptr_t(3));
+        sh = (uint32_t)(a & 3) * 8;
+    }
+    __device__ __forceinline__ uint32_t operator[](int k) const { return funnel(p[k], p[k + 1], sh); }
+};
+
+// sign-extending pair selectors: int16 {byte b of x, byte b of y}
+__device__ __forceinline__ uint32_t pair_sel(int b) {
+    return (uint32_t)(b | ((b | 8) << 4) | ((4 + b) << 8) | (((4 + b) | 8) << 12));
+}
+
+// Q6_K (src/kernels.c:480-523) and Q3_K (src/kernels.c:289-347): 16-element
+// sub-blocks, int8 quants built as 4*v (Q6_K) / 32*v (Q3_K) so the sign sits
+// in bit 7, paired by element (e, e+8) into int16 for dp2a.
+template <bool Q3>
+__device__ __forceinline__ void unit_q36k(const uint8_t *wb, const uint8_t *aq, float yd, float *t) {
+    const Words W(wb);
+    int aux[8];
+#pragma unroll
+    for (int l = 0; l < 8; ++l) aux[l] = 0;
+    // scales: 16 signed values, sub-block j
+    int sc[16];
+    float dx;
+    if constexpr (Q3) {
+        const uint32_t s0 = W[24], s1 = W[25], s2 = W[26];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            const uint32_t lo = j < 8 ? (byte_of(j < 4 ? s0 : s1, j & 3) & 15u) : (byte_of(j < 12 ? s0 : s1, j & 3) >> 4);
+            const uint32_t hi = (byte_of(s2, j & 3) >> (2 * (j / 4))) & 3u;
+            sc[j] = (int)(lo | (hi << 4)) - 32;
+        }
+        dx = h2f(W[27] & 0xffffu);
+    } else {
+        const uint32_t s[4] = {W[48], W[49], W[50], W[51]};
+#pragma unroll
+        for (int j = 0; j < 16; ++j) sc[j] = sbyte_of(s[j / 4], j & 3);
+        dx = h2f(W[52] & 0xffffu);
+    }
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        // element words E[g][k]: elements 128h + 32g + 4k .. +3
+        uint32_t E[4][8];
+        if constexpr (Q3) {
+            uint32_t HM[8], QS[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) { HM[k] = W[k]; QS[k] = W[8 + 8 * h + k]; }
+#pragma unroll
+            for (int g = 0; g < 4; ++g) {
+                const int p = 4 * h + g;   // hmask bit
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                    const uint32_t qs = (5 - 2 * g) >= 0 ? (QS[k] << (5 - 2 * g)) : (QS[k] >> 1);
+                    const uint32_t hb = and_xor(HM[k] << (7 - p), 0x80808080u, 0x80808080u);
+                    E[g][k] = and_or(qs, 0x60606060u, hb);
+                }
+            }
+        } else {
+            uint32_t QL[16], QH[8];
+#pragma unroll
+            for (int k = 0; k < 16; ++k) QL[k] = W[16 * h + k];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) QH[k] = W[32 + 8 * h + k];
+#pragma unroll
+            for (int g = 0; g < 4; ++g) {
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                    const uint32_t ql = QL[(g & 1) ? 8 + k : k];
+                    const uint32_t lo = g < 2 ? (ql << 2) : (ql >> 2);
+                    const uint32_t hi = and_xor(QH[k] << (6 - 2 * g), 0xc0c0c0c0u, 0x80808080u);
+                    E[g][k] = and_or(lo, 0x3c3c3c3cu, hi);
+                }
+            }
+        }
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+#pragma unroll
+            for (int k4 = 0; k4 < 2; ++k4) {
+                const int j = 8 * h + 2 * g + k4;
+                const uint4 aw = *reinterpret_cast<const uint4 *>(aq + 16 * j);
+                const uint32_t awv[4] = {aw.x, aw.y, aw.z, aw.w};
+                const uint32_t e0 = E[g][4 * k4], e1 = E[g][4 * k4 + 1], e2 = E[g][4 * k4 + 2], e3 = E[g][4 * k4 + 3];
+#pragma unroll
+                for (int b = 0; b < 4; ++b) {
+                    const uint32_t plo = prmt(e0, e2, pair_sel(b));   // lane b
+                    const uint32_t phi = prmt(e1, e3, pair_sel(b));   // lane 4+b
+                    aux[b] += sc[j] * dp2a_lo(plo, awv[b], 0);
+                    aux[4 + b] += sc[j] * dp2a_hi(phi, awv[b], 0);
+                }
+            }
+        }
+    }
+    const float d = __fmul_rn(dx, yd);
+#pragma unroll
+    for (int l = 0; l < 8; ++l) t[l] = __fmul_rn(d, __int2float_rn(aux[l] >> (Q3 ? 5 : 2)));
+}
+
+// Q2_K (src/kernels.c:249-287): one integer sum per super-block. 4-byte aligned.
+__device__ __forceinline__ void unit_q2k(const uint8_t *wb, const uint8_t *aq, float yd, const int *bs, float *t) {
+    const uint32_t *w = reinterpret_cast<const uint32_t *>(wb);
+    const uint32_t scw[4] = {w[0], w[1], w[2], w[3]};
+    int isum = 0;
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+        uint32_t QS[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) QS[i] = w[4 + 8 * k + i];
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) {
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh) {
+                const int is = 8 * k + 2 * jj + hh;
+                const uint4 a = *reinterpret_cast<const uint4 *>(aq + 4 * (32 * k + 8 * jj + 4 * hh));
+                const uint32_t av[4] = {a.x, a.y, a.z, a.w};
+                int s = 0;
+#pragma unroll
+                for (int m = 0; m < 4; ++m) s = dp4a((QS[4 * hh + m] >> (2 * jj)) & 0x03030303u, av[m], s);
+                isum += (int)(byte_of(scw[is / 4], is & 3) & 15u) * s;
+            }
+        }
+    }
+    int summs = 0;
+#pragma unroll
+    for (int g = 0; g < 16; ++g) summs += bs[g] * (int)(byte_of(scw[g / 4], g & 3) >> 4);
+    const uint32_t dd = w[20];
+    const float dall = __fmul_rn(yd, h2f(dd & 0xffffu));
+    const float dmin = __fmul_rn(yd, h2f(dd >> 16));
+    t[0] = __fsub_rn(__fmul_rn(dall, __int2float_rn(isum)), __fmul_rn(dmin, __int2float_rn(summs)));
+}
+
+// Classic 32-blocks (src/kernels.c:197-247): up to eight blocks per unit,
+// 2-byte aligned. Terms: Q4_0/Q5_0 (sumi*dx)*dy, Q8_0 sumi*(dx*dy).
+template <uint32_t T>
+__device__ __forceinline__ void unit_classic(const uint8_t *wb, int nblk, const uint8_t *aq, const float *dy,
+                                             const int *asum, float *t) {
+    const Words W(wb);
+    constexpr int BW = (T == T_Q4_0) ? 9 : (T == T_Q5_0) ? 11 : 17;   // words per block pair
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+            const int b = 2 * p + half;
+            if (b < nblk) {
+                const uint4 a0 = *reinterpret_cast<const uint4 *>(aq + 32 * b);
+                const uint4 a1 = *reinterpret_cast<const uint4 *>(aq + 32 * b + 16);
+                const uint32_t av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+                const int base = BW * p;
+                uint32_t d16;
+                int s = 0;
+                if constexpr (T == T_Q4_0) {
+                    // pair: [d0 qs0(16)] [d1 qs1(16)], 36 bytes
+                    uint32_t q[4];
+                    if (half == 0) {
+                        const uint32_t x0 = W[base];
+                        d16 = x0 & 0xffffu;
+                        uint32_t prev = x0;
+#pragma unroll
+                        for (int m = 0; m < 4; ++m) { const uint32_t nx = W[base + 1 + m]; q[m] = funnel(prev, nx, 16); prev = nx; }
+                    } else {
+                        d16 = W[base + 4] >> 16;
+#pragma unroll
+                        for (int m = 0; m < 4; ++m) q[m] = W[base + 5 + m];
+                    }
+#pragma unroll
+                    for (int m = 0; m < 4; ++m) {
+                        s = dp4a(q[m] & 0x0f0f0f0fu, av[m], s);
+                        s = dp4a((q[m] >> 4) & 0x0f0f0f0fu, av[4 + m], s);
+                    }
+                    s -= 8 * asum[b];
+                } else if constexpr (T == T_Q5_0) {
+                    // pair: [d0 qh0(4) qs0(16)] [d1 qh1 qs1], 44 bytes
+                    uint32_t q[4], qh;
+                    if (half == 0) {
+                        const uint32_t x0 = W[base], x1 = W[base + 1];
+                        d16 = x0 & 0xffffu;
+                        qh = funnel(x0, x1, 16);
+                        uint32_t prev = x1;
+#pragma unroll
+                        for (int m = 0; m < 4; ++m) { const uint32_t nx = W[base + 2 + m]; q[m] = funnel(prev, nx, 16); prev = nx; }
+                    } else {
+                        d16 = W[base + 5] >> 16;
+                        qh = W[base + 6];
+#pragma unroll
+                        for (int m = 0; m < 4; ++m) q[m] = W[base + 7 + m];
+                    }
+#pragma unroll
+                    for (int m = 0; m < 4; ++m) {
+                        // bits 4m..4m+3 (low nibbles) and 16+4m.. (high) of qh to bit 4 of each byte
+                        const uint32_t b_lo = (((qh >> (4 * m)) & 15u) * 0x02040810u) & 0x10101010u;
+                        const uint32_t b_hi = (((qh >> (16 + 4 * m)) & 15u) * 0x02040810u) & 0x10101010u;
+                        s = dp4a(and_or(q[m], 0x0f0f0f0fu, b_lo), av[m], s);
+                        s = dp4a(and_or(q[m] >> 4, 0x0f0f0f0fu, b_hi), av[4 + m], s);
+                    }
+                    s -= 16 * asum[b];
+                } else {
+                    // Q8_0 pair: [d0 qs0(32)] [d1 qs1(32)], 68 bytes
+                    uint32_t q[8];
+                    if (half == 0) {
+                        const uint32_t x0 = W[base];
+                        d16 = x0 & 0xffffu;
+                        uint32_t prev = x0;
+#pragma unroll
+                        for (int m = 0; m < 8; ++m) { const uint32_t nx = W[base + 1 + m]; q[m] = funnel(prev, nx, 16); prev = nx; }
+                    } else {
+                        d16 = W[base + 8] >> 16;
+#pragma unroll
+                        for (int m = 0; m < 8; ++m) q[m] = W[base + 9 + m];
+                    }
+#pragma unroll
+                    for (int m = 0; m < 8; ++m) s = dp4a_ss(q[m], av[m], s);
+                }
+                const float dx = h2f(d16);
+                if constexpr (T == T_Q8_0) {
+                    t[b] = __fmul_rn(__int2float_rn(s), __fmul_rn(dx, dy[b]));
+                } else {
+                    t[b] = __fmul_rn(__fmul_rn(__int2float_rn(s), dx), dy[b]);
+                }
+            }
+        }
+    }
+}
+
+}  // namespace sicu

@@ -1,0 +1,35 @@
+// Host-side launch helpers shared by the kernels' translation units and the
+// C ABI (abi.cu). Return 0 on success, negative on a launch problem.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace sicu {
+
+struct GemvLaunch {
+    const void *w;        // weight blocks (device)
+    const void *xq;       // pair-format activation (device) or null
+    const float *xf;      // f32 activation (device) for the fused quantizer, or null
+    float *y;             // [n_out] (device)
+    int64_t n_out;
+    int n_in;
+    int num_sms;
+    int smem_limit;       // opt-in dynamic shared memory per block
+    int device;
+    int *status;          // device status word
+};
+
+// quantized formats (K and classic); fails with -3 for other types
+int launch_gemv(uint32_t wtype, const GemvLaunch &L, cudaStream_t st);
+// F16 weights (pair activation: f16 row, or f32 converted in the kernel)
+int launch_gemv_f16(const GemvLaunch &L, cudaStream_t st);
+
+// activation conversion of m rows of n floats into the pair format
+int launch_quantize(uint32_t pair, const float *x, void *y, int64_t n, int64_t m, cudaStream_t st);
+
+// dequantise rows (row_to_f32): rows[i] of w into out[i * n_in]
+int launch_dequant(uint32_t wtype, const void *w, int64_t n_in, const int64_t *rows_dev, int64_t nrows,
+                   float *out, cudaStream_t st);
+
+}  // namespace sicu

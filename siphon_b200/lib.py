@@ -1,0 +1,161 @@
+"""ctypes binding of libsiphon_cuda.so (the C ABI in include/siphon_cuda.h).
+
+This is the Python mirror of the reference's backend interface for the
+quantized matrix path: ``gemv`` / ``gemv_f32`` / ``gemv_host`` stand where
+``si_backend.gemv`` (include/siphon/tensor.h:43-55) stands, ``quantize_*``
+where ``si_quant_row_q8_K`` / ``si_quant_row_q8_0`` stand, ``row_to_f32``
+where ``si_backend.row_to_f32`` stands. Errors raise :class:`SicuError`
+carrying the reference-style negative code and the library's message.
+
+There is no fallback: if the shared library is missing the import of any
+compute entry point raises.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+from pathlib import Path
+
+from . import quant as Q
+
+LIB_PATH = Path(__file__).resolve().parent / "libsiphon_cuda.so"
+
+SICU_OK, SICU_ENOMEM, SICU_EIO, SICU_EFORMAT, SICU_ENOTSUP, SICU_EINVAL = 0, -1, -2, -3, -4, -5
+
+# every entry point of include/siphon_cuda.h with its ctypes signature
+_i64, _u32, _vp, _fp = C.c_int64, C.c_uint32, C.c_void_p, C.c_void_p
+SIGNATURES = {
+    "sicu_init": [C.c_int],
+    "sicu_shutdown": [],
+    "sicu_last_error": [C.c_char_p, C.c_size_t],
+    "sicu_status": [C.POINTER(C.c_int)],
+    "sicu_malloc": [C.POINTER(C.c_void_p), C.c_size_t],
+    "sicu_free": [_vp],
+    "sicu_upload": [_vp, C.c_size_t, C.POINTER(C.c_void_p)],
+    "sicu_memcpy_h2d": [_vp, _vp, C.c_size_t, _vp],
+    "sicu_memcpy_d2h": [_vp, _vp, C.c_size_t, _vp],
+    "sicu_stream_sync": [_vp],
+    "sicu_quant_geometry": [_u32, C.POINTER(C.c_uint32), C.POINTER(C.c_uint32)],
+    "sicu_vec_dot_pair": [_u32, C.POINTER(C.c_uint32)],
+    "sicu_quantize_q8_K": [_fp, _vp, _i64, _i64, _vp],
+    "sicu_quantize_q8_0": [_fp, _vp, _i64, _i64, _vp],
+    "sicu_convert_f16": [_fp, _vp, _i64, _i64, _vp],
+    "sicu_quantize_pair": [_u32, _fp, _vp, _i64, _i64, _vp],
+    "sicu_gemv": [_u32, _vp, _i64, _i64, _vp, _fp, _i64, _vp],
+    "sicu_gemv_f32": [_u32, _vp, _i64, _i64, _fp, _fp, _i64, _vp],
+    "sicu_gemv_host": [_u32, _vp, _i64, _i64, _fp, _fp, _vp],
+    "sicu_row_to_f32": [_u32, _vp, _i64, C.POINTER(C.c_int64), _i64, _fp, _vp],
+}
+
+
+class SicuError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"libsiphon_cuda error {code}: {msg}")
+        self.code = code
+
+
+def _ptr(x) -> int | None:
+    """Device/host address of a torch tensor, numpy array or int."""
+    if x is None:
+        return None
+    if isinstance(x, int):
+        return x
+    if hasattr(x, "data_ptr"):
+        return x.data_ptr()
+    if hasattr(x, "ctypes"):
+        return x.ctypes.data
+    raise TypeError(f"cannot take the address of {type(x)}")
+
+
+class SiphonCuda:
+    def __init__(self, path: Path = LIB_PATH):
+        if not Path(path).exists():
+            raise FileNotFoundError(f"{path} is not built; run `python -m siphon_b200.build`")
+        self.lib = C.CDLL(str(path))
+        for name, args in SIGNATURES.items():
+            f = getattr(self.lib, name)
+            f.argtypes = args
+            f.restype = C.c_int
+
+    # -- errors ---------------------------------------------------------------
+    def last_error(self) -> str:
+        buf = C.create_string_buffer(512)
+        self.lib.sicu_last_error(buf, 512)
+        return buf.value.decode(errors="replace")
+
+    def check(self, rc: int) -> None:
+        if rc != SICU_OK:
+            raise SicuError(rc, self.last_error())
+
+    # -- lifecycle --------------------------------------------------------------
+    def init(self, device: int = 0) -> None:
+        self.check(self.lib.sicu_init(device))
+
+    def shutdown(self) -> None:
+        self.check(self.lib.sicu_shutdown())
+
+    def status(self) -> int:
+        flags = C.c_int(0)
+        self.check(self.lib.sicu_status(C.byref(flags)))
+        return flags.value
+
+    # -- geometry -----------------------------------------------------------------
+    def geometry(self, t: int) -> tuple[int, int]:
+        b, s = C.c_uint32(), C.c_uint32()
+        self.check(self.lib.sicu_quant_geometry(t, C.byref(b), C.byref(s)))
+        return b.value, s.value
+
+    def pair_type(self, wtype: int) -> int:
+        p = C.c_uint32()
+        self.check(self.lib.sicu_vec_dot_pair(wtype, C.byref(p)))
+        return p.value
+
+    # -- compute ----------------------------------------------------------------------
+    def quantize_q8_K(self, dx, dy, n: int, m: int = 1, stream=None) -> None:
+        self.check(self.lib.sicu_quantize_q8_K(_ptr(dx), _ptr(dy), n, m, _ptr(stream)))
+
+    def quantize_q8_0(self, dx, dy, n: int, m: int = 1, stream=None) -> None:
+        self.check(self.lib.sicu_quantize_q8_0(_ptr(dx), _ptr(dy), n, m, _ptr(stream)))
+
+    def convert_f16(self, dx, dy, n: int, m: int = 1, stream=None) -> None:
+        self.check(self.lib.sicu_convert_f16(_ptr(dx), _ptr(dy), n, m, _ptr(stream)))
+
+    def quantize_pair(self, wtype: int, dx, dxq, n: int, m: int = 1, stream=None) -> None:
+        self.check(self.lib.sicu_quantize_pair(wtype, _ptr(dx), _ptr(dxq), n, m, _ptr(stream)))
+
+    def gemv(self, wtype: int, dw, n_in: int, n_out: int, dxq, dy, m: int = 1, stream=None) -> None:
+        self.check(self.lib.sicu_gemv(wtype, _ptr(dw), n_in, n_out, _ptr(dxq), _ptr(dy), m, _ptr(stream)))
+
+    def gemv_f32(self, wtype: int, dw, n_in: int, n_out: int, dx, dy, m: int = 1, stream=None) -> None:
+        self.check(self.lib.sicu_gemv_f32(wtype, _ptr(dw), n_in, n_out, _ptr(dx), _ptr(dy), m, _ptr(stream)))
+
+    def gemv_host(self, wtype: int, dw, n_in: int, n_out: int, hx, hy, stream=None) -> None:
+        self.check(self.lib.sicu_gemv_host(wtype, _ptr(dw), n_in, n_out, _ptr(hx), _ptr(hy), _ptr(stream)))
+
+    def row_to_f32(self, wtype: int, dw, n_in: int, rows, dout, stream=None) -> None:
+        arr = (C.c_int64 * len(rows))(*rows)
+        self.check(self.lib.sicu_row_to_f32(wtype, _ptr(dw), n_in, arr, len(rows), _ptr(dout), _ptr(stream)))
+
+    # -- memory ---------------------------------------------------------------------
+    def upload(self, host) -> int:
+        p = C.c_void_p()
+        self.check(self.lib.sicu_upload(_ptr(host), host.nbytes, C.byref(p)))
+        return p.value
+
+    def free(self, dev: int) -> None:
+        self.check(self.lib.sicu_free(dev))
+
+
+_LIB: SiphonCuda | None = None
+
+
+def load() -> SiphonCuda:
+    """The process-wide binding (raises if the library is not built)."""
+    global _LIB
+    if _LIB is None:
+        _LIB = SiphonCuda()
+    return _LIB
+
+
+def pair_row_bytes(wtype: int, n: int) -> int:
+    return Q.row_bytes(Q.pair_type(wtype), n)

@@ -1,0 +1,85 @@
+"""The C-ABI library loads on a CPU-only machine, exports every entry point
+include/siphon_cuda.h declares, and rejects bad arguments on the host with
+the reference's error codes before touching CUDA."""
+
+from __future__ import annotations
+
+import ctypes as C
+import re
+
+import numpy as np
+import pytest
+
+from siphon_b200 import lib as L
+from siphon_b200 import quant as Q
+
+HEADER = L.LIB_PATH.parents[1] / "include" / "siphon_cuda.h"
+
+
+def declared() -> list[str]:
+    text = HEADER.read_text()
+    return re.findall(r"SICU_API\s+int\s+(sicu_\w+)\s*\(", text)
+
+
+@pytest.fixture(scope="module")
+def so():
+    return L.SiphonCuda()
+
+
+def test_every_declared_symbol_is_exported(so):
+    names = declared()
+    assert len(names) >= 20
+    for n in names:
+        assert hasattr(so.lib, n), n
+    assert set(names) == set(L.SIGNATURES), "binding and header disagree"
+
+
+def test_geometry_and_pairing_without_gpu(so):
+    for t, (blck, size) in Q.GEOMETRY.items():
+        assert so.geometry(t) == (blck, size)
+    for t in Q.WEIGHT_TYPES:
+        assert so.pair_type(t) == Q.pair_type(t)
+    with pytest.raises(L.SicuError) as e:
+        so.pair_type(3)   # Q4_1: recognised by ggml, not on this path
+    assert e.value.code == L.SICU_ENOTSUP
+
+
+def _call_gemv(so, wt=Q.Q4_K, w=16, n_in=256, n_out=4, x=32, y=64, m=1):
+    return so.lib.sicu_gemv(wt, w, n_in, n_out, x, y, m, None)
+
+
+def test_matvec_argument_checks_run_on_host(so):
+    assert _call_gemv(so, wt=3) == L.SICU_ENOTSUP          # unsupported type
+    assert _call_gemv(so, n_in=300) == L.SICU_EINVAL        # not a whole super-block
+    assert _call_gemv(so, n_in=0) == L.SICU_EINVAL
+    assert _call_gemv(so, m=0) == L.SICU_EINVAL
+    assert _call_gemv(so, w=None) == L.SICU_EINVAL          # null
+    assert _call_gemv(so, w=24) == L.SICU_EINVAL            # weight not 16-byte aligned
+    assert _call_gemv(so, y=66) == L.SICU_EINVAL            # output misaligned
+    assert "aligned" in so.last_error()
+    # well-formed, but no device initialised: refused without a CUDA call
+    assert _call_gemv(so) == L.SICU_EINVAL
+    assert "sicu_init" in so.last_error()
+
+
+def test_quantizer_argument_checks_run_on_host(so):
+    assert so.lib.sicu_quantize_q8_K(16, 32, 300, 1, None) == L.SICU_EINVAL
+    assert so.lib.sicu_quantize_q8_0(16, 32, 40, 1, None) == L.SICU_EINVAL
+    assert so.lib.sicu_quantize_q8_K(20, 32, 256, 1, None) == L.SICU_EINVAL   # f32 input misaligned
+    assert so.lib.sicu_quantize_pair(3, 16, 32, 256, 1, None) == L.SICU_ENOTSUP
+    assert so.lib.sicu_quantize_q8_K(16, 32, 256, 1, None) == L.SICU_EINVAL   # not initialised
+
+
+def test_last_error_is_per_thread(so):
+    import threading
+    _call_gemv(so, wt=3)
+    msgs = {}
+
+    def other():
+        msgs["t"] = so.last_error()
+
+    t = threading.Thread(target=other)
+    t.start()
+    t.join()
+    assert "unsupported" in so.last_error()
+    assert msgs["t"] == ""

@@ -1,0 +1,128 @@
+"""Decode matvec parity: the CUDA kernels against the oracle's scalar
+reference semantics, bit for bit, through the C ABI."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from siphon_b200 import quant as Q
+from siphon_b200 import synth
+from tests.gpu_util import assert_bits_equal, assert_within_tol, dev, empty_f32, empty_u8, host
+
+pytestmark = pytest.mark.gpu
+
+K_TYPES = (Q.Q2_K, Q.Q3_K, Q.Q4_K, Q.Q5_K, Q.Q6_K)
+C_TYPES = (Q.Q4_0, Q.Q5_0, Q.Q8_0)
+
+# (n_out, n_in): tiny, ragged row counts, rows that are not 16-byte aligned
+# (odd super-block counts), long rows that stream in chunks
+K_SHAPES = [(1, 256), (5, 256), (37, 512), (64, 2048), (200, 768), (33, 1280), (129, 5632), (300, 12544)]
+C_SHAPES = [(1, 32), (7, 96), (37, 160), (64, 2048), (33, 4128), (129, 5632), (100, 14336)]
+F_SHAPES = [(1, 8), (7, 100), (64, 2048), (33, 4100)]
+
+
+def _case(sicu, oracle, wt, n_out, n_in, seed=0, scale=1.0):
+    w = synth.weights(wt, n_out, n_in, seed=seed)
+    x = synth.activations(n_in, 1, seed=seed + 1) * np.float32(scale)
+    xq = oracle.quantize_pair(wt, x)
+    want = oracle.gemv(wt, w, n_in, n_out, xq[0])
+    dw = dev(w)
+    # pre-quantized activation
+    y = empty_f32(n_out)
+    sicu.gemv(wt, dw, n_in, n_out, dev(xq), y)
+    got = host(y)
+    assert_bits_equal(got, want, f"{Q.NAMES[wt]} {n_out}x{n_in} gemv")
+    assert_within_tol(got, want, "gemv")
+    # fused f32 activation
+    y2 = empty_f32(n_out)
+    sicu.gemv_f32(wt, dw, n_in, n_out, dev(x), y2)
+    assert_bits_equal(host(y2), want, f"{Q.NAMES[wt]} {n_out}x{n_in} gemv_f32")
+
+
+@pytest.mark.parametrize("shape", K_SHAPES, ids=str)
+@pytest.mark.parametrize("wt", K_TYPES, ids=lambda t: Q.NAMES[t])
+def test_k_formats(sicu, oracle, wt, shape):
+    _case(sicu, oracle, wt, *shape)
+
+
+@pytest.mark.parametrize("shape", C_SHAPES, ids=str)
+@pytest.mark.parametrize("wt", C_TYPES, ids=lambda t: Q.NAMES[t])
+def test_classic_formats(sicu, oracle, wt, shape):
+    _case(sicu, oracle, wt, *shape)
+
+
+@pytest.mark.parametrize("shape", F_SHAPES, ids=str)
+def test_f16(sicu, oracle, shape):
+    _case(sicu, oracle, Q.F16, *shape)
+
+
+@pytest.mark.parametrize("wt", Q.WEIGHT_TYPES, ids=lambda t: Q.NAMES[t])
+def test_activation_scales(sicu, oracle, wt):
+    for s, scale in enumerate((1e-20, 1e-3, 1e3, 1e20)):
+        _case(sicu, oracle, wt, 24, 1024, seed=10 + s, scale=scale)
+
+
+@pytest.mark.parametrize("wt", Q.WEIGHT_TYPES, ids=lambda t: Q.NAMES[t])
+def test_zero_activation_blocks(sicu, oracle, wt):
+    n_in, n_out = 1024, 40
+    w = synth.weights(wt, n_out, n_in, seed=5)
+    x = synth.activations(n_in, 1, seed=6)
+    x[0, 256:512] = 0.0
+    xq = oracle.quantize_pair(wt, x)
+    want = oracle.gemv(wt, w, n_in, n_out, xq[0])
+    y = empty_f32(n_out)
+    sicu.gemv_f32(wt, dev(w), n_in, n_out, dev(x), y)
+    assert_bits_equal(host(y), want, "zero block")
+
+
+@pytest.mark.slow
+@pytest.mark.parametrize("shape", [(4096, 4096), (14336, 4096), (4096, 14336), (5632, 2048)], ids=str)
+@pytest.mark.parametrize("wt", Q.WEIGHT_TYPES, ids=lambda t: Q.NAMES[t])
+def test_baseline_sizes(sicu, oracle, wt, shape):
+    """BASELINE.json configs[0] and configs[1] shapes, bit-exact at full size."""
+    n_out, n_in = shape
+    w = synth.weights(wt, n_out, n_in, seed=wt)
+    x = synth.activations(n_in, 1, seed=100 + wt)
+    xq = oracle.quantize_pair(wt, x)
+    want = oracle.gemv_batch(wt, w, n_in, n_out, xq)[0]
+    y = empty_f32(n_out)
+    sicu.gemv_f32(wt, dev(w), n_in, n_out, dev(x), y)
+    assert_bits_equal(host(y), want, f"{Q.NAMES[wt]} {shape}")
+
+
+def test_batched_rows(sicu, oracle):
+    wt, n_in, n_out, m = Q.Q4_K, 2048, 96, 5
+    w = synth.weights(wt, n_out, n_in, seed=8)
+    x = synth.activations(n_in, m, seed=9)
+    xq = oracle.quantize_pair(wt, x)
+    want = oracle.gemv_batch(wt, w, n_in, n_out, xq)
+    y = empty_f32(m, n_out)
+    sicu.gemv(wt, dev(w), n_in, n_out, dev(xq), y, m=m)
+    assert_bits_equal(host(y), want, "batched gemv")
+
+
+def test_host_buffers(sicu, oracle):
+    wt, n_in, n_out = Q.Q6_K, 2048, 300
+    w = synth.weights(wt, n_out, n_in, seed=12)
+    x = synth.activations(n_in, 1, seed=13)[0]
+    want = oracle.gemv(wt, w, n_in, n_out, oracle.quantize_pair(wt, x)[0])
+    hy = np.zeros(n_out, np.float32)
+    sicu.gemv_host(wt, dev(w), n_in, n_out, x, hy)
+    assert_bits_equal(hy, want, "gemv_host")
+
+
+@pytest.mark.parametrize("wt", Q.WEIGHT_TYPES, ids=lambda t: Q.NAMES[t])
+def test_row_to_f32(sicu, oracle, wt):
+    n_in, n_out = 2048, 9
+    w = synth.weights(wt, n_out, n_in, seed=14)
+    rows = [8, 0, 3, 3]
+    out = empty_f32(len(rows), n_in)
+    sicu.row_to_f32(wt, dev(w), n_in, rows, out)
+    rb = Q.row_bytes(wt, n_in)
+    want = np.stack([oracle.dequant_row(wt, w[r * rb:(r + 1) * rb], n_in) for r in rows])
+    assert_bits_equal(host(out), want, "row_to_f32")
+
+
+def test_status_clean_after_runs(sicu):
+    assert sicu.status() == 0

@@ -64,6 +64,8 @@ def workload_config(copies: dict | None, extra: dict | None = None) -> dict:
         "weights": "seeded random Q4_K blocks (f16 d,dmin U[1e-4,1e-2]; other bits uniform); x ~ N(0,1)",
         "l2": "inputs larger than L2: each shape rotates through distinct weight copies totalling >= 4x L2",
         "parallelism": "replicas",
+        "launch": "one CUDA graph of K steps; per step and shape one sicu_gemv_multi launch over the shape's "
+                  "weight copies (shared activation); programmatic dependent launch between launches",
     }
     if copies:
         cfg["copies_per_shape"] = copies
@@ -101,7 +103,7 @@ class ClockSampler:
                 self.reasons |= self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
             except Exception:
                 pass
-            time.sleep(0.0005)
+            time.sleep(0.0002)
 
     def __enter__(self):
         if self.ok:
@@ -285,6 +287,9 @@ def run_ours(args, world, rank, local) -> None:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     s = lib.load()
     s.init(local)
+    # programmatic dependent launch: each matvec starts streaming its (immutable)
+    # weights while the previous one drains
+    s.set_overlap(True)
     props = torch.cuda.get_device_properties(dev)
     l2 = int(getattr(props, "L2_cache_size", 126 * 2 ** 20))
     copies = copies_for(l2)
@@ -302,19 +307,25 @@ def run_ours(args, world, rank, local) -> None:
     step_bytes = sum(len(ws) * Q.matvec_bytes(WTYPE, n_out, n_in) for n_out, n_in, ws, _, _ in mats)
     launches_per_step = sum(len(ws) for _, _, ws, _, _ in mats)
 
-    def step(st, evs=None):
+    def step(st, evs=None, single=False):
+        # one launch per shape: the shape's weight copies share the activation
+        # (sicu_gemv_multi); single=True launches one matvec per copy instead
         h = st.cuda_stream
         for si, (n_out, n_in, ws, x, ys) in enumerate(mats):
             if evs is not None:
                 evs[si][0].record(st)
-            for w, y in zip(ws, ys):
-                s.gemv_f32(WTYPE, w, n_in, n_out, x, y, stream=h)
+            if single:
+                for w, y in zip(ws, ys):
+                    s.gemv_f32(WTYPE, w, n_in, n_out, x, y, stream=h)
+            else:
+                s.gemv_multi(WTYPE, ws, [n_out] * len(ws), n_in, x, ys, stream=h)
             if evs is not None:
                 evs[si][1].record(st)
 
     with torch.cuda.stream(stream):
         for _ in range(args.warmup):
             step(stream)
+            step(stream, single=True)
     torch.cuda.synchronize()
     for n_out, n_in, ws, x, ys in mats:
         assert torch.isfinite(ys[-1]).all(), "non-finite matvec output"
@@ -327,16 +338,17 @@ def run_ours(args, world, rank, local) -> None:
     with torch.cuda.graph(g, stream=stream):
         for k in range(args.steps):
             step(stream, evs[k])
-    g.replay()                       # graph upload + K more warm-up steps
+    with torch.cuda.stream(stream):
+        g.replay()                   # graph upload + K more warm-up steps
     torch.cuda.synchronize()
 
     barrier(world)
     torch.cuda.synchronize()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
+    with ClockSampler(local) as clk, torch.cuda.stream(stream):
         e0.record(stream)
-        g.replay()
+        g.replay()                   # replays on the current stream: `stream`
         e1.record(stream)
         torch.cuda.synchronize()
     barrier(world)
@@ -344,7 +356,7 @@ def run_ours(args, world, rank, local) -> None:
     ms_max = max_over_ranks(ms, world, dev)
     value = world * args.steps * step_bytes / (ms_max * 1e-3) / 1e9
 
-    # dominant kernel: gemv_kernel<Q4_K>, per-shape groups of back-to-back launches
+    # dominant kernel: gemv_kernel<Q4_K>, one launch per shape per step
     per_shape_ms = [0.0] * len(SHAPES)
     for k in range(args.steps):
         for si in range(len(SHAPES)):
@@ -353,12 +365,28 @@ def run_ours(args, world, rank, local) -> None:
     achieved = kern_bytes / (sum(per_shape_ms) * 1e-3) / 1e9
     peak, peak_kind = peak_hbm()
     traffic = NCU_TRAFFIC.get("per_launch_bytes")
+
+    # the same sweep with one launch per matvec (informational)
+    sevs = [[[torch.cuda.Event(enable_timing=True, external=True) for _ in range(2)] for _ in SHAPES]
+            for _ in range(2)]
+    g1 = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g1, stream=stream):
+        for k in range(2):
+            step(stream, sevs[k], single=True)
+    with torch.cuda.stream(stream):
+        g1.replay()
+        g1.replay()
+    torch.cuda.synchronize()
     shape_detail = {}
     for si, (n_out, n_in, ws, _, _) in enumerate(mats):
         b = Q.matvec_bytes(WTYPE, n_out, n_in)
         us = per_shape_ms[si] * 1e3 / (args.steps * len(ws))
-        shape_detail[f"{n_out}x{n_in}"] = {"us_per_launch": round(us, 3), "bytes_per_launch": b,
-                                           "GBps": round(b / (us * 1e-6) / 1e9, 1)}
+        us1 = sum(sevs[k][si][0].elapsed_time(sevs[k][si][1]) for k in range(2)) * 1e3 / (2 * len(ws))
+        shape_detail[f"{n_out}x{n_in}"] = {
+            "batched_us_per_matrix": round(us, 3), "batched_GBps": round(b / (us * 1e-6) / 1e9, 1),
+            "single_launch_us": round(us1, 3), "single_launch_GBps": round(b / (us1 * 1e-6) / 1e9, 1),
+            "bytes_per_matrix": b}
+    del g1
 
     # e2e through the host-buffer entry point (reference backend call shape)
     hx = [torch.from_numpy(synth.activations(n_in, 1, seed=7)[0]).pin_memory() for _, n_in, _, _, _ in mats]
@@ -398,12 +426,12 @@ def run_ours(args, world, rank, local) -> None:
         "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
         "config": workload_config(copies, {"parallelism": f"replicas x{world}" if world > 1 else "single GPU",
                                            "per_shape": shape_detail}),
-        "roofline": {"bound": "hbm", "kernel": "gemv_kernel<Q4_K>", "achieved": round(achieved, 1),
+        "roofline": {"bound": "hbm", "kernel": "gemv_kernel<Q4_K> (one launch = all copies of a shape)", "achieved": round(achieved, 1),
                      "peak": peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),
                      "traffic": traffic},
         "e2e": {"value": round(e2e_value, 1), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "path": "sicu_gemv_host per matvec (pinned host x in, host y out, stream sync per call)"},
-        "gpu_launches": args.steps * launches_per_step,
+        "gpu_launches": args.steps * len(SHAPES),
         "clocks": clk.summary(),
     }
     if cpu is not None:
@@ -414,7 +442,7 @@ def run_ours(args, world, rank, local) -> None:
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")

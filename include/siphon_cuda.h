@@ -74,6 +74,15 @@ SICU_API int sicu_last_error(char *buf, size_t len);
  * launch are invalid). Synchronises the device. */
 SICU_API int sicu_status(int *flags);
 
+/* Programmatic dependent launch for the matvec kernels (default off). When
+ * on, a matvec may start streaming its weight blocks while earlier work in
+ * the same stream is still running (it still waits for that work before it
+ * reads its activation or writes its output), which hides kernel ramp-up in
+ * chains of matvecs. Only valid when no earlier work in the stream writes
+ * the weight buffer. No counterpart in the reference, which has no kernel
+ * launches. */
+SICU_API int sicu_set_overlap(int on);
+
 /* ---- memory ------------------------------------------------------------- */
 
 SICU_API int sicu_malloc(void **dev, size_t bytes);
@@ -126,6 +135,16 @@ SICU_API int sicu_gemv(uint32_t wtype, const void *dw, int64_t n_in, int64_t n_o
  * cpu_gemv (src/backend.c:85-120; include/siphon/tensor.h:43-55). */
 SICU_API int sicu_gemv_f32(uint32_t wtype, const void *dw, int64_t n_in, int64_t n_out,
                   const float *dx, float *dy, int64_t m, void *stream);
+/* Several matvecs sharing one f32 activation: y_i = W_i x for i < n_mats
+ * (1..64), every W_i of type wtype with row length n_in and n_out[i] rows;
+ * dw, n_out and dy are host arrays of device pointers / sizes. One kernel
+ * launch streams all the matrices back to back and quantizes x once, so the
+ * launch ramp and drain are paid once. Replaces consecutive backend gemv
+ * calls on one activation in the reference's forward pass (src/engine.c:
+ * 317-319 for Wq/Wk/Wv, 375-376 for gate/up); results are identical to
+ * n_mats separate sicu_gemv_f32 calls. */
+SICU_API int sicu_gemv_multi(uint32_t wtype, int n_mats, const void *const *dw, const int64_t *n_out,
+                             int64_t n_in, const float *dx, float *const *dy, void *stream);
 /* Same, with host input and output buffers (one activation row): copies x
  * in, runs sicu_gemv_f32, copies y out and waits. This is the exact call
  * shape of the reference's backend gemv slot. */

@@ -6,7 +6,7 @@
 #include <cstring>
 #include <mutex>
 
-#include "../../include/siphon_cuda.h"
+#include "siphon_cuda.h"
 #include "common.cuh"
 #include "launch.h"
 
@@ -28,6 +28,8 @@ struct DevState {
     bool ready = false;
     int sms = 0;
     int smem_optin = 0;
+    int smem_per_sm = 0;
+    int smem_reserved = 0;
     int *status = nullptr;      // device status word
     // growable staging for the host-buffer entry points
     void *stage = nullptr;
@@ -35,6 +37,7 @@ struct DevState {
 };
 
 constexpr int MAX_DEV = 64;
+int g_overlap = 0;   // sicu_set_overlap
 DevState g_dev[MAX_DEV];
 std::mutex g_mu;
 
@@ -119,7 +122,9 @@ int check_matvec(uint32_t wt, const void *dw, int64_t n_in, int64_t n_out, const
         return fail(SICU_EINVAL, "matvec: bad shape n_in=%lld n_out=%lld m=%lld", (long long)n_in, (long long)n_out, (long long)m);
     if (n_in % blck) return fail(SICU_EINVAL, "matvec: row length %lld of %s is not a multiple of %u", (long long)n_in, tname(wt), blck);
     if (n_in > (int64_t)1 << 24) return fail(SICU_EINVAL, "matvec: row length %lld too large", (long long)n_in);
-    if (!dw || !dx || !dy) return fail(SICU_EINVAL, "matvec: null pointer");
+    if (!dx) return fail(SICU_EINVAL, "matvec: null activation");
+    if (n_out == 0) return SICU_OK;   // nothing is read or written
+    if (!dw || !dy) return fail(SICU_EINVAL, "matvec: null pointer");
     if (!aligned(dw, 16)) return fail(SICU_EINVAL, "matvec: weight pointer must be 16-byte aligned");
     if (!aligned(dy, 4)) return fail(SICU_EINVAL, "matvec: output must be 4-byte aligned");
     return SICU_OK;
@@ -136,9 +141,16 @@ GemvLaunch make_launch(const DevState &ds, const void *dw, int64_t n_in, int64_t
     L.w = dw;
     L.y = dy;
     L.n_out = n_out;
+    L.nmat = 1;
+    L.wm[0] = dw;
+    L.ym[0] = dy;
+    L.n_outm[0] = n_out;
     L.n_in = (int)n_in;
     L.num_sms = ds.sms;
     L.smem_limit = ds.smem_optin;
+    L.smem_per_sm = ds.smem_per_sm;
+    L.smem_reserved = ds.smem_reserved;
+    L.overlap = g_overlap;
     int dev = 0;
     cudaGetDevice(&dev);
     L.device = dev;
@@ -174,6 +186,8 @@ int sicu_init(int device) {
         return fail(SICU_ENOTSUP, "device %d is sm_%d%d; this library is built for sm_100a only", device, prop.major, prop.minor);
     ds.sms = prop.multiProcessorCount;
     ds.smem_optin = (int)prop.sharedMemPerBlockOptin;
+    ds.smem_per_sm = (int)prop.sharedMemPerMultiprocessor;
+    ds.smem_reserved = (int)prop.reservedSharedMemPerBlock;
     if ((e = cudaMalloc(&ds.status, sizeof(int))) != cudaSuccess) return cuda_fail(e, "cudaMalloc(status)");
     if ((e = cudaMemset(ds.status, 0, sizeof(int))) != cudaSuccess) return cuda_fail(e, "cudaMemset(status)");
     ds.ready = true;
@@ -193,6 +207,11 @@ int sicu_shutdown(void) {
         ds = DevState{};
     }
     if (have && cur >= 0) cudaSetDevice(cur);
+    return SICU_OK;
+}
+
+int sicu_set_overlap(int on) {
+    g_overlap = on ? 1 : 0;
     return SICU_OK;
 }
 
@@ -334,6 +353,38 @@ int sicu_gemv_f32(uint32_t wtype, const void *dw, int64_t n_in, int64_t n_out, c
         if (int rc = run_gemv(wtype, L, (cudaStream_t)stream)) return rc;
     }
     return SICU_OK;
+}
+
+int sicu_gemv_multi(uint32_t wtype, int n_mats, const void *const *dw, const int64_t *n_out, int64_t n_in,
+                    const float *dx, float *const *dy, void *stream) {
+    if (n_mats < 1 || n_mats > MAX_MATS) return fail(SICU_EINVAL, "matvec multi: %d matrices (1..%d)", n_mats, MAX_MATS);
+    if (!dw || !n_out || !dy) return fail(SICU_EINVAL, "matvec multi: null array");
+    uint32_t pair;
+    for (int i = 0; i < n_mats; ++i) {
+        if (int rc = check_matvec(wtype, dw[i], n_in, n_out[i], dx, dy[i], 1, pair)) return rc;
+        if (n_out[i] > ((int64_t)1 << 30)) return fail(SICU_EINVAL, "matvec multi: too many rows");
+    }
+    if (!aligned(dx, 16)) return fail(SICU_EINVAL, "matvec: f32 activation must be 16-byte aligned");
+    DevState *ds;
+    if (int rc = current(ds)) return rc;
+    if (wtype == T_F16) {
+        for (int i = 0; i < n_mats; ++i) {
+            if (n_out[i] == 0) continue;
+            GemvLaunch L = make_launch(*ds, dw[i], n_in, n_out[i], dy[i]);
+            L.xf = dx;
+            if (int rc = run_gemv(wtype, L, (cudaStream_t)stream)) return rc;
+        }
+        return SICU_OK;
+    }
+    GemvLaunch L = make_launch(*ds, dw[0], n_in, n_out[0], dy[0]);
+    L.xf = dx;
+    L.nmat = n_mats;
+    for (int i = 0; i < n_mats; ++i) {
+        L.wm[i] = dw[i];
+        L.ym[i] = dy[i];
+        L.n_outm[i] = n_out[i];
+    }
+    return run_gemv(wtype, L, (cudaStream_t)stream);
 }
 
 int sicu_gemv_host(uint32_t wtype, const void *dw, int64_t n_in, int64_t n_out, const float *hx, float *hy,

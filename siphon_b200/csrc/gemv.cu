@@ -1,4 +1,7 @@
 // Persistent streaming matvec driver (see gemv.cuh for the design notes).
+#include <map>
+#include <mutex>
+
 #include "gemv.cuh"
 #include "quantize.cuh"
 #include "launch.h"
@@ -7,191 +10,220 @@ namespace sicu {
 
 namespace {
 
-struct Item {
-    int64_t task, row0;
-    int rows, chunk, u0, cu;
-    int64_t byte_start, byte_len;
+// Producer cursor over a warp's items: task t (global over all matrices),
+// its matrix, chunk. Advances without divisions.
+struct Cursor {
+    int task, mat, chunk;
+    __device__ void seek(const GemvParams &p) {
+        while (mat + 1 < p.nmat && task >= p.task0[mat + 1]) ++mat;
+    }
+    __device__ void next(const GemvParams &p, int step) {
+        if (++chunk == p.nchunks) { chunk = 0; task += step; seek(p); }
+    }
 };
 
+// Producer (lane 0): fill a ring slot with the cursor's item, a 16-byte
+// aligned bulk copy plus, at the very end of a matrix, up to 15 tail bytes,
+// and publish the item's geometry next to the slot.
 template <uint32_t T>
-__device__ __forceinline__ Item item_of(const GemvParams &p, int64_t t0, int warp, int64_t k) {
-    Item it;
-    it.task = t0 + warp + (k / p.nchunks) * GEMV_WARPS;
-    it.chunk = (int)(k % p.nchunks);
-    it.row0 = it.task * p.rows_per_task;
-    const int64_t left = p.n_out - it.row0;
-    it.rows = left < p.rows_per_task ? (int)left : p.rows_per_task;
-    it.u0 = it.chunk * p.cu;
-    it.cu = min(p.cu, p.nu - it.u0);
-    it.byte_start = it.row0 * p.row_bytes + (int64_t)it.u0 * Fmt<T>::unit_bytes;
+__device__ __forceinline__ void produce(const GemvParams &p, const Cursor &c, uint8_t *slot, int4 *info,
+                                        uint32_t full, uint64_t policy) {
+    const int row0 = (c.task - p.task0[c.mat]) * p.rows_per_task;
+    const int left = p.n_out[c.mat] - row0;
+    const int rows = left < p.rows_per_task ? left : p.rows_per_task;
+    const int u0 = c.chunk * p.cu;
+    const int cu = min(p.cu, p.nu - u0);
+    const uint8_t *w = p.w[c.mat];
+    const int64_t start = (int64_t)row0 * p.row_bytes + (int64_t)u0 * Fmt<T>::unit_bytes;
+    int64_t len;
     if (p.nchunks == 1) {
-        it.byte_len = it.rows * p.row_bytes;
+        len = (int64_t)rows * p.row_bytes;
     } else {
-        const int64_t rest = p.row_bytes - (int64_t)it.u0 * Fmt<T>::unit_bytes;
-        const int64_t want = (int64_t)it.cu * Fmt<T>::unit_bytes;
-        it.byte_len = want < rest ? want : rest;
+        const int64_t rest = p.row_bytes - (int64_t)u0 * Fmt<T>::unit_bytes;
+        const int64_t want = (int64_t)cu * Fmt<T>::unit_bytes;
+        len = want < rest ? want : rest;
     }
-    return it;
-}
-
-// Fill one ring slot with an item's bytes: a 16-byte aligned bulk copy plus,
-// at the very end of the matrix, up to 15 tail bytes copied by lanes.
-__device__ __forceinline__ void issue_item(const GemvParams &p, const Item &it, uint8_t *slot, uint32_t bar,
-                                           int lane, uint64_t policy) {
-    const uint8_t *src = p.w + it.byte_start;
-    const uintptr_t a = reinterpret_cast<uintptr_t>(src);
+    const uintptr_t a = reinterpret_cast<uintptr_t>(w + start);
     const uint8_t *al = reinterpret_cast<const uint8_t *>(a & ~uintptr_t(15));
-    const int64_t head = (int64_t)(a & 15);
-    const uint8_t *mend = p.w + p.n_out * p.row_bytes;
-    int64_t bulk = (head + it.byte_len + 15) & ~int64_t(15);
+    const int head = (int)(a & 15);
+    const uint8_t *mend = w + (int64_t)p.n_out[c.mat] * p.row_bytes;
+    int64_t bulk = (head + len + 15) & ~int64_t(15);
     if (al + bulk > mend) bulk = (int64_t)(mend - al) & ~int64_t(15);
-    const int64_t tail = head + it.byte_len - bulk;
-    if (lane == 0) {
-        fence_proxy_async();
-        mbar_expect_tx(bar, (uint32_t)bulk);
-        if (bulk > 0) bulk_g2s_hint(smem_addr(slot), al, (uint32_t)bulk, bar, policy);
-    }
-    if (tail > 0 && lane < tail) slot[bulk + lane] = (uint8_t)ldg_u8(al + bulk + lane);
+    const int tail = (int)(head + len - bulk);
+    for (int i = 0; i < tail; ++i) slot[bulk + i] = (uint8_t)ldg_u8(al + bulk + i);
+    info[0] = make_int4(row0, rows | (head << 16), u0, cu);
+    info[1] = make_int4(c.mat, 0, 0, 0);
+    fence_proxy_async();
+    mbar_expect_tx(full, (uint32_t)bulk);   // also the phase's one arrival
+    if (bulk > 0) bulk_g2s_hint(smem_addr(slot), al, (uint32_t)bulk, full, policy);
 }
 
+// a += src[0]; a += src[1]; ... in order, each a separate IEEE rounding.
+// src is 16-byte aligned.
+__device__ __forceinline__ float chain_add(float a, const float *src, int n) {
+    const float4 *s4 = reinterpret_cast<const float4 *>(src);
+    const int n4 = n >> 2;
+#pragma unroll 4
+    for (int g = 0; g < n4; ++g) {
+        const float4 v = s4[g];
+        a = __fadd_rn(a, v.x); a = __fadd_rn(a, v.y); a = __fadd_rn(a, v.z); a = __fadd_rn(a, v.w);
+    }
+    for (int u = n4 << 2; u < n; ++u) a = __fadd_rn(a, src[u]);
+    return a;
+}
+
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Every warp streams and decodes its own tasks: warp w of a CTA owns the
+// CTA's tasks w, w+W, ... (all chunks of a task, so a row's float chains stay
+// in one warp) and a private ring of nslots shared-memory slots. Lane 0 keeps
+// the ring full with bulk copies; a slot's geometry is published next to it,
+// so the consuming side does no address arithmetic of its own.
 template <uint32_t T>
-__global__ void __launch_bounds__(GEMV_WARPS * 32, 1) gemv_kernel(const GemvParams p) {
+__global__ void __launch_bounds__(GEMV_WARPS * 32, 2) gemv_kernel(const GemvParams p) {
     using F = Fmt<T>;
+    constexpr int CH = F::chains;
+    constexpr int W = GEMV_WARPS;
     extern __shared__ __align__(128) uint8_t smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int S = p.nslots;
 
     const ActView av{smem, p.nu};
     uint8_t *wreg = smem + p.act_bytes + (size_t)warp * p.warp_bytes;
-    uint64_t *bars = reinterpret_cast<uint64_t *>(wreg);   // up to 8 slots
-    float *terms = reinterpret_cast<float *>(wreg + 64);   // TERM_FLOATS
-    float *fin = terms + TERM_FLOATS;                      // 64 chain results
-    uint8_t *slots = wreg + WARP_HDR;
+    uint64_t *full = reinterpret_cast<uint64_t *>(wreg);          // [S]
+    int4 *info = reinterpret_cast<int4 *>(wreg + 64);              // [S][2]
+    float *terms = reinterpret_cast<float *>(wreg + 192);          // TERM_FLOATS
+    float *fin = terms + TERM_FLOATS;                              // 64 chain results
+    uint8_t *slots = wreg + 192 + CONS_BYTES;
 
-    const int64_t t0 = (int64_t)blockIdx.x * p.ntasks / gridDim.x;
-    const int64_t t1 = (int64_t)(blockIdx.x + 1) * p.ntasks / gridDim.x;
-    const int64_t mine = (t1 - t0 > warp) ? (t1 - t0 - warp + GEMV_WARPS - 1) / GEMV_WARPS : 0;
-    const int64_t items = mine * p.nchunks;
-    const uint64_t policy = policy_evict_first();
+    const int t0 = (int)((int64_t)blockIdx.x * p.ntasks / gridDim.x);
+    const int t1 = (int)((int64_t)(blockIdx.x + 1) * p.ntasks / gridDim.x);
+    const int ntask = t1 - t0;
+    const int items = warp < ntask ? ((ntask - warp + W - 1) / W) * p.nchunks : 0;
+    grid_dep_launch();
 
     if (lane == 0) {
-        for (int s = 0; s < p.nslots; ++s) mbar_init(smem_addr(&bars[s]), 1);
+        for (int i = 0; i < S; ++i) mbar_init(smem_addr(&full[i]), 1);
         fence_mbar_init();
     }
     __syncwarp();
-    for (int64_t k = 0; k < items && k < p.nslots; ++k) {
-        const Item it = item_of<T>(p, t0, warp, k);
-        issue_item(p, it, slots + (size_t)k * p.slot_bytes, smem_addr(&bars[k]), lane, policy);
+    // producer cursor: item m is task t0 + warp + (m / nchunks) * W, chunk m % nchunks
+    Cursor pc{t0 + warp, 0, 0};
+    int pm = 0;
+    uint64_t policy = 0;
+    if (lane == 0) {
+        pc.seek(p);
+        // weights never depend on earlier kernels: start streaming right away
+        policy = policy_evict_first();
+        for (; pm < items && pm < S; ++pm) {
+            produce<T>(p, pc, slots + (size_t)pm * p.slot_bytes, &info[2 * pm], smem_addr(&full[pm]), policy);
+            pc.next(p, W);
+        }
     }
 
-    // activation: the caller's pair-format row, or quantized here from f32
-    if (p.xf) {
-        // the term buffer is idle until the main loop: use it as the 292-byte stage
-        quantize_into_act<F::act>(av, p.xf, p.n_in, reinterpret_cast<uint8_t *>(terms));
-    } else {
-        prep_activation<F::act>(av, p.xq, p.n_in);
-    }
-    __syncthreads();
+    // the activation may be produced by the previous kernel in the stream;
+    // each CTA of the cluster builds 1/nrank of the records for every member
+    grid_dep_wait();
+    const uint32_t rank = cluster_rank(), nrank = cluster_size();
+    if (p.xf) quantize_into_act<F::act>(av, p.xf, p.n_in, rank, nrank);
+    else prep_activation<F::act>(av, p.xq, p.n_in, rank, nrank);
+    cluster_sync();
 
-    constexpr int CH = F::chains;
+    const int r_l = p.nchunks == 1 ? lane / p.cu : 0;
+    const int u_l = p.nchunks == 1 ? lane - r_l * p.cu : lane;
+    const int cup = (p.cu + 3) & ~3;   // K formats: padded chain stride
     float acc[2] = {0.f, 0.f};
-    int64_t failed_at = -1;
-    for (int64_t k = 0; k < items; ++k) {
-        const int s = (int)(k % p.nslots);
-        const uint32_t parity = (uint32_t)((k / p.nslots) & 1);
-        // warp-uniform verdict: a lane that timed out takes the whole warp out
-        const bool landed = mbar_wait(smem_addr(&bars[s]), parity);
-        if (!__all_sync(0xffffffffu, landed)) { failed_at = k; break; }
-        __syncwarp();
-        const Item it = item_of<T>(p, t0, warp, k);
+    int s = 0, chunk = 0;
+    uint32_t parity = 0;
+    for (int m = 0; m < items; ++m) {
+        const bool landed = mbar_wait(smem_addr(&full[s]), parity);
+        if (!__all_sync(0xffffffffu, landed)) {
+            if (lane == 0) atomicOr(p.status, STATUS_WAIT_TIMEOUT);
+            // let the copies still in flight land before the CTA's memory goes away
+            for (int k = m; k < items && k < m + S; ++k)
+                (void)mbar_wait(smem_addr(&full[k % S]), (uint32_t)((k / S) & 1), 100000000ull);
+            break;
+        }
+        const int4 g = info[2 * s];
+        const int mat = info[2 * s + 1].x;
+        const int rows = g.y & 0xffff, u0 = g.z, cu = g.w;
         uint8_t *slot = slots + (size_t)s * p.slot_bytes;
-        const uint8_t *data = slot + (reinterpret_cast<uintptr_t>(p.w + it.byte_start) & 15);
+        const uint8_t *data = slot + (g.y >> 16);
 
-        // ---- phase 1: one unit per lane ----
-        const int units = it.rows * it.cu;
-        for (int q = lane; q < units; q += 32) {
-            const int r = q / it.cu, u = q % it.cu, ug = it.u0 + u;
-            const uint8_t *wb = data + (p.nchunks == 1 ? (int64_t)r * p.row_bytes : 0) + (int64_t)u * F::unit_bytes;
+        // ---- phase 1: each lane decodes its unit ----
+        if (r_l < rows && u_l < cu) {
+            const int ug = u0 + u_l;
+            const uint8_t *wb = data + (int64_t)r_l * (p.nchunks == 1 ? p.row_bytes : 0) + u_l * F::unit_bytes;
+            const uint8_t *rec = av.rec(ug);
             if constexpr (F::kind == 3) {
-                const int nblk_row = p.n_in / 32;
-                const int nb = min(8, nblk_row - ug * 8);
+                const int nb = min(8, p.n_in / 32 - ug * 8);
                 float t[8];
-                unit_classic<T>(wb, nb, av.aq(ug), av.ad(ug), av.ax(ug), t);
-                float *dst = terms + (r * it.cu + u) * 8;
+                unit_classic<T>(wb, nb, rec, t);
+                float *dst = terms + (r_l * cu + u_l) * 8;
 #pragma unroll
                 for (int b = 0; b < 8; ++b) if (b < nb) dst[b] = t[b];
             } else {
                 float t[MAX_CHAINS];
-                if constexpr (T == T_Q4_K) unit_q45k<false>(wb, av.aq(ug), av.ad(ug)[0], av.ax(ug), t);
-                else if constexpr (T == T_Q5_K) unit_q45k<true>(wb, av.aq(ug), av.ad(ug)[0], av.ax(ug), t);
-                else if constexpr (T == T_Q6_K) unit_q36k<false>(wb, av.aq(ug), av.ad(ug)[0], t);
-                else if constexpr (T == T_Q3_K) unit_q36k<true>(wb, av.aq(ug), av.ad(ug)[0], t);
-                else unit_q2k(wb, av.aq(ug), av.ad(ug)[0], av.ax(ug), t);
+                if constexpr (T == T_Q4_K) unit_q45k<false>(wb, rec, t);
+                else if constexpr (T == T_Q5_K) unit_q45k<true>(wb, rec, t);
+                else if constexpr (T == T_Q6_K) unit_q36k<false>(wb, rec, t);
+                else if constexpr (T == T_Q3_K) unit_q36k<true>(wb, rec, t);
+                else unit_q2k(wb, rec, t);
 #pragma unroll
-                for (int c = 0; c < CH; ++c) terms[(r * CH + c) * it.cu + u] = t[c];
+                for (int ch = 0; ch < CH; ++ch) terms[(ch * p.rows_per_task + r_l) * cup + u_l] = t[ch];
             }
         }
         __syncwarp();
-        // the slot is consumed: refill it with item k + nslots
-        if (k + p.nslots < items) {
-            const Item nx = item_of<T>(p, t0, warp, k + p.nslots);
-            issue_item(p, nx, slot, smem_addr(&bars[s]), lane, policy);
+        // the slot is consumed: refill it with item m + S
+        if (lane == 0 && pm < items) {
+            produce<T>(p, pc, slot, &info[2 * s], smem_addr(&full[s]), policy);
+            pc.next(p, W);
+            ++pm;
         }
 
         // ---- phase 2: ordered float chains, one lane per (row, chain) ----
-        if (it.chunk == 0) { acc[0] = 0.f; acc[1] = 0.f; }
-        const int pairs = it.rows * CH;
+        const int pairs = rows * CH;
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
             const int q = lane + 32 * h;
             if (q < pairs) {
-                float a = acc[h];
+                const int r = q / CH, ch = q - r * CH;
                 if constexpr (F::kind == 3) {
-                    const int nblk_row = p.n_in / 32;
-                    const int nb = min(it.cu * 8, nblk_row - it.u0 * 8);
-                    const float *src = terms + q * it.cu * 8;
-                    for (int b = 0; b < nb; ++b) a = __fadd_rn(a, src[b]);
+                    const int nb = min(cu * 8, p.n_in / 32 - u0 * 8);
+                    acc[h] = chain_add(acc[h], terms + r * cu * 8, nb);
                 } else {
-                    const float *src = terms + q * it.cu;
-                    const bool sub = (F::kind == 0) && (q % CH == 8);
-                    if (sub) {
-                        for (int u = 0; u < it.cu; ++u) a = __fsub_rn(a, src[u]);
-                    } else {
-                        for (int u = 0; u < it.cu; ++u) a = __fadd_rn(a, src[u]);
-                    }
+                    acc[h] = chain_add(acc[h], terms + (ch * p.rows_per_task + r) * cup, cu);
                 }
-                acc[h] = a;
             }
         }
-        if (it.chunk == p.nchunks - 1) {
+        if (++chunk == p.nchunks) {
+            chunk = 0;
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
                 const int q = lane + 32 * h;
                 if (q < pairs) fin[q] = acc[h];
+                acc[h] = 0.f;
             }
             __syncwarp();
-            if (lane < it.rows) {
-                float s;
+            if (lane < rows) {
+                float r;
                 if constexpr (F::kind == 0) {
-                    s = fin[lane * CH + 8];
+                    r = fin[lane * CH + 8];
 #pragma unroll
-                    for (int l = 0; l < 8; ++l) s = __fadd_rn(s, fin[lane * CH + l]);
+                    for (int l = 0; l < 8; ++l) r = __fadd_rn(r, fin[lane * CH + l]);
                 } else if constexpr (F::kind == 1) {
-                    s = 0.0f;
+                    r = 0.0f;
 #pragma unroll
-                    for (int l = 0; l < 8; ++l) s = __fadd_rn(s, fin[lane * CH + l]);
+                    for (int l = 0; l < 8; ++l) r = __fadd_rn(r, fin[lane * CH + l]);
                 } else {
-                    s = fin[lane];
+                    r = fin[lane];
                 }
-                p.y[it.row0 + lane] = s;
+                p.y[mat][g.x + lane] = r;
             }
         }
         __syncwarp();
-    }
-    if (failed_at >= 0) {
-        if (lane == 0) atomicOr(p.status, STATUS_WAIT_TIMEOUT);
-        // let the copies still in flight land before the CTA's memory goes away
-        for (int64_t k = failed_at; k < items && k < failed_at + p.nslots; ++k)
-            (void)mbar_wait(smem_addr(&bars[k % p.nslots]), (uint32_t)((k / p.nslots) & 1), 1u << 16);
+        if (++s == S) { s = 0; parity ^= 1u; }
     }
 }
 
@@ -203,11 +235,9 @@ template <uint32_t T>
 static int launch_gemv_t(const GemvLaunch &L, cudaStream_t st) {
     using F = Fmt<T>;
     GemvParams p{};
-    p.w = static_cast<const uint8_t *>(L.w);
+    p.nmat = L.nmat;
     p.xq = static_cast<const uint8_t *>(L.xq);
     p.xf = L.xf;
-    p.y = L.y;
-    p.n_out = L.n_out;
     p.n_in = L.n_in;
     p.status = L.status;
     const int nblk = (F::kind == 3) ? L.n_in / 32 : L.n_in / 256;
@@ -224,14 +254,31 @@ static int launch_gemv_t(const GemvLaunch &L, cudaStream_t st) {
         p.cu = (p.nu + p.nchunks - 1) / p.nchunks;
         p.rows_per_task = 1;
     }
-    p.ntasks = (p.n_out + p.rows_per_task - 1) / p.rows_per_task;
+    int64_t tasks = 0;
+    for (int i = 0; i < L.nmat; ++i) {
+        p.w[i] = static_cast<const uint8_t *>(L.wm[i]);
+        p.y[i] = L.ym[i];
+        p.n_out[i] = (int)L.n_outm[i];
+        p.task0[i] = (int)tasks;
+        tasks += (L.n_outm[i] + p.rows_per_task - 1) / p.rows_per_task;
+    }
+    p.task0[L.nmat] = (int)tasks;
+    p.ntasks = tasks;
+    if (tasks == 0) return 0;
     const int64_t item_max = (p.nchunks == 1) ? p.rows_per_task * p.row_bytes : (int64_t)p.cu * F::unit_bytes;
     p.slot_bytes = (int)((item_max + 32 + 127) & ~int64_t(127));
     p.act_bytes = (ActView::bytes(p.nu) + 127) & ~127;
-    const int hdr = WARP_HDR;
-    const int budget = L.smem_limit - p.act_bytes;
-    int slots = (budget / GEMV_WARPS - hdr) / p.slot_bytes;
-    if (slots > 4) slots = 4;
+    // two CTAs per SM when each warp keeps >= 2 ring slots, else one with up to 4
+    int ctas = 2, slots = 0;
+    const int hdr = 192 + CONS_BYTES;
+    for (; ctas >= 1; --ctas) {
+        const int per_cta = (ctas == 2) ? L.smem_per_sm / 2 - L.smem_reserved : L.smem_limit;
+        // a 128-aligned budget per warp, so rounding the region up stays inside it
+        const int per_warp = ((per_cta - p.act_bytes) / GEMV_WARPS & ~127) - hdr;
+        slots = per_warp > 0 ? per_warp / p.slot_bytes : 0;
+        if (slots > 4) slots = 4;
+        if (slots >= 2) break;
+    }
     if (slots < 2) return -1;
     p.nslots = slots;
     p.warp_bytes = (hdr + slots * p.slot_bytes + 127) & ~127;
@@ -243,10 +290,67 @@ static int launch_gemv_t(const GemvLaunch &L, cudaStream_t st) {
             return -2;
         attr_set[dev] = true;
     }
-    int64_t grid = p.ntasks < L.num_sms ? p.ntasks : L.num_sms;
+    // thread-block cluster size: the largest of 8/4/2 that still keeps
+    // (almost) every CTA slot of the launch co-resident
+    const int target = ctas * L.num_sms;
+    int csize = 1, capacity = target;
+    {
+        static std::mutex mu;
+        static std::map<std::pair<int, int>, std::pair<int, int>> cache;   // (device, smem) -> (C, capacity)
+        std::lock_guard<std::mutex> lk(mu);
+        const auto key = std::make_pair(dev, smem);
+        auto hit = cache.find(key);
+        if (hit == cache.end()) {
+            int best_c = 1, best_cap = target;
+            for (int c = 8; c >= 2; c /= 2) {
+                cudaLaunchConfig_t q{};
+                q.gridDim = dim3((unsigned)(target / c * c));
+                q.blockDim = dim3(GEMV_WARPS * 32);
+                q.dynamicSmemBytes = (size_t)smem;
+                cudaLaunchAttribute ca[1];
+                ca[0].id = cudaLaunchAttributeClusterDimension;
+                ca[0].val.clusterDim.x = c;
+                ca[0].val.clusterDim.y = 1;
+                ca[0].val.clusterDim.z = 1;
+                q.attrs = ca;
+                q.numAttrs = 1;
+                int n = 0;
+                if (cudaOccupancyMaxActiveClusters(&n, gemv_kernel<T>, &q) != cudaSuccess) {
+                    cudaGetLastError();
+                    continue;
+                }
+                if (n * c >= target - target / 16) {
+                    best_c = c;
+                    best_cap = n * c < target ? n * c : target;
+                    break;
+                }
+            }
+            hit = cache.emplace(key, std::make_pair(best_c, best_cap)).first;
+        }
+        csize = hit->second.first;
+        capacity = hit->second.second;
+    }
+    int64_t grid = capacity;
+    if (p.ntasks < grid) grid = p.ntasks;
+    if (grid < csize) csize = 1;
+    grid = grid / csize * csize;
     if (grid < 1) grid = 1;
-    gemv_kernel<T><<<(unsigned)grid, GEMV_WARPS * 32, smem, st>>>(p);
-    return cudaGetLastError() == cudaSuccess ? 0 : -2;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3(GEMV_WARPS * 32);
+    cfg.dynamicSmemBytes = (size_t)smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = L.overlap ? 1 : 0;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = csize;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    if (cudaLaunchKernelEx(&cfg, gemv_kernel<T>, p) != cudaSuccess) return -2;
+    return 0;
 }
 
 int launch_gemv(uint32_t wtype, const GemvLaunch &L, cudaStream_t st) {

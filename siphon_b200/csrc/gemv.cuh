@@ -27,18 +27,24 @@
 namespace sicu {
 
 constexpr int GEMV_WARPS = 8;
-constexpr int ACT_STRIDE = 272;    // bytes per prepared 256-element activation unit (17 x 16 B)
 constexpr int MAX_CHAINS = 9;
-constexpr int TERM_FLOATS = 32 * MAX_CHAINS;   // >= 32 units x 9 chains, >= 32 units x 8 blocks
-constexpr int WARP_HDR = 64 + 4 * (TERM_FLOATS + 64) + 64;   // barriers, terms, chain results (128-aligned)
+// term buffer: K formats [chain][row][unit padded to 4] with rows x units <= 32
+// and rows <= 7 (<= 9 x 53 floats); classic [row][8 x unit] (<= 256 floats)
+constexpr int TERM_FLOATS = 480;
+constexpr int CONS_BYTES = 4 * (TERM_FLOATS + 64);   // per consumer warp: terms, chain results
+
+constexpr int GEMV_MAX_MATS = 64;
 
 struct GemvParams {
-    const uint8_t *w;      // weight blocks, row-major, 16-byte aligned base
+    // the matrices of one launch: same format and row length, one activation
+    int nmat;
+    const uint8_t *w[GEMV_MAX_MATS];   // weight blocks, row-major, 16-byte aligned
+    float *y[GEMV_MAX_MATS];
+    int n_out[GEMV_MAX_MATS];
+    int task0[GEMV_MAX_MATS + 1];      // first task of each matrix (prefix sums)
     const uint8_t *xq;     // pair-format activation (Q8_K / Q8_0 blocks), or null
     const float *xf;       // f32 activation for the fused quantize variant, or null
-    float *y;
     int64_t row_bytes;
-    int64_t n_out;
     int n_in;
     int nu;                // units per row
     int cu;                // units per chunk
@@ -46,9 +52,9 @@ struct GemvParams {
     int rows_per_task;     // R
     int64_t ntasks;
     int slot_bytes;
-    int nslots;
+    int nslots;            // ring slots per warp
     int act_bytes;         // prepared-activation region
-    int warp_bytes;        // per-warp region (barriers, terms, ring)
+    int warp_bytes;        // per-warp region: barriers, slot geometry, terms, ring
     int *status;
 };
 
@@ -59,14 +65,19 @@ struct GemvParams {
 //   ax : K formats: extra integer sums; classic: 8 per-block quant sums
 // ---------------------------------------------------------------------------
 struct ActView {
+    // one 368-byte record (23 x 16 B, an odd number of 16-byte units so lanes
+    // reading consecutive records never share a bank group) per 256 elements:
+    //   [0,256)   aq: 64 words of int8 quants in the decoder's order
+    //   [256,320) ax: 16 ints (format-dependent integer sums)
+    //   [320,352) ad: 8 floats (scales)
     uint8_t *base;
     int nu;
-    __device__ uint8_t *aq(int u) const { return base + (size_t)u * ACT_STRIDE; }
-    __device__ float *ad(int u) const { return reinterpret_cast<float *>(base + (size_t)nu * ACT_STRIDE) + u * 8; }
-    __device__ int *ax(int u) const {
-        return reinterpret_cast<int *>(base + (size_t)nu * ACT_STRIDE + (size_t)nu * 32) + u * 16;
-    }
-    static __host__ __device__ int bytes(int nu) { return nu * (ACT_STRIDE + 32 + 64); }
+    static constexpr int STRIDE = 368;
+    __device__ uint8_t *rec(int u) const { return base + (size_t)u * STRIDE; }
+    __device__ uint8_t *aq(int u) const { return rec(u); }
+    __device__ int *ax(int u) const { return reinterpret_cast<int *>(rec(u) + 256); }
+    __device__ float *ad(int u) const { return reinterpret_cast<float *>(rec(u) + 320); }
+    static __host__ __device__ int bytes(int nu) { return nu * STRIDE; }
 };
 
 // ---- format traits ----------------------------------------------------------
@@ -95,65 +106,95 @@ template <> struct Fmt<T_Q8_0> { static constexpr int kind = 3, unit_bytes = 8 *
 //         the block's 32 quants.
 // src points at the raw pair-format row (global or shared memory).
 // ---------------------------------------------------------------------------
-// K formats: prepare 32-element piece j of super-block u from a raw Q8_K block.
+// Writes a record field into the same place of every CTA of the thread-block
+// cluster (distributed shared memory), so each activation record is built once
+// per cluster instead of once per CTA.
+struct RecWriter {
+    uint32_t nrank;
+    __device__ void put4(const void *local, uint32_t a, uint32_t b, uint32_t c, uint32_t d) const {
+        const uint32_t addr = smem_addr(local);
+        for (uint32_t r = 0; r < nrank; ++r) st_cluster4(mapa(addr, r), a, b, c, d);
+    }
+    __device__ void put(const void *local, uint32_t v) const {
+        const uint32_t addr = smem_addr(local);
+        for (uint32_t r = 0; r < nrank; ++r) st_cluster(mapa(addr, r), v);
+    }
+};
+
+// K formats: piece j (elements 32j..32j+31) of record u from 8 natural-order
+// quant words, the piece's two 16-element sums, and (j == 0) the block scale.
 template <int ACT>
-__device__ __forceinline__ void prep_piece(const ActView av, const uint8_t *blk, int u, int j) {
-    const uint32_t *qs = reinterpret_cast<const uint32_t *>(blk + 4 + 32 * j);
-    uint32_t v[8];
-#pragma unroll
-    for (int k = 0; k < 8; ++k) v[k] = qs[k];
-    uint32_t *dst = reinterpret_cast<uint32_t *>(av.aq(u)) + 8 * j;
+__device__ __forceinline__ void put_piece(const ActView av, const RecWriter &wr, int u, int j, const uint32_t q[8],
+                                          int s0, int s1, float d) {
+    uint32_t o[8];
     if constexpr (ACT == 0) {
-        transpose4(v[0], v[2], v[4], v[6], dst[0], dst[1], dst[2], dst[3]);
-        transpose4(v[1], v[3], v[5], v[7], dst[4], dst[5], dst[6], dst[7]);
+        transpose4(q[0], q[2], q[4], q[6], o[0], o[1], o[2], o[3]);
+        transpose4(q[1], q[3], q[5], q[7], o[4], o[5], o[6], o[7]);
     } else if constexpr (ACT == 1) {
-        // two 16-element sub-blocks: words (v0,v1,v2,v3) = elements 0..15
-        transpose4(v[0], v[2], v[1], v[3], dst[0], dst[1], dst[2], dst[3]);
-        transpose4(v[4], v[6], v[5], v[7], dst[4], dst[5], dst[6], dst[7]);
+        // two 16-element sub-blocks: words (q0,q1,q2,q3) = elements 0..15
+        transpose4(q[0], q[2], q[1], q[3], o[0], o[1], o[2], o[3]);
+        transpose4(q[4], q[6], q[5], q[7], o[4], o[5], o[6], o[7]);
     } else {
 #pragma unroll
-        for (int k = 0; k < 8; ++k) dst[k] = v[k];
+        for (int k = 0; k < 8; ++k) o[k] = q[k];
     }
-    if (j == 0) {
-        av.ad(u)[0] = *reinterpret_cast<const float *>(blk);
-        const int16_t *bs = reinterpret_cast<const int16_t *>(blk + 260);
-        if constexpr (ACT == 0) {
-#pragma unroll
-            for (int k = 0; k < 8; ++k) av.ax(u)[k] = (int)bs[2 * k] + (int)bs[2 * k + 1];
-        } else if constexpr (ACT == 2) {
-#pragma unroll
-            for (int k = 0; k < 16; ++k) av.ax(u)[k] = bs[k];
-        }
+    uint8_t *rec = av.rec(u);
+    wr.put4(rec + 32 * j, o[0], o[1], o[2], o[3]);
+    wr.put4(rec + 32 * j + 16, o[4], o[5], o[6], o[7]);
+    if constexpr (ACT == 0) {
+        wr.put(av.ax(u) + j, (uint32_t)(s0 + s1));
+    } else if constexpr (ACT == 2) {
+        wr.put(av.ax(u) + 2 * j, (uint32_t)s0);
+        wr.put(av.ax(u) + 2 * j + 1, (uint32_t)s1);
     }
+    if (j == 0) wr.put(av.ad(u), __float_as_uint(d));
 }
 
-// Build the prepared layout from the caller's pair-format row (global memory).
+// Classic formats: block bi of record u.
+__device__ __forceinline__ void put_block(const ActView av, const RecWriter &wr, int u, int bi, const uint32_t q[8],
+                                          float d, int asum) {
+    uint8_t *rec = av.rec(u);
+    wr.put4(rec + 32 * bi, q[0], q[1], q[2], q[3]);
+    wr.put4(rec + 32 * bi + 16, q[4], q[5], q[6], q[7]);
+    wr.put(av.ad(u) + bi, __float_as_uint(d));
+    wr.put(av.ax(u) + bi, (uint32_t)asum);
+}
+
+// Build the records this cluster rank owns (u % nrank == rank) from the
+// caller's pair-format row in global memory.
 template <int ACT>
-__device__ void prep_activation(const ActView av, const uint8_t *src, int n_in) {
+__device__ void prep_activation(const ActView av, const uint8_t *src, int n_in, uint32_t rank, uint32_t nrank) {
+    const RecWriter wr{nrank};
     const int tid = threadIdx.x, nt = blockDim.x;
     if constexpr (ACT == 3) {
-        const int nblk = n_in / 32;
-        for (int b = tid; b < nblk; b += nt) {
+        const int nblk = n_in / 32, nu = (nblk + 7) / 8;
+        const int mine = (nu - (int)rank + (int)nrank - 1) / (int)nrank;
+        for (int i = tid; i < mine * 8; i += nt) {
+            const int u = (int)rank + (int)nrank * (i >> 3), b = 8 * u + (i & 7);
+            if (b >= nblk) continue;
             // qs start at byte 2 of a 34-byte block: read halves and rejoin
             const uint16_t *h = reinterpret_cast<const uint16_t *>(src + (size_t)b * B_Q8_0);
-            uint32_t wv[8];
+            uint32_t q[8];
             int s = 0;
 #pragma unroll
             for (int k = 0; k < 8; ++k) {
-                wv[k] = (uint32_t)h[1 + 2 * k] | ((uint32_t)h[2 + 2 * k] << 16);
-                s = dp4a_ss(wv[k], 0x01010101u, s);
+                q[k] = (uint32_t)h[1 + 2 * k] | ((uint32_t)h[2 + 2 * k] << 16);
+                s = dp4a_ss(q[k], 0x01010101u, s);
             }
-            const int u = b >> 3, bi = b & 7;
-            uint32_t *dst = reinterpret_cast<uint32_t *>(av.aq(u)) + bi * 8;
-#pragma unroll
-            for (int k = 0; k < 8; ++k) dst[k] = wv[k];
-            av.ad(u)[bi] = h2f(h[0]);
-            av.ax(u)[bi] = s;
+            put_block(av, wr, u, i & 7, q, h2f(h[0]), s);
         }
     } else {
-        for (int p = tid; p < (n_in / 256) * 8; p += nt) {
-            const int u = p >> 3;
-            prep_piece<ACT>(av, src + (size_t)u * B_Q8_K, u, p & 7);
+        const int nu = n_in / 256;
+        const int mine = (nu - (int)rank + (int)nrank - 1) / (int)nrank;
+        for (int i = tid; i < mine * 8; i += nt) {
+            const int u = (int)rank + (int)nrank * (i >> 3), j = i & 7;
+            const uint8_t *blk = src + (size_t)u * B_Q8_K;
+            const uint32_t *qs = reinterpret_cast<const uint32_t *>(blk + 4 + 32 * j);
+            uint32_t q[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) q[k] = qs[k];
+            const int16_t *bs = reinterpret_cast<const int16_t *>(blk + 260);
+            put_piece<ACT>(av, wr, u, j, q, bs[2 * j], bs[2 * j + 1], *reinterpret_cast<const float *>(blk));
         }
     }
 }
@@ -168,8 +209,12 @@ __device__ __forceinline__ int sbyte_of(uint32_t w, int i) { return ((int)(w << 
 
 // Q4_K (src/kernels.c:349-410): 16-byte aligned in shared memory.
 template <bool Q5>
-__device__ __forceinline__ void unit_q45k(const uint8_t *wb, const uint8_t *aq, float yd, const int *pb, float *t) {
+__device__ __forceinline__ void unit_q45k(const uint8_t *wb, const uint8_t *aq, float *t) {
     const uint4 h = *reinterpret_cast<const uint4 *>(wb);
+    const int4 pb0 = *reinterpret_cast<const int4 *>(aq + 256);
+    const int4 pb1 = *reinterpret_cast<const int4 *>(aq + 272);
+    const int pb[8] = {pb0.x, pb0.y, pb0.z, pb0.w, pb1.x, pb1.y, pb1.z, pb1.w};
+    const float yd = reinterpret_cast<const float4 *>(aq + 320)->x;
     // 6-bit scales/mins (src/kernels.c:377-382 / 648-656), four per word
     const uint32_t sc_lo = h.y & 0x3f3f3f3fu;
     const uint32_t mn_lo = h.z & 0x3f3f3f3fu;
@@ -201,20 +246,30 @@ __device__ __forceinline__ void unit_q45k(const uint8_t *wb, const uint8_t *aq, 
         const uint32_t alo[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
         const uint32_t ahi[8] = {a2.x, a2.y, a2.z, a2.w, a3.x, a3.y, a3.z, a3.w};
         const uint32_t scw = c < 2 ? sc_lo : sc_hi;
-        const int s0 = (int)byte_of(scw, (2 * c) & 3), s1 = (int)byte_of(scw, (2 * c + 1) & 3);
+        // the high nibbles stay in place (16x their value); the low-nibble
+        // scale carries the same factor 16, divided out exactly below
+        const int s0 = 16 * (int)byte_of(scw, (2 * c) & 3), s1 = (int)byte_of(scw, (2 * c + 1) & 3);
 #pragma unroll
         for (int l = 0; l < 8; ++l) {
-            uint32_t lo = tq[l] & 0x0f0f0f0fu;
-            uint32_t hi = (tq[l] >> 4) & 0x0f0f0f0fu;
+            uint32_t lo, hi;
             if constexpr (Q5) {
-                // fifth bit of sub-block 2c / 2c+1 is bit 2c / 2c+1 of qh[b]
+                // fifth bit of sub-block 2c / 2c+1 is bit 2c / 2c+1 of qh[b]:
+                // bit 4 of a low byte, bit 8 (= bit 4 of 16 x value) of a high one
                 const uint32_t b0 = (c <= 2 ? (ht[l] << (4 - 2 * c)) : (ht[l] >> (2 * c - 4))) & 0x10101010u;
                 const uint32_t b1 = (c <= 1 ? (ht[l] << (3 - 2 * c)) : (ht[l] >> (2 * c - 3))) & 0x10101010u;
-                lo |= b0;
-                hi |= b1;
+                lo = and_or(tq[l], 0x0f0f0f0fu, b0);
+                hi = ((tq[l] >> 4) & 0x0f0f0f0fu) | b1;
+                aux[l] += dp4a(lo, alo[l], 0) * (s0 >> 4) + dp4a(hi, ahi[l], 0) * s1;
+            } else {
+                lo = tq[l] & 0x0f0f0f0fu;
+                hi = tq[l] & 0xf0f0f0f0u;
+                aux[l] += dp4a(lo, alo[l], 0) * s0 + dp4a(hi, ahi[l], 0) * s1;
             }
-            aux[l] += dp4a(lo, alo[l], 0) * s0 + dp4a(hi, ahi[l], 0) * s1;
         }
+    }
+    if constexpr (!Q5) {
+#pragma unroll
+        for (int l = 0; l < 8; ++l) aux[l] >>= 4;   // exact: every term carries a factor 16
     }
     const int mins = (int)byte_of(mn_lo, 0) * pb[0] + (int)byte_of(mn_lo, 1) * pb[1] +
                      (int)byte_of(mn_lo, 2) * pb[2] + (int)byte_of(mn_lo, 3) * pb[3] +
@@ -223,7 +278,9 @@ __device__ __forceinline__ void unit_q45k(const uint8_t *wb, const uint8_t *aq, 
     const float d = __fmul_rn(h2f(h.x & 0xffffu), yd);
 #pragma unroll
     for (int l = 0; l < 8; ++l) t[l] = __fmul_rn(d, __int2float_rn(aux[l]));
-    t[8] = __fmul_rn(__fmul_rn(h2f(h.x >> 16), yd), __int2float_rn(mins));
+    // the reference subtracts this term (sumf -= dmin*sumi); a - b == a + (-b)
+    // exactly in IEEE arithmetic, so it is stored negated and added like the rest
+    t[8] = -__fmul_rn(__fmul_rn(h2f(h.x >> 16), yd), __int2float_rn(mins));
 }
 
 // Realigned 32-bit reads from a 2-byte aligned shared address.
@@ -247,8 +304,9 @@ __device__ __forceinline__ uint32_t pair_sel(int b) {
 // sub-blocks, int8 quants built as 4*v (Q6_K) / 32*v (Q3_K) so the sign sits
 // in bit 7, paired by element (e, e+8) into int16 for dp2a.
 template <bool Q3>
-__device__ __forceinline__ void unit_q36k(const uint8_t *wb, const uint8_t *aq, float yd, float *t) {
+__device__ __forceinline__ void unit_q36k(const uint8_t *wb, const uint8_t *aq, float *t) {
     const Words W(wb);
+    const float yd = reinterpret_cast<const float4 *>(aq + 320)->x;
     int aux[8];
 #pragma unroll
     for (int l = 0; l < 8; ++l) aux[l] = 0;
@@ -329,8 +387,15 @@ __device__ __forceinline__ void unit_q36k(const uint8_t *wb, const uint8_t *aq, 
 }
 
 // Q2_K (src/kernels.c:249-287): one integer sum per super-block. 4-byte aligned.
-__device__ __forceinline__ void unit_q2k(const uint8_t *wb, const uint8_t *aq, float yd, const int *bs, float *t) {
+__device__ __forceinline__ void unit_q2k(const uint8_t *wb, const uint8_t *aq, float *t) {
     const uint32_t *w = reinterpret_cast<const uint32_t *>(wb);
+    int bs[16];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const int4 v = reinterpret_cast<const int4 *>(aq + 256)[k];
+        bs[4 * k] = v.x; bs[4 * k + 1] = v.y; bs[4 * k + 2] = v.z; bs[4 * k + 3] = v.w;
+    }
+    const float yd = reinterpret_cast<const float4 *>(aq + 320)->x;
     const uint32_t scw[4] = {w[0], w[1], w[2], w[3]};
     int isum = 0;
 #pragma unroll
@@ -364,9 +429,17 @@ __device__ __forceinline__ void unit_q2k(const uint8_t *wb, const uint8_t *aq, f
 // Classic 32-blocks (src/kernels.c:197-247): up to eight blocks per unit,
 // 2-byte aligned. Terms: Q4_0/Q5_0 (sumi*dx)*dy, Q8_0 sumi*(dx*dy).
 template <uint32_t T>
-__device__ __forceinline__ void unit_classic(const uint8_t *wb, int nblk, const uint8_t *aq, const float *dy,
-                                             const int *asum, float *t) {
+__device__ __forceinline__ void unit_classic(const uint8_t *wb, int nblk, const uint8_t *aq, float *t) {
     const Words W(wb);
+    float dy[8];
+    int asum[8];
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+        const float4 d = reinterpret_cast<const float4 *>(aq + 320)[k];
+        const int4 a = reinterpret_cast<const int4 *>(aq + 256)[k];
+        dy[4 * k] = d.x; dy[4 * k + 1] = d.y; dy[4 * k + 2] = d.z; dy[4 * k + 3] = d.w;
+        asum[4 * k] = a.x; asum[4 * k + 1] = a.y; asum[4 * k + 2] = a.z; asum[4 * k + 3] = a.w;
+    }
     constexpr int BW = (T == T_Q4_0) ? 9 : (T == T_Q5_0) ? 11 : 17;   // words per block pair
 #pragma unroll
     for (int p = 0; p < 4; ++p) {

@@ -7,15 +7,27 @@
 
 namespace sicu {
 
+constexpr int MAX_MATS = 64;
+
 struct GemvLaunch {
-    const void *w;        // weight blocks (device)
+    const void *w;        // weight blocks (device), single-matrix launches
     const void *xq;       // pair-format activation (device) or null
     const float *xf;      // f32 activation (device) for the fused quantizer, or null
-    float *y;             // [n_out] (device)
+    float *y;             // [n_out] (device), single-matrix launches
     int64_t n_out;
     int n_in;
+    // matrices of the launch (same format, same n_in, one activation):
+    // filled from w / y / n_out when nmat == 1
+    int nmat;
+    const void *wm[MAX_MATS];
+    float *ym[MAX_MATS];
+    int64_t n_outm[MAX_MATS];
     int num_sms;
     int smem_limit;       // opt-in dynamic shared memory per block
+    int smem_per_sm;      // shared memory per multiprocessor
+    int smem_reserved;    // shared memory the runtime reserves per block
+    int overlap;          // programmatic dependent launch: weights may stream before
+                          // earlier work in the stream completes
     int device;
     int *status;          // device status word
 };

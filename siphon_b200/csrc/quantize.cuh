@@ -113,31 +113,78 @@ __device__ __forceinline__ void q8_0_block(const float *x, uint32_t &d16, uint32
 }
 
 // Fused prologue: quantize the f32 activation straight into the prepared
-// shared-memory layout. `stage` is a 292-byte per-warp scratch in shared memory.
+// records this cluster rank owns (u % nrank == rank), writing each into every
+// CTA of the cluster. K formats: eight lanes per 256-element block, lane j
+// owning elements 32j..32j+31, so after one 3-step max reduction every lane
+// emits its own piece. Classic formats: one thread per 32-element block.
 template <int ACT>
-__device__ void quantize_into_act(const ActView av, const float *xf, int n_in, uint8_t *stage) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+__device__ void quantize_into_act(const ActView av, const float *xf, int n_in, uint32_t rank, uint32_t nrank) {
+    const RecWriter wr{nrank};
     if constexpr (ACT == 3) {
-        const int nblk = n_in / 32;
-        for (int b = threadIdx.x; b < nblk; b += blockDim.x) {
-            uint32_t d16, qw[8];
-            q8_0_block(xf + 32 * b, d16, qw);
+        const int nblk = n_in / 32, nu = (nblk + 7) / 8;
+        const int mine = (nu - (int)rank + (int)nrank - 1) / (int)nrank;
+        for (int i = threadIdx.x; i < mine * 8; i += blockDim.x) {
+            const int u = (int)rank + (int)nrank * (i >> 3), b = 8 * u + (i & 7);
+            if (b >= nblk) continue;
+            uint32_t d16, q[8];
+            q8_0_block(xf + 32 * b, d16, q);
             int s = 0;
 #pragma unroll
-            for (int k = 0; k < 8; ++k) s = dp4a_ss(qw[k], 0x01010101u, s);
-            const int u = b >> 3, bi = b & 7;
-            uint32_t *dst = reinterpret_cast<uint32_t *>(av.aq(u)) + bi * 8;
-#pragma unroll
-            for (int k = 0; k < 8; ++k) dst[k] = qw[k];
-            av.ad(u)[bi] = h2f(d16);
-            av.ax(u)[bi] = s;
+            for (int k = 0; k < 8; ++k) s = dp4a_ss(q[k], 0x01010101u, s);
+            put_block(av, wr, u, i & 7, q, h2f(d16), s);
         }
     } else {
-        for (int u = warp; u < n_in / 256; u += nw) {
-            q8k_block_warp(xf + 256 * u, stage, lane);
-            __syncwarp();
-            if (lane < 8) prep_piece<ACT>(av, stage, u, lane);
-            __syncwarp();
+        const int nsb = n_in / 256;
+        const int lane = threadIdx.x & 31, j = lane & 7;
+        const unsigned gmask = 0xffu << (lane & 24);
+        const int groups = blockDim.x >> 3;
+        for (int u = (int)rank + (int)nrank * (threadIdx.x >> 3); u < nsb; u += (int)nrank * groups) {
+            const float4 *src = reinterpret_cast<const float4 *>(xf + 256 * u + 32 * j);
+            float v[32];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                const float4 f = src[k];
+                v[4 * k] = f.x; v[4 * k + 1] = f.y; v[4 * k + 2] = f.z; v[4 * k + 3] = f.w;
+            }
+            // first element of largest magnitude (strict '>' keeps the earliest)
+            float best = 0.0f, bval = 0.0f;
+            int bi = 256;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+                const float a = fabsf(v[i]);
+                if (a > best) { best = a; bval = v[i]; bi = 32 * j + i; }
+            }
+#pragma unroll
+            for (int off = 1; off < 8; off <<= 1) {
+                const float ob = __shfl_xor_sync(gmask, best, off, 8);
+                const float ov = __shfl_xor_sync(gmask, bval, off, 8);
+                const int oi = __shfl_xor_sync(gmask, bi, off, 8);
+                if (ob > best || (ob == best && oi < bi)) { best = ob; bval = ov; bi = oi; }
+            }
+            uint32_t q[8];
+            int s0 = 0, s1 = 0;
+            float d = 0.0f;
+            if (best > 0.0f) {
+                const float iscale = __fdiv_rn(-127.0f, bval);
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                    uint32_t w = 0;
+#pragma unroll
+                    for (int b = 0; b < 4; ++b) {
+                        const float x = v[4 * k + b];
+                        int qq = isnan(x) ? (int)(__float_as_uint(x) & 0x3fffffu) : __float2int_rn(__fmul_rn(iscale, x));
+                        qq = qq < 127 ? qq : 127;
+                        if (k < 4) s0 += qq; else s1 += qq;
+                        w |= ((uint32_t)qq & 0xffu) << (8 * b);
+                    }
+                    q[k] = w;
+                }
+                d = __fdiv_rn(1.0f, iscale);
+            } else {
+#pragma unroll
+                for (int k = 0; k < 8; ++k) q[k] = 0u;
+            }
+            put_piece<ACT>(av, wr, u, j, q, s0, s1, d);
         }
     }
 }

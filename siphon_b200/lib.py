@@ -29,6 +29,7 @@ SIGNATURES = {
     "sicu_shutdown": [],
     "sicu_last_error": [C.c_char_p, C.c_size_t],
     "sicu_status": [C.POINTER(C.c_int)],
+    "sicu_set_overlap": [C.c_int],
     "sicu_malloc": [C.POINTER(C.c_void_p), C.c_size_t],
     "sicu_free": [_vp],
     "sicu_upload": [_vp, C.c_size_t, C.POINTER(C.c_void_p)],
@@ -43,6 +44,8 @@ SIGNATURES = {
     "sicu_quantize_pair": [_u32, _fp, _vp, _i64, _i64, _vp],
     "sicu_gemv": [_u32, _vp, _i64, _i64, _vp, _fp, _i64, _vp],
     "sicu_gemv_f32": [_u32, _vp, _i64, _i64, _fp, _fp, _i64, _vp],
+    "sicu_gemv_multi": [_u32, C.c_int, C.POINTER(C.c_void_p), C.POINTER(C.c_int64), _i64, _fp,
+                        C.POINTER(C.c_void_p), _vp],
     "sicu_gemv_host": [_u32, _vp, _i64, _i64, _fp, _fp, _vp],
     "sicu_row_to_f32": [_u32, _vp, _i64, C.POINTER(C.c_int64), _i64, _fp, _vp],
 }
@@ -94,6 +97,9 @@ class SiphonCuda:
     def shutdown(self) -> None:
         self.check(self.lib.sicu_shutdown())
 
+    def set_overlap(self, on: bool) -> None:
+        self.check(self.lib.sicu_set_overlap(1 if on else 0))
+
     def status(self) -> int:
         flags = C.c_int(0)
         self.check(self.lib.sicu_status(C.byref(flags)))
@@ -128,6 +134,13 @@ class SiphonCuda:
 
     def gemv_f32(self, wtype: int, dw, n_in: int, n_out: int, dx, dy, m: int = 1, stream=None) -> None:
         self.check(self.lib.sicu_gemv_f32(wtype, _ptr(dw), n_in, n_out, _ptr(dx), _ptr(dy), m, _ptr(stream)))
+
+    def gemv_multi(self, wtype: int, dws, n_outs, n_in: int, dx, dys, stream=None) -> None:
+        n = len(dws)
+        w_arr = (C.c_void_p * n)(*[_ptr(w) for w in dws])
+        y_arr = (C.c_void_p * n)(*[_ptr(y) for y in dys])
+        o_arr = (C.c_int64 * n)(*n_outs)
+        self.check(self.lib.sicu_gemv_multi(wtype, n, w_arr, o_arr, n_in, _ptr(dx), y_arr, _ptr(stream)))
 
     def gemv_host(self, wtype: int, dw, n_in: int, n_out: int, hx, hy, stream=None) -> None:
         self.check(self.lib.sicu_gemv_host(wtype, _ptr(dw), n_in, n_out, _ptr(hx), _ptr(hy), _ptr(stream)))

@@ -59,7 +59,9 @@ def test_f16(sicu, oracle, shape):
 
 @pytest.mark.parametrize("wt", Q.WEIGHT_TYPES, ids=lambda t: Q.NAMES[t])
 def test_activation_scales(sicu, oracle, wt):
-    for s, scale in enumerate((1e-20, 1e-3, 1e3, 1e20)):
+    # F16 activations saturate past 65504 and go subnormal below 6e-5
+    scales = (1e-6, 1e-3, 1e3, 1e4) if wt == Q.F16 else (1e-20, 1e-3, 1e3, 1e20)
+    for s, scale in enumerate(scales):
         _case(sicu, oracle, wt, 24, 1024, seed=10 + s, scale=scale)
 
 
@@ -126,3 +128,55 @@ def test_row_to_f32(sicu, oracle, wt):
 
 def test_status_clean_after_runs(sicu):
     assert sicu.status() == 0
+
+
+@pytest.mark.parametrize("wt", (Q.Q4_K, Q.Q6_K, Q.Q8_0), ids=lambda t: Q.NAMES[t])
+def test_overlap_dependent_chain(sicu, oracle, wt):
+    """With programmatic dependent launch on, a matvec whose activation is the
+    previous matvec's output must still read it only after it is complete."""
+    n = 2048
+    ws = [synth.weights(wt, n, n, seed=40 + i) for i in range(4)]
+    x = synth.activations(n, 1, seed=41)[0]
+    want = x
+    for w in ws:
+        want = oracle.gemv(wt, w, n, n, oracle.quantize_pair(wt, want)[0])
+    dws = [dev(w) for w in ws]
+    bufs = [dev(x)] + [empty_f32(n) for _ in ws]
+    sicu.set_overlap(True)
+    try:
+        for i, dw in enumerate(dws):
+            sicu.gemv_f32(wt, dw, n, n, bufs[i], bufs[i + 1])
+        got = host(bufs[-1])
+    finally:
+        sicu.set_overlap(False)
+    assert_bits_equal(got, want, "overlapped chain")
+
+
+@pytest.mark.parametrize("wt", Q.WEIGHT_TYPES, ids=lambda t: Q.NAMES[t])
+def test_multi_matrix_launch(sicu, oracle, wt):
+    """One launch over several matrices sharing an activation (the Q/K/V and
+    gate/up pattern) equals separate matvecs, bit for bit; empty matrices and
+    ragged row counts included."""
+    n_in = 2048
+    n_outs = [512, 128, 0, 77, 1024]
+    ws = [synth.weights(wt, n, n_in, seed=60 + i) for i, n in enumerate(n_outs)]
+    x = synth.activations(n_in, 1, seed=61)
+    xq = oracle.quantize_pair(wt, x)[0]
+    ys = [empty_f32(max(n, 1)) for n in n_outs]
+    sicu.gemv_multi(wt, [dev(w) for w in ws], n_outs, n_in, dev(x), ys)
+    for i, (w, n) in enumerate(zip(ws, n_outs)):
+        if n:
+            assert_bits_equal(host(ys[i])[:n], oracle.gemv(wt, w, n_in, n, xq), f"matrix {i}")
+
+
+def test_multi_matrix_many_copies(sicu, oracle):
+    wt, n_in, n_out, copies = Q.Q4_K, 4096, 1024, 40
+    w = synth.weights(wt, n_out, n_in, seed=70)
+    x = synth.activations(n_in, 1, seed=71)
+    want = oracle.gemv(wt, w, n_in, n_out, oracle.quantize_pair(wt, x)[0])
+    dw = dev(w)
+    dws = [dw] + [dw.clone() for _ in range(copies - 1)]
+    ys = [empty_f32(n_out) for _ in range(copies)]
+    sicu.gemv_multi(wt, dws, [n_out] * copies, n_in, dev(x), ys)
+    for i in range(copies):
+        assert_bits_equal(host(ys[i]), want, f"copy {i}")

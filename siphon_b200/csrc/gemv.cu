@@ -10,53 +10,72 @@ namespace sicu {
 
 namespace {
 
-// Producer cursor over a warp's items: task t (global over all matrices),
-// its matrix, chunk. Advances without divisions.
-struct Cursor {
-    int task, mat, chunk;
-    __device__ void seek(const GemvParams &p) {
+// Producer state of one warp: its next item (task t over all matrices, the
+// task's matrix, chunk) and the item's geometry, advanced incrementally.
+struct Producer {
+    int task, mat, chunk, row0, rows, u0, cu;
+    const uint8_t *w, *mend;   // current matrix and its end
+    const uint8_t *src;        // first byte of the item
+    uint32_t tailmask;         // slots that received lane-written tail bytes
+
+    template <uint32_t T>
+    __device__ void locate(const GemvParams &p) {   // task/chunk -> geometry
         while (mat + 1 < p.nmat && task >= p.task0[mat + 1]) ++mat;
+        w = p.w[mat];
+        mend = w + (int64_t)p.n_out[mat] * p.row_bytes;
+        row0 = (task - p.task0[mat]) * p.rows_per_task;
+        const int left = p.n_out[mat] - row0;
+        rows = left < p.rows_per_task ? left : p.rows_per_task;
+        u0 = chunk * p.cu;
+        cu = min(p.cu, p.nu - u0);
+        src = w + (int64_t)row0 * p.row_bytes + (int64_t)u0 * Fmt<T>::unit_bytes;
     }
+    template <uint32_t T>
     __device__ void next(const GemvParams &p, int step) {
-        if (++chunk == p.nchunks) { chunk = 0; task += step; seek(p); }
+        if (++chunk < p.nchunks) {
+            src += (int64_t)cu * Fmt<T>::unit_bytes;
+            u0 += cu;
+            cu = min(p.cu, p.nu - u0);
+        } else {
+            chunk = 0;
+            task += step;
+            locate<T>(p);
+        }
+    }
+    // Fill ring slot s with the current item: a 16-byte aligned bulk copy
+    // plus, at the very end of a matrix, up to 15 tail bytes written by this
+    // lane; publish the geometry next to the slot.
+    template <uint32_t T>
+    __device__ void produce(const GemvParams &p, int s, uint8_t *slot, int4 *info, uint32_t full, uint64_t policy) {
+        int64_t len;
+        if (p.nchunks == 1) {
+            len = (int64_t)rows * p.row_bytes;
+        } else {
+            const int64_t rest = p.row_bytes - (int64_t)u0 * Fmt<T>::unit_bytes;
+            const int64_t want = (int64_t)cu * Fmt<T>::unit_bytes;
+            len = want < rest ? want : rest;
+        }
+        const uintptr_t a = reinterpret_cast<uintptr_t>(src);
+        const uint8_t *al = reinterpret_cast<const uint8_t *>(a & ~uintptr_t(15));
+        const int head = (int)(a & 15);
+        int64_t bulk = (head + len + 15) & ~int64_t(15);
+        if (al + bulk > mend) bulk = (int64_t)(mend - al) & ~int64_t(15);
+        const int tail = (int)(head + len - bulk);
+        // generic writes to this slot before an async-proxy write to it need a proxy fence
+        if (tailmask & (1u << s)) {
+            fence_proxy_async();
+            tailmask &= ~(1u << s);
+        }
+        if (tail > 0) {
+            for (int i = 0; i < tail; ++i) slot[bulk + i] = (uint8_t)ldg_u8(al + bulk + i);
+            tailmask |= 1u << s;
+        }
+        info[0] = make_int4(row0, rows | (head << 16), u0, cu);
+        info[1] = make_int4(mat, 0, 0, 0);
+        mbar_expect_tx(full, (uint32_t)bulk);   // also the phase's one arrival
+        if (bulk > 0) bulk_g2s_hint(smem_addr(slot), al, (uint32_t)bulk, full, policy);
     }
 };
-
-// Producer (lane 0): fill a ring slot with the cursor's item, a 16-byte
-// aligned bulk copy plus, at the very end of a matrix, up to 15 tail bytes,
-// and publish the item's geometry next to the slot.
-template <uint32_t T>
-__device__ __forceinline__ void produce(const GemvParams &p, const Cursor &c, uint8_t *slot, int4 *info,
-                                        uint32_t full, uint64_t policy) {
-    const int row0 = (c.task - p.task0[c.mat]) * p.rows_per_task;
-    const int left = p.n_out[c.mat] - row0;
-    const int rows = left < p.rows_per_task ? left : p.rows_per_task;
-    const int u0 = c.chunk * p.cu;
-    const int cu = min(p.cu, p.nu - u0);
-    const uint8_t *w = p.w[c.mat];
-    const int64_t start = (int64_t)row0 * p.row_bytes + (int64_t)u0 * Fmt<T>::unit_bytes;
-    int64_t len;
-    if (p.nchunks == 1) {
-        len = (int64_t)rows * p.row_bytes;
-    } else {
-        const int64_t rest = p.row_bytes - (int64_t)u0 * Fmt<T>::unit_bytes;
-        const int64_t want = (int64_t)cu * Fmt<T>::unit_bytes;
-        len = want < rest ? want : rest;
-    }
-    const uintptr_t a = reinterpret_cast<uintptr_t>(w + start);
-    const uint8_t *al = reinterpret_cast<const uint8_t *>(a & ~uintptr_t(15));
-    const int head = (int)(a & 15);
-    const uint8_t *mend = w + (int64_t)p.n_out[c.mat] * p.row_bytes;
-    int64_t bulk = (head + len + 15) & ~int64_t(15);
-    if (al + bulk > mend) bulk = (int64_t)(mend - al) & ~int64_t(15);
-    const int tail = (int)(head + len - bulk);
-    for (int i = 0; i < tail; ++i) slot[bulk + i] = (uint8_t)ldg_u8(al + bulk + i);
-    info[0] = make_int4(row0, rows | (head << 16), u0, cu);
-    info[1] = make_int4(c.mat, 0, 0, 0);
-    fence_proxy_async();
-    mbar_expect_tx(full, (uint32_t)bulk);   // also the phase's one arrival
-    if (bulk > 0) bulk_g2s_hint(smem_addr(slot), al, (uint32_t)bulk, full, policy);
-}
 
 // a += src[0]; a += src[1]; ... in order, each a separate IEEE rounding.
 // src is 16-byte aligned.
@@ -108,17 +127,21 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 2) gemv_kernel(const GemvPara
         fence_mbar_init();
     }
     __syncwarp();
-    // producer cursor: item m is task t0 + warp + (m / nchunks) * W, chunk m % nchunks
-    Cursor pc{t0 + warp, 0, 0};
+    // producer: item m is task t0 + warp + (m / nchunks) * W, chunk m % nchunks
+    Producer pc;
+    pc.task = t0 + warp;
+    pc.mat = 0;
+    pc.chunk = 0;
+    pc.tailmask = 0;
     int pm = 0;
     uint64_t policy = 0;
-    if (lane == 0) {
-        pc.seek(p);
+    if (lane == 0 && items > 0) {
+        pc.locate<T>(p);
         // weights never depend on earlier kernels: start streaming right away
         policy = policy_evict_first();
         for (; pm < items && pm < S; ++pm) {
-            produce<T>(p, pc, slots + (size_t)pm * p.slot_bytes, &info[2 * pm], smem_addr(&full[pm]), policy);
-            pc.next(p, W);
+            pc.produce<T>(p, pm, slots + (size_t)pm * p.slot_bytes, &info[2 * pm], smem_addr(&full[pm]), policy);
+            pc.next<T>(p, W);
         }
     }
 
@@ -132,7 +155,11 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 2) gemv_kernel(const GemvPara
 
     const int r_l = p.nchunks == 1 ? lane / p.cu : 0;
     const int u_l = p.nchunks == 1 ? lane - r_l * p.cu : lane;
-    const int cup = (p.cu + 3) & ~3;   // K formats: padded chain stride
+    // chain strides in floats: a multiple of 4 that is an odd number of
+    // 16-byte units, so the chain lanes' vector loads hit distinct banks
+    int cup = (p.cu + 3) & ~3;
+    if (((cup >> 2) & 1) == 0) cup += 4;   // K formats: [chain][row] stride
+    const int rstride = 8 * p.cu + 4;      // classic formats: row stride
     float acc[2] = {0.f, 0.f};
     int s = 0, chunk = 0;
     uint32_t parity = 0;
@@ -160,7 +187,7 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 2) gemv_kernel(const GemvPara
                 const int nb = min(8, p.n_in / 32 - ug * 8);
                 float t[8];
                 unit_classic<T>(wb, nb, rec, t);
-                float *dst = terms + (r_l * cu + u_l) * 8;
+                float *dst = terms + r_l * rstride + u_l * 8;
 #pragma unroll
                 for (int b = 0; b < 8; ++b) if (b < nb) dst[b] = t[b];
             } else {
@@ -177,8 +204,8 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 2) gemv_kernel(const GemvPara
         __syncwarp();
         // the slot is consumed: refill it with item m + S
         if (lane == 0 && pm < items) {
-            produce<T>(p, pc, slot, &info[2 * s], smem_addr(&full[s]), policy);
-            pc.next(p, W);
+            pc.produce<T>(p, s, slot, &info[2 * s], smem_addr(&full[s]), policy);
+            pc.next<T>(p, W);
             ++pm;
         }
 
@@ -191,7 +218,7 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 2) gemv_kernel(const GemvPara
                 const int r = q / CH, ch = q - r * CH;
                 if constexpr (F::kind == 3) {
                     const int nb = min(cu * 8, p.n_in / 32 - u0 * 8);
-                    acc[h] = chain_add(acc[h], terms + r * cu * 8, nb);
+                    acc[h] = chain_add(acc[h], terms + r * rstride, nb);
                 } else {
                     acc[h] = chain_add(acc[h], terms + (ch * p.rows_per_task + r) * cup, cu);
                 }

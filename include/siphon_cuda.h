@@ -151,6 +151,25 @@ SICU_API int sicu_gemv_multi(uint32_t wtype, int n_mats, const void *const *dw, 
 SICU_API int sicu_gemv_host(uint32_t wtype, const void *dw, int64_t n_in, int64_t n_out,
                    const float *hx, float *hy, void *stream);
 
+/* sicu_gemv_host for callers that must not allocate device memory: host
+ * code running under an application-owned device allocator that has already
+ * claimed the GPU's memory (so a library cudaMalloc would fail), hosts that
+ * forbid device allocation on the hot path because cudaMalloc/cudaFree can
+ * synchronise the device, and tools that load the library into a process
+ * whose allocations they do not control. The activation copy, the output
+ * before it returns to the host and a status word live in a fixed array
+ * compiled into the library (1.25 MiB on every device that loads it, held
+ * until the process exits); no call allocates anything. Limits: n_in <=
+ * 65536 and n_out <= 262144 (larger shapes are rejected with SICU_EINVAL;
+ * use sicu_gemv_host). The first call on a device resolves the array's device
+ * address and reads the device's launch limits, so make that first call
+ * before any stream capture. Every call uses the same array: calls whose GPU
+ * work overlaps (other streams, other host threads on the same device) race
+ * on it and must be serialised by the caller. sicu_init is not required.
+ * Same results as sicu_gemv_host. No counterpart in the reference. */
+SICU_API int sicu_gemv_host_noalloc(uint32_t wtype, const void *dw, int64_t n_in, int64_t n_out,
+                                    const float *hx, float *hy, void *stream);
+
 /* ---- dequantisation --------------------------------------------------------
  * Rows rows[0..nrows) (host array) of W into dout[nrows][n_in] f32, reference
  * semantics. Replaces cpu_row_to_f32 (src/backend.c:122-131) with

@@ -168,6 +168,18 @@ int run_gemv(uint32_t wt, GemvLaunch &L, cudaStream_t st) {
 
 }  // namespace
 
+namespace sicu {
+// Sets the calling thread's error message (read by sicu_last_error) from
+// other translation units of the library; returns code.
+int report_error(int code, const char *fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_err, sizeof g_err, fmt, ap);
+    va_end(ap);
+    return code;
+}
+}  // namespace sicu
+
 extern "C" {
 
 int sicu_init(int device) {

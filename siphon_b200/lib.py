@@ -47,6 +47,7 @@ SIGNATURES = {
     "sicu_gemv_multi": [_u32, C.c_int, C.POINTER(C.c_void_p), C.POINTER(C.c_int64), _i64, _fp,
                         C.POINTER(C.c_void_p), _vp],
     "sicu_gemv_host": [_u32, _vp, _i64, _i64, _fp, _fp, _vp],
+    "sicu_gemv_host_noalloc": [_u32, _vp, _i64, _i64, _fp, _fp, _vp],
     "sicu_row_to_f32": [_u32, _vp, _i64, C.POINTER(C.c_int64), _i64, _fp, _vp],
 }
 
@@ -144,6 +145,9 @@ class SiphonCuda:
 
     def gemv_host(self, wtype: int, dw, n_in: int, n_out: int, hx, hy, stream=None) -> None:
         self.check(self.lib.sicu_gemv_host(wtype, _ptr(dw), n_in, n_out, _ptr(hx), _ptr(hy), _ptr(stream)))
+
+    def gemv_host_noalloc(self, wtype: int, dw, n_in: int, n_out: int, hx, hy, stream=None) -> None:
+        self.check(self.lib.sicu_gemv_host_noalloc(wtype, _ptr(dw), n_in, n_out, _ptr(hx), _ptr(hy), _ptr(stream)))
 
     def row_to_f32(self, wtype: int, dw, n_in: int, rows, dout, stream=None) -> None:
         arr = (C.c_int64 * len(rows))(*rows)

@@ -293,3 +293,58 @@ class RefCpuGemv:
 
 def have_reference() -> bool:
     return REF_SO.exists()
+
+
+# ---- the reference engine, with the CPU or the CUDA backend ---------------------------
+
+E2E_SO = HERE / "_ref" / "libsiphon_e2e.so"
+
+
+class RefEngine:
+    """The reference's forward pass (si_engine_forward) on a GGUF file, every
+    layer's gemv on the reference CPU backend or on the CUDA backend adapter
+    (siphon_b200/csrc/backend_cuda.c). The output head runs on the CPU in
+    both, as in the reference (src/engine.c:393). scalar=True runs the
+    reference's scalar kernels for all host work (the parity target);
+    the first engine of a process fixes the mode."""
+
+    _lib = None
+
+    def __init__(self, path, use_cuda: bool = False, device: int = 0, n_ctx: int = 512, threads: int = 0,
+                 scalar: bool = True):
+        if RefEngine._lib is None:
+            if not E2E_SO.exists():
+                raise FileNotFoundError(f"{E2E_SO} not built (make -C oracle e2e)")
+            L = C.CDLL(str(E2E_SO))
+            L.e2e_error.restype = C.c_char_p
+            L.e2e_open.argtypes = [C.c_char_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(C.c_void_p)]
+            L.e2e_kern_impl.restype = C.c_char_p
+            L.e2e_open.restype = C.c_int
+            L.e2e_forward.argtypes = [C.c_void_p, C.c_uint32]
+            L.e2e_forward.restype = C.POINTER(C.c_float)
+            L.e2e_n_vocab.argtypes = [C.c_void_p]
+            L.e2e_n_vocab.restype = C.c_uint32
+            L.e2e_close.argtypes = [C.c_void_p]
+            L.e2e_close.restype = None
+            RefEngine._lib = L
+        self.L = RefEngine._lib
+        threads = threads or min(os.cpu_count() or 1, 16)
+        h = C.c_void_p()
+        rc = self.L.e2e_open(str(path).encode(), 1 if use_cuda else 0, device, n_ctx, threads,
+                             1 if scalar else 0, C.byref(h))
+        if rc != 0:
+            raise RuntimeError(f"e2e_open failed ({rc}): {self.L.e2e_error().decode()}")
+        self.h = h
+        self.n_vocab = self.L.e2e_n_vocab(h)
+        self.kern_impl = self.L.e2e_kern_impl().decode()
+
+    def forward(self, token: int) -> np.ndarray:
+        p = self.L.e2e_forward(self.h, token)
+        if not p:
+            raise RuntimeError(f"forward failed: {self.L.e2e_error().decode()}")
+        return np.ctypeslib.as_array(p, shape=(self.n_vocab,)).copy()
+
+    def close(self) -> None:
+        if self.h:
+            self.L.e2e_close(self.h)
+            self.h = None

@@ -170,6 +170,26 @@ SICU_API int sicu_gemv_host(uint32_t wtype, const void *dw, int64_t n_in, int64_
 SICU_API int sicu_gemv_host_noalloc(uint32_t wtype, const void *dw, int64_t n_in, int64_t n_out,
                                     const float *hx, float *hy, void *stream);
 
+/* ---- prefill ---------------------------------------------------------------
+ * Y = X W^T for a block of m prompt tokens: dy[t * n_out + r] = (W x_t)[r]
+ * for t < m (0 <= m <= 65535). dxq holds m consecutive rows of pair-format
+ * blocks (Q8_K for the K formats: sicu_quantize_q8_K); the _f32 form takes m
+ * f32 rows (16-byte aligned) and quantizes them first.
+ * Q4_K runs on the tensor cores (tcgen05 MMAs, accumulators in tensor memory,
+ * the token operand loaded by TMA): the integer sums per super-block are exact
+ * and the d / dmin scaling is applied per super-block, so each output agrees
+ * with the reference's per-row dot (src/kernels.c:349-410) within a relative
+ * 1e-5 of the L1 norm of its products, but is not bit-identical. Other types
+ * run the decode matvec once per token (bit-identical to the reference).
+ * The reference has no batched product: its prompt loop calls
+ * si_engine_forward once per token (src/cmd_run.c:276), i.e. one backend gemv
+ * per token and matrix. A per-device workspace grows on the first call with a
+ * larger m x n_in; make that call before any stream capture. */
+SICU_API int sicu_gemm_prefill(uint32_t wtype, const void *dw, int64_t n_in, int64_t n_out,
+                               const void *dxq, int64_t m, float *dy, void *stream);
+SICU_API int sicu_gemm_prefill_f32(uint32_t wtype, const void *dw, int64_t n_in, int64_t n_out,
+                                   const float *dx, int64_t m, float *dy, void *stream);
+
 /* ---- dequantisation --------------------------------------------------------
  * Rows rows[0..nrows) (host array) of W into dout[nrows][n_in] f32, reference
  * semantics. Replaces cpu_row_to_f32 (src/backend.c:122-131) with

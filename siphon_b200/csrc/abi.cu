@@ -34,6 +34,9 @@ struct DevState {
     // growable staging for the host-buffer entry points
     void *stage = nullptr;
     size_t stage_bytes = 0;
+    // growable workspace of the prefill product (token operand, f32 quantization)
+    void *pf_ws = nullptr;
+    size_t pf_ws_bytes = 0;
 };
 
 constexpr int MAX_DEV = 64;
@@ -94,6 +97,11 @@ int current(DevState *&ds) {
         return fail(SICU_EINVAL, "device %d not initialised (call sicu_init first)", dev);
     ds = &g_dev[dev];
     return SICU_OK;
+}
+
+int current_ok() {
+    DevState *ds;
+    return current(ds);
 }
 
 bool any_ready() {
@@ -216,6 +224,7 @@ int sicu_shutdown(void) {
         cudaSetDevice(d);
         cudaFree(ds.status);
         if (ds.stage) cudaFree(ds.stage);
+        if (ds.pf_ws) cudaFree(ds.pf_ws);
         ds = DevState{};
     }
     if (have && cur >= 0) cudaSetDevice(cur);
@@ -429,6 +438,97 @@ int sicu_gemv_host(uint32_t wtype, const void *dw, int64_t n_in, int64_t n_out, 
     }
     if ((e = cudaStreamSynchronize(st)) != cudaSuccess) return cuda_fail(e, "gemv_host sync");
     return SICU_OK;
+}
+
+// ---- prefill product -----------------------------------------------------------
+static int check_prefill(uint32_t wtype, const void *dw, int64_t n_in, int64_t n_out, const void *dx, int64_t m,
+                         const float *dy, uint32_t &pair) {
+    if (!pair_of(wtype, pair)) return fail(SICU_ENOTSUP, "prefill: unsupported weight type %s (%u)", tname(wtype), wtype);
+    uint32_t blck, bytes;
+    geometry(wtype, blck, bytes);
+    if (n_in <= 0 || n_out < 0 || m < 0)
+        return fail(SICU_EINVAL, "prefill: bad shape n_in=%lld n_out=%lld m=%lld", (long long)n_in, (long long)n_out,
+                    (long long)m);
+    if (n_in % blck)
+        return fail(SICU_EINVAL, "prefill: row length %lld of %s is not a multiple of %u", (long long)n_in, tname(wtype), blck);
+    if (n_in > (int64_t)1 << 20 || n_out > (int64_t)1 << 30 || m > 65535)
+        return fail(SICU_EINVAL, "prefill: shape too large (n_in <= 2^20, n_out <= 2^30, m <= 65535)");
+    if (m == 0 || n_out == 0) return SICU_OK;
+    if (!dw || !dx || !dy) return fail(SICU_EINVAL, "prefill: null pointer");
+    if (!aligned(dw, 16)) return fail(SICU_EINVAL, "prefill: weight pointer must be 16-byte aligned");
+    if (!aligned(dy, 4)) return fail(SICU_EINVAL, "prefill: output must be 4-byte aligned");
+    return SICU_OK;
+}
+
+static int grow_prefill_ws(DevState &ds, size_t need) {
+    if (ds.pf_ws_bytes >= need) return SICU_OK;
+    if (ds.pf_ws) cudaFree(ds.pf_ws);
+    ds.pf_ws = nullptr;
+    ds.pf_ws_bytes = 0;
+    if (cudaMalloc(&ds.pf_ws, need) != cudaSuccess) {
+        cudaGetLastError();
+        return fail(SICU_ENOMEM, "prefill workspace of %zu bytes", need);
+    }
+    ds.pf_ws_bytes = need;
+    return SICU_OK;
+}
+
+// xq: m rows of pair-format activation blocks (device), or null with xf set
+static int prefill_common(uint32_t wtype, const void *dw, int64_t n_in, int64_t n_out, const void *xq,
+                          const float *xf, int64_t m, float *dy, cudaStream_t st) {
+    DevState *ds;
+    if (int rc = current(ds)) return rc;
+    uint32_t pair;
+    pair_of(wtype, pair);
+    if (!prefill_supported(wtype)) {
+        // formats without a tensor-core kernel: the decode matvec per token
+        const int64_t prb = pair_row_bytes(pair, n_in);
+        for (int64_t i = 0; i < m; ++i) {
+            GemvLaunch L = make_launch(*ds, dw, n_in, n_out, dy + i * n_out);
+            if (xq) L.xq = static_cast<const uint8_t *>(xq) + i * prb;
+            else L.xf = xf + i * n_in;
+            if (int rc = run_gemv(wtype, L, st)) return rc;
+        }
+        return SICU_OK;
+    }
+    const size_t qbytes = xq ? 0 : (((size_t)m * pair_row_bytes(pair, n_in) + 255) & ~size_t(255));
+    if (int rc = grow_prefill_ws(*ds, qbytes + prefill_workspace_bytes(n_in, m))) return rc;
+    if (!xq) {
+        if (launch_quantize(pair, xf, ds->pf_ws, n_in, m, st) != 0) return cuda_fail(cudaGetLastError(), "prefill quantize");
+        xq = ds->pf_ws;
+    }
+    PrefillLaunch L{};
+    L.w = dw;
+    L.n_in = n_in;
+    L.n_out = n_out;
+    L.xq = xq;
+    L.m = m;
+    L.y = dy;
+    L.ws = static_cast<uint8_t *>(ds->pf_ws) + qbytes;
+    cudaGetDevice(&L.device);
+    L.status = ds->status;
+    const int rc = launch_prefill(wtype, L, st);
+    if (rc == -4) return fail(SICU_EIO, "prefill: tensor map encoding failed");
+    if (rc != 0) return cuda_fail(cudaGetLastError(), "prefill launch");
+    return SICU_OK;
+}
+
+int sicu_gemm_prefill(uint32_t wtype, const void *dw, int64_t n_in, int64_t n_out, const void *dxq, int64_t m,
+                      float *dy, void *stream) {
+    uint32_t pair;
+    if (int rc = check_prefill(wtype, dw, n_in, n_out, dxq, m, dy, pair)) return rc;
+    if (m == 0 || n_out == 0) return current_ok();
+    if (!aligned(dxq, pair == T_Q8_K ? 4 : 2)) return fail(SICU_EINVAL, "prefill: activation misaligned");
+    return prefill_common(wtype, dw, n_in, n_out, dxq, nullptr, m, dy, (cudaStream_t)stream);
+}
+
+int sicu_gemm_prefill_f32(uint32_t wtype, const void *dw, int64_t n_in, int64_t n_out, const float *dx, int64_t m,
+                          float *dy, void *stream) {
+    uint32_t pair;
+    if (int rc = check_prefill(wtype, dw, n_in, n_out, dx, m, dy, pair)) return rc;
+    if (m == 0 || n_out == 0) return current_ok();
+    if (!aligned(dx, 16)) return fail(SICU_EINVAL, "prefill: f32 activation must be 16-byte aligned");
+    return prefill_common(wtype, dw, n_in, n_out, nullptr, dx, m, dy, (cudaStream_t)stream);
 }
 
 int sicu_row_to_f32(uint32_t wtype, const void *dw, int64_t n_in, const int64_t *rows, int64_t nrows, float *dout,

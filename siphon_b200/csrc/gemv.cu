@@ -103,7 +103,7 @@ template <uint32_t T>
 __global__ void __launch_bounds__(GEMV_WARPS * 32, 2) gemv_kernel(const GemvParams p) {
     using F = Fmt<T>;
     constexpr int CH = F::chains;
-    constexpr int W = GEMV_WARPS;
+    const int W = (int)(blockDim.x >> 5);   // warps per CTA (<= GEMV_WARPS)
     extern __shared__ __align__(128) uint8_t smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int S = p.nslots;
@@ -295,21 +295,26 @@ static int launch_gemv_t(const GemvLaunch &L, cudaStream_t st) {
     const int64_t item_max = (p.nchunks == 1) ? p.rows_per_task * p.row_bytes : (int64_t)p.cu * F::unit_bytes;
     p.slot_bytes = (int)((item_max + 32 + 127) & ~int64_t(127));
     p.act_bytes = (ActView::bytes(p.nu) + 127) & ~127;
-    // two CTAs per SM when each warp keeps >= 2 ring slots, else one with up to 4
-    int ctas = 2, slots = 0;
+    // two CTAs per SM when each warp keeps >= 2 ring slots, with 8 warps per
+    // CTA or, for large slots, down to 6 (12 warps per SM still hide more
+    // latency than one CTA of 8); else one CTA of 8 warps with up to 4 slots
+    int ctas = 2, slots = 0, warps = GEMV_WARPS;
     const int hdr = 192 + CONS_BYTES;
-    for (; ctas >= 1; --ctas) {
+    for (bool found = false; ctas >= 1 && !found; --ctas) {
         const int per_cta = (ctas == 2) ? L.smem_per_sm / 2 - L.smem_reserved : L.smem_limit;
-        // a 128-aligned budget per warp, so rounding the region up stays inside it
-        const int per_warp = ((per_cta - p.act_bytes) / GEMV_WARPS & ~127) - hdr;
-        slots = per_warp > 0 ? per_warp / p.slot_bytes : 0;
-        if (slots > 4) slots = 4;
-        if (slots >= 2) break;
+        for (warps = GEMV_WARPS; warps >= (ctas == 2 ? 6 : GEMV_WARPS); --warps) {
+            // a 128-aligned budget per warp, so rounding the region up stays inside it
+            const int per_warp = ((per_cta - p.act_bytes) / warps & ~127) - hdr;
+            slots = per_warp > 0 ? per_warp / p.slot_bytes : 0;
+            if (slots > 4) slots = 4;
+            if (slots >= 2) { found = true; break; }
+        }
+        if (found) break;
     }
     if (slots < 2) return -1;
     p.nslots = slots;
     p.warp_bytes = (hdr + slots * p.slot_bytes + 127) & ~127;
-    const int smem = p.act_bytes + GEMV_WARPS * p.warp_bytes;
+    const int smem = p.act_bytes + warps * p.warp_bytes;
     static bool attr_set[64] = {};
     const int dev = L.device & 63;
     if (!attr_set[dev]) {
@@ -323,16 +328,16 @@ static int launch_gemv_t(const GemvLaunch &L, cudaStream_t st) {
     int csize = 1, capacity = target;
     {
         static std::mutex mu;
-        static std::map<std::pair<int, int>, std::pair<int, int>> cache;   // (device, smem) -> (C, capacity)
+        static std::map<std::pair<int, int>, std::pair<int, int>> cache;   // (device, smem x warps) -> (C, capacity)
         std::lock_guard<std::mutex> lk(mu);
-        const auto key = std::make_pair(dev, smem);
+        const auto key = std::make_pair(dev, smem * 16 + warps);
         auto hit = cache.find(key);
         if (hit == cache.end()) {
             int best_c = 1, best_cap = target;
             for (int c = 8; c >= 2; c /= 2) {
                 cudaLaunchConfig_t q{};
                 q.gridDim = dim3((unsigned)(target / c * c));
-                q.blockDim = dim3(GEMV_WARPS * 32);
+                q.blockDim = dim3(warps * 32);
                 q.dynamicSmemBytes = (size_t)smem;
                 cudaLaunchAttribute ca[1];
                 ca[0].id = cudaLaunchAttributeClusterDimension;
@@ -364,7 +369,7 @@ static int launch_gemv_t(const GemvLaunch &L, cudaStream_t st) {
     if (grid < 1) grid = 1;
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3((unsigned)grid);
-    cfg.blockDim = dim3(GEMV_WARPS * 32);
+    cfg.blockDim = dim3(warps * 32);
     cfg.dynamicSmemBytes = (size_t)smem;
     cfg.stream = st;
     cudaLaunchAttribute attr[2];

@@ -40,6 +40,22 @@ int launch_gemv_f16(const GemvLaunch &L, cudaStream_t st);
 // activation conversion of m rows of n floats into the pair format
 int launch_quantize(uint32_t pair, const float *x, void *y, int64_t n, int64_t m, cudaStream_t st);
 
+// prefill matrix product on the tensor cores: y[t][r] for m tokens (Q8_K rows)
+struct PrefillLaunch {
+    const void *w;        // weight blocks (device)
+    int64_t n_in, n_out;
+    const void *xq;       // m rows of Q8_K blocks (device)
+    int64_t m;
+    float *y;             // [m][n_out] (device)
+    void *ws;             // prefill_workspace_bytes(n_in, m) bytes, 256-byte aligned
+    int device;
+    int *status;
+};
+bool prefill_supported(uint32_t wtype);
+size_t prefill_workspace_bytes(int64_t n_in, int64_t m);
+// -3: no tensor-core kernel for the type; -4: tensor map encoding failed; -2: launch
+int launch_prefill(uint32_t wtype, const PrefillLaunch &L, cudaStream_t st);
+
 // dequantise rows (row_to_f32): rows[i] of w into out[i * n_in]
 int launch_dequant(uint32_t wtype, const void *w, int64_t n_in, const int64_t *rows_dev, int64_t nrows,
                    float *out, cudaStream_t st);

@@ -1,0 +1,120 @@
+// Inline-PTX wrappers for the 5th-generation tensor cores (tcgen05: MMA with
+// accumulators in tensor memory) and tiled TMA loads. sm_100a only.
+//
+// Descriptor layouts follow the PTX ISA "shared memory descriptor" and
+// "instruction descriptor" tables for tcgen05.mma (the same bit fields
+// CUTLASS names UMMA::SmemDescriptor / UMMA::InstrDescriptor).
+#pragma once
+
+#include <cuda.h>
+
+#include "common.cuh"
+
+namespace sicu {
+
+// ---- descriptors -----------------------------------------------------------------
+// Swizzle modes of a K-major operand tile in shared memory.
+constexpr uint32_t SMEM_SWZ_128B = 2, SMEM_SWZ_32B = 6;
+
+// Shared-memory matrix descriptor of a K-major operand:
+//   [0,14)  start address >> 4
+//   [16,30) leading-dimension byte offset >> 4 (not used by swizzled K-major
+//           tiles; 1 by convention)
+//   [32,46) stride byte offset >> 4: distance between 8-row core-matrix groups
+//   [46,48) descriptor version (1 on sm_100)
+//   [49,52) base offset (0: every tile starts on a swizzle-pattern boundary)
+//   [61,64) swizzle mode
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t sbo_bytes, uint32_t swizzle) {
+    return (uint64_t)((addr & 0x3ffffu) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(sbo_bytes >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)swizzle << 61);
+}
+
+// Instruction descriptor for kind::f16 with f16 A and B, f32 accumulation,
+// both operands K-major: [4,6) D format (1 = f32), [7,10) A format (0 = f16),
+// [10,13) B format (0 = f16), [15]/[16] A/B major (0 = K), [17,23) N >> 3,
+// [24,29) M >> 4.
+__host__ __device__ constexpr uint32_t idesc_f16_f32(int m, int n) {
+    return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+
+// ---- MMA ---------------------------------------------------------------------------
+// D[tmem] (+)= A[smem] * B[smem]^T, one elected thread issues.
+__device__ __forceinline__ void tc_mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                           uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+        :: "r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// The mbarrier gets one arrival once every MMA this thread issued so far has
+// completed (its shared-memory operands may then be overwritten, its
+// accumulator read).
+__device__ __forceinline__ void tc_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" :: "r"(bar)
+                 : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// ---- tensor memory -------------------------------------------------------------------
+// Whole warp: allocate ncols columns (power of two >= 32), address written to
+// shared memory at dst.
+__device__ __forceinline__ void tmem_alloc(uint32_t dst, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" :: "r"(dst), "r"(ncols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" :: "r"(taddr), "r"(ncols) : "memory");
+}
+// Whole warp: 32 lanes x 16 consecutive 32-bit columns; thread i receives lane
+// (lane field of taddr) + i. A warp may only address the 32-lane quarter
+// (warp id % 4) of tensor memory.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+        : "r"(taddr));
+}
+// Waits for this thread's tensor-memory loads; the registers are passed
+// through so no use of them can be scheduled before the wait.
+__device__ __forceinline__ void tmem_wait_ld(uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.wait::ld.sync.aligned;"
+        : "+r"(v[0]), "+r"(v[1]), "+r"(v[2]), "+r"(v[3]), "+r"(v[4]), "+r"(v[5]), "+r"(v[6]), "+r"(v[7]),
+          "+r"(v[8]), "+r"(v[9]), "+r"(v[10]), "+r"(v[11]), "+r"(v[12]), "+r"(v[13]), "+r"(v[14]), "+r"(v[15])
+        :: "memory");
+}
+
+// ---- tiled TMA ---------------------------------------------------------------------------
+// 2-D tile of a tensor map into this CTA's shared memory; x is the inner
+// (contiguous) coordinate and must be a multiple of 16 bytes.
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map, int x, int y, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+        :: "r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+        : "memory");
+}
+__device__ __forceinline__ void tma_prefetch_map(const CUtensorMap *map) {
+    asm volatile("prefetch.tensormap [%0];" :: "l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// ---- packed f16 ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t hfma2_u32(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t d;
+    asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+__device__ __forceinline__ uint32_t half2_bits(float lo, float hi) {
+    const __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t *>(&h);
+}
+__device__ __forceinline__ void sts128(uint32_t a, uint32_t x, uint32_t y, uint32_t z, uint32_t w) {
+    asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" :: "r"(a), "r"(x), "r"(y), "r"(z), "r"(w) : "memory");
+}
+
+}  // namespace sicu

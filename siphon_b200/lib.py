@@ -49,6 +49,8 @@ SIGNATURES = {
     "sicu_gemv_host": [_u32, _vp, _i64, _i64, _fp, _fp, _vp],
     "sicu_gemv_host_noalloc": [_u32, _vp, _i64, _i64, _fp, _fp, _vp],
     "sicu_row_to_f32": [_u32, _vp, _i64, C.POINTER(C.c_int64), _i64, _fp, _vp],
+    "sicu_gemm_prefill": [_u32, _vp, _i64, _i64, _vp, _i64, _fp, _vp],
+    "sicu_gemm_prefill_f32": [_u32, _vp, _i64, _i64, _fp, _i64, _fp, _vp],
 }
 
 
@@ -148,6 +150,12 @@ class SiphonCuda:
 
     def gemv_host_noalloc(self, wtype: int, dw, n_in: int, n_out: int, hx, hy, stream=None) -> None:
         self.check(self.lib.sicu_gemv_host_noalloc(wtype, _ptr(dw), n_in, n_out, _ptr(hx), _ptr(hy), _ptr(stream)))
+
+    def gemm_prefill(self, wtype: int, dw, n_in: int, n_out: int, dxq, m: int, dy, stream=None) -> None:
+        self.check(self.lib.sicu_gemm_prefill(wtype, _ptr(dw), n_in, n_out, _ptr(dxq), m, _ptr(dy), _ptr(stream)))
+
+    def gemm_prefill_f32(self, wtype: int, dw, n_in: int, n_out: int, dx, m: int, dy, stream=None) -> None:
+        self.check(self.lib.sicu_gemm_prefill_f32(wtype, _ptr(dw), n_in, n_out, _ptr(dx), m, _ptr(dy), _ptr(stream)))
 
     def row_to_f32(self, wtype: int, dw, n_in: int, rows, dout, stream=None) -> None:
         arr = (C.c_int64 * len(rows))(*rows)

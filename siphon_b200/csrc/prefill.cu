@@ -14,13 +14,15 @@
 // from the reference's lane sums. Outputs agree with the reference within a
 // relative 1e-5 of the L1 norm of the products.
 //
-// One CTA computes a 128-row x 128-token tile (one SM; 15 warps):
+// One CTA computes a 128-row x 128-token tile (one SM; 19 warps):
 //   warp 0      TMA: token operand (f16, 128-byte swizzle), bsums, dA
 //   warp 1      TMEM owner; lane 0 issues the MMAs
-//   warp 2      bulk copies of raw weight super-blocks (3 buffers)
-//   warps 3-6   weight converters: raw blocks -> f16 (sc*q) tiles in the
-//               swizzled K-major layout, mins tile, per-row d / dmin
-//   warps 7-14  epilogue: per super-block, S1/S2 from tensor memory, scale,
+//   warp 2      TMA of raw weight super-blocks (one 128-row tile of GGUF
+//               block bytes per super-block, 3 buffers)
+//   warps 3-10  weight converters: raw blocks -> f16 (sc*q) tiles in the
+//               swizzled K-major layout, mins tile, per-row d / dmin (thread =
+//               one row and one nibble half: 256 threads, two per scheduler)
+//   warps 11-18 epilogue: per super-block, S1/S2 from tensor memory, scale,
 //               accumulate in registers; write Y at the end (two warps per
 //               32-lane quarter of tensor memory, 64 token columns each)
 // Tensor memory: two accumulator sets (S1, S2: 128 columns each), so the MMAs
@@ -38,47 +40,72 @@ constexpr int PF_BM = 128;        // weight rows per tile (MMA M)
 constexpr int PF_BN = 128;        // tokens per tile (MMA N)
 constexpr int PF_KS = 64;         // k slots per pipeline stage: one 128-byte swizzle atom of f16
 constexpr int PF_STAGES = 4;
-constexpr int PF_NRAW = 3;
+constexpr int PF_NSB = 4;         // per-super-block buffers: mins / bsums tiles, scales
 constexpr int PF_STAGE_BYTES = PF_BM * PF_KS * 2;   // 16 KB; the token stage has the same size
 constexpr int PF_MIN_BYTES = PF_BM * 16 * 2;        // 4 KB: 128 rows x 16 f16 (32-byte swizzle)
 
-constexpr int W_TMA = 0, W_MMA = 1, W_RAW = 2, W_CONV = 3, N_CONV = 4, W_EPI = 7, N_EPI = 8;
-constexpr int PF_WARPS = 15;
+constexpr int W_TMA = 0, W_MMA = 1, W_RAW = 2, W_CONV = 3, N_CONV = 8, W_EPI = 11, N_EPI = 8;
+constexpr int PF_WARPS = 19;
 constexpr int EPI_COLS = PF_BN / 2;   // token columns per epilogue warp
 
-// shared-memory map (offsets from a 1024-byte aligned base)
-constexpr int OFF_A = 0;
-constexpr int OFF_B = OFF_A + PF_STAGES * PF_STAGE_BYTES;
-constexpr int OFF_RAW = OFF_B + PF_STAGES * PF_STAGE_BYTES;
-constexpr int RAW_BUF = PF_BM * B_Q4_K;                                  // 18432
-constexpr int OFF_A2 = (OFF_RAW + PF_NRAW * RAW_BUF + 1023) & ~1023;
-constexpr int OFF_B2 = OFF_A2 + 2 * PF_MIN_BYTES;
-constexpr int OFF_DA = OFF_B2 + 2 * PF_MIN_BYTES;
-constexpr int OFF_DW = OFF_DA + 2 * PF_BN * 4;
-constexpr int OFF_DM = OFF_DW + 2 * PF_BM * 4;
-constexpr int OFF_BAR = OFF_DM + 2 * PF_BM * 4;
+// Per-format geometry of the prefill kernel.
+//   KSTEPS  64-slot K-steps per super-block (weight slots = 64 * KSTEPS)
+//   RAW_ROW bytes per row of a raw weight tile (TMA box width; the 16-byte
+//           aligned span that holds the row's super-block)
+//   MINS    the format has a dmin * mins term (second accumulator)
+template <uint32_t T> struct PfFmt;
+// Q4_K: one f16 plane (sc * q); slots of K-step c = elements 64c..64c+63
+template <> struct PfFmt<T_Q4_K> {
+    static constexpr int BLOCK = B_Q4_K, RAW_ROW = 144, KSTEPS = 4, NRAW = 3;
+    static constexpr bool MINS = true;
+};
+// Q6_K: (q - 32) * sc with int8 sc = 16 hi + lo is split into two exact f16
+// planes, (q - 32) * lo against x and (q - 32) * hi against 16 x; K-steps 2c
+// and 2c+1 hold the two planes of elements 64c..64c+63. A super-block starts
+// at any even byte: the raw row is the 240-byte aligned span around it (an
+// odd number of 16-byte units, so 16-byte shared loads of consecutive rows
+// are free of bank conflicts).
+template <> struct PfFmt<T_Q6_K> {
+    static constexpr int BLOCK = B_Q6_K, RAW_ROW = 240, KSTEPS = 8, NRAW = 2;
+    static constexpr bool MINS = false;
+};
+
+template <uint32_t T> struct PfLayout {
+    using F = PfFmt<T>;
+    static constexpr int RAW_BUF = PF_BM * F::RAW_ROW;
+    static constexpr int OFF_A = 0;
+    static constexpr int OFF_B = OFF_A + PF_STAGES * PF_STAGE_BYTES;
+    static constexpr int OFF_RAW = OFF_B + PF_STAGES * PF_STAGE_BYTES;
+    static constexpr int MINB = F::MINS ? PF_NSB * PF_MIN_BYTES : 0;
+    static constexpr int OFF_A2 = (OFF_RAW + F::NRAW * RAW_BUF + 1023) & ~1023;
+    static constexpr int OFF_B2 = OFF_A2 + MINB;
+    static constexpr int OFF_DA = OFF_B2 + MINB;
+    static constexpr int OFF_DW = OFF_DA + PF_NSB * PF_BN * 4;
+    static constexpr int OFF_DM = OFF_DW + PF_NSB * PF_BM * 4;
+    static constexpr int OFF_BAR = OFF_DM + PF_NSB * PF_BM * 4;
+    static constexpr int OFF_FLAGS = OFF_BAR + 8 * 64;     // abort flag, TMEM address
+    static constexpr int SMEM = OFF_FLAGS + 16 + 1024;     // + alignment slack
+};
+
 // barriers
 enum {
     BAR_B_FULL = 0,                          // [4] token stage landed (TMA bytes)
-    BAR_A_FULL = BAR_B_FULL + PF_STAGES,     // [4] weight stage converted (4 warps)
+    BAR_A_FULL = BAR_B_FULL + PF_STAGES,     // [4] weight stage converted (8 warps)
     BAR_ST_EMPTY = BAR_A_FULL + PF_STAGES,   // [4] stage consumed by the MMAs (commit)
-    BAR_RAW_FULL = BAR_ST_EMPTY + PF_STAGES, // [3] raw super-block landed (bulk bytes)
-    BAR_RAW_EMPTY = BAR_RAW_FULL + PF_NRAW,  // [3] raw super-block converted (4 warps)
-    BAR_SBD_FULL = BAR_RAW_EMPTY + PF_NRAW,  // [2] bsums tile + dA landed (TMA bytes)
-    BAR_A2_FULL = BAR_SBD_FULL + 2,          // [2] mins tile, d, dmin written (4 warps)
-    BAR_SB_FREE = BAR_A2_FULL + 2,           // [2] epilogue done with a super-block (8 warps)
-    BAR_ACC_FULL = BAR_SB_FREE + 2,          // [2] accumulators of a super-block ready (commit)
+    BAR_RAW_FULL = BAR_ST_EMPTY + PF_STAGES, // [3] raw super-block landed (TMA bytes)
+    BAR_RAW_EMPTY = BAR_RAW_FULL + 3,        // [3] raw super-block converted (8 warps)
+    BAR_SBD_FULL = BAR_RAW_EMPTY + 3,        // [4] bsums tile + dA landed (TMA bytes)
+    BAR_A2_FULL = BAR_SBD_FULL + PF_NSB,     // [4] mins tile, d, dmin written (8 warps)
+    BAR_SB_FREE = BAR_A2_FULL + PF_NSB,      // [4] epilogue done with a super-block (8 warps)
+    BAR_ACC_FULL = BAR_SB_FREE + PF_NSB,     // [2] accumulators of a super-block ready (commit)
     BAR_ACC_EMPTY = BAR_ACC_FULL + 2,        // [2] accumulators read (8 warps)
     BAR_DRAIN = BAR_ACC_EMPTY + 2,           // teardown after an abandoned wait
     NBARS = BAR_DRAIN + 1,
 };
-constexpr int OFF_FLAGS = OFF_BAR + 8 * NBARS;   // abort flag, TMEM address
-constexpr int PF_SMEM = OFF_FLAGS + 16 + 1024;   // + alignment slack
+static_assert(NBARS <= 64, "barrier area");
 constexpr uint32_t PF_TMEM_COLS = 512;
 
 struct PfParams {
-    const uint8_t *w;     // weight blocks, row-major
-    int64_t row_bytes;
     int n_out;
     int nsb;              // super-blocks per row
     const float *da;      // [nsb][m_pad] token scales
@@ -91,9 +118,9 @@ struct PfParams {
 // Bounded wait shared by all roles: gives up when another role already gave
 // up, or after 2 s, recording the failure in the status word.
 __device__ __forceinline__ bool pf_wait(uint32_t bar, uint32_t parity, volatile int *abort_flag, int *status) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_poll(bar, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
-    while (!mbar_try_wait(bar, parity)) {
+    while (!mbar_poll(bar, parity)) {
         if (*abort_flag) return false;
         if (globaltimer_ns() - t0 > 2000000000ull) {
             *abort_flag = 1;
@@ -127,9 +154,183 @@ __device__ __forceinline__ uint32_t nib_f16(uint32_t x, uint32_t mask, uint32_t 
     return hfma2_u32(and_or(x, mask, 0x64006400u), mul, add);
 }
 
+// N words of a shared-memory span that starts at byte `head` (even, < 16)
+// of 16-byte aligned address a: loads the (N + 7) / 4 aligned 16-byte units
+// that cover it and funnels. head is the same for every thread of the CTA.
+template <int N>
+__device__ __forceinline__ void span_words(uint32_t a, int head, uint32_t (&W)[N]) {
+    constexpr int U = (N + 7) / 4;
+    uint32_t w[4 * U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+        const uint4 v = lds128(a + 16 * u);
+        w[4 * u] = v.x; w[4 * u + 1] = v.y; w[4 * u + 2] = v.z; w[4 * u + 3] = v.w;
+    }
+    const uint32_t sh = (uint32_t)(head & 2) * 8;
+    switch (head >> 2) {
+        case 0:
+#pragma unroll
+            for (int k = 0; k < N; ++k) W[k] = funnel(w[k], w[k + 1], sh);
+            break;
+        case 1:
+#pragma unroll
+            for (int k = 0; k < N; ++k) W[k] = funnel(w[k + 1], w[k + 2], sh);
+            break;
+        case 2:
+#pragma unroll
+            for (int k = 0; k < N; ++k) W[k] = funnel(w[k + 2], w[k + 3], sh);
+            break;
+        default:
+#pragma unroll
+            for (int k = 0; k < N; ++k) W[k] = funnel(w[k + 3], w[k + 4], sh);
+            break;
+    }
+}
+
+struct PfCtx {
+    uint32_t sb0;
+    uint8_t *smem;
+    volatile int *abort_flag;
+    int *status;
+};
+
+// Q4_K converter for one super-block. Thread: tile row r, nibble half g
+// (0: sub-block 2c from the low nibbles of qs[32c..], 1: 2c+1 from the high).
+template <class Lay>
+__device__ __forceinline__ bool convert_q4k(const PfCtx &cx, uint32_t base, int sb, int rb, int b4, int r, int g,
+                                            bool valid, uint32_t barbase) {
+    constexpr uint32_t FULL = 0xffffffffu;
+    auto bar = [&](int i) { return barbase + 8u * (uint32_t)i; };
+    const uint32_t raw = base + Lay::OFF_RAW + rb * Lay::RAW_BUF + r * B_Q4_K;
+    const uint4 h = valid ? lds128(raw) : make_uint4(0, 0, 0, 0);
+    // 6-bit scales / mins (src/kernels.c:377-382)
+    const uint32_t sc_lo = h.y & 0x3f3f3f3fu;
+    const uint32_t sc_hi = (h.w & 0x0f0f0f0fu) | ((h.y >> 2) & 0x30303030u);
+    // mins tile: column i (bsums index) holds mn[i / 2]; half g writes columns 8g..8g+7
+    const uint32_t mnw = g ? (((h.w >> 4) & 0x0f0f0f0fu) | ((h.z >> 2) & 0x30303030u)) : (h.z & 0x3f3f3f3fu);
+    uint32_t mw[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const float mv = (float)byte_at(mnw, j);
+        mw[j] = half2_bits(mv, mv);
+    }
+    sts128(base + Lay::OFF_A2 + b4 * PF_MIN_BYTES + swz32(r, g), mw[0], mw[1], mw[2], mw[3]);
+    if (g == 0) {
+        reinterpret_cast<float *>(cx.smem + Lay::OFF_DW)[b4 * PF_BM + r] = valid ? h2f(h.x & 0xffffu) : 0.0f;
+        reinterpret_cast<float *>(cx.smem + Lay::OFF_DM)[b4 * PF_BM + r] = valid ? h2f(h.x >> 16) : 0.0f;
+    }
+    fence_proxy_async();
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0) mbar_arrive(bar(BAR_A2_FULL + b4));
+    const uint32_t nmask = g ? 0x00f000f0u : 0x000f000fu;
+    for (int c = 0; c < 4; ++c) {
+        const int t = 4 * sb + c, s = t & 3;
+        if (!__all_sync(FULL, pf_wait(bar(BAR_ST_EMPTY + s), ((t >> 2) & 1) ^ 1, cx.abort_flag, cx.status)))
+            return false;
+        const uint32_t abase = base + Lay::OFF_A + s * PF_STAGE_BYTES;
+        const uint4 q0 = lds128(raw + 16 + 32 * c), q1 = lds128(raw + 32 + 32 * c);
+        const uint32_t x[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+        const float sv = valid ? (float)byte_at(c < 2 ? sc_lo : sc_hi, (2 * c + g) & 3) : 0.0f;
+        // (1024 + q) * sc - 1024 sc, or (1024 + 16 q) * sc/16 - 64 sc
+        const float mf = g ? 0.0625f * sv : sv, af = g ? -64.0f * sv : -1024.0f * sv;
+        const uint32_t mul = half2_bits(mf, mf), add = half2_bits(af, af);
+        // slot order inside each group of four: elements 0, 2, 1, 3
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const uint32_t u = x[2 * j], v = x[2 * j + 1];
+            sts128(abase + swz128(r, 4 * g + j), nib_f16(u, nmask, mul, add), nib_f16(u >> 8, nmask, mul, add),
+                   nib_f16(v, nmask, mul, add), nib_f16(v >> 8, nmask, mul, add));
+        }
+        fence_proxy_async();
+        __syncwarp();
+        if ((threadIdx.x & 31) == 0) mbar_arrive(bar(BAR_A_FULL + s));
+    }
+    return true;
+}
+
+// Q6_K converter for one super-block (src/kernels.c:480-523). Thread: tile
+// row r, half g of each 64-element quarter (elements 32g..32g+31 of it).
+// Quarter cq (h = cq / 2, group G = 2 (cq & 1) + g of half h) element l:
+// ql[64h + 32g + l] (low nibble for even cq, high for odd), qh[32h + l] bits
+// 2G..2G+1, scale sc[4cq + 2g + l / 16].
+template <class Lay>
+__device__ __forceinline__ bool convert_q6k(const PfCtx &cx, uint32_t base, int sb, int rb, int b4, int r, int g,
+                                            bool valid, uint32_t barbase) {
+    constexpr uint32_t FULL = 0xffffffffu;
+    auto bar = [&](int i) { return barbase + 8u * (uint32_t)i; };
+    const int head = (int)(((int64_t)sb * B_Q6_K) & 15);
+    const uint32_t row = base + Lay::OFF_RAW + rb * Lay::RAW_BUF + r * PfFmt<T_Q6_K>::RAW_ROW;
+    // scales (bytes 192..207) and d (208..209)
+    uint32_t S[5];
+    span_words<5>(row + 192, head, S);
+    if (!valid) {
+#pragma unroll
+        for (int k = 0; k < 5; ++k) S[k] = 0;
+    }
+    if (g == 0) reinterpret_cast<float *>(cx.smem + Lay::OFF_DW)[b4 * PF_BM + r] = h2f(S[4] & 0xffffu);
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0) mbar_arrive(bar(BAR_A2_FULL + b4));
+    for (int cq = 0; cq < 4; ++cq) {
+        const int t0 = 8 * sb + 2 * cq, s0 = t0 & 3, s1 = (t0 + 1) & 3;
+        if (!__all_sync(FULL, pf_wait(bar(BAR_ST_EMPTY + s0), ((t0 >> 2) & 1) ^ 1, cx.abort_flag, cx.status) &&
+                                  pf_wait(bar(BAR_ST_EMPTY + s1), (((t0 + 1) >> 2) & 1) ^ 1, cx.abort_flag, cx.status)))
+            return false;
+        const int h = cq >> 1, G = 2 * (cq & 1) + g;
+        uint32_t QL[8], QH[8];
+        span_words<8>(row + 64 * h + 32 * g, head, QL);
+        span_words<8>(row + 128 + 32 * h, head, QH);
+        // the two 16-element sub-blocks of this thread's 32 elements
+        const int sbi = 4 * cq + 2 * g;
+        const int sa = (int)(int8_t)byte_at(S[sbi >> 2], sbi & 3);
+        const int sb2 = (int)(int8_t)byte_at(S[(sbi + 1) >> 2], (sbi + 1) & 3);
+        const int sv[2] = {valid ? sa : 0, valid ? sb2 : 0};
+        uint32_t mul0[2], add0[2], mul1[2], add1[2];
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            const float lo = (float)(sv[i] & 15), hi = (float)(sv[i] >> 4);   // sc = 16 hi + lo
+            mul0[i] = half2_bits(lo, lo);
+            add0[i] = half2_bits(-1056.0f * lo, -1056.0f * lo);              // (1024 + q) lo - 1056 lo
+            mul1[i] = half2_bits(hi, hi);
+            add1[i] = half2_bits(-1056.0f * hi, -1056.0f * hi);
+        }
+        const uint32_t a0 = base + Lay::OFF_A + s0 * PF_STAGE_BYTES, a1 = base + Lay::OFF_A + s1 * PF_STAGE_BYTES;
+        const int nsh = (cq & 1) ? 4 : 0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int i = j >> 1;   // sub-block of words 2j, 2j+1
+            uint32_t p0[4], p1[4];
+#pragma unroll
+            for (int w2 = 0; w2 < 2; ++w2) {
+                const int k = 2 * j + w2;
+                // 6-bit q of elements 4k..4k+3, one per byte
+                const uint32_t q = ((QL[k] >> nsh) & 0x0f0f0f0fu) | (((QH[k] >> (2 * G)) & 0x03030303u) << 4);
+                const uint32_t e02 = and_or(q, 0x00ff00ffu, 0x64006400u);
+                const uint32_t e13 = and_or(q >> 8, 0x00ff00ffu, 0x64006400u);
+                p0[2 * w2] = hfma2_u32(e02, mul0[i], add0[i]);
+                p0[2 * w2 + 1] = hfma2_u32(e13, mul0[i], add0[i]);
+                p1[2 * w2] = hfma2_u32(e02, mul1[i], add1[i]);
+                p1[2 * w2 + 1] = hfma2_u32(e13, mul1[i], add1[i]);
+            }
+            sts128(a0 + swz128(r, 4 * g + j), p0[0], p0[1], p0[2], p0[3]);
+            sts128(a1 + swz128(r, 4 * g + j), p1[0], p1[1], p1[2], p1[3]);
+        }
+        fence_proxy_async();
+        __syncwarp();
+        if ((threadIdx.x & 31) == 0) {
+            mbar_arrive(bar(BAR_A_FULL + s0));
+            mbar_arrive(bar(BAR_A_FULL + s1));
+        }
+    }
+    return true;
+}
+
+template <uint32_t T>
 __global__ void __launch_bounds__(PF_WARPS * 32, 1)
-prefill_q4k_kernel(const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmS,
-                   const PfParams p) {
+prefill_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmB,
+               const __grid_constant__ CUtensorMap tmS, const PfParams p) {
+    using F = PfFmt<T>;
+    using Lay = PfLayout<T>;
+    constexpr int KST = F::KSTEPS;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const uint32_t sb0 = smem_addr(smem);
@@ -138,9 +339,10 @@ prefill_q4k_kernel(const __grid_constant__ CUtensorMap tmB, const __grid_constan
     const int row0 = rt * PF_BM, tok0 = tt * PF_BN;
     const int rows = min(PF_BM, p.n_out - row0);
     const int nsb = p.nsb;
-    volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + OFF_FLAGS);
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + OFF_FLAGS + 4);
-    auto bar = [&](int i) { return sb0 + OFF_BAR + 8u * (uint32_t)i; };
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + Lay::OFF_FLAGS);
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + Lay::OFF_FLAGS + 4);
+    const uint32_t barbase = sb0 + Lay::OFF_BAR;
+    auto bar = [&](int i) { return barbase + 8u * (uint32_t)i; };
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < PF_STAGES; ++i) {
@@ -148,14 +350,16 @@ prefill_q4k_kernel(const __grid_constant__ CUtensorMap tmB, const __grid_constan
             mbar_init(bar(BAR_A_FULL + i), N_CONV);
             mbar_init(bar(BAR_ST_EMPTY + i), 1);
         }
-        for (int i = 0; i < PF_NRAW; ++i) {
+        for (int i = 0; i < F::NRAW; ++i) {
             mbar_init(bar(BAR_RAW_FULL + i), 1);
             mbar_init(bar(BAR_RAW_EMPTY + i), N_CONV);
         }
-        for (int i = 0; i < 2; ++i) {
+        for (int i = 0; i < PF_NSB; ++i) {
             mbar_init(bar(BAR_SBD_FULL + i), 1);
             mbar_init(bar(BAR_A2_FULL + i), N_CONV);
             mbar_init(bar(BAR_SB_FREE + i), N_EPI);
+        }
+        for (int i = 0; i < 2; ++i) {
             mbar_init(bar(BAR_ACC_FULL + i), 1);
             mbar_init(bar(BAR_ACC_EMPTY + i), N_EPI);
         }
@@ -165,8 +369,9 @@ prefill_q4k_kernel(const __grid_constant__ CUtensorMap tmB, const __grid_constan
     }
     if (warp == W_MMA) tmem_alloc(smem_addr(tmem_slot), PF_TMEM_COLS);
     if (warp == W_TMA && lane == 0) {
+        tma_prefetch_map(&tmW);
         tma_prefetch_map(&tmB);
-        tma_prefetch_map(&tmS);
+        if constexpr (F::MINS) tma_prefetch_map(&tmS);
     }
     tc_fence_before();
     __syncthreads();
@@ -179,26 +384,28 @@ prefill_q4k_kernel(const __grid_constant__ CUtensorMap tmB, const __grid_constan
         if (lane == 0) {
             int t_issued = 0, sb_issued = 0;
             for (int sb = 0; sb < nsb; ++sb) {
-                const int b2 = sb & 1;
-                if (!pf_wait(bar(BAR_SB_FREE + b2), ((sb >> 1) & 1) ^ 1, abort_flag, p.status)) break;
-                mbar_expect_tx(bar(BAR_SBD_FULL + b2), PF_MIN_BYTES + PF_BN * 4);
-                tma_load_2d(sb0 + OFF_B2 + b2 * PF_MIN_BYTES, &tmS, 16 * sb, tok0, bar(BAR_SBD_FULL + b2));
-                bulk_g2s(sb0 + OFF_DA + b2 * PF_BN * 4, p.da + (size_t)sb * p.m_pad + tok0, PF_BN * 4,
-                         bar(BAR_SBD_FULL + b2));
+                const int b4 = sb % PF_NSB;
+                if (!pf_wait(bar(BAR_SB_FREE + b4), ((sb / PF_NSB) & 1) ^ 1, abort_flag, p.status)) break;
+                mbar_expect_tx(bar(BAR_SBD_FULL + b4), (F::MINS ? PF_MIN_BYTES : 0) + PF_BN * 4);
+                if constexpr (F::MINS)
+                    tma_load_2d(sb0 + Lay::OFF_B2 + b4 * PF_MIN_BYTES, &tmS, 16 * sb, tok0, bar(BAR_SBD_FULL + b4));
+                bulk_g2s(sb0 + Lay::OFF_DA + b4 * PF_BN * 4, p.da + (size_t)sb * p.m_pad + tok0, PF_BN * 4,
+                         bar(BAR_SBD_FULL + b4));
                 sb_issued = sb + 1;
                 bool ok = true;
-                for (int c = 0; c < 4; ++c) {
-                    const int t = 4 * sb + c, s = t & 3;
+                for (int c = 0; c < KST; ++c) {
+                    const int t = KST * sb + c, s = t & 3;
                     if (!pf_wait(bar(BAR_ST_EMPTY + s), ((t >> 2) & 1) ^ 1, abort_flag, p.status)) { ok = false; break; }
                     mbar_expect_tx(bar(BAR_B_FULL + s), PF_STAGE_BYTES);
-                    tma_load_2d(sb0 + OFF_B + s * PF_STAGE_BYTES, &tmB, PF_KS * t, tok0, bar(BAR_B_FULL + s));
+                    tma_load_2d(sb0 + Lay::OFF_B + s * PF_STAGE_BYTES, &tmB, PF_KS * t, tok0, bar(BAR_B_FULL + s));
                     t_issued = t + 1;
                 }
                 if (!ok) break;
             }
             if (*abort_flag) {
                 for (int t = max(0, t_issued - PF_STAGES); t < t_issued; ++t) pf_settle(bar(BAR_B_FULL + (t & 3)), (t >> 2) & 1);
-                for (int sb = max(0, sb_issued - 2); sb < sb_issued; ++sb) pf_settle(bar(BAR_SBD_FULL + (sb & 1)), (sb >> 1) & 1);
+                for (int sb = max(0, sb_issued - PF_NSB); sb < sb_issued; ++sb)
+                    pf_settle(bar(BAR_SBD_FULL + sb % PF_NSB), (sb / PF_NSB) & 1);
             }
         }
     } else if (warp == W_MMA) {
@@ -212,13 +419,13 @@ prefill_q4k_kernel(const __grid_constant__ CUtensorMap tmB, const __grid_constan
                 tc_fence_after();
                 const uint32_t d1 = tmem + (uint32_t)buf * 256u, d2 = d1 + 128u;
                 bool ok = true;
-                for (int c = 0; c < 4; ++c) {
-                    const int t = 4 * sb + c, s = t & 3;
+                for (int c = 0; c < KST; ++c) {
+                    const int t = KST * sb + c, s = t & 3;
                     const uint32_t sph = (t >> 2) & 1;
                     if (!pf_wait(bar(BAR_A_FULL + s), sph, abort_flag, p.status) ||
                         !pf_wait(bar(BAR_B_FULL + s), sph, abort_flag, p.status)) { ok = false; break; }
                     tc_fence_after();
-                    const uint32_t a = sb0 + OFF_A + s * PF_STAGE_BYTES, b = sb0 + OFF_B + s * PF_STAGE_BYTES;
+                    const uint32_t a = sb0 + Lay::OFF_A + s * PF_STAGE_BYTES, b = sb0 + Lay::OFF_B + s * PF_STAGE_BYTES;
 #pragma unroll
                     for (int kk = 0; kk < PF_KS / 16; ++kk)
                         tc_mma_f16(d1, smem_desc(a + 32 * kk, 1024, SMEM_SWZ_128B),
@@ -226,11 +433,15 @@ prefill_q4k_kernel(const __grid_constant__ CUtensorMap tmB, const __grid_constan
                     tc_commit(bar(BAR_ST_EMPTY + s));
                 }
                 if (!ok) break;
-                if (!pf_wait(bar(BAR_A2_FULL + buf), ph, abort_flag, p.status) ||
-                    !pf_wait(bar(BAR_SBD_FULL + buf), ph, abort_flag, p.status)) break;
-                tc_fence_after();
-                tc_mma_f16(d2, smem_desc(sb0 + OFF_A2 + buf * PF_MIN_BYTES, 256, SMEM_SWZ_32B),
-                           smem_desc(sb0 + OFF_B2 + buf * PF_MIN_BYTES, 256, SMEM_SWZ_32B), idesc, 0);
+                if constexpr (F::MINS) {
+                    const int b4 = sb % PF_NSB;
+                    const uint32_t ph4 = (sb / PF_NSB) & 1;
+                    if (!pf_wait(bar(BAR_A2_FULL + b4), ph4, abort_flag, p.status) ||
+                        !pf_wait(bar(BAR_SBD_FULL + b4), ph4, abort_flag, p.status)) break;
+                    tc_fence_after();
+                    tc_mma_f16(d2, smem_desc(sb0 + Lay::OFF_A2 + b4 * PF_MIN_BYTES, 256, SMEM_SWZ_32B),
+                               smem_desc(sb0 + Lay::OFF_B2 + b4 * PF_MIN_BYTES, 256, SMEM_SWZ_32B), idesc, 0);
+                }
                 tc_commit(bar(BAR_ACC_FULL + buf));
             }
             if (*abort_flag) {
@@ -239,83 +450,35 @@ prefill_q4k_kernel(const __grid_constant__ CUtensorMap tmB, const __grid_constan
             }
         }
     } else if (warp == W_RAW) {
-        // ---- raw weight super-blocks: one 144-byte bulk copy per row ----
-        int sb_issued = 0;
-        for (int sb = 0; sb < nsb; ++sb) {
-            const int rb = sb % PF_NRAW;
-            if (!__all_sync(FULL, pf_wait(bar(BAR_RAW_EMPTY + rb), ((sb / PF_NRAW) & 1) ^ 1, abort_flag, p.status)))
-                break;
-            if (lane == 0) mbar_expect_tx(bar(BAR_RAW_FULL + rb), (uint32_t)rows * B_Q4_K);
-            __syncwarp();
-            const uint8_t *src = p.w + (int64_t)row0 * p.row_bytes + (int64_t)sb * B_Q4_K;
-            for (int r = lane; r < rows; r += 32)
-                bulk_g2s(sb0 + OFF_RAW + rb * RAW_BUF + r * B_Q4_K, src + (int64_t)r * p.row_bytes, B_Q4_K,
-                         bar(BAR_RAW_FULL + rb));
-            sb_issued = sb + 1;
+        // ---- raw weight super-blocks: one 2-D tile (128 rows x RAW_ROW bytes) each ----
+        if (lane == 0) {
+            int sb_issued = 0;
+            for (int sb = 0; sb < nsb; ++sb) {
+                const int rb = sb % F::NRAW;
+                if (!pf_wait(bar(BAR_RAW_EMPTY + rb), ((sb / F::NRAW) & 1) ^ 1, abort_flag, p.status)) break;
+                mbar_expect_tx(bar(BAR_RAW_FULL + rb), Lay::RAW_BUF);
+                tma_load_2d(sb0 + Lay::OFF_RAW + rb * Lay::RAW_BUF, &tmW, (int)(((int64_t)sb * F::BLOCK) & ~int64_t(15)),
+                            row0, bar(BAR_RAW_FULL + rb));
+                sb_issued = sb + 1;
+            }
+            if (*abort_flag)
+                for (int sb = max(0, sb_issued - F::NRAW); sb < sb_issued; ++sb)
+                    pf_settle(bar(BAR_RAW_FULL + sb % F::NRAW), (sb / F::NRAW) & 1);
         }
-        if (*abort_flag && lane == 0)
-            for (int sb = max(0, sb_issued - PF_NRAW); sb < sb_issued; ++sb)
-                pf_settle(bar(BAR_RAW_FULL + sb % PF_NRAW), (sb / PF_NRAW) & 1);
     } else if (warp < W_EPI) {
-        // ---- weight converters: thread = tile row ----
-        const int r = (warp - W_CONV) * 32 + lane;
+        // ---- weight converters ----
+        const int cw = warp - W_CONV;
+        const int r = (cw & 3) * 32 + lane;
+        const int g = cw >> 2;
         const bool valid = r < rows;
+        const PfCtx cx{sb0, smem, abort_flag, p.status};
         for (int sb = 0; sb < nsb; ++sb) {
-            const int rb = sb % PF_NRAW, b2 = sb & 1;
-            if (!__all_sync(FULL, pf_wait(bar(BAR_RAW_FULL + rb), (sb / PF_NRAW) & 1, abort_flag, p.status))) break;
-            if (!__all_sync(FULL, pf_wait(bar(BAR_SB_FREE + b2), ((sb >> 1) & 1) ^ 1, abort_flag, p.status))) break;
-            const uint32_t raw = sb0 + OFF_RAW + rb * RAW_BUF + r * B_Q4_K;
-            const uint4 h = valid ? lds128(raw) : make_uint4(0, 0, 0, 0);
-            // 6-bit scales / mins (src/kernels.c:377-382)
-            const uint32_t sc_lo = h.y & 0x3f3f3f3fu;
-            const uint32_t mn_lo = h.z & 0x3f3f3f3fu;
-            const uint32_t sc_hi = (h.w & 0x0f0f0f0fu) | ((h.y >> 2) & 0x30303030u);
-            const uint32_t mn_hi = ((h.w >> 4) & 0x0f0f0f0fu) | ((h.z >> 2) & 0x30303030u);
-            reinterpret_cast<float *>(smem + OFF_DW)[b2 * PF_BM + r] = valid ? h2f(h.x & 0xffffu) : 0.0f;
-            reinterpret_cast<float *>(smem + OFF_DM)[b2 * PF_BM + r] = valid ? h2f(h.x >> 16) : 0.0f;
-            // mins tile: column i (bsums index) holds mn[i / 2]
-            uint32_t mw[8];
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const float mv = (float)byte_at(j < 4 ? mn_lo : mn_hi, j & 3);
-                mw[j] = half2_bits(mv, mv);
-            }
-            const uint32_t a2 = sb0 + OFF_A2 + b2 * PF_MIN_BYTES;
-            sts128(a2 + swz32(r, 0), mw[0], mw[1], mw[2], mw[3]);
-            sts128(a2 + swz32(r, 1), mw[4], mw[5], mw[6], mw[7]);
-            fence_proxy_async();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(bar(BAR_A2_FULL + b2));
-            bool ok = true;
-            for (int c = 0; c < 4; ++c) {
-                const int t = 4 * sb + c, s = t & 3;
-                if (!__all_sync(FULL, pf_wait(bar(BAR_ST_EMPTY + s), ((t >> 2) & 1) ^ 1, abort_flag, p.status))) {
-                    ok = false;
-                    break;
-                }
-                const uint32_t abase = sb0 + OFF_A + s * PF_STAGE_BYTES;
-                // sub-block 2c: low nibbles of qs[32c..32c+31]; 2c+1: high nibbles
-                const uint4 q0 = lds128(raw + 16 + 32 * c), q1 = lds128(raw + 32 + 32 * c);
-                const uint32_t x[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
-                const uint32_t scw = c < 2 ? sc_lo : sc_hi;
-                const float slo = valid ? (float)byte_at(scw, (2 * c) & 3) : 0.0f;
-                const float shi = valid ? (float)byte_at(scw, (2 * c + 1) & 3) : 0.0f;
-                const uint32_t mlo = half2_bits(slo, slo), alo = half2_bits(-1024.0f * slo, -1024.0f * slo);
-                const uint32_t mhi = half2_bits(0.0625f * shi, 0.0625f * shi), ahi = half2_bits(-64.0f * shi, -64.0f * shi);
-                // slot order inside each group of four: elements 0, 2, 1, 3
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const uint32_t u = x[2 * j], v = x[2 * j + 1];
-                    sts128(abase + swz128(r, j), nib_f16(u, 0x000f000fu, mlo, alo), nib_f16(u >> 8, 0x000f000fu, mlo, alo),
-                           nib_f16(v, 0x000f000fu, mlo, alo), nib_f16(v >> 8, 0x000f000fu, mlo, alo));
-                    sts128(abase + swz128(r, 4 + j), nib_f16(u, 0x00f000f0u, mhi, ahi),
-                           nib_f16(u >> 8, 0x00f000f0u, mhi, ahi), nib_f16(v, 0x00f000f0u, mhi, ahi),
-                           nib_f16(v >> 8, 0x00f000f0u, mhi, ahi));
-                }
-                fence_proxy_async();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(bar(BAR_A_FULL + s));
-            }
+            const int rb = sb % F::NRAW, b4 = sb % PF_NSB;
+            if (!__all_sync(FULL, pf_wait(bar(BAR_RAW_FULL + rb), (sb / F::NRAW) & 1, abort_flag, p.status))) break;
+            if (!__all_sync(FULL, pf_wait(bar(BAR_SB_FREE + b4), ((sb / PF_NSB) & 1) ^ 1, abort_flag, p.status))) break;
+            bool ok;
+            if constexpr (T == T_Q4_K) ok = convert_q4k<Lay>(cx, sb0, sb, rb, b4, r, g, valid, barbase);
+            else ok = convert_q6k<Lay>(cx, sb0, sb, rb, b4, r, g, valid, barbase);
             if (!ok) break;
             __syncwarp();
             if (lane == 0) mbar_arrive(bar(BAR_RAW_EMPTY + rb));
@@ -330,35 +493,36 @@ prefill_q4k_kernel(const __grid_constant__ CUtensorMap tmB, const __grid_constan
         for (int j = 0; j < EPI_COLS; ++j) acc[j] = 0.0f;
         bool ok = true;
         for (int sb = 0; sb < nsb && ok; ++sb) {
-            const int buf = sb & 1;
-            const uint32_t ph = (sb >> 1) & 1;
+            const int buf = sb & 1, b4 = sb % PF_NSB;
+            const uint32_t ph = (sb >> 1) & 1, ph4 = (sb / PF_NSB) & 1;
             if (!__all_sync(FULL, pf_wait(bar(BAR_ACC_FULL + buf), ph, abort_flag, p.status) &&
-                                      pf_wait(bar(BAR_A2_FULL + buf), ph, abort_flag, p.status) &&
-                                      pf_wait(bar(BAR_SBD_FULL + buf), ph, abort_flag, p.status))) {
+                                      pf_wait(bar(BAR_A2_FULL + b4), ph4, abort_flag, p.status) &&
+                                      pf_wait(bar(BAR_SBD_FULL + b4), ph4, abort_flag, p.status))) {
                 ok = false;
                 break;
             }
             tc_fence_after();
-            const float dw = reinterpret_cast<const float *>(smem + OFF_DW)[buf * PF_BM + r];
-            const float ndm = -reinterpret_cast<const float *>(smem + OFF_DM)[buf * PF_BM + r];
-            const float4 *da4 = reinterpret_cast<const float4 *>(smem + OFF_DA + buf * PF_BN * 4 + c0 * 4);
+            const float dw = reinterpret_cast<const float *>(smem + Lay::OFF_DW)[b4 * PF_BM + r];
+            const float ndm = F::MINS ? -reinterpret_cast<const float *>(smem + Lay::OFF_DM)[b4 * PF_BM + r] : 0.0f;
+            const float4 *da4 = reinterpret_cast<const float4 *>(smem + Lay::OFF_DA + b4 * PF_BN * 4 + c0 * 4);
             const uint32_t ta = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)buf * 256u + (uint32_t)c0;
 #pragma unroll
-            for (int cc = 0; cc < EPI_COLS / 16; ++cc) {
-                uint32_t v1[16], v2[16];
-                tmem_ld16(ta + 16 * cc, v1);
-                tmem_ld16(ta + 128 + 16 * cc, v2);
+            for (int cc = 0; cc < EPI_COLS / 8; ++cc) {
+                uint32_t v1[8], v2[8];
+                tmem_ld8(ta + 8 * cc, v1);
+                if constexpr (F::MINS) tmem_ld8(ta + 128 + 8 * cc, v2);
                 tmem_wait_ld(v1);
-                tmem_wait_ld(v2);
+                if constexpr (F::MINS) tmem_wait_ld(v2);
 #pragma unroll
-                for (int g = 0; g < 4; ++g) {
-                    const float4 d = da4[4 * cc + g];
+                for (int gq = 0; gq < 2; ++gq) {
+                    const float4 d = da4[2 * cc + gq];
                     const float dv[4] = {d.x, d.y, d.z, d.w};
 #pragma unroll
                     for (int e = 0; e < 4; ++e) {
-                        const int j = 4 * g + e;
-                        const float sv = fmaf(ndm, __uint_as_float(v2[j]), dw * __uint_as_float(v1[j]));
-                        acc[16 * cc + j] = fmaf(dv[e], sv, acc[16 * cc + j]);
+                        const int j = 4 * gq + e;
+                        float sv = dw * __uint_as_float(v1[j]);
+                        if constexpr (F::MINS) sv = fmaf(ndm, __uint_as_float(v2[j]), sv);
+                        acc[8 * cc + j] = fmaf(dv[e], sv, acc[8 * cc + j]);
                     }
                 }
             }
@@ -366,7 +530,7 @@ prefill_q4k_kernel(const __grid_constant__ CUtensorMap tmB, const __grid_constan
             __syncwarp();
             if (lane == 0) {
                 mbar_arrive(bar(BAR_ACC_EMPTY + buf));
-                mbar_arrive(bar(BAR_SB_FREE + buf));
+                mbar_arrive(bar(BAR_SB_FREE + b4));
             }
         }
         if (ok && !*abort_flag && r < rows) {
@@ -387,29 +551,49 @@ prefill_q4k_kernel(const __grid_constant__ CUtensorMap tmB, const __grid_constan
 
 // Q8_K rows -> token operand for the MMAs: f16 quants with the slots of each
 // group of four holding elements 0, 2, 1, 3 (the order the weight converters
-// produce), f16 bsums, and the block scales transposed to [sb][token].
-// Tokens m..m_pad-1 are zero.
+// produce); for two-plane formats (Q6_K) each 64-element quarter is followed by
+// the same quarter times 16. Also f16 bsums (formats with mins) and the block
+// scales transposed to [sb][token]. Tokens m..m_pad-1 are zero.
+template <int PLANES>
 __global__ void prefill_prep_q8k(const uint8_t *xq, int m, int nsb, int m_pad, uint16_t *B, uint16_t *S, float *DA) {
-    const int sb = blockIdx.x, t = blockIdx.y, i = threadIdx.x;   // 64 threads
+    const int sb = blockIdx.x, t = blockIdx.y, i = threadIdx.x;   // 64 threads, 4 elements each
     const int64_t K = (int64_t)nsb * QK_K;
-    uint2 out = make_uint2(0, 0);
+    uint32_t e[4] = {0, 0, 0, 0};
     if (t < m) {
         const uint8_t *blk = xq + ((int64_t)t * nsb + sb) * B_Q8_K;
         const uint32_t w = *reinterpret_cast<const uint32_t *>(blk + 4 + 4 * i);
-        const float e0 = (float)(int8_t)byte_at(w, 0), e1 = (float)(int8_t)byte_at(w, 1);
-        const float e2 = (float)(int8_t)byte_at(w, 2), e3 = (float)(int8_t)byte_at(w, 3);
-        out.x = half2_bits(e0, e2);
-        out.y = half2_bits(e1, e3);
-        if (i < 16) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) e[k] = (uint32_t)(int)(int8_t)byte_at(w, k);
+        if (S && i < 16) {
             const int16_t bs = *reinterpret_cast<const int16_t *>(blk + 260 + 2 * i);
             S[(int64_t)t * (K / 16) + 16 * sb + i] = __half_as_ushort(__float2half_rn((float)bs));
         }
         if (i == 0) DA[(int64_t)sb * m_pad + t] = *reinterpret_cast<const float *>(blk);
     } else {
-        if (i < 16) S[(int64_t)t * (K / 16) + 16 * sb + i] = 0;
+        if (S && i < 16) S[(int64_t)t * (K / 16) + 16 * sb + i] = 0;
         if (i == 0) DA[(int64_t)sb * m_pad + t] = 0.0f;
     }
-    *reinterpret_cast<uint2 *>(B + (int64_t)t * K + (int64_t)QK_K * sb + 4 * i) = out;
+    const float a0 = (float)(int)e[0], a1 = (float)(int)e[1], a2 = (float)(int)e[2], a3 = (float)(int)e[3];
+    uint16_t *row = B + (int64_t)t * K * PLANES + (int64_t)QK_K * PLANES * sb;
+    if (PLANES == 1) {
+        *reinterpret_cast<uint2 *>(row + 4 * i) = make_uint2(half2_bits(a0, a2), half2_bits(a1, a3));
+    } else {
+        const int cq = i >> 4, e64 = (4 * i) & 63;
+        *reinterpret_cast<uint2 *>(row + 128 * cq + e64) = make_uint2(half2_bits(a0, a2), half2_bits(a1, a3));
+        *reinterpret_cast<uint2 *>(row + 128 * cq + 64 + e64) =
+            make_uint2(half2_bits(16.0f * a0, 16.0f * a2), half2_bits(16.0f * a1, 16.0f * a3));
+    }
+}
+
+// Weight rows whose byte length is not a multiple of 16 (Q6_K with a
+// super-block count that is not a multiple of 8) cannot be described by a
+// tensor map; they are copied to rows of `stride` bytes first.
+__global__ void prefill_pad_rows(const uint16_t *src, int64_t row_bytes, int64_t n_out, uint16_t *dst, int64_t stride) {
+    const int64_t hw = row_bytes / 2;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n_out * hw; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r = i / hw, c = i - r * hw;
+        dst[r * (stride / 2) + c] = src[i];
+    }
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -424,59 +608,86 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     return fn;
 }
 
-// 2-D f16 tensor [rows][cols] (cols contiguous), box {bx cols, by rows}
-bool make_map(CUtensorMap *map, const void *base, uint64_t cols, uint64_t rows, uint32_t bx, uint32_t by,
-              CUtensorMapSwizzle swz) {
+// 2-D tensor [rows][cols] of f16 (esize 2) or bytes (esize 1), cols contiguous
+// with rows `pitch` bytes apart, box {bx cols, by rows}; reads past the ends
+// return zeros
+bool make_map(CUtensorMap *map, const void *base, uint64_t cols, uint64_t rows, uint64_t pitch, uint32_t bx,
+              uint32_t by, CUtensorMapSwizzle swz, int esize) {
     auto fn = encode_fn();
     if (!fn) return false;
     cuuint64_t dims[2] = {cols, rows};
-    cuuint64_t strides[1] = {cols * 2};
+    cuuint64_t strides[1] = {pitch};
     cuuint32_t box[2] = {bx, by};
     cuuint32_t es[2] = {1, 1};
-    return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(base), dims, strides, box, es,
-              CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+    return fn(map, esize == 2 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8, 2,
+              const_cast<void *>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 
-}  // namespace
-
-bool prefill_supported(uint32_t wtype) { return wtype == T_Q4_K; }
-
-size_t prefill_workspace_bytes(int64_t n_in, int64_t m) {
+struct WsParts {
+    size_t b, s, da, pad;
+};
+WsParts ws_parts(uint32_t wtype, int64_t n_in, int64_t n_out, int64_t m) {
     const int64_t m_pad = (m + PF_BN - 1) / PF_BN * PF_BN;
-    return align256((size_t)m_pad * n_in * 2) + align256((size_t)m_pad * (n_in / 16) * 2) +
-           align256((size_t)(n_in / QK_K) * m_pad * 4);
+    const int planes = wtype == T_Q6_K ? 2 : 1;
+    WsParts w{};
+    w.b = align256((size_t)m_pad * n_in * 2 * planes);
+    w.s = wtype == T_Q4_K ? align256((size_t)m_pad * (n_in / 16) * 2) : 0;
+    w.da = align256((size_t)(n_in / QK_K) * m_pad * 4);
+    const int64_t rb = n_in / QK_K * B_Q6_K;
+    w.pad = (wtype == T_Q6_K && rb % 16) ? align256((size_t)n_out * ((rb + 15) & ~int64_t(15))) : 0;
+    return w;
 }
 
-int launch_prefill(uint32_t wtype, const PrefillLaunch &L, cudaStream_t st) {
-    if (wtype != T_Q4_K) return -3;
+template <uint32_t T>
+int launch_t(const PrefillLaunch &L, cudaStream_t st) {
+    using F = PfFmt<T>;
+    using Lay = PfLayout<T>;
     const int64_t K = L.n_in, nsb = K / QK_K;
     const int64_t m_pad = (L.m + PF_BN - 1) / PF_BN * PF_BN;
+    const WsParts parts = ws_parts(T, L.n_in, L.n_out, L.m);
     uint8_t *ws = static_cast<uint8_t *>(L.ws);
     uint16_t *B = reinterpret_cast<uint16_t *>(ws);
-    uint16_t *S = reinterpret_cast<uint16_t *>(ws + align256((size_t)m_pad * K * 2));
-    float *DA = reinterpret_cast<float *>(ws + align256((size_t)m_pad * K * 2) + align256((size_t)m_pad * (K / 16) * 2));
-    prefill_prep_q8k<<<dim3((unsigned)nsb, (unsigned)m_pad), 64, 0, st>>>(static_cast<const uint8_t *>(L.xq), (int)L.m,
-                                                                          (int)nsb, (int)m_pad, B, S, DA);
+    uint16_t *S = F::MINS ? reinterpret_cast<uint16_t *>(ws + parts.b) : nullptr;
+    float *DA = reinterpret_cast<float *>(ws + parts.b + parts.s);
+    prefill_prep_q8k<F::KSTEPS / 4><<<dim3((unsigned)nsb, (unsigned)m_pad), 64, 0, st>>>(
+        static_cast<const uint8_t *>(L.xq), (int)L.m, (int)nsb, (int)m_pad, B, S, DA);
     if (cudaGetLastError() != cudaSuccess) return -2;
 
-    CUtensorMap tmB, tmS;
-    if (!make_map(&tmB, B, (uint64_t)K, (uint64_t)m_pad, PF_KS, PF_BN, CU_TENSOR_MAP_SWIZZLE_128B) ||
-        !make_map(&tmS, S, (uint64_t)(K / 16), (uint64_t)m_pad, 16, PF_BN, CU_TENSOR_MAP_SWIZZLE_32B))
+    const int64_t row_bytes = nsb * F::BLOCK;
+    const void *w = L.w;
+    int64_t pitch = row_bytes;
+    if (row_bytes % 16 || reinterpret_cast<uintptr_t>(w) % 16) {
+        pitch = (row_bytes + 15) & ~int64_t(15);
+        uint16_t *dst = reinterpret_cast<uint16_t *>(ws + parts.b + parts.s + parts.da);
+        prefill_pad_rows<<<1024, 256, 0, st>>>(static_cast<const uint16_t *>(w), row_bytes, L.n_out, dst, pitch);
+        if (cudaGetLastError() != cudaSuccess) return -2;
+        w = dst;
+    }
+    CUtensorMap tmW, tmB, tmS;
+    if (!make_map(&tmW, w, (uint64_t)row_bytes, (uint64_t)L.n_out, (uint64_t)pitch, F::RAW_ROW, PF_BM,
+                  CU_TENSOR_MAP_SWIZZLE_NONE, 1) ||
+        !make_map(&tmB, B, (uint64_t)(K * F::KSTEPS / 4), (uint64_t)m_pad, (uint64_t)(K * F::KSTEPS / 4) * 2, PF_KS,
+                  PF_BN, CU_TENSOR_MAP_SWIZZLE_128B, 2))
         return -4;
+    if (F::MINS) {
+        if (!make_map(&tmS, S, (uint64_t)(K / 16), (uint64_t)m_pad, (uint64_t)(K / 16) * 2, 16, PF_BN,
+                      CU_TENSOR_MAP_SWIZZLE_32B, 2))
+            return -4;
+    } else {
+        tmS = tmB;   // unused
+    }
     static bool attr_set[64] = {};
     const int dev = L.device & 63;
     if (!attr_set[dev]) {
-        if (cudaFuncSetAttribute(prefill_q4k_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, PF_SMEM) !=
+        if (cudaFuncSetAttribute(prefill_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, Lay::SMEM) !=
             cudaSuccess)
             return -2;
         attr_set[dev] = true;
     }
     PfParams p{};
-    p.w = static_cast<const uint8_t *>(L.w);
-    p.row_bytes = nsb * B_Q4_K;
     p.n_out = (int)L.n_out;
     p.nsb = (int)nsb;
     p.da = DA;
@@ -486,9 +697,26 @@ int launch_prefill(uint32_t wtype, const PrefillLaunch &L, cudaStream_t st) {
     p.ntt = (int)(m_pad / PF_BN);
     p.status = L.status;
     const int64_t tiles = (L.n_out + PF_BM - 1) / PF_BM * p.ntt;
-    prefill_q4k_kernel<<<(unsigned)tiles, PF_WARPS * 32, PF_SMEM, st>>>(tmB, tmS, p);
+    prefill_kernel<T><<<(unsigned)tiles, PF_WARPS * 32, Lay::SMEM, st>>>(tmW, tmB, tmS, p);
     if (cudaGetLastError() != cudaSuccess) return -2;
     return 0;
+}
+
+}  // namespace
+
+bool prefill_supported(uint32_t wtype) { return wtype == T_Q4_K || wtype == T_Q6_K; }
+
+size_t prefill_workspace_bytes(uint32_t wtype, int64_t n_in, int64_t n_out, int64_t m) {
+    const WsParts w = ws_parts(wtype, n_in, n_out, m);
+    return w.b + w.s + w.da + w.pad;
+}
+
+int launch_prefill(uint32_t wtype, const PrefillLaunch &L, cudaStream_t st) {
+    switch (wtype) {
+        case T_Q4_K: return launch_t<T_Q4_K>(L, st);
+        case T_Q6_K: return launch_t<T_Q6_K>(L, st);
+        default: return -3;
+    }
 }
 
 }  // namespace sicu

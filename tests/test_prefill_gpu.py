@@ -75,6 +75,20 @@ def test_prefill_q4k_vs_reference(sicu, oracle, n_out, n_in, m):
     assert np.isfinite(got).all()
 
 
+@pytest.mark.parametrize("n_out,n_in,m", [
+    (128, 256, 128),     # one super-block, one tile
+    (256, 2048, 128),    # rows of 8 super-blocks: 16-byte multiple, no padding copy
+    (200, 1280, 77),     # 5 super-blocks per row: rows padded to 16 bytes first
+    (130, 5632, 140),    # 22 super-blocks, ragged rows and tokens
+])
+def test_prefill_q6k_vs_reference(sicu, oracle, n_out, n_in, m):
+    wt = Q.Q6_K
+    w, x, xq, want, got = _run(sicu, oracle, wt, n_out, n_in, m, seed=n_out + 3 * n_in + m)
+    l1 = np.abs(_dequant_q8k(xq, n_in)) @ np.abs(_dequant_w(oracle, wt, w, n_in, n_out)).T
+    _check_tol(got, want, l1, f"Q6_K prefill {n_out}x{n_in} m={m}")
+    assert np.isfinite(got).all()
+
+
 def test_prefill_q4k_exact_value(sicu, oracle):
     """Against the exact value of the product (float64 over the dequantized
     operands) at a larger size, where the scalar oracle would be slow."""
@@ -125,7 +139,7 @@ def test_prefill_f32_entry_matches_quantized(sicu, oracle):
     assert_bits_equal(host(y2), host(y1), "prefill f32 entry vs pre-quantized")
 
 
-@pytest.mark.parametrize("wt", [Q.Q8_0, Q.Q6_K, Q.F16])
+@pytest.mark.parametrize("wt", [Q.Q8_0, Q.Q5_K, Q.F16])
 def test_prefill_other_types_bit_exact(sicu, oracle, wt):
     """Types without a tensor-core kernel: the decode matvec per token."""
     n_out, n_in, m = 96, 512, 5

@@ -273,6 +273,154 @@ def run_reference(args, world, rank) -> None:
 
 
 # ---- our arm ----------------------------------------------------------------------------------
+# ---- model-level matrix path (configs[2..4]) -----------------------------------------
+DECODE_PER_GRAPH = 8      # decode tokens per captured graph
+
+
+def _time_graph(torch, g, stream, reps, world, dev) -> float:
+    """ms of `reps` replays of graph g on `stream` (max over ranks)."""
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            g.replay()
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(reps):
+            g.replay()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    return max_over_ranks(e0.elapsed_time(e1), world, dev)
+
+
+def model_decode(torch, s, shape, dev, stream, world, rank, group, reps) -> dict:
+    """Decode tok/s of the matrix path of `shape` (batch 1), tensor parallel
+    over the world: every weight matrix of one token per step."""
+    from siphon_b200 import model_path as mp
+    m = mp.MatrixPath(s, shape, dev, world, rank, group, seed=4)
+    with torch.cuda.stream(stream):
+        for _ in range(2):
+            launches = m.decode_step(stream)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        for _ in range(DECODE_PER_GRAPH):
+            m.decode_step(stream)
+    ms = _time_graph(torch, g, stream, reps, world, dev)
+    del g
+    tok = reps * DECODE_PER_GRAPH
+    us = ms * 1e3 / tok
+    gbps = m.weight_bytes / (us * 1e-6) / 1e9
+    peak, peak_kind = peak_hbm()
+    out = {"tok_s": round(tok / (ms * 1e-3), 1), "us_per_token": round(us, 2),
+           "weight_bytes_per_token_per_gpu": m.weight_bytes, "GBps_per_gpu": round(gbps, 1),
+           "hbm_frac": round(gbps / peak, 4), "peak_kind": peak_kind,
+           "kernel_launches_per_token": launches, "allreduces_per_token": 2 * shape.n_layer if world > 1 else 0}
+    del m
+    torch.cuda.empty_cache()
+    return out
+
+
+def model_prefill(torch, s, shape, dev, stream, world, rank, group, m_tok, reps) -> dict:
+    """Prefill tok/s of the matrix path of `shape` for an m_tok-token prompt."""
+    from siphon_b200 import model_path as mp
+    m = mp.MatrixPath(s, shape, dev, world, rank, group, seed=5, max_tokens=m_tok)
+    with torch.cuda.stream(stream):
+        m.prefill(stream, m_tok)          # sizes the workspace outside capture
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        m.prefill(stream, m_tok)
+    ms = _time_graph(torch, g, stream, reps, world, dev)
+    del g
+    sec = ms * 1e-3 / reps
+    params = sum(n_out * n_in for n_out, n_in in
+                 [m.shapes[k] for k in ("q", "k", "v", "o", "gate", "up", "down")]) * shape.n_layer \
+        + m.shapes["head"][0] * m.shapes["head"][1]
+    tflops = 2.0 * m_tok * params / sec / 1e12
+    try:
+        f16_peak = float(json.loads(PEAKS.read_text())["bf16_tflops"])
+        kind = "measured"
+    except Exception:
+        f16_peak, kind = 1590.0, "fallback"
+    out = {"tok_s": round(m_tok / sec, 1), "ms_per_prompt": round(sec * 1e3, 3), "prompt_tokens": m_tok,
+           "TFLOPs": round(tflops, 1), "f16_tensor_frac": round(tflops / f16_peak, 4),
+           "int8_tensor_frac_proxy": round(tflops / (2 * f16_peak), 4), "peak_kind": kind,
+           "note": "tensor-core kernel for Q4_K and Q6_K (kind::f16 MMAs on exact f16 (scale x quant) operands); "
+                   "int8 peak taken as 2x the measured bf16 dense peak"}
+    del m
+    torch.cuda.empty_cache()
+    return out
+
+
+def model_cpu_baseline(budget_s: float = 8.0) -> dict | None:
+    """The reference's CPU gemv over the TinyLlama-shape matrix path (host
+    copies), a bounded number of tokens; larger shapes are estimated from the
+    bandwidth it reaches (the CPU path is bandwidth-bound; its prefill is
+    token-serial, so CPU prefill tok/s = CPU decode tok/s)."""
+    from siphon_b200 import model_path as mp
+    from siphon_b200 import synth_model as sm
+    gemv, kind, threads = cpu_gemv_handle()
+    if gemv is None:
+        return None
+    sh = sm.TINYLLAMA
+    shp = mp.shard_shapes(sh, mp.tp_partition(sh, 1, 0))
+    mats = []
+    for il in range(sh.n_layer):
+        t = mp.layer_types(il)
+        for j, name in enumerate(("q", "k", "v", "o", "gate", "up", "down")):
+            n_out, n_in = shp[name]
+            mats.append((t[name], synth.weights(t[name], n_out, n_in, seed=il * 16 + j), n_out, n_in))
+    n_out, n_in = shp["head"]
+    mats.append((Q.Q6_K, synth.weights(Q.Q6_K, n_out, n_in, seed=999), n_out, n_in))
+    xs = {n: synth.activations(n, 1, seed=3)[0] for n in {m[3] for m in mats}}
+    ys = {n: np.zeros(n, np.float32) for n in {m[2] for m in mats}}
+    tens = [(gemv.tensor(t, w, n_in, n_out), n_in, n_out) for t, w, n_out, n_in in mats]
+
+    def token():
+        for te, n_in, n_out in tens:
+            gemv(te, xs[n_in], ys[n_out])
+
+    token()
+    t0 = time.perf_counter()
+    n = 0
+    while time.perf_counter() - t0 < budget_s or n < 2:
+        token()
+        n += 1
+    dt = time.perf_counter() - t0
+    gemv.close()
+    wb = mp.step_weight_bytes(sh)
+    gbps = wb * n / dt / 1e9
+    return {"decode_tok_s": round(n / dt, 2), "GBps": round(gbps, 2), "cores": threads, "kind": kind,
+            "sample": f"{n} TinyLlama-shape tokens (all 155 weight matrices each), si_backend_cpu()->gemv",
+            "est_llama3_8b_prefill_tok_s": round(gbps * 1e9 / mp.step_weight_bytes(sm.LLAMA3_8B), 3),
+            "est_qwen32b_decode_tok_s": round(gbps * 1e9 / mp.step_weight_bytes(sm.QWEN25_32B), 3)}
+
+
+def model_metrics(torch, s, dev, stream, world, rank, quick: bool) -> dict:
+    from siphon_b200 import synth_model as sm
+    out = {}
+    reps = 3 if quick else 10
+    out["tp_decode"] = {"config": "configs[4] Qwen2.5-32B shape, batch 1, matrix path, "
+                                  f"tensor parallel x{world} (column-split QKV/gate/up/head, row-split o/down, "
+                                  "one NCCL all-reduce after o and after down per layer)" if world > 1 else
+                                  "configs[4] Qwen2.5-32B shape, batch 1, matrix path, one GPU",
+                        **model_decode(torch, s, sm.QWEN25_32B, dev, stream, world, rank, None, reps)}
+    if world == 1:
+        out["decode"] = {"config": "configs[2] TinyLlama-1.1B shape, batch 1, matrix path",
+                         **model_decode(torch, s, sm.TINYLLAMA, dev, stream, 1, 0, None, reps * 4)}
+        out["prefill"] = {"config": "configs[3] Llama-3-8B shape, 512-token prompt, matrix path",
+                          **model_prefill(torch, s, sm.LLAMA3_8B, dev, stream, 1, 0, None, 512, max(2, reps // 2))}
+    out["scope"] = ("every weight-matrix product of the forward pass (per layer Wq, Wk, Wv, Wo, W_gate, W_up, "
+                    "W_down; then the output head) with synthetic Q4_K_M-style weights; attention, norms, RoPE "
+                    "and SwiGLU between them are outside the matrix path and not run, so these rates are upper "
+                    "bounds for a full forward step")
+    return out
+
+
 def run_ours(args, world, rank, local) -> None:
     import torch
 
@@ -410,11 +558,19 @@ def run_ours(args, world, rank, local) -> None:
     h2d = sum(len(ws) * 4 * n_in for _, n_in, ws, _, _ in mats)
     d2h = sum(len(ws) * 4 * n_out for n_out, _, ws, _, _ in mats)
 
+    del g
+    model = None
+    if not args.no_model:
+        model = model_metrics(torch, s, dev, stream, world, rank, quick=args.steps < 10)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(copies)
+        if model is not None:
+            mc = model_cpu_baseline()
+            if mc is not None:
+                model["cpu_baseline"] = mc
 
-    del g
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()
@@ -436,6 +592,8 @@ def run_ours(args, world, rank, local) -> None:
     }
     if cpu is not None:
         line["cpu_baseline"] = cpu
+    if model is not None:
+        line["model_path"] = model
     print(json.dumps(line))
 
 
@@ -446,6 +604,7 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-model", action="store_true", help="skip the model-level matrix-path measurements")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")

@@ -1,0 +1,198 @@
+"""The quantized matrix path of a llama-architecture forward pass, on device.
+
+The reference's forward pass (src/engine.c:290-400) calls its backend gemv
+once per weight matrix and token: Wq, Wk, Wv (engine.c:317-319), Wo
+(engine.c:368), W_gate and W_up (engine.c:375-376), W_down (engine.c:378) per
+layer, then the output head (engine.c:393). This module runs exactly that
+sequence of products through libsiphon_cuda for the model shapes of the
+benchmark configs (synthetic Q4_K_M-style weights generated on the device):
+
+* ``decode_step``: one token (batch 1), sicu_gemv_multi for products that
+  share an activation and type (Wq/Wk[/Wv], W_gate/W_up), sicu_gemv_f32 for
+  the rest;
+* ``prefill``: m tokens at once through sicu_gemm_prefill_f32.
+
+The attention, normalisation, RoPE and SwiGLU steps between the products are
+not part of this path; each product reads a fixed activation buffer of its
+input length, so a step is the matrix work of one token (or one prompt) and
+nothing else, and its time is a lower bound on a full forward step.
+
+Tensor parallelism (``world > 1``) follows the layout the 32B-class configs
+name: Wq/Wk/Wv, W_gate/W_up and the output head are split by output rows
+(attention heads, FFN rows, vocabulary), Wo and W_down by input columns, and
+the partial Wo and W_down outputs are summed with one all-reduce each per
+layer (attention block and FFN block). Column shards are whole 256-element
+super-blocks (Q8_K quantizes whole blocks), so shards can be uneven.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+from . import quant as Q
+from .synth_model import LlamaShape
+
+# byte offsets of the f16 scale fields inside one block (include/siphon/quant.h)
+F16_FIELDS = {
+    Q.Q4_0: (0,), Q.Q5_0: (0,), Q.Q8_0: (0,),
+    Q.Q2_K: (80, 82), Q.Q3_K: (108,), Q.Q4_K: (0, 2), Q.Q5_K: (0, 2), Q.Q6_K: (208,),
+}
+
+
+def _split(n_units: int, world: int, rank: int) -> range:
+    """Units [start, stop) of rank in a balanced split (first ranks get the extra)."""
+    base, extra = divmod(n_units, world)
+    start = rank * base + min(rank, extra)
+    return range(start, start + base + (1 if rank < extra else 0))
+
+
+@dataclass(frozen=True)
+class Shard:
+    heads: range          # query heads
+    kv_heads: tuple       # key/value heads those query heads read (replicated where shared)
+    ff: range             # FFN rows (elements)
+    vocab: range          # output-head rows
+
+
+def tp_partition(sh: LlamaShape, world: int, rank: int) -> Shard:
+    hd = sh.head_dim
+    heads_per_unit = 256 // math.gcd(256, hd)        # Wo's column shard must be whole super-blocks
+    if sh.n_head % heads_per_unit or sh.n_ff % 256:
+        raise ValueError("shape cannot be split on 256-element boundaries")
+    hu = _split(sh.n_head // heads_per_unit, world, rank)
+    heads = range(hu.start * heads_per_unit, hu.stop * heads_per_unit)
+    group = sh.n_head // sh.n_head_kv
+    kv = tuple(sorted({h // group for h in heads}))
+    fu = _split(sh.n_ff // 256, world, rank)
+    vu = _split(sh.n_vocab, world, rank)
+    return Shard(heads, kv, range(fu.start * 256, fu.stop * 256), vu)
+
+
+def layer_types(il: int) -> dict:
+    """Q4_K_M-style mix: Q6_K for attn_v and ffn_down on even layers."""
+    mix = Q.Q6_K if il % 2 == 0 else Q.Q4_K
+    return {"q": Q.Q4_K, "k": Q.Q4_K, "v": mix, "o": Q.Q4_K, "gate": Q.Q4_K, "up": Q.Q4_K, "down": mix}
+
+
+def shard_shapes(sh: LlamaShape, shard: Shard) -> dict:
+    """(n_out, n_in) of every matrix one rank holds."""
+    hd = sh.head_dim
+    nq, nkv, nff = len(shard.heads) * hd, len(shard.kv_heads) * hd, len(shard.ff)
+    return {"q": (nq, sh.n_embd), "k": (nkv, sh.n_embd), "v": (nkv, sh.n_embd), "o": (sh.n_embd, nq),
+            "gate": (nff, sh.n_embd), "up": (nff, sh.n_embd), "down": (sh.n_embd, nff),
+            "head": (len(shard.vocab), sh.n_embd)}
+
+
+def step_weight_bytes(sh: LlamaShape, world: int = 1, rank: int = 0) -> int:
+    """Weight bytes one rank streams per decode token."""
+    shp = shard_shapes(sh, tp_partition(sh, world, rank))
+    total = Q.row_bytes(Q.Q6_K, sh.n_embd) * shp["head"][0]
+    for il in range(sh.n_layer):
+        t = layer_types(il)
+        for name in ("q", "k", "v", "o", "gate", "up", "down"):
+            n_out, n_in = shp[name]
+            total += n_out * Q.row_bytes(t[name], n_in)
+    return total
+
+
+def device_weights(wtype: int, n_out: int, n_in: int, seed: int, device):
+    """Synthetic GGUF blocks generated on the device (same distribution as
+    synth.weights: f16 scales U[1e-4, 1e-2], every other bit uniform)."""
+    import torch
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    rb = Q.row_bytes(wtype, n_in)
+    raw = torch.randint(0, 256, (n_out * rb,), dtype=torch.uint8, device=device, generator=g)
+    bsz = Q.GEOMETRY[wtype][1]
+    blocks = raw.view(-1, bsz)
+    for off in F16_FIELDS[wtype]:
+        d = torch.empty(blocks.shape[0], dtype=torch.float32, device=device).uniform_(1e-4, 1e-2, generator=g)
+        blocks[:, off:off + 2] = d.half().view(torch.uint8).view(-1, 2)
+    return raw
+
+
+class MatrixPath:
+    """One rank's shard of the model's weight matrices and the launch
+    sequence of a decode step / a prefill over them."""
+
+    def __init__(self, sicu, sh: LlamaShape, device, world: int = 1, rank: int = 0, group=None, seed: int = 0,
+                 max_tokens: int = 1):
+        import torch
+        self.s, self.sh, self.dev, self.world, self.group = sicu, sh, device, world, group
+        self.shard = tp_partition(sh, world, rank)
+        self.shapes = shard_shapes(sh, self.shard)
+        self.layers = []
+        for il in range(sh.n_layer):
+            t = layer_types(il)
+            lay = {}
+            for j, name in enumerate(("q", "k", "v", "o", "gate", "up", "down")):
+                n_out, n_in = self.shapes[name]
+                lay[name] = (t[name], device_weights(t[name], n_out, n_in, seed * 7919 + il * 16 + j + 1000 * rank,
+                                                     device))
+            self.layers.append(lay)
+        n_out, n_in = self.shapes["head"]
+        self.head = (Q.Q6_K, device_weights(Q.Q6_K, n_out, n_in, seed * 7919 + 999 + 1000 * rank, device))
+        m = max_tokens
+        gen = torch.Generator(device=device)
+        gen.manual_seed(seed + 17)
+
+        def act(n):
+            return torch.randn(m, n, device=device, generator=gen)
+
+        nq, nff = self.shapes["q"][0], self.shapes["gate"][0]
+        # fixed inputs per input length; outputs per product
+        self.x_model, self.x_attn, self.x_ff = act(sh.n_embd), act(nq), act(nff)
+        self.y = {name: torch.empty(m, self.shapes[name][0], device=device) for name in self.shapes}
+        self.weight_bytes = step_weight_bytes(sh, world, rank)
+
+    def _allreduce(self, t) -> None:
+        if self.world > 1:
+            import torch.distributed as dist
+            dist.all_reduce(t, group=self.group)
+
+    def decode_step(self, stream) -> int:
+        """Launch one token's products on `stream`; returns the number of
+        library kernel launches."""
+        s, h, y = self.s, stream.cuda_stream, self.y
+        x, xa, xf = self.x_model[0], self.x_attn[0], self.x_ff[0]
+        n = 0
+        for lay in self.layers:
+            (tq, wq), (tk, wk), (tv, wv) = lay["q"], lay["k"], lay["v"]
+            (nq, _), (nkv, _) = self.shapes["q"], self.shapes["k"]
+            if tv == tq:
+                s.gemv_multi(tq, [wq, wk, wv], [nq, nkv, nkv], self.sh.n_embd, x, [y["q"], y["k"], y["v"]], stream=h)
+                n += 1
+            else:
+                s.gemv_multi(tq, [wq, wk], [nq, nkv], self.sh.n_embd, x, [y["q"], y["k"]], stream=h)
+                s.gemv_f32(tv, wv, self.sh.n_embd, nkv, x, y["v"], stream=h)
+                n += 2
+            to, wo = lay["o"]
+            s.gemv_f32(to, wo, nq, self.sh.n_embd, xa, y["o"], stream=h)
+            self._allreduce(y["o"])
+            (tg, wg), (_, wu) = lay["gate"], lay["up"]
+            nff = self.shapes["gate"][0]
+            s.gemv_multi(tg, [wg, wu], [nff, nff], self.sh.n_embd, x, [y["gate"], y["up"]], stream=h)
+            td, wd = lay["down"]
+            s.gemv_f32(td, wd, nff, self.sh.n_embd, xf, y["down"], stream=h)
+            self._allreduce(y["down"])
+            n += 3
+        th, wh = self.head
+        s.gemv_f32(th, wh, self.sh.n_embd, self.shapes["head"][0], x, y["head"], stream=h)
+        return n + 1
+
+    def prefill(self, stream, m: int) -> None:
+        """Launch the products of an m-token prompt on `stream`."""
+        s, h, y = self.s, stream.cuda_stream, self.y
+        d = self.sh.n_embd
+        nq, nkv, nff = self.shapes["q"][0], self.shapes["k"][0], self.shapes["gate"][0]
+        for lay in self.layers:
+            for name, n_in, xin in (("q", d, self.x_model), ("k", d, self.x_model), ("v", d, self.x_model),
+                                    ("o", nq, self.x_attn), ("gate", d, self.x_model), ("up", d, self.x_model),
+                                    ("down", nff, self.x_ff)):
+                t, w = lay[name]
+                s.gemm_prefill_f32(t, w, n_in, self.shapes[name][0], xin, m, y[name], stream=h)
+                if name in ("o", "down"):
+                    self._allreduce(y[name][:m])
+        th, wh = self.head
+        s.gemm_prefill_f32(th, wh, d, self.shapes["head"][0], self.x_model, m, y["head"], stream=h)

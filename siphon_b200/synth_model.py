@@ -38,6 +38,11 @@ class LlamaShape:
 
 # TinyLlama-1.1B shape
 TINYLLAMA = LlamaShape(22, 2048, 5632, 32, 4, 32000, 10000.0, 1e-5, 2048)
+# Llama-3-8B shape
+LLAMA3_8B = LlamaShape(32, 4096, 14336, 32, 8, 128256, 500000.0, 1e-5, 2048)
+# Qwen2.5-32B shape (its QKV bias adds are vector
+# work outside the matrix path)
+QWEN25_32B = LlamaShape(64, 5120, 27648, 40, 8, 152064, 1000000.0, 1e-6, 2048)
 # a small model of the same family for parity tests
 SMALL = LlamaShape(3, 512, 1536, 8, 2, 1024, 10000.0, 1e-5, 1024)
 

@@ -45,9 +45,12 @@ SHAPES = [(4096, 4096), (14336, 4096), (4096, 14336)]   # rows x K
 WTYPE = Q.Q4_K
 PEAKS = ROOT / "MEASURED_PEAKS.json"
 FALLBACK_HBM = 6650.0
-# DRAM bytes per launch from the ncu capture summarised in
-# profiles/gemv_q4k_launches.md (null until a capture exists)
-NCU_TRAFFIC = {}
+# DRAM traffic of the dominant kernel from the ncu capture summarised in
+# profiles/gemv_q4k_sweep.md: one batched launch of 17 Q4_K 14336x4096 copies
+# read+wrote 1.005x its algorithmic bytes; traffic grows with the matrices a
+# launch streams, so a bench launch's traffic is that ratio times its bytes
+NCU_TRAFFIC = {"ratio_to_algorithmic": 1.005,
+               "source": "profiles/gemv_q4k_sweep.md (ncu --set full, 17 x 14336x4096 launch)"}
 
 
 def peak_hbm() -> tuple[float, str]:
@@ -350,7 +353,8 @@ def model_prefill(torch, s, shape, dev, stream, world, rank, group, m_tok, reps)
            "TFLOPs": round(tflops, 1), "f16_tensor_frac": round(tflops / f16_peak, 4),
            "int8_tensor_frac_proxy": round(tflops / (2 * f16_peak), 4), "peak_kind": kind,
            "note": "tensor-core kernel for Q4_K and Q6_K (kind::f16 MMAs on exact f16 (scale x quant) operands); "
-                   "int8 peak taken as 2x the measured bf16 dense peak"}
+                   "int8 peak taken as 2x the measured bf16 dense peak",
+           "profile": "profiles/prefill_q4k_4096x4096_m512.md (ncu: utchmma f16->f32 ops = 22.6% of peak)"}
     del m
     torch.cuda.empty_cache()
     return out
@@ -512,7 +516,9 @@ def run_ours(args, world, rank, local) -> None:
     kern_bytes = args.steps * step_bytes
     achieved = kern_bytes / (sum(per_shape_ms) * 1e-3) / 1e9
     peak, peak_kind = peak_hbm()
-    traffic = NCU_TRAFFIC.get("per_launch_bytes")
+    # per launch (one launch = all copies of one shape), averaged over the shapes
+    per_launch = step_bytes / len(SHAPES)
+    traffic = round(NCU_TRAFFIC["ratio_to_algorithmic"] * per_launch) if NCU_TRAFFIC else None
 
     # the same sweep with one launch per matvec (informational)
     sevs = [[[torch.cuda.Event(enable_timing=True, external=True) for _ in range(2)] for _ in SHAPES]
@@ -584,7 +590,8 @@ def run_ours(args, world, rank, local) -> None:
                                            "per_shape": shape_detail}),
         "roofline": {"bound": "hbm", "kernel": "gemv_kernel<Q4_K> (one launch = all copies of a shape)", "achieved": round(achieved, 1),
                      "peak": peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),
-                     "traffic": traffic},
+                     "traffic": traffic, "algorithmic_bytes_per_launch": round(per_launch),
+                     "traffic_source": NCU_TRAFFIC.get("source")},
         "e2e": {"value": round(e2e_value, 1), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "path": "sicu_gemv_host per matvec (pinned host x in, host y out, stream sync per call)"},
         "gpu_launches": args.steps * len(SHAPES),

@@ -56,6 +56,7 @@ int launch_gemv_f16(const GemvLaunch &L, cudaStream_t st) {
     static bool attr_set[64] = {};
     const int dev = L.device & 63;
     if (!attr_set[dev]) {
+        cudaFuncSetAttribute(gemv_f16_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
         if (cudaFuncSetAttribute(gemv_f16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L.smem_limit) != cudaSuccess)
             return -2;
         attr_set[dev] = true;

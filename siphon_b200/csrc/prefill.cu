@@ -682,6 +682,7 @@ int launch_t(const PrefillLaunch &L, cudaStream_t st) {
     static bool attr_set[64] = {};
     const int dev = L.device & 63;
     if (!attr_set[dev]) {
+        cudaFuncSetAttribute(prefill_kernel<T>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
         if (cudaFuncSetAttribute(prefill_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, Lay::SMEM) !=
             cudaSuccess)
             return -2;

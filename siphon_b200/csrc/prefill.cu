@@ -1,32 +1,38 @@
 // Prefill matrix product on the 5th-generation tensor cores: Y = X W^T for a
 // block of m >= 64 tokens, X quantized to Q8_K rows, W in its GGUF K-quant
 // blocks. Y[t][r] is the reference's per-row dot product (for Q4_K,
-// si_dot_q4_K_q8_K, src/kernels.c:349-410) for every (token, row) pair:
+// si_dot_q4_K_q8_K, src/kernels.c:349-410; Q6_K, si_dot_q6_K_q8_K,
+// src/kernels.c:480-523) for every (token, row) pair:
 //
 //   Y[t][r] = sum_sb dA[t][sb] * ( d[r][sb] * S1 - dmin[r][sb] * S2 )
 //   S1 = sum_k (sc * q)[r][k] * qa[t][k]                         (256 k)
-//   S2 = sum_j mn[r][j] * (bsums[t][2j] + bsums[t][2j+1])
+//   S2 = sum_j mn[r][j] * (bsums[t][2j] + bsums[t][2j+1])         (Q4_K only)
 //
-// Every factor of S1 and S2 is a small integer that f16 holds exactly
-// (sc * q <= 945, |qa| <= 127, |bsums| <= 2032), so kind::f16 MMAs with f32
-// accumulation produce the integer sums (exactly while partial sums stay below
-// 2^24), and only the float scaling per super-block rounds in a different order
-// from the reference's lane sums. Outputs agree with the reference within a
-// relative 1e-5 of the L1 norm of the products.
+// S1's factors are small integers that f16 holds exactly (sc * q <= 945 for
+// Q4_K; Q6_K's (q - 32) * sc is split into two exact planes), so kind::f16
+// MMAs with f32 accumulation produce the integer sums. The dmin term joins the
+// same accumulator: with f = d * 2^s (s >= 0 the smallest that keeps the mins
+// in f16 range) the super-block is f * (sum_k (sc q 2^-s) qa - sum_i
+// (dmin / f) mn[i/2] bsums[i]), the mins factor split into two f16 parts
+// (hi + lo, 22 bits). Outputs agree with the reference within a relative 1e-5
+// of the L1 norm of the products.
 //
 // One CTA computes a 128-row x 128-token tile (one SM; 19 warps):
 //   warp 0      TMA: token operand (f16, 128-byte swizzle), bsums, dA
 //   warp 1      TMEM owner; lane 0 issues the MMAs
 //   warp 2      TMA of raw weight super-blocks (one 128-row tile of GGUF
-//               block bytes per super-block, 3 buffers)
-//   warps 3-10  weight converters: raw blocks -> f16 (sc*q) tiles in the
-//               swizzled K-major layout, mins tile, per-row d / dmin (thread =
-//               one row and one nibble half: 256 threads, two per scheduler)
-//   warps 11-18 epilogue: per super-block, S1/S2 from tensor memory, scale,
-//               accumulate in registers; write Y at the end (two warps per
-//               32-lane quarter of tensor memory, 64 token columns each)
-// Tensor memory: two accumulator sets (S1, S2: 128 columns each), so the MMAs
-// of super-block sb+1 run while the epilogue drains sb.
+//               block bytes per super-block)
+//   warps 3-10  weight converters: raw blocks -> f16 weights written straight
+//               into tensor memory (the MMA's A operand), the mins operand
+//               and the per-row scale f; thread = one row; the two groups of
+//               four warps convert alternate K-steps, so two are in flight
+//   warps 11-18 epilogue: per super-block, the accumulator from tensor memory,
+//               scaled by f * dA and added in registers; Y written at the end
+//               (two warps per 32-lane quarter of tensor memory, 64 tokens each)
+// Tensor memory (512 columns): two accumulators (128 columns each), so the
+// MMAs of super-block sb+1 run while the epilogue drains sb; four 32-column A
+// stages (64 k each); four 16-column mins operands. Only the token operand
+// and the raw blocks pass through shared memory.
 #include <cudaTypedefs.h>
 
 #include "launch.h"
@@ -39,7 +45,7 @@ namespace {
 constexpr int PF_BM = 128;        // weight rows per tile (MMA M)
 constexpr int PF_BN = 128;        // tokens per tile (MMA N)
 constexpr int PF_KS = 64;         // k slots per pipeline stage: one 128-byte swizzle atom of f16
-constexpr int PF_STAGES = 4;
+constexpr int PF_STAGES = 6;     // K-steps in flight (even: each stage belongs to one converter group)
 constexpr int PF_NSB = 4;         // per-super-block buffers: mins / bsums tiles, scales
 constexpr int PF_STAGE_BYTES = PF_BM * PF_KS * 2;   // 16 KB; the token stage has the same size
 constexpr int PF_MIN_BYTES = PF_BM * 16 * 2;        // 4 KB: 128 rows x 16 f16 (32-byte swizzle)
@@ -73,29 +79,26 @@ template <> struct PfFmt<T_Q6_K> {
 template <uint32_t T> struct PfLayout {
     using F = PfFmt<T>;
     static constexpr int RAW_BUF = PF_BM * F::RAW_ROW;
-    static constexpr int OFF_A = 0;
-    static constexpr int OFF_B = OFF_A + PF_STAGES * PF_STAGE_BYTES;
+    static constexpr int OFF_B = 0;
     static constexpr int OFF_RAW = OFF_B + PF_STAGES * PF_STAGE_BYTES;
     static constexpr int MINB = F::MINS ? PF_NSB * PF_MIN_BYTES : 0;
-    static constexpr int OFF_A2 = (OFF_RAW + F::NRAW * RAW_BUF + 1023) & ~1023;
-    static constexpr int OFF_B2 = OFF_A2 + MINB;
+    static constexpr int OFF_B2 = (OFF_RAW + F::NRAW * RAW_BUF + 1023) & ~1023;
     static constexpr int OFF_DA = OFF_B2 + MINB;
-    static constexpr int OFF_DW = OFF_DA + PF_NSB * PF_BN * 4;
-    static constexpr int OFF_DM = OFF_DW + PF_NSB * PF_BM * 4;
-    static constexpr int OFF_BAR = OFF_DM + PF_NSB * PF_BM * 4;
+    static constexpr int OFF_DW = OFF_DA + PF_NSB * PF_BN * 4;          // per-row scale f
+    static constexpr int OFF_BAR = OFF_DW + PF_NSB * PF_BM * 4;
     static constexpr int OFF_FLAGS = OFF_BAR + 8 * 64;     // abort flag, TMEM address
     static constexpr int SMEM = OFF_FLAGS + 16 + 1024;     // + alignment slack
 };
 
 // barriers
 enum {
-    BAR_B_FULL = 0,                          // [4] token stage landed (TMA bytes)
-    BAR_A_FULL = BAR_B_FULL + PF_STAGES,     // [4] weight stage converted (8 warps)
-    BAR_ST_EMPTY = BAR_A_FULL + PF_STAGES,   // [4] stage consumed by the MMAs (commit)
+    BAR_B_FULL = 0,                          // [S] token stage landed (TMA bytes)
+    BAR_A_FULL = BAR_B_FULL + PF_STAGES,     // [S] weight stage converted (the 4 warps of one group)
+    BAR_ST_EMPTY = BAR_A_FULL + PF_STAGES,   // [S] stage consumed by the MMAs (commit)
     BAR_RAW_FULL = BAR_ST_EMPTY + PF_STAGES, // [3] raw super-block landed (TMA bytes)
     BAR_RAW_EMPTY = BAR_RAW_FULL + 3,        // [3] raw super-block converted (8 warps)
     BAR_SBD_FULL = BAR_RAW_EMPTY + 3,        // [4] bsums tile + dA landed (TMA bytes)
-    BAR_A2_FULL = BAR_SBD_FULL + PF_NSB,     // [4] mins tile, d, dmin written (8 warps)
+    BAR_A2_FULL = BAR_SBD_FULL + PF_NSB,     // [4] mins operand, row scales written (group 0, 4 warps)
     BAR_SB_FREE = BAR_A2_FULL + PF_NSB,      // [4] epilogue done with a super-block (8 warps)
     BAR_ACC_FULL = BAR_SB_FREE + PF_NSB,     // [2] accumulators of a super-block ready (commit)
     BAR_ACC_EMPTY = BAR_ACC_FULL + 2,        // [2] accumulators read (8 warps)
@@ -104,6 +107,15 @@ enum {
 };
 static_assert(NBARS <= 64, "barrier area");
 constexpr uint32_t PF_TMEM_COLS = 512;
+// tensor-memory columns
+constexpr uint32_t TM_ACC = 0;      // accumulators: 128 * buf
+constexpr uint32_t TM_A = 256;      // A stages: 32 * stage
+constexpr uint32_t TM_MIN = TM_A + 32 * PF_STAGES;   // mins operands: 16 * (sb % PF_NSB): 8 columns hi, 8 lo
+static_assert(TM_MIN + 16 * PF_NSB <= PF_TMEM_COLS, "tensor-memory columns");
+static_assert(PF_STAGES % 2 == 0, "stages alternate between the two converter groups");
+// pipeline stage of K-step t and the parity of its use
+__device__ __forceinline__ int stage_of(int t) { return t % PF_STAGES; }
+__device__ __forceinline__ uint32_t use_of(int t) { return (uint32_t)(t / PF_STAGES) & 1u; }
 
 struct PfParams {
     int n_out;
@@ -116,11 +128,15 @@ struct PfParams {
 };
 
 // Bounded wait shared by all roles: gives up when another role already gave
-// up, or after 2 s, recording the failure in the status word.
+// up, or after 2 s, recording the failure in the status word. Roles other
+// than the MMA issuer wait suspended (a suspend-time hint), so they take no
+// issue slots from the warps that share their scheduler (the MMA issuer's
+// warp among them); the MMA issuer polls.
+template <bool POLL = false>
 __device__ __forceinline__ bool pf_wait(uint32_t bar, uint32_t parity, volatile int *abort_flag, int *status) {
     if (mbar_poll(bar, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
-    while (!mbar_poll(bar, parity)) {
+    while (!(POLL ? mbar_poll(bar, parity) : mbar_try_wait(bar, parity))) {
         if (*abort_flag) return false;
         if (globaltimer_ns() - t0 > 2000000000ull) {
             *abort_flag = 1;
@@ -136,15 +152,6 @@ __device__ __forceinline__ void pf_settle(uint32_t bar, uint32_t parity) {
 }
 
 __device__ __forceinline__ uint32_t byte_at(uint32_t w, int i) { return (w >> (8 * i)) & 0xffu; }
-
-// 128-byte swizzle, K-major: row r, 16-byte chunk j of a 128-row x 64-f16 tile
-__device__ __forceinline__ uint32_t swz128(int r, int j) {
-    return (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + ((j ^ (r & 7)) << 4));
-}
-// 32-byte swizzle, K-major: row r, chunk j (0/1) of a 128-row x 16-f16 tile
-__device__ __forceinline__ uint32_t swz32(int r, int j) {
-    return (uint32_t)((r >> 3) * 256 + (r & 7) * 32 + ((j ^ ((r >> 2) & 1)) << 4));
-}
 
 // f16 pair (1024 + q0, 1024 + q2) from the low nibbles of bytes 0 and 2 of x
 // (mask 0x000f000f) or 1024 + 16 q from the high nibbles (mask 0x00f000f0),
@@ -194,11 +201,14 @@ struct PfCtx {
     int *status;
 };
 
-// Q4_K converter for one super-block. Thread: tile row r, nibble half g
-// (0: sub-block 2c from the low nibbles of qs[32c..], 1: 2c+1 from the high).
+// Q4_K converter for one super-block. Thread: tile row r (tensor-memory lane
+// of this warp's quarter); converter group G converts the K-steps c with
+// c % 2 == G (c: qs[32c..32c+31], low nibbles = sub-block 2c, high = 2c+1).
+// Group 0 also writes the mins operand and the row scale. tl = this warp's
+// lane base in tensor memory.
 template <class Lay>
-__device__ __forceinline__ bool convert_q4k(const PfCtx &cx, uint32_t base, int sb, int rb, int b4, int r, int g,
-                                            bool valid, uint32_t barbase) {
+__device__ __forceinline__ bool convert_q4k(const PfCtx &cx, uint32_t base, uint32_t tl, int sb, int rb, int b4,
+                                            int r, int G, bool valid, uint32_t barbase) {
     constexpr uint32_t FULL = 0xffffffffu;
     auto bar = [&](int i) { return barbase + 8u * (uint32_t)i; };
     const uint32_t raw = base + Lay::OFF_RAW + rb * Lay::RAW_BUF + r * B_Q4_K;
@@ -206,42 +216,69 @@ __device__ __forceinline__ bool convert_q4k(const PfCtx &cx, uint32_t base, int 
     // 6-bit scales / mins (src/kernels.c:377-382)
     const uint32_t sc_lo = h.y & 0x3f3f3f3fu;
     const uint32_t sc_hi = (h.w & 0x0f0f0f0fu) | ((h.y >> 2) & 0x30303030u);
-    // mins tile: column i (bsums index) holds mn[i / 2]; half g writes columns 8g..8g+7
-    const uint32_t mnw = g ? (((h.w >> 4) & 0x0f0f0f0fu) | ((h.z >> 2) & 0x30303030u)) : (h.z & 0x3f3f3f3fu);
-    uint32_t mw[4];
+    const uint32_t mn_lo = h.z & 0x3f3f3f3fu;
+    const uint32_t mn_hi = ((h.w >> 4) & 0x0f0f0f0fu) | ((h.z >> 2) & 0x30303030u);
+    const float d = h2f(h.x & 0xffffu), dmin = h2f(h.x >> 16);
+    uint32_t mn_max = 0;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        const float mv = (float)byte_at(mnw, j);
-        mw[j] = half2_bits(mv, mv);
+    for (int j = 0; j < 4; ++j) mn_max = max(mn_max, max(byte_at(mn_lo, j), byte_at(mn_hi, j)));
+    // f = d 2^s with the mins factor dmin / f * mn inside f16 range; a zero
+    // (or, past s = 14, negligible) d leaves only the mins term, exactly
+    int sexp = 0;
+    bool keep_main = d != 0.0f;
+    if (keep_main) {
+        const float ratio = fabsf(dmin) * (float)mn_max / (60000.0f * fabsf(d));
+        if (ratio > 1.0f) sexp = ilogbf(ratio) + 1;
+        if (sexp > 14) keep_main = false;
     }
-    sts128(base + Lay::OFF_A2 + b4 * PF_MIN_BYTES + swz32(r, g), mw[0], mw[1], mw[2], mw[3]);
-    if (g == 0) {
-        reinterpret_cast<float *>(cx.smem + Lay::OFF_DW)[b4 * PF_BM + r] = valid ? h2f(h.x & 0xffffu) : 0.0f;
-        reinterpret_cast<float *>(cx.smem + Lay::OFF_DM)[b4 * PF_BM + r] = valid ? h2f(h.x >> 16) : 0.0f;
+    if (G == 0) {
+        const float f = keep_main ? ldexpf(d, sexp) : ldexpf(dmin, -10);
+        const float mfac = f != 0.0f ? dmin / f : 0.0f;
+        reinterpret_cast<float *>(cx.smem + Lay::OFF_DW)[b4 * PF_BM + r] = valid ? f : 0.0f;
+        // mins operand: 16 k (the bsums index i, mn[i / 2]) as -(hi + lo), the
+        // hi parts in columns 0-7, the lo parts in 8-15, two f16 per column
+        uint32_t mw[16];
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+            const float mu = mfac * (float)byte_at(c < 4 ? mn_lo : mn_hi, c & 3);
+            const float hi = __half2float(__float2half_rn(mu));
+            mw[c] = valid ? half2_bits(-hi, -hi) : 0u;
+            mw[8 + c] = valid ? half2_bits(hi - mu, hi - mu) : 0u;
+        }
+        tc_fence_after();
+        tmem_st16(tl + TM_MIN + 16 * b4, mw);
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if ((threadIdx.x & 31) == 0) mbar_arrive(bar(BAR_A2_FULL + b4));
     }
-    fence_proxy_async();
-    __syncwarp();
-    if ((threadIdx.x & 31) == 0) mbar_arrive(bar(BAR_A2_FULL + b4));
-    const uint32_t nmask = g ? 0x00f000f0u : 0x000f000fu;
-    for (int c = 0; c < 4; ++c) {
-        const int t = 4 * sb + c, s = t & 3;
-        if (!__all_sync(FULL, pf_wait(bar(BAR_ST_EMPTY + s), ((t >> 2) & 1) ^ 1, cx.abort_flag, cx.status)))
+    for (int c = G; c < 4; c += 2) {
+        const int t = 4 * sb + c, s = stage_of(t);
+        if (!__all_sync(FULL, pf_wait(bar(BAR_ST_EMPTY + s), use_of(t) ^ 1, cx.abort_flag, cx.status)))
             return false;
-        const uint32_t abase = base + Lay::OFF_A + s * PF_STAGE_BYTES;
         const uint4 q0 = lds128(raw + 16 + 32 * c), q1 = lds128(raw + 32 + 32 * c);
         const uint32_t x[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
-        const float sv = valid ? (float)byte_at(c < 2 ? sc_lo : sc_hi, (2 * c + g) & 3) : 0.0f;
-        // (1024 + q) * sc - 1024 sc, or (1024 + 16 q) * sc/16 - 64 sc
-        const float mf = g ? 0.0625f * sv : sv, af = g ? -64.0f * sv : -1024.0f * sv;
-        const uint32_t mul = half2_bits(mf, mf), add = half2_bits(af, af);
-        // slot order inside each group of four: elements 0, 2, 1, 3
+        const uint32_t scw = c < 2 ? sc_lo : sc_hi;
+        const float s0 = (valid && keep_main) ? ldexpf((float)byte_at(scw, (2 * c) & 3), -sexp) : 0.0f;
+        const float s1 = (valid && keep_main) ? ldexpf((float)byte_at(scw, (2 * c + 1) & 3), -sexp) : 0.0f;
+        // (1024 + q) * sc - 1024 sc for the low nibbles, (1024 + 16 q) * sc/16 -
+        // 64 sc for the high ones: exact
+        const uint32_t mul0 = half2_bits(s0, s0), add0 = half2_bits(-1024.0f * s0, -1024.0f * s0);
+        const uint32_t mul1 = half2_bits(0.0625f * s1, 0.0625f * s1), add1 = half2_bits(-64.0f * s1, -64.0f * s1);
+        // columns 0-15: sub-block 2c, 16-31: 2c+1; slot order inside each group
+        // of four elements: 0, 2, 1, 3
+        uint32_t w[32];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const uint32_t u = x[2 * j], v = x[2 * j + 1];
-            sts128(abase + swz128(r, 4 * g + j), nib_f16(u, nmask, mul, add), nib_f16(u >> 8, nmask, mul, add),
-                   nib_f16(v, nmask, mul, add), nib_f16(v >> 8, nmask, mul, add));
+        for (int k = 0; k < 8; ++k) {
+            w[2 * k] = nib_f16(x[k], 0x000f000fu, mul0, add0);
+            w[2 * k + 1] = nib_f16(x[k] >> 8, 0x000f000fu, mul0, add0);
+            w[16 + 2 * k] = nib_f16(x[k], 0x00f000f0u, mul1, add1);
+            w[16 + 2 * k + 1] = nib_f16(x[k] >> 8, 0x00f000f0u, mul1, add1);
         }
-        fence_proxy_async();
+        tc_fence_after();
+        tmem_st32(tl + TM_A + 32 * s, w);
+        tmem_wait_st();
+        tc_fence_before();
         __syncwarp();
         if ((threadIdx.x & 31) == 0) mbar_arrive(bar(BAR_A_FULL + s));
     }
@@ -249,13 +286,14 @@ __device__ __forceinline__ bool convert_q4k(const PfCtx &cx, uint32_t base, int 
 }
 
 // Q6_K converter for one super-block (src/kernels.c:480-523). Thread: tile
-// row r, half g of each 64-element quarter (elements 32g..32g+31 of it).
-// Quarter cq (h = cq / 2, group G = 2 (cq & 1) + g of half h) element l:
+// row r; converter group G converts the quarters cq (64 elements, K-steps
+// 2cq and 2cq+1: the two planes) with cq % 2 == G. Quarter cq (h = cq / 2)
+// element 32g + l (g = 0, 1; group G' = 2 (cq & 1) + g of half h):
 // ql[64h + 32g + l] (low nibble for even cq, high for odd), qh[32h + l] bits
-// 2G..2G+1, scale sc[4cq + 2g + l / 16].
+// 2G'..2G'+1, scale sc[4cq + 2g + l / 16].
 template <class Lay>
-__device__ __forceinline__ bool convert_q6k(const PfCtx &cx, uint32_t base, int sb, int rb, int b4, int r, int g,
-                                            bool valid, uint32_t barbase) {
+__device__ __forceinline__ bool convert_q6k(const PfCtx &cx, uint32_t base, uint32_t tl, int sb, int rb, int b4,
+                                            int r, int G, bool valid, uint32_t barbase) {
     constexpr uint32_t FULL = 0xffffffffu;
     auto bar = [&](int i) { return barbase + 8u * (uint32_t)i; };
     const int head = (int)(((int64_t)sb * B_Q6_K) & 15);
@@ -267,54 +305,58 @@ __device__ __forceinline__ bool convert_q6k(const PfCtx &cx, uint32_t base, int 
 #pragma unroll
         for (int k = 0; k < 5; ++k) S[k] = 0;
     }
-    if (g == 0) reinterpret_cast<float *>(cx.smem + Lay::OFF_DW)[b4 * PF_BM + r] = h2f(S[4] & 0xffffu);
-    __syncwarp();
-    if ((threadIdx.x & 31) == 0) mbar_arrive(bar(BAR_A2_FULL + b4));
-    for (int cq = 0; cq < 4; ++cq) {
-        const int t0 = 8 * sb + 2 * cq, s0 = t0 & 3, s1 = (t0 + 1) & 3;
-        if (!__all_sync(FULL, pf_wait(bar(BAR_ST_EMPTY + s0), ((t0 >> 2) & 1) ^ 1, cx.abort_flag, cx.status) &&
-                                  pf_wait(bar(BAR_ST_EMPTY + s1), (((t0 + 1) >> 2) & 1) ^ 1, cx.abort_flag, cx.status)))
+    if (G == 0) {
+        reinterpret_cast<float *>(cx.smem + Lay::OFF_DW)[b4 * PF_BM + r] = h2f(S[4] & 0xffffu);
+        __syncwarp();
+        if ((threadIdx.x & 31) == 0) mbar_arrive(bar(BAR_A2_FULL + b4));
+    }
+    for (int cq = G; cq < 4; cq += 2) {
+        const int t0 = 8 * sb + 2 * cq, s0 = stage_of(t0), s1 = stage_of(t0 + 1);
+        if (!__all_sync(FULL, pf_wait(bar(BAR_ST_EMPTY + s0), use_of(t0) ^ 1, cx.abort_flag, cx.status) &&
+                                  pf_wait(bar(BAR_ST_EMPTY + s1), use_of(t0 + 1) ^ 1, cx.abort_flag, cx.status)))
             return false;
-        const int h = cq >> 1, G = 2 * (cq & 1) + g;
-        uint32_t QL[8], QH[8];
-        span_words<8>(row + 64 * h + 32 * g, head, QL);
-        span_words<8>(row + 128 + 32 * h, head, QH);
-        // the two 16-element sub-blocks of this thread's 32 elements
-        const int sbi = 4 * cq + 2 * g;
-        const int sa = (int)(int8_t)byte_at(S[sbi >> 2], sbi & 3);
-        const int sb2 = (int)(int8_t)byte_at(S[(sbi + 1) >> 2], (sbi + 1) & 3);
-        const int sv[2] = {valid ? sa : 0, valid ? sb2 : 0};
-        uint32_t mul0[2], add0[2], mul1[2], add1[2];
-#pragma unroll
-        for (int i = 0; i < 2; ++i) {
-            const float lo = (float)(sv[i] & 15), hi = (float)(sv[i] >> 4);   // sc = 16 hi + lo
-            mul0[i] = half2_bits(lo, lo);
-            add0[i] = half2_bits(-1056.0f * lo, -1056.0f * lo);              // (1024 + q) lo - 1056 lo
-            mul1[i] = half2_bits(hi, hi);
-            add1[i] = half2_bits(-1056.0f * hi, -1056.0f * hi);
-        }
-        const uint32_t a0 = base + Lay::OFF_A + s0 * PF_STAGE_BYTES, a1 = base + Lay::OFF_A + s1 * PF_STAGE_BYTES;
+        const int h = cq >> 1;
         const int nsh = (cq & 1) ? 4 : 0;
+        uint32_t QH[8];
+        span_words<8>(row + 128 + 32 * h, head, QH);
+        uint32_t p0[32], p1[32];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const int i = j >> 1;   // sub-block of words 2j, 2j+1
-            uint32_t p0[4], p1[4];
+        for (int g = 0; g < 2; ++g) {
+            const int Gp = 2 * (cq & 1) + g;
+            uint32_t QL[8];
+            span_words<8>(row + 64 * h + 32 * g, head, QL);
+            // the two 16-element sub-blocks of these 32 elements
+            const int sbi = 4 * cq + 2 * g;
+            const int sa = (int)(int8_t)byte_at(S[sbi >> 2], sbi & 3);
+            const int sb2 = (int)(int8_t)byte_at(S[(sbi + 1) >> 2], (sbi + 1) & 3);
+            const int sv[2] = {valid ? sa : 0, valid ? sb2 : 0};
+            uint32_t mul0[2], add0[2], mul1[2], add1[2];
 #pragma unroll
-            for (int w2 = 0; w2 < 2; ++w2) {
-                const int k = 2 * j + w2;
+            for (int i = 0; i < 2; ++i) {
+                const float lo = (float)(sv[i] & 15), hi = (float)(sv[i] >> 4);   // sc = 16 hi + lo
+                mul0[i] = half2_bits(lo, lo);
+                add0[i] = half2_bits(-1056.0f * lo, -1056.0f * lo);              // (1024 + q) lo - 1056 lo
+                mul1[i] = half2_bits(hi, hi);
+                add1[i] = half2_bits(-1056.0f * hi, -1056.0f * hi);
+            }
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                const int i = k >> 2;   // sub-block of word k
                 // 6-bit q of elements 4k..4k+3, one per byte
-                const uint32_t q = ((QL[k] >> nsh) & 0x0f0f0f0fu) | (((QH[k] >> (2 * G)) & 0x03030303u) << 4);
+                const uint32_t q = ((QL[k] >> nsh) & 0x0f0f0f0fu) | (((QH[k] >> (2 * Gp)) & 0x03030303u) << 4);
                 const uint32_t e02 = and_or(q, 0x00ff00ffu, 0x64006400u);
                 const uint32_t e13 = and_or(q >> 8, 0x00ff00ffu, 0x64006400u);
-                p0[2 * w2] = hfma2_u32(e02, mul0[i], add0[i]);
-                p0[2 * w2 + 1] = hfma2_u32(e13, mul0[i], add0[i]);
-                p1[2 * w2] = hfma2_u32(e02, mul1[i], add1[i]);
-                p1[2 * w2 + 1] = hfma2_u32(e13, mul1[i], add1[i]);
+                p0[16 * g + 2 * k] = hfma2_u32(e02, mul0[i], add0[i]);
+                p0[16 * g + 2 * k + 1] = hfma2_u32(e13, mul0[i], add0[i]);
+                p1[16 * g + 2 * k] = hfma2_u32(e02, mul1[i], add1[i]);
+                p1[16 * g + 2 * k + 1] = hfma2_u32(e13, mul1[i], add1[i]);
             }
-            sts128(a0 + swz128(r, 4 * g + j), p0[0], p0[1], p0[2], p0[3]);
-            sts128(a1 + swz128(r, 4 * g + j), p1[0], p1[1], p1[2], p1[3]);
         }
-        fence_proxy_async();
+        tc_fence_after();
+        tmem_st32(tl + TM_A + 32 * s0, p0);
+        tmem_st32(tl + TM_A + 32 * s1, p1);
+        tmem_wait_st();
+        tc_fence_before();
         __syncwarp();
         if ((threadIdx.x & 31) == 0) {
             mbar_arrive(bar(BAR_A_FULL + s0));
@@ -347,7 +389,7 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
     if (threadIdx.x == 0) {
         for (int i = 0; i < PF_STAGES; ++i) {
             mbar_init(bar(BAR_B_FULL + i), 1);
-            mbar_init(bar(BAR_A_FULL + i), N_CONV);
+            mbar_init(bar(BAR_A_FULL + i), N_CONV / 2);
             mbar_init(bar(BAR_ST_EMPTY + i), 1);
         }
         for (int i = 0; i < F::NRAW; ++i) {
@@ -356,7 +398,7 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
         }
         for (int i = 0; i < PF_NSB; ++i) {
             mbar_init(bar(BAR_SBD_FULL + i), 1);
-            mbar_init(bar(BAR_A2_FULL + i), N_CONV);
+            mbar_init(bar(BAR_A2_FULL + i), N_CONV / 2);
             mbar_init(bar(BAR_SB_FREE + i), N_EPI);
         }
         for (int i = 0; i < 2; ++i) {
@@ -394,8 +436,8 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
                 sb_issued = sb + 1;
                 bool ok = true;
                 for (int c = 0; c < KST; ++c) {
-                    const int t = KST * sb + c, s = t & 3;
-                    if (!pf_wait(bar(BAR_ST_EMPTY + s), ((t >> 2) & 1) ^ 1, abort_flag, p.status)) { ok = false; break; }
+                    const int t = KST * sb + c, s = stage_of(t);
+                    if (!pf_wait(bar(BAR_ST_EMPTY + s), use_of(t) ^ 1, abort_flag, p.status)) { ok = false; break; }
                     mbar_expect_tx(bar(BAR_B_FULL + s), PF_STAGE_BYTES);
                     tma_load_2d(sb0 + Lay::OFF_B + s * PF_STAGE_BYTES, &tmB, PF_KS * t, tok0, bar(BAR_B_FULL + s));
                     t_issued = t + 1;
@@ -403,7 +445,7 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
                 if (!ok) break;
             }
             if (*abort_flag) {
-                for (int t = max(0, t_issued - PF_STAGES); t < t_issued; ++t) pf_settle(bar(BAR_B_FULL + (t & 3)), (t >> 2) & 1);
+                for (int t = max(0, t_issued - PF_STAGES); t < t_issued; ++t) pf_settle(bar(BAR_B_FULL + stage_of(t)), use_of(t));
                 for (int sb = max(0, sb_issued - PF_NSB); sb < sb_issued; ++sb)
                     pf_settle(bar(BAR_SBD_FULL + sb % PF_NSB), (sb / PF_NSB) & 1);
             }
@@ -415,32 +457,34 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
             for (int sb = 0; sb < nsb; ++sb) {
                 const int buf = sb & 1;
                 const uint32_t ph = (sb >> 1) & 1;
-                if (!pf_wait(bar(BAR_ACC_EMPTY + buf), ph ^ 1, abort_flag, p.status)) break;
+                if (!pf_wait<true>(bar(BAR_ACC_EMPTY + buf), ph ^ 1, abort_flag, p.status)) break;
                 tc_fence_after();
-                const uint32_t d1 = tmem + (uint32_t)buf * 256u, d2 = d1 + 128u;
+                const uint32_t dacc = tmem + TM_ACC + (uint32_t)buf * 128u;
                 bool ok = true;
                 for (int c = 0; c < KST; ++c) {
-                    const int t = KST * sb + c, s = t & 3;
-                    const uint32_t sph = (t >> 2) & 1;
-                    if (!pf_wait(bar(BAR_A_FULL + s), sph, abort_flag, p.status) ||
-                        !pf_wait(bar(BAR_B_FULL + s), sph, abort_flag, p.status)) { ok = false; break; }
+                    const int t = KST * sb + c, s = stage_of(t);
+                    const uint32_t sph = use_of(t);
+                    if (!pf_wait<true>(bar(BAR_A_FULL + s), sph, abort_flag, p.status) ||
+                        !pf_wait<true>(bar(BAR_B_FULL + s), sph, abort_flag, p.status)) { ok = false; break; }
                     tc_fence_after();
-                    const uint32_t a = sb0 + Lay::OFF_A + s * PF_STAGE_BYTES, b = sb0 + Lay::OFF_B + s * PF_STAGE_BYTES;
+                    const uint32_t b = sb0 + Lay::OFF_B + s * PF_STAGE_BYTES;
 #pragma unroll
                     for (int kk = 0; kk < PF_KS / 16; ++kk)
-                        tc_mma_f16(d1, smem_desc(a + 32 * kk, 1024, SMEM_SWZ_128B),
-                                   smem_desc(b + 32 * kk, 1024, SMEM_SWZ_128B), idesc, (c | kk) != 0);
+                        tc_mma_f16_ts(dacc, tmem + TM_A + 32u * s + 8u * kk, smem_desc(b + 32 * kk, 1024, SMEM_SWZ_128B),
+                                      idesc, (c | kk) != 0);
                     tc_commit(bar(BAR_ST_EMPTY + s));
                 }
                 if (!ok) break;
                 if constexpr (F::MINS) {
+                    // the mins term, into the same accumulator: -(hi + lo) x bsums
                     const int b4 = sb % PF_NSB;
                     const uint32_t ph4 = (sb / PF_NSB) & 1;
-                    if (!pf_wait(bar(BAR_A2_FULL + b4), ph4, abort_flag, p.status) ||
-                        !pf_wait(bar(BAR_SBD_FULL + b4), ph4, abort_flag, p.status)) break;
+                    if (!pf_wait<true>(bar(BAR_A2_FULL + b4), ph4, abort_flag, p.status) ||
+                        !pf_wait<true>(bar(BAR_SBD_FULL + b4), ph4, abort_flag, p.status)) break;
                     tc_fence_after();
-                    tc_mma_f16(d2, smem_desc(sb0 + Lay::OFF_A2 + b4 * PF_MIN_BYTES, 256, SMEM_SWZ_32B),
-                               smem_desc(sb0 + Lay::OFF_B2 + b4 * PF_MIN_BYTES, 256, SMEM_SWZ_32B), idesc, 0);
+                    const uint64_t bd = smem_desc(sb0 + Lay::OFF_B2 + b4 * PF_MIN_BYTES, 256, SMEM_SWZ_32B);
+                    tc_mma_f16_ts(dacc, tmem + TM_MIN + 16u * b4, bd, idesc, 1);
+                    tc_mma_f16_ts(dacc, tmem + TM_MIN + 16u * b4 + 8u, bd, idesc, 1);
                 }
                 tc_commit(bar(BAR_ACC_FULL + buf));
             }
@@ -467,18 +511,19 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
         }
     } else if (warp < W_EPI) {
         // ---- weight converters ----
-        const int cw = warp - W_CONV;
-        const int r = (cw & 3) * 32 + lane;
-        const int g = cw >> 2;
+        // a warp may only address its own 32-lane quarter of tensor memory
+        const int r = 32 * (warp & 3) + lane;
+        const int grp = (warp - W_CONV) >> 2;   // converter group
         const bool valid = r < rows;
+        const uint32_t tl = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
         const PfCtx cx{sb0, smem, abort_flag, p.status};
         for (int sb = 0; sb < nsb; ++sb) {
             const int rb = sb % F::NRAW, b4 = sb % PF_NSB;
             if (!__all_sync(FULL, pf_wait(bar(BAR_RAW_FULL + rb), (sb / F::NRAW) & 1, abort_flag, p.status))) break;
             if (!__all_sync(FULL, pf_wait(bar(BAR_SB_FREE + b4), ((sb / PF_NSB) & 1) ^ 1, abort_flag, p.status))) break;
             bool ok;
-            if constexpr (T == T_Q4_K) ok = convert_q4k<Lay>(cx, sb0, sb, rb, b4, r, g, valid, barbase);
-            else ok = convert_q6k<Lay>(cx, sb0, sb, rb, b4, r, g, valid, barbase);
+            if constexpr (T == T_Q4_K) ok = convert_q4k<Lay>(cx, sb0, tl, sb, rb, b4, r, grp, valid, barbase);
+            else ok = convert_q6k<Lay>(cx, sb0, tl, sb, rb, b4, r, grp, valid, barbase);
             if (!ok) break;
             __syncwarp();
             if (lane == 0) mbar_arrive(bar(BAR_RAW_EMPTY + rb));
@@ -502,17 +547,14 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
                 break;
             }
             tc_fence_after();
-            const float dw = reinterpret_cast<const float *>(smem + Lay::OFF_DW)[b4 * PF_BM + r];
-            const float ndm = F::MINS ? -reinterpret_cast<const float *>(smem + Lay::OFF_DM)[b4 * PF_BM + r] : 0.0f;
+            const float fr = reinterpret_cast<const float *>(smem + Lay::OFF_DW)[b4 * PF_BM + r];
             const float4 *da4 = reinterpret_cast<const float4 *>(smem + Lay::OFF_DA + b4 * PF_BN * 4 + c0 * 4);
-            const uint32_t ta = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)buf * 256u + (uint32_t)c0;
+            const uint32_t ta = tmem + ((uint32_t)(32 * q) << 16) + TM_ACC + (uint32_t)buf * 128u + (uint32_t)c0;
 #pragma unroll
             for (int cc = 0; cc < EPI_COLS / 8; ++cc) {
-                uint32_t v1[8], v2[8];
-                tmem_ld8(ta + 8 * cc, v1);
-                if constexpr (F::MINS) tmem_ld8(ta + 128 + 8 * cc, v2);
-                tmem_wait_ld(v1);
-                if constexpr (F::MINS) tmem_wait_ld(v2);
+                uint32_t v[8];
+                tmem_ld8(ta + 8 * cc, v);
+                tmem_wait_ld(v);
 #pragma unroll
                 for (int gq = 0; gq < 2; ++gq) {
                     const float4 d = da4[2 * cc + gq];
@@ -520,9 +562,7 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
 #pragma unroll
                     for (int e = 0; e < 4; ++e) {
                         const int j = 4 * gq + e;
-                        float sv = dw * __uint_as_float(v1[j]);
-                        if constexpr (F::MINS) sv = fmaf(ndm, __uint_as_float(v2[j]), sv);
-                        acc[8 * cc + j] = fmaf(dv[e], sv, acc[8 * cc + j]);
+                        acc[8 * cc + j] = fmaf(dv[e], fr * __uint_as_float(v[j]), acc[8 * cc + j]);
                     }
                 }
             }

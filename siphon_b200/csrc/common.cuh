@@ -126,6 +126,12 @@ __device__ __forceinline__ void fence_proxy_async() {
 __device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" :: "r"(bar), "r"(bytes) : "memory");
 }
+// Arrival that sets the expected transaction bytes without release ordering:
+// for an arrive whose barrier only tracks asynchronous copies into the slot
+// (no generic writes before it need to be seen by the waiting threads).
+__device__ __forceinline__ void mbar_expect_tx_relaxed(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.relaxed.cta.shared::cta.b64 _, [%0], %1;" :: "r"(bar), "r"(bytes) : "memory");
+}
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" :: "r"(bar) : "memory");
 }

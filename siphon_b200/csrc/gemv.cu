@@ -42,61 +42,38 @@ struct Producer {
             locate<T>(p);
         }
     }
-    // One contiguous piece: bytes [src, src + len) into dst, as a 16-byte
-    // aligned bulk copy plus, at the very end of a matrix, up to 15 tail bytes
-    // written by this lane. Returns the bulk bytes; *head = src & 15.
-    __device__ int64_t piece(const uint8_t *psrc, int64_t len, uint8_t *dst, int *head, bool &lane_bytes) {
-        const uintptr_t a = reinterpret_cast<uintptr_t>(psrc);
-        const uint8_t *al = reinterpret_cast<const uint8_t *>(a & ~uintptr_t(15));
-        *head = (int)(a & 15);
-        int64_t bulk = (*head + len + 15) & ~int64_t(15);
-        if (al + bulk > mend) bulk = (int64_t)(mend - al) & ~int64_t(15);
-        const int tail = (int)(*head + len - bulk);
-        if (tail > 0) {
-            for (int i = 0; i < tail; ++i) dst[bulk + i] = (uint8_t)ldg_u8(al + bulk + i);
-            lane_bytes = true;
-        }
-        return bulk;
-    }
-    // Fill ring slot s with the current item and publish its geometry next
-    // to it. Whole rows (one chunk per row) arrive as one contiguous piece;
-    // chunks of several rows as one piece per row, p.piece_stride apart.
+    // Fill ring slot s with the current item: a 16-byte aligned bulk copy
+    // plus, at the very end of a matrix, up to 15 tail bytes written by this
+    // lane; publish the geometry next to the slot.
     template <uint32_t T>
     __device__ void produce(const GemvParams &p, int s, uint8_t *slot, int4 *info, uint32_t full, uint64_t policy) {
+        int64_t len;
+        if (p.nchunks == 1) {
+            len = (int64_t)rows * p.row_bytes;
+        } else {
+            const int64_t rest = p.row_bytes - (int64_t)u0 * Fmt<T>::unit_bytes;
+            const int64_t want = (int64_t)cu * Fmt<T>::unit_bytes;
+            len = want < rest ? want : rest;
+        }
+        const uintptr_t a = reinterpret_cast<uintptr_t>(src);
+        const uint8_t *al = reinterpret_cast<const uint8_t *>(a & ~uintptr_t(15));
+        const int head = (int)(a & 15);
+        int64_t bulk = (head + len + 15) & ~int64_t(15);
+        if (al + bulk > mend) bulk = (int64_t)(mend - al) & ~int64_t(15);
+        const int tail = (int)(head + len - bulk);
         // generic writes to this slot before an async-proxy write to it need a proxy fence
         if (tailmask & (1u << s)) {
             fence_proxy_async();
             tailmask &= ~(1u << s);
         }
-        bool lane_bytes = false;
-        int head = 0, heads = 0;
-        if (p.nchunks == 1) {
-            const int64_t bulk = piece(src, (int64_t)rows * p.row_bytes, slot, &head, lane_bytes);
-            mbar_expect_tx(full, (uint32_t)bulk);   // also the phase's one arrival
-            if (bulk > 0) bulk_g2s_hint(smem_addr(slot), src - head, (uint32_t)bulk, full, policy);
-        } else {
-            const int64_t rest = p.row_bytes - (int64_t)u0 * Fmt<T>::unit_bytes;
-            const int64_t want = (int64_t)cu * Fmt<T>::unit_bytes;
-            const int64_t len = want < rest ? want : rest;
-            int64_t bulk[4];
-            int64_t total = 0;
-            for (int r = 0; r < rows; ++r) {
-                int h;
-                bulk[r] = piece(src + (int64_t)r * p.row_bytes, len, slot + r * p.piece_stride, &h, lane_bytes);
-                heads |= h << (4 * r);
-                total += bulk[r];
-            }
-            mbar_expect_tx(full, (uint32_t)total);
-            for (int r = 0; r < rows; ++r) {
-                const uint8_t *ps = src + (int64_t)r * p.row_bytes;
-                const int h = (heads >> (4 * r)) & 15;
-                if (bulk[r] > 0)
-                    bulk_g2s_hint(smem_addr(slot + r * p.piece_stride), ps - h, (uint32_t)bulk[r], full, policy);
-            }
+        if (tail > 0) {
+            for (int i = 0; i < tail; ++i) slot[bulk + i] = (uint8_t)ldg_u8(al + bulk + i);
+            tailmask |= 1u << s;
         }
-        if (lane_bytes) tailmask |= 1u << s;
         info[0] = make_int4(row0, rows | (head << 16), u0, cu);
-        info[1] = make_int4(mat, heads, 0, 0);
+        info[1] = make_int4(mat, 0, 0, 0);
+        mbar_expect_tx(full, (uint32_t)bulk);   // also the phase's one arrival
+        if (bulk > 0) bulk_g2s_hint(smem_addr(slot), al, (uint32_t)bulk, full, policy);
     }
 };
 
@@ -176,8 +153,8 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 2) gemv_kernel(const GemvPara
     else prep_activation<F::act>(av, p.xq, p.n_in, rank, nrank);
     cluster_sync();
 
-    const int r_l = lane / p.cu;
-    const int u_l = lane - r_l * p.cu;
+    const int r_l = p.nchunks == 1 ? lane / p.cu : 0;
+    const int u_l = p.nchunks == 1 ? lane - r_l * p.cu : lane;
     // chain strides in floats: a multiple of 4 that is an odd number of
     // 16-byte units, so the chain lanes' vector loads hit distinct banks
     int cup = (p.cu + 3) & ~3;
@@ -196,7 +173,7 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 2) gemv_kernel(const GemvPara
             break;
         }
         const int4 g = info[2 * s];
-        const int mat = info[2 * s + 1].x, heads = info[2 * s + 1].y;
+        const int mat = info[2 * s + 1].x;
         const int rows = g.y & 0xffff, u0 = g.z, cu = g.w;
         uint8_t *slot = slots + (size_t)s * p.slot_bytes;
         const uint8_t *data = slot + (g.y >> 16);
@@ -204,9 +181,7 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 2) gemv_kernel(const GemvPara
         // ---- phase 1: each lane decodes its unit ----
         if (r_l < rows && u_l < cu) {
             const int ug = u0 + u_l;
-            const uint8_t *wb = p.nchunks == 1 ? data + (int64_t)r_l * p.row_bytes + u_l * F::unit_bytes
-                                               : slot + r_l * p.piece_stride + ((heads >> (4 * r_l)) & 15) +
-                                                     u_l * F::unit_bytes;
+            const uint8_t *wb = data + (int64_t)r_l * (p.nchunks == 1 ? p.row_bytes : 0) + u_l * F::unit_bytes;
             const uint8_t *rec = av.rec(ug);
             if constexpr (F::kind == 3) {
                 const int nb = min(8, p.n_in / 32 - ug * 8);
@@ -295,23 +270,20 @@ static int launch_gemv_t(const GemvLaunch &L, cudaStream_t st) {
     const int nblk = (F::kind == 3) ? L.n_in / 32 : L.n_in / 256;
     p.row_bytes = (int64_t)nblk * (F::kind == 3 ? F::unit_bytes / 8 : F::unit_bytes);
     p.nu = (F::kind == 3) ? (nblk + 7) / 8 : nblk;
-    // Task tiling: R rows x chunks of cu units, R * cu <= 32 (one unit per
-    // lane), R * chains <= 64 (two chain lanes each). Whole rows when they fit
-    // (R = 32 / nu); longer rows are cut into balanced chunks of one row each
-    // (one contiguous bulk copy per item: several small copies per item, to
-    // fill the lanes left idle when nu does not divide 32, measured slower).
-    {
-        const int rmax_chain = F::chains > 1 ? 64 / F::chains : 64;
-        if (p.nu <= 32) {
-            p.nchunks = 1;
-            p.cu = p.nu;
-            p.rows_per_task = min(32 / p.nu, rmax_chain);
-        } else {
-            p.nchunks = (p.nu + 31) / 32;
-            p.cu = (p.nu + p.nchunks - 1) / p.nchunks;
-            p.rows_per_task = 1;
-        }
-        p.piece_stride = (int)(((int64_t)p.cu * F::unit_bytes + 15 + 15) & ~int64_t(15));
+    // rows x units-per-chunk <= 32 (one unit per lane); rows x chains <= 64.
+    // Whole rows when they fit (R = 32 / nu); longer rows stream in balanced
+    // chunks of one row each, one contiguous bulk copy per item. (Items of
+    // several rows' chunks, one bulk copy per row piece, fill the lanes left
+    // idle when nu does not divide 32, but measured slower.)
+    if (p.nu <= 32) {
+        p.nchunks = 1;
+        p.cu = p.nu;
+        p.rows_per_task = 32 / p.nu;
+        if (F::chains > 1 && p.rows_per_task > 64 / F::chains) p.rows_per_task = 64 / F::chains;
+    } else {
+        p.nchunks = (p.nu + 31) / 32;
+        p.cu = (p.nu + p.nchunks - 1) / p.nchunks;
+        p.rows_per_task = 1;
     }
     int64_t tasks = 0;
     for (int i = 0; i < L.nmat; ++i) {
@@ -324,9 +296,8 @@ static int launch_gemv_t(const GemvLaunch &L, cudaStream_t st) {
     p.task0[L.nmat] = (int)tasks;
     p.ntasks = tasks;
     if (tasks == 0) return 0;
-    const int64_t item_max = (p.nchunks == 1) ? p.rows_per_task * p.row_bytes + 32
-                                              : (int64_t)p.rows_per_task * p.piece_stride;
-    p.slot_bytes = (int)((item_max + 127) & ~int64_t(127));
+    const int64_t item_max = (p.nchunks == 1) ? p.rows_per_task * p.row_bytes : (int64_t)p.cu * F::unit_bytes;
+    p.slot_bytes = (int)((item_max + 32 + 127) & ~int64_t(127));
     p.act_bytes = (ActView::bytes(p.nu) + 127) & ~127;
     // two CTAs per SM when each warp keeps >= 2 ring slots, with 8 warps per
     // CTA or, for large slots, down to 6 (12 warps per SM still hide more

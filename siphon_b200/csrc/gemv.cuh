@@ -50,7 +50,6 @@ struct GemvParams {
     int cu;                // units per chunk
     int nchunks;           // chunks per row (1 unless R == 1)
     int rows_per_task;     // R
-    int piece_stride;      // slot bytes between row pieces (chunked rows, R > 1)
     int64_t ntasks;
     int slot_bytes;
     int nslots;            // ring slots per warp

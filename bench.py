@@ -360,6 +360,34 @@ def model_prefill(torch, s, shape, dev, stream, world, rank, group, m_tok, reps)
     return out
 
 
+def model_batch_decode(torch, s, shape, dev, stream, world, rank, group, batch, reps) -> dict:
+    """Decode tok/s of the matrix path for `batch` sequences per step (one
+    token each): every weight product once per step for all of them, through
+    sicu_gemm_prefill_f32 (the tensor-core kernel with 32-token tiles)."""
+    from siphon_b200 import model_path as mp
+    m = mp.MatrixPath(s, shape, dev, world, rank, group, seed=6, max_tokens=batch)
+    with torch.cuda.stream(stream):
+        m.prefill(stream, batch)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        for _ in range(DECODE_PER_GRAPH):
+            m.prefill(stream, batch)
+    ms = _time_graph(torch, g, stream, reps, world, dev)
+    del g
+    steps = reps * DECODE_PER_GRAPH
+    us = ms * 1e3 / steps
+    gbps = m.weight_bytes / (us * 1e-6) / 1e9
+    peak, peak_kind = peak_hbm()
+    out = {"batch": batch, "tok_s": round(batch * steps / (ms * 1e-3), 1), "us_per_step": round(us, 2),
+           "weight_bytes_per_step_per_gpu": m.weight_bytes, "GBps_per_gpu": round(gbps, 1),
+           "hbm_frac": round(gbps / peak, 4), "peak_kind": peak_kind,
+           "allreduces_per_step": 2 * shape.n_layer if world > 1 else 0}
+    del m
+    torch.cuda.empty_cache()
+    return out
+
+
 def model_cpu_baseline(budget_s: float = 8.0) -> dict | None:
     """The reference's CPU gemv over the TinyLlama-shape matrix path (host
     copies), a bounded number of tokens; larger shapes are estimated from the
@@ -413,6 +441,9 @@ def model_metrics(torch, s, dev, stream, world, rank, quick: bool) -> dict:
                                   "one NCCL all-reduce after o and after down per layer)" if world > 1 else
                                   "configs[4] Qwen2.5-32B shape, batch 1, matrix path, one GPU",
                         **model_decode(torch, s, sm.QWEN25_32B, dev, stream, world, rank, None, reps)}
+    out["tp_decode_batch8"] = {"config": "configs[4] Qwen2.5-32B shape, batch 8, matrix path, "
+                                         + (f"tensor parallel x{world}" if world > 1 else "one GPU"),
+                               **model_batch_decode(torch, s, sm.QWEN25_32B, dev, stream, world, rank, None, 8, reps)}
     if world == 1:
         out["decode"] = {"config": "configs[2] TinyLlama-1.1B shape, batch 1, matrix path",
                          **model_decode(torch, s, sm.TINYLLAMA, dev, stream, 1, 0, None, reps * 4)}

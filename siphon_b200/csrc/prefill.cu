@@ -43,16 +43,17 @@ namespace sicu {
 namespace {
 
 constexpr int PF_BM = 128;        // weight rows per tile (MMA M)
-constexpr int PF_BN = 128;        // tokens per tile (MMA N)
+constexpr int PF_BN = 128;        // tokens per tile (MMA N) for prompts
+constexpr int PF_BN_SMALL = 32;   // tokens per tile for blocks of <= 32 tokens (batched decode)
 constexpr int PF_KS = 64;         // k slots per pipeline stage: one 128-byte swizzle atom of f16
 constexpr int PF_STAGES = 6;     // K-steps in flight (even: each stage belongs to one converter group)
 constexpr int PF_NSB = 4;         // per-super-block buffers: mins / bsums tiles, scales
-constexpr int PF_STAGE_BYTES = PF_BM * PF_KS * 2;   // 16 KB; the token stage has the same size
-constexpr int PF_MIN_BYTES = PF_BM * 16 * 2;        // 4 KB: 128 rows x 16 f16 (32-byte swizzle)
+// token stage: BN rows x 64 f16 (128-byte swizzle); bsums tile: BN rows x 16 f16 (32-byte swizzle)
+__host__ __device__ constexpr int stage_bytes(int bn) { return bn * PF_KS * 2; }
+__host__ __device__ constexpr int min_bytes(int bn) { return bn * 16 * 2; }
 
 constexpr int W_TMA = 0, W_MMA = 1, W_RAW = 2, W_CONV = 3, N_CONV = 8, W_EPI = 11, N_EPI = 8;
 constexpr int PF_WARPS = 19;
-constexpr int EPI_COLS = PF_BN / 2;   // token columns per epilogue warp
 
 // Per-format geometry of the prefill kernel.
 //   KSTEPS  64-slot K-steps per super-block (weight slots = 64 * KSTEPS)
@@ -76,15 +77,15 @@ template <> struct PfFmt<T_Q6_K> {
     static constexpr bool MINS = false;
 };
 
-template <uint32_t T> struct PfLayout {
+template <uint32_t T, int BN> struct PfLayout {
     using F = PfFmt<T>;
     static constexpr int RAW_BUF = PF_BM * F::RAW_ROW;
     static constexpr int OFF_B = 0;
-    static constexpr int OFF_RAW = OFF_B + PF_STAGES * PF_STAGE_BYTES;
-    static constexpr int MINB = F::MINS ? PF_NSB * PF_MIN_BYTES : 0;
+    static constexpr int OFF_RAW = OFF_B + PF_STAGES * stage_bytes(BN);
+    static constexpr int MINB = F::MINS ? PF_NSB * min_bytes(BN) : 0;
     static constexpr int OFF_B2 = (OFF_RAW + F::NRAW * RAW_BUF + 1023) & ~1023;
     static constexpr int OFF_DA = OFF_B2 + MINB;
-    static constexpr int OFF_DW = OFF_DA + PF_NSB * PF_BN * 4;          // per-row scale f
+    static constexpr int OFF_DW = OFF_DA + PF_NSB * BN * 4;             // per-row scale f
     static constexpr int OFF_BAR = OFF_DW + PF_NSB * PF_BM * 4;
     static constexpr int OFF_FLAGS = OFF_BAR + 8 * 64;     // abort flag, TMEM address
     static constexpr int SMEM = OFF_FLAGS + 16 + 1024;     // + alignment slack
@@ -366,19 +367,20 @@ __device__ __forceinline__ bool convert_q6k(const PfCtx &cx, uint32_t base, uint
     return true;
 }
 
-template <uint32_t T>
+template <uint32_t T, int BN>
 __global__ void __launch_bounds__(PF_WARPS * 32, 1)
 prefill_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmB,
                const __grid_constant__ CUtensorMap tmS, const PfParams p) {
     using F = PfFmt<T>;
-    using Lay = PfLayout<T>;
+    using Lay = PfLayout<T, BN>;
     constexpr int KST = F::KSTEPS;
+    constexpr int EPI_COLS = BN / 2;   // token columns per epilogue warp
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const uint32_t sb0 = smem_addr(smem);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int rt = blockIdx.x / p.ntt, tt = blockIdx.x - rt * p.ntt;
-    const int row0 = rt * PF_BM, tok0 = tt * PF_BN;
+    const int row0 = rt * PF_BM, tok0 = tt * BN;
     const int rows = min(PF_BM, p.n_out - row0);
     const int nsb = p.nsb;
     volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + Lay::OFF_FLAGS);
@@ -428,18 +430,18 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
             for (int sb = 0; sb < nsb; ++sb) {
                 const int b4 = sb % PF_NSB;
                 if (!pf_wait(bar(BAR_SB_FREE + b4), ((sb / PF_NSB) & 1) ^ 1, abort_flag, p.status)) break;
-                mbar_expect_tx(bar(BAR_SBD_FULL + b4), (F::MINS ? PF_MIN_BYTES : 0) + PF_BN * 4);
+                mbar_expect_tx(bar(BAR_SBD_FULL + b4), (F::MINS ? min_bytes(BN) : 0) + BN * 4);
                 if constexpr (F::MINS)
-                    tma_load_2d(sb0 + Lay::OFF_B2 + b4 * PF_MIN_BYTES, &tmS, 16 * sb, tok0, bar(BAR_SBD_FULL + b4));
-                bulk_g2s(sb0 + Lay::OFF_DA + b4 * PF_BN * 4, p.da + (size_t)sb * p.m_pad + tok0, PF_BN * 4,
+                    tma_load_2d(sb0 + Lay::OFF_B2 + b4 * min_bytes(BN), &tmS, 16 * sb, tok0, bar(BAR_SBD_FULL + b4));
+                bulk_g2s(sb0 + Lay::OFF_DA + b4 * BN * 4, p.da + (size_t)sb * p.m_pad + tok0, BN * 4,
                          bar(BAR_SBD_FULL + b4));
                 sb_issued = sb + 1;
                 bool ok = true;
                 for (int c = 0; c < KST; ++c) {
                     const int t = KST * sb + c, s = stage_of(t);
                     if (!pf_wait(bar(BAR_ST_EMPTY + s), use_of(t) ^ 1, abort_flag, p.status)) { ok = false; break; }
-                    mbar_expect_tx(bar(BAR_B_FULL + s), PF_STAGE_BYTES);
-                    tma_load_2d(sb0 + Lay::OFF_B + s * PF_STAGE_BYTES, &tmB, PF_KS * t, tok0, bar(BAR_B_FULL + s));
+                    mbar_expect_tx(bar(BAR_B_FULL + s), stage_bytes(BN));
+                    tma_load_2d(sb0 + Lay::OFF_B + s * stage_bytes(BN), &tmB, PF_KS * t, tok0, bar(BAR_B_FULL + s));
                     t_issued = t + 1;
                 }
                 if (!ok) break;
@@ -453,7 +455,7 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
     } else if (warp == W_MMA) {
         // ---- MMA issue ----
         if (lane == 0) {
-            constexpr uint32_t idesc = idesc_f16_f32(PF_BM, PF_BN);
+            constexpr uint32_t idesc = idesc_f16_f32(PF_BM, BN);
             for (int sb = 0; sb < nsb; ++sb) {
                 const int buf = sb & 1;
                 const uint32_t ph = (sb >> 1) & 1;
@@ -467,7 +469,7 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
                     if (!pf_wait<true>(bar(BAR_A_FULL + s), sph, abort_flag, p.status) ||
                         !pf_wait<true>(bar(BAR_B_FULL + s), sph, abort_flag, p.status)) { ok = false; break; }
                     tc_fence_after();
-                    const uint32_t b = sb0 + Lay::OFF_B + s * PF_STAGE_BYTES;
+                    const uint32_t b = sb0 + Lay::OFF_B + s * stage_bytes(BN);
 #pragma unroll
                     for (int kk = 0; kk < PF_KS / 16; ++kk)
                         tc_mma_f16_ts(dacc, tmem + TM_A + 32u * s + 8u * kk, smem_desc(b + 32 * kk, 1024, SMEM_SWZ_128B),
@@ -482,7 +484,7 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
                     if (!pf_wait<true>(bar(BAR_A2_FULL + b4), ph4, abort_flag, p.status) ||
                         !pf_wait<true>(bar(BAR_SBD_FULL + b4), ph4, abort_flag, p.status)) break;
                     tc_fence_after();
-                    const uint64_t bd = smem_desc(sb0 + Lay::OFF_B2 + b4 * PF_MIN_BYTES, 256, SMEM_SWZ_32B);
+                    const uint64_t bd = smem_desc(sb0 + Lay::OFF_B2 + b4 * min_bytes(BN), 256, SMEM_SWZ_32B);
                     tc_mma_f16_ts(dacc, tmem + TM_MIN + 16u * b4, bd, idesc, 1);
                     tc_mma_f16_ts(dacc, tmem + TM_MIN + 16u * b4 + 8u, bd, idesc, 1);
                 }
@@ -548,7 +550,7 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
             }
             tc_fence_after();
             const float fr = reinterpret_cast<const float *>(smem + Lay::OFF_DW)[b4 * PF_BM + r];
-            const float4 *da4 = reinterpret_cast<const float4 *>(smem + Lay::OFF_DA + b4 * PF_BN * 4 + c0 * 4);
+            const float4 *da4 = reinterpret_cast<const float4 *>(smem + Lay::OFF_DA + b4 * BN * 4 + c0 * 4);
             const uint32_t ta = tmem + ((uint32_t)(32 * q) << 16) + TM_ACC + (uint32_t)buf * 128u + (uint32_t)c0;
 #pragma unroll
             for (int cc = 0; cc < EPI_COLS / 8; ++cc) {
@@ -681,12 +683,12 @@ WsParts ws_parts(uint32_t wtype, int64_t n_in, int64_t n_out, int64_t m) {
     return w;
 }
 
-template <uint32_t T>
-int launch_t(const PrefillLaunch &L, cudaStream_t st) {
+template <uint32_t T, int BN>
+int launch_tb(const PrefillLaunch &L, cudaStream_t st) {
     using F = PfFmt<T>;
-    using Lay = PfLayout<T>;
+    using Lay = PfLayout<T, BN>;
     const int64_t K = L.n_in, nsb = K / QK_K;
-    const int64_t m_pad = (L.m + PF_BN - 1) / PF_BN * PF_BN;
+    const int64_t m_pad = (L.m + BN - 1) / BN * BN;
     const WsParts parts = ws_parts(T, L.n_in, L.n_out, L.m);
     uint8_t *ws = static_cast<uint8_t *>(L.ws);
     uint16_t *B = reinterpret_cast<uint16_t *>(ws);
@@ -710,10 +712,10 @@ int launch_t(const PrefillLaunch &L, cudaStream_t st) {
     if (!make_map(&tmW, w, (uint64_t)row_bytes, (uint64_t)L.n_out, (uint64_t)pitch, F::RAW_ROW, PF_BM,
                   CU_TENSOR_MAP_SWIZZLE_NONE, 1) ||
         !make_map(&tmB, B, (uint64_t)(K * F::KSTEPS / 4), (uint64_t)m_pad, (uint64_t)(K * F::KSTEPS / 4) * 2, PF_KS,
-                  PF_BN, CU_TENSOR_MAP_SWIZZLE_128B, 2))
+                  BN, CU_TENSOR_MAP_SWIZZLE_128B, 2))
         return -4;
     if (F::MINS) {
-        if (!make_map(&tmS, S, (uint64_t)(K / 16), (uint64_t)m_pad, (uint64_t)(K / 16) * 2, 16, PF_BN,
+        if (!make_map(&tmS, S, (uint64_t)(K / 16), (uint64_t)m_pad, (uint64_t)(K / 16) * 2, 16, BN,
                       CU_TENSOR_MAP_SWIZZLE_32B, 2))
             return -4;
     } else {
@@ -722,8 +724,8 @@ int launch_t(const PrefillLaunch &L, cudaStream_t st) {
     static bool attr_set[64] = {};
     const int dev = L.device & 63;
     if (!attr_set[dev]) {
-        cudaFuncSetAttribute(prefill_kernel<T>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
-        if (cudaFuncSetAttribute(prefill_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, Lay::SMEM) !=
+        cudaFuncSetAttribute(prefill_kernel<T, BN>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+        if (cudaFuncSetAttribute(prefill_kernel<T, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, Lay::SMEM) !=
             cudaSuccess)
             return -2;
         attr_set[dev] = true;
@@ -735,12 +737,19 @@ int launch_t(const PrefillLaunch &L, cudaStream_t st) {
     p.y = L.y;
     p.m = (int)L.m;
     p.m_pad = (int)m_pad;
-    p.ntt = (int)(m_pad / PF_BN);
+    p.ntt = (int)(m_pad / BN);
     p.status = L.status;
     const int64_t tiles = (L.n_out + PF_BM - 1) / PF_BM * p.ntt;
-    prefill_kernel<T><<<(unsigned)tiles, PF_WARPS * 32, Lay::SMEM, st>>>(tmW, tmB, tmS, p);
+    prefill_kernel<T, BN><<<(unsigned)tiles, PF_WARPS * 32, Lay::SMEM, st>>>(tmW, tmB, tmS, p);
     if (cudaGetLastError() != cudaSuccess) return -2;
     return 0;
+}
+
+// blocks of up to 32 tokens (batched decode) use 32-token tiles: the weights
+// still stream once per token tile, with a quarter of the token-operand traffic
+template <uint32_t T>
+int launch_t(const PrefillLaunch &L, cudaStream_t st) {
+    return L.m <= PF_BN_SMALL ? launch_tb<T, PF_BN_SMALL>(L, st) : launch_tb<T, PF_BN>(L, st);
 }
 
 }  // namespace

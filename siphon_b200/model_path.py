@@ -182,7 +182,9 @@ class MatrixPath:
         return n + 1
 
     def prefill(self, stream, m: int) -> None:
-        """Launch the products of an m-token prompt on `stream`."""
+        """Launch the products of an m-token prompt on `stream` (or, with m
+        up to the batch size, one decode step of a batch of m sequences:
+        the same products, every weight matrix streamed once for all m)."""
         s, h, y = self.s, stream.cuda_stream, self.y
         d = self.sh.n_embd
         nq, nkv, nff = self.shapes["q"][0], self.shapes["k"][0], self.shapes["gate"][0]

@@ -89,6 +89,20 @@ def test_prefill_q6k_vs_reference(sicu, oracle, n_out, n_in, m):
     assert np.isfinite(got).all()
 
 
+@pytest.mark.parametrize("wt", [Q.Q4_K, Q.Q6_K])
+@pytest.mark.parametrize("n_out,n_in,m", [
+    (128, 512, 1),       # one token: a 32-token tile with 31 padding tokens
+    (200, 1024, 8),      # a batched-decode block
+    (256, 2048, 32),     # a full 32-token tile
+    (130, 1280, 20),     # ragged rows; Q6_K rows padded to 16 bytes
+])
+def test_prefill_small_token_blocks(sicu, oracle, wt, n_out, n_in, m):
+    """Blocks of <= 32 tokens take the 32-token tile variant of the kernel."""
+    w, x, xq, want, got = _run(sicu, oracle, wt, n_out, n_in, m, seed=n_out + m)
+    l1 = np.abs(_dequant_q8k(xq, n_in)) @ np.abs(_dequant_w(oracle, wt, w, n_in, n_out)).T
+    _check_tol(got, want, l1, f"{Q.NAMES[wt]} prefill {n_out}x{n_in} m={m}")
+
+
 def test_prefill_q4k_exact_value(sicu, oracle):
     """Against the exact value of the product (float64 over the dequantized
     operands) at a larger size, where the scalar oracle would be slow."""

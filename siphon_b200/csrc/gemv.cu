@@ -2,6 +2,7 @@
 #include <map>
 #include <mutex>
 
+#include "allreduce.cuh"
 #include "gemv.cuh"
 #include "quantize.cuh"
 #include "launch.h"
@@ -99,7 +100,9 @@ __device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol
 // in one warp) and a private ring of nslots shared-memory slots. Lane 0 keeps
 // the ring full with bulk copies; a slot's geometry is published next to it,
 // so the consuming side does no address arithmetic of its own.
-template <uint32_t T>
+// AR: the launch consumes from and/or delivers to a fused all-reduce group
+// (a separate instantiation, so the plain matvec carries none of it).
+template <uint32_t T, bool AR>
 __global__ void __launch_bounds__(GEMV_WARPS * 32, 2) gemv_kernel(const GemvParams p) {
     using F = Fmt<T>;
     constexpr int CH = F::chains;
@@ -149,8 +152,30 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 2) gemv_kernel(const GemvPara
     // each CTA of the cluster builds 1/nrank of the records for every member
     grid_dep_wait();
     const uint32_t rank = cluster_rank(), nrank = cluster_size();
-    if (p.xf) quantize_into_act<F::act>(av, p.xf, p.n_in, rank, nrank);
-    else prep_activation<F::act>(av, p.xq, p.n_in, rank, nrank);
+    // fused all-reduce: wait for the group's partials (consumption) and read
+    // the delivery count (delivery) while the weights keep streaming. The
+    // state lives in the 16 bytes after the activation records and is re-read
+    // where used (the loop below is at the launch bound's register limit):
+    // [0] consumed count, [1] delivery count, [2] delivery allowed.
+    volatile unsigned *const ar_st = reinterpret_cast<volatile unsigned *>(smem + ActView::bytes(p.nu));
+    if constexpr (AR) {
+        if (threadIdx.x == 0) {
+            if (p.ar_in.n) ar_st[0] = ar_consume_wait(p.ar_in, p.status);
+            unsigned e = 0;
+            ar_st[2] = (p.ar_out.n && ar_deliver_begin(p.ar_out, p.status, e)) ? 1u : 0u;
+            ar_st[1] = e;
+        }
+        __syncthreads();
+    }
+    if (AR && p.ar_in.n) {
+        const ArDev &a = p.ar_in;
+        const float *part = a.slot[a.rank] + (int64_t)((ar_st[0] - 1u) & 1u) * a.n * a.len;
+        quantize_into_act<F::act, true>(av, part, p.n_in, rank, nrank, a.n, a.len);
+    } else if (p.xf) {
+        quantize_into_act<F::act, false>(av, p.xf, p.n_in, rank, nrank, 1, 0);
+    } else {
+        prep_activation<F::act>(av, p.xq, p.n_in, rank, nrank);
+    }
     cluster_sync();
 
     const int r_l = p.nchunks == 1 ? lane / p.cu : 0;
@@ -247,10 +272,22 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 2) gemv_kernel(const GemvPara
                     r = fin[lane];
                 }
                 p.y[mat][g.x + lane] = r;
+                if (AR && ar_st[2]) {
+                    const unsigned eo = ar_st[1];
+#pragma unroll
+                    for (int q = 0; q < AR_MAX; ++q)
+                        if (q < p.ar_out.n) ar_dst(p.ar_out, q, eo)[g.x + lane] = r;
+                }
             }
         }
         __syncwarp();
         if (++s == S) { s = 0; parity ^= 1u; }
+    }
+    if (AR && ar_st[2]) {
+        // every thread's peer stores are ordered before the CTA's arrival
+        __threadfence_system();
+        __syncthreads();
+        if (threadIdx.x == 0) ar_deliver_arrive(p.ar_out, ar_st[1]);
     }
 }
 
@@ -267,6 +304,8 @@ static int launch_gemv_t(const GemvLaunch &L, cudaStream_t st) {
     p.xf = L.xf;
     p.n_in = L.n_in;
     p.status = L.status;
+    p.ar_in = L.ar_in;
+    p.ar_out = L.ar_out;
     const int nblk = (F::kind == 3) ? L.n_in / 32 : L.n_in / 256;
     p.row_bytes = (int64_t)nblk * (F::kind == 3 ? F::unit_bytes / 8 : F::unit_bytes);
     p.nu = (F::kind == 3) ? (nblk + 7) / 8 : nblk;
@@ -298,7 +337,8 @@ static int launch_gemv_t(const GemvLaunch &L, cudaStream_t st) {
     if (tasks == 0) return 0;
     const int64_t item_max = (p.nchunks == 1) ? p.rows_per_task * p.row_bytes : (int64_t)p.cu * F::unit_bytes;
     p.slot_bytes = (int)((item_max + 32 + 127) & ~int64_t(127));
-    p.act_bytes = (ActView::bytes(p.nu) + 127) & ~127;
+    const bool ar = L.ar_in.n > 0 || L.ar_out.n > 0;
+    p.act_bytes = (ActView::bytes(p.nu) + (ar ? 16 : 0) + 127) & ~127;
     // two CTAs per SM when each warp keeps >= 2 ring slots, with 8 warps per
     // CTA or, for large slots, down to 6 (12 warps per SM still hide more
     // latency than one CTA of 8); else one CTA of 8 warps with up to 4 slots
@@ -319,16 +359,17 @@ static int launch_gemv_t(const GemvLaunch &L, cudaStream_t st) {
     p.nslots = slots;
     p.warp_bytes = (hdr + slots * p.slot_bytes + 127) & ~127;
     const int smem = p.act_bytes + warps * p.warp_bytes;
-    static bool attr_set[64] = {};
+    const auto kern = ar ? gemv_kernel<T, true> : gemv_kernel<T, false>;
+    static bool attr_set[64][2] = {};
     const int dev = L.device & 63;
-    if (!attr_set[dev]) {
-        if (cudaFuncSetAttribute(gemv_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, L.smem_limit) != cudaSuccess)
+    if (!attr_set[dev][ar]) {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L.smem_limit) != cudaSuccess)
             return -2;
         // every kernel of the library asks for the same (largest) shared-memory
         // carveout, so consecutive launches of different kernels never wait
         // for an SM to reconfigure its L1 / shared-memory split
-        cudaFuncSetAttribute(gemv_kernel<T>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
-        attr_set[dev] = true;
+        cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+        attr_set[dev][ar] = true;
     }
     // thread-block cluster size: 2 when pairs still keep (almost) every CTA
     // slot of the launch co-resident, else 1
@@ -336,9 +377,9 @@ static int launch_gemv_t(const GemvLaunch &L, cudaStream_t st) {
     int csize = 1, capacity = target;
     {
         static std::mutex mu;
-        static std::map<std::pair<int, int>, std::pair<int, int>> cache;   // (device, smem x warps) -> (C, capacity)
+        static std::map<std::pair<int, int>, std::pair<int, int>> cache;   // (device x variant, smem x warps) -> (C, capacity)
         std::lock_guard<std::mutex> lk(mu);
-        const auto key = std::make_pair(dev, smem * 16 + warps);
+        const auto key = std::make_pair(dev * 2 + (ar ? 1 : 0), smem * 16 + warps);
         auto hit = cache.find(key);
         if (hit == cache.end()) {
             int best_c = 1, best_cap = target;
@@ -359,7 +400,7 @@ static int launch_gemv_t(const GemvLaunch &L, cudaStream_t st) {
                 q.attrs = ca;
                 q.numAttrs = 1;
                 int n = 0;
-                if (cudaOccupancyMaxActiveClusters(&n, gemv_kernel<T>, &q) != cudaSuccess) {
+                if (cudaOccupancyMaxActiveClusters(&n, kern, &q) != cudaSuccess) {
                     cudaGetLastError();
                     continue;
                 }
@@ -393,7 +434,7 @@ static int launch_gemv_t(const GemvLaunch &L, cudaStream_t st) {
     attr[1].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 2;
-    if (cudaLaunchKernelEx(&cfg, gemv_kernel<T>, p) != cudaSuccess) return -2;
+    if (cudaLaunchKernelEx(&cfg, kern, p) != cudaSuccess) return -2;
     return 0;
 }
 

@@ -23,6 +23,7 @@
 #pragma once
 
 #include "common.cuh"
+#include "launch.h"
 
 namespace sicu {
 
@@ -56,6 +57,8 @@ struct GemvParams {
     int act_bytes;         // prepared-activation region
     int warp_bytes;        // per-warp region: barriers, slot geometry, terms, ring
     int *status;
+    ArDev ar_in;           // n > 0: the activation is the group's reduced partials (xf, xq unused)
+    ArDev ar_out;          // n > 0: the outputs are also delivered to the group (one matrix)
 };
 
 // ---------------------------------------------------------------------------

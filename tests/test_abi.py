@@ -83,3 +83,30 @@ def test_last_error_is_per_thread(so):
     t.join()
     assert "unsupported" in so.last_error()
     assert msgs["t"] == ""
+
+
+def test_allreduce_group_checks_run_on_host(so):
+    h = C.c_void_p()
+    buf = C.create_string_buffer(L.AR_HANDLE_BYTES)
+    assert so.lib.sicu_ar_create(0, 0, 256, C.byref(h), buf) == L.SICU_EINVAL      # no ranks
+    assert so.lib.sicu_ar_create(9, 0, 256, C.byref(h), buf) == L.SICU_EINVAL      # more than 8
+    assert so.lib.sicu_ar_create(2, 2, 256, C.byref(h), buf) == L.SICU_EINVAL      # rank out of range
+    assert so.lib.sicu_ar_create(2, 0, 300, C.byref(h), buf) == L.SICU_EINVAL      # not whole super-blocks
+    assert so.lib.sicu_ar_create(2, 0, 256, None, buf) == L.SICU_EINVAL
+    # well-formed, but no device initialised: refused without a CUDA call
+    assert so.lib.sicu_ar_create(2, 0, 256, C.byref(h), buf) == L.SICU_EINVAL
+    assert "sicu_init" in so.last_error()
+    assert h.value is None
+    assert so.lib.sicu_ar_open(None, buf) == L.SICU_EINVAL
+    assert so.lib.sicu_ar_deliver(None, 16, None) == L.SICU_EINVAL
+    assert so.lib.sicu_ar_reduce(None, 16, None) == L.SICU_EINVAL
+    assert so.lib.sicu_ar_set_timeout(None, 1000) == L.SICU_EINVAL
+    assert so.lib.sicu_ar_destroy(None) == L.SICU_OK
+    # the fused matvec: an activation and a group to consume are exclusive,
+    # F16 has no fused form
+    w = (C.c_void_p * 1)(4096)
+    y = (C.c_void_p * 1)(8192)
+    n = (C.c_int64 * 1)(256)
+    assert so.lib.sicu_gemv_ar(Q.Q4_K, 1, w, n, 256, None, None, y, None, None) == L.SICU_EINVAL
+    assert so.lib.sicu_gemv_ar(Q.F16, 1, w, n, 256, 16, None, y, None, None) == L.SICU_ENOTSUP
+    assert so.lib.sicu_gemv_ar(Q.Q4_K, 0, w, n, 256, 16, None, y, None, None) == L.SICU_EINVAL

@@ -299,11 +299,12 @@ def _time_graph(torch, g, stream, reps, world, dev) -> float:
     return max_over_ranks(e0.elapsed_time(e1), world, dev)
 
 
-def model_decode(torch, s, shape, dev, stream, world, rank, group, reps) -> dict:
+def model_decode(torch, s, shape, dev, stream, world, rank, group, reps, fused=False) -> dict:
     """Decode tok/s of the matrix path of `shape` (batch 1), tensor parallel
-    over the world: every weight matrix of one token per step."""
+    over the world: every weight matrix of one token per step. fused: the
+    all-reduces ride in the matvecs (sicu_gemv_ar), else NCCL all-reduces."""
     from siphon_b200 import model_path as mp
-    m = mp.MatrixPath(s, shape, dev, world, rank, group, seed=4)
+    m = mp.MatrixPath(s, shape, dev, world, rank, group, seed=4, fused=fused)
     with torch.cuda.stream(stream):
         for _ in range(2):
             launches = m.decode_step(stream)
@@ -322,6 +323,10 @@ def model_decode(torch, s, shape, dev, stream, world, rank, group, reps) -> dict
            "weight_bytes_per_token_per_gpu": m.weight_bytes, "GBps_per_gpu": round(gbps, 1),
            "hbm_frac": round(gbps / peak, 4), "peak_kind": peak_kind,
            "kernel_launches_per_token": launches, "allreduces_per_token": 2 * shape.n_layer if world > 1 else 0}
+    if world > 1:
+        out["allreduce"] = "fused into the matvecs (NVLink peer stores, sicu_gemv_ar)" if fused else "NCCL"
+    assert s.status() == 0, "a matvec or all-reduce wait gave up"
+    m.close()
     del m
     torch.cuda.empty_cache()
     return out
@@ -438,9 +443,13 @@ def model_metrics(torch, s, dev, stream, world, rank, quick: bool) -> dict:
     reps = 3 if quick else 10
     out["tp_decode"] = {"config": "configs[4] Qwen2.5-32B shape, batch 1, matrix path, "
                                   f"tensor parallel x{world} (column-split QKV/gate/up/head, row-split o/down, "
-                                  "one NCCL all-reduce after o and after down per layer)" if world > 1 else
-                                  "configs[4] Qwen2.5-32B shape, batch 1, matrix path, one GPU",
-                        **model_decode(torch, s, sm.QWEN25_32B, dev, stream, world, rank, None, reps)}
+                                  "an all-reduce after o and after down per layer, fused into the matvecs)"
+                                  if world > 1 else "configs[4] Qwen2.5-32B shape, batch 1, matrix path, one GPU",
+                        **model_decode(torch, s, sm.QWEN25_32B, dev, stream, world, rank, None, reps,
+                                       fused=world > 1)}
+    if world > 1:
+        out["tp_decode_nccl"] = {"config": "as tp_decode, the all-reduces as NCCL calls between the matvecs",
+                                 **model_decode(torch, s, sm.QWEN25_32B, dev, stream, world, rank, None, reps)}
     out["tp_decode_batch8"] = {"config": "configs[4] Qwen2.5-32B shape, batch 8, matrix path, "
                                          + (f"tensor parallel x{world}" if world > 1 else "one GPU"),
                                **model_batch_decode(torch, s, sm.QWEN25_32B, dev, stream, world, rank, None, 8, reps)}

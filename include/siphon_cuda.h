@@ -71,12 +71,11 @@ SICU_API int sicu_shutdown(void);
 SICU_API int sicu_last_error(char *buf, size_t len);
 /* Read and clear the device status word of the current device: bit 0 set
  * means a kernel's bounded wait on its own copies gave up (outputs of that
- * launch are invalid); SICU_STATUS_AR_TIMEOUT and SICU_STATUS_AR_ORDER report
- * a failed all-reduce group (below). Synchronises the device. */
+ * launch are invalid); SICU_STATUS_AR_TIMEOUT reports a failed all-reduce
+ * group (below). Synchronises the device. */
 SICU_API int sicu_status(int *flags);
 #define SICU_STATUS_WAIT_TIMEOUT 1
 #define SICU_STATUS_AR_TIMEOUT   2
-#define SICU_STATUS_AR_ORDER     4
 
 /* Programmatic dependent launch for the matvec kernels (default off). When
  * on, a matvec may start streaming its weight blocks while earlier work in
@@ -194,36 +193,32 @@ SICU_API int sicu_gemm_prefill(uint32_t wtype, const void *dw, int64_t n_in, int
 SICU_API int sicu_gemm_prefill_f32(uint32_t wtype, const void *dw, int64_t n_in, int64_t n_out,
                                    const float *dx, int64_t m, float *dy, void *stream);
 
-/* ---- tensor-parallel all-reduce fused into the matvecs ----------------------
- * Row-split products (Wo, W_down) of a tensor-parallel decode step leave a
- * partial output vector on every rank that must be summed before the next
- * product reads it. The reference runs one process on one CPU and has no such
- * step; its forward pass (src/engine.c:368-378) applies Wo and W_down to the
- * whole activation. A group replaces an NCCL all-reduce between the two
- * matvecs with plain NVLink peer stores made by the matvecs themselves:
- *
- *   - a DELIVERING matvec (sicu_gemv_ar with `deliver`) stores each output
- *     row into every rank's partial buffer as it finishes it, and its last
- *     CTA raises the rank's delivery flag on every rank;
- *   - a CONSUMING matvec (sicu_gemv_ar with `consume`) streams its weights
- *     while it waits (bounded) for every rank's flag, then takes as its
- *     activation the sum of the n partials, added in rank order in f32
- *     (((p0 + p1) + p2) + ...), quantized as sicu_gemv_f32 would.
+/* ---- tensor-parallel all-reduce fused into the matvec ------------------------
+ * A row-split product (Wo, W_down split by input columns across a
+ * tensor-parallel group) leaves a partial output vector on every rank that
+ * must be summed before the next product reads it. The reference runs one
+ * process on one CPU and has no such step: its forward pass applies Wo and
+ * W_down to the whole activation (src/engine.c:368, 378). sicu_gemv_ar runs
+ * the row-split matvec and the all-reduce as one kernel: each CTA sends the
+ * partial outputs of the rows it computed to every rank with plain NVLink
+ * peer stores (each element a 64-bit word carrying its delivery tag), then
+ * waits (bounded) for the other ranks' parts of the same rows and writes
+ * their sum, added in rank order in f32 (((p0 + p1) + p2) + ...), so every
+ * rank ends with bit-identical outputs. No collective launch, fence or flag
+ * is involved; the next matvec reads dy as a plain activation.
  *
  * A group has n_ranks (1..8) members, one process per GPU, and vectors of
  * len floats (a multiple of 256, <= 2^24). Setup, in every rank:
  *   sicu_ar_create(n, rank, len, &g, handle)  -> this rank's 64-byte handle
  *   exchange the handles (any host channel; all ranks get all n, rank order)
  *   sicu_ar_open(g, handles)                  -> maps the peers' buffers
- * Use: on every rank, deliveries and consumptions alternate (each delivery is
- * consumed at least once before the rank's next delivery), in the same order
- * on every rank; the counters live on the device, so a captured CUDA graph
- * can replay the sequence. A consumption waits at most the group's timeout
- * (default 2 s, sicu_ar_set_timeout), then sets SICU_STATUS_AR_TIMEOUT and
- * marks the group broken: every later step of the group returns at once with
- * the same bit, and its outputs are invalid. Misuse of the order sets
- * SICU_STATUS_AR_ORDER and breaks the group too. A broken group is
- * destroyed and created again. Teardown: every rank synchronises its streams
+ * Every rank issues the group's operations (sicu_gemv_ar, sicu_ar_allreduce)
+ * on one stream, in the same order. The delivery counter lives on the device,
+ * so a captured CUDA graph replays the sequence. A wait gives up after the
+ * group's timeout (default 2 s, sicu_ar_set_timeout), sets
+ * SICU_STATUS_AR_TIMEOUT and marks the group broken: every later operation
+ * returns at once with the same bit and outputs the local partial; destroy
+ * and create the group again. Teardown: every rank synchronises its streams
  * and meets the others (a host barrier) before sicu_ar_destroy. */
 #define SICU_AR_HANDLE_BYTES 64
 typedef struct sicu_ar sicu_ar;
@@ -232,17 +227,14 @@ SICU_API int sicu_ar_create(int n_ranks, int rank, int64_t len, sicu_ar **group,
 SICU_API int sicu_ar_open(sicu_ar *group, const void *handles);
 SICU_API int sicu_ar_set_timeout(sicu_ar *group, uint64_t ns);
 SICU_API int sicu_ar_destroy(sicu_ar *group);
-/* Standalone steps: deliver dsrc[len] / consume the sum into ddst[len]
- * (device, 16-byte aligned); for vectors that no matvec produces or reads. */
-SICU_API int sicu_ar_deliver(sicu_ar *group, const float *dsrc, void *stream);
-SICU_API int sicu_ar_reduce(sicu_ar *group, float *ddst, void *stream);
-/* sicu_gemv_multi with the group steps fused in. consume != NULL: the
- * activation is the consumed sum (n_in == the group's len; dx must be NULL).
- * deliver != NULL: one matrix (n_mats == 1, n_out[0] == the group's len); its
- * output goes to dy[0] and to the group. Quantized weight types only. */
-SICU_API int sicu_gemv_ar(uint32_t wtype, int n_mats, const void *const *dw, const int64_t *n_out,
-                          int64_t n_in, const float *dx, sicu_ar *consume, float *const *dy,
-                          sicu_ar *deliver, void *stream);
+/* ddst[i] = sum over ranks of their dsrc[i] (len floats, device; in place
+ * allowed), same protocol, for partial sums the library did not produce. */
+SICU_API int sicu_ar_allreduce(sicu_ar *group, const float *dsrc, float *ddst, void *stream);
+/* dy = sum over the group's ranks of (W_rank x_rank): sicu_gemv_f32 of this
+ * rank's column shard (n_out == the group's len) with the all-reduce fused
+ * in. Quantized weight types only. */
+SICU_API int sicu_gemv_ar(uint32_t wtype, const void *dw, int64_t n_in, int64_t n_out,
+                          const float *dx, float *dy, sicu_ar *group, void *stream);
 
 /* ---- dequantisation --------------------------------------------------------
  * Rows rows[0..nrows) (host array) of W into dout[nrows][n_in] f32, reference

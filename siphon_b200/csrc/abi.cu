@@ -614,8 +614,7 @@ int sicu_ar_open(sicu_ar *g, const void *handles) {
             }
             g->peer[q] = base;
         }
-        g->d.slot[q] = static_cast<float *>(base);
-        g->d.flag[q] = reinterpret_cast<unsigned *>(static_cast<uint8_t *>(base) + ar_flag_offset(g->d.n, g->d.len));
+        g->d.slot[q] = static_cast<uint64_t *>(base);
     }
     g->opened = true;
     return SICU_OK;
@@ -642,63 +641,29 @@ int sicu_ar_destroy(sicu_ar *g) {
     return SICU_OK;
 }
 
-int sicu_ar_deliver(sicu_ar *g, const float *dsrc, void *stream) {
+int sicu_ar_allreduce(sicu_ar *g, const float *dsrc, float *ddst, void *stream) {
     DevState *ds;
     if (int rc = ar_current(g, ds)) return rc;
-    if (!dsrc || !aligned(dsrc, 16)) return fail(SICU_EINVAL, "all-reduce: source must be non-null and 16-byte aligned");
-    if (launch_ar_deliver(g->d, dsrc, ds->status, ds->sms, (cudaStream_t)stream))
-        return cuda_fail(cudaGetLastError(), "all-reduce deliver launch");
+    if (!dsrc || !ddst) return fail(SICU_EINVAL, "all-reduce: null vector");
+    if (launch_allreduce(g->d, dsrc, ddst, ds->status, ds->sms, (cudaStream_t)stream))
+        return cuda_fail(cudaGetLastError(), "all-reduce launch");
     return SICU_OK;
 }
 
-int sicu_ar_reduce(sicu_ar *g, float *ddst, void *stream) {
-    DevState *ds;
-    if (int rc = ar_current(g, ds)) return rc;
-    if (!ddst || !aligned(ddst, 16)) return fail(SICU_EINVAL, "all-reduce: destination must be non-null and 16-byte aligned");
-    if (launch_ar_reduce(g->d, ddst, ds->status, ds->sms, (cudaStream_t)stream))
-        return cuda_fail(cudaGetLastError(), "all-reduce reduce launch");
-    return SICU_OK;
-}
-
-int sicu_gemv_ar(uint32_t wtype, int n_mats, const void *const *dw, const int64_t *n_out, int64_t n_in,
-                 const float *dx, sicu_ar *consume, float *const *dy, sicu_ar *deliver, void *stream) {
-    if (n_mats < 1 || n_mats > MAX_MATS) return fail(SICU_EINVAL, "matvec ar: %d matrices (1..%d)", n_mats, MAX_MATS);
-    if (!dw || !n_out || !dy) return fail(SICU_EINVAL, "matvec ar: null array");
+int sicu_gemv_ar(uint32_t wtype, const void *dw, int64_t n_in, int64_t n_out, const float *dx, float *dy,
+                 sicu_ar *g, void *stream) {
     if (wtype == T_F16) return fail(SICU_ENOTSUP, "matvec ar: F16 weights are not supported");
-    if (consume ? dx != nullptr : dx == nullptr)
-        return fail(SICU_EINVAL, "matvec ar: give either an activation or a group to consume, not both");
     uint32_t pair;
-    // the activation operand for the checks: the group stands in for x
-    const void *act = consume ? static_cast<const void *>(consume) : dx;
-    for (int i = 0; i < n_mats; ++i) {
-        if (int rc = check_matvec(wtype, dw[i], n_in, n_out[i], act, dy[i], 1, pair)) return rc;
-        // every matrix has rows: a launch must run for the group steps to happen
-        if (n_out[i] < 1 || n_out[i] > ((int64_t)1 << 30)) return fail(SICU_EINVAL, "matvec ar: %lld rows", (long long)n_out[i]);
-    }
-    if (dx && !aligned(dx, 16)) return fail(SICU_EINVAL, "matvec: f32 activation must be 16-byte aligned");
+    if (int rc = check_matvec(wtype, dw, n_in, n_out, dx, dy, 1, pair)) return rc;
+    if (!aligned(dx, 16)) return fail(SICU_EINVAL, "matvec: f32 activation must be 16-byte aligned");
     DevState *ds;
-    if (consume) {
-        if (int rc = ar_current(consume, ds)) return rc;
-        if (consume->d.len != n_in)
-            return fail(SICU_EINVAL, "matvec ar: consumed length %lld != n_in %lld", (long long)consume->d.len, (long long)n_in);
-    }
-    if (deliver) {
-        if (int rc = ar_current(deliver, ds)) return rc;
-        if (n_mats != 1 || n_out[0] != deliver->d.len)
-            return fail(SICU_EINVAL, "matvec ar: a delivering launch has one matrix of the group's length %lld rows",
-                        (long long)deliver->d.len);
-    }
-    if (int rc = current(ds)) return rc;
-    GemvLaunch L = make_launch(*ds, dw[0], n_in, n_out[0], dy[0]);
+    if (int rc = ar_current(g, ds)) return rc;
+    if (n_out != g->d.len)
+        return fail(SICU_EINVAL, "matvec ar: %lld rows, the group reduces vectors of %lld", (long long)n_out,
+                    (long long)g->d.len);
+    GemvLaunch L = make_launch(*ds, dw, n_in, n_out, dy);
     L.xf = dx;
-    L.nmat = n_mats;
-    for (int i = 0; i < n_mats; ++i) {
-        L.wm[i] = dw[i];
-        L.ym[i] = dy[i];
-        L.n_outm[i] = n_out[i];
-    }
-    if (consume) L.ar_in = consume->d;
-    if (deliver) L.ar_out = deliver->d;
+    L.ar = g->d;
     return run_gemv(wtype, L, (cudaStream_t)stream);
 }
 

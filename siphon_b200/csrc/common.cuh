@@ -22,12 +22,9 @@ constexpr int B_Q4_K = 144, B_Q5_K = 176, B_Q6_K = 210, B_Q8_K = 292;
 
 // device status word: set by a kernel whose bounded wait gave up
 constexpr int STATUS_WAIT_TIMEOUT = 1;
-// a fused all-reduce consumption gave up waiting for a peer's delivery, or
-// its group was already broken by an earlier failure
+// an all-reduce gave up waiting for a peer's part, or its group was already
+// broken by an earlier failure
 constexpr int STATUS_AR_TIMEOUT = 2;
-// a fused all-reduce group was used out of order (a delivery before the
-// previous one was consumed, or a consumption before any delivery)
-constexpr int STATUS_AR_ORDER = 4;
 
 // ---- f16 ---------------------------------------------------------------------
 // f16 -> f32 is exact in hardware for every finite half and inf.

@@ -100,8 +100,9 @@ __device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol
 // in one warp) and a private ring of nslots shared-memory slots. Lane 0 keeps
 // the ring full with bulk copies; a slot's geometry is published next to it,
 // so the consuming side does no address arithmetic of its own.
-// AR: the launch consumes from and/or delivers to a fused all-reduce group
-// (a separate instantiation, so the plain matvec carries none of it).
+// AR: a row-split product whose partial outputs are all-reduced over the
+// tensor-parallel group inside the kernel (a separate instantiation, so the
+// plain matvec carries none of it).
 template <uint32_t T, bool AR>
 __global__ void __launch_bounds__(GEMV_WARPS * 32, 2) gemv_kernel(const GemvParams p) {
     using F = Fmt<T>;
@@ -152,31 +153,26 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 2) gemv_kernel(const GemvPara
     // each CTA of the cluster builds 1/nrank of the records for every member
     grid_dep_wait();
     const uint32_t rank = cluster_rank(), nrank = cluster_size();
-    // fused all-reduce: wait for the group's partials (consumption) and read
-    // the delivery count (delivery) while the weights keep streaming. The
-    // state lives in the 16 bytes after the activation records and is re-read
-    // where used (the loop below is at the launch bound's register limit):
-    // [0] consumed count, [1] delivery count, [2] delivery allowed.
+    // row-split product with a fused all-reduce: the delivery count and the
+    // group's state, read once per CTA, live in the 16 bytes after the
+    // activation records ([0] count e, [1] intact) and are re-read where used
+    // (the loop below is at the launch bound's register limit)
     volatile unsigned *const ar_st = reinterpret_cast<volatile unsigned *>(smem + ActView::bytes(p.nu));
+    ArState as{};
+    if constexpr (AR) {
+        if (threadIdx.x == 0) as = ar_load_state(p.ar);   // used after the quantizer
+    }
+    if (p.xf) quantize_into_act<F::act>(av, p.xf, p.n_in, rank, nrank);
+    else prep_activation<F::act>(av, p.xq, p.n_in, rank, nrank);
     if constexpr (AR) {
         if (threadIdx.x == 0) {
-            if (p.ar_in.n) ar_st[0] = ar_consume_wait(p.ar_in, p.status);
-            unsigned e = 0;
-            ar_st[2] = (p.ar_out.n && ar_deliver_begin(p.ar_out, p.status, e)) ? 1u : 0u;
-            ar_st[1] = e;
+            if (as.broken) atomicOr(p.status, STATUS_AR_TIMEOUT);
+            ar_st[0] = as.e;
+            ar_st[1] = as.broken ? 0u : 1u;
+            if (!as.broken) ar_arrive(p.ar, as.e);
         }
-        __syncthreads();
     }
-    if (AR && p.ar_in.n) {
-        const ArDev &a = p.ar_in;
-        const float *part = a.slot[a.rank] + (int64_t)((ar_st[0] - 1u) & 1u) * a.n * a.len;
-        quantize_into_act<F::act, true>(av, part, p.n_in, rank, nrank, a.n, a.len);
-    } else if (p.xf) {
-        quantize_into_act<F::act, false>(av, p.xf, p.n_in, rank, nrank, 1, 0);
-    } else {
-        prep_activation<F::act>(av, p.xq, p.n_in, rank, nrank);
-    }
-    cluster_sync();
+    cluster_sync();   // also publishes ar_st to the CTA
 
     const int r_l = p.nchunks == 1 ? lane / p.cu : 0;
     const int u_l = p.nchunks == 1 ? lane - r_l * p.cu : lane;
@@ -271,23 +267,27 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 2) gemv_kernel(const GemvPara
                 } else {
                     r = fin[lane];
                 }
-                p.y[mat][g.x + lane] = r;
-                if (AR && ar_st[2]) {
-                    const unsigned eo = ar_st[1];
-#pragma unroll
-                    for (int q = 0; q < AR_MAX; ++q)
-                        if (q < p.ar_out.n) ar_dst(p.ar_out, q, eo)[g.x + lane] = r;
-                }
+                // row-split product: the partial goes to every rank; y gets
+                // the sum after the loop
+                if (AR && ar_st[1]) ar_send(p.ar, ar_st[0], g.x + lane, r);
+                else p.y[mat][g.x + lane] = r;
             }
         }
         __syncwarp();
         if (++s == S) { s = 0; parity ^= 1u; }
     }
-    if (AR && ar_st[2]) {
-        // every thread's peer stores are ordered before the CTA's arrival
-        __threadfence_system();
-        __syncthreads();
-        if (threadIdx.x == 0) ar_deliver_arrive(p.ar_out, ar_st[1]);
+    if constexpr (AR) {
+        // the sums of this warp's rows: by now the other ranks' CTAs that
+        // compute the same rows have usually sent their parts
+        if (ar_st[1]) {
+            const unsigned e = ar_st[0];
+            bool live = true;
+            for (int t = t0 + warp; t < t1; t += W) {
+                const int64_t row = (int64_t)t * p.rows_per_task + lane;
+                if (lane < p.rows_per_task && row < p.n_out[0])
+                    p.y[0][row] = ar_sum(p.ar, e, row, p.status, live);
+            }
+        }
     }
 }
 
@@ -304,8 +304,7 @@ static int launch_gemv_t(const GemvLaunch &L, cudaStream_t st) {
     p.xf = L.xf;
     p.n_in = L.n_in;
     p.status = L.status;
-    p.ar_in = L.ar_in;
-    p.ar_out = L.ar_out;
+    p.ar = L.ar;
     const int nblk = (F::kind == 3) ? L.n_in / 32 : L.n_in / 256;
     p.row_bytes = (int64_t)nblk * (F::kind == 3 ? F::unit_bytes / 8 : F::unit_bytes);
     p.nu = (F::kind == 3) ? (nblk + 7) / 8 : nblk;
@@ -337,7 +336,7 @@ static int launch_gemv_t(const GemvLaunch &L, cudaStream_t st) {
     if (tasks == 0) return 0;
     const int64_t item_max = (p.nchunks == 1) ? p.rows_per_task * p.row_bytes : (int64_t)p.cu * F::unit_bytes;
     p.slot_bytes = (int)((item_max + 32 + 127) & ~int64_t(127));
-    const bool ar = L.ar_in.n > 0 || L.ar_out.n > 0;
+    const bool ar = L.ar.n > 0;
     p.act_bytes = (ActView::bytes(p.nu) + (ar ? 16 : 0) + 127) & ~127;
     // two CTAs per SM when each warp keeps >= 2 ring slots, with 8 warps per
     // CTA or, for large slots, down to 6 (12 warps per SM still hide more

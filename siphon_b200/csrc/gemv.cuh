@@ -57,8 +57,7 @@ struct GemvParams {
     int act_bytes;         // prepared-activation region
     int warp_bytes;        // per-warp region: barriers, slot geometry, terms, ring
     int *status;
-    ArDev ar_in;           // n > 0: the activation is the group's reduced partials (xf, xq unused)
-    ArDev ar_out;          // n > 0: the outputs are also delivered to the group (one matrix)
+    ArDev ar;              // n > 0: one row-split matrix; y = the group's sum of the partial outputs
 };
 
 // ---------------------------------------------------------------------------

@@ -9,29 +9,30 @@ namespace sicu {
 
 constexpr int MAX_MATS = 64;
 
-// Fused all-reduce of a tensor-parallel group, as the kernels see it. Every
+// All-reduce group of a tensor-parallel decode, as the kernels see it. Every
 // rank owns one peer-mapped allocation:
-//   slot[2][n][len]  f32 partial vectors, double-buffered by delivery parity
-//   flag[AR_MAX]     u32, flag[q] = number of deliveries rank q has completed
-//   epoch[4]         u32, this rank only: [0] deliveries made, [1] deliveries
-//                    consumed, [2] CTA arrival counter, [3] broken (a wait
-//                    timed out or the order was violated)
-// A delivery by rank r stores its vector into slot[e & 1][r] of every rank
-// (e = its delivery count) and raises its flag on every rank to e + 1 once
-// all its CTAs are done; a consumption waits for every flag to reach the
-// local delivery count and adds the n partials of that parity in rank order.
+//   slot[2][n][len]  u64 tagged elements: (tag << 32) | f32 bits, double
+//                    buffered by delivery parity
+//   epoch[4]         u32, this rank only: [0] deliveries made, [2] CTA arrival
+//                    counter, [3] broken (a wait timed out)
+// Delivery k (1-based) of rank r stores element i as one 64-bit word with tag
+// k into slot[(k - 1) & 1][r][i] of every rank; each rank reads
+// slot[(k - 1) & 1][q][i] of its own memory for every q until the word
+// carries tag k, so value and readiness arrive in one single-copy-atomic
+// store. Rank q's delivery k + 2 (same buffer) cannot start before every rank
+// finished reading delivery k: it follows q's delivery k + 1, which waited
+// for every rank's part k + 1, which each rank sends only after its own
+// delivery k completed.
 constexpr int AR_MAX = 8;
 struct ArDev {
     int n = 0, rank = 0;
-    int64_t len = 0;                  // floats per partial
+    int64_t len = 0;                  // elements per partial
     uint64_t limit_ns = 0;            // bound of a consumption's wait
-    float *slot[AR_MAX] = {};         // slot array of rank q (this rank's own at [rank])
-    unsigned *flag[AR_MAX] = {};      // flag array of rank q
+    uint64_t *slot[AR_MAX] = {};      // slot array of rank q (this rank's own at [rank])
     unsigned *epoch = nullptr;        // this rank's epoch words
 };
 // byte offsets inside one rank's allocation
-inline int64_t ar_flag_offset(int n, int64_t len) { return 2 * (int64_t)n * len * 4; }
-inline int64_t ar_epoch_offset(int n, int64_t len) { return ar_flag_offset(n, len) + 4 * AR_MAX; }
+inline int64_t ar_epoch_offset(int n, int64_t len) { return 2 * (int64_t)n * len * 8; }
 inline int64_t ar_alloc_bytes(int n, int64_t len) { return ar_epoch_offset(n, len) + 16; }
 
 struct GemvLaunch {
@@ -55,8 +56,7 @@ struct GemvLaunch {
                           // earlier work in the stream completes
     int device;
     int *status;          // device status word
-    ArDev ar_in;          // n > 0: the activation is the group's reduced partials
-    ArDev ar_out;         // n > 0: the single matrix's outputs are delivered to the group
+    ArDev ar;             // n > 0: row-split product, y = the group's sum of the partial outputs
 };
 
 // quantized formats (K and classic); fails with -3 for other types
@@ -83,9 +83,8 @@ size_t prefill_workspace_bytes(uint32_t wtype, int64_t n_in, int64_t n_out, int6
 // -3: no tensor-core kernel for the type; -4: tensor map encoding failed; -2: launch
 int launch_prefill(uint32_t wtype, const PrefillLaunch &L, cudaStream_t st);
 
-// standalone delivery of src[len] / consumption into dst[len] of a group
-int launch_ar_deliver(const ArDev &a, const float *src, int *status, int num_sms, cudaStream_t st);
-int launch_ar_reduce(const ArDev &a, float *dst, int *status, int num_sms, cudaStream_t st);
+// all-reduce of src[len] into dst[len] over the group (one delivery)
+int launch_allreduce(const ArDev &a, const float *src, float *dst, int *status, int num_sms, cudaStream_t st);
 
 // dequantise rows (row_to_f32): rows[i] of w into out[i * n_in]
 int launch_dequant(uint32_t wtype, const void *w, int64_t n_in, const int64_t *rows_dev, int64_t nrows,

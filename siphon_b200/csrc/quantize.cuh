@@ -76,35 +76,15 @@ __device__ __forceinline__ int sat8_rounded(float r) {
     return i > 127 ? 127 : (i < -128 ? -128 : i);
 }
 
-// 32 consecutive floats (16-byte aligned). SUM: the element-wise sum of nsum
-// such vectors `stride` floats apart, added in order in f32; these are
-// written by other GPUs, so they are read from L2 (never a stale L1 line).
-template <bool SUM>
-__device__ __forceinline__ void load32(const float *x, int nsum, int64_t stride, float v[32]) {
-    const float4 *src = reinterpret_cast<const float4 *>(x);
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-        const float4 f = SUM ? __ldcg(src + k) : src[k];
-        v[4 * k] = f.x; v[4 * k + 1] = f.y; v[4 * k + 2] = f.z; v[4 * k + 3] = f.w;
-    }
-    if constexpr (SUM) {
-        for (int r = 1; r < nsum; ++r) {
-            const float4 *sr = reinterpret_cast<const float4 *>(x + r * stride);
-#pragma unroll
-            for (int k = 0; k < 8; ++k) {
-                const float4 f = __ldcg(sr + k);
-                v[4 * k] = __fadd_rn(v[4 * k], f.x);
-                v[4 * k + 1] = __fadd_rn(v[4 * k + 1], f.y);
-                v[4 * k + 2] = __fadd_rn(v[4 * k + 2], f.z);
-                v[4 * k + 3] = __fadd_rn(v[4 * k + 3], f.w);
-            }
-        }
-    }
-}
-
 // One thread quantizes one 32-element block (AVX2 form): v in, f16 d and
 // 32 int8 quants (8 little-endian words) out.
-__device__ __forceinline__ void q8_0_block_v(const float (&v)[32], uint32_t &d16, uint32_t qw[8]) {
+__device__ __forceinline__ void q8_0_block(const float *x, uint32_t &d16, uint32_t qw[8]) {
+    float v[32];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        const float4 f = reinterpret_cast<const float4 *>(x)[k];
+        v[4 * k] = f.x; v[4 * k + 1] = f.y; v[4 * k + 2] = f.z; v[4 * k + 3] = f.w;
+    }
     float lane[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
@@ -132,22 +112,13 @@ __device__ __forceinline__ void q8_0_block_v(const float (&v)[32], uint32_t &d16
     }
 }
 
-__device__ __forceinline__ void q8_0_block(const float *x, uint32_t &d16, uint32_t qw[8]) {
-    float v[32];
-    load32<false>(x, 1, 0, v);
-    q8_0_block_v(v, d16, qw);
-}
-
 // Fused prologue: quantize the f32 activation straight into the prepared
 // records this cluster rank owns (u % nrank == rank), writing each into every
 // CTA of the cluster. K formats: eight lanes per 256-element block, lane j
 // owning elements 32j..32j+31, so after one 3-step max reduction every lane
 // emits its own piece. Classic formats: one thread per 32-element block.
-// SUM: the activation is the sum of nsum vectors `stride` floats apart (the
-// partial outputs of a tensor-parallel group, added in rank order).
-template <int ACT, bool SUM>
-__device__ void quantize_into_act(const ActView av, const float *xf, int n_in, uint32_t rank, uint32_t nrank,
-                                  int nsum, int64_t stride) {
+template <int ACT>
+__device__ void quantize_into_act(const ActView av, const float *xf, int n_in, uint32_t rank, uint32_t nrank) {
     const RecWriter wr{nrank};
     if constexpr (ACT == 3) {
         const int nblk = n_in / 32, nu = (nblk + 7) / 8;
@@ -156,9 +127,7 @@ __device__ void quantize_into_act(const ActView av, const float *xf, int n_in, u
             const int u = (int)rank + (int)nrank * (i >> 3), b = 8 * u + (i & 7);
             if (b >= nblk) continue;
             uint32_t d16, q[8];
-            float v[32];
-            load32<SUM>(xf + 32 * b, nsum, stride, v);
-            q8_0_block_v(v, d16, q);
+            q8_0_block(xf + 32 * b, d16, q);
             int s = 0;
 #pragma unroll
             for (int k = 0; k < 8; ++k) s = dp4a_ss(q[k], 0x01010101u, s);
@@ -170,8 +139,13 @@ __device__ void quantize_into_act(const ActView av, const float *xf, int n_in, u
         const unsigned gmask = 0xffu << (lane & 24);
         const int groups = blockDim.x >> 3;
         for (int u = (int)rank + (int)nrank * (threadIdx.x >> 3); u < nsb; u += (int)nrank * groups) {
+            const float4 *src = reinterpret_cast<const float4 *>(xf + 256 * u + 32 * j);
             float v[32];
-            load32<SUM>(xf + 256 * u + 32 * j, nsum, stride, v);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                const float4 f = src[k];
+                v[4 * k] = f.x; v[4 * k + 1] = f.y; v[4 * k + 2] = f.z; v[4 * k + 3] = f.w;
+            }
             // first element of largest magnitude (strict '>' keeps the earliest)
             float best = 0.0f, bval = 0.0f;
             int bi = 256;

@@ -55,14 +55,12 @@ SIGNATURES = {
     "sicu_ar_open": [_vp, _vp],
     "sicu_ar_set_timeout": [_vp, C.c_uint64],
     "sicu_ar_destroy": [_vp],
-    "sicu_ar_deliver": [_vp, _fp, _vp],
-    "sicu_ar_reduce": [_vp, _fp, _vp],
-    "sicu_gemv_ar": [_u32, C.c_int, C.POINTER(C.c_void_p), C.POINTER(C.c_int64), _i64, _fp, _vp,
-                     C.POINTER(C.c_void_p), _vp, _vp],
+    "sicu_ar_allreduce": [_vp, _fp, _fp, _vp],
+    "sicu_gemv_ar": [_u32, _vp, _i64, _i64, _fp, _fp, _vp, _vp],
 }
 
 AR_HANDLE_BYTES = 64
-STATUS_WAIT_TIMEOUT, STATUS_AR_TIMEOUT, STATUS_AR_ORDER = 1, 2, 4
+STATUS_WAIT_TIMEOUT, STATUS_AR_TIMEOUT = 1, 2
 
 
 class SicuError(RuntimeError):
@@ -172,17 +170,10 @@ class SiphonCuda:
     def ar_create(self, n_ranks: int, rank: int, length: int) -> "ArGroup":
         return ArGroup(self, n_ranks, rank, length)
 
-    def gemv_ar(self, wtype: int, dws, n_outs, n_in: int, dx, dys, consume=None, deliver=None, stream=None) -> None:
-        """sicu_gemv_ar: gemv_multi with the activation taken from `consume`
-        (an opened ArGroup; dx None) and/or the single output delivered to
-        `deliver`."""
-        n = len(dws)
-        w_arr = (C.c_void_p * n)(*[_ptr(w) for w in dws])
-        y_arr = (C.c_void_p * n)(*[_ptr(y) for y in dys])
-        o_arr = (C.c_int64 * n)(*n_outs)
-        self.check(self.lib.sicu_gemv_ar(wtype, n, w_arr, o_arr, n_in, _ptr(dx),
-                                         consume.handle if consume else None, y_arr,
-                                         deliver.handle if deliver else None, _ptr(stream)))
+    def gemv_ar(self, wtype: int, dw, n_in: int, n_out: int, dx, dy, group: "ArGroup", stream=None) -> None:
+        """sicu_gemv_ar: this rank's column shard times x, summed over the group."""
+        self.check(self.lib.sicu_gemv_ar(wtype, _ptr(dw), n_in, n_out, _ptr(dx), _ptr(dy), group.handle,
+                                         _ptr(stream)))
 
     def row_to_f32(self, wtype: int, dw, n_in: int, rows, dout, stream=None) -> None:
         arr = (C.c_int64 * len(rows))(*rows)
@@ -199,9 +190,9 @@ class SiphonCuda:
 
 
 class ArGroup:
-    """One rank's member of a fused all-reduce group (sicu_ar_*): create,
-    exchange `local_handle` with the other ranks, `open` with all of them in
-    rank order, then pass it to gemv_ar / deliver / reduce."""
+    """One rank's member of an all-reduce group (sicu_ar_*): create, exchange
+    `local_handle` with the other ranks, `open` with all of them in rank
+    order, then pass it to gemv_ar / allreduce."""
 
     def __init__(self, sicu: SiphonCuda, n_ranks: int, rank: int, length: int):
         self.s, self.n, self.rank, self.len = sicu, n_ranks, rank, length
@@ -220,11 +211,8 @@ class ArGroup:
     def set_timeout(self, ns: int) -> None:
         self.s.check(self.s.lib.sicu_ar_set_timeout(self.handle, ns))
 
-    def deliver(self, dsrc, stream=None) -> None:
-        self.s.check(self.s.lib.sicu_ar_deliver(self.handle, _ptr(dsrc), _ptr(stream)))
-
-    def reduce(self, ddst, stream=None) -> None:
-        self.s.check(self.s.lib.sicu_ar_reduce(self.handle, _ptr(ddst), _ptr(stream)))
+    def allreduce(self, dsrc, ddst, stream=None) -> None:
+        self.s.check(self.s.lib.sicu_ar_allreduce(self.handle, _ptr(dsrc), _ptr(ddst), _ptr(stream)))
 
     def destroy(self) -> None:
         if self.handle:

@@ -23,6 +23,17 @@ name: Wq/Wk/Wv, W_gate/W_up and the output head are split by output rows
 the partial Wo and W_down outputs are summed with one all-reduce each per
 layer (attention block and FFN block). Column shards are whole 256-element
 super-blocks (Q8_K quantizes whole blocks), so shards can be uneven.
+
+Two forms of that all-reduce:
+
+* ``fused=True`` (decode): sicu_gemv_ar runs Wo and W_down as row-split
+  products with the all-reduce inside the kernel (NVLink peer stores of the
+  partial rows, a bounded wait for the other ranks' parts, the sum in rank
+  order). The next products read the sum: W_gate/W_up read Wo's, the next
+  layer's Wq/Wk/Wv (or the head) read W_down's, where a full forward pass
+  would put the residual add and norm between them.
+* otherwise: ``torch.distributed.all_reduce`` (NCCL) on each partial output,
+  and every product reads a fixed activation.
 """
 
 from __future__ import annotations
@@ -117,9 +128,10 @@ class MatrixPath:
     sequence of a decode step / a prefill over them."""
 
     def __init__(self, sicu, sh: LlamaShape, device, world: int = 1, rank: int = 0, group=None, seed: int = 0,
-                 max_tokens: int = 1):
+                 max_tokens: int = 1, fused: bool = False):
         import torch
         self.s, self.sh, self.dev, self.world, self.group = sicu, sh, device, world, group
+        self.ar = None
         self.shard = tp_partition(sh, world, rank)
         self.shapes = shard_shapes(sh, self.shard)
         self.layers = []
@@ -145,6 +157,24 @@ class MatrixPath:
         self.x_model, self.x_attn, self.x_ff = act(sh.n_embd), act(nq), act(nff)
         self.y = {name: torch.empty(m, self.shapes[name][0], device=device) for name in self.shapes}
         self.weight_bytes = step_weight_bytes(sh, world, rank)
+        if fused and world > 1:
+            import torch.distributed as dist
+            self.ar = sicu.ar_create(world, rank, sh.n_embd)
+            handles = [None] * world
+            dist.all_gather_object(handles, self.ar.local_handle, group=group)
+            self.ar.open(handles)
+
+    def close(self) -> None:
+        """Release the fused group (every rank calls this at the same point:
+        streams are drained and the ranks meet before and after)."""
+        if self.ar is not None:
+            import torch
+            import torch.distributed as dist
+            torch.cuda.synchronize()
+            dist.barrier(group=self.group)
+            self.ar.destroy()
+            self.ar = None
+            dist.barrier(group=self.group)
 
     def _allreduce(self, t) -> None:
         if self.world > 1:
@@ -154,6 +184,8 @@ class MatrixPath:
     def decode_step(self, stream) -> int:
         """Launch one token's products on `stream`; returns the number of
         library kernel launches."""
+        if self.ar is not None:
+            return self._decode_step_fused(stream)
         s, h, y = self.s, stream.cuda_stream, self.y
         x, xa, xf = self.x_model[0], self.x_attn[0], self.x_ff[0]
         n = 0
@@ -179,6 +211,35 @@ class MatrixPath:
             n += 3
         th, wh = self.head
         s.gemv_f32(th, wh, self.sh.n_embd, self.shapes["head"][0], x, y["head"], stream=h)
+        return n + 1
+
+    def _decode_step_fused(self, stream) -> int:
+        """decode_step with the all-reduces fused into Wo and W_down: 4 or 5
+        launches per layer and no collective launches."""
+        s, h, y, ar, d = self.s, stream.cuda_stream, self.y, self.ar, self.sh.n_embd
+        (nq, _), (nkv, _) = self.shapes["q"], self.shapes["k"]
+        nff = self.shapes["gate"][0]
+        x = self.x_model[0]                  # layer 0 reads the embedding row
+        n = 0
+        for lay in self.layers:
+            (tq, wq), (tk, wk), (tv, wv) = lay["q"], lay["k"], lay["v"]
+            if tv == tq:
+                s.gemv_multi(tq, [wq, wk, wv], [nq, nkv, nkv], d, x, [y["q"], y["k"], y["v"]], stream=h)
+                n += 1
+            else:
+                s.gemv_multi(tq, [wq, wk], [nq, nkv], d, x, [y["q"], y["k"]], stream=h)
+                s.gemv_f32(tv, wv, d, nkv, x, y["v"], stream=h)
+                n += 2
+            to, wo = lay["o"]
+            s.gemv_ar(to, wo, nq, d, self.x_attn[0], y["o"][0], ar, stream=h)
+            (tg, wg), (_, wu) = lay["gate"], lay["up"]
+            s.gemv_multi(tg, [wg, wu], [nff, nff], d, y["o"][0], [y["gate"], y["up"]], stream=h)
+            td, wd = lay["down"]
+            s.gemv_ar(td, wd, nff, d, self.x_ff[0], y["down"][0], ar, stream=h)
+            x = y["down"][0]
+            n += 3
+        th, wh = self.head
+        s.gemv_f32(th, wh, d, self.shapes["head"][0], x, y["head"], stream=h)
         return n + 1
 
     def prefill(self, stream, m: int) -> None:

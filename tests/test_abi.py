@@ -98,15 +98,10 @@ def test_allreduce_group_checks_run_on_host(so):
     assert "sicu_init" in so.last_error()
     assert h.value is None
     assert so.lib.sicu_ar_open(None, buf) == L.SICU_EINVAL
-    assert so.lib.sicu_ar_deliver(None, 16, None) == L.SICU_EINVAL
-    assert so.lib.sicu_ar_reduce(None, 16, None) == L.SICU_EINVAL
+    assert so.lib.sicu_ar_allreduce(None, 16, 16, None) == L.SICU_EINVAL
     assert so.lib.sicu_ar_set_timeout(None, 1000) == L.SICU_EINVAL
     assert so.lib.sicu_ar_destroy(None) == L.SICU_OK
-    # the fused matvec: an activation and a group to consume are exclusive,
-    # F16 has no fused form
-    w = (C.c_void_p * 1)(4096)
-    y = (C.c_void_p * 1)(8192)
-    n = (C.c_int64 * 1)(256)
-    assert so.lib.sicu_gemv_ar(Q.Q4_K, 1, w, n, 256, None, None, y, None, None) == L.SICU_EINVAL
-    assert so.lib.sicu_gemv_ar(Q.F16, 1, w, n, 256, 16, None, y, None, None) == L.SICU_ENOTSUP
-    assert so.lib.sicu_gemv_ar(Q.Q4_K, 0, w, n, 256, 16, None, y, None, None) == L.SICU_EINVAL
+    # the fused matvec: F16 has no fused form; shapes are checked first
+    assert so.lib.sicu_gemv_ar(Q.F16, 4096, 256, 256, 16, 8192, None, None) == L.SICU_ENOTSUP
+    assert so.lib.sicu_gemv_ar(Q.Q4_K, 4096, 300, 256, 16, 8192, None, None) == L.SICU_EINVAL
+    assert so.lib.sicu_gemv_ar(Q.Q4_K, 4096, 256, 256, 16, 8192, None, None) == L.SICU_EINVAL   # no group

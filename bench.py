@@ -450,6 +450,11 @@ def model_metrics(torch, s, dev, stream, world, rank, quick: bool) -> dict:
     if world > 1:
         out["tp_decode_nccl"] = {"config": "as tp_decode, the all-reduces as NCCL calls between the matvecs",
                                  **model_decode(torch, s, sm.QWEN25_32B, dev, stream, world, rank, None, reps)}
+    out["tp_prefill"] = {"config": "configs[4] Qwen2.5-32B shape, 512-token prompt, matrix path, "
+                                   + (f"tensor parallel x{world} (an NCCL all-reduce of the 512 x 5120 partial "
+                                      "after o and after down per layer)" if world > 1 else "one GPU"),
+                         **model_prefill(torch, s, sm.QWEN25_32B, dev, stream, world, rank, None, 512,
+                                         max(2, reps // 2))}
     out["tp_decode_batch8"] = {"config": "configs[4] Qwen2.5-32B shape, batch 8, matrix path, "
                                          + (f"tensor parallel x{world}" if world > 1 else "one GPU"),
                                **model_batch_decode(torch, s, sm.QWEN25_32B, dev, stream, world, rank, None, 8, reps)}

@@ -291,6 +291,210 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 2) gemv_kernel(const GemvPara
     }
 }
 
+// ---- flattened items ------------------------------------------------------------
+// When a row's unit count nu does not divide 32, whole-row items leave lanes
+// idle (nu = 20: 20 of 32). Here a task is R consecutive rows of one matrix
+// and its R x nu units are streamed as items of up to 32 consecutive units --
+// one contiguous bulk copy, rows being back to back -- so every lane decodes a
+// unit. A row whose units straddle two items continues its float chains in
+// the next item of the same warp, in order (the partial chains wait in shared
+// memory), so every output is bit-identical to the whole-row kernel's.
+
+// a += src[0]; a += src[1]; ... in order; src 4-byte aligned
+__device__ __forceinline__ float chain_add_any(float a, const float *src, int n) {
+    int i = 0;
+    const int head = min(n, (int)((4u - ((uint32_t)(reinterpret_cast<uintptr_t>(src) >> 2) & 3u)) & 3u));
+    for (; i < head; ++i) a = __fadd_rn(a, src[i]);
+    const float4 *s4 = reinterpret_cast<const float4 *>(src + i);
+    const int n4 = (n - i) >> 2;
+#pragma unroll 2
+    for (int g = 0; g < n4; ++g) {
+        const float4 v = s4[g];
+        a = __fadd_rn(a, v.x); a = __fadd_rn(a, v.y); a = __fadd_rn(a, v.z); a = __fadd_rn(a, v.w);
+    }
+    for (i += n4 << 2; i < n; ++i) a = __fadd_rn(a, src[i]);
+    return a;
+}
+
+// Item cursor of one warp: task (over all matrices), item k of the task.
+struct FlatCursor {
+    int task, k, mat, row0, units;
+    __device__ void locate(const GemvParams &p) {
+        while (mat + 1 < p.nmat && task >= p.task0[mat + 1]) ++mat;
+        row0 = (task - p.task0[mat]) * p.rows_per_task;
+        units = min(p.rows_per_task, p.n_out[mat] - row0) * p.nu;
+    }
+    __device__ void next(const GemvParams &p, int step) {
+        if (32 * (k + 1) < units) {
+            ++k;
+        } else {
+            k = 0;
+            task += step;
+            if (task < p.ntasks) locate(p);
+        }
+    }
+};
+
+constexpr int FLAT_TS = 36;    // terms row stride (floats): an odd number of 16-byte units
+
+template <uint32_t T>
+__global__ void __launch_bounds__(GEMV_WARPS * 32, 2) gemv_flat_kernel(const GemvParams p) {
+    using F = Fmt<T>;
+    constexpr int CH = F::chains;
+    const int W = (int)(blockDim.x >> 5);
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int S = p.nslots, nu = p.nu;
+
+    const ActView av{smem, nu};
+    uint8_t *wreg = smem + p.act_bytes + (size_t)warp * p.warp_bytes;
+    uint64_t *full = reinterpret_cast<uint64_t *>(wreg);          // [S]
+    int4 *info = reinterpret_cast<int4 *>(wreg + 64);              // [S][2]
+    float *terms = reinterpret_cast<float *>(wreg + 192);          // [CH][FLAT_TS]
+    float *carry = terms + 448;                                    // [2][CH] chains continuing
+    float *fin = terms + TERM_FLOATS;                              // 64 chain results
+    uint8_t *slots = wreg + 192 + CONS_BYTES;
+
+    const int t0 = (int)((int64_t)blockIdx.x * p.ntasks / gridDim.x);
+    const int t1 = (int)((int64_t)(blockIdx.x + 1) * p.ntasks / gridDim.x);
+    grid_dep_launch();
+
+    if (lane == 0) {
+        for (int i = 0; i < S; ++i) mbar_init(smem_addr(&full[i]), 1);
+        fence_mbar_init();
+    }
+    __syncwarp();
+    // producer (lane 0): its own cursor, S items ahead of the consumer
+    FlatCursor pc{t0 + warp, 0, 0, 0, 0};
+    uint32_t tailmask = 0;
+    uint64_t policy = 0;
+    auto produce = [&](int s) {
+        const uint8_t *w = p.w[pc.mat];
+        const uint8_t *mend = w + (int64_t)p.n_out[pc.mat] * p.row_bytes;
+        const int fs = 32 * pc.k, c = min(32, pc.units - fs);
+        const uint8_t *src = w + (int64_t)pc.row0 * p.row_bytes + (int64_t)fs * F::unit_bytes;
+        const int64_t len = (int64_t)c * F::unit_bytes;
+        uint8_t *slot = slots + (size_t)s * p.slot_bytes;
+        const uintptr_t a = reinterpret_cast<uintptr_t>(src);
+        const uint8_t *al = reinterpret_cast<const uint8_t *>(a & ~uintptr_t(15));
+        const int head = (int)(a & 15);
+        int64_t bulk = (head + len + 15) & ~int64_t(15);
+        if (al + bulk > mend) bulk = (int64_t)(mend - al) & ~int64_t(15);
+        const int tail = (int)(head + len - bulk);
+        if (tailmask & (1u << s)) {
+            fence_proxy_async();
+            tailmask &= ~(1u << s);
+        }
+        if (tail > 0) {
+            for (int i = 0; i < tail; ++i) slot[bulk + i] = (uint8_t)ldg_u8(al + bulk + i);
+            tailmask |= 1u << s;
+        }
+        info[2 * s] = make_int4(pc.row0, fs | (head << 16), c, pc.units);
+        info[2 * s + 1] = make_int4(pc.mat, 0, 0, 0);
+        const uint32_t bar = smem_addr(&full[s]);
+        mbar_expect_tx(bar, (uint32_t)bulk);
+        if (bulk > 0) bulk_g2s_hint(smem_addr(slot), al, (uint32_t)bulk, bar, policy);
+    };
+    if (lane == 0 && pc.task < t1) {
+        pc.locate(p);
+        policy = policy_evict_first();
+        for (int i = 0; i < S && pc.task < t1; ++i) {
+            produce(i);
+            pc.next(p, W);
+        }
+    }
+
+    grid_dep_wait();
+    const uint32_t rank = cluster_rank(), nrank = cluster_size();
+    if (p.xf) quantize_into_act<F::act>(av, p.xf, p.n_in, rank, nrank);
+    else prep_activation<F::act>(av, p.xq, p.n_in, rank, nrank);
+    cluster_sync();
+
+    int s = 0, cpar = 0;
+    uint32_t parity = 0;
+    bool ok = true;
+    for (int task = t0 + warp; task < t1 && ok; task += W) {
+        for (int k = 0;; ++k) {
+            const bool landed = mbar_wait(smem_addr(&full[s]), parity);
+            if (!__all_sync(0xffffffffu, landed)) {
+                if (lane == 0) atomicOr(p.status, STATUS_WAIT_TIMEOUT);
+                // let the copies still in flight land before the CTA's memory goes away
+                for (int j = 0; j < S; ++j) {
+                    const int sj = (s + j) % S;
+                    (void)mbar_wait(smem_addr(&full[sj]), parity ^ (uint32_t)(sj < s), 100000000ull);
+                }
+                ok = false;
+                break;
+            }
+            const int4 g = info[2 * s];
+            const int mat = info[2 * s + 1].x;
+            const int row0 = g.x, fs = g.y & 0xffff, c = g.z, units = g.w;
+            const uint8_t *data = slots + (size_t)s * p.slot_bytes + (g.y >> 16);
+
+            // ---- phase 1: lane l decodes unit fs + l of the task ----
+            const int r_first = fs / nu, r_last = (fs + c - 1) / nu;
+            if (lane < c) {
+                int ug = fs - r_first * nu + lane;   // unit within its row
+                while (ug >= nu) ug -= nu;
+                float t[MAX_CHAINS];
+                const uint8_t *wb = data + lane * F::unit_bytes;
+                const uint8_t *rec = av.rec(ug);
+                if constexpr (T == T_Q4_K) unit_q45k<false>(wb, rec, t);
+                else if constexpr (T == T_Q5_K) unit_q45k<true>(wb, rec, t);
+                else if constexpr (T == T_Q6_K) unit_q36k<false>(wb, rec, t);
+                else if constexpr (T == T_Q3_K) unit_q36k<true>(wb, rec, t);
+                else unit_q2k(wb, rec, t);
+#pragma unroll
+                for (int ch = 0; ch < CH; ++ch) terms[ch * FLAT_TS + lane] = t[ch];
+            }
+            __syncwarp();
+            if (lane == 0 && pc.task < t1) {
+                produce(s);
+                pc.next(p, W);
+            }
+
+            // ---- phase 2: the rows' chains over this item's units, in order ----
+            const int pairs = (r_last - r_first + 1) * CH;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int q = lane + 32 * h;
+                if (q < pairs) {
+                    const int kp = q / CH, ch = q - kp * CH;
+                    const int r = r_first + kp;
+                    const int b0 = r * nu, b1 = b0 + nu;
+                    const int p0 = max(b0, fs) - fs, p1 = min(b1, fs + c) - fs;
+                    float a = b0 < fs ? carry[cpar * CH + ch] : 0.0f;
+                    a = chain_add_any(a, terms + ch * FLAT_TS + p0, p1 - p0);
+                    if (b1 <= fs + c) fin[kp * CH + ch] = a;
+                    else carry[(cpar ^ 1) * CH + ch] = a;
+                }
+            }
+            cpar ^= 1;
+            __syncwarp();
+            // ---- rows completed in this item ----
+            const int ncomp = (r_last - r_first + 1) - (((r_last + 1) * nu > fs + c) ? 1 : 0);
+            if (lane < ncomp) {
+                float r;
+                if constexpr (F::kind == 0) {
+                    r = fin[lane * CH + 8];
+#pragma unroll
+                    for (int l = 0; l < 8; ++l) r = __fadd_rn(r, fin[lane * CH + l]);
+                } else if constexpr (F::kind == 1) {
+                    r = 0.0f;
+#pragma unroll
+                    for (int l = 0; l < 8; ++l) r = __fadd_rn(r, fin[lane * CH + l]);
+                } else {
+                    r = fin[lane];
+                }
+                p.y[mat][row0 + r_first + lane] = r;
+            }
+            __syncwarp();
+            if (++s == S) { s = 0; parity ^= 1u; }
+            if (32 * (k + 1) >= units) break;
+        }
+    }
+}
+
 }  // namespace
 
 // ---- host side ------------------------------------------------------------------
@@ -323,6 +527,38 @@ static int launch_gemv_t(const GemvLaunch &L, cudaStream_t st) {
         p.cu = (p.nu + p.nchunks - 1) / p.nchunks;
         p.rows_per_task = 1;
     }
+    // flattened items (gemv_flat_kernel) when rows leave lanes idle and the
+    // launch has enough rows that fewer, fuller items per warp win: compare
+    // the items the busiest warp processes (grid of 2 CTAs x 8 warps per SM)
+    const bool ar = L.ar.n > 0;
+    bool flat = false;
+    // (only when whole-row items leave a quarter of the lanes idle or more:
+    // at 87.5 % lane use, e.g. 56 units in chunks of 28, the whole-row kernel's
+    // aligned register-carried chains measured faster)
+    const double row_lanes = p.nchunks == 1 ? (double)(p.rows_per_task * p.nu) / 32.0
+                                            : (double)p.nu / (32.0 * p.nchunks);
+    if (F::kind != 3 && !ar && p.nu >= 6 && row_lanes < 0.8) {
+        const int64_t G = 2LL * L.num_sms;
+        auto busiest = [&](int rows, int64_t items_per_task) {
+            int64_t tasks = 0;
+            for (int i = 0; i < L.nmat; ++i) tasks += (L.n_outm[i] + rows - 1) / rows;
+            const int64_t per_cta = (tasks + G - 1) / G;
+            return (per_cta + GEMV_WARPS - 1) / GEMV_WARPS * items_per_task;
+        };
+        int64_t best = busiest(p.rows_per_task, p.nchunks);
+        for (int r = 1; r <= 8; ++r) {
+            const int64_t v = busiest(r, (r * p.nu + 31) / 32);
+            if (v < best) {
+                best = v;
+                flat = true;
+                p.rows_per_task = r;
+            }
+        }
+        if (flat) {
+            p.nchunks = 1;
+            p.cu = 32;
+        }
+    }
     int64_t tasks = 0;
     for (int i = 0; i < L.nmat; ++i) {
         p.w[i] = static_cast<const uint8_t *>(L.wm[i]);
@@ -334,9 +570,9 @@ static int launch_gemv_t(const GemvLaunch &L, cudaStream_t st) {
     p.task0[L.nmat] = (int)tasks;
     p.ntasks = tasks;
     if (tasks == 0) return 0;
-    const int64_t item_max = (p.nchunks == 1) ? p.rows_per_task * p.row_bytes : (int64_t)p.cu * F::unit_bytes;
+    const int64_t item_max = flat ? 32LL * F::unit_bytes
+                                  : (p.nchunks == 1) ? p.rows_per_task * p.row_bytes : (int64_t)p.cu * F::unit_bytes;
     p.slot_bytes = (int)((item_max + 32 + 127) & ~int64_t(127));
-    const bool ar = L.ar.n > 0;
     p.act_bytes = (ActView::bytes(p.nu) + (ar ? 16 : 0) + 127) & ~127;
     // two CTAs per SM when each warp keeps >= 2 ring slots, with 8 warps per
     // CTA or, for large slots, down to 6 (12 warps per SM still hide more
@@ -358,17 +594,21 @@ static int launch_gemv_t(const GemvLaunch &L, cudaStream_t st) {
     p.nslots = slots;
     p.warp_bytes = (hdr + slots * p.slot_bytes + 127) & ~127;
     const int smem = p.act_bytes + warps * p.warp_bytes;
-    const auto kern = ar ? gemv_kernel<T, true> : gemv_kernel<T, false>;
-    static bool attr_set[64][2] = {};
+    auto kern = ar ? gemv_kernel<T, true> : gemv_kernel<T, false>;
+    if constexpr (F::kind != 3) {
+        if (flat) kern = gemv_flat_kernel<T>;
+    }
+    const int variant = flat ? 2 : ar ? 1 : 0;
+    static bool attr_set[64][3] = {};
     const int dev = L.device & 63;
-    if (!attr_set[dev][ar]) {
+    if (!attr_set[dev][variant]) {
         if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L.smem_limit) != cudaSuccess)
             return -2;
         // every kernel of the library asks for the same (largest) shared-memory
         // carveout, so consecutive launches of different kernels never wait
         // for an SM to reconfigure its L1 / shared-memory split
         cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
-        attr_set[dev][ar] = true;
+        attr_set[dev][variant] = true;
     }
     // thread-block cluster size: 2 when pairs still keep (almost) every CTA
     // slot of the launch co-resident, else 1
@@ -378,7 +618,7 @@ static int launch_gemv_t(const GemvLaunch &L, cudaStream_t st) {
         static std::mutex mu;
         static std::map<std::pair<int, int>, std::pair<int, int>> cache;   // (device x variant, smem x warps) -> (C, capacity)
         std::lock_guard<std::mutex> lk(mu);
-        const auto key = std::make_pair(dev * 2 + (ar ? 1 : 0), smem * 16 + warps);
+        const auto key = std::make_pair(dev * 4 + variant, smem * 16 + warps);
         auto hit = cache.find(key);
         if (hit == cache.end()) {
             int best_c = 1, best_cap = target;

@@ -236,41 +236,6 @@ SICU_API int sicu_ar_allreduce(sicu_ar *group, const float *dsrc, float *ddst, v
 SICU_API int sicu_gemv_ar(uint32_t wtype, const void *dw, int64_t n_in, int64_t n_out,
                           const float *dx, float *dy, sicu_ar *group, void *stream);
 
-/* ---- a decode step's products in one launch ---------------------------------
- * The reference's forward pass calls its backend gemv once per weight matrix
- * and token (src/engine.c:317-319, 368, 375-378, 393); on a GPU each such
- * call is a kernel launch whose ramp-up and drain cost more than streaming a
- * small matrix. A chain runs a fixed sequence of matvec stages in ONE
- * persistent launch: all CTAs meet at a grid barrier between stages, so a
- * stage may read (as its activation x) what an earlier stage wrote, and the
- * weights of the coming stages stream into shared memory across the barrier.
- * Every stage's outputs are bit-identical to sicu_gemv_multi / sicu_gemv_ar
- * on the same inputs. Each stage: one to four matrices of one type (Q4_K or
- * Q6_K) sharing the f32 activation x (device, 16-byte aligned); with
- * all_reduce set, one row-split matrix whose output is summed over `group`
- * (as sicu_gemv_ar). sicu_chain_create checks the stages, plans the launch
- * and copies the stage table to the device (it allocates: call it before any
- * stream capture); sicu_chain_run launches it (pointers are fixed at create
- * time; their contents may change between runs). Waits are bounded (2 s for a
- * grid barrier, the group's timeout for an all-reduce) and report through
- * sicu_status; a chain holds every SM of the GPU for its whole run, so run
- * nothing else on the device concurrently with it. No counterpart in the
- * reference. */
-typedef struct {
-    uint32_t wtype;        /* SICU_T_Q4_K or SICU_T_Q6_K */
-    int n_mats;            /* 1..4 */
-    const void *w[4];      /* weight blocks (device) */
-    int64_t n_out[4];
-    float *y[4];           /* outputs (device) */
-    int64_t n_in;          /* a multiple of 256, <= 65536 */
-    const float *x;        /* activation (device): the caller's or an earlier stage's y */
-    int all_reduce;        /* 1: y[0] = sum over the group of this rank's row-split product */
-} sicu_chain_stage;
-typedef struct sicu_chain sicu_chain;
-SICU_API int sicu_chain_create(const sicu_chain_stage *stages, int n_stages, sicu_ar *group, sicu_chain **chain);
-SICU_API int sicu_chain_run(sicu_chain *chain, void *stream);
-SICU_API int sicu_chain_destroy(sicu_chain *chain);
-
 /* ---- dequantisation --------------------------------------------------------
  * Rows rows[0..nrows) (host array) of W into dout[nrows][n_in] f32, reference
  * semantics. Replaces cpu_row_to_f32 (src/backend.c:122-131) with

@@ -5,7 +5,6 @@
 #include <cstdio>
 #include <cstring>
 #include <mutex>
-#include <vector>
 
 #include "siphon_cuda.h"
 #include "common.cuh"
@@ -666,117 +665,6 @@ int sicu_gemv_ar(uint32_t wtype, const void *dw, int64_t n_in, int64_t n_out, co
     L.xf = dx;
     L.ar = g->d;
     return run_gemv(wtype, L, (cudaStream_t)stream);
-}
-
-// ---- chains of dependent matvecs in one launch ------------------------------------
-}  // extern "C"
-
-struct sicu_chain {
-    ChainParams p{};
-    ChainLaunch L{};
-    ChainStage *dst = nullptr;   // device copy of the stages
-    unsigned *barrier = nullptr;
-    int device = -1;
-};
-
-extern "C" {
-
-int sicu_chain_create(const sicu_chain_stage *stages, int n_stages, sicu_ar *group, sicu_chain **out) {
-    if (!out) return fail(SICU_EINVAL, "chain: null out pointer");
-    *out = nullptr;
-    if (!stages || n_stages < 1 || n_stages > 4096) return fail(SICU_EINVAL, "chain: %d stages (1..4096)", n_stages);
-    DevState *ds;
-    if (int rc = current(ds)) return rc;
-    if (group) {
-        int dev = -1;
-        cudaGetDevice(&dev);
-        if (!group->opened) return fail(SICU_EINVAL, "chain: group not opened (sicu_ar_open)");
-        if (dev != group->device) return fail(SICU_EINVAL, "chain: group belongs to device %d", group->device);
-    }
-    std::vector<ChainStage> st((size_t)n_stages);
-    for (int i = 0; i < n_stages; ++i) {
-        const sicu_chain_stage &a = stages[i];
-        ChainStage &c = st[(size_t)i];
-        c = ChainStage{};
-        if (a.wtype != T_Q4_K && a.wtype != T_Q6_K)
-            return fail(SICU_ENOTSUP, "chain stage %d: %s weights (Q4_K and Q6_K only)", i, tname(a.wtype));
-        if (a.n_mats < 1 || a.n_mats > CHAIN_MAX_MATS)
-            return fail(SICU_EINVAL, "chain stage %d: %d matrices (1..%d)", i, a.n_mats, CHAIN_MAX_MATS);
-        if (a.n_in <= 0 || a.n_in % 256 || a.n_in > 65536)
-            return fail(SICU_EINVAL, "chain stage %d: row length %lld (a multiple of 256, <= 65536)", i, (long long)a.n_in);
-        if (!a.x || !aligned(a.x, 16)) return fail(SICU_EINVAL, "chain stage %d: activation null or not 16-byte aligned", i);
-        for (int k = 0; k < a.n_mats; ++k) {
-            if (a.n_out[k] < 1 || a.n_out[k] > ((int64_t)1 << 24))
-                return fail(SICU_EINVAL, "chain stage %d: matrix %d has %lld rows", i, k, (long long)a.n_out[k]);
-            if (!a.w[k] || !aligned(a.w[k], 16)) return fail(SICU_EINVAL, "chain stage %d: weights null or misaligned", i);
-            if (!a.y[k] || !aligned(a.y[k], 4)) return fail(SICU_EINVAL, "chain stage %d: output null or misaligned", i);
-            c.w[k] = static_cast<const uint8_t *>(a.w[k]);
-            c.y[k] = a.y[k];
-            c.n_out[k] = (int)a.n_out[k];
-        }
-        if (a.all_reduce) {
-            if (!group) return fail(SICU_EINVAL, "chain stage %d: an all-reduce stage needs a group", i);
-            if (a.n_mats != 1 || a.n_out[0] != group->d.len)
-                return fail(SICU_EINVAL, "chain stage %d: an all-reduce stage has one matrix of the group's %lld rows", i,
-                            (long long)group->d.len);
-        }
-        c.type = a.wtype;
-        c.nmat = a.n_mats;
-        c.x = a.x;
-        c.n_in = (int)a.n_in;
-        c.ar = a.all_reduce ? 1 : 0;
-    }
-    ChainParams p{};
-    ChainLaunch L{};
-    L.num_sms = ds->sms;
-    L.smem_per_sm = ds->smem_per_sm;
-    L.smem_reserved = ds->smem_reserved;
-    const int rc = chain_prepare(st.data(), n_stages, p, L);
-    if (rc == -1) return fail(SICU_ENOTSUP, "chain: a stage's rows do not fit the kernel's shared memory");
-    if (rc) return cuda_fail(cudaGetLastError(), "chain: launch geometry");
-    sicu_chain *c = new sicu_chain;
-    cudaGetDevice(&c->device);
-    cudaError_t e;
-    if ((e = cudaMalloc(&c->dst, sizeof(ChainStage) * (size_t)n_stages)) != cudaSuccess ||
-        (e = cudaMalloc(&c->barrier, sizeof(unsigned))) != cudaSuccess ||
-        (e = cudaMemcpy(c->dst, st.data(), sizeof(ChainStage) * (size_t)n_stages, cudaMemcpyHostToDevice)) != cudaSuccess) {
-        if (c->dst) cudaFree(c->dst);
-        if (c->barrier) cudaFree(c->barrier);
-        delete c;
-        return e == cudaErrorMemoryAllocation ? fail(SICU_ENOMEM, "chain: stage table") : cuda_fail(e, "chain: create");
-    }
-    p.st = c->dst;
-    p.barrier = c->barrier;
-    p.status = ds->status;
-    if (group) p.ar = group->d;
-    c->p = p;
-    c->L = L;
-    *out = c;
-    return SICU_OK;
-}
-
-int sicu_chain_run(sicu_chain *c, void *stream) {
-    if (!c) return fail(SICU_EINVAL, "chain: null chain");
-    DevState *ds;
-    if (int rc = current(ds)) return rc;
-    int dev = -1;
-    cudaGetDevice(&dev);
-    if (dev != c->device) return fail(SICU_EINVAL, "chain: belongs to device %d, current is %d", c->device, dev);
-    if (launch_chain(c->p, c->L, (cudaStream_t)stream)) return cuda_fail(cudaGetLastError(), "chain launch");
-    return SICU_OK;
-}
-
-int sicu_chain_destroy(sicu_chain *c) {
-    if (!c) return SICU_OK;
-    int cur = -1;
-    cudaGetDevice(&cur);
-    if (c->device >= 0) cudaSetDevice(c->device);
-    cudaDeviceSynchronize();
-    cudaFree(c->dst);
-    cudaFree(c->barrier);
-    if (cur >= 0) cudaSetDevice(cur);
-    delete c;
-    return SICU_OK;
 }
 
 int sicu_row_to_f32(uint32_t wtype, const void *dw, int64_t n_in, const int64_t *rows, int64_t nrows, float *dout,

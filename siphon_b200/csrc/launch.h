@@ -83,38 +83,6 @@ size_t prefill_workspace_bytes(uint32_t wtype, int64_t n_in, int64_t n_out, int6
 // -3: no tensor-core kernel for the type; -4: tensor map encoding failed; -2: launch
 int launch_prefill(uint32_t wtype, const PrefillLaunch &L, cudaStream_t st);
 
-// ---- chains of dependent matvecs in one persistent launch (chain.cu) ----
-constexpr int CHAIN_MAX_MATS = 4;
-struct ChainStage {
-    uint32_t type;                      // T_Q4_K or T_Q6_K
-    int nmat;
-    const uint8_t *w[CHAIN_MAX_MATS];
-    float *y[CHAIN_MAX_MATS];
-    int n_out[CHAIN_MAX_MATS];
-    int task0[CHAIN_MAX_MATS + 1];      // first task of each matrix
-    const float *x;                     // f32 activation (device)
-    int n_in, nu, cu, nchunks, rows_per_task, ntasks, unit_bytes;
-    int64_t row_bytes;
-    int ar;                             // 1: row-split stage, all-reduced over the chain's group
-    int ar_index;                       // its position among the chain's all-reduce stages
-};
-struct ChainParams {
-    const ChainStage *st;               // device copy of the stages
-    int nstages, n_ar, max_nu;
-    int slot_bytes, nslots, act_bytes, warp_bytes;
-    unsigned *barrier;                  // grid barrier counter, zeroed before every launch
-    int *status;
-    ArDev ar;                           // the group (n = 0: none)
-};
-struct ChainLaunch {
-    int num_sms, smem_per_sm, smem_reserved;   // in
-    int grid, threads, smem;                    // out
-};
-// geometry, shared-memory layout and grid of a chain (fills st[] and p);
-// -1: a stage's items do not fit, -2: CUDA error
-int chain_prepare(ChainStage *st, int n, ChainParams &p, ChainLaunch &L);
-int launch_chain(const ChainParams &p, const ChainLaunch &L, cudaStream_t st);
-
 // all-reduce of src[len] into dst[len] over the group (one delivery)
 int launch_allreduce(const ArDev &a, const float *src, float *dst, int *status, int num_sms, cudaStream_t st);
 

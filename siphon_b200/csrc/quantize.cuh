@@ -117,11 +117,8 @@ __device__ __forceinline__ void q8_0_block(const float *x, uint32_t &d16, uint32
 // CTA of the cluster. K formats: eight lanes per 256-element block, lane j
 // owning elements 32j..32j+31, so after one 3-step max reduction every lane
 // emits its own piece. Classic formats: one thread per 32-element block.
-// CG: read x through L2 only (it was written by other CTAs of the same
-// kernel, so an L1 line from an earlier read could be stale). K formats only.
-template <int ACT, bool CG = false>
+template <int ACT>
 __device__ void quantize_into_act(const ActView av, const float *xf, int n_in, uint32_t rank, uint32_t nrank) {
-    static_assert(!CG || ACT != 3, "L2-only activation reads are for the K formats");
     const RecWriter wr{nrank};
     if constexpr (ACT == 3) {
         const int nblk = n_in / 32, nu = (nblk + 7) / 8;
@@ -146,7 +143,7 @@ __device__ void quantize_into_act(const ActView av, const float *xf, int n_in, u
             float v[32];
 #pragma unroll
             for (int k = 0; k < 8; ++k) {
-                const float4 f = CG ? __ldcg(src + k) : src[k];
+                const float4 f = src[k];
                 v[4 * k] = f.x; v[4 * k + 1] = f.y; v[4 * k + 2] = f.z; v[4 * k + 3] = f.w;
             }
             // first element of largest magnitude (strict '>' keeps the earliest)

@@ -57,18 +57,7 @@ SIGNATURES = {
     "sicu_ar_destroy": [_vp],
     "sicu_ar_allreduce": [_vp, _fp, _fp, _vp],
     "sicu_gemv_ar": [_u32, _vp, _i64, _i64, _fp, _fp, _vp, _vp],
-    "sicu_chain_create": [_vp, C.c_int, _vp, C.POINTER(C.c_void_p)],
-    "sicu_chain_run": [_vp, _vp],
-    "sicu_chain_destroy": [_vp],
 }
-
-
-
-class ChainStage(C.Structure):
-    """sicu_chain_stage (include/siphon_cuda.h)."""
-    _fields_ = [("wtype", C.c_uint32), ("n_mats", C.c_int), ("w", C.c_void_p * 4), ("n_out", C.c_int64 * 4),
-                ("y", C.c_void_p * 4), ("n_in", C.c_int64), ("x", C.c_void_p), ("all_reduce", C.c_int)]
-
 
 AR_HANDLE_BYTES = 64
 STATUS_WAIT_TIMEOUT, STATUS_AR_TIMEOUT = 1, 2
@@ -186,12 +175,6 @@ class SiphonCuda:
         self.check(self.lib.sicu_gemv_ar(wtype, _ptr(dw), n_in, n_out, _ptr(dx), _ptr(dy), group.handle,
                                          _ptr(stream)))
 
-    # -- chains of dependent matvecs in one launch ----------------------------------
-    def chain_create(self, stages, group: "ArGroup | None" = None) -> "Chain":
-        """stages: dicts with wtype, w (list), n_out (list), y (list), n_in, x
-        and optionally all_reduce (bool)."""
-        return Chain(self, stages, group)
-
     def row_to_f32(self, wtype: int, dw, n_in: int, rows, dout, stream=None) -> None:
         arr = (C.c_int64 * len(rows))(*rows)
         self.check(self.lib.sicu_row_to_f32(wtype, _ptr(dw), n_in, arr, len(rows), _ptr(dout), _ptr(stream)))
@@ -234,37 +217,6 @@ class ArGroup:
     def destroy(self) -> None:
         if self.handle:
             self.s.check(self.s.lib.sicu_ar_destroy(self.handle))
-            self.handle = None
-
-
-class Chain:
-    """A planned sequence of matvec stages run as one launch (sicu_chain_*).
-    The tensors named in the stages must outlive the chain."""
-
-    def __init__(self, sicu: SiphonCuda, stages, group: ArGroup | None = None):
-        self.s = sicu
-        arr = (ChainStage * len(stages))()
-        self._keep = []
-        for i, st in enumerate(stages):
-            a = arr[i]
-            a.wtype = st["wtype"]
-            a.n_mats = len(st["w"])
-            for k, (w, n, y) in enumerate(zip(st["w"], st["n_out"], st["y"])):
-                a.w[k], a.n_out[k], a.y[k] = _ptr(w), n, _ptr(y)
-            a.n_in = st["n_in"]
-            a.x = _ptr(st["x"])
-            a.all_reduce = 1 if st.get("all_reduce") else 0
-            self._keep.append(st)
-        h = C.c_void_p()
-        sicu.check(sicu.lib.sicu_chain_create(arr, len(stages), group.handle if group else None, C.byref(h)))
-        self.handle = h.value
-
-    def run(self, stream=None) -> None:
-        self.s.check(self.s.lib.sicu_chain_run(self.handle, _ptr(stream)))
-
-    def destroy(self) -> None:
-        if self.handle:
-            self.s.check(self.s.lib.sicu_chain_destroy(self.handle))
             self.handle = None
 
 

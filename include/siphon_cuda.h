@@ -186,8 +186,11 @@ SICU_API int sicu_gemv_host_noalloc(uint32_t wtype, const void *dw, int64_t n_in
  * run the decode matvec once per token (bit-identical to the reference).
  * The reference has no batched product: its prompt loop calls
  * si_engine_forward once per token (src/cmd_run.c:276), i.e. one backend gemv
- * per token and matrix. A per-device workspace grows on the first call with a
- * larger m x n_in; make that call before any stream capture. */
+ * per token and matrix. When a product has fewer 128-row x token tiles than
+ * the GPU has SMs, each row's super-blocks are split into ranges computed by
+ * separate CTAs and their partial products added in a fixed order (same bits
+ * on every run). A per-device workspace grows on the first call with a larger
+ * m, n_in or n_out; make that call before any stream capture. */
 SICU_API int sicu_gemm_prefill(uint32_t wtype, const void *dw, int64_t n_in, int64_t n_out,
                                const void *dxq, int64_t m, float *dy, void *stream);
 SICU_API int sicu_gemm_prefill_f32(uint32_t wtype, const void *dw, int64_t n_in, int64_t n_out,

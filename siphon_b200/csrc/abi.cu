@@ -492,7 +492,7 @@ static int prefill_common(uint32_t wtype, const void *dw, int64_t n_in, int64_t 
         return SICU_OK;
     }
     const size_t qbytes = xq ? 0 : (((size_t)m * pair_row_bytes(pair, n_in) + 255) & ~size_t(255));
-    if (int rc = grow_prefill_ws(*ds, qbytes + prefill_workspace_bytes(wtype, n_in, n_out, m))) return rc;
+    if (int rc = grow_prefill_ws(*ds, qbytes + prefill_workspace_bytes(wtype, n_in, n_out, m, ds->sms))) return rc;
     if (!xq) {
         if (launch_quantize(pair, xf, ds->pf_ws, n_in, m, st) != 0) return cuda_fail(cudaGetLastError(), "prefill quantize");
         xq = ds->pf_ws;
@@ -506,6 +506,7 @@ static int prefill_common(uint32_t wtype, const void *dw, int64_t n_in, int64_t 
     L.y = dy;
     L.ws = static_cast<uint8_t *>(ds->pf_ws) + qbytes;
     cudaGetDevice(&L.device);
+    L.num_sms = ds->sms;
     L.status = ds->status;
     const int rc = launch_prefill(wtype, L, st);
     if (rc == -4) return fail(SICU_EIO, "prefill: tensor map encoding failed");

@@ -74,12 +74,13 @@ struct PrefillLaunch {
     const void *xq;       // m rows of Q8_K blocks (device)
     int64_t m;
     float *y;             // [m][n_out] (device)
-    void *ws;             // prefill_workspace_bytes(wtype, n_in, n_out, m) bytes, 256-byte aligned
+    void *ws;             // prefill_workspace_bytes(wtype, n_in, n_out, m, num_sms) bytes, 256-byte aligned
     int device;
+    int num_sms;
     int *status;
 };
 bool prefill_supported(uint32_t wtype);
-size_t prefill_workspace_bytes(uint32_t wtype, int64_t n_in, int64_t n_out, int64_t m);
+size_t prefill_workspace_bytes(uint32_t wtype, int64_t n_in, int64_t n_out, int64_t m, int num_sms);
 // -3: no tensor-core kernel for the type; -4: tensor map encoding failed; -2: launch
 int launch_prefill(uint32_t wtype, const PrefillLaunch &L, cudaStream_t st);
 

@@ -121,6 +121,9 @@ __device__ __forceinline__ uint32_t use_of(int t) { return (uint32_t)(t / PF_STA
 struct PfParams {
     int n_out;
     int nsb;              // super-blocks per row
+    int nsplit;           // the row's super-blocks split into this many ranges (one CTA each)
+    int sb_per_split;
+    float *part;          // nsplit > 1: [nsplit][m][n_out] partial products, summed afterwards
     const float *da;      // [nsb][m_pad] token scales
     float *y;             // [m][n_out]
     int m, m_pad;
@@ -293,11 +296,11 @@ __device__ __forceinline__ bool convert_q4k(const PfCtx &cx, uint32_t base, uint
 // ql[64h + 32g + l] (low nibble for even cq, high for odd), qh[32h + l] bits
 // 2G'..2G'+1, scale sc[4cq + 2g + l / 16].
 template <class Lay>
-__device__ __forceinline__ bool convert_q6k(const PfCtx &cx, uint32_t base, uint32_t tl, int sb, int rb, int b4,
-                                            int r, int G, bool valid, uint32_t barbase) {
+__device__ __forceinline__ bool convert_q6k(const PfCtx &cx, uint32_t base, uint32_t tl, int sb, int gsb, int rb,
+                                            int b4, int r, int G, bool valid, uint32_t barbase) {
     constexpr uint32_t FULL = 0xffffffffu;
     auto bar = [&](int i) { return barbase + 8u * (uint32_t)i; };
-    const int head = (int)(((int64_t)sb * B_Q6_K) & 15);
+    const int head = (int)(((int64_t)gsb * B_Q6_K) & 15);
     const uint32_t row = base + Lay::OFF_RAW + rb * Lay::RAW_BUF + r * PfFmt<T_Q6_K>::RAW_ROW;
     // scales (bytes 192..207) and d (208..209)
     uint32_t S[5];
@@ -379,10 +382,16 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const uint32_t sb0 = smem_addr(smem);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int rt = blockIdx.x / p.ntt, tt = blockIdx.x - rt * p.ntt;
+    // blockIdx: split-major over (row tile, token tile); this CTA's super-blocks
+    // are sbb .. sbb + nsb - 1 (sb below counts from 0 within them)
+    const int ntiles = (int)(gridDim.x / (unsigned)p.nsplit);
+    const int split = blockIdx.x / ntiles, tile = blockIdx.x - split * ntiles;
+    const int rt = tile / p.ntt, tt = tile - rt * p.ntt;
     const int row0 = rt * PF_BM, tok0 = tt * BN;
     const int rows = min(PF_BM, p.n_out - row0);
-    const int nsb = p.nsb;
+    const int sbb = split * p.sb_per_split;
+    const int nsb = min(p.sb_per_split, p.nsb - sbb);
+    float *const yout = p.nsplit > 1 ? p.part + (size_t)split * p.m * p.n_out : p.y;
     volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + Lay::OFF_FLAGS);
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + Lay::OFF_FLAGS + 4);
     const uint32_t barbase = sb0 + Lay::OFF_BAR;
@@ -432,8 +441,8 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
                 if (!pf_wait(bar(BAR_SB_FREE + b4), ((sb / PF_NSB) & 1) ^ 1, abort_flag, p.status)) break;
                 mbar_expect_tx(bar(BAR_SBD_FULL + b4), (F::MINS ? min_bytes(BN) : 0) + BN * 4);
                 if constexpr (F::MINS)
-                    tma_load_2d(sb0 + Lay::OFF_B2 + b4 * min_bytes(BN), &tmS, 16 * sb, tok0, bar(BAR_SBD_FULL + b4));
-                bulk_g2s(sb0 + Lay::OFF_DA + b4 * BN * 4, p.da + (size_t)sb * p.m_pad + tok0, BN * 4,
+                    tma_load_2d(sb0 + Lay::OFF_B2 + b4 * min_bytes(BN), &tmS, 16 * (sbb + sb), tok0, bar(BAR_SBD_FULL + b4));
+                bulk_g2s(sb0 + Lay::OFF_DA + b4 * BN * 4, p.da + (size_t)(sbb + sb) * p.m_pad + tok0, BN * 4,
                          bar(BAR_SBD_FULL + b4));
                 sb_issued = sb + 1;
                 bool ok = true;
@@ -441,7 +450,8 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
                     const int t = KST * sb + c, s = stage_of(t);
                     if (!pf_wait(bar(BAR_ST_EMPTY + s), use_of(t) ^ 1, abort_flag, p.status)) { ok = false; break; }
                     mbar_expect_tx(bar(BAR_B_FULL + s), stage_bytes(BN));
-                    tma_load_2d(sb0 + Lay::OFF_B + s * stage_bytes(BN), &tmB, PF_KS * t, tok0, bar(BAR_B_FULL + s));
+                    tma_load_2d(sb0 + Lay::OFF_B + s * stage_bytes(BN), &tmB, PF_KS * (KST * sbb + t), tok0,
+                                bar(BAR_B_FULL + s));
                     t_issued = t + 1;
                 }
                 if (!ok) break;
@@ -503,8 +513,8 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
                 const int rb = sb % F::NRAW;
                 if (!pf_wait(bar(BAR_RAW_EMPTY + rb), ((sb / F::NRAW) & 1) ^ 1, abort_flag, p.status)) break;
                 mbar_expect_tx(bar(BAR_RAW_FULL + rb), Lay::RAW_BUF);
-                tma_load_2d(sb0 + Lay::OFF_RAW + rb * Lay::RAW_BUF, &tmW, (int)(((int64_t)sb * F::BLOCK) & ~int64_t(15)),
-                            row0, bar(BAR_RAW_FULL + rb));
+                tma_load_2d(sb0 + Lay::OFF_RAW + rb * Lay::RAW_BUF, &tmW,
+                            (int)(((int64_t)(sbb + sb) * F::BLOCK) & ~int64_t(15)), row0, bar(BAR_RAW_FULL + rb));
                 sb_issued = sb + 1;
             }
             if (*abort_flag)
@@ -525,7 +535,7 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
             if (!__all_sync(FULL, pf_wait(bar(BAR_SB_FREE + b4), ((sb / PF_NSB) & 1) ^ 1, abort_flag, p.status))) break;
             bool ok;
             if constexpr (T == T_Q4_K) ok = convert_q4k<Lay>(cx, sb0, tl, sb, rb, b4, r, grp, valid, barbase);
-            else ok = convert_q6k<Lay>(cx, sb0, tl, sb, rb, b4, r, grp, valid, barbase);
+            else ok = convert_q6k<Lay>(cx, sb0, tl, sb, sbb + sb, rb, b4, r, grp, valid, barbase);
             if (!ok) break;
             __syncwarp();
             if (lane == 0) mbar_arrive(bar(BAR_RAW_EMPTY + rb));
@@ -576,7 +586,7 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
             }
         }
         if (ok && !*abort_flag && r < rows) {
-            float *yr = p.y + row0 + r;
+            float *yr = yout + row0 + r;
 #pragma unroll
             for (int j = 0; j < EPI_COLS; ++j)
                 if (tok0 + c0 + j < p.m) yr[(int64_t)(tok0 + c0 + j) * p.n_out] = acc[j];
@@ -627,6 +637,16 @@ __global__ void prefill_prep_q8k(const uint8_t *xq, int m, int nsb, int m_pad, u
     }
 }
 
+// Y = the splits' partial products added in split order (one f32 add per
+// split, the same order on every run)
+__global__ void prefill_sum_splits(const float *part, int nsplit, int64_t n, float *y) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        float a = part[i];
+        for (int k = 1; k < nsplit; ++k) a = __fadd_rn(a, part[(int64_t)k * n + i]);
+        y[i] = a;
+    }
+}
+
 // Weight rows whose byte length is not a multiple of 16 (Q6_K with a
 // super-block count that is not a multiple of 8) cannot be described by a
 // tensor map; they are copied to rows of `stride` bytes first.
@@ -668,10 +688,41 @@ bool make_map(CUtensorMap *map, const void *base, uint64_t cols, uint64_t rows, 
 
 size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 
+// Super-block ranges per row: when a product's 128-row x token tiles fill the
+// SMs in few or ragged waves (the kernel holds one SM per CTA), splitting each
+// row's super-blocks over s CTAs shortens the busiest SM's work; the partial
+// products then cost s x m x n_out x 8 bytes of traffic (written, read back
+// and added). s minimises (waves / s) x per-tile time + that traffic, with a
+// tile costing ~2.5 us per super-block and traffic at ~5 TB/s (measured
+// orders of magnitude; only the comparison matters). The split changes only
+// the float order in which super-blocks are added.
+int split_count(int64_t n_in, int64_t n_out, int64_t m, int num_sms) {
+    const int64_t bn = m <= PF_BN_SMALL ? PF_BN_SMALL : PF_BN;
+    const int64_t tiles = (n_out + PF_BM - 1) / PF_BM * ((m + bn - 1) / bn);
+    const int64_t nsb = n_in / QK_K;
+    if (num_sms <= 0 || tiles <= 0) return 1;
+    const double tile_us = 2.5 * (double)nsb;
+    auto cost = [&](int s) {
+        const double waves = (double)((tiles * s + num_sms - 1) / num_sms) / s;
+        const double traffic_us = s > 1 ? (double)s * m * n_out * 8.0 / 5e6 : 0.0;
+        return waves * tile_us + traffic_us;
+    };
+    int best = 1;
+    double best_c = cost(1);
+    for (int s = 2; s <= 8 && nsb / s >= 4; ++s) {
+        const double c = cost(s);
+        if (c < best_c * 0.97) {
+            best_c = c;
+            best = s;
+        }
+    }
+    return best;
+}
+
 struct WsParts {
-    size_t b, s, da, pad;
+    size_t b, s, da, pad, part;
 };
-WsParts ws_parts(uint32_t wtype, int64_t n_in, int64_t n_out, int64_t m) {
+WsParts ws_parts(uint32_t wtype, int64_t n_in, int64_t n_out, int64_t m, int num_sms) {
     const int64_t m_pad = (m + PF_BN - 1) / PF_BN * PF_BN;
     const int planes = wtype == T_Q6_K ? 2 : 1;
     WsParts w{};
@@ -680,6 +731,8 @@ WsParts ws_parts(uint32_t wtype, int64_t n_in, int64_t n_out, int64_t m) {
     w.da = align256((size_t)(n_in / QK_K) * m_pad * 4);
     const int64_t rb = n_in / QK_K * B_Q6_K;
     w.pad = (wtype == T_Q6_K && rb % 16) ? align256((size_t)n_out * ((rb + 15) & ~int64_t(15))) : 0;
+    const int ns = split_count(n_in, n_out, m, num_sms);
+    w.part = ns > 1 ? align256((size_t)ns * m * n_out * 4) : 0;
     return w;
 }
 
@@ -689,7 +742,7 @@ int launch_tb(const PrefillLaunch &L, cudaStream_t st) {
     using Lay = PfLayout<T, BN>;
     const int64_t K = L.n_in, nsb = K / QK_K;
     const int64_t m_pad = (L.m + BN - 1) / BN * BN;
-    const WsParts parts = ws_parts(T, L.n_in, L.n_out, L.m);
+    const WsParts parts = ws_parts(T, L.n_in, L.n_out, L.m, L.num_sms);
     uint8_t *ws = static_cast<uint8_t *>(L.ws);
     uint16_t *B = reinterpret_cast<uint16_t *>(ws);
     uint16_t *S = F::MINS ? reinterpret_cast<uint16_t *>(ws + parts.b) : nullptr;
@@ -739,9 +792,19 @@ int launch_tb(const PrefillLaunch &L, cudaStream_t st) {
     p.m_pad = (int)m_pad;
     p.ntt = (int)(m_pad / BN);
     p.status = L.status;
+    p.nsplit = split_count(L.n_in, L.n_out, L.m, L.num_sms);
+    p.sb_per_split = (int)((nsb + p.nsplit - 1) / p.nsplit);
+    p.nsplit = (int)((nsb + p.sb_per_split - 1) / p.sb_per_split);   // no empty range
+    p.part = p.nsplit > 1 ? reinterpret_cast<float *>(ws + parts.b + parts.s + parts.da + parts.pad) : nullptr;
     const int64_t tiles = (L.n_out + PF_BM - 1) / PF_BM * p.ntt;
-    prefill_kernel<T, BN><<<(unsigned)tiles, PF_WARPS * 32, Lay::SMEM, st>>>(tmW, tmB, tmS, p);
+    prefill_kernel<T, BN><<<(unsigned)(tiles * p.nsplit), PF_WARPS * 32, Lay::SMEM, st>>>(tmW, tmB, tmS, p);
     if (cudaGetLastError() != cudaSuccess) return -2;
+    if (p.nsplit > 1) {
+        const int64_t n = L.m * L.n_out;
+        const int64_t blocks = (n + 255) / 256 < 4 * L.num_sms ? (n + 255) / 256 : 4 * L.num_sms;
+        prefill_sum_splits<<<(unsigned)blocks, 256, 0, st>>>(p.part, p.nsplit, n, L.y);
+        if (cudaGetLastError() != cudaSuccess) return -2;
+    }
     return 0;
 }
 
@@ -756,9 +819,9 @@ int launch_t(const PrefillLaunch &L, cudaStream_t st) {
 
 bool prefill_supported(uint32_t wtype) { return wtype == T_Q4_K || wtype == T_Q6_K; }
 
-size_t prefill_workspace_bytes(uint32_t wtype, int64_t n_in, int64_t n_out, int64_t m) {
-    const WsParts w = ws_parts(wtype, n_in, n_out, m);
-    return w.b + w.s + w.da + w.pad;
+size_t prefill_workspace_bytes(uint32_t wtype, int64_t n_in, int64_t n_out, int64_t m, int num_sms) {
+    const WsParts w = ws_parts(wtype, n_in, n_out, m, num_sms);
+    return w.b + w.s + w.da + w.pad + w.part;
 }
 
 int launch_prefill(uint32_t wtype, const PrefillLaunch &L, cudaStream_t st) {

@@ -179,3 +179,20 @@ def test_prefill_empty_and_errors(sicu):
     with pytest.raises(SicuError):
         sicu.gemm_prefill_f32(Q.Q4_K, w, 256, 128, x, 70000, y)
     assert sicu.status() == 0
+
+
+@pytest.mark.parametrize("wt,n_out,n_in,m", [
+    (Q.Q4_K, 256, 8192, 8),      # two row tiles, 32 super-blocks: the row split into ranges
+    (Q.Q6_K, 200, 5632, 5),      # 22 super-blocks, ragged rows, padded Q6_K rows
+    (Q.Q4_K, 640, 4096, 300),    # prompt tiles with the split
+])
+def test_prefill_split_rows(sicu, oracle, wt, n_out, n_in, m):
+    """Launches with few tiles split each row's super-blocks across CTAs and
+    add the partial products afterwards: within the tolerance, and the same
+    bits on every run (the partials are added in a fixed order)."""
+    w, x, xq, want, got = _run(sicu, oracle, wt, n_out, n_in, m, seed=n_in + m)
+    l1 = np.abs(_dequant_q8k(xq, n_in)) @ np.abs(_dequant_w(oracle, wt, w, n_in, n_out)).T
+    _check_tol(got, want, l1, f"{Q.NAMES[wt]} prefill {n_out}x{n_in} m={m} (split)")
+    y2 = empty_f32(m, n_out)
+    sicu.gemm_prefill(wt, dev(w), n_in, n_out, dev(xq), m, y2)
+    assert_bits_equal(host(y2), got, "second run")

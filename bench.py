@@ -638,7 +638,8 @@ def run_ours(args, world, rank, local) -> None:
                      "traffic": traffic, "algorithmic_bytes_per_launch": round(per_launch),
                      "traffic_source": NCU_TRAFFIC.get("source")},
         "e2e": {"value": round(e2e_value, 1), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "path": "sicu_gemv_host per matvec (pinned host x in, host y out, stream sync per call)"},
+                "path": "sicu_gemv_host per matvec (page-locked host x and y, read and written by the GPU "
+                        "directly; stream sync per call)"},
         "gpu_launches": args.steps * len(SHAPES),
         "clocks": clk.summary(),
     }

@@ -150,7 +150,11 @@ SICU_API int sicu_gemv_multi(uint32_t wtype, int n_mats, const void *const *dw, 
                              int64_t n_in, const float *dx, float *const *dy, void *stream);
 /* Same, with host input and output buffers (one activation row): copies x
  * in, runs sicu_gemv_f32, copies y out and waits. This is the exact call
- * shape of the reference's backend gemv slot. */
+ * shape of the reference's backend gemv slot. When both buffers are
+ * page-locked (cudaHostAlloc / cudaHostRegister) and the type is quantized,
+ * the GPU reads x and writes y through their device views instead of two
+ * copy-engine transfers, and the matvec starts streaming its weights while x
+ * is being read; results are identical. */
 SICU_API int sicu_gemv_host(uint32_t wtype, const void *dw, int64_t n_in, int64_t n_out,
                    const float *hx, float *hy, void *stream);
 

@@ -427,6 +427,27 @@ int sicu_gemv_host(uint32_t wtype, const void *dw, int64_t n_in, int64_t n_out, 
     float *dx = static_cast<float *>(ds->stage);
     float *dy = reinterpret_cast<float *>(static_cast<uint8_t *>(ds->stage) + xb);
     const cudaStream_t st = (cudaStream_t)stream;
+    // page-locked x and y (and a quantized format): the GPU reads x and writes
+    // y through their device views, with no copy-engine operation: a small
+    // kernel copies x and the matvec, launched behind it, streams its weights
+    // meanwhile (the call's latency, not its bandwidth, sets its time)
+    cudaPointerAttributes ax{}, ay{};
+    const bool direct = wtype != T_F16 && n_out > 0 && n_in % 4 == 0 &&
+                        cudaPointerGetAttributes(&ax, hx) == cudaSuccess && ax.type == cudaMemoryTypeHost &&
+                        ax.devicePointer && aligned(ax.devicePointer, 16) &&
+                        cudaPointerGetAttributes(&ay, hy) == cudaSuccess && ay.type == cudaMemoryTypeHost &&
+                        ay.devicePointer;
+    cudaGetLastError();
+    if (direct) {
+        if (launch_host_copy(static_cast<const float *>(ax.devicePointer), dx, n_in, st))
+            return cuda_fail(cudaGetLastError(), "gemv_host copy");
+        GemvLaunch L = make_launch(*ds, dw, n_in, n_out, static_cast<float *>(ay.devicePointer));
+        L.xf = dx;
+        L.overlap = 1;
+        if (int rc = run_gemv(wtype, L, st)) return rc;
+        if ((e = cudaStreamSynchronize(st)) != cudaSuccess) return cuda_fail(e, "gemv_host sync");
+        return SICU_OK;
+    }
     if ((e = cudaMemcpyAsync(dx, hx, (size_t)n_in * 4, cudaMemcpyHostToDevice, st)) != cudaSuccess)
         return cuda_fail(e, "gemv_host h2d");
     if (n_out > 0) {

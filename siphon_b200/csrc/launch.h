@@ -64,6 +64,10 @@ int launch_gemv(uint32_t wtype, const GemvLaunch &L, cudaStream_t st);
 // F16 weights (pair activation: f16 row, or f32 converted in the kernel)
 int launch_gemv_f16(const GemvLaunch &L, cudaStream_t st);
 
+// n floats (a multiple of 4, 16-byte aligned) from the device view of
+// page-locked host memory into device memory
+int launch_host_copy(const float *src, float *dst, int64_t n, cudaStream_t st);
+
 // activation conversion of m rows of n floats into the pair format
 int launch_quantize(uint32_t pair, const float *x, void *y, int64_t n, int64_t m, cudaStream_t st);
 

@@ -29,6 +29,15 @@ __global__ void __launch_bounds__(256) quant_q80_kernel(const float *x, uint8_t 
     }
 }
 
+// n floats from page-locked host memory (its device view) into device
+// memory, one 16-byte load per thread; lets the next kernel (programmatic
+// dependent launch) start streaming its weights right away
+__global__ void __launch_bounds__(256) host_copy_kernel(const float4 *src, float4 *dst, int64_t n4) {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n4) dst[i] = src[i];
+}
+
 __global__ void __launch_bounds__(256) convert_f16_kernel(const float *x, uint16_t *y, int64_t n) {
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
         y[i] = f2h(x[i]);
@@ -117,6 +126,13 @@ __global__ void __launch_bounds__(256) dequant_kernel(uint32_t t, const uint8_t 
 }
 
 }  // namespace
+
+int launch_host_copy(const float *src, float *dst, int64_t n, cudaStream_t st) {
+    const int64_t n4 = n / 4;
+    host_copy_kernel<<<(unsigned)((n4 + 255) / 256), 256, 0, st>>>(reinterpret_cast<const float4 *>(src),
+                                                                    reinterpret_cast<float4 *>(dst), n4);
+    return cudaPeekAtLastError() == cudaSuccess ? 0 : -2;
+}
 
 int launch_quantize(uint32_t pair, const float *x, void *y, int64_t n, int64_t m, cudaStream_t st) {
     if (pair == T_Q8_K) {

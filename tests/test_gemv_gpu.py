@@ -114,6 +114,28 @@ def test_host_buffers(sicu, oracle):
     assert_bits_equal(hy, want, "gemv_host")
 
 
+@pytest.mark.parametrize("wt,n_out,n_in", [(Q.Q6_K, 300, 2048), (Q.Q4_K, 5000, 5120), (Q.Q8_0, 77, 1024),
+                                           (Q.F16, 64, 512)])
+def test_host_buffers_page_locked(sicu, oracle, wt, n_out, n_in):
+    """Page-locked host buffers take the path where the GPU reads x and
+    writes y in host memory directly; pageable ones the copy-engine path.
+    Both must give the reference's bits, several calls in a row."""
+    import torch
+    w = synth.weights(wt, n_out, n_in, seed=n_out)
+    dw = dev(w)
+    for call in range(3):
+        x = synth.activations(n_in, 1, seed=100 + call)[0]
+        want = oracle.gemv(wt, w, n_in, n_out, oracle.quantize_pair(wt, x)[0])
+        hx = torch.from_numpy(x.copy()).pin_memory()
+        hy = torch.full((n_out,), float("nan")).pin_memory()
+        sicu.gemv_host(wt, dw, n_in, n_out, hx, hy)
+        assert_bits_equal(hy.numpy(), want, f"{Q.NAMES[wt]} gemv_host, page-locked, call {call}")
+        hy2 = np.full(n_out, np.nan, np.float32)
+        sicu.gemv_host(wt, dw, n_in, n_out, x, hy2)
+        assert_bits_equal(hy2, want, f"{Q.NAMES[wt]} gemv_host, pageable, call {call}")
+    assert sicu.status() == 0
+
+
 @pytest.mark.parametrize("wt", Q.WEIGHT_TYPES, ids=lambda t: Q.NAMES[t])
 def test_row_to_f32(sicu, oracle, wt):
     n_in, n_out = 2048, 9

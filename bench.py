@@ -299,12 +299,14 @@ def _time_graph(torch, g, stream, reps, world, dev) -> float:
     return max_over_ranks(e0.elapsed_time(e1), world, dev)
 
 
-def model_decode(torch, s, shape, dev, stream, world, rank, group, reps, fused=False) -> dict:
+def model_decode(torch, s, shape, dev, stream, world, rank, group, reps, fused=False, steps=True) -> dict:
     """Decode tok/s of the matrix path of `shape` (batch 1), tensor parallel
-    over the world: every weight matrix of one token per step. fused: the
-    all-reduces ride in the matvecs (sicu_gemv_ar), else NCCL all-reduces."""
+    over the world: every weight matrix of one token per step, with (steps)
+    the residual adds, RMS norms and SwiGLU between them fused into the
+    products (sicu_gemv_fused). fused: the all-reduces ride in the matvecs
+    too, else NCCL all-reduces."""
     from siphon_b200 import model_path as mp
-    m = mp.MatrixPath(s, shape, dev, world, rank, group, seed=4, fused=fused)
+    m = mp.MatrixPath(s, shape, dev, world, rank, group, seed=4, fused=fused, steps=steps)
     with torch.cuda.stream(stream):
         for _ in range(2):
             launches = m.decode_step(stream)

@@ -18,7 +18,9 @@
  * for the calling thread from sicu_last_error(). Argument checks run on the
  * host before any CUDA call. All device memory handed in is owned by the
  * caller; the library allocates device memory only in sicu_init, sicu_upload
- * / sicu_malloc and the growable staging buffers of sicu_gemv_host.
+ * / sicu_malloc, the all-reduce groups, and the growable buffers of
+ * sicu_gemv_host, sicu_row_to_f32, the prefill product and sicu_gemv_fused's
+ * F16 path.
  */
 #ifndef SIPHON_CUDA_H
 #define SIPHON_CUDA_H
@@ -242,6 +244,72 @@ SICU_API int sicu_ar_allreduce(sicu_ar *group, const float *dsrc, float *ddst, v
  * in. Quantized weight types only. */
 SICU_API int sicu_gemv_ar(uint32_t wtype, const void *dw, int64_t n_in, int64_t n_out,
                           const float *dx, float *dy, sicu_ar *group, void *stream);
+
+/* ---- activation steps fused into the product ---------------------------------
+ * Between two products the reference's forward pass runs a step on the f32
+ * activation on the host: the residual add and RMS norm before Wq/Wk/Wv, before
+ * W_gate/W_up and before the output head, and SwiGLU before W_down
+ * (src/engine.c:313-315, 369-377, 379-389). sicu_gemv_fused takes the step's
+ * inputs and runs it inside the matvec: each CTA applies it while quantizing
+ * the activation, so the step needs no launch and no f32 round trip through
+ * memory. Results are bit-identical to the reference's step followed by its
+ * gemv, for finite inputs and results (non-finite values give NaN or inf as
+ * there, but NaN payloads are not matched):
+ *   SICU_PRO_RMS_NORM  h = x + residual (x alone when residual is NULL),
+ *                      a_i = h_i * s * weight_i, s = 1 / sqrtf(mean(h^2) + eps),
+ *                      mean(h^2) as the reference computes it (f32 squares
+ *                      added in double in index order, the mean rounded to
+ *                      f32); sum_out (optional) receives h, the new residual
+ *                      stream (src/engine.c:12-18, 369; src/kernels.c:892-900)
+ *   SICU_PRO_SWIGLU    a_i = silu(x_i) * up_i, silu(v) = v / (1 + e(0 - v)) with
+ *                      the reference's exp polynomial
+ *                      (src/engine.c:162-179; src/kernels.c:821-853)
+ *   SICU_PRO_MUL       a_i = x_i * up_i: SwiGLU's product when x already holds
+ *                      silu(gate), i.e. when the gate product ran with the
+ *                      SICU_EPI_SILU epilogue. Computing silu once per element
+ *                      in the gate product's epilogue costs little there, while
+ *                      SICU_PRO_SWIGLU evaluates it in every CTA cluster that
+ *                      quantizes x.
+ * weight, residual, sum_out and up are device vectors of n_in floats, 16-byte
+ * aligned; sum_out must not overlap x, residual, weight or an output. */
+#define SICU_PRO_NONE     0
+#define SICU_PRO_RMS_NORM 1
+#define SICU_PRO_SWIGLU   2
+#define SICU_PRO_MUL      3
+typedef struct sicu_prologue {
+    int32_t kind;            /* SICU_PRO_* */
+    float eps;               /* RMS norm epsilon (the model's rms_eps) */
+    const float *weight;     /* RMS norm weight */
+    const float *residual;   /* added to x before the norm, or NULL */
+    float *sum_out;          /* receives x + residual, or NULL */
+    const float *up;         /* SwiGLU / MUL: the up projection's output */
+} sicu_prologue;
+/* Epilogues, per matrix: SICU_EPI_SILU writes silu(W_i a) instead of W_i a
+ * (the gate half of SwiGLU, src/engine.c:162-179, with the reference's exp
+ * polynomial), for a following SICU_PRO_MUL step. */
+#define SICU_EPI_NONE 0
+#define SICU_EPI_SILU 1
+/* dy_i = W_i a for i < n_mats, a = the step pro (NULL: none) applied to dx,
+ * each output through its epilogue epi[i] (epi NULL: none; a host array of
+ * n_mats entries): sicu_gemv_multi with the steps fused in. group: NULL, or
+ * an all-reduce group (n_mats == 1, n_out[0] == the group's len): the
+ * sicu_gemv_ar form, the epilogue applied to the sum. Quantized weight types
+ * run the steps inside the matvec; F16 weights run them as separate kernels,
+ * the prologue into a per-device buffer (grown on first use, so make such a
+ * call once before any stream capture). */
+SICU_API int sicu_gemv_fused(uint32_t wtype, int n_mats, const void *const *dw, const int64_t *n_out,
+                             int64_t n_in, const float *dx, const sicu_prologue *pro, const int32_t *epi,
+                             float *const *dy, sicu_ar *group, void *stream);
+/* The steps on their own, m rows of n floats (16-byte aligned rows, n a
+ * multiple of 4): dy = rmsnorm(dx + dres) * dw with dsum = dx + dres (dres and
+ * dsum per row, each NULL allowed), and dy = silu(dx) * dup. For prompts
+ * (before sicu_gemm_prefill_f32) and other callers that need the f32 result.
+ * The reference sends the last n % 8 elements of a SwiGLU row through libm's
+ * expf instead of the polynomial; sicu_swiglu rejects such n (every K-quant
+ * FFN width is a multiple of 256). */
+SICU_API int sicu_rms_norm(const float *dx, const float *dres, float *dsum, const float *dw, int64_t n, int64_t m,
+                           float eps, float *dy, void *stream);
+SICU_API int sicu_swiglu(const float *dx, const float *dup, int64_t n, int64_t m, float *dy, void *stream);
 
 /* ---- dequantisation --------------------------------------------------------
  * Rows rows[0..nrows) (host array) of W into dout[nrows][n_in] f32, reference

@@ -79,6 +79,15 @@ class Oracle:
         L.orc_geometry.restype = C.c_int
         L.orc_pair_type.argtypes = [C.c_uint32, C.POINTER(C.c_uint32)]
         L.orc_pair_type.restype = C.c_int
+        for name in ("orc_expf", "orc_silu"):
+            getattr(L, name).argtypes = [C.c_float]
+            getattr(L, name).restype = C.c_float
+        L.orc_rms_scale.argtypes = [_f32, C.c_int, C.c_float]
+        L.orc_rms_scale.restype = C.c_float
+        L.orc_rms_norm.argtypes = [_f32, C.c_void_p, _f32, _f32, C.c_int, C.c_float, _f32]
+        L.orc_rms_norm.restype = None
+        L.orc_swiglu.argtypes = [_f32, _f32, C.c_int, _f32]
+        L.orc_swiglu.restype = None
 
     # -- conversions / quantizers ------------------------------------------
     def f16_to_f32(self, h: int) -> float:
@@ -116,6 +125,37 @@ class Oracle:
             rc = self.lib.orc_quantize_pair(wtype, row, out[i].ctypes.data, n)
             assert rc == 0
         return out
+
+    # -- activation steps between products -----------------------------------
+    def expf(self, x: float) -> float:
+        return self.lib.orc_expf(x)
+
+    def silu(self, x: float) -> float:
+        return self.lib.orc_silu(x)
+
+    def rms_scale(self, x, eps: float) -> float:
+        x = _as_f32(x).reshape(-1)
+        return self.lib.orc_rms_scale(x, x.size, eps)
+
+    def rms_norm(self, x, w, eps: float, res=None):
+        """(h, y): h = x (+ res), y = h * rms_scale(h) * w, one row."""
+        x, w = _as_f32(x).reshape(-1), _as_f32(w).reshape(-1)
+        h = np.zeros_like(x)
+        y = np.zeros_like(x)
+        r = None if res is None else _as_f32(res).reshape(-1)
+        self.lib.orc_rms_norm(x, None if r is None else r.ctypes.data, h, w, x.size, eps, y)
+        return h, y
+
+    def swiglu(self, x, g) -> np.ndarray:
+        """swiglu_row: silu(x) * g, the n % 8 tail through libm's expf."""
+        x, g = _as_f32(x).reshape(-1), _as_f32(g).reshape(-1)
+        y = np.zeros_like(x)
+        self.lib.orc_swiglu(x, g, x.size, y)
+        return y
+
+    def silu_vec(self, x) -> np.ndarray:
+        """si_silu element by element (no tail rule)."""
+        return np.array([self.lib.orc_silu(float(v)) for v in np.asarray(x, np.float32).reshape(-1)], np.float32)
 
     # -- products -------------------------------------------------------------
     def vec_dot(self, wtype: int, n: int, x: np.ndarray, y: np.ndarray) -> float:
@@ -218,6 +258,11 @@ class Reference:
         L.si_tp_create.restype = C.c_void_p
         L.si_tp_free.argtypes = [C.c_void_p]
         L.si_tp_free.restype = None
+        for name in ("si_expf", "si_silu"):
+            getattr(L, name).argtypes = [C.c_float]
+            getattr(L, name).restype = C.c_float
+        L.si_rms_scale.argtypes = [_f32, C.c_int, C.c_float]
+        L.si_rms_scale.restype = C.c_float
 
     @property
     def impl(self) -> str:
@@ -252,6 +297,16 @@ class Reference:
         for r in range(n_out):
             y[r] = self.vec_dot(wtype, n_in, w[r * rb:(r + 1) * rb], xq)
         return y
+
+    def expf(self, x: float) -> float:
+        return self.lib.si_expf(x)
+
+    def silu(self, x: float) -> float:
+        return self.lib.si_silu(x)
+
+    def rms_scale(self, x, eps: float) -> float:
+        x = _as_f32(x).reshape(-1)
+        return self.lib.si_rms_scale(x, x.size, eps)
 
     def dequant_row(self, t: int, x: np.ndarray, n: int) -> np.ndarray:
         y = np.zeros(n, np.float32)

@@ -14,6 +14,11 @@
  *   - scalar dot products ............... src/kernels.c:189-523
  *   - row dequantisation ................ src/kernels.c:599-817
  *   - block geometry / dot pairing ...... src/kernels.c:904-919, 946-960
+ *   - activation steps between products:
+ *     exp polynomial, silu .............. src/kernels.c:821-853
+ *     RMS scale ......................... src/kernels.c:892-900
+ *     residual add, rms_norm_mul ........ src/engine.c:12-18, 369, 379
+ *     swiglu_row ........................ src/engine.c:162-179
  *
  * Integer partial sums are order-free, so they are written here in whatever
  * order reads best. Every floating-point operation is written one rounding
@@ -578,4 +583,59 @@ ORC_API int orc_dequant_row(uint32_t t, const void *xv, float *y, int n) {
         default:
             return -4;
     }
+}
+
+/* ---- activation steps between the products ----------------------------------
+ * The residual add, RMS norm and SwiGLU the reference's forward pass runs on
+ * the host between two gemv calls (src/engine.c:12-18, 162-179, 369, 379). */
+
+/* exp polynomial, src/kernels.c:821-849: round x / ln2 to n with the 1.5 * 2^23
+ * shifter, reduce b = x - n ln2 (ln2 split in two), degree-5 polynomial p(b),
+ * result 2^n (1 + p); two-factor scaling past |n| = 126, saturation past 192. */
+ORC_API float orc_expf(float x) {
+    const float shift = 0x1.8p23f;
+    const float z = fmaf(x, 0x1.715476p+0f, shift);
+    const float n = z - shift;
+    const float b = fmaf(-n, 0x1.7f7d1cp-20f, fmaf(-n, 0x1.62e4p-1f, x));
+    const uint32_t e = f32_bits(z) << 23;
+    const float two_n = bits_f32(e + 0x3f800000u);
+    const float b2 = b * b;
+    const float p45 = fmaf(0x1.0e4020p-7f, b, 0x1.573e2ep-5f);
+    const float p23 = fmaf(0x1.555e66p-3f, b, 0x1.fffdb6p-2f);
+    const float p1 = 0x1.ffffecp-1f * b;
+    const float p = fmaf(fmaf(p45, b2, p23), b2, p1);
+    if (!(fabsf(n) > 126.0f)) return fmaf(p, two_n, two_n);
+    const uint32_t g = n <= 0.0f ? 0x82000000u : 0u;
+    const float s1 = bits_f32(g + 0x7f000000u);
+    if (fabsf(n) > 192.0f) return s1 * s1;
+    const float s2 = bits_f32(e - g);
+    return fmaf(s2, p, s2) * s1;
+}
+
+/* src/kernels.c:851-853 */
+ORC_API float orc_silu(float x) { return x / (1.0f + orc_expf(0.0f - x)); }
+
+/* src/kernels.c:892-900: f32 squares summed in double in index order */
+ORC_API float orc_rms_scale(const float *x, int n, float eps) {
+    double sum = 0.0;
+    for (int i = 0; i < n; i++) sum += (double)(x[i] * x[i]);
+    const float mean = (float)(sum / n);
+    return 1.0f / sqrtf(mean + eps);
+}
+
+/* residual add (src/engine.c:369, 379; res may be NULL) into h, then
+ * rms_norm_mul (src/engine.c:12-18) into y */
+ORC_API void orc_rms_norm(const float *x, const float *res, float *h, const float *w, int n, float eps, float *y) {
+    for (int i = 0; i < n; i++) h[i] = res ? x[i] + res[i] : x[i];
+    const float scale = orc_rms_scale(h, n, eps);
+    for (int i = 0; i < n; i++) y[i] = h[i] * scale * w[i];
+}
+
+/* swiglu_row (src/engine.c:162-179): 8-wide groups through the polynomial,
+ * the n % 8 tail through libm's expf */
+ORC_API void orc_swiglu(const float *x, const float *g, int n, float *y) {
+    const int body = n - n % 8;
+    int i = 0;
+    for (; i < body; i++) y[i] = orc_silu(x[i]) * g[i];
+    for (; i < n; i++) y[i] = x[i] / (1.0f + expf(0.0f - x[i])) * g[i];
 }

@@ -20,8 +20,8 @@ CSRC = PKG / "csrc"
 ROOT = PKG.parent
 LIB = PKG / "libsiphon_cuda.so"
 
-SOURCES = ["abi.cu", "gemv.cu", "gemv_f16.cu", "quantize.cu", "noalloc.cu", "prefill.cu", "allreduce.cu"]
-HEADERS = ["common.cuh", "gemv.cuh", "quantize.cuh", "launch.h", "tc.cuh", "allreduce.cuh"]
+SOURCES = ["abi.cu", "gemv.cu", "gemv_f16.cu", "quantize.cu", "noalloc.cu", "prefill.cu", "allreduce.cu", "prologue.cu"]
+HEADERS = ["common.cuh", "gemv.cuh", "quantize.cuh", "launch.h", "tc.cuh", "allreduce.cuh", "prologue.cuh"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

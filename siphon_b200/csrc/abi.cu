@@ -37,6 +37,9 @@ struct DevState {
     // growable workspace of the prefill product (token operand, f32 quantization)
     void *pf_ws = nullptr;
     size_t pf_ws_bytes = 0;
+    // growable f32 activation of sicu_gemv_fused's F16 path (the step's output)
+    float *pro_buf = nullptr;
+    size_t pro_buf_bytes = 0;
 };
 
 constexpr int MAX_DEV = 64;
@@ -225,6 +228,7 @@ int sicu_shutdown(void) {
         cudaFree(ds.status);
         if (ds.stage) cudaFree(ds.stage);
         if (ds.pf_ws) cudaFree(ds.pf_ws);
+        if (ds.pro_buf) cudaFree(ds.pro_buf);
         ds = DevState{};
     }
     if (have && cur >= 0) cudaSetDevice(cur);
@@ -687,6 +691,177 @@ int sicu_gemv_ar(uint32_t wtype, const void *dw, int64_t n_in, int64_t n_out, co
     L.xf = dx;
     L.ar = g->d;
     return run_gemv(wtype, L, (cudaStream_t)stream);
+}
+
+}  // extern "C"
+
+namespace {
+
+// [a, a + abytes) and [b, b + bbytes) share a byte (bbytes < 0: same as abytes)
+bool overlaps(const void *a, const void *b, int64_t abytes, int64_t bbytes = -1) {
+    if (!a || !b) return false;
+    if (bbytes < 0) bbytes = abytes;
+    const uintptr_t x = reinterpret_cast<uintptr_t>(a), y = reinterpret_cast<uintptr_t>(b);
+    return x < y + (uintptr_t)bbytes && y < x + (uintptr_t)abytes;
+}
+
+// Checks a step's vectors (n floats each) and turns it into the kernels' form.
+int check_prologue(const sicu_prologue *pro, int64_t n, const float *dx, ProDev &pd) {
+    pd = ProDev{};
+    if (!pro || pro->kind == SICU_PRO_NONE) return SICU_OK;
+    if (n % 4) return fail(SICU_EINVAL, "activation step: length %lld is not a multiple of 4", (long long)n);
+    if (pro->kind == SICU_PRO_RMS_NORM) {
+        if (!pro->weight) return fail(SICU_EINVAL, "rms norm: null weight");
+        if (!aligned(pro->weight, 16) || !aligned(pro->residual, 16) || !aligned(pro->sum_out, 16))
+            return fail(SICU_EINVAL, "rms norm: vectors must be 16-byte aligned");
+        if (!(pro->eps >= 0.0f)) return fail(SICU_EINVAL, "rms norm: eps must be >= 0");
+        if (n > INT32_MAX) return fail(SICU_EINVAL, "rms norm: row too long");
+        const int64_t b = n * 4;
+        if (overlaps(pro->sum_out, dx, b) || overlaps(pro->sum_out, pro->residual, b) ||
+            overlaps(pro->sum_out, pro->weight, b))
+            return fail(SICU_EINVAL, "rms norm: sum_out overlaps an input");
+        pd.kind = PRO_RMS_NORM;
+        pd.eps = pro->eps;
+        pd.g = pro->weight;
+        pd.res = pro->residual;
+        pd.h_out = pro->sum_out;
+        pd.inv_n = 1.0 / (double)n;
+        return SICU_OK;
+    }
+    if (pro->kind == SICU_PRO_SWIGLU || pro->kind == SICU_PRO_MUL) {
+        if (!pro->up) return fail(SICU_EINVAL, "swiglu: null up vector");
+        if (!aligned(pro->up, 16)) return fail(SICU_EINVAL, "swiglu: up vector must be 16-byte aligned");
+        if (n % 8) return fail(SICU_EINVAL, "swiglu: length %lld is not a multiple of 8", (long long)n);
+        pd.kind = pro->kind == SICU_PRO_SWIGLU ? PRO_SWIGLU : PRO_MUL;
+        pd.up = pro->up;
+        return SICU_OK;
+    }
+    return fail(SICU_EINVAL, "activation step: unknown kind %d", (int)pro->kind);
+}
+
+int run_step(const ProDev &pd, const float *dx, int64_t n, float *dy, cudaStream_t st) {
+    int rc;
+    if (pd.kind == PRO_RMS_NORM) rc = launch_rms_norm(dx, pd.res, pd.h_out, pd.g, n, 1, pd.eps, dy, st);
+    else if (pd.kind == PRO_SWIGLU) rc = launch_swiglu(dx, pd.up, n, 1, dy, st);
+    else rc = launch_mul(dx, pd.up, n, dy, st);
+    return rc ? cuda_fail(cudaGetLastError(), "activation step launch") : SICU_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int sicu_gemv_fused(uint32_t wtype, int n_mats, const void *const *dw, const int64_t *n_out, int64_t n_in,
+                    const float *dx, const sicu_prologue *pro, const int32_t *epi, float *const *dy, sicu_ar *group,
+                    void *stream) {
+    if (n_mats < 1 || n_mats > MAX_MATS) return fail(SICU_EINVAL, "matvec fused: %d matrices (1..%d)", n_mats, MAX_MATS);
+    if (!dw || !n_out || !dy) return fail(SICU_EINVAL, "matvec fused: null array");
+    uint32_t pair;
+    for (int i = 0; i < n_mats; ++i) {
+        if (int rc = check_matvec(wtype, dw[i], n_in, n_out[i], dx, dy[i], 1, pair)) return rc;
+        if (n_out[i] > ((int64_t)1 << 30)) return fail(SICU_EINVAL, "matvec fused: too many rows");
+    }
+    if (!aligned(dx, 16)) return fail(SICU_EINVAL, "matvec: f32 activation must be 16-byte aligned");
+    ProDev pd;
+    if (int rc = check_prologue(pro, n_in, dx, pd)) return rc;
+    if (pd.h_out)
+        for (int i = 0; i < n_mats; ++i)
+            if (overlaps(pd.h_out, dy[i], 4 * n_in, 4 * n_out[i]))
+                return fail(SICU_EINVAL, "rms norm: sum_out overlaps an output");
+    uint64_t silu_mask = 0;
+    if (epi)
+        for (int i = 0; i < n_mats; ++i) {
+            if (epi[i] == SICU_EPI_SILU) silu_mask |= 1ull << i;
+            else if (epi[i] != SICU_EPI_NONE) return fail(SICU_EINVAL, "matvec fused: unknown epilogue %d", (int)epi[i]);
+        }
+    DevState *ds;
+    const cudaStream_t st = (cudaStream_t)stream;
+    if (group) {
+        if (n_mats != 1) return fail(SICU_EINVAL, "matvec fused: an all-reduce group takes one matrix");
+        if (wtype == T_F16) return fail(SICU_ENOTSUP, "matvec ar: F16 weights are not supported");
+        if (int rc = ar_current(group, ds)) return rc;
+        if (n_out[0] != group->d.len)
+            return fail(SICU_EINVAL, "matvec ar: %lld rows, the group reduces vectors of %lld", (long long)n_out[0],
+                        (long long)group->d.len);
+        GemvLaunch L = make_launch(*ds, dw[0], n_in, n_out[0], dy[0]);
+        L.xf = dx;
+        L.ar = group->d;
+        L.pro = pd;
+        L.epi_silu = silu_mask;
+        return run_gemv(wtype, L, st);
+    }
+    if (int rc = current(ds)) return rc;
+    if (wtype == T_F16) {
+        const float *x = dx;
+        if (pd.kind != PRO_NONE) {
+            const size_t need = (size_t)n_in * 4;
+            if (ds->pro_buf_bytes < need) {
+                if (ds->pro_buf) cudaFree(ds->pro_buf);
+                ds->pro_buf = nullptr;
+                ds->pro_buf_bytes = 0;
+                if (cudaMalloc(&ds->pro_buf, need) != cudaSuccess) {
+                    cudaGetLastError();
+                    return fail(SICU_ENOMEM, "activation step buffer");
+                }
+                ds->pro_buf_bytes = need;
+            }
+            if (int rc = run_step(pd, dx, n_in, ds->pro_buf, st)) return rc;
+            x = ds->pro_buf;
+        }
+        for (int i = 0; i < n_mats; ++i) {
+            if (n_out[i] == 0) continue;
+            GemvLaunch L = make_launch(*ds, dw[i], n_in, n_out[i], dy[i]);
+            L.xf = x;
+            if (int rc = run_gemv(wtype, L, st)) return rc;
+            if (((silu_mask >> i) & 1) && launch_silu_inplace(dy[i], n_out[i], st))
+                return cuda_fail(cudaGetLastError(), "silu launch");
+        }
+        return SICU_OK;
+    }
+    GemvLaunch L = make_launch(*ds, dw[0], n_in, n_out[0], dy[0]);
+    L.xf = dx;
+    L.pro = pd;
+    L.epi_silu = silu_mask;
+    L.nmat = n_mats;
+    for (int i = 0; i < n_mats; ++i) {
+        L.wm[i] = dw[i];
+        L.ym[i] = dy[i];
+        L.n_outm[i] = n_out[i];
+    }
+    return run_gemv(wtype, L, st);
+}
+
+int sicu_rms_norm(const float *dx, const float *dres, float *dsum, const float *dw, int64_t n, int64_t m, float eps,
+                  float *dy, void *stream) {
+    if (n <= 0 || m < 0 || m > INT32_MAX)
+        return fail(SICU_EINVAL, "rms norm: bad shape n=%lld m=%lld", (long long)n, (long long)m);
+    if (!dx || !dy) return fail(SICU_EINVAL, "rms norm: null pointer");
+    if (!aligned(dx, 16) || !aligned(dy, 16)) return fail(SICU_EINVAL, "rms norm: rows must be 16-byte aligned");
+    sicu_prologue pro{SICU_PRO_RMS_NORM, eps, dw, dres, dsum, nullptr};
+    ProDev pd;
+    if (int rc = check_prologue(&pro, n, dx, pd)) return rc;
+    if (overlaps(dsum, dy, 4 * n * m) || overlaps(dsum, dx, 4 * n * m) || overlaps(dsum, dres, 4 * n * m))
+        return fail(SICU_EINVAL, "rms norm: sum_out overlaps another row block");
+    DevState *ds;
+    if (int rc = current(ds)) return rc;
+    if (m == 0) return SICU_OK;
+    if (launch_rms_norm(dx, dres, dsum, dw, n, m, eps, dy, (cudaStream_t)stream))
+        return cuda_fail(cudaGetLastError(), "rms norm launch");
+    return SICU_OK;
+}
+
+int sicu_swiglu(const float *dx, const float *dup, int64_t n, int64_t m, float *dy, void *stream) {
+    if (n <= 0 || m < 0) return fail(SICU_EINVAL, "swiglu: bad shape n=%lld m=%lld", (long long)n, (long long)m);
+    if (!dx || !dy) return fail(SICU_EINVAL, "swiglu: null pointer");
+    if (!aligned(dx, 16) || !aligned(dy, 16)) return fail(SICU_EINVAL, "swiglu: rows must be 16-byte aligned");
+    sicu_prologue pro{SICU_PRO_SWIGLU, 0.0f, nullptr, nullptr, nullptr, dup};
+    ProDev pd;
+    if (int rc = check_prologue(&pro, n, dx, pd)) return rc;
+    DevState *ds;
+    if (int rc = current(ds)) return rc;
+    if (m == 0) return SICU_OK;
+    if (launch_swiglu(dx, dup, n, m, dy, (cudaStream_t)stream)) return cuda_fail(cudaGetLastError(), "swiglu launch");
+    return SICU_OK;
 }
 
 int sicu_row_to_f32(uint32_t wtype, const void *dw, int64_t n_in, const int64_t *rows, int64_t nrows, float *dout,

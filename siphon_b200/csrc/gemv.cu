@@ -101,9 +101,13 @@ __device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol
 // the ring full with bulk copies; a slot's geometry is published next to it,
 // so the consuming side does no address arithmetic of its own.
 // AR: a row-split product whose partial outputs are all-reduced over the
-// tensor-parallel group inside the kernel (a separate instantiation, so the
-// plain matvec carries none of it).
-template <uint32_t T, bool AR>
+// tensor-parallel group inside the kernel. STEPS: the launch has an
+// activation step or an output epilogue (p.pro, p.epi_silu). Both are
+// separate instantiations, so the plain matvec carries none of their code
+// (kernels that follow one another in a decode step measured ~1.5 us slower
+// per launch with the step code inlined, and ~2 % slower per step with it out
+// of line but still present).
+template <uint32_t T, bool AR, bool STEPS>
 __global__ void __launch_bounds__(GEMV_WARPS * 32, 2) gemv_kernel(const GemvParams p) {
     using F = Fmt<T>;
     constexpr int CH = F::chains;
@@ -143,7 +147,7 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 2) gemv_kernel(const GemvPara
         pc.locate<T>(p);
         // weights never depend on earlier kernels: start streaming right away
         policy = policy_evict_first();
-        for (; pm < items && pm < S; ++pm) {
+        for (; pm < items && pm < S && pm < GEMV_PRE_WAIT_SLOTS; ++pm) {
             pc.produce<T>(p, pm, slots + (size_t)pm * p.slot_bytes, &info[2 * pm], smem_addr(&full[pm]), policy);
             pc.next<T>(p, W);
         }
@@ -162,7 +166,9 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 2) gemv_kernel(const GemvPara
     if constexpr (AR) {
         if (threadIdx.x == 0) as = ar_load_state(p.ar);   // used after the quantizer
     }
-    if (p.xf) quantize_into_act<F::act>(av, p.xf, p.n_in, rank, nrank);
+    if (STEPS && p.pro.kind != PRO_NONE)
+        quantize_steps<F::act>(av, p.xf, p.n_in, rank, nrank, p.pro, smem + ActView::bytes(p.nu) + 16);
+    else if (p.xf) quantize_into_act<F::act>(av, p.xf, p.n_in, rank, nrank);
     else prep_activation<F::act>(av, p.xq, p.n_in, rank, nrank);
     if constexpr (AR) {
         if (threadIdx.x == 0) {
@@ -173,6 +179,14 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 2) gemv_kernel(const GemvPara
         }
     }
     cluster_sync();   // also publishes ar_st to the CTA
+    // the rest of the ring, held back so the activation's loads do not queue
+    // behind the weight stream
+    if (lane == 0 && items > 0) {
+        for (; pm < items && pm < S; ++pm) {
+            pc.produce<T>(p, pm, slots + (size_t)pm * p.slot_bytes, &info[2 * pm], smem_addr(&full[pm]), policy);
+            pc.next<T>(p, W);
+        }
+    }
 
     const int r_l = p.nchunks == 1 ? lane / p.cu : 0;
     const int u_l = p.nchunks == 1 ? lane - r_l * p.cu : lane;
@@ -270,6 +284,7 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 2) gemv_kernel(const GemvPara
                 // row-split product: the partial goes to every rank; y gets
                 // the sum after the loop
                 if (AR && ar_st[1]) ar_send(p.ar, ar_st[0], g.x + lane, r);
+                else if (STEPS && ((p.epi_silu >> mat) & 1)) p.y[mat][g.x + lane] = silu_call(r);
                 else p.y[mat][g.x + lane] = r;
             }
         }
@@ -284,8 +299,10 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 2) gemv_kernel(const GemvPara
             bool live = true;
             for (int t = t0 + warp; t < t1; t += W) {
                 const int64_t row = (int64_t)t * p.rows_per_task + lane;
-                if (lane < p.rows_per_task && row < p.n_out[0])
-                    p.y[0][row] = ar_sum(p.ar, e, row, p.status, live);
+                if (lane < p.rows_per_task && row < p.n_out[0]) {
+                    const float v = ar_sum(p.ar, e, row, p.status, live);
+                    p.y[0][row] = (STEPS && (p.epi_silu & 1)) ? silu_call(v) : v;
+                }
             }
         }
     }
@@ -337,7 +354,7 @@ struct FlatCursor {
 
 constexpr int FLAT_TS = 36;    // terms row stride (floats): an odd number of 16-byte units
 
-template <uint32_t T>
+template <uint32_t T, bool STEPS>
 __global__ void __launch_bounds__(GEMV_WARPS * 32, 2) gemv_flat_kernel(const GemvParams p) {
     using F = Fmt<T>;
     constexpr int CH = F::chains;
@@ -395,20 +412,29 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 2) gemv_flat_kernel(const Gem
         mbar_expect_tx(bar, (uint32_t)bulk);
         if (bulk > 0) bulk_g2s_hint(smem_addr(slot), al, (uint32_t)bulk, bar, policy);
     };
+    int pi = 0;   // ring slots filled before the activation phase
     if (lane == 0 && pc.task < t1) {
         pc.locate(p);
         policy = policy_evict_first();
-        for (int i = 0; i < S && pc.task < t1; ++i) {
-            produce(i);
+        for (; pi < S && pi < GEMV_PRE_WAIT_SLOTS && pc.task < t1; ++pi) {
+            produce(pi);
             pc.next(p, W);
         }
     }
 
     grid_dep_wait();
     const uint32_t rank = cluster_rank(), nrank = cluster_size();
-    if (p.xf) quantize_into_act<F::act>(av, p.xf, p.n_in, rank, nrank);
+    if (STEPS && p.pro.kind != PRO_NONE)
+        quantize_steps<F::act>(av, p.xf, p.n_in, rank, nrank, p.pro, smem + ActView::bytes(p.nu) + 16);
+    else if (p.xf) quantize_into_act<F::act>(av, p.xf, p.n_in, rank, nrank);
     else prep_activation<F::act>(av, p.xq, p.n_in, rank, nrank);
     cluster_sync();
+    if (lane == 0) {
+        for (; pi < S && pc.task < t1; ++pi) {
+            produce(pi);
+            pc.next(p, W);
+        }
+    }
 
     int s = 0, cpar = 0;
     uint32_t parity = 0;
@@ -486,7 +512,7 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 2) gemv_flat_kernel(const Gem
                 } else {
                     r = fin[lane];
                 }
-                p.y[mat][row0 + r_first + lane] = r;
+                p.y[mat][row0 + r_first + lane] = (STEPS && ((p.epi_silu >> mat) & 1)) ? silu_call(r) : r;
             }
             __syncwarp();
             if (++s == S) { s = 0; parity ^= 1u; }
@@ -573,7 +599,12 @@ static int launch_gemv_t(const GemvLaunch &L, cudaStream_t st) {
     const int64_t item_max = flat ? 32LL * F::unit_bytes
                                   : (p.nchunks == 1) ? p.rows_per_task * p.row_bytes : (int64_t)p.cu * F::unit_bytes;
     p.slot_bytes = (int)((item_max + 32 + 127) & ~int64_t(127));
-    p.act_bytes = (ActView::bytes(p.nu) + (ar ? 16 : 0) + 127) & ~127;
+    // after the records: the all-reduce state (16 bytes), then the norm's
+    // reduction scratch
+    p.pro = L.pro;
+    p.epi_silu = L.epi_silu;
+    const bool rms = L.pro.kind == PRO_RMS_NORM;
+    p.act_bytes = (ActView::bytes(p.nu) + (ar || rms ? 16 : 0) + (rms ? RMS_SCRATCH : 0) + 127) & ~127;
     // two CTAs per SM when each warp keeps >= 2 ring slots, with 8 warps per
     // CTA or, for large slots, down to 6 (12 warps per SM still hide more
     // latency than one CTA of 8); else one CTA of 8 warps with up to 4 slots
@@ -594,12 +625,14 @@ static int launch_gemv_t(const GemvLaunch &L, cudaStream_t st) {
     p.nslots = slots;
     p.warp_bytes = (hdr + slots * p.slot_bytes + 127) & ~127;
     const int smem = p.act_bytes + warps * p.warp_bytes;
-    auto kern = ar ? gemv_kernel<T, true> : gemv_kernel<T, false>;
+    const bool steps = L.pro.kind != PRO_NONE || L.epi_silu != 0;
+    auto kern = ar ? (steps ? gemv_kernel<T, true, true> : gemv_kernel<T, true, false>)
+                   : (steps ? gemv_kernel<T, false, true> : gemv_kernel<T, false, false>);
     if constexpr (F::kind != 3) {
-        if (flat) kern = gemv_flat_kernel<T>;
+        if (flat) kern = steps ? gemv_flat_kernel<T, true> : gemv_flat_kernel<T, false>;
     }
-    const int variant = flat ? 2 : ar ? 1 : 0;
-    static bool attr_set[64][3] = {};
+    const int variant = (flat ? 2 : ar ? 1 : 0) + (steps ? 3 : 0);
+    static bool attr_set[64][6] = {};
     const int dev = L.device & 63;
     if (!attr_set[dev][variant]) {
         if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L.smem_limit) != cudaSuccess)
@@ -618,7 +651,7 @@ static int launch_gemv_t(const GemvLaunch &L, cudaStream_t st) {
         static std::mutex mu;
         static std::map<std::pair<int, int>, std::pair<int, int>> cache;   // (device x variant, smem x warps) -> (C, capacity)
         std::lock_guard<std::mutex> lk(mu);
-        const auto key = std::make_pair(dev * 4 + variant, smem * 16 + warps);
+        const auto key = std::make_pair(dev * 8 + variant, smem * 16 + warps);
         auto hit = cache.find(key);
         if (hit == cache.end()) {
             int best_c = 1, best_cap = target;

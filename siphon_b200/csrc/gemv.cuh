@@ -35,6 +35,8 @@ constexpr int TERM_FLOATS = 480;
 constexpr int CONS_BYTES = 4 * (TERM_FLOATS + 64);   // per consumer warp: terms, chain results
 
 constexpr int GEMV_MAX_MATS = 64;
+// Ring slots each warp fills before the activation is ready (the rest after)
+constexpr int GEMV_PRE_WAIT_SLOTS = 64;
 
 struct GemvParams {
     // the matrices of one launch: same format and row length, one activation
@@ -58,6 +60,8 @@ struct GemvParams {
     int warp_bytes;        // per-warp region: barriers, slot geometry, terms, ring
     int *status;
     ArDev ar;              // n > 0: one row-split matrix; y = the group's sum of the partial outputs
+    ProDev pro;            // activation step the quantizer applies to xf first (STEPS kernels)
+    uint64_t epi_silu;     // bit i: write silu(y) for matrix i (STEPS kernels)
 };
 
 // ---------------------------------------------------------------------------

@@ -35,6 +35,25 @@ struct ArDev {
 inline int64_t ar_epoch_offset(int n, int64_t len) { return 2 * (int64_t)n * len * 8; }
 inline int64_t ar_alloc_bytes(int n, int64_t len) { return ar_epoch_offset(n, len) + 16; }
 
+// Activation step between two products of the reference's forward pass,
+// applied by the product's quantizer to the f32 activation x (n_in floats)
+// before it quantizes:
+//   PRO_RMS_NORM  h = x (+ res: the residual add), a = h * rms_scale(h) * g,
+//                 h also written to h_out when given (by the first cluster)
+//   PRO_SWIGLU    a = silu(x) * up
+//   PRO_MUL       a = x * up (SwiGLU's product when x already holds silu(gate),
+//                 written by the gate product's silu epilogue)
+constexpr int PRO_NONE = 0, PRO_RMS_NORM = 1, PRO_SWIGLU = 2, PRO_MUL = 3;
+struct ProDev {
+    int kind = PRO_NONE;
+    float eps = 0.0f;
+    const float *g = nullptr;      // norm weight [n_in]
+    const float *res = nullptr;    // residual [n_in] or null
+    float *h_out = nullptr;        // x + res [n_in] or null
+    const float *up = nullptr;     // SwiGLU / MUL: up projection [n_in]
+    double inv_n = 0.0;            // RMS norm: 1.0 / n_in
+};
+
 struct GemvLaunch {
     const void *w;        // weight blocks (device), single-matrix launches
     const void *xq;       // pair-format activation (device) or null
@@ -57,6 +76,8 @@ struct GemvLaunch {
     int device;
     int *status;          // device status word
     ArDev ar;             // n > 0: row-split product, y = the group's sum of the partial outputs
+    ProDev pro;           // step applied to xf before quantizing (quantized types)
+    uint64_t epi_silu;    // bit i: matrix i's outputs are written as silu(y)
 };
 
 // quantized formats (K and classic); fails with -3 for other types
@@ -87,6 +108,16 @@ bool prefill_supported(uint32_t wtype);
 size_t prefill_workspace_bytes(uint32_t wtype, int64_t n_in, int64_t n_out, int64_t m, int num_sms);
 // -3: no tensor-core kernel for the type; -4: tensor map encoding failed; -2: launch
 int launch_prefill(uint32_t wtype, const PrefillLaunch &L, cudaStream_t st);
+
+// the activation steps on their own, m rows of n floats (f32 out): RMS norm
+// (res, h_out per row, or null) and SwiGLU (n * m a multiple of 4)
+int launch_rms_norm(const float *x, const float *res, float *h_out, const float *g, int64_t n, int64_t m,
+                    float eps, float *y, cudaStream_t st);
+int launch_swiglu(const float *x, const float *up, int64_t n, int64_t m, float *y, cudaStream_t st);
+// y = x * up, n floats
+int launch_mul(const float *x, const float *up, int64_t n, float *y, cudaStream_t st);
+// y = silu(y), n floats in place (F16 products with a silu epilogue)
+int launch_silu_inplace(float *y, int64_t n, cudaStream_t st);
 
 // all-reduce of src[len] into dst[len] over the group (one delivery)
 int launch_allreduce(const ArDev &a, const float *src, float *dst, int *status, int num_sms, cudaStream_t st);

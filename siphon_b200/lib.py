@@ -57,10 +57,40 @@ SIGNATURES = {
     "sicu_ar_destroy": [_vp],
     "sicu_ar_allreduce": [_vp, _fp, _fp, _vp],
     "sicu_gemv_ar": [_u32, _vp, _i64, _i64, _fp, _fp, _vp, _vp],
+    "sicu_gemv_fused": [_u32, C.c_int, C.POINTER(C.c_void_p), C.POINTER(C.c_int64), _i64, _fp, _vp, _vp,
+                        C.POINTER(C.c_void_p), _vp, _vp],
+    "sicu_rms_norm": [_fp, _fp, _fp, _fp, _i64, _i64, C.c_float, _fp, _vp],
+    "sicu_swiglu": [_fp, _fp, _i64, _i64, _fp, _vp],
 }
+
+PRO_NONE, PRO_RMS_NORM, PRO_SWIGLU, PRO_MUL = 0, 1, 2, 3
+EPI_NONE, EPI_SILU = 0, 1
+
+
+class Prologue(C.Structure):
+    """sicu_prologue: the activation step sicu_gemv_fused applies before
+    quantizing (RMS norm with an optional residual add, SwiGLU, or the
+    multiply that completes a SwiGLU whose silu ran as the gate's epilogue)."""
+    _fields_ = [("kind", C.c_int32), ("eps", C.c_float), ("weight", C.c_void_p), ("residual", C.c_void_p),
+                ("sum_out", C.c_void_p), ("up", C.c_void_p)]
 
 AR_HANDLE_BYTES = 64
 STATUS_WAIT_TIMEOUT, STATUS_AR_TIMEOUT = 1, 2
+
+
+def rms_norm_step(weight, eps: float, residual=None, sum_out=None) -> Prologue:
+    """a = (x + residual) * rms_scale * weight; sum_out receives x + residual."""
+    return Prologue(PRO_RMS_NORM, eps, _ptr(weight), _ptr(residual), _ptr(sum_out), None)
+
+
+def swiglu_step(up) -> Prologue:
+    """a = silu(x) * up."""
+    return Prologue(PRO_SWIGLU, 0.0, None, None, None, _ptr(up))
+
+
+def mul_step(up) -> Prologue:
+    """a = x * up (x already through silu: the gate product's EPI_SILU)."""
+    return Prologue(PRO_MUL, 0.0, None, None, None, _ptr(up))
 
 
 class SicuError(RuntimeError):
@@ -174,6 +204,27 @@ class SiphonCuda:
         """sicu_gemv_ar: this rank's column shard times x, summed over the group."""
         self.check(self.lib.sicu_gemv_ar(wtype, _ptr(dw), n_in, n_out, _ptr(dx), _ptr(dy), group.handle,
                                          _ptr(stream)))
+
+    # -- activation steps ------------------------------------------------------------
+    def gemv_fused(self, wtype: int, dws, n_outs, n_in: int, dx, step: Prologue | None, dys,
+                   group: "ArGroup | None" = None, stream=None, epi=None) -> None:
+        """sicu_gemv_fused: dys[i] = epi[i](W_i (step applied to dx)),
+        optionally all-reduced over group (one matrix)."""
+        n = len(dws)
+        w_arr = (C.c_void_p * n)(*[_ptr(w) for w in dws])
+        y_arr = (C.c_void_p * n)(*[_ptr(y) for y in dys])
+        o_arr = (C.c_int64 * n)(*n_outs)
+        e_arr = (C.c_int32 * n)(*epi) if epi is not None else None
+        pro = C.byref(step) if step is not None else None
+        self.check(self.lib.sicu_gemv_fused(wtype, n, w_arr, o_arr, n_in, _ptr(dx), pro, e_arr, y_arr,
+                                            group.handle if group is not None else None, _ptr(stream)))
+
+    def rms_norm(self, dx, dw, n: int, m: int, eps: float, dy, dres=None, dsum=None, stream=None) -> None:
+        self.check(self.lib.sicu_rms_norm(_ptr(dx), _ptr(dres), _ptr(dsum), _ptr(dw), n, m, eps, _ptr(dy),
+                                          _ptr(stream)))
+
+    def swiglu(self, dx, dup, n: int, m: int, dy, stream=None) -> None:
+        self.check(self.lib.sicu_swiglu(_ptr(dx), _ptr(dup), n, m, _ptr(dy), _ptr(stream)))
 
     def row_to_f32(self, wtype: int, dw, n_in: int, rows, dout, stream=None) -> None:
         arr = (C.c_int64 * len(rows))(*rows)

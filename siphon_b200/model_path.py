@@ -12,10 +12,17 @@ benchmark configs (synthetic Q4_K_M-style weights generated on the device):
   the rest;
 * ``prefill``: m tokens at once through sicu_gemm_prefill_f32.
 
-The attention, normalisation, RoPE and SwiGLU steps between the products are
-not part of this path; each product reads a fixed activation buffer of its
+With ``steps=True`` the decode step also runs the activation steps between
+the products the way the reference's forward pass does (engine.c:313-315,
+367-379, 387-389), each fused into the product that reads its result
+(sicu_gemv_fused): the residual add and RMS norm before Wq/Wk/Wv, before
+W_gate/W_up and before the output head, and SwiGLU split into a silu
+epilogue on W_gate's output and a multiply in W_down's prologue. The
+residual stream starts from a fixed embedding row. Attention and RoPE are not
+part of this path: Wo reads a fixed activation in place of the attention
+output. Without ``steps`` each product reads a fixed activation buffer of its
 input length, so a step is the matrix work of one token (or one prompt) and
-nothing else, and its time is a lower bound on a full forward step.
+nothing else.
 
 Tensor parallelism (``world > 1``) follows the layout the 32B-class configs
 name: Wq/Wk/Wv, W_gate/W_up and the output head are split by output rows
@@ -128,10 +135,11 @@ class MatrixPath:
     sequence of a decode step / a prefill over them."""
 
     def __init__(self, sicu, sh: LlamaShape, device, world: int = 1, rank: int = 0, group=None, seed: int = 0,
-                 max_tokens: int = 1, fused: bool = False):
+                 max_tokens: int = 1, fused: bool = False, steps: bool = False):
         import torch
         self.s, self.sh, self.dev, self.world, self.group = sicu, sh, device, world, group
         self.ar = None
+        self.steps = steps
         self.shard = tp_partition(sh, world, rank)
         self.shapes = shard_shapes(sh, self.shard)
         self.layers = []
@@ -157,6 +165,15 @@ class MatrixPath:
         self.x_model, self.x_attn, self.x_ff = act(sh.n_embd), act(nq), act(nff)
         self.y = {name: torch.empty(m, self.shapes[name][0], device=device) for name in self.shapes}
         self.weight_bytes = step_weight_bytes(sh, world, rank)
+        if steps:
+            # norm weights near 1 (replicated on every rank), two residual
+            # stream buffers used in turn
+            def norm_w():
+                return 1.0 + 0.1 * torch.randn(sh.n_embd, device=device, generator=gen)
+            self.attn_norm = [norm_w() for _ in range(sh.n_layer)]
+            self.ffn_norm = [norm_w() for _ in range(sh.n_layer)]
+            self.out_norm = norm_w()
+            self.resid = [torch.empty(sh.n_embd, device=device) for _ in range(2)]
         if fused and world > 1:
             import torch.distributed as dist
             self.ar = sicu.ar_create(world, rank, sh.n_embd)
@@ -184,6 +201,8 @@ class MatrixPath:
     def decode_step(self, stream) -> int:
         """Launch one token's products on `stream`; returns the number of
         library kernel launches."""
+        if self.steps:
+            return self._decode_step_steps(stream)
         if self.ar is not None:
             return self._decode_step_fused(stream)
         s, h, y = self.s, stream.cuda_stream, self.y
@@ -240,6 +259,57 @@ class MatrixPath:
             n += 3
         th, wh = self.head
         s.gemv_f32(th, wh, d, self.shapes["head"][0], x, y["head"], stream=h)
+        return n + 1
+
+    def _decode_step_steps(self, stream) -> int:
+        """One token with the activation steps fused into the products:
+        per layer h += (previous W_down output); Wq/Wk/Wv of norm(h); h += Wo
+        output; W_gate/W_up of norm(h), the gate output written through silu;
+        W_down of silu(gate) * up; after the last layer the head of
+        norm(h + W_down output). The residual sums are written by the
+        products that norm them (sum_out). Row-split products all-reduce in
+        the kernel (fused groups) or through NCCL. y["gate"] ends up holding
+        silu(gate)."""
+        from .lib import EPI_NONE, EPI_SILU, mul_step, rms_norm_step
+        s, h, y, d, eps = self.s, stream.cuda_stream, self.y, self.sh.n_embd, self.sh.rms_eps
+        (nq, _), (nkv, _) = self.shapes["q"], self.shapes["k"]
+        nff = self.shapes["gate"][0]
+        cur, res = self.x_model[0], None      # residual stream so far, and the output still to be added
+        nxt = 0
+        n = 0
+        for il, lay in enumerate(self.layers):
+            (tq, wq), (tk, wk), (tv, wv) = lay["q"], lay["k"], lay["v"]
+            out = self.resid[nxt]
+            step = rms_norm_step(self.attn_norm[il], eps, res, out)
+            if tv == tq:
+                s.gemv_fused(tq, [wq, wk, wv], [nq, nkv, nkv], d, cur, step, [y["q"], y["k"], y["v"]], stream=h)
+                n += 1
+            else:
+                s.gemv_fused(tq, [wq, wk], [nq, nkv], d, cur, step, [y["q"], y["k"]], stream=h)
+                s.gemv_fused(tv, [wv], [nkv], d, out, rms_norm_step(self.attn_norm[il], eps), [y["v"]], stream=h)
+                n += 2
+            cur, nxt = out, 1 - nxt
+            to, wo = lay["o"]
+            s.gemv_fused(to, [wo], [d], nq, self.x_attn[0], None, [y["o"]], group=self.ar, stream=h)
+            if self.ar is None:
+                self._allreduce(y["o"])
+            (tg, wg), (_, wu) = lay["gate"], lay["up"]
+            out = self.resid[nxt]
+            # SwiGLU split in two: silu in the gate product's epilogue (once
+            # per element), the product with up in W_down's prologue
+            s.gemv_fused(tg, [wg, wu], [nff, nff], d, cur, rms_norm_step(self.ffn_norm[il], eps, y["o"][0], out),
+                         [y["gate"], y["up"]], stream=h, epi=[EPI_SILU, EPI_NONE])
+            cur, nxt = out, 1 - nxt
+            td, wd = lay["down"]
+            s.gemv_fused(td, [wd], [d], nff, y["gate"][0], mul_step(y["up"][0]), [y["down"]], group=self.ar,
+                         stream=h)
+            if self.ar is None:
+                self._allreduce(y["down"])
+            res = y["down"][0]
+            n += 3
+        th, wh = self.head
+        s.gemv_fused(th, [wh], [self.shapes["head"][0]], d, cur, rms_norm_step(self.out_norm, eps, res),
+                     [y["head"]], stream=h)
         return n + 1
 
     def prefill(self, stream, m: int) -> None:

@@ -18,6 +18,13 @@ Contents:
   dequant.npz per type: two rows of bytes and si_dequant_row outputs.
   f16.npz     f32 -> f16 of edge values and random bit patterns, and a
               digest of the f16 -> f32 table over all 65536 halves.
+  steps.npz   the activation steps between products: si_expf and si_silu
+              of edge values and random floats over the polynomial's whole
+              range, and si_rms_scale of rows of 256 and 5120 floats at two
+              epsilons, among them rows whose mean of squares lies exactly
+              halfway between two floats (the last two rows of rows256: the
+              same values in two orders, whose sequential double sums round
+              the mean to different floats).
 """
 
 from __future__ import annotations
@@ -58,6 +65,41 @@ def quant_inputs() -> np.ndarray:
     spiky = np.zeros(n); spiky[::37] = rng.standard_normal(len(spiky[::37]))
     rows.append(spiky)
     return np.stack(rows).astype(np.float32)
+
+
+def halfway_rows() -> np.ndarray:
+    """Rows of 256 floats whose f32 mean of squares is decided by the
+    reference's summation order. x0 = 16.279024 (0x41823b71) squares to t0
+    with t0 + 247 exactly halfway between two multiples of the f32 spacing
+    of the mean times 256 (the lower one even), so rounding the mean is a tie
+    that goes down. Eight elements of 2^-23 (squares 2^-46) follow x0 in the
+    second row: each is below half a double ulp of the running sum and is
+    lost, the tie stands and the mean rounds down. In the third row they come
+    first, add up to 2^-43 and survive, the sum is above halfway and the mean
+    rounds up. The first row has zeros in their place (an exact tie)."""
+    x0 = np.array([0x41823B71], np.uint32).view(np.float32)[0]
+    tiny = np.float32(2.0 ** -23)
+    a = np.ones(256, np.float32); a[0] = x0; a[1:9] = tiny
+    c = np.ones(256, np.float32); c[0:8] = tiny; c[8] = x0
+    z = np.ones(256, np.float32); z[0] = x0; z[1:9] = 0.0
+    return np.stack([z, a, c])
+
+
+def steps_inputs():
+    rng = np.random.default_rng(4321)
+    edge = np.array([0.0, -0.0, 1.0, -1.0, 88.0, 88.7, 89.0, -87.0, -88.0, -103.0, -104.0, 126.0 * 0.6931472,
+                     -126.0 * 0.6931472, 130.0, -130.0, 150.0, -150.0, 192.0 * 0.6931472, 200.0, -200.0, 1e-30,
+                     -1e-30, 1e-45, 3e38, -3e38, np.inf, -np.inf], np.float32)
+    ex = np.concatenate([edge, rng.standard_normal(4000) * 8, rng.uniform(-220, 220, 4000),
+                         rng.standard_normal(1000) * 1e-3]).astype(np.float32)
+    r256 = [rng.standard_normal(256) * s for s in (1.0, 1e-3, 40.0)]
+    r256.append(np.zeros(256))
+    r256.append(rng.standard_normal(256) * 1e20)                # squares overflow to inf: scale 0
+    spread = rng.standard_normal(256) * np.exp2(rng.uniform(-40, 20, 256))
+    r256.append(spread)                                         # squares over 120 binades
+    r256 = np.concatenate([np.stack(r256).astype(np.float32), halfway_rows()])
+    r5120 = np.stack([rng.standard_normal(5120) * s for s in (1.0, 0.05, 3.0)]).astype(np.float32)
+    return ex, r256, r5120
 
 
 def main() -> None:
@@ -109,6 +151,15 @@ def main() -> None:
     table = np.array([ref.lib.si_f16_to_f32(i) for i in range(65536)], np.float32)
     digest = hashlib.sha256(table.tobytes()).hexdigest()
     np.savez_compressed(OUT / "f16.npz", f32=f, f16=h, table_sha256=np.array(digest))
+
+    ex, r256, r5120 = steps_inputs()
+    eps = np.array([1e-5, 1e-6], np.float32)
+    np.savez_compressed(OUT / "steps.npz", ex=ex,
+                        expf=np.array([ref.expf(float(v)) for v in ex], np.float32),
+                        silu=np.array([ref.silu(float(v)) for v in ex], np.float32),
+                        eps=eps, rows256=r256, rows5120=r5120,
+                        scale256=np.array([[ref.rms_scale(r, float(e)) for e in eps] for r in r256], np.float32),
+                        scale5120=np.array([[ref.rms_scale(r, float(e)) for e in eps] for r in r5120], np.float32))
     print("wrote", sorted(p.name for p in OUT.glob("*.npz")))
 
 

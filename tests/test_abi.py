@@ -105,3 +105,38 @@ def test_allreduce_group_checks_run_on_host(so):
     assert so.lib.sicu_gemv_ar(Q.F16, 4096, 256, 256, 16, 8192, None, None) == L.SICU_ENOTSUP
     assert so.lib.sicu_gemv_ar(Q.Q4_K, 4096, 300, 256, 16, 8192, None, None) == L.SICU_EINVAL
     assert so.lib.sicu_gemv_ar(Q.Q4_K, 4096, 256, 256, 16, 8192, None, None) == L.SICU_EINVAL   # no group
+
+
+def test_activation_step_checks_run_on_host(so):
+    """sicu_gemv_fused / sicu_rms_norm / sicu_swiglu reject malformed steps
+    before any CUDA call (fake, aligned device addresses; no device)."""
+    one = (C.c_void_p * 1)(0x10000)
+    outs = (C.c_void_p * 1)(0x20000)
+    rows = (C.c_int64 * 1)(64)
+
+    def fused(step, n_in=256):
+        return so.lib.sicu_gemv_fused(Q.Q4_K, 1, one, rows, n_in, 0x30000, C.byref(step) if step else None,
+                                      None, outs, None, None)
+
+    assert fused(L.Prologue(7, 0.0, None, None, None, None)) == L.SICU_EINVAL            # unknown kind
+    assert fused(L.Prologue(L.PRO_RMS_NORM, 1e-5, None, None, None, None)) == L.SICU_EINVAL  # no weight
+    assert fused(L.Prologue(L.PRO_RMS_NORM, 1e-5, 0x40004, None, None, None)) == L.SICU_EINVAL  # misaligned
+    assert fused(L.Prologue(L.PRO_RMS_NORM, -1.0, 0x40000, None, None, None)) == L.SICU_EINVAL  # eps < 0
+    assert fused(L.Prologue(L.PRO_RMS_NORM, 1e-5, 0x40000, None, 0x30000, None)) == L.SICU_EINVAL  # sum_out == x
+    assert fused(L.Prologue(L.PRO_RMS_NORM, 1e-5, 0x40000, None, 0x20000, None)) == L.SICU_EINVAL  # sum_out == y
+    assert fused(L.Prologue(L.PRO_SWIGLU, 0.0, None, None, None, None)) == L.SICU_EINVAL       # no up vector
+    assert fused(L.Prologue(L.PRO_MUL, 0.0, None, None, None, None)) == L.SICU_EINVAL          # no up vector
+    bad_epi = (C.c_int32 * 1)(5)
+    assert so.lib.sicu_gemv_fused(Q.Q4_K, 1, one, rows, 256, 0x30000, None, bad_epi, outs, None, None) == L.SICU_EINVAL
+    assert "epilogue" in so.last_error()
+    # well-formed: refused only for want of an initialised device
+    assert fused(L.Prologue(L.PRO_RMS_NORM, 1e-5, 0x40000, 0x50000, 0x60000, None)) == L.SICU_EINVAL
+    assert "sicu_init" in so.last_error()
+    assert fused(L.Prologue(L.PRO_SWIGLU, 0.0, None, None, None, 0x50000)) == L.SICU_EINVAL
+    assert "sicu_init" in so.last_error()
+    assert fused(None) == L.SICU_EINVAL and "sicu_init" in so.last_error()
+    assert so.lib.sicu_swiglu(0x10000, 0x20000, 12, 1, 0x30000, None) == L.SICU_EINVAL      # 12 % 8
+    assert "multiple of 8" in so.last_error()
+    assert so.lib.sicu_rms_norm(0x10000, None, None, None, 256, 1, 1e-5, 0x30000, None) == L.SICU_EINVAL
+    assert so.lib.sicu_rms_norm(0x10000, None, 0x10000, 0x20000, 256, 1, 1e-5, 0x30000, None) == L.SICU_EINVAL
+    assert "overlaps" in so.last_error()

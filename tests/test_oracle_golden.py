@@ -45,3 +45,25 @@ def test_f16_conversions_match_golden(oracle, golden_dir):
     assert (got == g["f16"]).all()
     table = np.array([oracle.f16_to_f32(i) for i in range(65536)], np.float32)
     assert hashlib.sha256(table.tobytes()).hexdigest() == str(g["table_sha256"])
+
+
+def test_activation_steps_match_golden(oracle, golden_dir):
+    g = np.load(golden_dir / "steps.npz")
+    ex = g["ex"]
+    assert (np.array([oracle.expf(float(v)) for v in ex], np.float32).view(np.uint32) == g["expf"].view(np.uint32)).all()
+    assert (np.array([oracle.silu(float(v)) for v in ex], np.float32).view(np.uint32) == g["silu"].view(np.uint32)).all()
+    for rows, scales in ((g["rows256"], g["scale256"]), (g["rows5120"], g["scale5120"])):
+        for i, r in enumerate(rows):
+            got = np.array([oracle.rms_scale(r, float(e)) for e in g["eps"]], np.float32)
+            assert (got.view(np.uint32) == scales[i].view(np.uint32)).all(), f"row {i}"
+
+
+def test_halfway_rows_depend_on_summation_order(golden_dir):
+    """The fixture's last two rows hold the same values, yet the reference's
+    scales differ: a kernel must follow the reference's sequential sum there,
+    not any exact or reordered sum."""
+    g = np.load(golden_dir / "steps.npz")
+    rows, sc = g["rows256"], g["scale256"]
+    a, c = rows[-2], rows[-1]
+    assert sorted(a.tolist()) == sorted(c.tolist())
+    assert (sc[-2] != sc[-1]).all()

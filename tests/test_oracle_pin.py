@@ -85,3 +85,18 @@ def test_scalar_and_avx2_q8_0_forms_differ_rarely(oracle):
     b = oracle.quant_q8_0(x, scalar=True).reshape(-1, 34)
     frac = float((a != b).any(axis=1).mean())
     assert frac < 1e-3
+
+
+def test_activation_steps_bit_identical_to_reference(oracle, reference):
+    rng = np.random.default_rng(77)
+    xs = np.concatenate([rng.standard_normal(3000) * 10, rng.uniform(-230, 230, 3000)]).astype(np.float32)
+    for v in xs:
+        v = float(v)
+        assert np.float32(oracle.expf(v)).view(np.uint32) == np.float32(reference.expf(v)).view(np.uint32), v
+        assert np.float32(oracle.silu(v)).view(np.uint32) == np.float32(reference.silu(v)).view(np.uint32), v
+    for n in (256, 4096, 5120, 8192):
+        for s in (1e-4, 1.0, 100.0):
+            x = (rng.standard_normal(n) * s).astype(np.float32)
+            for eps in (1e-5, 1e-6):
+                a, b = np.float32(oracle.rms_scale(x, eps)), np.float32(reference.rms_scale(x, eps))
+                assert a.view(np.uint32) == b.view(np.uint32)

@@ -299,7 +299,7 @@ def _time_graph(torch, g, stream, reps, world, dev) -> float:
     return max_over_ranks(e0.elapsed_time(e1), world, dev)
 
 
-def model_decode(torch, s, shape, dev, stream, world, rank, group, reps, fused=False, steps=True) -> dict:
+def model_decode(torch, s, shape, dev, stream, world, rank, group, reps, fused=False, steps=False) -> dict:
     """Decode tok/s of the matrix path of `shape` (batch 1), tensor parallel
     over the world: every weight matrix of one token per step, with (steps)
     the residual adds, RMS norms and SwiGLU between them fused into the
@@ -449,6 +449,10 @@ def model_metrics(torch, s, dev, stream, world, rank, quick: bool) -> dict:
                                   if world > 1 else "configs[4] Qwen2.5-32B shape, batch 1, matrix path, one GPU",
                         **model_decode(torch, s, sm.QWEN25_32B, dev, stream, world, rank, None, reps,
                                        fused=world > 1)}
+    out["tp_decode_steps"] = {"config": "as tp_decode, with the residual adds, RMS norms and SwiGLU between the "
+                                        "products fused into them (sicu_gemv_fused)",
+                              **model_decode(torch, s, sm.QWEN25_32B, dev, stream, world, rank, None, reps,
+                                             fused=world > 1, steps=True)}
     if world > 1:
         out["tp_decode_nccl"] = {"config": "as tp_decode, the all-reduces as NCCL calls between the matvecs",
                                  **model_decode(torch, s, sm.QWEN25_32B, dev, stream, world, rank, None, reps)}
@@ -463,12 +467,16 @@ def model_metrics(torch, s, dev, stream, world, rank, quick: bool) -> dict:
     if world == 1:
         out["decode"] = {"config": "configs[2] TinyLlama-1.1B shape, batch 1, matrix path",
                          **model_decode(torch, s, sm.TINYLLAMA, dev, stream, 1, 0, None, reps * 4)}
+        out["decode_steps"] = {"config": "as decode, with the residual adds, RMS norms and SwiGLU between the "
+                                         "products fused into them (sicu_gemv_fused)",
+                               **model_decode(torch, s, sm.TINYLLAMA, dev, stream, 1, 0, None, reps * 4, steps=True)}
         out["prefill"] = {"config": "configs[3] Llama-3-8B shape, 512-token prompt, matrix path",
                           **model_prefill(torch, s, sm.LLAMA3_8B, dev, stream, 1, 0, None, 512, max(2, reps // 2))}
     out["scope"] = ("every weight-matrix product of the forward pass (per layer Wq, Wk, Wv, Wo, W_gate, W_up, "
-                    "W_down; then the output head) with synthetic Q4_K_M-style weights; attention, norms, RoPE "
-                    "and SwiGLU between them are outside the matrix path and not run, so these rates are upper "
-                    "bounds for a full forward step")
+                    "W_down; then the output head) with synthetic Q4_K_M-style weights; the *_steps lines also run "
+                    "the residual adds, RMS norms and SwiGLU between them, fused into the products; attention and "
+                    "RoPE are not run (Wo reads a fixed activation), so these rates are upper bounds for a full "
+                    "forward step")
     return out
 
 

@@ -44,3 +44,30 @@ def test_greedy_decode_128_tokens_token_identical(sicu, model):
     finally:
         cpu.close()
         gpu.close()
+
+
+def test_cuda_backend_dump_passes_reference_golden_check(sicu, model, tmp_path):
+    """The reference's golden protocol (src/cmd_run.c:132-248) on a dump made
+    through the CUDA backend: the reference CLI (CPU backend, scalar kernels)
+    teacher-forces its tokens and finds every logit identical."""
+    import os
+    import subprocess
+    from oracle.oracle import RefEngine
+    from siphon_b200 import slgd
+    cli = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "oracle", "_ref", "siphon")
+    if not os.path.exists(cli):
+        pytest.skip("reference CLI oracle/_ref/siphon not built")
+    prompt = np.random.default_rng(5).integers(0, synth_model.SMALL.n_vocab, 16).tolist()
+    gpu = RefEngine(model, use_cuda=True, n_ctx=256, scalar=True)
+    try:
+        g = slgd.record(gpu.forward, prompt, 32)
+    finally:
+        gpu.close()
+    path = slgd.write(tmp_path / "gpu.slgd", g.tokens, g.logits, g.n_prompt)
+    r = subprocess.run([cli, "run", "--golden", str(path), "--ctx", "256", "-t", "2", str(model)],
+                       capture_output=True, text=True, env=dict(os.environ, SI_SCALAR="1"), timeout=600)
+    assert r.returncode == 0, r.stdout + r.stderr
+    assert "result: PASS" in r.stdout
+    assert "prefill logits: max abs diff 0.0000" in r.stdout
+    assert "decode  logits: max abs diff 0.0000" in r.stdout
+    assert "argmax flips: 0 total" in r.stdout

@@ -12,6 +12,7 @@ from __future__ import annotations
 import pytest
 
 from siphon_b200 import model_path as mp
+from siphon_b200 import quant as Q
 from siphon_b200 import synth_model as sm
 from tests.gpu_util import assert_bits_equal, host
 
@@ -58,3 +59,116 @@ def test_decode_step_with_steps_matches_oracle(sicu, oracle, shape):
     assert_bits_equal(host(m.resid[1]), cur, "residual stream")
     assert_bits_equal(host(m.y["head"][0]), logits, "logits")
     m.close()
+
+
+def _free_port() -> int:
+    import socket
+    with socket.socket() as sk:
+        sk.bind(("127.0.0.1", 0))
+        return sk.getsockname()[1]
+
+
+def _tp_rank(rank, world, port, q):
+    """One rank of the tensor-parallel step flow: a decode step with the
+    all-reduces fused into Wo / W_down and the steps fused into the products,
+    then rank 0 replays the whole step on the CPU from every rank's shards
+    (rank-order f32 sums for the row-split products) and every rank checks
+    its residual stream, W_down sum and head shard bit for bit."""
+    import datetime
+    import os
+
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from oracle.oracle import Oracle
+    from siphon_b200 import lib
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120))
+    m = None
+    try:
+        s = lib.load()
+        s.init(rank)
+        orc = Oracle()
+        shape = sm.LlamaShape(2, 1024, 2048, 16, 4, 2048, 10000.0, 1e-5, 1024)
+        dev = torch.device("cuda", rank)
+        m = mp.MatrixPath(s, shape, dev, world, rank, None, seed=9, fused=True, steps=True)
+        st = torch.cuda.Stream(device=dev)
+        with torch.cuda.stream(st):
+            m.decode_step(st)
+        torch.cuda.synchronize()
+        assert s.status() == 0
+        mine = {"layers": [{k: (t, host(w)) for k, (t, w) in lay.items()} for lay in m.layers],
+                "head": (m.head[0], host(m.head[1])), "x_attn": host(m.x_attn[0])}
+        shards = [None] * world
+        dist.all_gather_object(shards, mine)
+        eps, d = shape.rms_eps, shape.n_embd
+        cur, res = host(m.x_model[0]), None
+
+        def gemv(wt, w, n_out, a):
+            return orc.gemv(wt, w, a.size, n_out, orc.quantize_pair(wt, a[None, :])[0])
+
+        def rank_sum(parts):
+            total = parts[0].copy()
+            for p in parts[1:]:
+                total = (total + p).astype(np.float32)
+            return total
+
+        for il in range(shape.n_layer):
+            h, a = orc.rms_norm(cur, host(m.attn_norm[il]), eps, res)
+            o = rank_sum([gemv(*sh["layers"][il]["o"], d, sh["x_attn"]) for sh in shards])
+            h2, a2 = orc.rms_norm(h, host(m.ffn_norm[il]), eps, o)
+            parts = []
+            for sh in shards:
+                (tg, wg), (tu, wu), (td, wd) = sh["layers"][il]["gate"], sh["layers"][il]["up"], sh["layers"][il]["down"]
+                nff = wg.size // Q.row_bytes(tg, d)
+                gate, up = gemv(tg, wg, nff, a2), gemv(tu, wu, nff, a2)
+                parts.append(gemv(td, wd, d, orc.swiglu(gate, up)))
+            down = rank_sum(parts)
+            cur, res = h2, down
+        _, a = orc.rms_norm(cur, host(m.out_norm), eps, res)
+        th, wh = shards[rank]["head"]
+        logits = gemv(th, wh, wh.size // Q.row_bytes(th, d), a)
+        assert_bits_equal(host(m.resid[1]), cur, f"rank {rank}: residual stream")
+        assert_bits_equal(host(m.y["down"][0]), down, f"rank {rank}: W_down sum")
+        assert_bits_equal(host(m.y["head"][0]), logits, f"rank {rank}: head shard")
+        torch.cuda.synchronize()
+        dist.barrier()
+        if rank == 0:
+            q.put(("ok", None))
+    except BaseException as e:
+        q.put(("fail", f"rank {rank}: {type(e).__name__}: {e}"))
+        raise
+    finally:
+        try:
+            if m is not None:
+                m.close()
+        finally:
+            dist.destroy_process_group()
+
+
+def test_tensor_parallel_step_flow_matches_oracle():
+    import torch
+    ngpu = torch.cuda.device_count()
+    if ngpu < 2:
+        pytest.skip("needs two or more GPUs")
+    world = 2 if ngpu < 4 else 4
+    import torch.multiprocessing as tmp
+    ctx = tmp.get_context("spawn")
+    q = ctx.SimpleQueue()
+    port = _free_port()
+    procs = [ctx.Process(target=_tp_rank, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=600)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    msgs = []
+    while not q.empty():
+        msgs.append(q.get())
+    assert all(p.exitcode == 0 for p in procs), msgs
+    assert ("ok", None) in msgs, msgs

@@ -4,6 +4,9 @@ captured on, runnable under `ncu` on one GPU:
     python -m siphon_b200.profile_cases flat      # gemv_flat_kernel<Q4_K>, 4 x 27648x5120
     python -m siphon_b200.profile_cases ar        # gemv_kernel<Q4_K, AR> beside the plain one, 5120x13824
     python -m siphon_b200.profile_cases prefill   # prefill_kernel<Q4_K>, 4096x4096, 512 tokens
+    python -m siphon_b200.profile_cases steps     # Wq/Wk/Wv of the 32B shape (5120 -> 5120+1024+1024,
+                                                  # Q4_K) with the residual add + RMS norm fused,
+                                                  # beside the same launch without the step
 
 Each case runs a few launches (the summaries' `-s` skips the first ones) and
 exits non-zero if the library reports a device-side status bit.
@@ -52,8 +55,19 @@ def main(case: str, reps: int = 4) -> int:
         y = torch.empty(m, n, device=dev)
         for _ in range(2):
             s.gemm_prefill_f32(wt, w, n, n, x, m, y)
+    elif case == "steps":
+        wt, n_in, outs = Q.Q4_K, 5120, [5120, 1024, 1024]
+        ws = [device_weights(wt, n, n_in, seed=1 + i, device=dev) for i, n in enumerate(outs)]
+        x = torch.randn(n_in, device=dev)
+        r = torch.randn(n_in, device=dev)
+        gam = 1.0 + 0.1 * torch.randn(n_in, device=dev)
+        h = torch.empty(n_in, device=dev)
+        ys = [torch.empty(n, device=dev) for n in outs]
+        for _ in range(reps):
+            s.gemv_multi(wt, ws, outs, n_in, x, ys)
+            s.gemv_fused(wt, ws, outs, n_in, x, lib.rms_norm_step(gam, 1e-6, r, h), ys)
     else:
-        raise SystemExit(f"unknown case {case!r} (flat, ar, prefill)")
+        raise SystemExit(f"unknown case {case!r} (flat, ar, prefill, steps)")
     torch.cuda.synchronize()
     st = s.status()
     print(case, "status", st)

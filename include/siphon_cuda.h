@@ -311,6 +311,17 @@ SICU_API int sicu_rms_norm(const float *dx, const float *dres, float *dsum, cons
                            float eps, float *dy, void *stream);
 SICU_API int sicu_swiglu(const float *dx, const float *dup, int64_t n, int64_t m, float *dy, void *stream);
 
+/* ---- attention softmax ------------------------------------------------------
+ * dy_r = softmax(dx_r) for m rows of n floats, as the reference's attention
+ * computes it (src/engine.c:124-130 with si_softmax, src/kernels.c:855-890):
+ * the row maximum, exp(x - max) through the exp polynomial in groups of 8 with
+ * each group's sum in an 8-wide horizontal add's lane order added into a
+ * double, the last n % 8 elements through libm's expf (restated as this image's
+ * glibc computes it on hosts with FMA), then every element times
+ * (float)(1 / sum). Bit-identical to the reference for finite inputs.
+ * In place (dx == dy) allowed. A building block of the device attention. */
+SICU_API int sicu_softmax(const float *dx, float *dy, int64_t n, int64_t m, void *stream);
+
 /* ---- dequantisation --------------------------------------------------------
  * Rows rows[0..nrows) (host array) of W into dout[nrows][n_in] f32, reference
  * semantics. Replaces cpu_row_to_f32 (src/backend.c:122-131) with

@@ -88,6 +88,10 @@ class Oracle:
         L.orc_rms_norm.restype = None
         L.orc_swiglu.argtypes = [_f32, _f32, C.c_int, _f32]
         L.orc_swiglu.restype = None
+        L.orc_softmax.argtypes = [_f32, _f32, C.c_int]
+        L.orc_softmax.restype = None
+        L.orc_expf_restated_mismatches.argtypes = [C.c_uint32, C.c_uint32, C.c_uint32]
+        L.orc_expf_restated_mismatches.restype = C.c_long
 
     # -- conversions / quantizers ------------------------------------------
     def f16_to_f32(self, h: int) -> float:
@@ -151,6 +155,13 @@ class Oracle:
         x, g = _as_f32(x).reshape(-1), _as_f32(g).reshape(-1)
         y = np.zeros_like(x)
         self.lib.orc_swiglu(x, g, x.size, y)
+        return y
+
+    def softmax(self, x) -> np.ndarray:
+        """The attention softmax of one row (row max, then si_softmax)."""
+        x = _as_f32(x).reshape(-1)
+        y = np.zeros_like(x)
+        self.lib.orc_softmax(x, y, x.size)
         return y
 
     def silu_vec(self, x) -> np.ndarray:
@@ -263,6 +274,8 @@ class Reference:
             getattr(L, name).restype = C.c_float
         L.si_rms_scale.argtypes = [_f32, C.c_int, C.c_float]
         L.si_rms_scale.restype = C.c_float
+        L.si_softmax.argtypes = [_f32, _f32, C.c_int, C.c_float]
+        L.si_softmax.restype = None
 
     @property
     def impl(self) -> str:
@@ -307,6 +320,18 @@ class Reference:
     def rms_scale(self, x, eps: float) -> float:
         x = _as_f32(x).reshape(-1)
         return self.lib.si_rms_scale(x, x.size, eps)
+
+    def softmax(self, x) -> np.ndarray:
+        """The reference's attention softmax: its row-max loop
+        (src/engine.c:124-128) written here, then its si_softmax."""
+        x = _as_f32(x).reshape(-1)
+        mx = -np.inf
+        for v in x:
+            if v > mx:
+                mx = v
+        y = np.zeros_like(x)
+        self.lib.si_softmax(y, x, x.size, np.float32(mx))
+        return y
 
     def dequant_row(self, t: int, x: np.ndarray, n: int) -> np.ndarray:
         y = np.zeros(n, np.float32)

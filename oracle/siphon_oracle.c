@@ -19,6 +19,8 @@
  *     RMS scale ......................... src/kernels.c:892-900
  *     residual add, rms_norm_mul ........ src/engine.c:12-18, 369, 379
  *     swiglu_row ........................ src/engine.c:162-179
+ *     attention softmax (row max, si_softmax) src/engine.c:124-130,
+ *                                         src/kernels.c:855-890
  *
  * Integer partial sums are order-free, so they are written here in whatever
  * order reads best. Every floating-point operation is written one rounding
@@ -638,4 +640,82 @@ ORC_API void orc_swiglu(const float *x, const float *g, int n, float *y) {
     int i = 0;
     for (; i < body; i++) y[i] = orc_silu(x[i]) * g[i];
     for (; i < n; i++) y[i] = x[i] / (1.0f + expf(0.0f - x[i])) * g[i];
+}
+
+/* the attention's softmax: the row maximum (src/engine.c:124-128), then
+ * si_softmax (src/kernels.c:855-890): 8-wide groups through the polynomial,
+ * each group's lanes summed as the AVX2 horizontal add orders them, into a
+ * double; the n % 8 tail through libm's expf; y *= (float)(1 / sum) */
+ORC_API void orc_softmax(const float *x, float *y, int n) {
+    float max = -INFINITY;
+    for (int j = 0; j < n; j++)
+        if (x[j] > max) max = x[j];
+    double sum = 0;
+    int i = 0;
+    for (; i + 7 < n; i += 8) {
+        float v[8];
+        for (int k = 0; k < 8; k++) v[k] = orc_expf(x[i + k] - max);
+        for (int k = 0; k < 8; k++) y[i + k] = v[k];
+        const float s0 = v[4] + v[0], s1 = v[5] + v[1], s2 = v[6] + v[2], s3 = v[7] + v[3];
+        const float t0 = s0 + s2, t1 = s1 + s3;
+        sum += (double)(t0 + t1);
+    }
+    for (; i < n; ++i) {
+        const float val = expf(x[i] - max);
+        sum += (double)val;
+        y[i] = val;
+    }
+    const float scale = (float)(1.0 / sum);
+    for (i = 0; i < n; ++i) y[i] *= scale;
+}
+
+/* The device softmax's restatement of libm's expf (the table-driven
+ * algorithm of this image's glibc, FMA build), for checking that algorithm
+ * against the host's expf on the CPU. Not used by the other functions here,
+ * which call libm itself as the reference does. */
+static const uint64_t orc_exp2tab[32] = {
+    0x3ff0000000000000ull, 0x3fefd9b0d3158574ull, 0x3fefb5586cf9890full, 0x3fef9301d0125b51ull,
+    0x3fef72b83c7d517bull, 0x3fef54873168b9aaull, 0x3fef387a6e756238ull, 0x3fef1e9df51fdee1ull,
+    0x3fef06fe0a31b715ull, 0x3feef1a7373aa9cbull, 0x3feedea64c123422ull, 0x3feece086061892dull,
+    0x3feebfdad5362a27ull, 0x3feeb42b569d4f82ull, 0x3feeab07dd485429ull, 0x3feea47eb03a5585ull,
+    0x3feea09e667f3bcdull, 0x3fee9f75e8ec5f74ull, 0x3feea11473eb0187ull, 0x3feea589994cce13ull,
+    0x3feeace5422aa0dbull, 0x3feeb737b0cdc5e5ull, 0x3feec49182a3f090ull, 0x3feed503b23e255dull,
+    0x3feee89f995ad3adull, 0x3feeff76f2fb5e47ull, 0x3fef199bdd85529cull, 0x3fef3720dcef9069ull,
+    0x3fef5818dcfba487ull, 0x3fef7c97337b9b5full, 0x3fefa4afa2a490daull, 0x3fefd0765b6e4540ull,
+};
+ORC_API float orc_expf_libm_restated(float x) {
+    const uint32_t ux = f32_bits(x), abstop = (ux >> 20) & 0x7ffu;
+    if (abstop >= (f32_bits(88.0f) >> 20)) {
+        if (ux == 0xff800000u) return 0.0f;
+        if (abstop >= 0x7f8u) return x + x;
+        if (x > 0x1.62e42ep6f) return INFINITY;
+        if (x < -0x1.9fe368p6f) return 0.0f;
+    }
+    const double invln2n = 0x1.71547652b82fep+0 * 32, shift = 0x1.8p+52;
+    const double xd = (double)x, z = invln2n * xd;
+    double kd = z + shift;
+    uint64_t ki;
+    memcpy(&ki, &kd, 8);
+    kd -= shift;
+    const double r = fma(invln2n, xd, -kd);
+    uint64_t t = orc_exp2tab[ki % 32] + (ki << 47);
+    double sv;
+    memcpy(&sv, &t, 8);
+    const double c0 = 0x1.c6af84b912394p-5 / 32 / 32 / 32, c1 = 0x1.ebfce50fac4f3p-3 / 32 / 32,
+                 c2 = 0x1.62e42ff0c52d6p-1 / 32;
+    const double p = fma(c0, r, c1), r2 = r * r;
+    double y = fma(c2, r, 1.0);
+    y = fma(p, r2, y);
+    return (float)(y * sv);
+}
+
+/* count of inputs in [lo_bits, hi_bits] (stride) where the restatement and
+ * libm's expf differ */
+ORC_API long orc_expf_restated_mismatches(uint32_t lo_bits, uint32_t hi_bits, uint32_t stride) {
+    long bad = 0;
+    for (uint64_t u = lo_bits; u <= hi_bits; u += stride) {
+        const float x = bits_f32((uint32_t)u);
+        if (f32_bits(expf(x)) != f32_bits(orc_expf_libm_restated(x))) bad++;
+    }
+    return bad;
 }

@@ -864,6 +864,18 @@ int sicu_swiglu(const float *dx, const float *dup, int64_t n, int64_t m, float *
     return SICU_OK;
 }
 
+int sicu_softmax(const float *dx, float *dy, int64_t n, int64_t m, void *stream) {
+    if (n <= 0 || n > INT32_MAX || m < 0 || m > INT32_MAX)
+        return fail(SICU_EINVAL, "softmax: bad shape n=%lld m=%lld", (long long)n, (long long)m);
+    if (!dx || !dy) return fail(SICU_EINVAL, "softmax: null pointer");
+    if (dx != dy && overlaps(dx, dy, 4 * n * m)) return fail(SICU_EINVAL, "softmax: rows overlap partially");
+    DevState *ds;
+    if (int rc = current(ds)) return rc;
+    if (m == 0) return SICU_OK;
+    if (launch_softmax(dx, dy, n, m, (cudaStream_t)stream)) return cuda_fail(cudaGetLastError(), "softmax launch");
+    return SICU_OK;
+}
+
 int sicu_row_to_f32(uint32_t wtype, const void *dw, int64_t n_in, const int64_t *rows, int64_t nrows, float *dout,
                     void *stream) {
     uint32_t blck, bytes;

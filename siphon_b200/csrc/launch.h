@@ -119,6 +119,10 @@ int launch_mul(const float *x, const float *up, int64_t n, float *y, cudaStream_
 // y = silu(y), n floats in place (F16 products with a silu epilogue)
 int launch_silu_inplace(float *y, int64_t n, cudaStream_t st);
 
+// the reference's attention softmax over m rows of n floats (row maximum
+// taken here); in place allowed
+int launch_softmax(const float *x, float *y, int64_t n, int64_t m, cudaStream_t st);
+
 // all-reduce of src[len] into dst[len] over the group (one delivery)
 int launch_allreduce(const ArDev &a, const float *src, float *dst, int *status, int num_sms, cudaStream_t st);
 

@@ -1,0 +1,157 @@
+// Softmax over rows on the device, bit-identical with the reference's
+// si_softmax (src/kernels.c:855-890) with the row maximum its attention code
+// passes (src/engine.c:124-130): 8-element groups through the exp polynomial
+// (expf_ref), each group's sum in the lane order of an 8-wide horizontal add
+// added into a double, the n % 8 tail through libm's expf (restated below),
+// then every element times (float)(1 / sum).
+#include "prologue.cuh"
+
+namespace sicu {
+
+namespace {
+
+// libm expf as this image's glibc computes it on hosts with FMA (its x86-64
+// FMA build; the table-driven algorithm of ARM's optimized routines): x / ln2
+// scaled by N = 32 and rounded to an integer k with the 1.5 * 2^52 shifter, the
+// remainder r formed with one fused multiply-add, 2^(k/N) from a 32-entry table
+// plus k's integer part in the exponent field, and 2^(r/N) by a degree-3
+// polynomial, all in double, rounded to float once. Special cases as there:
+// -inf -> 0, NaN -> x + x, overflow above 0x1.62e42ep6, 0 below -0x1.9fe368p6.
+// Checked bit for bit against the host's expf on every float in
+// [-0x1.9fe368p6, 0] (tests/test_softmax.py runs the same check on the host).
+// kExp2Tab[i] = bits of 2^(i/32) rounded to the nearest double, minus i << 47.
+__device__ const uint64_t kExp2Tab[32] = {
+    0x3ff0000000000000ull, 0x3fefd9b0d3158574ull, 0x3fefb5586cf9890full, 0x3fef9301d0125b51ull,
+    0x3fef72b83c7d517bull, 0x3fef54873168b9aaull, 0x3fef387a6e756238ull, 0x3fef1e9df51fdee1ull,
+    0x3fef06fe0a31b715ull, 0x3feef1a7373aa9cbull, 0x3feedea64c123422ull, 0x3feece086061892dull,
+    0x3feebfdad5362a27ull, 0x3feeb42b569d4f82ull, 0x3feeab07dd485429ull, 0x3feea47eb03a5585ull,
+    0x3feea09e667f3bcdull, 0x3fee9f75e8ec5f74ull, 0x3feea11473eb0187ull, 0x3feea589994cce13ull,
+    0x3feeace5422aa0dbull, 0x3feeb737b0cdc5e5ull, 0x3feec49182a3f090ull, 0x3feed503b23e255dull,
+    0x3feee89f995ad3adull, 0x3feeff76f2fb5e47ull, 0x3fef199bdd85529cull, 0x3fef3720dcef9069ull,
+    0x3fef5818dcfba487ull, 0x3fef7c97337b9b5full, 0x3fefa4afa2a490daull, 0x3fefd0765b6e4540ull,
+};
+
+__device__ __forceinline__ float expf_libm(float x) {
+    const uint32_t ux = __float_as_uint(x);
+    const uint32_t abstop = (ux >> 20) & 0x7ffu;
+    if (abstop >= (__float_as_uint(88.0f) >> 20)) {
+        if (ux == 0xff800000u) return 0.0f;
+        if (abstop >= 0x7f8u) return __fadd_rn(x, x);
+        if (x > 0x1.62e42ep6f) return __uint_as_float(0x7f800000u);
+        if (x < -0x1.9fe368p6f) return 0.0f;
+    }
+    const double invln2n = 0x1.71547652b82fep+0 * 32;
+    const double shift = 0x1.8p+52;
+    const double xd = (double)x;
+    const double z = __dmul_rn(invln2n, xd);
+    double kd = __dadd_rn(z, shift);
+    const uint64_t ki = (uint64_t)__double_as_longlong(kd);
+    kd = __dsub_rn(kd, shift);
+    const double r = __fma_rn(invln2n, xd, -kd);
+    uint64_t t = kExp2Tab[ki % 32];
+    t += ki << 47;
+    const double s = __longlong_as_double((long long)t);
+    const double c0 = 0x1.c6af84b912394p-5 / 32 / 32 / 32, c1 = 0x1.ebfce50fac4f3p-3 / 32 / 32,
+                 c2 = 0x1.62e42ff0c52d6p-1 / 32;
+    const double p = __fma_rn(c0, r, c1);
+    const double r2 = __dmul_rn(r, r);
+    double y = __fma_rn(c2, r, 1.0);
+    y = __fma_rn(p, r2, y);
+    return __double2float_rn(__dmul_rn(y, s));
+}
+
+// The sum of one 8-element group in the lane order of the reference's
+// horizontal add: ((v4 + v0) + (v6 + v2)) + ((v5 + v1) + (v7 + v3)).
+__device__ __forceinline__ float group_sum(const float v[8]) {
+    const float s0 = __fadd_rn(v[4], v[0]), s1 = __fadd_rn(v[5], v[1]);
+    const float s2 = __fadd_rn(v[6], v[2]), s3 = __fadd_rn(v[7], v[3]);
+    return __fadd_rn(__fadd_rn(s0, s2), __fadd_rn(s1, s3));
+}
+
+// One CTA per row (blockDim 256). The reference adds the group sums and then
+// the tail values into a double in index order; the CTA adds them in
+// parallel. As for the RMS norm's mean, the terms are nonnegative, so any
+// order lies within nt 2^-52 of the sequential sum (nt terms), and
+// (float)(1 / sum) is decided when both ends of the widened interval around
+// 1 / S narrow to the same float (1 / s is monotone); otherwise thread 0
+// redoes the sum in the reference's order from the stored values.
+__global__ void __launch_bounds__(256) softmax_kernel(const float *x, float *y, int n) {
+    __shared__ double red[8];
+    __shared__ float bmax[8];
+    __shared__ float out[2];
+    const int64_t off = (int64_t)blockIdx.x * n;
+    const float *xr = x + off;
+    float *yr = y + off;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
+    // the row maximum: the largest element, NaNs never selected, -inf when
+    // there is none (src/engine.c:124-128)
+    float mx = -__int_as_float(0x7f800000);
+    for (int i = tid; i < n; i += blockDim.x) {
+        const float v = xr[i];
+        if (v > mx) mx = v;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float v = __shfl_xor_sync(0xffffffffu, mx, o);
+        if (v > mx) mx = v;
+    }
+    if (lane == 0) bmax[warp] = mx;
+    __syncthreads();
+    mx = bmax[0];
+    for (int w = 1; w < nw; ++w)
+        if (bmax[w] > mx) mx = bmax[w];
+    const int ng = n / 8, body = 8 * ng;
+    double s = 0.0;
+    for (int g = tid; g < ng; g += blockDim.x) {
+        float v[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) v[k] = expf_ref(__fsub_rn(xr[8 * g + k], mx));
+#pragma unroll
+        for (int k = 0; k < 8; ++k) yr[8 * g + k] = v[k];
+        s += (double)group_sum(v);
+    }
+    for (int i = body + tid; i < n; i += blockDim.x) {
+        const float v = expf_libm(__fsub_rn(xr[i], mx));
+        yr[i] = v;
+        s += (double)v;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if (lane == 0) red[warp] = s;
+    __syncthreads();
+    if (tid == 0) {
+        double S = 0.0;
+        for (int w = 0; w < nw; ++w) S += red[w];
+        const double nt = (double)(ng + (n - body));
+        const double q = __ddiv_rn(1.0, S);
+        const double w = nt * 0x1p-50 + 0x1p-49;
+        const float lo = __double2float_rn(__dmul_rd(q, 1.0 - w));
+        const float hi = __double2float_rn(__dmul_ru(q, 1.0 + w));
+        float scale = lo;
+        if (!(lo == hi)) {
+            double t = 0.0;
+            for (int g = 0; g < ng; ++g) {
+                float v[8];
+#pragma unroll
+                for (int k = 0; k < 8; ++k) v[k] = yr[8 * g + k];
+                t = __dadd_rn(t, (double)group_sum(v));
+            }
+            for (int i = body; i < n; ++i) t = __dadd_rn(t, (double)yr[i]);
+            scale = __double2float_rn(__ddiv_rn(1.0, t));
+        }
+        out[0] = scale;
+    }
+    __syncthreads();
+    const float scale = out[0];
+    for (int i = tid; i < n; i += blockDim.x) yr[i] = __fmul_rn(yr[i], scale);
+}
+
+}  // namespace
+
+int launch_softmax(const float *x, float *y, int64_t n, int64_t m, cudaStream_t st) {
+    if (m <= 0 || n <= 0) return 0;
+    softmax_kernel<<<(unsigned)m, 256, 0, st>>>(x, y, (int)n);
+    return cudaPeekAtLastError() == cudaSuccess ? 0 : -2;
+}
+
+}  // namespace sicu

@@ -61,6 +61,7 @@ SIGNATURES = {
                         C.POINTER(C.c_void_p), _vp, _vp],
     "sicu_rms_norm": [_fp, _fp, _fp, _fp, _i64, _i64, C.c_float, _fp, _vp],
     "sicu_swiglu": [_fp, _fp, _i64, _i64, _fp, _vp],
+    "sicu_softmax": [_fp, _fp, _i64, _i64, _vp],
 }
 
 PRO_NONE, PRO_RMS_NORM, PRO_SWIGLU, PRO_MUL = 0, 1, 2, 3
@@ -225,6 +226,10 @@ class SiphonCuda:
 
     def swiglu(self, dx, dup, n: int, m: int, dy, stream=None) -> None:
         self.check(self.lib.sicu_swiglu(_ptr(dx), _ptr(dup), n, m, _ptr(dy), _ptr(stream)))
+
+    def softmax(self, dx, dy, n: int, m: int = 1, stream=None) -> None:
+        """sicu_softmax: the reference's attention softmax over m rows."""
+        self.check(self.lib.sicu_softmax(_ptr(dx), _ptr(dy), n, m, _ptr(stream)))
 
     def row_to_f32(self, wtype: int, dw, n_in: int, rows, dout, stream=None) -> None:
         arr = (C.c_int64 * len(rows))(*rows)

@@ -140,3 +140,12 @@ def test_activation_step_checks_run_on_host(so):
     assert so.lib.sicu_rms_norm(0x10000, None, None, None, 256, 1, 1e-5, 0x30000, None) == L.SICU_EINVAL
     assert so.lib.sicu_rms_norm(0x10000, None, 0x10000, 0x20000, 256, 1, 1e-5, 0x30000, None) == L.SICU_EINVAL
     assert "overlaps" in so.last_error()
+
+
+def test_softmax_checks_run_on_host(so):
+    assert so.lib.sicu_softmax(0x10000, 0x20000, 0, 1, None) == L.SICU_EINVAL       # empty row
+    assert so.lib.sicu_softmax(None, 0x20000, 16, 1, None) == L.SICU_EINVAL
+    assert so.lib.sicu_softmax(0x10000, 0x10004, 16, 1, None) == L.SICU_EINVAL     # partial overlap
+    assert "overlap" in so.last_error()
+    assert so.lib.sicu_softmax(0x10000, 0x10000, 16, 1, None) == L.SICU_EINVAL     # in place: needs a device
+    assert "sicu_init" in so.last_error()

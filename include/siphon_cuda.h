@@ -322,6 +322,34 @@ SICU_API int sicu_swiglu(const float *dx, const float *dup, int64_t n, int64_t m
  * In place (dx == dy) allowed. A building block of the device attention. */
 SICU_API int sicu_softmax(const float *dx, float *dy, int64_t n, int64_t m, void *stream);
 
+/* ---- attention over the f16 KV cache ---------------------------------------
+ * The reference's per-layer attention step (src/engine.c:90-147, 336-366) on
+ * the device, on its cache layout (one layer's base pointers):
+ *   K cache: f16 [n_head_kv][n_ctx][head_dim] (position-major)
+ *   V cache: f16 [n_head_kv][head_dim][n_ctx] (transposed)
+ * sicu_rope rotates n_heads heads of head_dim floats in place with the
+ * position's cos / sin tables (n_rot / 2 entries, device; the engine computes
+ * them with libm, src/engine.c:26-40): pairs (2j, 2j+1) as fma(x0, c, -(x1 s)),
+ * fma(x0, s, x1 c) (neox = 0), or (j, j + head_dim/2) with plain products and
+ * sums (neox != 0); channels from n_rot on unchanged.
+ * sicu_kv_store writes one position's K and V (n_head_kv x head_dim floats
+ * each) into the caches as f16 (round to nearest even).
+ * sicu_attention computes, for every query head h (KV head h / (n_head /
+ * n_head_kv)), the scores of positions 0..pos (f16 dot of the head's q as f16
+ * with each cached K row, times kq_scale), their softmax (sicu_softmax), the
+ * probabilities as f16, and out[h][c] = f16 dot of V row c with them. Every
+ * f16 dot is the reference's scalar si_dot_f16 (src/kernels.c:189-195: exact
+ * products added into a double in index order), so results are bit-identical
+ * to the reference engine run with its scalar kernels (SI_SCALAR=1, the form
+ * the library's parity tests use). pos + 1 <= 32768, head_dim <= 1024. */
+SICU_API int sicu_rope(float *dx, int64_t n_heads, int64_t head_dim, int64_t n_rot, const float *dcos,
+                       const float *dsin, int neox, void *stream);
+SICU_API int sicu_kv_store(const float *dk, const float *dv, void *dk_cache, void *dv_cache, int64_t n_head_kv,
+                           int64_t head_dim, int64_t n_ctx, int64_t pos, void *stream);
+SICU_API int sicu_attention(const float *dq, const void *dk_cache, const void *dv_cache, int64_t n_head,
+                            int64_t n_head_kv, int64_t head_dim, int64_t n_ctx, int64_t pos, float kq_scale,
+                            float *dout, void *stream);
+
 /* ---- dequantisation --------------------------------------------------------
  * Rows rows[0..nrows) (host array) of W into dout[nrows][n_in] f32, reference
  * semantics. Replaces cpu_row_to_f32 (src/backend.c:122-131) with

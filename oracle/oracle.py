@@ -92,6 +92,10 @@ class Oracle:
         L.orc_softmax.restype = None
         L.orc_expf_restated_mismatches.argtypes = [C.c_uint32, C.c_uint32, C.c_uint32]
         L.orc_expf_restated_mismatches.restype = C.c_long
+        L.orc_rope.argtypes = [_f32, C.c_int, C.c_int, C.c_int, _f32, _f32, C.c_int]
+        L.orc_rope.restype = None
+        L.orc_attention.argtypes = [_f32, _u16, _u16, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_float, _f32]
+        L.orc_attention.restype = None
 
     # -- conversions / quantizers ------------------------------------------
     def f16_to_f32(self, h: int) -> float:
@@ -163,6 +167,20 @@ class Oracle:
         y = np.zeros_like(x)
         self.lib.orc_softmax(x, y, x.size)
         return y
+
+    def rope(self, x, n_heads: int, hd: int, n_rot: int, cs, sn, neox: bool = False) -> np.ndarray:
+        y = _as_f32(x).reshape(-1).copy()
+        self.lib.orc_rope(y, n_heads, hd, n_rot, _as_f32(cs), _as_f32(sn), 1 if neox else 0)
+        return y
+
+    def attention(self, q, k_cache, v_cache, n_head: int, n_head_kv: int, hd: int, n_ctx: int, pos: int,
+                  ks: float) -> np.ndarray:
+        """attn_head for every query head; caches as uint16 f16 bits."""
+        out = np.zeros(n_head * hd, np.float32)
+        self.lib.orc_attention(_as_f32(q).reshape(-1), np.ascontiguousarray(k_cache, np.uint16).reshape(-1),
+                               np.ascontiguousarray(v_cache, np.uint16).reshape(-1), n_head, n_head_kv, hd, n_ctx,
+                               pos, ks, out)
+        return out
 
     def silu_vec(self, x) -> np.ndarray:
         """si_silu element by element (no tail rule)."""

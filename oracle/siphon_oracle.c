@@ -21,6 +21,8 @@
  *     swiglu_row ........................ src/engine.c:162-179
  *     attention softmax (row max, si_softmax) src/engine.c:124-130,
  *                                         src/kernels.c:855-890
+ *     rope_apply, attn_head (scalar f16
+ *     dots), the f16 cache writes ........ src/engine.c:42-75, 90-147, 344-362
  *
  * Integer partial sums are order-free, so they are written here in whatever
  * order reads best. Every floating-point operation is written one rounding
@@ -35,6 +37,7 @@
  */
 #include <math.h>
 #include <stdint.h>
+#include <stdlib.h>
 #include <string.h>
 
 #define ORC_API __attribute__((visibility("default")))
@@ -718,4 +721,51 @@ ORC_API long orc_expf_restated_mismatches(uint32_t lo_bits, uint32_t hi_bits, ui
         if (f32_bits(expf(x)) != f32_bits(orc_expf_libm_restated(x))) bad++;
     }
     return bad;
+}
+
+/* rope_apply (src/engine.c:42-75) on n_heads heads in place */
+ORC_API void orc_rope(float *x, int n_heads, int hd, int n_rot, const float *cs, const float *sn, int neox) {
+    const int np = n_rot / 2;
+    for (int hh = 0; hh < n_heads; hh++) {
+        float *v = x + (size_t)hh * hd;
+        for (int j = 0; j < np; j++) {
+            if (!neox) {
+                const float x0 = v[2 * j], x1 = v[2 * j + 1];
+                v[2 * j] = fmaf(x0, cs[j], -(x1 * sn[j]));
+                v[2 * j + 1] = fmaf(x0, sn[j], x1 * cs[j]);
+            } else {
+                const int half = hd / 2;
+                const float x0 = v[j], x1 = v[j + half];
+                v[j] = x0 * cs[j] - x1 * sn[j];
+                v[j + half] = x0 * sn[j] + x1 * cs[j];
+            }
+        }
+    }
+}
+
+static float dot_f16_scalar(int n, const uint16_t *x, size_t sx, const uint16_t *y) {
+    double s = 0.0;
+    for (int i = 0; i < n; i++) s += (double)(orc_f16_to_f32(x[(size_t)i * sx]) * orc_f16_to_f32(y[i]));
+    return (float)s;
+}
+
+/* attn_head (src/engine.c:90-147) for every query head, with the scalar
+ * si_dot_f16 (src/kernels.c:189-195) the reference runs under SI_SCALAR;
+ * caches in the engine's layout (src/engine.c:344-362) */
+ORC_API void orc_attention(const float *q, const uint16_t *kc, const uint16_t *vc, int n_head, int n_head_kv, int hd,
+                           int n_ctx, int pos, float ks, float *out) {
+    const int n_score = pos + 1, gqa = n_head / n_head_kv;
+    float *sc = malloc(sizeof(float) * (size_t)n_score), *pr = malloc(sizeof(float) * (size_t)n_score);
+    uint16_t *pr16 = malloc(2 * (size_t)n_score), *q16 = malloc(2 * (size_t)hd);
+    for (int h = 0; h < n_head; h++) {
+        const int hk = h / gqa;
+        const uint16_t *kh = kc + (size_t)hk * n_ctx * hd, *vh = vc + (size_t)hk * hd * n_ctx;
+        for (int d = 0; d < hd; d++) q16[d] = orc_f32_to_f16(q[(size_t)h * hd + d]);
+        for (int j = 0; j < n_score; j++) sc[j] = dot_f16_scalar(hd, kh + (size_t)j * hd, 1, q16);
+        for (int j = 0; j < n_score; j++) sc[j] = sc[j] * ks;
+        orc_softmax(sc, pr, n_score);
+        for (int j = 0; j < n_score; j++) pr16[j] = orc_f32_to_f16(pr[j]);
+        for (int c = 0; c < hd; c++) out[(size_t)h * hd + c] = dot_f16_scalar(n_score, vh + (size_t)c * n_ctx, 1, pr16);
+    }
+    free(sc); free(pr); free(pr16); free(q16);
 }

@@ -876,6 +876,50 @@ int sicu_softmax(const float *dx, float *dy, int64_t n, int64_t m, void *stream)
     return SICU_OK;
 }
 
+int sicu_rope(float *dx, int64_t n_heads, int64_t head_dim, int64_t n_rot, const float *dcos, const float *dsin,
+              int neox, void *stream) {
+    if (n_heads < 0 || head_dim <= 0 || n_rot < 0 || n_rot > head_dim || n_rot % 2 || (neox && head_dim % 2) ||
+        n_heads * head_dim > INT32_MAX)
+        return fail(SICU_EINVAL, "rope: bad shape");
+    if (!dx || (n_rot && (!dcos || !dsin))) return fail(SICU_EINVAL, "rope: null pointer");
+    DevState *ds;
+    if (int rc = current(ds)) return rc;
+    if (launch_rope(dx, (int)n_heads, (int)head_dim, (int)n_rot, dcos, dsin, neox ? 1 : 0, (cudaStream_t)stream))
+        return cuda_fail(cudaGetLastError(), "rope launch");
+    return SICU_OK;
+}
+
+int sicu_kv_store(const float *dk, const float *dv, void *dk_cache, void *dv_cache, int64_t n_head_kv,
+                  int64_t head_dim, int64_t n_ctx, int64_t pos, void *stream) {
+    if (n_head_kv <= 0 || head_dim <= 0 || n_ctx <= 0 || pos < 0 || pos >= n_ctx || n_head_kv * head_dim > INT32_MAX ||
+        n_ctx > INT32_MAX)
+        return fail(SICU_EINVAL, "kv store: bad shape or position");
+    if (!dk || !dv || !dk_cache || !dv_cache) return fail(SICU_EINVAL, "kv store: null pointer");
+    if (!aligned(dk_cache, 2) || !aligned(dv_cache, 2)) return fail(SICU_EINVAL, "kv store: caches must be 2-byte aligned");
+    DevState *ds;
+    if (int rc = current(ds)) return rc;
+    if (launch_kv_store(dk, dv, dk_cache, dv_cache, (int)n_head_kv, (int)head_dim, (int)n_ctx, (int)pos,
+                        (cudaStream_t)stream))
+        return cuda_fail(cudaGetLastError(), "kv store launch");
+    return SICU_OK;
+}
+
+int sicu_attention(const float *dq, const void *dk_cache, const void *dv_cache, int64_t n_head, int64_t n_head_kv,
+                   int64_t head_dim, int64_t n_ctx, int64_t pos, float kq_scale, float *dout, void *stream) {
+    if (n_head <= 0 || n_head_kv <= 0 || n_head % n_head_kv || head_dim <= 0 || head_dim > 1024 || n_ctx <= 0 ||
+        n_ctx > INT32_MAX || pos < 0 || pos >= n_ctx || n_head * head_dim > INT32_MAX)
+        return fail(SICU_EINVAL, "attention: bad shape or position");
+    if (pos + 1 > 32768) return fail(SICU_EINVAL, "attention: at most 32768 positions per call");
+    if (!dq || !dk_cache || !dv_cache || !dout) return fail(SICU_EINVAL, "attention: null pointer");
+    if (!aligned(dk_cache, 2) || !aligned(dv_cache, 2)) return fail(SICU_EINVAL, "attention: caches must be 2-byte aligned");
+    DevState *ds;
+    if (int rc = current(ds)) return rc;
+    if (launch_attention(dq, dk_cache, dv_cache, (int)n_head, (int)n_head_kv, (int)head_dim, (int)n_ctx, (int)pos,
+                         kq_scale, dout, (cudaStream_t)stream))
+        return cuda_fail(cudaGetLastError(), "attention launch");
+    return SICU_OK;
+}
+
 int sicu_row_to_f32(uint32_t wtype, const void *dw, int64_t n_in, const int64_t *rows, int64_t nrows, float *dout,
                     void *stream) {
     uint32_t blck, bytes;

@@ -122,6 +122,13 @@ int launch_silu_inplace(float *y, int64_t n, cudaStream_t st);
 // the reference's attention softmax over m rows of n floats (row maximum
 // taken here); in place allowed
 int launch_softmax(const float *x, float *y, int64_t n, int64_t m, cudaStream_t st);
+// attention of one position over the f16 caches of one layer (one CTA per
+// query head), RoPE in place, and the K/V store of one position
+int launch_attention(const float *q, const void *kc, const void *vc, int n_head, int n_head_kv, int hd, int n_ctx,
+                     int pos, float ks, float *out, cudaStream_t st);
+int launch_rope(float *x, int n_heads, int hd, int n_rot, const float *cs, const float *sn, int neox, cudaStream_t st);
+int launch_kv_store(const float *k, const float *v, void *kc, void *vc, int n_head_kv, int hd, int n_ctx, int pos,
+                    cudaStream_t st);
 
 // all-reduce of src[len] into dst[len] over the group (one delivery)
 int launch_allreduce(const ArDev &a, const float *src, float *dst, int *status, int num_sms, cudaStream_t st);

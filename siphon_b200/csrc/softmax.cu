@@ -75,13 +75,12 @@ __device__ __forceinline__ float group_sum(const float v[8]) {
 // (float)(1 / sum) is decided when both ends of the widened interval around
 // 1 / S narrow to the same float (1 / s is monotone); otherwise thread 0
 // redoes the sum in the reference's order from the stored values.
-__global__ void __launch_bounds__(256) softmax_kernel(const float *x, float *y, int n) {
+// The softmax of one row by one CTA (every thread calls; blockDim <= 256;
+// xr and yr may be the same row, in global or shared memory).
+__device__ void softmax_row(const float *xr, float *yr, int n) {
     __shared__ double red[8];
     __shared__ float bmax[8];
     __shared__ float out[2];
-    const int64_t off = (int64_t)blockIdx.x * n;
-    const float *xr = x + off;
-    float *yr = y + off;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
     // the row maximum: the largest element, NaNs never selected, -inf when
     // there is none (src/engine.c:124-128)
@@ -144,9 +143,121 @@ __global__ void __launch_bounds__(256) softmax_kernel(const float *x, float *y, 
     __syncthreads();
     const float scale = out[0];
     for (int i = tid; i < n; i += blockDim.x) yr[i] = __fmul_rn(yr[i], scale);
+    __syncthreads();
+}
+
+__global__ void __launch_bounds__(256) softmax_kernel(const float *x, float *y, int n) {
+    const int64_t off = (int64_t)blockIdx.x * n;
+    softmax_row(x + off, y + off, n);
+}
+
+// The reference's f16 dot on the scalar path (si_dot_f16, src/kernels.c:
+// 189-195): exact f32 products of the f16 values added into a double in index
+// order, rounded to f32 at the end. stride_x: element spacing in x.
+__device__ __forceinline__ float dot_f16_seq(const uint16_t *x, int64_t stride_x, const uint16_t *y, int n) {
+    double s = 0.0;
+    for (int i = 0; i < n; ++i) s = __dadd_rn(s, (double)__fmul_rn(h2f(x[(int64_t)i * stride_x]), h2f(y[i])));
+    return __double2float_rn(s);
+}
+
+// One query head per CTA (src/engine.c:90-147, attn_head, on the scalar dot
+// path): q as f16, a score per cached position 0..pos against the head's K
+// rows, times kq_scale, the row's softmax, the probabilities as f16, and per
+// channel the f16 dot of the head's transposed V row with them. Dynamic
+// shared memory: n_score floats (scores, then probabilities) and n_score
+// halves.
+__global__ void __launch_bounds__(256) attention_kernel(const float *q, const uint16_t *kc, const uint16_t *vc,
+                                                        int n_head, int gqa, int hd, int n_ctx, int n_score,
+                                                        float ks, float *out) {
+    extern __shared__ __align__(16) uint8_t sm[];
+    float *sc = reinterpret_cast<float *>(sm);
+    uint16_t *p16 = reinterpret_cast<uint16_t *>(sc + n_score);
+    __shared__ uint16_t q16[1024];
+    const int h = blockIdx.x, hk = h / gqa;
+    for (int d = threadIdx.x; d < hd; d += blockDim.x) q16[d] = (uint16_t)f2h(q[(int64_t)h * hd + d]);
+    __syncthreads();
+    const uint16_t *kh = kc + (int64_t)hk * n_ctx * hd;
+    const uint16_t *vh = vc + (int64_t)hk * hd * n_ctx;
+    for (int j = threadIdx.x; j < n_score; j += blockDim.x)
+        sc[j] = __fmul_rn(dot_f16_seq(kh + (int64_t)j * hd, 1, q16, hd), ks);
+    __syncthreads();
+    softmax_row(sc, sc, n_score);
+    for (int j = threadIdx.x; j < n_score; j += blockDim.x) p16[j] = (uint16_t)f2h(sc[j]);
+    __syncthreads();
+    for (int c = threadIdx.x; c < hd; c += blockDim.x)
+        out[(int64_t)h * hd + c] = dot_f16_seq(vh + (int64_t)c * n_ctx, 1, p16, n_score);
+}
+
+// RoPE in place on n_heads heads of hd floats (src/engine.c:42-75): pairs
+// (2j, 2j+1) rotated as fma(x0, c, -(x1 * s)), fma(x0, s, x1 * c) (the
+// interleaved form), or (j, j + hd/2) with plain products and sums (neox);
+// channels from n_rot on unchanged.
+__global__ void rope_kernel(float *x, int n_heads, int hd, int n_rot, const float *cs, const float *sn, int neox) {
+    const int np = n_rot / 2;
+    const int64_t total = (int64_t)n_heads * np;
+    for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
+        const int hh = (int)(t / np), j = (int)(t % np);
+        float *v = x + (int64_t)hh * hd;
+        const float c = cs[j], s = sn[j];
+        if (!neox) {
+            const float x0 = v[2 * j], x1 = v[2 * j + 1];
+            v[2 * j] = __fmaf_rn(x0, c, -__fmul_rn(x1, s));
+            v[2 * j + 1] = __fmaf_rn(x0, s, __fmul_rn(x1, c));
+        } else {
+            const int half = hd / 2;
+            const float x0 = v[j], x1 = v[j + half];
+            v[j] = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
+            v[j + half] = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
+        }
+    }
+}
+
+// K and V of one position into the f16 caches (src/engine.c:344-362): K
+// position-major [h][n_ctx][hd], V transposed [h][hd][n_ctx].
+__global__ void kv_store_kernel(const float *k, const float *v, uint16_t *kc, uint16_t *vc, int n_head_kv, int hd,
+                                int n_ctx, int pos) {
+    const int total = n_head_kv * hd;
+    for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < total; t += gridDim.x * blockDim.x) {
+        const int hh = t / hd, d = t % hd;
+        kc[((int64_t)hh * n_ctx + pos) * hd + d] = (uint16_t)f2h(k[t]);
+        vc[((int64_t)hh * hd + d) * n_ctx + pos] = (uint16_t)f2h(v[t]);
+    }
 }
 
 }  // namespace
+
+int launch_attention(const float *q, const void *kc, const void *vc, int n_head, int n_head_kv, int hd, int n_ctx,
+                     int pos, float ks, float *out, cudaStream_t st) {
+    const int n_score = pos + 1;
+    const size_t smem = (size_t)n_score * 6 + 16;
+    static bool attr[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!attr[dev & 63]) {
+        if (cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) != cudaSuccess)
+            return -2;
+        attr[dev & 63] = true;
+    }
+    attention_kernel<<<n_head, 256, smem, st>>>(q, static_cast<const uint16_t *>(kc), static_cast<const uint16_t *>(vc),
+                                                n_head, n_head / n_head_kv, hd, n_ctx, n_score, ks, out);
+    return cudaPeekAtLastError() == cudaSuccess ? 0 : -2;
+}
+
+int launch_rope(float *x, int n_heads, int hd, int n_rot, const float *cs, const float *sn, int neox, cudaStream_t st) {
+    const int64_t total = (int64_t)n_heads * (n_rot / 2);
+    if (total <= 0) return 0;
+    rope_kernel<<<(unsigned)((total + 255) / 256 > 1024 ? 1024 : (total + 255) / 256), 256, 0, st>>>(x, n_heads, hd, n_rot,
+                                                                                                   cs, sn, neox);
+    return cudaPeekAtLastError() == cudaSuccess ? 0 : -2;
+}
+
+int launch_kv_store(const float *k, const float *v, void *kc, void *vc, int n_head_kv, int hd, int n_ctx, int pos,
+                    cudaStream_t st) {
+    const int total = n_head_kv * hd;
+    kv_store_kernel<<<(total + 255) / 256, 256, 0, st>>>(k, v, static_cast<uint16_t *>(kc), static_cast<uint16_t *>(vc),
+                                                         n_head_kv, hd, n_ctx, pos);
+    return cudaPeekAtLastError() == cudaSuccess ? 0 : -2;
+}
 
 int launch_softmax(const float *x, float *y, int64_t n, int64_t m, cudaStream_t st) {
     if (m <= 0 || n <= 0) return 0;

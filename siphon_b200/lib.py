@@ -62,6 +62,9 @@ SIGNATURES = {
     "sicu_rms_norm": [_fp, _fp, _fp, _fp, _i64, _i64, C.c_float, _fp, _vp],
     "sicu_swiglu": [_fp, _fp, _i64, _i64, _fp, _vp],
     "sicu_softmax": [_fp, _fp, _i64, _i64, _vp],
+    "sicu_rope": [_fp, _i64, _i64, _i64, _fp, _fp, C.c_int, _vp],
+    "sicu_kv_store": [_fp, _fp, _vp, _vp, _i64, _i64, _i64, _i64, _vp],
+    "sicu_attention": [_fp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, C.c_float, _fp, _vp],
 }
 
 PRO_NONE, PRO_RMS_NORM, PRO_SWIGLU, PRO_MUL = 0, 1, 2, 3
@@ -230,6 +233,20 @@ class SiphonCuda:
     def softmax(self, dx, dy, n: int, m: int = 1, stream=None) -> None:
         """sicu_softmax: the reference's attention softmax over m rows."""
         self.check(self.lib.sicu_softmax(_ptr(dx), _ptr(dy), n, m, _ptr(stream)))
+
+    def rope(self, dx, n_heads: int, head_dim: int, n_rot: int, dcos, dsin, neox: bool = False, stream=None) -> None:
+        self.check(self.lib.sicu_rope(_ptr(dx), n_heads, head_dim, n_rot, _ptr(dcos), _ptr(dsin), 1 if neox else 0,
+                                      _ptr(stream)))
+
+    def kv_store(self, dk, dv, dk_cache, dv_cache, n_head_kv: int, head_dim: int, n_ctx: int, pos: int,
+                 stream=None) -> None:
+        self.check(self.lib.sicu_kv_store(_ptr(dk), _ptr(dv), _ptr(dk_cache), _ptr(dv_cache), n_head_kv, head_dim,
+                                          n_ctx, pos, _ptr(stream)))
+
+    def attention(self, dq, dk_cache, dv_cache, n_head: int, n_head_kv: int, head_dim: int, n_ctx: int, pos: int,
+                  kq_scale: float, dout, stream=None) -> None:
+        self.check(self.lib.sicu_attention(_ptr(dq), _ptr(dk_cache), _ptr(dv_cache), n_head, n_head_kv, head_dim,
+                                           n_ctx, pos, kq_scale, _ptr(dout), _ptr(stream)))
 
     def row_to_f32(self, wtype: int, dw, n_in: int, rows, dout, stream=None) -> None:
         arr = (C.c_int64 * len(rows))(*rows)

@@ -1,0 +1,64 @@
+"""RoPE, the f16 KV-cache store and the per-head attention on the device
+(sicu_rope, sicu_kv_store, sicu_attention) against the oracle's restatement
+of the reference's attention step (src/engine.c:42-147, 336-366; scalar f16
+dots), bit for bit."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from tests.gpu_util import assert_bits_equal, dev, empty_f32, host
+from tests.test_attention import random_cache
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("neox", [False, True])
+def test_rope(sicu, oracle, neox):
+    import torch
+    rng = np.random.default_rng(1)
+    for n_heads, hd, n_rot in ((32, 64, 64), (8, 128, 128), (4, 128, 64)):
+        x = (rng.standard_normal(n_heads * hd) * 3).astype(np.float32)
+        theta = rng.uniform(-50, 50, n_rot // 2)
+        c, s = np.cos(theta).astype(np.float32), np.sin(theta).astype(np.float32)
+        d = dev(x)
+        sicu.rope(d, n_heads, hd, n_rot, dev(c), dev(s), neox=neox)
+        assert_bits_equal(host(d), oracle.rope(x, n_heads, hd, n_rot, c, s, neox=neox), f"rope {n_heads}x{hd}/{n_rot}")
+    del torch
+
+
+def test_kv_store_layout(sicu, oracle):
+    import torch
+    rng = np.random.default_rng(2)
+    nkv, hd, n_ctx = 3, 64, 40
+    kc = torch.zeros(nkv * n_ctx * hd, dtype=torch.int16, device="cuda")
+    vc = torch.zeros(nkv * hd * n_ctx, dtype=torch.int16, device="cuda")
+    want_k = np.zeros((nkv, n_ctx, hd), np.uint16)
+    want_v = np.zeros((nkv, hd, n_ctx), np.uint16)
+    for pos in (0, 5, 39):
+        k = (rng.standard_normal(nkv * hd) * 4).astype(np.float32)
+        v = (rng.standard_normal(nkv * hd) * 4).astype(np.float32)
+        sicu.kv_store(dev(k), dev(v), kc, vc, nkv, hd, n_ctx, pos)
+        want_k[:, pos, :] = oracle.convert_f16(k).view(np.uint16).reshape(nkv, hd)
+        want_v[:, :, pos] = oracle.convert_f16(v).view(np.uint16).reshape(nkv, hd)
+    assert (host(kc).view(np.uint16) == want_k.reshape(-1)).all()
+    assert (host(vc).view(np.uint16) == want_v.reshape(-1)).all()
+
+
+@pytest.mark.parametrize("n_head,n_head_kv,hd,n_ctx", [(8, 2, 64, 512), (32, 8, 128, 2048), (4, 4, 64, 64)])
+def test_attention(sicu, oracle, n_head, n_head_kv, hd, n_ctx):
+    import torch
+    rng = np.random.default_rng(n_ctx + hd)
+    k, v = random_cache(rng, n_head_kv, hd, n_ctx)
+    kd = torch.from_numpy(k.view(np.int16).reshape(-1).copy()).cuda()
+    vd = torch.from_numpy(v.view(np.int16).reshape(-1).copy()).cuda()
+    ks = float(np.float32(1.0 / np.sqrt(hd)))
+    for pos in sorted({0, 1, 7, 8, 63, n_ctx // 2 + 3, n_ctx - 1}):
+        if pos >= n_ctx:
+            continue
+        q = (rng.standard_normal(n_head * hd) * 2).astype(np.float32)
+        out = empty_f32(n_head * hd)
+        sicu.attention(dev(q), kd, vd, n_head, n_head_kv, hd, n_ctx, pos, ks, out)
+        assert_bits_equal(host(out), oracle.attention(q, k, v, n_head, n_head_kv, hd, n_ctx, pos, ks),
+                          f"attention pos {pos}")

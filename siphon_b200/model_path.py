@@ -135,11 +135,14 @@ class MatrixPath:
     sequence of a decode step / a prefill over them."""
 
     def __init__(self, sicu, sh: LlamaShape, device, world: int = 1, rank: int = 0, group=None, seed: int = 0,
-                 max_tokens: int = 1, fused: bool = False, steps: bool = False):
+                 max_tokens: int = 1, fused: bool = False, steps: bool = False, attention: bool = False,
+                 n_ctx: int = 256):
         import torch
         self.s, self.sh, self.dev, self.world, self.group = sicu, sh, device, world, group
         self.ar = None
-        self.steps = steps
+        self.steps = steps or attention
+        self.attention = attention
+        self.pos = 0
         self.shard = tp_partition(sh, world, rank)
         self.shapes = shard_shapes(sh, self.shard)
         self.layers = []
@@ -165,7 +168,7 @@ class MatrixPath:
         self.x_model, self.x_attn, self.x_ff = act(sh.n_embd), act(nq), act(nff)
         self.y = {name: torch.empty(m, self.shapes[name][0], device=device) for name in self.shapes}
         self.weight_bytes = step_weight_bytes(sh, world, rank)
-        if steps:
+        if self.steps:
             # norm weights near 1 (replicated on every rank), two residual
             # stream buffers used in turn
             def norm_w():
@@ -174,6 +177,30 @@ class MatrixPath:
             self.ffn_norm = [norm_w() for _ in range(sh.n_layer)]
             self.out_norm = norm_w()
             self.resid = [torch.empty(sh.n_embd, device=device) for _ in range(2)]
+        if attention:
+            # f16 caches per layer in the engine's layout (K [kv][n_ctx][hd],
+            # V [kv][hd][n_ctx]), zero; RoPE tables of every position (the
+            # engine's theta recurrence in f32; cos/sin by numpy here)
+            import numpy as np
+            hd, nkv = sh.head_dim, len(self.shard.kv_heads)
+            group = sh.n_head // sh.n_head_kv
+            if not (len(self.shard.heads) == nkv * group or nkv == 1):
+                raise ValueError("a rank's query heads must cover whole KV groups")
+            self.n_ctx = n_ctx
+            self.kc = [torch.zeros(nkv * n_ctx * hd, dtype=torch.int16, device=device) for _ in range(sh.n_layer)]
+            self.vc = [torch.zeros(nkv * hd * n_ctx, dtype=torch.int16, device=device) for _ in range(sh.n_layer)]
+            theta_scale = np.float32(np.power(np.float32(sh.rope_base), np.float32(-2.0 / hd)))
+            cos = np.zeros((n_ctx, hd // 2), np.float32)
+            sin = np.zeros((n_ctx, hd // 2), np.float32)
+            for p in range(n_ctx):
+                th = np.float32(p)
+                for j in range(hd // 2):
+                    cos[p, j], sin[p, j] = np.cos(th), np.sin(th)
+                    th = np.float32(th * theta_scale)
+            self.rope_cos = torch.from_numpy(cos).to(device)
+            self.rope_sin = torch.from_numpy(sin).to(device)
+            self.kq_scale = float(np.float32(1.0) / np.sqrt(np.float32(hd)))
+            self.x_attn_buf = torch.empty(len(self.shard.heads) * hd, device=device)
         if fused and world > 1:
             import torch.distributed as dist
             self.ar = sicu.ar_create(world, rank, sh.n_embd)
@@ -289,8 +316,22 @@ class MatrixPath:
                 s.gemv_fused(tv, [wv], [nkv], d, out, rms_norm_step(self.attn_norm[il], eps), [y["v"]], stream=h)
                 n += 2
             cur, nxt = out, 1 - nxt
+            xa = self.x_attn[0]
+            if self.attention:
+                # RoPE on q and k, this position's K / V into the caches, the
+                # heads' attention over positions 0..pos (src/engine.c:336-366)
+                hd, p = self.sh.head_dim, self.pos
+                nh, nkvl = nq // hd, nkv // hd
+                c, sn = self.rope_cos[p], self.rope_sin[p]
+                s.rope(y["q"], nh, hd, hd, c, sn, stream=h)
+                s.rope(y["k"], nkvl, hd, hd, c, sn, stream=h)
+                s.kv_store(y["k"], y["v"], self.kc[il], self.vc[il], nkvl, hd, self.n_ctx, p, stream=h)
+                s.attention(y["q"], self.kc[il], self.vc[il], nh, nkvl, hd, self.n_ctx, p, self.kq_scale,
+                            self.x_attn_buf, stream=h)
+                xa = self.x_attn_buf
+                n += 4
             to, wo = lay["o"]
-            s.gemv_fused(to, [wo], [d], nq, self.x_attn[0], None, [y["o"]], group=self.ar, stream=h)
+            s.gemv_fused(to, [wo], [d], nq, xa, None, [y["o"]], group=self.ar, stream=h)
             if self.ar is None:
                 self._allreduce(y["o"])
             (tg, wg), (_, wu) = lay["gate"], lay["up"]

@@ -172,3 +172,55 @@ def test_tensor_parallel_step_flow_matches_oracle():
         msgs.append(q.get())
     assert all(p.exitcode == 0 for p in procs), msgs
     assert ("ok", None) in msgs, msgs
+
+
+@pytest.mark.parametrize("shape", [sm.SMALL, sm.LlamaShape(2, 1024, 2816, 16, 4, 2048, 10000.0, 1e-6, 1024)],
+                         ids=["small", "wide"])
+def test_decode_steps_with_attention_match_oracle(sicu, oracle, shape):
+    """Three consecutive positions through the device step with attention:
+    RoPE on q and k, the f16 caches, each head's attention over the positions
+    so far feeding Wo. The oracle replays every step in the reference's order
+    (its caches filled the same way) and the logits and the last layer's
+    attention output must agree bit for bit at every position."""
+    import numpy as np
+    import torch
+    dev = torch.device("cuda", 0)
+    n_ctx = 16
+    m = mp.MatrixPath(sicu, shape, dev, seed=5, attention=True, n_ctx=n_ctx)
+    stream = torch.cuda.Stream()
+    eps, d, hd = shape.rms_eps, shape.n_embd, shape.head_dim
+    nh, nkv = m.shapes["q"][0] // hd, m.shapes["k"][0] // hd
+    W = [{k: (t, host(w)) for k, (t, w) in lay.items()} for lay in m.layers]
+    cos, sin = host(m.rope_cos), host(m.rope_sin)
+    kc = [np.zeros((nkv, n_ctx, hd), np.uint16) for _ in m.layers]
+    vc = [np.zeros((nkv, hd, n_ctx), np.uint16) for _ in m.layers]
+    x0 = host(m.x_model[0])
+    for pos in range(3):
+        m.pos = pos
+        with torch.cuda.stream(stream):
+            m.decode_step(stream)
+        torch.cuda.synchronize()
+        assert sicu.status() == 0
+        # the device flow starts every step from the same embedding row
+        cur, res = x0, None
+        for il, lw in enumerate(W):
+            h, a = oracle.rms_norm(cur, host(m.attn_norm[il]), eps, res)
+            q = _gemv(oracle, *lw["q"], nh * hd, a)
+            k = _gemv(oracle, *lw["k"], nkv * hd, a)
+            v = _gemv(oracle, *lw["v"], nkv * hd, a)
+            q = oracle.rope(q, nh, hd, hd, cos[pos], sin[pos])
+            k = oracle.rope(k, nkv, hd, hd, cos[pos], sin[pos])
+            kc[il][:, pos, :] = oracle.convert_f16(k).view(np.uint16).reshape(nkv, hd)
+            vc[il][:, :, pos] = oracle.convert_f16(v).view(np.uint16).reshape(nkv, hd)
+            att = oracle.attention(q, kc[il], vc[il], nh, nkv, hd, n_ctx, pos, m.kq_scale)
+            o = _gemv(oracle, *lw["o"], d, att)
+            h2, a2 = oracle.rms_norm(h, host(m.ffn_norm[il]), eps, o)
+            gate = _gemv(oracle, *lw["gate"], m.shapes["gate"][0], a2)
+            up = _gemv(oracle, *lw["up"], m.shapes["up"][0], a2)
+            down = _gemv(oracle, *lw["down"], d, oracle.swiglu(gate, up))
+            cur, res = h2, down
+        _, a = oracle.rms_norm(cur, host(m.out_norm), eps, res)
+        logits = _gemv(oracle, m.head[0], host(m.head[1]), m.shapes["head"][0], a)
+        assert_bits_equal(host(m.x_attn_buf), att, f"pos {pos}: last layer's attention output")
+        assert_bits_equal(host(m.y["head"][0]), logits, f"pos {pos}: logits")
+    m.close()

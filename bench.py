@@ -299,14 +299,21 @@ def _time_graph(torch, g, stream, reps, world, dev) -> float:
     return max_over_ranks(e0.elapsed_time(e1), world, dev)
 
 
-def model_decode(torch, s, shape, dev, stream, world, rank, group, reps, fused=False, steps=False) -> dict:
+def model_decode(torch, s, shape, dev, stream, world, rank, group, reps, fused=False, steps=False,
+                 attention_ctx=0) -> dict:
     """Decode tok/s of the matrix path of `shape` (batch 1), tensor parallel
     over the world: every weight matrix of one token per step, with (steps)
     the residual adds, RMS norms and SwiGLU between them fused into the
     products (sicu_gemv_fused). fused: the all-reduces ride in the matvecs
     too, else NCCL all-reduces."""
     from siphon_b200 import model_path as mp
-    m = mp.MatrixPath(s, shape, dev, world, rank, group, seed=4, fused=fused, steps=steps)
+    if attention_ctx:
+        # the whole step but the embedding lookup, at the last position of an
+        # attention_ctx-long context
+        m = mp.MatrixPath(s, shape, dev, world, rank, group, seed=4, fused=fused, attention=True, n_ctx=attention_ctx)
+        m.pos = attention_ctx - 1
+    else:
+        m = mp.MatrixPath(s, shape, dev, world, rank, group, seed=4, fused=fused, steps=steps)
     with torch.cuda.stream(stream):
         for _ in range(2):
             launches = m.decode_step(stream)
@@ -453,6 +460,10 @@ def model_metrics(torch, s, dev, stream, world, rank, quick: bool) -> dict:
                                         "products fused into them (sicu_gemv_fused)",
                               **model_decode(torch, s, sm.QWEN25_32B, dev, stream, world, rank, None, reps,
                                              fused=world > 1, steps=True)}
+    out["tp_decode_full"] = {"config": "as tp_decode_steps, plus RoPE, the f16 KV-cache store and attention over a "
+                                       "512-position context (the token at position 511)",
+                             **model_decode(torch, s, sm.QWEN25_32B, dev, stream, world, rank, None, reps,
+                                            fused=world > 1, attention_ctx=512)}
     if world > 1:
         out["tp_decode_nccl"] = {"config": "as tp_decode, the all-reduces as NCCL calls between the matvecs",
                                  **model_decode(torch, s, sm.QWEN25_32B, dev, stream, world, rank, None, reps)}
@@ -470,13 +481,18 @@ def model_metrics(torch, s, dev, stream, world, rank, quick: bool) -> dict:
         out["decode_steps"] = {"config": "as decode, with the residual adds, RMS norms and SwiGLU between the "
                                          "products fused into them (sicu_gemv_fused)",
                                **model_decode(torch, s, sm.TINYLLAMA, dev, stream, 1, 0, None, reps * 4, steps=True)}
+        out["decode_full"] = {"config": "as decode_steps, plus RoPE, the f16 KV-cache store and attention over a "
+                                        "512-position context (the token at position 511): every step of the "
+                                        "reference's forward pass but the embedding lookup",
+                              **model_decode(torch, s, sm.TINYLLAMA, dev, stream, 1, 0, None, reps * 4,
+                                             attention_ctx=512)}
         out["prefill"] = {"config": "configs[3] Llama-3-8B shape, 512-token prompt, matrix path",
                           **model_prefill(torch, s, sm.LLAMA3_8B, dev, stream, 1, 0, None, 512, max(2, reps // 2))}
     out["scope"] = ("every weight-matrix product of the forward pass (per layer Wq, Wk, Wv, Wo, W_gate, W_up, "
                     "W_down; then the output head) with synthetic Q4_K_M-style weights; the *_steps lines also run "
-                    "the residual adds, RMS norms and SwiGLU between them, fused into the products; attention and "
-                    "RoPE are not run (Wo reads a fixed activation), so these rates are upper bounds for a full "
-                    "forward step")
+                    "the residual adds, RMS norms and SwiGLU between them, fused into the products (Wo reading a "
+                    "fixed activation); decode_full also runs RoPE, the KV cache and attention: the whole step but "
+                    "the embedding lookup")
     return out
 
 

@@ -349,6 +349,17 @@ SICU_API int sicu_kv_store(const float *dk, const float *dv, void *dk_cache, voi
 SICU_API int sicu_attention(const float *dq, const void *dk_cache, const void *dv_cache, int64_t n_head,
                             int64_t n_head_kv, int64_t head_dim, int64_t n_ctx, int64_t pos, float kq_scale,
                             float *dout, void *stream);
+/* The three above in one launch, the engine's order for one layer and
+ * position: RoPE on q (n_head heads) and k (n_head_kv heads) with the
+ * position's tables, k and v stored into the caches at pos, then the
+ * attention; dq and dk are left unrotated (the rotated values live only in
+ * the launch). Same results as sicu_rope x2 + sicu_kv_store + sicu_attention.
+ * With sicu_set_overlap(1) the matvec that follows may launch while it runs
+ * (and stream its weights). pos + 1 <= 30000. */
+SICU_API int sicu_attention_step(const float *dq, const float *dk, const float *dv, void *dk_cache, void *dv_cache,
+                                 const float *dcos, const float *dsin, int64_t n_head, int64_t n_head_kv,
+                                 int64_t head_dim, int64_t n_rot, int neox, int64_t n_ctx, int64_t pos,
+                                 float kq_scale, float *dout, void *stream);
 
 /* ---- dequantisation --------------------------------------------------------
  * Rows rows[0..nrows) (host array) of W into dout[nrows][n_in] f32, reference

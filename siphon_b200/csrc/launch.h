@@ -129,6 +129,11 @@ int launch_attention(const float *q, const void *kc, const void *vc, int n_head,
 int launch_rope(float *x, int n_heads, int hd, int n_rot, const float *cs, const float *sn, int neox, cudaStream_t st);
 int launch_kv_store(const float *k, const float *v, void *kc, void *vc, int n_head_kv, int hd, int n_ctx, int pos,
                     cudaStream_t st);
+// the three in one launch (overlap: unused; the launch always waits for the
+// previous kernel to finish)
+int launch_attention_step(const float *q, const float *k, const float *v, void *kc, void *vc, const float *cs,
+                          const float *sn, int n_head, int n_head_kv, int hd, int n_rot, int neox, int n_ctx, int pos,
+                          float ks, float *out, int overlap, cudaStream_t st);
 
 // all-reduce of src[len] into dst[len] over the group (one delivery)
 int launch_allreduce(const ArDev &a, const float *src, float *dst, int *status, int num_sms, cudaStream_t st);

@@ -188,6 +188,108 @@ __global__ void __launch_bounds__(256) attention_kernel(const float *q, const ui
         out[(int64_t)h * hd + c] = dot_f16_seq(vh + (int64_t)c * n_ctx, 1, p16, n_score);
 }
 
+// dot_f16_seq with x's elements 8 at a time: the eight loads of a chunk are
+// issued before its eight additions, which stay in index order.
+__device__ __forceinline__ float dot_f16_seq8(const uint16_t *x, const uint16_t *y, int n) {
+    double s = 0.0;
+    int i = 0;
+    for (; i + 8 <= n; i += 8) {
+        uint16_t a[8], b[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) { a[k] = x[i + k]; b[k] = y[i + k]; }
+#pragma unroll
+        for (int k = 0; k < 8; ++k) s = __dadd_rn(s, (double)__fmul_rn(h2f(a[k]), h2f(b[k])));
+    }
+    for (; i < n; ++i) s = __dadd_rn(s, (double)__fmul_rn(h2f(x[i]), h2f(y[i])));
+    return __double2float_rn(s);
+}
+
+// The attention step of one layer and position in one launch, one CTA per
+// query head: the head's q and its KV head's k rotated (the rotation of
+// rope_kernel) in shared memory, this position's K and V stored into the
+// caches (by the first CTA of each KV group; the others only read earlier
+// positions), the scores of positions 0..pos (this position's from the f16 k
+// in shared memory, the same bits the cache holds), softmax, f16
+// probabilities and the value dots (this position's V from shared memory).
+// Same results as rope_kernel + kv_store_kernel + attention_kernel. Launched
+// after the producing matvec has finished (launched early behind it, the
+// decode step measured slower: 3.0 ms per TinyLlama-shape token against 1.86),
+// it lets the next matvec launch early and stream its weights meanwhile.
+__global__ void __launch_bounds__(256) attention_step_kernel(const float *q, const float *k, const float *v,
+                                                             uint16_t *kc, uint16_t *vc, const float *cs,
+                                                             const float *sn, int n_head, int gqa, int hd, int n_rot,
+                                                             int neox, int n_ctx, int pos, float ks, float *out) {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    extern __shared__ __align__(16) uint8_t sm[];
+    const int n_score = pos + 1;
+    float *sc = reinterpret_cast<float *>(sm);
+    uint16_t *p16 = reinterpret_cast<uint16_t *>(sc + n_score);
+    __shared__ __align__(16) float qf[1024], kf[1024];
+    __shared__ __align__(16) uint16_t q16[1024], k16[1024], v16[1024];
+    const int h = blockIdx.x, hk = h / gqa, tid = threadIdx.x;
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    for (int d = tid; d < hd; d += blockDim.x) {
+        qf[d] = q[(int64_t)h * hd + d];
+        kf[d] = k[(int64_t)hk * hd + d];
+        v16[d] = (uint16_t)f2h(v[(int64_t)hk * hd + d]);
+    }
+    __syncthreads();
+    const int np = n_rot / 2;
+    for (int j = tid; j < np; j += blockDim.x) {
+        const float c = cs[j], s = sn[j];
+        const int i0 = neox ? j : 2 * j, i1 = neox ? j + hd / 2 : 2 * j + 1;
+        const float q0 = qf[i0], q1 = qf[i1], k0 = kf[i0], k1 = kf[i1];
+        if (!neox) {
+            qf[i0] = __fmaf_rn(q0, c, -__fmul_rn(q1, s));
+            qf[i1] = __fmaf_rn(q0, s, __fmul_rn(q1, c));
+            kf[i0] = __fmaf_rn(k0, c, -__fmul_rn(k1, s));
+            kf[i1] = __fmaf_rn(k0, s, __fmul_rn(k1, c));
+        } else {
+            qf[i0] = __fsub_rn(__fmul_rn(q0, c), __fmul_rn(q1, s));
+            qf[i1] = __fadd_rn(__fmul_rn(q0, s), __fmul_rn(q1, c));
+            kf[i0] = __fsub_rn(__fmul_rn(k0, c), __fmul_rn(k1, s));
+            kf[i1] = __fadd_rn(__fmul_rn(k0, s), __fmul_rn(k1, c));
+        }
+    }
+    __syncthreads();
+    uint16_t *kh = kc + (int64_t)hk * n_ctx * hd;
+    uint16_t *vh = vc + (int64_t)hk * hd * n_ctx;
+    const bool writer = (h % gqa) == 0;
+    for (int d = tid; d < hd; d += blockDim.x) {
+        q16[d] = (uint16_t)f2h(qf[d]);
+        k16[d] = (uint16_t)f2h(kf[d]);
+        if (writer) {
+            kh[(int64_t)pos * hd + d] = k16[d];
+            vh[(int64_t)d * n_ctx + pos] = v16[d];
+        }
+    }
+    __syncthreads();
+    for (int j = tid; j < n_score; j += blockDim.x) {
+        const uint16_t *row = j == pos ? k16 : kh + (int64_t)j * hd;
+        sc[j] = __fmul_rn(dot_f16_seq8(row, q16, hd), ks);
+    }
+    __syncthreads();
+    softmax_row(sc, sc, n_score);
+    for (int j = tid; j < n_score; j += blockDim.x) p16[j] = (uint16_t)f2h(sc[j]);
+    __syncthreads();
+    for (int c = tid; c < hd; c += blockDim.x) {
+        // positions 0..pos-1 from the cache, then this position's v
+        const uint16_t *row = vh + (int64_t)c * n_ctx;
+        double s = 0.0;
+        int j = 0;
+        for (; j + 8 <= pos; j += 8) {
+            uint16_t a[8], b[8];
+#pragma unroll
+            for (int t = 0; t < 8; ++t) { a[t] = row[j + t]; b[t] = p16[j + t]; }
+#pragma unroll
+            for (int t = 0; t < 8; ++t) s = __dadd_rn(s, (double)__fmul_rn(h2f(a[t]), h2f(b[t])));
+        }
+        for (; j < pos; ++j) s = __dadd_rn(s, (double)__fmul_rn(h2f(row[j]), h2f(p16[j])));
+        s = __dadd_rn(s, (double)__fmul_rn(h2f(v16[c]), h2f(p16[pos])));
+        out[(int64_t)h * hd + c] = __double2float_rn(s);
+    }
+}
+
 // RoPE in place on n_heads heads of hd floats (src/engine.c:42-75): pairs
 // (2j, 2j+1) rotated as fma(x0, c, -(x1 * s)), fma(x0, s, x1 * c) (the
 // interleaved form), or (j, j + hd/2) with plain products and sums (neox);
@@ -241,6 +343,36 @@ int launch_attention(const float *q, const void *kc, const void *vc, int n_head,
     attention_kernel<<<n_head, 256, smem, st>>>(q, static_cast<const uint16_t *>(kc), static_cast<const uint16_t *>(vc),
                                                 n_head, n_head / n_head_kv, hd, n_ctx, n_score, ks, out);
     return cudaPeekAtLastError() == cudaSuccess ? 0 : -2;
+}
+
+int launch_attention_step(const float *q, const float *k, const float *v, void *kc, void *vc, const float *cs,
+                          const float *sn, int n_head, int n_head_kv, int hd, int n_rot, int neox, int n_ctx, int pos,
+                          float ks, float *out, int overlap, cudaStream_t st) {
+    static bool attr[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!attr[dev & 63]) {
+        if (cudaFuncSetAttribute(attention_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 180 * 1024) !=
+            cudaSuccess)
+            return -2;
+        attr[dev & 63] = true;
+    }
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((unsigned)n_head);
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = (size_t)(pos + 1) * 6 + 16;
+    cfg.stream = st;
+    cudaLaunchAttribute attr1[1];
+    attr1[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr1[0].val.programmaticStreamSerializationAllowed = 0;
+    (void)overlap;
+    cfg.attrs = attr1;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, attention_step_kernel, q, k, v, static_cast<uint16_t *>(kc),
+                           static_cast<uint16_t *>(vc), cs, sn, n_head, n_head / n_head_kv, hd, n_rot, neox, n_ctx,
+                           pos, ks, out) != cudaSuccess)
+        return -2;
+    return 0;
 }
 
 int launch_rope(float *x, int n_heads, int hd, int n_rot, const float *cs, const float *sn, int neox, cudaStream_t st) {

@@ -65,6 +65,8 @@ SIGNATURES = {
     "sicu_rope": [_fp, _i64, _i64, _i64, _fp, _fp, C.c_int, _vp],
     "sicu_kv_store": [_fp, _fp, _vp, _vp, _i64, _i64, _i64, _i64, _vp],
     "sicu_attention": [_fp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, C.c_float, _fp, _vp],
+    "sicu_attention_step": [_fp, _fp, _fp, _vp, _vp, _fp, _fp, _i64, _i64, _i64, _i64, C.c_int, _i64, _i64,
+                            C.c_float, _fp, _vp],
 }
 
 PRO_NONE, PRO_RMS_NORM, PRO_SWIGLU, PRO_MUL = 0, 1, 2, 3
@@ -247,6 +249,13 @@ class SiphonCuda:
                   kq_scale: float, dout, stream=None) -> None:
         self.check(self.lib.sicu_attention(_ptr(dq), _ptr(dk_cache), _ptr(dv_cache), n_head, n_head_kv, head_dim,
                                            n_ctx, pos, kq_scale, _ptr(dout), _ptr(stream)))
+
+    def attention_step(self, dq, dk, dv, dk_cache, dv_cache, dcos, dsin, n_head: int, n_head_kv: int, head_dim: int,
+                       n_rot: int, n_ctx: int, pos: int, kq_scale: float, dout, neox: bool = False,
+                       stream=None) -> None:
+        self.check(self.lib.sicu_attention_step(_ptr(dq), _ptr(dk), _ptr(dv), _ptr(dk_cache), _ptr(dv_cache),
+                                                _ptr(dcos), _ptr(dsin), n_head, n_head_kv, head_dim, n_rot,
+                                                1 if neox else 0, n_ctx, pos, kq_scale, _ptr(dout), _ptr(stream)))
 
     def row_to_f32(self, wtype: int, dw, n_in: int, rows, dout, stream=None) -> None:
         arr = (C.c_int64 * len(rows))(*rows)

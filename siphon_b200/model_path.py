@@ -322,14 +322,11 @@ class MatrixPath:
                 # heads' attention over positions 0..pos (src/engine.c:336-366)
                 hd, p = self.sh.head_dim, self.pos
                 nh, nkvl = nq // hd, nkv // hd
-                c, sn = self.rope_cos[p], self.rope_sin[p]
-                s.rope(y["q"], nh, hd, hd, c, sn, stream=h)
-                s.rope(y["k"], nkvl, hd, hd, c, sn, stream=h)
-                s.kv_store(y["k"], y["v"], self.kc[il], self.vc[il], nkvl, hd, self.n_ctx, p, stream=h)
-                s.attention(y["q"], self.kc[il], self.vc[il], nh, nkvl, hd, self.n_ctx, p, self.kq_scale,
-                            self.x_attn_buf, stream=h)
+                s.attention_step(y["q"], y["k"], y["v"], self.kc[il], self.vc[il], self.rope_cos[p],
+                                 self.rope_sin[p], nh, nkvl, hd, hd, self.n_ctx, p, self.kq_scale, self.x_attn_buf,
+                                 stream=h)
                 xa = self.x_attn_buf
-                n += 4
+                n += 1
             to, wo = lay["o"]
             s.gemv_fused(to, [wo], [d], nq, xa, None, [y["o"]], group=self.ar, stream=h)
             if self.ar is None:

@@ -62,3 +62,34 @@ def test_attention(sicu, oracle, n_head, n_head_kv, hd, n_ctx):
         sicu.attention(dev(q), kd, vd, n_head, n_head_kv, hd, n_ctx, pos, ks, out)
         assert_bits_equal(host(out), oracle.attention(q, k, v, n_head, n_head_kv, hd, n_ctx, pos, ks),
                           f"attention pos {pos}")
+
+
+@pytest.mark.parametrize("neox", [False, True])
+def test_attention_step_equals_separate_launches(sicu, oracle, neox):
+    """sicu_attention_step (RoPE, cache store and attention in one launch)
+    against the three separate entry points: the same caches and outputs."""
+    import torch
+    rng = np.random.default_rng(11)
+    n_head, nkv, hd, n_ctx = 8, 2, 128, 64
+    k0, v0 = random_cache(rng, nkv, hd, n_ctx)
+    theta = rng.uniform(-20, 20, hd // 2)
+    c, s = dev(np.cos(theta).astype(np.float32)), dev(np.sin(theta).astype(np.float32))
+    ks = float(np.float32(1.0 / np.sqrt(hd)))
+    for pos in (0, 9, 63):
+        q = (rng.standard_normal(n_head * hd) * 2).astype(np.float32)
+        k = (rng.standard_normal(nkv * hd) * 2).astype(np.float32)
+        v = (rng.standard_normal(nkv * hd) * 2).astype(np.float32)
+        kc1 = torch.from_numpy(k0.view(np.int16).reshape(-1).copy()).cuda()
+        vc1 = torch.from_numpy(v0.view(np.int16).reshape(-1).copy()).cuda()
+        kc2, vc2 = kc1.clone(), vc1.clone()
+        o1, o2 = empty_f32(n_head * hd), empty_f32(n_head * hd)
+        qd, kd, vd = dev(q), dev(k), dev(v)
+        sicu.attention_step(qd, kd, vd, kc1, vc1, c, s, n_head, nkv, hd, hd, n_ctx, pos, ks, o1, neox=neox)
+        q2, k2 = dev(q), dev(k)
+        sicu.rope(q2, n_head, hd, hd, c, s, neox=neox)
+        sicu.rope(k2, nkv, hd, hd, c, s, neox=neox)
+        sicu.kv_store(k2, vd, kc2, vc2, nkv, hd, n_ctx, pos)
+        sicu.attention(q2, kc2, vc2, n_head, nkv, hd, n_ctx, pos, ks, o2)
+        assert_bits_equal(host(o1), host(o2), f"pos {pos} output")
+        assert (host(kc1) == host(kc2)).all() and (host(vc1) == host(vc2)).all(), f"pos {pos} caches"
+        assert_bits_equal(host(qd), q, "q left unrotated")

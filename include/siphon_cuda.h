@@ -78,6 +78,7 @@ SICU_API int sicu_last_error(char *buf, size_t len);
 SICU_API int sicu_status(int *flags);
 #define SICU_STATUS_WAIT_TIMEOUT 1
 #define SICU_STATUS_AR_TIMEOUT   2
+#define SICU_STATUS_BAD_ROW      4   /* sicu_row_to_f32_dev: a row id out of range */
 
 /* Programmatic dependent launch for the matvec kernels (default off). When
  * on, a matvec may start streaming its weight blocks while earlier work in
@@ -367,6 +368,17 @@ SICU_API int sicu_attention_step(const float *dq, const float *dk, const float *
  * si_dequant_row (src/kernels.c:803-817). */
 SICU_API int sicu_row_to_f32(uint32_t wtype, const void *dw, int64_t n_in, const int64_t *rows,
                     int64_t nrows, float *dout, void *stream);
+/* The same with the row ids in device memory (e.g. the token the previous
+ * decode step chose on the device, for the embedding lookup of
+ * src/engine.c:295-300), so the call neither copies nor waits. W has n_rows
+ * rows; an id outside [0, n_rows) yields a NaN row and sets
+ * SICU_STATUS_BAD_ROW. */
+SICU_API int sicu_row_to_f32_dev(uint32_t wtype, const void *dw, int64_t n_in, int64_t n_rows,
+                                 const int64_t *drows, int64_t nrows, float *dout, void *stream);
+/* dout[r] = the greedy choice of row r of m rows of n floats, as the
+ * reference's si_sample_greedy picks it (src/sampler.c:6-12): the first
+ * maximum among the non-NaN values, 0 when element 0 is NaN. */
+SICU_API int sicu_argmax(const float *dx, int64_t n, int64_t m, int64_t *dout, void *stream);
 
 #ifdef __cplusplus
 }

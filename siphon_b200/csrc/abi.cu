@@ -941,6 +941,33 @@ int sicu_attention_step(const float *dq, const float *dk, const float *dv, void 
     return SICU_OK;
 }
 
+int sicu_row_to_f32_dev(uint32_t wtype, const void *dw, int64_t n_in, int64_t n_rows, const int64_t *drows,
+                        int64_t nrows, float *dout, void *stream) {
+    uint32_t blck, bytes;
+    if (!geometry(wtype, blck, bytes) || wtype == T_F32 || wtype == T_Q8_K)
+        return fail(SICU_ENOTSUP, "row_to_f32: unsupported type %s (%u)", tname(wtype), wtype);
+    if (n_in <= 0 || n_rows <= 0 || nrows < 0 || n_in % blck) return fail(SICU_EINVAL, "row_to_f32: bad shape");
+    if (nrows > 65535) return fail(SICU_EINVAL, "row_to_f32: at most 65535 rows per call");
+    if (!dw || !dout || (nrows && !drows)) return fail(SICU_EINVAL, "row_to_f32: null pointer");
+    if (!aligned(drows, 8)) return fail(SICU_EINVAL, "row_to_f32: row ids must be 8-byte aligned");
+    DevState *ds;
+    if (int rc = current(ds)) return rc;
+    if (nrows == 0) return SICU_OK;
+    if (launch_dequant(wtype, dw, n_in, drows, nrows, dout, (cudaStream_t)stream, n_rows, ds->status))
+        return cuda_fail(cudaGetLastError(), "dequant launch");
+    return SICU_OK;
+}
+
+int sicu_argmax(const float *dx, int64_t n, int64_t m, int64_t *dout, void *stream) {
+    if (n <= 0 || m < 0 || m > INT32_MAX) return fail(SICU_EINVAL, "argmax: bad shape");
+    if (!dx || !dout) return fail(SICU_EINVAL, "argmax: null pointer");
+    if (!aligned(dout, 8)) return fail(SICU_EINVAL, "argmax: output must be 8-byte aligned");
+    DevState *ds;
+    if (int rc = current(ds)) return rc;
+    if (launch_argmax(dx, n, m, dout, (cudaStream_t)stream)) return cuda_fail(cudaGetLastError(), "argmax launch");
+    return SICU_OK;
+}
+
 int sicu_row_to_f32(uint32_t wtype, const void *dw, int64_t n_in, const int64_t *rows, int64_t nrows, float *dout,
                     void *stream) {
     uint32_t blck, bytes;

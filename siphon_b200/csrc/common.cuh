@@ -25,6 +25,7 @@ constexpr int STATUS_WAIT_TIMEOUT = 1;
 // an all-reduce gave up waiting for a peer's part, or its group was already
 // broken by an earlier failure
 constexpr int STATUS_AR_TIMEOUT = 2;
+constexpr int STATUS_BAD_ROW = 4;    // a row id read from device memory was out of range
 
 // ---- f16 ---------------------------------------------------------------------
 // f16 -> f32 is exact in hardware for every finite half and inf.

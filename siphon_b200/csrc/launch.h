@@ -138,8 +138,11 @@ int launch_attention_step(const float *q, const float *k, const float *v, void *
 // all-reduce of src[len] into dst[len] over the group (one delivery)
 int launch_allreduce(const ArDev &a, const float *src, float *dst, int *status, int num_sms, cudaStream_t st);
 
-// dequantise rows (row_to_f32): rows[i] of w into out[i * n_in]
+// dequantise rows (row_to_f32): rows[i] of w into out[i * n_in]; row ids
+// outside [0, n_rows) give a NaN row and STATUS_BAD_ROW in *status
 int launch_dequant(uint32_t wtype, const void *w, int64_t n_in, const int64_t *rows_dev, int64_t nrows,
-                   float *out, cudaStream_t st);
+                   float *out, cudaStream_t st, int64_t n_rows = INT64_MAX, int *status = nullptr);
+// greedy choice (first maximum) of m rows of n floats into out[m]
+int launch_argmax(const float *x, int64_t n, int64_t m, int64_t *out, cudaStream_t st);
 
 }  // namespace sicu

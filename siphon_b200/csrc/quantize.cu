@@ -117,12 +117,47 @@ __device__ float dequant_elem(uint32_t t, const uint8_t *row, int e) {
     }
 }
 
+// rows[i] outside [0, n_rows) (ids read from device memory): the output row
+// is NaN and the status word gets STATUS_BAD_ROW; nothing is read
 __global__ void __launch_bounds__(256) dequant_kernel(uint32_t t, const uint8_t *w, int64_t row_bytes, int n_in,
-                                                    const int64_t *rows, float *out) {
+                                                    const int64_t *rows, float *out, int64_t n_rows, int *status) {
     const int64_t r = rows[blockIdx.y];
+    if (r < 0 || r >= n_rows) {
+        for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < n_in; e += gridDim.x * blockDim.x)
+            out[(int64_t)blockIdx.y * n_in + e] = __uint_as_float(0x7fc00000u);
+        if (status && blockIdx.x == 0 && threadIdx.x == 0) atomicOr(status, STATUS_BAD_ROW);
+        return;
+    }
     const uint8_t *row = w + r * row_bytes;
     for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < n_in; e += gridDim.x * blockDim.x)
         out[(int64_t)blockIdx.y * n_in + e] = dequant_elem(t, row, e);
+}
+
+// Greedy choice per row (si_sample_greedy, src/sampler.c:6-12): best = 0, then
+// every later element strictly greater than the best so far takes its place;
+// i.e. the first maximum among the non-NaN values, or 0 when x[0] is NaN.
+__global__ void __launch_bounds__(256) argmax_kernel(const float *x, int64_t n, int64_t *out) {
+    __shared__ float bv[8];
+    __shared__ int64_t bi[8];
+    const float *xr = x + (int64_t)blockIdx.x * n;
+    float v = -__int_as_float(0x7f800000);
+    int64_t idx = -1;
+    for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
+        const float a = xr[i];
+        if (a > v || (idx < 0 && a == v)) { v = a; idx = i; }
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+        const int64_t oi = __shfl_xor_sync(0xffffffffu, idx, o);
+        if (oi >= 0 && (idx < 0 || ov > v || (ov == v && oi < idx))) { v = ov; idx = oi; }
+    }
+    if ((threadIdx.x & 31) == 0) { bv[threadIdx.x >> 5] = v; bi[threadIdx.x >> 5] = idx; }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < (int)(blockDim.x >> 5); ++w)
+            if (bi[w] >= 0 && (idx < 0 || bv[w] > v || (bv[w] == v && bi[w] < idx))) { v = bv[w]; idx = bi[w]; }
+        out[blockIdx.x] = (isnan(xr[0]) || idx < 0) ? 0 : idx;
+    }
 }
 
 }  // namespace
@@ -155,8 +190,14 @@ int launch_quantize(uint32_t pair, const float *x, void *y, int64_t n, int64_t m
     return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }
 
+int launch_argmax(const float *x, int64_t n, int64_t m, int64_t *out, cudaStream_t st) {
+    if (m <= 0 || n <= 0) return 0;
+    argmax_kernel<<<(unsigned)m, 256, 0, st>>>(x, n, out);
+    return cudaPeekAtLastError() == cudaSuccess ? 0 : -2;
+}
+
 int launch_dequant(uint32_t wtype, const void *w, int64_t n_in, const int64_t *rows_dev, int64_t nrows,
-                   float *out, cudaStream_t st) {
+                   float *out, cudaStream_t st, int64_t n_rows, int *status) {
     int64_t blk = 1, bsz = 2;
     switch (wtype) {
         case T_F16: blk = 1; bsz = 2; break;
@@ -175,7 +216,8 @@ int launch_dequant(uint32_t wtype, const void *w, int64_t n_in, const int64_t *r
     int64_t gx = (n_in + 255) / 256;
     if (gx > 1024) gx = 1024;
     dim3 grid((unsigned)gx, (unsigned)nrows);
-    dequant_kernel<<<grid, 256, 0, st>>>(wtype, static_cast<const uint8_t *>(w), row_bytes, (int)n_in, rows_dev, out);
+    dequant_kernel<<<grid, 256, 0, st>>>(wtype, static_cast<const uint8_t *>(w), row_bytes, (int)n_in, rows_dev, out,
+                                         n_rows, status);
     return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }
 

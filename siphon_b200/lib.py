@@ -65,6 +65,8 @@ SIGNATURES = {
     "sicu_rope": [_fp, _i64, _i64, _i64, _fp, _fp, C.c_int, _vp],
     "sicu_kv_store": [_fp, _fp, _vp, _vp, _i64, _i64, _i64, _i64, _vp],
     "sicu_attention": [_fp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, C.c_float, _fp, _vp],
+    "sicu_row_to_f32_dev": [_u32, _vp, _i64, _i64, _vp, _i64, _fp, _vp],
+    "sicu_argmax": [_fp, _i64, _i64, _vp, _vp],
     "sicu_attention_step": [_fp, _fp, _fp, _vp, _vp, _fp, _fp, _i64, _i64, _i64, _i64, C.c_int, _i64, _i64,
                             C.c_float, _fp, _vp],
 }
@@ -81,7 +83,7 @@ class Prologue(C.Structure):
                 ("sum_out", C.c_void_p), ("up", C.c_void_p)]
 
 AR_HANDLE_BYTES = 64
-STATUS_WAIT_TIMEOUT, STATUS_AR_TIMEOUT = 1, 2
+STATUS_WAIT_TIMEOUT, STATUS_AR_TIMEOUT, STATUS_BAD_ROW = 1, 2, 4
 
 
 def rms_norm_step(weight, eps: float, residual=None, sum_out=None) -> Prologue:
@@ -256,6 +258,13 @@ class SiphonCuda:
         self.check(self.lib.sicu_attention_step(_ptr(dq), _ptr(dk), _ptr(dv), _ptr(dk_cache), _ptr(dv_cache),
                                                 _ptr(dcos), _ptr(dsin), n_head, n_head_kv, head_dim, n_rot,
                                                 1 if neox else 0, n_ctx, pos, kq_scale, _ptr(dout), _ptr(stream)))
+
+    def row_to_f32_dev(self, wtype: int, dw, n_in: int, n_rows: int, drows, nrows: int, dout, stream=None) -> None:
+        self.check(self.lib.sicu_row_to_f32_dev(wtype, _ptr(dw), n_in, n_rows, _ptr(drows), nrows, _ptr(dout),
+                                                _ptr(stream)))
+
+    def argmax(self, dx, n: int, m: int, dout, stream=None) -> None:
+        self.check(self.lib.sicu_argmax(_ptr(dx), n, m, _ptr(dout), _ptr(stream)))
 
     def row_to_f32(self, wtype: int, dw, n_in: int, rows, dout, stream=None) -> None:
         arr = (C.c_int64 * len(rows))(*rows)

@@ -136,12 +136,13 @@ class MatrixPath:
 
     def __init__(self, sicu, sh: LlamaShape, device, world: int = 1, rank: int = 0, group=None, seed: int = 0,
                  max_tokens: int = 1, fused: bool = False, steps: bool = False, attention: bool = False,
-                 n_ctx: int = 256):
+                 n_ctx: int = 256, embed: bool = False):
         import torch
         self.s, self.sh, self.dev, self.world, self.group = sicu, sh, device, world, group
         self.ar = None
-        self.steps = steps or attention
-        self.attention = attention
+        self.steps = steps or attention or embed
+        self.attention = attention or embed
+        self.embed = embed
         self.pos = 0
         self.shard = tp_partition(sh, world, rank)
         self.shapes = shard_shapes(sh, self.shard)
@@ -177,7 +178,7 @@ class MatrixPath:
             self.ffn_norm = [norm_w() for _ in range(sh.n_layer)]
             self.out_norm = norm_w()
             self.resid = [torch.empty(sh.n_embd, device=device) for _ in range(2)]
-        if attention:
+        if self.attention:
             # f16 caches per layer in the engine's layout (K [kv][n_ctx][hd],
             # V [kv][hd][n_ctx]), zero; RoPE tables of every position (the
             # engine's theta recurrence in f32; cos/sin by numpy here)
@@ -201,6 +202,15 @@ class MatrixPath:
             self.rope_sin = torch.from_numpy(sin).to(device)
             self.kq_scale = float(np.float32(1.0) / np.sqrt(np.float32(hd)))
             self.x_attn_buf = torch.empty(len(self.shard.heads) * hd, device=device)
+        if embed:
+            # a device-resident token loop: the step starts from the embedding
+            # row of self.token (on the device) and ends by writing the greedy
+            # choice of its logits back into it (one GPU: the head is whole)
+            if world != 1:
+                raise ValueError("the device token loop needs the whole output head on one GPU")
+            self.embd = device_weights(Q.Q4_K, sh.n_vocab, sh.n_embd, seed * 7919 + 555, device)
+            self.token = torch.zeros(1, dtype=torch.int64, device=device)
+            self.x_embed = torch.empty(sh.n_embd, device=device)
         if fused and world > 1:
             import torch.distributed as dist
             self.ar = sicu.ar_create(world, rank, sh.n_embd)
@@ -304,6 +314,10 @@ class MatrixPath:
         cur, res = self.x_model[0], None      # residual stream so far, and the output still to be added
         nxt = 0
         n = 0
+        if self.embed:
+            s.row_to_f32_dev(Q.Q4_K, self.embd, d, self.sh.n_vocab, self.token, 1, self.x_embed, stream=h)
+            cur = self.x_embed
+            n += 1
         for il, lay in enumerate(self.layers):
             (tq, wq), (tk, wk), (tv, wv) = lay["q"], lay["k"], lay["v"]
             out = self.resid[nxt]
@@ -348,6 +362,9 @@ class MatrixPath:
         th, wh = self.head
         s.gemv_fused(th, [wh], [self.shapes["head"][0]], d, cur, rms_norm_step(self.out_norm, eps, res),
                      [y["head"]], stream=h)
+        if self.embed:
+            s.argmax(y["head"], self.shapes["head"][0], 1, self.token, stream=h)
+            n += 1
         return n + 1
 
     def prefill(self, stream, m: int) -> None:

@@ -224,3 +224,80 @@ def test_decode_steps_with_attention_match_oracle(sicu, oracle, shape):
         assert_bits_equal(host(m.x_attn_buf), att, f"pos {pos}: last layer's attention output")
         assert_bits_equal(host(m.y["head"][0]), logits, f"pos {pos}: logits")
     m.close()
+
+
+def test_device_resident_greedy_decode(sicu, oracle):
+    """Four greedy tokens with the whole loop on the device: the embedding
+    row of the token the previous step chose (sicu_row_to_f32_dev), every
+    layer's steps and attention, the head, and the greedy choice
+    (sicu_argmax) written back for the next step. The oracle replays each step
+    from the same token and must choose the same token with bit-identical
+    logits."""
+    import numpy as np
+    import torch
+    shape = sm.SMALL
+    dev = torch.device("cuda", 0)
+    n_ctx = 16
+    m = mp.MatrixPath(sicu, shape, dev, seed=6, embed=True, n_ctx=n_ctx)
+    stream = torch.cuda.Stream()
+    eps, d, hd = shape.rms_eps, shape.n_embd, shape.head_dim
+    nh, nkv = m.shapes["q"][0] // hd, m.shapes["k"][0] // hd
+    W = [{k: (t, host(w)) for k, (t, w) in lay.items()} for lay in m.layers]
+    emb = host(m.embd)
+    rb = Q.row_bytes(Q.Q4_K, d)
+    cos, sin = host(m.rope_cos), host(m.rope_sin)
+    kc = [np.zeros((nkv, n_ctx, hd), np.uint16) for _ in m.layers]
+    vc = [np.zeros((nkv, hd, n_ctx), np.uint16) for _ in m.layers]
+    m.token.fill_(123)
+    tok = 123
+    for pos in range(4):
+        m.pos = pos
+        with torch.cuda.stream(stream):
+            m.decode_step(stream)
+        torch.cuda.synchronize()
+        assert sicu.status() == 0
+        cur, res = oracle.dequant_row(Q.Q4_K, emb[tok * rb:(tok + 1) * rb], d), None
+        for il, lw in enumerate(W):
+            h, a = oracle.rms_norm(cur, host(m.attn_norm[il]), eps, res)
+            q = oracle.rope(_gemv(oracle, *lw["q"], nh * hd, a), nh, hd, hd, cos[pos], sin[pos])
+            k = oracle.rope(_gemv(oracle, *lw["k"], nkv * hd, a), nkv, hd, hd, cos[pos], sin[pos])
+            v = _gemv(oracle, *lw["v"], nkv * hd, a)
+            kc[il][:, pos, :] = oracle.convert_f16(k).view(np.uint16).reshape(nkv, hd)
+            vc[il][:, :, pos] = oracle.convert_f16(v).view(np.uint16).reshape(nkv, hd)
+            att = oracle.attention(q, kc[il], vc[il], nh, nkv, hd, n_ctx, pos, m.kq_scale)
+            o = _gemv(oracle, *lw["o"], d, att)
+            h2, a2 = oracle.rms_norm(h, host(m.ffn_norm[il]), eps, o)
+            gate = _gemv(oracle, *lw["gate"], m.shapes["gate"][0], a2)
+            up = _gemv(oracle, *lw["up"], m.shapes["up"][0], a2)
+            cur, res = h2, _gemv(oracle, *lw["down"], d, oracle.swiglu(gate, up))
+        _, a = oracle.rms_norm(cur, host(m.out_norm), eps, res)
+        logits = _gemv(oracle, m.head[0], host(m.head[1]), m.shapes["head"][0], a)
+        assert_bits_equal(host(m.y["head"][0]), logits, f"pos {pos}: logits")
+        tok = int(np.argmax(logits))
+        assert int(host(m.token)[0]) == tok, f"pos {pos}: greedy token"
+    m.close()
+
+
+def test_argmax_and_device_rows(sicu, oracle):
+    import numpy as np
+    import torch
+    from siphon_b200.lib import STATUS_BAD_ROW
+    from tests.gpu_util import dev as todev
+    x = np.random.default_rng(3).standard_normal((5, 1000)).astype(np.float32)
+    x[1, [10, 500]] = 9.0                       # tie: the first one
+    x[2, 0] = np.nan                            # NaN first: 0
+    x[3, [7, 8]] = np.nan
+    x[4, :] = -np.inf
+    out = torch.zeros(5, dtype=torch.int64, device="cuda")
+    sicu.argmax(todev(x), 1000, 5, out)
+    assert host(out).tolist() == [int(np.argmax(x[0])), 10, 0, int(np.nanargmax(x[3])), 0]
+    w = todev(oracle_rows := np.random.default_rng(4).integers(0, 256, Q.row_bytes(Q.Q6_K, 512) * 6, dtype=np.uint8))
+    ids = torch.tensor([5, 0, 6], dtype=torch.int64, device="cuda")
+    y = torch.empty(3, 512, device="cuda")
+    sicu.row_to_f32_dev(Q.Q6_K, w, 512, 6, ids, 3, y)
+    rb = Q.row_bytes(Q.Q6_K, 512)
+    got = host(y)
+    for i, r in enumerate((5, 0)):
+        assert (got[i].view(np.uint32) == oracle.dequant_row(Q.Q6_K, oracle_rows[r * rb:(r + 1) * rb], 512).view(np.uint32)).all()
+    assert np.isnan(got[2]).all()               # id 6 of 6 rows: out of range
+    assert sicu.status() & STATUS_BAD_ROW

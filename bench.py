@@ -299,6 +299,18 @@ def _time_graph(torch, g, stream, reps, world, dev) -> float:
     return max_over_ranks(e0.elapsed_time(e1), world, dev)
 
 
+def _heads_align(shape, world) -> bool:
+    """Every rank's query heads cover whole KV groups (the device attention
+    step maps local heads to local KV heads by that)."""
+    from siphon_b200 import model_path as mp
+    group = shape.n_head // shape.n_head_kv
+    for r in range(world):
+        sh = mp.tp_partition(shape, world, r)
+        if not (len(sh.heads) == len(sh.kv_heads) * group or len(sh.kv_heads) == 1):
+            return False
+    return True
+
+
 def model_decode(torch, s, shape, dev, stream, world, rank, group, reps, fused=False, steps=False,
                  attention_ctx=0) -> dict:
     """Decode tok/s of the matrix path of `shape` (batch 1), tensor parallel
@@ -460,10 +472,15 @@ def model_metrics(torch, s, dev, stream, world, rank, quick: bool) -> dict:
                                         "products fused into them (sicu_gemv_fused)",
                               **model_decode(torch, s, sm.QWEN25_32B, dev, stream, world, rank, None, reps,
                                              fused=world > 1, steps=True)}
-    out["tp_decode_full"] = {"config": "as tp_decode_steps, plus RoPE, the f16 KV-cache store and attention over a "
-                                       "512-position context (the token at position 511)",
-                             **model_decode(torch, s, sm.QWEN25_32B, dev, stream, world, rank, None, reps,
-                                            fused=world > 1, attention_ctx=512)}
+    full_cfg = ("as tp_decode_steps, plus RoPE, the f16 KV-cache store and attention over a 512-position "
+                "context (the token at position 511)")
+    if _heads_align(sm.QWEN25_32B, world):
+        out["tp_decode_full"] = {"config": full_cfg,
+                                 **model_decode(torch, s, sm.QWEN25_32B, dev, stream, world, rank, None, reps,
+                                                fused=world > 1, attention_ctx=512)}
+    else:
+        out["tp_decode_full"] = {"config": full_cfg, "skipped": f"the query heads do not split into whole KV groups "
+                                                                f"over {world} ranks"}
     if world > 1:
         out["tp_decode_nccl"] = {"config": "as tp_decode, the all-reduces as NCCL calls between the matvecs",
                                  **model_decode(torch, s, sm.QWEN25_32B, dev, stream, world, rank, None, reps)}

@@ -184,8 +184,8 @@ class MatrixPath:
             # engine's theta recurrence in f32; cos/sin by numpy here)
             import numpy as np
             hd, nkv = sh.head_dim, len(self.shard.kv_heads)
-            group = sh.n_head // sh.n_head_kv
-            if not (len(self.shard.heads) == nkv * group or nkv == 1):
+            per_kv = sh.n_head // sh.n_head_kv
+            if not (len(self.shard.heads) == nkv * per_kv or nkv == 1):
                 raise ValueError("a rank's query heads must cover whole KV groups")
             self.n_ctx = n_ctx
             self.kc = [torch.zeros(nkv * n_ctx * hd, dtype=torch.int16, device=device) for _ in range(sh.n_layer)]
@@ -215,7 +215,7 @@ class MatrixPath:
             import torch.distributed as dist
             self.ar = sicu.ar_create(world, rank, sh.n_embd)
             handles = [None] * world
-            dist.all_gather_object(handles, self.ar.local_handle, group=group)
+            dist.all_gather_object(handles, self.ar.local_handle, group=self.group)
             self.ar.open(handles)
 
     def close(self) -> None:

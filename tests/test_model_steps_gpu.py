@@ -68,12 +68,14 @@ def _free_port() -> int:
         return sk.getsockname()[1]
 
 
-def _tp_rank(rank, world, port, q):
+def _tp_rank(rank, world, port, q, attention=False):
     """One rank of the tensor-parallel step flow: a decode step with the
     all-reduces fused into Wo / W_down and the steps fused into the products,
-    then rank 0 replays the whole step on the CPU from every rank's shards
-    (rank-order f32 sums for the row-split products) and every rank checks
-    its residual stream, W_down sum and head shard bit for bit."""
+    then every rank replays the whole step on the CPU from every rank's shards
+    (rank-order f32 sums for the row-split products) and checks its residual
+    stream, W_down sum and head shard bit for bit. With attention, two
+    consecutive positions run through RoPE, each rank's f16 caches and its
+    own heads' attention, and the replay does the same per rank."""
     import datetime
     import os
 
@@ -94,21 +96,22 @@ def _tp_rank(rank, world, port, q):
         orc = Oracle()
         shape = sm.LlamaShape(2, 1024, 2048, 16, 4, 2048, 10000.0, 1e-5, 1024)
         dev = torch.device("cuda", rank)
-        m = mp.MatrixPath(s, shape, dev, world, rank, None, seed=9, fused=True, steps=True)
+        n_ctx = 8
+        m = mp.MatrixPath(s, shape, dev, world, rank, None, seed=9, fused=True, steps=True, attention=attention,
+                          n_ctx=n_ctx)
         st = torch.cuda.Stream(device=dev)
-        with torch.cuda.stream(st):
-            m.decode_step(st)
-        torch.cuda.synchronize()
-        assert s.status() == 0
         mine = {"layers": [{k: (t, host(w)) for k, (t, w) in lay.items()} for lay in m.layers],
                 "head": (m.head[0], host(m.head[1])), "x_attn": host(m.x_attn[0])}
         shards = [None] * world
         dist.all_gather_object(shards, mine)
-        eps, d = shape.rms_eps, shape.n_embd
-        cur, res = host(m.x_model[0]), None
+        eps, d, hd = shape.rms_eps, shape.n_embd, shape.head_dim
+        x0 = host(m.x_model[0])
 
         def gemv(wt, w, n_out, a):
             return orc.gemv(wt, w, a.size, n_out, orc.quantize_pair(wt, a[None, :])[0])
+
+        def rows(wt, w):
+            return w.size // Q.row_bytes(wt, d)
 
         def rank_sum(parts):
             total = parts[0].copy()
@@ -116,24 +119,56 @@ def _tp_rank(rank, world, port, q):
                 total = (total + p).astype(np.float32)
             return total
 
-        for il in range(shape.n_layer):
-            h, a = orc.rms_norm(cur, host(m.attn_norm[il]), eps, res)
-            o = rank_sum([gemv(*sh["layers"][il]["o"], d, sh["x_attn"]) for sh in shards])
-            h2, a2 = orc.rms_norm(h, host(m.ffn_norm[il]), eps, o)
-            parts = []
+        if attention:
+            cos, sin = host(m.rope_cos), host(m.rope_sin)
+            caches = []
             for sh in shards:
-                (tg, wg), (tu, wu), (td, wd) = sh["layers"][il]["gate"], sh["layers"][il]["up"], sh["layers"][il]["down"]
-                nff = wg.size // Q.row_bytes(tg, d)
-                gate, up = gemv(tg, wg, nff, a2), gemv(tu, wu, nff, a2)
-                parts.append(gemv(td, wd, d, orc.swiglu(gate, up)))
-            down = rank_sum(parts)
-            cur, res = h2, down
-        _, a = orc.rms_norm(cur, host(m.out_norm), eps, res)
-        th, wh = shards[rank]["head"]
-        logits = gemv(th, wh, wh.size // Q.row_bytes(th, d), a)
-        assert_bits_equal(host(m.resid[1]), cur, f"rank {rank}: residual stream")
-        assert_bits_equal(host(m.y["down"][0]), down, f"rank {rank}: W_down sum")
-        assert_bits_equal(host(m.y["head"][0]), logits, f"rank {rank}: head shard")
+                nkv = rows(*sh["layers"][0]["k"]) // hd
+                caches.append([(np.zeros((nkv, n_ctx, hd), np.uint16), np.zeros((nkv, hd, n_ctx), np.uint16))
+                               for _ in range(shape.n_layer)])
+        for pos in range(2 if attention else 1):
+            m.pos = pos
+            with torch.cuda.stream(st):
+                m.decode_step(st)
+            torch.cuda.synchronize()
+            assert s.status() == 0
+            cur, res = x0, None
+            for il in range(shape.n_layer):
+                h, a = orc.rms_norm(cur, host(m.attn_norm[il]), eps, res)
+                if attention:
+                    xa = []
+                    for r, sh in enumerate(shards):
+                        lw = sh["layers"][il]
+                        nq, nk = rows(*lw["q"]), rows(*lw["k"])
+                        nh, nkv = nq // hd, nk // hd
+                        qv = orc.rope(gemv(*lw["q"], nq, a), nh, hd, hd, cos[pos], sin[pos])
+                        kv = orc.rope(gemv(*lw["k"], nk, a), nkv, hd, hd, cos[pos], sin[pos])
+                        vv = gemv(*lw["v"], nk, a)
+                        kc, vc = caches[r][il]
+                        kc[:, pos, :] = orc.convert_f16(kv).view(np.uint16).reshape(nkv, hd)
+                        vc[:, :, pos] = orc.convert_f16(vv).view(np.uint16).reshape(nkv, hd)
+                        xa.append(orc.attention(qv, kc, vc, nh, nkv, hd, n_ctx, pos, m.kq_scale))
+                else:
+                    xa = [sh["x_attn"] for sh in shards]
+                o = rank_sum([gemv(*sh["layers"][il]["o"], d, xa[r]) for r, sh in enumerate(shards)])
+                h2, a2 = orc.rms_norm(h, host(m.ffn_norm[il]), eps, o)
+                parts = []
+                for sh in shards:
+                    lw = sh["layers"][il]
+                    (tg, wg), (tu, wu), (td, wd) = lw["gate"], lw["up"], lw["down"]
+                    nff = rows(tg, wg)
+                    gate, up = gemv(tg, wg, nff, a2), gemv(tu, wu, nff, a2)
+                    parts.append(gemv(td, wd, d, orc.swiglu(gate, up)))
+                down = rank_sum(parts)
+                cur, res = h2, down
+            _, a = orc.rms_norm(cur, host(m.out_norm), eps, res)
+            th, wh = shards[rank]["head"]
+            logits = gemv(th, wh, rows(th, wh), a)
+            if attention:
+                assert_bits_equal(host(m.x_attn_buf), xa[rank], f"rank {rank} pos {pos}: attention output")
+            assert_bits_equal(host(m.resid[1]), cur, f"rank {rank} pos {pos}: residual stream")
+            assert_bits_equal(host(m.y["down"][0]), down, f"rank {rank} pos {pos}: W_down sum")
+            assert_bits_equal(host(m.y["head"][0]), logits, f"rank {rank} pos {pos}: head shard")
         torch.cuda.synchronize()
         dist.barrier()
         if rank == 0:
@@ -149,7 +184,8 @@ def _tp_rank(rank, world, port, q):
             dist.destroy_process_group()
 
 
-def test_tensor_parallel_step_flow_matches_oracle():
+@pytest.mark.parametrize("attention", [False, True], ids=["fixed_x_attn", "attention"])
+def test_tensor_parallel_step_flow_matches_oracle(attention):
     import torch
     ngpu = torch.cuda.device_count()
     if ngpu < 2:
@@ -159,7 +195,7 @@ def test_tensor_parallel_step_flow_matches_oracle():
     ctx = tmp.get_context("spawn")
     q = ctx.SimpleQueue()
     port = _free_port()
-    procs = [ctx.Process(target=_tp_rank, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_tp_rank, args=(r, world, port, q, attention)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:

@@ -188,15 +188,36 @@ __global__ void __launch_bounds__(256) attention_kernel(const float *q, const ui
         out[(int64_t)h * hd + c] = dot_f16_seq(vh + (int64_t)c * n_ctx, 1, p16, n_score);
 }
 
-// dot_f16_seq with x's elements 8 at a time: the eight loads of a chunk are
+// Eight f16 values x[0..7]: one 16-byte load when vec (x 16-byte aligned),
+// else eight 2-byte loads; the same bits either way. Lanes of a warp read
+// rows a whole row apart, so the wide load cuts the cache wavefronts of a
+// chunk eightfold.
+__device__ __forceinline__ void ld_h8(const uint16_t *x, bool vec, uint16_t a[8]) {
+    if (vec) {
+        const uint4 u = *reinterpret_cast<const uint4 *>(x);
+        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            a[2 * k] = (uint16_t)(w[k] & 0xffffu);
+            a[2 * k + 1] = (uint16_t)(w[k] >> 16);
+        }
+    } else {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) a[k] = x[k];
+    }
+}
+
+// dot_f16_seq with x's elements 8 at a time: the loads of a chunk are
 // issued before its eight additions, which stay in index order.
 __device__ __forceinline__ float dot_f16_seq8(const uint16_t *x, const uint16_t *y, int n) {
     double s = 0.0;
     int i = 0;
+    const bool vec = (reinterpret_cast<uintptr_t>(x) & 15) == 0;
     for (; i + 8 <= n; i += 8) {
         uint16_t a[8], b[8];
+        ld_h8(x + i, vec, a);
 #pragma unroll
-        for (int k = 0; k < 8; ++k) { a[k] = x[i + k]; b[k] = y[i + k]; }
+        for (int k = 0; k < 8; ++k) b[k] = y[i + k];
 #pragma unroll
         for (int k = 0; k < 8; ++k) s = __dadd_rn(s, (double)__fmul_rn(h2f(a[k]), h2f(b[k])));
     }
@@ -275,12 +296,14 @@ __global__ void __launch_bounds__(256) attention_step_kernel(const float *q, con
     for (int c = tid; c < hd; c += blockDim.x) {
         // positions 0..pos-1 from the cache, then this position's v
         const uint16_t *row = vh + (int64_t)c * n_ctx;
+        const bool vec = (reinterpret_cast<uintptr_t>(row) & 15) == 0;
         double s = 0.0;
         int j = 0;
         for (; j + 8 <= pos; j += 8) {
             uint16_t a[8], b[8];
+            ld_h8(row + j, vec, a);
 #pragma unroll
-            for (int t = 0; t < 8; ++t) { a[t] = row[j + t]; b[t] = p16[j + t]; }
+            for (int t = 0; t < 8; ++t) b[t] = p16[j + t];
 #pragma unroll
             for (int t = 0; t < 8; ++t) s = __dadd_rn(s, (double)__fmul_rn(h2f(a[t]), h2f(b[t])));
         }

@@ -7,6 +7,9 @@ captured on, runnable under `ncu` on one GPU:
     python -m siphon_b200.profile_cases steps     # Wq/Wk/Wv of the 32B shape (5120 -> 5120+1024+1024,
                                                   # Q4_K) with the residual add + RMS norm fused,
                                                   # beside the same launch without the step
+    python -m siphon_b200.profile_cases decode_full  # three eager decode steps of the TinyLlama-1.1B
+                                                  # shape with the steps and attention, the token at
+                                                  # position 511 of a 512-position context
 
 Each case runs a few launches (the summaries' `-s` skips the first ones) and
 exits non-zero if the library reports a device-side status bit.
@@ -66,8 +69,19 @@ def main(case: str, reps: int = 4) -> int:
         for _ in range(reps):
             s.gemv_multi(wt, ws, outs, n_in, x, ys)
             s.gemv_fused(wt, ws, outs, n_in, x, lib.rms_norm_step(gam, 1e-6, r, h), ys)
+    elif case == "decode_full":
+        from . import model_path as mp
+        from . import synth_model as sm
+        m = mp.MatrixPath(s, sm.TINYLLAMA, dev, seed=4, attention=True, n_ctx=512)
+        m.pos = 511
+        st = torch.cuda.Stream(device=dev)
+        with torch.cuda.stream(st):
+            for _ in range(3):
+                m.decode_step(st)
+        torch.cuda.synchronize()
+        m.close()
     else:
-        raise SystemExit(f"unknown case {case!r} (flat, ar, prefill, steps)")
+        raise SystemExit(f"unknown case {case!r} (flat, ar, prefill, steps, decode_full)")
     torch.cuda.synchronize()
     st = s.status()
     print(case, "status", st)

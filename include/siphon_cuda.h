@@ -176,7 +176,10 @@ SICU_API int sicu_gemv_host(uint32_t wtype, const void *dw, int64_t n_in, int64_
  * before any stream capture. Every call uses the same array: calls whose GPU
  * work overlaps (other streams, other host threads on the same device) race
  * on it and must be serialised by the caller. sicu_init is not required.
- * Same results as sicu_gemv_host. No counterpart in the reference. */
+ * The resolved address is kept for the life of the process and does not
+ * survive a cudaDeviceReset of that device (do not reset a device this entry
+ * point has used). Same results as sicu_gemv_host. No counterpart in the
+ * reference. */
 SICU_API int sicu_gemv_host_noalloc(uint32_t wtype, const void *dw, int64_t n_in, int64_t n_out,
                                     const float *hx, float *hy, void *stream);
 

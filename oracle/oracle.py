@@ -92,6 +92,8 @@ class Oracle:
         L.orc_softmax.restype = None
         L.orc_expf_restated_mismatches.argtypes = [C.c_uint32, C.c_uint32, C.c_uint32]
         L.orc_expf_restated_mismatches.restype = C.c_long
+        L.orc_rope_table.argtypes = [C.c_float, C.c_int, C.c_int, _f32, _f32]
+        L.orc_rope_table.restype = None
         L.orc_rope.argtypes = [_f32, C.c_int, C.c_int, C.c_int, _f32, _f32, C.c_int]
         L.orc_rope.restype = None
         L.orc_attention.argtypes = [_f32, _u16, _u16, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_float, _f32]
@@ -167,6 +169,12 @@ class Oracle:
         y = np.zeros_like(x)
         self.lib.orc_softmax(x, y, x.size)
         return y
+
+    def rope_table(self, base: float, n_rot: int, n_pos: int) -> tuple[np.ndarray, np.ndarray]:
+        cs = np.zeros((n_pos, n_rot // 2), np.float32)
+        sn = np.zeros((n_pos, n_rot // 2), np.float32)
+        self.lib.orc_rope_table(base, n_rot, n_pos, cs, sn)
+        return cs, sn
 
     def rope(self, x, n_heads: int, hd: int, n_rot: int, cs, sn, neox: bool = False) -> np.ndarray:
         y = _as_f32(x).reshape(-1).copy()
@@ -400,11 +408,11 @@ E2E_SO = HERE / "_ref" / "libsiphon_e2e.so"
 
 class RefEngine:
     """The reference's forward pass (si_engine_forward) on a GGUF file, every
-    layer's gemv on the reference CPU backend or on the CUDA backend adapter
-    (siphon_b200/csrc/backend_cuda.c). The output head runs on the CPU in
-    both, as in the reference (src/engine.c:393). scalar=True runs the
-    reference's scalar kernels for all host work (the parity target);
-    the first engine of a process fixes the mode."""
+    matrix product on the reference CPU backend or on the CUDA backend adapter
+    (siphon_b200/csrc/backend_cuda.c): with use_cuda, every layer's gemv, the
+    embedding lookup (src/engine.c:302) and the output head (:393) run on the
+    GPU. scalar=True runs the reference's scalar kernels for all host work
+    (the parity target); the first engine of a process fixes the mode."""
 
     _lib = None
 

@@ -723,6 +723,22 @@ ORC_API long orc_expf_restated_mismatches(uint32_t lo_bits, uint32_t hi_bits, ui
     return bad;
 }
 
+/* rope_table (src/engine.c:26-40) for positions 0..n_pos-1 with the engine's
+ * theta_scale = powf(base, -2.0f / n_rot) (src/engine.c:196), no frequency
+ * factors: cs / sn [n_pos][n_rot / 2] */
+ORC_API void orc_rope_table(float base, int n_rot, int n_pos, float *cs, float *sn) {
+    const float theta_scale = powf(base, -2.0f / (float)n_rot);
+    const int np = n_rot / 2;
+    for (int p = 0; p < n_pos; p++) {
+        float theta = (float)p;
+        for (int j = 0; j < np; j++) {
+            cs[(size_t)p * np + j] = cosf(theta);
+            sn[(size_t)p * np + j] = sinf(theta);
+            theta *= theta_scale;
+        }
+    }
+}
+
 /* rope_apply (src/engine.c:42-75) on n_heads heads in place */
 ORC_API void orc_rope(float *x, int n_heads, int hd, int n_rot, const float *cs, const float *sn, int neox) {
     const int np = n_rot / 2;

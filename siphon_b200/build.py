@@ -41,14 +41,31 @@ def stale() -> bool:
 
 
 def build(force: bool = False, verbose: bool = False) -> Path:
+    """Compile every source to an object (in parallel), then link the shared
+    library; rebuilds only when a source or header is newer than it."""
     if not force and not stale():
         return LIB
-    cmd = [nvcc(), *ARCH, "-O3", "-lineinfo", "-std=c++17", "-shared", "-Xcompiler", "-fPIC,-fvisibility=hidden",
-           "-I", str(ROOT / "include"), "-o", str(LIB) + ".tmp", *[str(CSRC / s) for s in SOURCES]]
+    from concurrent.futures import ThreadPoolExecutor
+    objdir = PKG / "_build"
+    objdir.mkdir(exist_ok=True)
+    flags = [*ARCH, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC,-fvisibility=hidden",
+             "-I", str(ROOT / "include")]
     if os.environ.get("SICU_PTXAS_VERBOSE"):
-        cmd.insert(1, "-Xptxas=-v")
+        flags.insert(0, "-Xptxas=-v")
+
+    def compile_one(src: str) -> Path:
+        obj = objdir / (Path(src).stem + ".o")
+        cmd = [nvcc(), *flags, "-c", "-o", str(obj), str(CSRC / src)]
+        if verbose:
+            print(" ".join(cmd), flush=True)
+        subprocess.run(cmd, check=True)
+        return obj
+
+    with ThreadPoolExecutor(max_workers=min(len(SOURCES), os.cpu_count() or 1)) as ex:
+        objs = list(ex.map(compile_one, SOURCES))
+    cmd = [nvcc(), *ARCH, "-shared", "-o", str(LIB) + ".tmp", *map(str, objs)]
     if verbose:
-        print(" ".join(cmd))
+        print(" ".join(cmd), flush=True)
     subprocess.run(cmd, check=True)
     os.replace(str(LIB) + ".tmp", LIB)
     return LIB

@@ -5,11 +5,12 @@
  * the `gemv` slot runs the matvec on the GPU through sicu_gemv_host (host x
  * in, host y out, synchronous, results bit-identical to cpu_gemv's scalar
  * dots); weight blocks are uploaded once, on first use, straight from the
- * GGUF mmap. The `row_to_f32` slot (embedding lookup) stays on the host like
- * the reference's own engine does it (src/engine.c:302-304).
+ * GGUF mmap. The `row_to_f32` slot (the embedding lookup, src/engine.c:
+ * 300-304) dequantizes the row on the device (sicu_row_to_f32, the
+ * reference's si_dequant_row semantics) and copies it back.
  *
- * Built against the reference's headers; the reference's si_set_err and
- * si_backend_cpu are resolved from the process it is loaded into. */
+ * Built against the reference's headers; the reference's si_set_err is
+ * resolved from the process it is loaded into. */
 #include "siphon/tensor.h"
 #include "siphon_cuda.h"
 
@@ -62,10 +63,30 @@ static void cuda_gemv(si_backend *be, const si_tensor *w, const float *x, float 
     }
 }
 
+static float *g_row;          /* device buffer of one dequantized row */
+static size_t g_row_bytes;
+
 static void cuda_row_to_f32(si_backend *be, const si_tensor *w, uint64_t row, float *out) {
-    si_backend *cpu = si_backend_cpu();
     (void)be;
-    cpu->row_to_f32(cpu, w, row, out);
+    void *dw = device_copy(w);
+    if (!dw) return;
+    const size_t need = (size_t)w->ne[0] * sizeof(float);
+    char msg[256];
+    if (g_row_bytes < need) {
+        if (g_row) sicu_free(g_row);
+        g_row = NULL;
+        g_row_bytes = 0;
+        if (sicu_malloc((void **)&g_row, need) != SICU_OK) goto fail;
+        g_row_bytes = need;
+    }
+    const int64_t r = (int64_t)row;
+    if (sicu_row_to_f32(w->type, dw, (int64_t)w->ne[0], &r, 1, g_row, NULL) != SICU_OK ||
+        sicu_memcpy_d2h(out, g_row, need, NULL) != SICU_OK || sicu_stream_sync(NULL) != SICU_OK)
+        goto fail;
+    return;
+fail:
+    sicu_last_error(msg, sizeof msg);
+    si_set_err("cuda row_to_f32: %s", msg);
 }
 
 static si_backend g_cuda_backend = {
@@ -91,4 +112,7 @@ __attribute__((visibility("default"))) void si_backend_cuda_release(void) {
     for (int i = 0; i < g_ntab; i++) sicu_free(g_tab[i].dev);
     g_ntab = 0;
     g_last = 0;
+    if (g_row) sicu_free(g_row);
+    g_row = NULL;
+    g_row_bytes = 0;
 }

@@ -40,15 +40,20 @@ int na_cuda_fail(cudaError_t e, const char *what) {
 }
 
 // First call on a device: with that device current, resolve the scratch
-// array's device address and read the launch limits. No allocation.
+// array's device address and read the launch limits. No allocation. The
+// address is kept for the life of the process: after a cudaDeviceReset the
+// module loads again in a new context, and the kept address is stale.
 int na_setup(int dev, NaDev *&out) {
     std::lock_guard<std::mutex> lk(g_na_mu);
     NaDev &d = g_na[dev];
     if (!d.ready) {
-        int major = 0;
+        int major = 0, minor = 0;
         cudaError_t e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+        if (e == cudaSuccess) e = cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
         if (e != cudaSuccess) return na_cuda_fail(e, "device attributes");
-        if (major != 10) return report_error(SICU_ENOTSUP, "gemv_host_noalloc: device %d is not sm_100", dev);
+        if (major != 10 || minor != 0)
+            return report_error(SICU_ENOTSUP, "gemv_host_noalloc: device %d is sm_%d%d; this library is built for "
+                                "sm_100a only", dev, major, minor);
         void *ptr = nullptr;
         e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
         if (e != cudaSuccess || !ptr) return na_cuda_fail(e, "scratch address");
@@ -129,6 +134,7 @@ extern "C" int sicu_gemv_host_noalloc(uint32_t wtype, const void *dw, int64_t n_
         if (rc == -1)
             return report_error(SICU_ENOTSUP, "gemv_host_noalloc: row of %lld elements does not fit shared memory",
                                 (long long)n_in);
+        if (rc == -3) return report_error(SICU_ENOTSUP, "gemv_host_noalloc: no kernel for weight type %u", wtype);
         if (rc != 0) return na_cuda_fail(cudaGetLastError(), "launch");
         if ((e = cudaMemcpyAsync(hy, dy, (size_t)n_out * 4, cudaMemcpyDeviceToHost, st)) != cudaSuccess)
             return na_cuda_fail(e, "copy out");

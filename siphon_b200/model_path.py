@@ -49,7 +49,7 @@ import math
 from dataclasses import dataclass
 
 from . import quant as Q
-from .synth_model import LlamaShape
+from .synth_model import GGUF_NAMES, LlamaShape, layer_types
 
 # byte offsets of the f16 scale fields inside one block (include/siphon/quant.h)
 F16_FIELDS = {
@@ -87,10 +87,31 @@ def tp_partition(sh: LlamaShape, world: int, rank: int) -> Shard:
     return Shard(heads, kv, range(fu.start * 256, fu.stop * 256), vu)
 
 
-def layer_types(il: int) -> dict:
-    """Q4_K_M-style mix: Q6_K for attn_v and ffn_down on even layers."""
-    mix = Q.Q6_K if il % 2 == 0 else Q.Q4_K
-    return {"q": Q.Q4_K, "k": Q.Q4_K, "v": mix, "o": Q.Q4_K, "gate": Q.Q4_K, "up": Q.Q4_K, "down": mix}
+def rope_tables(sh: LlamaShape, n_ctx: int):
+    """cos / sin tables [n_ctx][n_rot / 2] of every position, computed as the
+    reference engine computes them on the host (src/engine.c:26-40, 196):
+    theta_scale = powf(base, -2 / n_rot); per position theta starts at the
+    position and is multiplied by theta_scale (f32) after each pair; cosf /
+    sinf from the C library (the same libm the reference build calls)."""
+    import ctypes
+    import ctypes.util
+
+    import numpy as np
+    libm = ctypes.CDLL(ctypes.util.find_library("m") or "libm.so.6")
+    for fn in ("powf", "cosf", "sinf"):
+        getattr(libm, fn).restype = ctypes.c_float
+    libm.powf.argtypes = [ctypes.c_float, ctypes.c_float]
+    libm.cosf.argtypes = libm.sinf.argtypes = [ctypes.c_float]
+    n_rot = sh.head_dim
+    theta_scale = np.float32(libm.powf(np.float32(sh.rope_base), np.float32(-2.0) / np.float32(n_rot)))
+    cos = np.zeros((n_ctx, n_rot // 2), np.float32)
+    sin = np.zeros((n_ctx, n_rot // 2), np.float32)
+    for p in range(n_ctx):
+        th = np.float32(p)
+        for j in range(n_rot // 2):
+            cos[p, j], sin[p, j] = libm.cosf(th), libm.sinf(th)
+            th = np.float32(th * theta_scale)
+    return cos, sin
 
 
 def shard_shapes(sh: LlamaShape, shard: Shard) -> dict:
@@ -132,11 +153,16 @@ def device_weights(wtype: int, n_out: int, n_in: int, seed: int, device):
 
 class MatrixPath:
     """One rank's shard of the model's weight matrices and the launch
-    sequence of a decode step / a prefill over them."""
+    sequence of a decode step / a prefill over them.
+
+    Weights are synthetic blocks generated on the device, or, with
+    ``gguf_path`` (one GPU), a model file's tensors uploaded unchanged: the
+    matrices, the embedding, the norm weights and any Q/K/V biases."""
 
     def __init__(self, sicu, sh: LlamaShape, device, world: int = 1, rank: int = 0, group=None, seed: int = 0,
                  max_tokens: int = 1, fused: bool = False, steps: bool = False, attention: bool = False,
-                 n_ctx: int = 256, embed: bool = False):
+                 n_ctx: int = 256, embed: bool = False, gguf_path=None):
+        import numpy as np
         import torch
         self.s, self.sh, self.dev, self.world, self.group = sicu, sh, device, world, group
         self.ar = None
@@ -146,17 +172,36 @@ class MatrixPath:
         self.pos = 0
         self.shard = tp_partition(sh, world, rank)
         self.shapes = shard_shapes(sh, self.shard)
+        reader = None
+        if gguf_path is not None:
+            from . import gguf
+            if world != 1:
+                raise ValueError("a model file is loaded on one GPU")
+            reader = gguf.Reader(gguf_path)
+
+        def from_file(name, n_out=None, n_in=None):
+            info = reader.tensors[name]
+            if n_out is not None and info.dims[:2] != (n_in, n_out):
+                raise ValueError(f"{name}: dims {info.dims} in the file, ({n_in}, {n_out}) expected")
+            return info.type, torch.from_numpy(np.array(reader.data(name))).to(device)
+
         self.layers = []
         for il in range(sh.n_layer):
             t = layer_types(il)
             lay = {}
             for j, name in enumerate(("q", "k", "v", "o", "gate", "up", "down")):
                 n_out, n_in = self.shapes[name]
-                lay[name] = (t[name], device_weights(t[name], n_out, n_in, seed * 7919 + il * 16 + j + 1000 * rank,
-                                                     device))
+                if reader is not None:
+                    lay[name] = from_file(f"blk.{il}.{GGUF_NAMES[name]}.weight", n_out, n_in)
+                else:
+                    lay[name] = (t[name], device_weights(t[name], n_out, n_in,
+                                                         seed * 7919 + il * 16 + j + 1000 * rank, device))
             self.layers.append(lay)
         n_out, n_in = self.shapes["head"]
-        self.head = (Q.Q6_K, device_weights(Q.Q6_K, n_out, n_in, seed * 7919 + 999 + 1000 * rank, device))
+        if reader is not None:
+            self.head = from_file("output.weight", n_out, n_in)
+        else:
+            self.head = (Q.Q6_K, device_weights(Q.Q6_K, n_out, n_in, seed * 7919 + 999 + 1000 * rank, device))
         m = max_tokens
         gen = torch.Generator(device=device)
         gen.manual_seed(seed + 17)
@@ -169,20 +214,28 @@ class MatrixPath:
         self.x_model, self.x_attn, self.x_ff = act(sh.n_embd), act(nq), act(nff)
         self.y = {name: torch.empty(m, self.shapes[name][0], device=device) for name in self.shapes}
         self.weight_bytes = step_weight_bytes(sh, world, rank)
+
+        def vec(name):
+            return torch.from_numpy(np.array(reader.data(name)).view(np.float32)).to(device)
+
         if self.steps:
-            # norm weights near 1 (replicated on every rank), two residual
-            # stream buffers used in turn
+            # norm weights (near 1 when synthetic; replicated on every rank),
+            # two residual stream buffers used in turn
             def norm_w():
                 return 1.0 + 0.1 * torch.randn(sh.n_embd, device=device, generator=gen)
-            self.attn_norm = [norm_w() for _ in range(sh.n_layer)]
-            self.ffn_norm = [norm_w() for _ in range(sh.n_layer)]
-            self.out_norm = norm_w()
+            if reader is not None:
+                self.attn_norm = [vec(f"blk.{il}.attn_norm.weight") for il in range(sh.n_layer)]
+                self.ffn_norm = [vec(f"blk.{il}.ffn_norm.weight") for il in range(sh.n_layer)]
+                self.out_norm = vec("output_norm.weight")
+            else:
+                self.attn_norm = [norm_w() for _ in range(sh.n_layer)]
+                self.ffn_norm = [norm_w() for _ in range(sh.n_layer)]
+                self.out_norm = norm_w()
             self.resid = [torch.empty(sh.n_embd, device=device) for _ in range(2)]
         if self.attention:
             # f16 caches per layer in the engine's layout (K [kv][n_ctx][hd],
-            # V [kv][hd][n_ctx]), zero; RoPE tables of every position (the
-            # engine's theta recurrence in f32; cos/sin by numpy here)
-            import numpy as np
+            # V [kv][hd][n_ctx]), zero; the RoPE tables of every position as
+            # the engine computes them
             hd, nkv = sh.head_dim, len(self.shard.kv_heads)
             per_kv = sh.n_head // sh.n_head_kv
             if not (len(self.shard.heads) == nkv * per_kv or nkv == 1):
@@ -190,14 +243,7 @@ class MatrixPath:
             self.n_ctx = n_ctx
             self.kc = [torch.zeros(nkv * n_ctx * hd, dtype=torch.int16, device=device) for _ in range(sh.n_layer)]
             self.vc = [torch.zeros(nkv * hd * n_ctx, dtype=torch.int16, device=device) for _ in range(sh.n_layer)]
-            theta_scale = np.float32(np.power(np.float32(sh.rope_base), np.float32(-2.0 / hd)))
-            cos = np.zeros((n_ctx, hd // 2), np.float32)
-            sin = np.zeros((n_ctx, hd // 2), np.float32)
-            for p in range(n_ctx):
-                th = np.float32(p)
-                for j in range(hd // 2):
-                    cos[p, j], sin[p, j] = np.cos(th), np.sin(th)
-                    th = np.float32(th * theta_scale)
+            cos, sin = rope_tables(sh, n_ctx)
             self.rope_cos = torch.from_numpy(cos).to(device)
             self.rope_sin = torch.from_numpy(sin).to(device)
             self.kq_scale = float(np.float32(1.0) / np.sqrt(np.float32(hd)))
@@ -208,7 +254,11 @@ class MatrixPath:
             # choice of its logits back into it (one GPU: the head is whole)
             if world != 1:
                 raise ValueError("the device token loop needs the whole output head on one GPU")
-            self.embd = device_weights(Q.Q4_K, sh.n_vocab, sh.n_embd, seed * 7919 + 555, device)
+            if reader is not None:
+                self.embd_type, self.embd = from_file("token_embd.weight", sh.n_vocab, sh.n_embd)
+            else:
+                self.embd_type = Q.Q4_K
+                self.embd = device_weights(Q.Q4_K, sh.n_vocab, sh.n_embd, seed * 7919 + 555, device)
             self.token = torch.zeros(1, dtype=torch.int64, device=device)
             self.x_embed = torch.empty(sh.n_embd, device=device)
         if fused and world > 1:
@@ -315,7 +365,7 @@ class MatrixPath:
         nxt = 0
         n = 0
         if self.embed:
-            s.row_to_f32_dev(Q.Q4_K, self.embd, d, self.sh.n_vocab, self.token, 1, self.x_embed, stream=h)
+            s.row_to_f32_dev(self.embd_type, self.embd, d, self.sh.n_vocab, self.token, 1, self.x_embed, stream=h)
             cur = self.x_embed
             n += 1
         for il, lay in enumerate(self.layers):
@@ -338,7 +388,7 @@ class MatrixPath:
                 nh, nkvl = nq // hd, nkv // hd
                 s.attention_step(y["q"], y["k"], y["v"], self.kc[il], self.vc[il], self.rope_cos[p],
                                  self.rope_sin[p], nh, nkvl, hd, hd, self.n_ctx, p, self.kq_scale, self.x_attn_buf,
-                                 stream=h)
+                                 neox=self.sh.neox, stream=h)
                 xa = self.x_attn_buf
                 n += 1
             to, wo = lay["o"]

@@ -1,22 +1,31 @@
 #!/usr/bin/env python
-"""Q4_K decode-matvec HBM throughput on B200 (BASELINE.json metric).
+"""Q4_K decode-matvec HBM throughput on B200, with the model-level decode and
+prefill rates of the quantized matrix path beside it.
 
-Workload (the Q4_K leg of the per-format sweep):
-batch-1 matvecs y = W x with W a random Q4_K matrix of shape (rows x K)
-4096x4096, 14336x4096 and 4096x14336, x ~ N(0,1) f32 quantized to Q8_K. One
-step streams every weight copy of every shape once: each shape rotates
-through distinct device copies totalling >= 4x the L2 size, so no step reads
-weights from L2.
+Headline workload (the Q4_K leg of the per-format matvec sweep): batch-1
+matvecs y = W x with W a random Q4_K matrix of shape (rows x K) 4096x4096,
+14336x4096 and 4096x14336, x ~ N(0,1) f32 quantized to Q8_K. One step streams
+every weight copy of every shape once: each shape rotates through distinct
+device copies totalling >= 4x the L2 size, so no step reads weights from L2.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py --case NAME      # one small profiling workload (below)
 
 Under torchrun each rank runs the same sweep on its own GPU (independent
-replicas, weak scaling; there is no data-path collective). Rank 0 prints one
-JSON line. value = algorithmic bytes of all ranks' steps / max-over-ranks
-device time. e2e = the same metric through sicu_gemv_host, the call shape of
-the reference's backend gemv slot: pinned host x in, host y out, per matvec.
---impl reference times the reference's own CPU matvec (si_backend_cpu()->gemv,
-AVX2, all host threads) on host copies of the same sweep.
+replicas, weak scaling; there is no data-path collective in a matvec sweep).
+Rank 0 prints one JSON line. value = algorithmic bytes of all ranks' steps /
+max-over-ranks device time. e2e = the same metric through sicu_gemv_host, the
+call shape of the reference's backend gemv slot: pinned host x in, host y out,
+per matvec. --impl reference times the reference's own CPU matvec
+(si_backend_cpu()->gemv, AVX2, all host threads) on host copies of the sweep.
+
+Beside the headline: `per_format` (every weight format at every sweep shape
+and the 5632x2048 single-matvec shape, batched and one launch per matvec),
+`model_path` (decode / prefill tok/s of llama-shaped models: TinyLlama-1.1B,
+Llama-3-8B, Qwen2.5-32B tensor parallel over the run's GPUs), the reference
+engine's own CPU rates on the same model shapes (si_engine_forward, token
+serial, all host threads), and last `tp_curve`, the Qwen2.5-32B rates at this
+GPU count against one GPU measured in the same run.
 """
 
 from __future__ import annotations
@@ -45,12 +54,12 @@ SHAPES = [(4096, 4096), (14336, 4096), (4096, 14336)]   # rows x K
 WTYPE = Q.Q4_K
 PEAKS = ROOT / "MEASURED_PEAKS.json"
 FALLBACK_HBM = 6650.0
-# DRAM traffic of the dominant kernel from the ncu capture summarised in
-# profiles/gemv_q4k_sweep.md: one batched launch of 17 Q4_K 14336x4096 copies
-# read+wrote 1.005x its algorithmic bytes; traffic grows with the matrices a
-# launch streams, so a bench launch's traffic is that ratio times its bytes
+# DRAM traffic of the dominant kernel from an ncu capture (--set full) of one
+# batched launch of 17 Q4_K 14336x4096 copies: it read and wrote 1.005x its
+# algorithmic bytes; traffic grows with the matrices a launch streams, so a
+# bench launch's traffic is that ratio times its bytes
 NCU_TRAFFIC = {"ratio_to_algorithmic": 1.005,
-               "source": "profiles/gemv_q4k_sweep.md (ncu --set full, 17 x 14336x4096 launch)"}
+               "source": "ncu --set full of one batched launch of 17 x Q4_K 14336x4096 (gemv_kernel<12>)"}
 
 
 def peak_hbm() -> tuple[float, str]:
@@ -379,8 +388,7 @@ def model_prefill(torch, s, shape, dev, stream, world, rank, group, m_tok, reps)
            "TFLOPs": round(tflops, 1), "f16_tensor_frac": round(tflops / f16_peak, 4),
            "int8_tensor_frac_proxy": round(tflops / (2 * f16_peak), 4), "peak_kind": kind,
            "note": "tensor-core kernel for Q4_K and Q6_K (kind::f16 MMAs on exact f16 (scale x quant) operands); "
-                   "int8 peak taken as 2x the measured bf16 dense peak",
-           "profile": "profiles/prefill_q4k_4096x4096_m512.md (ncu: utchmma f16->f32 ops = 22.6% of peak)"}
+                   "int8 peak taken as 2x the measured bf16 dense peak"}
     del m
     torch.cuda.empty_cache()
     return out
@@ -389,16 +397,17 @@ def model_prefill(torch, s, shape, dev, stream, world, rank, group, m_tok, reps)
 def model_batch_decode(torch, s, shape, dev, stream, world, rank, group, batch, reps) -> dict:
     """Decode tok/s of the matrix path for `batch` sequences per step (one
     token each): every weight product once per step for all of them, through
-    sicu_gemm_prefill_f32 (the tensor-core kernel with 32-token tiles)."""
+    sicu_gemv_batch (the batch decode kernel: weights decoded in registers,
+    mma.sync tiles of 16 rows x 8 tokens)."""
     from siphon_b200 import model_path as mp
     m = mp.MatrixPath(s, shape, dev, world, rank, group, seed=6, max_tokens=batch)
     with torch.cuda.stream(stream):
-        m.prefill(stream, batch)
+        launches = m.batch_step(stream, batch)     # sizes the workspace outside capture
     torch.cuda.synchronize()
     g = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g, stream=stream):
         for _ in range(DECODE_PER_GRAPH):
-            m.prefill(stream, batch)
+            m.batch_step(stream, batch)
     ms = _time_graph(torch, g, stream, reps, world, dev)
     del g
     steps = reps * DECODE_PER_GRAPH
@@ -407,91 +416,232 @@ def model_batch_decode(torch, s, shape, dev, stream, world, rank, group, batch, 
     peak, peak_kind = peak_hbm()
     out = {"batch": batch, "tok_s": round(batch * steps / (ms * 1e-3), 1), "us_per_step": round(us, 2),
            "weight_bytes_per_step_per_gpu": m.weight_bytes, "GBps_per_gpu": round(gbps, 1),
-           "hbm_frac": round(gbps / peak, 4), "peak_kind": peak_kind,
+           "hbm_frac": round(gbps / peak, 4), "peak_kind": peak_kind, "library_calls_per_step": launches,
            "allreduces_per_step": 2 * shape.n_layer if world > 1 else 0}
+    assert s.status() == 0, "a batch matvec wait gave up"
     del m
     torch.cuda.empty_cache()
     return out
 
 
-def model_cpu_baseline(budget_s: float = 8.0) -> dict | None:
-    """The reference's CPU gemv over the TinyLlama-shape matrix path (host
-    copies), a bounded number of tokens; larger shapes are estimated from the
-    bandwidth it reaches (the CPU path is bandwidth-bound; its prefill is
-    token-serial, so CPU prefill tok/s = CPU decode tok/s)."""
+def _host_threads() -> int:
+    return len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+
+
+def _scratch_dir(need_bytes: int) -> str:
+    """A directory for temporary model files: RAM-backed /dev/shm when it has
+    room, else the system temporary directory."""
+    import shutil
+    import tempfile
+    for d in ("/dev/shm", tempfile.gettempdir()):
+        try:
+            if shutil.disk_usage(d).free > need_bytes * 1.2:
+                return d
+        except OSError:
+            pass
+    return tempfile.gettempdir()
+
+
+def engine_cpu_baseline(dev) -> dict | None:
+    """The reference engine's own CPU rates on the model shapes the GPU lines
+    run: si_engine_forward token-serial (src/engine.c:288-398; the reference's
+    prompt loop is token-serial too, src/cmd_run.c:273-321), its default
+    dispatch (AVX2 dots), a pthread pool of all host threads. Each model is a
+    synthetic GGUF of the full shape with random blocks (generated on the GPU,
+    written to RAM-backed storage), timed on a bounded sample:
+
+    * TinyLlama-1.1B shape: a 32-token prompt, then 128 greedy tokens (whole);
+    * Llama-3-8B shape: the first 64 tokens of a 512-token prompt;
+    * Qwen2.5-32B shape: the first 16 tokens of a 512-token prompt, then 16
+      greedy tokens. Batch-8 decode on the CPU is eight sequences run one
+      after the other, so its rate is the batch-1 rate."""
+    import zlib
+
+    from oracle.oracle import E2E_SO, RefEngine
     from siphon_b200 import model_path as mp
     from siphon_b200 import synth_model as sm
-    gemv, kind, threads = cpu_gemv_handle()
-    if gemv is None:
+    if not E2E_SO.exists():
         return None
-    sh = sm.TINYLLAMA
-    shp = mp.shard_shapes(sh, mp.tp_partition(sh, 1, 0))
-    mats = []
-    for il in range(sh.n_layer):
-        t = mp.layer_types(il)
-        for j, name in enumerate(("q", "k", "v", "o", "gate", "up", "down")):
-            n_out, n_in = shp[name]
-            mats.append((t[name], synth.weights(t[name], n_out, n_in, seed=il * 16 + j), n_out, n_in))
-    n_out, n_in = shp["head"]
-    mats.append((Q.Q6_K, synth.weights(Q.Q6_K, n_out, n_in, seed=999), n_out, n_in))
-    xs = {n: synth.activations(n, 1, seed=3)[0] for n in {m[3] for m in mats}}
-    ys = {n: np.zeros(n, np.float32) for n in {m[2] for m in mats}}
-    tens = [(gemv.tensor(t, w, n_in, n_out), n_in, n_out) for t, w, n_out, n_in in mats]
+    threads = _host_threads()
 
-    def token():
-        for te, n_in, n_out in tens:
-            gemv(te, xs[n_in], ys[n_out])
+    def gpu_blocks(wt, n_out, n_in, key):
+        seed = zlib.crc32(repr(key).encode())
+        return mp.device_weights(wt, n_out, n_in, seed, dev).cpu().numpy()
 
-    token()
-    t0 = time.perf_counter()
-    n = 0
-    while time.perf_counter() - t0 < budget_s or n < 2:
-        token()
-        n += 1
-    dt = time.perf_counter() - t0
-    gemv.close()
-    wb = mp.step_weight_bytes(sh)
-    gbps = wb * n / dt / 1e9
-    return {"decode_tok_s": round(n / dt, 2), "GBps": round(gbps, 2), "cores": threads, "kind": kind,
-            "sample": f"{n} TinyLlama-shape tokens (all 155 weight matrices each), si_backend_cpu()->gemv",
-            "est_llama3_8b_prefill_tok_s": round(gbps * 1e9 / mp.step_weight_bytes(sm.LLAMA3_8B), 3),
-            "est_qwen32b_decode_tok_s": round(gbps * 1e9 / mp.step_weight_bytes(sm.QWEN25_32B), 3)}
+    def run(sh, name, n_prompt, n_gen, prompt_len):
+        nbytes = sum(n_out * Q.row_bytes(wt, n_in) for _, wt, n_out, n_in in sm.matrices(sh))
+        path = Path(_scratch_dir(nbytes)) / f"siphon_bench_{name}_{os.getpid()}.gguf"
+        t0 = time.perf_counter()
+        sm.write_llama(path, sh, seed=1, blocks=gpu_blocks)
+        t_write = time.perf_counter() - t0
+        try:
+            e = RefEngine(path, use_cuda=False, n_ctx=max(512, n_prompt + n_gen), threads=threads, scalar=False)
+            try:
+                prompt = np.random.default_rng(2).integers(0, sh.n_vocab, n_prompt).tolist()
+                e.forward(prompt[0])                       # pages the mapped file in
+                t0 = time.perf_counter()
+                for tok in prompt[1:]:
+                    logits = e.forward(tok)
+                t1 = time.perf_counter()
+                tok = int(np.argmax(logits))
+                for _ in range(n_gen):
+                    tok = int(np.argmax(e.forward(tok)))
+                t2 = time.perf_counter()
+            finally:
+                e.close()
+        finally:
+            path.unlink(missing_ok=True)
+        out = {"prompt_tok_s": round((n_prompt - 1) / (t1 - t0), 3)}
+        if n_gen:
+            out["decode_tok_s"] = round(n_gen / (t2 - t1), 3)
+        out["sample"] = (f"prompt tokens 2..{n_prompt} of a {prompt_len}-token prompt"
+                         + (f", then {n_gen} greedy tokens" if n_gen else "")
+                         + f" (model file of random blocks written in {t_write:.1f} s)")
+        return out
+
+    res = {"engine": "si_engine_forward token-serial, AVX2 dispatch", "cores": threads, "kind": "reference",
+           "cpu": cpu_model(),
+           "decode_tinyllama": run(sm.TINYLLAMA, "tinyllama", 32, 128, 32),
+           "prefill_llama3_8b": run(sm.LLAMA3_8B, "llama3_8b", 64, 0, 512),
+           "qwen32b": run(sm.QWEN25_32B, "qwen32b", 16, 16, 512)}
+    res["qwen32b"]["note"] = ("prompt rate over the first tokens of a 512-token prompt; batch-8 decode on the CPU "
+                              "runs the 8 sequences one after the other (the batch-1 rate)")
+    torch_empty_cache()
+    return res
 
 
-def model_metrics(torch, s, dev, stream, world, rank, quick: bool) -> dict:
+def torch_empty_cache() -> None:
+    try:
+        import torch
+        torch.cuda.empty_cache()
+    except Exception:
+        pass
+
+
+def bench_weights(wt: int, n_out: int, n_in: int, seed: int, dev):
+    """Device weight blocks of the sweep's distribution: random blocks with
+    f16 scales U[1e-4, 1e-2] for the quantized formats, f16(U[-1, 1)) for F16."""
+    import torch
+
+    from siphon_b200 import model_path as mp
+    if wt == Q.F16:
+        g = torch.Generator(device=dev)
+        g.manual_seed(seed)
+        v = torch.rand(n_out * n_in, device=dev, generator=g) * 2 - 1
+        return v.half().view(torch.uint8)
+    return mp.device_weights(wt, n_out, n_in, seed, dev)
+
+
+PER_FORMAT_SHAPES = [(4096, 4096), (14336, 4096), (4096, 14336), (5632, 2048)]
+
+
+def per_format(torch, s, dev, stream, l2: int) -> dict:
+    """Every weight format at every sweep shape and at the single-matvec shape
+    5632x2048: GB/s (algorithmic bytes / device time) batched (one
+    sicu_gemv_multi launch over copies totalling >= 4x L2) and one launch per
+    matvec, each as a fraction of the measured HBM copy bandwidth."""
+    peak, peak_kind = peak_hbm()
+    out = {"peak_GBps": peak, "peak_kind": peak_kind,
+           "l2": "per shape, distinct weight copies totalling >= 4x L2, capped at 64 copies (>= 1.8x L2 for "
+                 "the smallest matrices)"}
+    h = stream.cuda_stream
+    for wt in Q.WEIGHT_TYPES:
+        row = {}
+        for n_out, n_in in PER_FORMAT_SHAPES:
+            wb = n_out * Q.row_bytes(wt, n_in)
+            c = min(64, max(2, math.ceil(4 * l2 / wb)))    # a launch takes up to 64 matrices
+            ws = [bench_weights(wt, n_out, n_in, 11 + i, dev) for i in range(c)]
+            x = torch.from_numpy(synth.activations(n_in, 1, seed=7)[0]).to(dev)
+            ys = [torch.empty(n_out, device=dev) for _ in range(c)]
+
+            def batched():
+                s.gemv_multi(wt, ws, [n_out] * c, n_in, x, ys, stream=h)
+
+            def single():
+                for w, y in zip(ws, ys):
+                    s.gemv_f32(wt, w, n_in, n_out, x, y, stream=h)
+
+            b = Q.matvec_bytes(wt, n_out, n_in)
+            res = {}
+            for name, fn, reps in (("batched", batched, 6), ("single", single, 2)):
+                with torch.cuda.stream(stream):
+                    fn()
+                torch.cuda.synchronize()
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=stream):
+                    for _ in range(reps):
+                        fn()
+                ms = _time_graph(torch, g, stream, 2, 1, dev) / 2
+                del g
+                us = ms * 1e3 / (reps * c)
+                gbps = b / (us * 1e-6) / 1e9
+                res[f"{name}_GBps"] = round(gbps, 1)
+                res[f"{name}_frac"] = round(gbps / peak, 4)
+            row[f"{n_out}x{n_in}"] = res
+            del ws, ys
+        out[Q.NAMES[wt]] = row
+    torch.cuda.empty_cache()
+    assert s.status() == 0, "a matvec wait gave up"
+    return out
+
+
+TP_ROWS = ("decode_b1", "decode_b1_steps", "decode_b1_full", "decode_b1_nccl", "decode_b8", "prefill512")
+
+
+def tp_rows(torch, s, shape, dev, stream, world, rank, reps) -> dict:
+    """The configs[4] measurements at this world size: batch-1 decode (matrix
+    path with the all-reduces fused into the matvecs; with the activation
+    steps; the whole step with attention; with NCCL all-reduces), batch-8
+    decode and the 512-token prefill."""
+    rows = {}
+    rows["decode_b1"] = model_decode(torch, s, shape, dev, stream, world, rank, None, reps, fused=world > 1)
+    rows["decode_b1_steps"] = model_decode(torch, s, shape, dev, stream, world, rank, None, reps,
+                                           fused=world > 1, steps=True)
+    if _heads_align(shape, world):
+        rows["decode_b1_full"] = model_decode(torch, s, shape, dev, stream, world, rank, None, reps,
+                                              fused=world > 1, attention_ctx=512)
+    if world > 1:
+        rows["decode_b1_nccl"] = model_decode(torch, s, shape, dev, stream, world, rank, None, reps)
+    rows["decode_b8"] = model_batch_decode(torch, s, shape, dev, stream, world, rank, None, 8, reps)
+    rows["prefill512"] = model_prefill(torch, s, shape, dev, stream, world, rank, None, 512, max(2, reps // 2))
+    return rows
+
+
+def tp_curve(world: int, rows: dict, one: dict) -> dict:
+    """Compact Qwen2.5-32B summary (printed last in the line): tok/s at this
+    GPU count, at one GPU in the same run, and the efficiency
+    (tok/s at N) / (N x tok/s at 1)."""
+    cur = {k: rows[k]["tok_s"] for k in TP_ROWS if k in rows}
+    base = {k: one[k]["tok_s"] for k in TP_ROWS if k in one}
+    eff = {}
+    for k, v in cur.items():
+        b = base.get("decode_b1" if k == "decode_b1_nccl" else k)
+        if b:
+            eff[k] = round(v / (world * b), 3)
+    return {"shape": "Qwen2.5-32B", "n_gpus": world, "tok_s": cur, "tok_s_1gpu": base, "efficiency": eff,
+            "allreduce": "fused into the matvecs over NVLink peer stores (decode_b1*), NCCL (decode_b1_nccl, "
+                         "decode_b8, prefill512)" if world > 1 else "none (one GPU)"}
+
+
+def model_metrics(torch, s, dev, stream, world, rank, quick: bool) -> tuple[dict, dict]:
     from siphon_b200 import synth_model as sm
     out = {}
     reps = 3 if quick else 10
-    out["tp_decode"] = {"config": "configs[4] Qwen2.5-32B shape, batch 1, matrix path, "
-                                  f"tensor parallel x{world} (column-split QKV/gate/up/head, row-split o/down, "
-                                  "an all-reduce after o and after down per layer, fused into the matvecs)"
-                                  if world > 1 else "configs[4] Qwen2.5-32B shape, batch 1, matrix path, one GPU",
-                        **model_decode(torch, s, sm.QWEN25_32B, dev, stream, world, rank, None, reps,
-                                       fused=world > 1)}
-    out["tp_decode_steps"] = {"config": "as tp_decode, with the residual adds, RMS norms and SwiGLU between the "
-                                        "products fused into them (sicu_gemv_fused)",
-                              **model_decode(torch, s, sm.QWEN25_32B, dev, stream, world, rank, None, reps,
-                                             fused=world > 1, steps=True)}
-    full_cfg = ("as tp_decode_steps, plus RoPE, the f16 KV-cache store and attention over a 512-position "
-                "context (the token at position 511)")
-    if _heads_align(sm.QWEN25_32B, world):
-        out["tp_decode_full"] = {"config": full_cfg,
-                                 **model_decode(torch, s, sm.QWEN25_32B, dev, stream, world, rank, None, reps,
-                                                fused=world > 1, attention_ctx=512)}
-    else:
-        out["tp_decode_full"] = {"config": full_cfg, "skipped": f"the query heads do not split into whole KV groups "
-                                                                f"over {world} ranks"}
-    if world > 1:
-        out["tp_decode_nccl"] = {"config": "as tp_decode, the all-reduces as NCCL calls between the matvecs",
-                                 **model_decode(torch, s, sm.QWEN25_32B, dev, stream, world, rank, None, reps)}
-    out["tp_prefill"] = {"config": "configs[4] Qwen2.5-32B shape, 512-token prompt, matrix path, "
-                                   + (f"tensor parallel x{world} (an NCCL all-reduce of the 512 x 5120 partial "
-                                      "after o and after down per layer)" if world > 1 else "one GPU"),
-                         **model_prefill(torch, s, sm.QWEN25_32B, dev, stream, world, rank, None, 512,
-                                         max(2, reps // 2))}
-    out["tp_decode_batch8"] = {"config": "configs[4] Qwen2.5-32B shape, batch 8, matrix path, "
-                                         + (f"tensor parallel x{world}" if world > 1 else "one GPU"),
-                               **model_batch_decode(torch, s, sm.QWEN25_32B, dev, stream, world, rank, None, 8, reps)}
+    sh = sm.QWEN25_32B
+    tp_desc = (f"configs[4] Qwen2.5-32B shape, tensor parallel x{world} (column-split QKV/gate/up/head, row-split "
+               "o/down, an all-reduce after o and after down per layer)" if world > 1
+               else "configs[4] Qwen2.5-32B shape, one GPU")
+    rows = tp_rows(torch, s, sh, dev, stream, world, rank, reps)
+    # at N > 1 the same measurements on this rank's GPU alone, for the
+    # efficiency (every rank runs them at the same time; no collective)
+    one = tp_rows(torch, s, sh, dev, stream, 1, 0, reps) if world > 1 else rows
+    out["tp"] = {"config": tp_desc, "rows": rows,
+                 "notes": {"decode_b1": "matrix path, batch 1 (every weight product of a token)",
+                           "decode_b1_steps": "plus the residual adds, RMS norms and SwiGLU fused into the products",
+                           "decode_b1_full": "plus RoPE, the f16 KV cache and attention, the token at position 511",
+                           "decode_b1_nccl": "decode_b1 with NCCL all-reduces between the matvecs",
+                           "decode_b8": "8 sequences per step, every weight product once per step for all 8",
+                           "prefill512": "a 512-token prompt's products"}}
     if world == 1:
         out["decode"] = {"config": "configs[2] TinyLlama-1.1B shape, batch 1, matrix path",
                          **model_decode(torch, s, sm.TINYLLAMA, dev, stream, 1, 0, None, reps * 4)}
@@ -508,9 +658,9 @@ def model_metrics(torch, s, dev, stream, world, rank, quick: bool) -> dict:
     out["scope"] = ("every weight-matrix product of the forward pass (per layer Wq, Wk, Wv, Wo, W_gate, W_up, "
                     "W_down; then the output head) with synthetic Q4_K_M-style weights; the *_steps lines also run "
                     "the residual adds, RMS norms and SwiGLU between them, fused into the products (Wo reading a "
-                    "fixed activation); decode_full also runs RoPE, the KV cache and attention: the whole step but "
+                    "fixed activation); *_full lines also run RoPE, the KV cache and attention: the whole step but "
                     "the embedding lookup")
-    return out
+    return out, tp_curve(world, rows, one)
 
 
 def run_ours(args, world, rank, local) -> None:
@@ -653,15 +803,18 @@ def run_ours(args, world, rank, local) -> None:
     d2h = sum(len(ws) * 4 * n_out for n_out, _, ws, _, _ in mats)
 
     del g
-    model = None
+    fmt = None
+    if world == 1 and not args.no_model:
+        fmt = per_format(torch, s, dev, stream, l2)
+    model = curve = None
     if not args.no_model:
-        model = model_metrics(torch, s, dev, stream, world, rank, quick=args.steps < 10)
+        model, curve = model_metrics(torch, s, dev, stream, world, rank, quick=args.steps < 10)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(copies)
         if model is not None:
-            mc = model_cpu_baseline()
+            mc = engine_cpu_baseline(dev)
             if mc is not None:
                 model["cpu_baseline"] = mc
 
@@ -688,13 +841,106 @@ def run_ours(args, world, rank, local) -> None:
     }
     if cpu is not None:
         line["cpu_baseline"] = cpu
+    if fmt is not None:
+        line["per_format"] = fmt
     if model is not None:
         line["model_path"] = model
+    if curve is not None:
+        line["tp_curve"] = curve            # last: kept by a reader of the line's tail
     print(json.dumps(line))
+
+
+# ---- single profiling workloads (run under ncu on one GPU) -----------------------------------
+CASES = {
+    "flat": "gemv_flat_kernel<Q4_K>: one sicu_gemv_multi launch over 4 copies of Q4_K 27648x5120, 4 times",
+    "ar": "gemv_kernel<Q4_K, AR> (one-rank group) and the plain gemv_kernel<Q4_K> alternating, Q4_K 5120x13824",
+    "prefill": "prefill_kernel<Q4_K>: 4096x4096, 512 tokens, twice",
+    "steps": "Q4_K Wq/Wk/Wv of the 32B shape (5120 -> 5120+1024+1024): plain and with the residual add + "
+             "RMS norm fused, alternating, 4 each",
+    "decode_full": "three eager decode steps of the TinyLlama-1.1B shape with the steps and attention, "
+                   "the token at position 511 of a 512-position context",
+    "batch8": "the batch-8 decode matvec: Q4_K and Q6_K 5120x27648, 8 tokens, 4 times each",
+}
+
+
+def run_case(case: str, reps: int = 4) -> int:
+    """Run one small workload on GPU 0 for an ncu capture; exits non-zero if
+    the library reports a device-side status bit."""
+    import torch
+
+    from siphon_b200 import lib
+    from siphon_b200 import model_path as mp
+    from siphon_b200 import synth_model as sm
+    if case not in CASES:
+        raise SystemExit(f"unknown case {case!r}: " + ", ".join(CASES))
+    torch.cuda.set_device(0)
+    s = lib.load()
+    s.init(0)
+    s.set_overlap(True)
+    dev = torch.device("cuda", 0)
+    if case == "flat":
+        wt, n_out, n_in, c = Q.Q4_K, 27648, 5120, 4
+        ws = [mp.device_weights(wt, n_out, n_in, 1 + i, dev) for i in range(c)]
+        x = torch.from_numpy(synth.activations(n_in, 1, seed=2)[0]).to(dev)
+        ys = [torch.empty(n_out, device=dev) for _ in range(c)]
+        for _ in range(reps):
+            s.gemv_multi(wt, ws, [n_out] * c, n_in, x, ys)
+    elif case == "ar":
+        wt, n_out, n_in = Q.Q4_K, 5120, 13824
+        g = s.ar_create(1, 0, n_out)
+        g.open([g.local_handle])
+        w = mp.device_weights(wt, n_out, n_in, 1, dev)
+        x = torch.from_numpy(synth.activations(n_in, 1, seed=2)[0]).to(dev)
+        y = torch.empty(n_out, device=dev)
+        for _ in range(reps):
+            s.gemv_ar(wt, w, n_in, n_out, x, y, g)
+            s.gemv_f32(wt, w, n_in, n_out, x, y)
+        torch.cuda.synchronize()
+        g.destroy()
+    elif case == "prefill":
+        wt, n, m = Q.Q4_K, 4096, 512
+        w = mp.device_weights(wt, n, n, 1, dev)
+        x = torch.randn(m, n, device=dev)
+        y = torch.empty(m, n, device=dev)
+        for _ in range(2):
+            s.gemm_prefill_f32(wt, w, n, n, x, m, y)
+    elif case == "steps":
+        wt, n_in, outs = Q.Q4_K, 5120, [5120, 1024, 1024]
+        ws = [mp.device_weights(wt, n, n_in, 1 + i, dev) for i, n in enumerate(outs)]
+        x = torch.randn(n_in, device=dev)
+        r = torch.randn(n_in, device=dev)
+        gam = 1.0 + 0.1 * torch.randn(n_in, device=dev)
+        h = torch.empty(n_in, device=dev)
+        ys = [torch.empty(n, device=dev) for n in outs]
+        for _ in range(reps):
+            s.gemv_multi(wt, ws, outs, n_in, x, ys)
+            s.gemv_fused(wt, ws, outs, n_in, x, lib.rms_norm_step(gam, 1e-6, r, h), ys)
+    elif case == "decode_full":
+        m = mp.MatrixPath(s, sm.TINYLLAMA, dev, seed=4, attention=True, n_ctx=512)
+        m.pos = 511
+        st = torch.cuda.Stream(device=dev)
+        with torch.cuda.stream(st):
+            for _ in range(3):
+                m.decode_step(st)
+        torch.cuda.synchronize()
+        m.close()
+    elif case == "batch8":
+        n_out, n_in, m = 5120, 27648, 8
+        x = torch.randn(m, n_in, device=dev)
+        y = torch.empty(m, n_out, device=dev)
+        for wt in (Q.Q4_K, Q.Q6_K):
+            w = mp.device_weights(wt, n_out, n_in, 1, dev)
+            for _ in range(reps):
+                s.gemm_prefill_f32(wt, w, n_in, n_out, x, m, y)
+    torch.cuda.synchronize()
+    st = s.status()
+    print(case, "status", st)
+    return 1 if st else 0
 
 
 def main() -> None:
     ap = argparse.ArgumentParser()
+    ap.add_argument("--case", choices=sorted(CASES), help="run one profiling workload and exit")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
@@ -702,6 +948,8 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-model", action="store_true", help="skip the model-level matrix-path measurements")
     args = ap.parse_args()
+    if args.case:
+        sys.exit(run_case(args.case))
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     world, rank, local = dist_setup()

@@ -19,8 +19,8 @@
  * host before any CUDA call. All device memory handed in is owned by the
  * caller; the library allocates device memory only in sicu_init, sicu_upload
  * / sicu_malloc, the all-reduce groups, and the growable buffers of
- * sicu_gemv_host, sicu_row_to_f32, the prefill product and sicu_gemv_fused's
- * F16 path.
+ * sicu_gemv_host, sicu_row_to_f32, the prefill product, the batch matvec and
+ * sicu_gemv_fused's F16 path.
  */
 #ifndef SIPHON_CUDA_H
 #define SIPHON_CUDA_H
@@ -151,6 +151,20 @@ SICU_API int sicu_gemv_f32(uint32_t wtype, const void *dw, int64_t n_in, int64_t
  * n_mats separate sicu_gemv_f32 calls. */
 SICU_API int sicu_gemv_multi(uint32_t wtype, int n_mats, const void *const *dw, const int64_t *n_out,
                              int64_t n_in, const float *dx, float *const *dy, void *stream);
+/* Batch decode: dy_i[t] = W_i x_t for m (0..8) f32 activation rows x_t
+ * (dx: [m][n_in], 16-byte aligned; dy[i]: [m][n_out[i]]) and n_mats (1..16)
+ * matrices of one type and row length: one decode step of up to eight
+ * sequences. Q4_K and Q6_K weights stream from memory once for all rows (a
+ * tensor-core kernel: weight blocks decoded in registers to exact f16
+ * products, exact integer lane sums, the reference's float chains); other
+ * types, and m == 1, run the matvec per row. Every output is bit-identical to
+ * sicu_gemv_f32 of that row, i.e. to the reference's scalar dot product per
+ * token. The reference has no batched step: it runs one si_engine_forward per
+ * token and sequence (src/engine.c:288-398), one backend gemv per matrix. A
+ * per-device workspace (about 4.3 KB per 256 inputs) grows on the first call
+ * with a larger n_in; make that call before any stream capture. */
+SICU_API int sicu_gemv_batch(uint32_t wtype, int n_mats, const void *const *dw, const int64_t *n_out, int64_t n_in,
+                             const float *dx, int64_t m, float *const *dy, void *stream);
 /* Same, with host input and output buffers (one activation row): copies x
  * in, runs sicu_gemv_f32, copies y out and waits. This is the exact call
  * shape of the reference's backend gemv slot. When both buffers are
@@ -188,7 +202,9 @@ SICU_API int sicu_gemv_host_noalloc(uint32_t wtype, const void *dw, int64_t n_in
  * for t < m (0 <= m <= 65535). dxq holds m consecutive rows of pair-format
  * blocks (Q8_K for the K formats: sicu_quantize_q8_K); the _f32 form takes m
  * f32 rows (16-byte aligned) and quantizes them first.
- * Q4_K and Q6_K run on the tensor cores (tcgen05 MMAs, accumulators in tensor
+ * For m <= 8, Q4_K and Q6_K run the batch decode kernel of sicu_gemv_batch
+ * (bit-identical with the per-token matvec). For larger m they run on the
+ * tensor cores (tcgen05 MMAs, accumulators in tensor
  * memory, the token operand loaded by TMA): the integer sums per super-block are exact
  * and the d / dmin scaling is applied per super-block, so each output agrees
  * with the reference's per-row dot (src/kernels.c:349-410) within a relative

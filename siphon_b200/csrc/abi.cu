@@ -40,6 +40,9 @@ struct DevState {
     // growable f32 activation of sicu_gemv_fused's F16 path (the step's output)
     float *pro_buf = nullptr;
     size_t pro_buf_bytes = 0;
+    // growable activation records of the batch matvec
+    void *bt_ws = nullptr;
+    size_t bt_ws_bytes = 0;
 };
 
 constexpr int MAX_DEV = 64;
@@ -229,6 +232,7 @@ int sicu_shutdown(void) {
         if (ds.stage) cudaFree(ds.stage);
         if (ds.pf_ws) cudaFree(ds.pf_ws);
         if (ds.pro_buf) cudaFree(ds.pro_buf);
+        if (ds.bt_ws) cudaFree(ds.bt_ws);
         ds = DevState{};
     }
     if (have && cur >= 0) cudaSetDevice(cur);
@@ -498,6 +502,48 @@ static int grow_prefill_ws(DevState &ds, size_t need) {
     return SICU_OK;
 }
 
+// The batch matvec (m <= 8 rows, Q4_K / Q6_K) for n_mats matrices sharing one
+// activation: xf (m f32 rows) or xq (m Q8_K rows).
+static int batch_common(uint32_t wtype, int n_mats, const void *const *dw, const int64_t *n_out, int64_t n_in,
+                        const float *xf, const void *xq, int64_t m, float *const *dy, cudaStream_t st) {
+    DevState *ds;
+    if (int rc = current(ds)) return rc;
+    const size_t need = batch_workspace_bytes(n_in);
+    if (ds->bt_ws_bytes < need) {
+        if (ds->bt_ws) cudaFree(ds->bt_ws);
+        ds->bt_ws = nullptr;
+        ds->bt_ws_bytes = 0;
+        if (cudaMalloc(&ds->bt_ws, need) != cudaSuccess) {
+            cudaGetLastError();
+            return fail(SICU_ENOMEM, "batch workspace of %zu bytes", need);
+        }
+        ds->bt_ws_bytes = need;
+    }
+    BatchLaunch L{};
+    L.nmat = n_mats;
+    for (int i = 0; i < n_mats; ++i) {
+        L.w[i] = dw[i];
+        L.y[i] = dy[i];
+        L.n_out[i] = n_out[i];
+    }
+    L.n_in = n_in;
+    L.xf = xf;
+    L.xq = xq;
+    L.m = (int)m;
+    L.ws = ds->bt_ws;
+    L.num_sms = ds->sms;
+    L.smem_per_sm = ds->smem_per_sm;
+    L.smem_reserved = ds->smem_reserved;
+    L.overlap = g_overlap;
+    cudaGetDevice(&L.device);
+    L.status = ds->status;
+    const int rc = launch_batch(wtype, L, st);
+    if (rc == -1) return fail(SICU_EINVAL, "batch matvec: %d matrices, %lld rows (1..16, 1..8)", n_mats, (long long)m);
+    if (rc == -3) return fail(SICU_ENOTSUP, "batch matvec: no kernel for %s", tname(wtype));
+    if (rc != 0) return cuda_fail(cudaGetLastError(), "batch matvec launch");
+    return SICU_OK;
+}
+
 // xq: m rows of pair-format activation blocks (device), or null with xf set
 static int prefill_common(uint32_t wtype, const void *dw, int64_t n_in, int64_t n_out, const void *xq,
                           const float *xf, int64_t m, float *dy, cudaStream_t st) {
@@ -505,6 +551,13 @@ static int prefill_common(uint32_t wtype, const void *dw, int64_t n_in, int64_t 
     if (int rc = current(ds)) return rc;
     uint32_t pair;
     pair_of(wtype, pair);
+    if (m <= BATCH_MAX && batch_supported(wtype)) {
+        // a few tokens (a batch of decode steps): every weight block read once
+        // for all of them, bit-identical with the per-token matvec
+        const void *w1[1] = {dw};
+        float *y1[1] = {dy};
+        return batch_common(wtype, 1, w1, &n_out, n_in, xf, xq, m, y1, st);
+    }
     if (!prefill_supported(wtype)) {
         // formats without a tensor-core kernel: the decode matvec per token
         const int64_t prb = pair_row_bytes(pair, n_in);
@@ -555,6 +608,39 @@ int sicu_gemm_prefill_f32(uint32_t wtype, const void *dw, int64_t n_in, int64_t 
     if (m == 0 || n_out == 0) return current_ok();
     if (!aligned(dx, 16)) return fail(SICU_EINVAL, "prefill: f32 activation must be 16-byte aligned");
     return prefill_common(wtype, dw, n_in, n_out, nullptr, dx, m, dy, (cudaStream_t)stream);
+}
+
+int sicu_gemv_batch(uint32_t wtype, int n_mats, const void *const *dw, const int64_t *n_out, int64_t n_in,
+                    const float *dx, int64_t m, float *const *dy, void *stream) {
+    if (n_mats < 1 || n_mats > 16) return fail(SICU_EINVAL, "batch matvec: %d matrices (1..16)", n_mats);
+    if (!dw || !n_out || !dy) return fail(SICU_EINVAL, "batch matvec: null array");
+    if (m < 0 || m > 8) return fail(SICU_EINVAL, "batch matvec: %lld activation rows (0..8)", (long long)m);
+    uint32_t pair;
+    for (int i = 0; i < n_mats; ++i)
+        if (int rc = check_matvec(wtype, dw[i], n_in, n_out[i], dx, dy[i], 1, pair)) return rc;
+    if (!aligned(dx, 16)) return fail(SICU_EINVAL, "batch matvec: f32 activation must be 16-byte aligned");
+    DevState *ds;
+    if (int rc = current(ds)) return rc;
+    if (m == 0) return SICU_OK;
+    const cudaStream_t st = (cudaStream_t)stream;
+    if (m > 1 && batch_supported(wtype)) return batch_common(wtype, n_mats, dw, n_out, n_in, dx, nullptr, m, dy, st);
+    // one activation row, or a type without a batch kernel: the matvec once per
+    // row (one launch for all matrices; F16 one launch per matrix)
+    for (int64_t t = 0; t < m; ++t) {
+        for (int i0 = 0; i0 < n_mats; i0 = (wtype == T_F16) ? i0 + 1 : n_mats) {
+            const int i1 = (wtype == T_F16) ? i0 + 1 : n_mats;
+            GemvLaunch L = make_launch(*ds, dw[i0], n_in, n_out[i0], dy[i0] + t * n_out[i0]);
+            L.xf = dx + t * n_in;
+            L.nmat = i1 - i0;
+            for (int i = i0; i < i1; ++i) {
+                L.wm[i - i0] = dw[i];
+                L.ym[i - i0] = dy[i] + t * n_out[i];
+                L.n_outm[i - i0] = n_out[i];
+            }
+            if (int rc = run_gemv(wtype, L, st)) return rc;
+        }
+    }
+    return SICU_OK;
 }
 
 // ---- fused all-reduce groups ---------------------------------------------------------

@@ -109,6 +109,30 @@ size_t prefill_workspace_bytes(uint32_t wtype, int64_t n_in, int64_t n_out, int6
 // -3: no tensor-core kernel for the type; -4: tensor map encoding failed; -2: launch
 int launch_prefill(uint32_t wtype, const PrefillLaunch &L, cudaStream_t st);
 
+// batch decode matvec on the tensor cores: y[i][t][r] = (W_i x_t)[r] for
+// t < m <= 8 activation rows, every weight block read once for all of them;
+// bit-identical with the per-token matvec (Q4_K and Q6_K)
+constexpr int BATCH_MAX = 8;
+struct BatchLaunch {
+    int nmat;                     // 1..16 matrices of one type and row length
+    const void *w[16];
+    float *y[16];                 // [m][n_out[i]] each (device)
+    int64_t n_out[16];
+    int64_t n_in;
+    const float *xf;              // m f32 rows (device), or null with xq set
+    const void *xq;               // m Q8_K rows (device)
+    int m;
+    void *ws;                     // batch_workspace_bytes(n_in) bytes, 16-byte aligned
+    int num_sms, smem_per_sm, smem_reserved;
+    int overlap;                  // programmatic dependent launch of the prep kernel
+    int device;
+    int *status;
+};
+bool batch_supported(uint32_t wtype);
+size_t batch_workspace_bytes(int64_t n_in);
+// -1: bad launch (matrix or row count); -3: type without a batch kernel; -2: launch
+int launch_batch(uint32_t wtype, const BatchLaunch &L, cudaStream_t st);
+
 // the activation steps on their own, m rows of n floats (f32 out): RMS norm
 // (res, h_out per row, or null) and SwiGLU (n * m a multiple of 4)
 int launch_rms_norm(const float *x, const float *res, float *h_out, const float *g, int64_t n, int64_t m,

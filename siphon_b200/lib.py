@@ -46,6 +46,8 @@ SIGNATURES = {
     "sicu_gemv_f32": [_u32, _vp, _i64, _i64, _fp, _fp, _i64, _vp],
     "sicu_gemv_multi": [_u32, C.c_int, C.POINTER(C.c_void_p), C.POINTER(C.c_int64), _i64, _fp,
                         C.POINTER(C.c_void_p), _vp],
+    "sicu_gemv_batch": [_u32, C.c_int, C.POINTER(C.c_void_p), C.POINTER(C.c_int64), _i64, _fp, _i64,
+                        C.POINTER(C.c_void_p), _vp],
     "sicu_gemv_host": [_u32, _vp, _i64, _i64, _fp, _fp, _vp],
     "sicu_gemv_host_noalloc": [_u32, _vp, _i64, _i64, _fp, _fp, _vp],
     "sicu_row_to_f32": [_u32, _vp, _i64, C.POINTER(C.c_int64), _i64, _fp, _vp],
@@ -191,6 +193,14 @@ class SiphonCuda:
         y_arr = (C.c_void_p * n)(*[_ptr(y) for y in dys])
         o_arr = (C.c_int64 * n)(*n_outs)
         self.check(self.lib.sicu_gemv_multi(wtype, n, w_arr, o_arr, n_in, _ptr(dx), y_arr, _ptr(stream)))
+
+    def gemv_batch(self, wtype: int, dws, n_outs, n_in: int, dx, m: int, dys, stream=None) -> None:
+        """dys[i][t] = W_i x_t for the m <= 8 f32 rows of dx (each dys[i] is [m][n_outs[i]])."""
+        n = len(dws)
+        w_arr = (C.c_void_p * n)(*[_ptr(w) for w in dws])
+        y_arr = (C.c_void_p * n)(*[_ptr(y) for y in dys])
+        o_arr = (C.c_int64 * n)(*n_outs)
+        self.check(self.lib.sicu_gemv_batch(wtype, n, w_arr, o_arr, n_in, _ptr(dx), m, y_arr, _ptr(stream)))
 
     def gemv_host(self, wtype: int, dw, n_in: int, n_out: int, hx, hy, stream=None) -> None:
         self.check(self.lib.sicu_gemv_host(wtype, _ptr(dw), n_in, n_out, _ptr(hx), _ptr(hy), _ptr(stream)))

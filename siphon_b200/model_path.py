@@ -417,6 +417,37 @@ class MatrixPath:
             n += 1
         return n + 1
 
+    def batch_step(self, stream, m: int) -> int:
+        """One decode step of m <= 8 sequences (one token each): every weight
+        product once for all m activation rows (sicu_gemv_batch; products that
+        share an activation and type in one launch), row-split partials
+        all-reduced through NCCL. Returns the number of library calls."""
+        s, h, y = self.s, stream.cuda_stream, self.y
+        d = self.sh.n_embd
+        nq, nkv, nff = self.shapes["q"][0], self.shapes["k"][0], self.shapes["gate"][0]
+        n = 0
+        for lay in self.layers:
+            (tq, wq), (tk, wk), (tv, wv) = lay["q"], lay["k"], lay["v"]
+            if tv == tq:
+                s.gemv_batch(tq, [wq, wk, wv], [nq, nkv, nkv], d, self.x_model, m, [y["q"], y["k"], y["v"]], stream=h)
+                n += 1
+            else:
+                s.gemv_batch(tq, [wq, wk], [nq, nkv], d, self.x_model, m, [y["q"], y["k"]], stream=h)
+                s.gemv_batch(tv, [wv], [nkv], d, self.x_model, m, [y["v"]], stream=h)
+                n += 2
+            to, wo = lay["o"]
+            s.gemv_batch(to, [wo], [d], nq, self.x_attn, m, [y["o"]], stream=h)
+            self._allreduce(y["o"][:m])
+            (tg, wg), (_, wu) = lay["gate"], lay["up"]
+            s.gemv_batch(tg, [wg, wu], [nff, nff], d, self.x_model, m, [y["gate"], y["up"]], stream=h)
+            td, wd = lay["down"]
+            s.gemv_batch(td, [wd], [d], nff, self.x_ff, m, [y["down"]], stream=h)
+            self._allreduce(y["down"][:m])
+            n += 3
+        th, wh = self.head
+        s.gemv_batch(th, [wh], [self.shapes["head"][0]], d, self.x_model, m, [y["head"]], stream=h)
+        return n + 1
+
     def prefill(self, stream, m: int) -> None:
         """Launch the products of an m-token prompt on `stream` (or, with m
         up to the batch size, one decode step of a batch of m sequences:

@@ -11,7 +11,9 @@ reference's loader reads (src/model.c:26-172).
 
 ``blocks="random"`` writes uniformly random block bytes instead (every f16
 scale U[1e-4, 1e-2], every other bit uniform), for models whose values do not
-matter (timing runs): far faster to make for the 8B and 32B shapes.
+matter (timing runs): far faster to make for the 8B and 32B shapes. A
+function ``blocks(wtype, n_out, n_in, key) -> uint8 array`` supplies the
+blocks of each matrix itself (e.g. generated on a GPU).
 """
 
 from __future__ import annotations
@@ -127,7 +129,7 @@ def _vector(name: str, n: int, seed: int) -> np.ndarray:
     return v.astype(np.float32)
 
 
-def write_llama(path: str | Path, sh: LlamaShape, seed: int = 0, blocks: str = "quantized") -> Path:
+def write_llama(path: str | Path, sh: LlamaShape, seed: int = 0, blocks="quantized") -> Path:
     a = sh.arch
     kvs = [
         ("general.architecture", gguf.STRING, a),
@@ -144,7 +146,9 @@ def write_llama(path: str | Path, sh: LlamaShape, seed: int = 0, blocks: str = "
     tensors = []
     for name, wt, n_out, n_in in matrices(sh):
         key = [seed, zlib.crc32(name.encode())]
-        if blocks == "random":
+        if callable(blocks):
+            fn = (lambda wt=wt, n_out=n_out, n_in=n_in, key=key: blocks(wt, n_out, n_in, key))
+        elif blocks == "random":
             fn = (lambda wt=wt, n_out=n_out, n_in=n_in, key=key:
                   synth.weights(wt, n_out, n_in, seed=key))
         elif blocks == "quantized":

@@ -82,7 +82,7 @@ def test_zero_activation_blocks(sicu, oracle, wt):
 @pytest.mark.parametrize("shape", [(4096, 4096), (14336, 4096), (4096, 14336), (5632, 2048)], ids=str)
 @pytest.mark.parametrize("wt", Q.WEIGHT_TYPES, ids=lambda t: Q.NAMES[t])
 def test_baseline_sizes(sicu, oracle, wt, shape):
-    """BASELINE.json configs[0] and configs[1] shapes, bit-exact at full size."""
+    """The single-matvec shape 5632x2048 and the sweep shapes, bit-exact at full size."""
     n_out, n_in = shape
     w = synth.weights(wt, n_out, n_in, seed=wt)
     x = synth.activations(n_in, 1, seed=100 + wt)

@@ -27,9 +27,12 @@
 //     the MMA's fragment order once per call by a small prep kernel, which
 //     also quantizes f32 rows with the reference's quantizer;
 //   * each warp turns its accumulators into the reference's float terms
-//     (d * aux32[l], -(dmin * sumi)) in shared memory; then one thread per
-//     (row, token) adds the round's terms to its nine float chains in
-//     super-block order with __fadd_rn, exactly the reference's sequence.
+//     (d * aux32[l], -(dmin * sumi)) in shared memory (double buffered);
+//     after one CTA barrier per round, one thread per (row, token) adds the
+//     round's terms to its nine float chains in super-block order with
+//     __fadd_rn, exactly the reference's sequence. The barrier sits where the
+//     threads have no global loads in flight (a barrier waits for them): the
+//     next round's activation loads are issued after it.
 //
 // Weights stream through a ring of shared-memory stages (16 rows x four
 // super-blocks) filled by 1-D bulk copies, one per row (rows that do not
@@ -105,8 +108,8 @@ __global__ void __launch_bounds__(256) batch_prep_kernel(const float *xf, const 
 constexpr int BATCH_MATS = 16;
 constexpr int BW = 4;                   // warps per CTA = super-blocks per round
 constexpr int NPAIR = 16 * BATCH_MAX;   // (row, token) pairs of a tile
-// float terms of one round: lane terms [buffer 2][warp][pair 128][8], then the
-// dmin terms [buffer 2][warp][pair 128]
+// float terms of a round, double buffered: lane terms [buffer 2][warp][pair 128][8],
+// then the dmin terms [buffer 2][warp][pair 128]
 constexpr int TERMS_LANE_FLOATS = 2 * BW * NPAIR * 8;
 constexpr int TERMS_BYTES = 2 * BW * NPAIR * 9 * 4;
 
@@ -349,11 +352,11 @@ __device__ __forceinline__ void batch_superblock(const uint8_t *b0, const uint8_
 template <uint32_t T>
 __global__ void __launch_bounds__(BW * 32, 3) gemv_batch_kernel(const __grid_constant__ BatchParams p) {
     constexpr int UB = BFmt<T>::ub;
-    constexpr int NCH = (T == T_Q4_K) ? 9 : 8;   // float chains per (row, token)
+    constexpr bool Q4 = T == T_Q4_K;
     extern __shared__ __align__(128) uint8_t smem[];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
     const int S = p.nstages, R = p.rounds;
-    uint64_t *full = reinterpret_cast<uint64_t *>(smem);
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem);   // [S <= 8]
     float *terms = reinterpret_cast<float *>(smem + 128);
     uint8_t *ring = smem + 128 + TERMS_BYTES;
     const int stage_bytes = 16 * p.rs;
@@ -368,16 +371,16 @@ __global__ void __launch_bounds__(BW * 32, 3) gemv_batch_kernel(const __grid_con
     const uint64_t policy = policy_evict_first();
     uint32_t tailmask = 0;
 
-    auto tile_geom = [&](int q, int &mat, int &row0) {
-        const int tile = (int)blockIdx.x + (q / R) * (int)gridDim.x;
+    auto tile_geom = [&](int tile, int &mat, int &row0) {
         mat = 0;
         while (mat + 1 < p.nmat && tile >= p.tile0[mat + 1]) ++mat;
         row0 = (tile - p.tile0[mat]) * 16;
     };
     // round q into stage s: lane r < 16 of warp 0 copies row r's super-blocks of the round
     auto produce = [&](int q, int s) {
+        if (lane >= 16) return;
         int mat, row0;
-        tile_geom(q, mat, row0);
+        tile_geom((int)blockIdx.x + (q / R) * (int)gridDim.x, mat, row0);
         const int u0 = (q % R) * BW, cnt = min(BW, p.nb - u0);
         const int row = row0 + lane;
         const uint32_t bar = smem_addr(&full[s]);
@@ -407,7 +410,7 @@ __global__ void __launch_bounds__(BW * 32, 3) gemv_batch_kernel(const __grid_con
         if (bulk > 0) bulk_g2s_hint(smem_addr(dst), al, (uint32_t)bulk, bar, policy);
     };
 
-    if (warp == 0 && lane < 16)
+    if (warp == 0)
         for (int q = 0; q < Q && q < S; ++q) produce(q, q);   // weights never depend on earlier kernels
     grid_dep_wait();                                          // the activation records do
 
@@ -424,65 +427,71 @@ __global__ void __launch_bounds__(BW * 32, 3) gemv_batch_kernel(const __grid_con
     };
     if (Q > 0 && warp < p.nb) load_rec(warp);
 
-    // chain thread: pair (row tid / 8, token tid % 8)
+    // chain thread: pair tid = (row tid / 8, token tid % 8), its nine chains
     float ch[9];
-    int mat = 0, row0 = 0;
+    int mat = 0, row0 = 0, tile = (int)blockIdx.x;
+    int r = 0, s = 0;
+    uint32_t sphase = 0;
+    bool failed = false;
     for (int q = 0; q < Q; ++q) {
-        const int s = q % S, r = q % R, buf = q & 1;
-        const bool landed = mbar_wait(smem_addr(&full[s]), (uint32_t)((q / S) & 1));
-        if (!__syncthreads_and(landed)) {
-            if (tid == 0) atomicOr(p.status, STATUS_WAIT_TIMEOUT);
-            // let the copies still in flight land before the CTA's memory goes away
-            for (int k = q; k < Q && k < q + S; ++k)
-                (void)mbar_wait(smem_addr(&full[k % S]), (uint32_t)((k / S) & 1), 100000000ull);
-            return;
-        }
+        const int buf = q & 1;
         if (r == 0) {
-            tile_geom(q, mat, row0);
+            tile_geom(tile, mat, row0);
 #pragma unroll
             for (int c = 0; c < 9; ++c) ch[c] = 0.0f;
         }
         const int u0 = r * BW, cnt = min(BW, p.nb - u0);
         if (warp < cnt) {
-            uint4 fc[8];
+            const bool ok = mbar_wait(smem_addr(&full[s]), sphase);
+            if (__all_sync(0xffffffffu, ok)) {
+                uint4 fc[8];
 #pragma unroll
-            for (int k = 0; k < 8; ++k) fc[k] = fr[k];
-            const float ydc0 = yd[0], ydc1 = yd[1];
-            const uint8_t *stage = ring + (size_t)s * stage_bytes;
-            const uint8_t *w0 = p.w[mat] + (int64_t)(row0 + g) * p.row_bytes + (int64_t)u0 * UB;
-            const uint8_t *w1 = w0 + 8 * p.row_bytes;
-            const uint8_t *b0 = stage + (size_t)g * p.rs + (reinterpret_cast<uintptr_t>(w0) & 15) + warp * UB;
-            const uint8_t *b1 = stage + (size_t)(g + 8) * p.rs + (reinterpret_cast<uintptr_t>(w1) & 15) + warp * UB;
-            float acc[8][4], accm[4], xd[2], xm[2];
-            batch_superblock<T>(b0, b1, fc, t, acc, accm, xd, xm);
-            // the reference's float terms of this super-block (src/kernels.c:405-407)
-            float *tl = terms + (size_t)(buf * BW + warp) * NPAIR * 8;
-            float *tm = terms + TERMS_LANE_FLOATS + (size_t)(buf * BW + warp) * NPAIR;
+                for (int k = 0; k < 8; ++k) fc[k] = fr[k];
+                const float ydc0 = yd[0], ydc1 = yd[1];
+                const uint8_t *stage = ring + (size_t)s * stage_bytes;
+                const uint8_t *w0 = p.w[mat] + (int64_t)(row0 + g) * p.row_bytes + (int64_t)u0 * UB;
+                const uint8_t *w1 = w0 + 8 * p.row_bytes;
+                const uint8_t *b0 = stage + (size_t)g * p.rs + (reinterpret_cast<uintptr_t>(w0) & 15) + warp * UB;
+                const uint8_t *b1 = stage + (size_t)(g + 8) * p.rs + (reinterpret_cast<uintptr_t>(w1) & 15) + warp * UB;
+                float acc[8][4], accm[4], xd[2], xm[2];
+                batch_superblock<T>(b0, b1, fc, t, acc, accm, xd, xm);
+                // the reference's float terms of this super-block (src/kernels.c:405-407)
+                float *tl = terms + (size_t)(buf * BW + warp) * NPAIR * 8;
+                float *tm = terms + TERMS_LANE_FLOATS + (size_t)(buf * BW + warp) * NPAIR;
 #pragma unroll
-            for (int rr = 0; rr < 2; ++rr) {
+                for (int rr = 0; rr < 2; ++rr) {
 #pragma unroll
-                for (int n = 0; n < 2; ++n) {
-                    const int q4 = 2 * rr + n, pi = (g + 8 * rr) * BATCH_MAX + 2 * t + n;
-                    const float ydn = n ? ydc1 : ydc0;
-                    const float d = __fmul_rn(xd[rr], ydn);
-                    float4 *dst = reinterpret_cast<float4 *>(tl + pi * 8);
-                    dst[0] = make_float4(__fmul_rn(d, acc[0][q4]), __fmul_rn(d, acc[1][q4]), __fmul_rn(d, acc[2][q4]),
-                                         __fmul_rn(d, acc[3][q4]));
-                    dst[1] = make_float4(__fmul_rn(d, acc[4][q4]), __fmul_rn(d, acc[5][q4]), __fmul_rn(d, acc[6][q4]),
-                                         __fmul_rn(d, acc[7][q4]));
-                    // sumf -= dmin * sumi, stored negated: a - b == a + (-b) in IEEE arithmetic
-                    if constexpr (T == T_Q4_K) tm[pi] = -__fmul_rn(__fmul_rn(xm[rr], ydn), accm[q4]);
+                    for (int n = 0; n < 2; ++n) {
+                        const int q4 = 2 * rr + n, pi = (g + 8 * rr) * BATCH_MAX + 2 * t + n;
+                        const float ydn = n ? ydc1 : ydc0;
+                        const float d = __fmul_rn(xd[rr], ydn);
+                        float4 *dst = reinterpret_cast<float4 *>(tl + pi * 8);
+                        dst[0] = make_float4(__fmul_rn(d, acc[0][q4]), __fmul_rn(d, acc[1][q4]),
+                                             __fmul_rn(d, acc[2][q4]), __fmul_rn(d, acc[3][q4]));
+                        dst[1] = make_float4(__fmul_rn(d, acc[4][q4]), __fmul_rn(d, acc[5][q4]),
+                                             __fmul_rn(d, acc[6][q4]), __fmul_rn(d, acc[7][q4]));
+                        // sumf -= dmin * sumi, stored negated: a - b == a + (-b) in IEEE arithmetic
+                        if (Q4) tm[pi] = -__fmul_rn(__fmul_rn(xm[rr], ydn), accm[q4]);
+                    }
                 }
+            } else {
+                failed = true;
             }
         }
-        // the next round's fragments, loading while the chains run
-        if (q + 1 < Q) {
-            const int un = ((q + 1) % R) * BW + warp;
-            if (un < p.nb) load_rec(un);
+        // terms written and the stage consumed by every warp. No load of this
+        // thread is in flight here (a barrier waits for them), so the next
+        // round's loads are issued after it.
+        if (__syncthreads_or(failed)) {
+            failed = true;
+            break;
         }
-        __syncthreads();   // terms written; stage s consumed by every warp
-        if (warp == 0 && lane < 16 && q + S < Q) produce(q + S, s);
-        // chains: super-blocks of the round in order
+        {
+            const int rn = r + 1 == R ? 0 : r + 1;
+            const int un = rn * BW + warp;
+            if (q + 1 < Q && un < p.nb) load_rec(un);
+        }
+        if (warp == 0 && q + S < Q) produce(q + S, s);
+        // chains: the round's super-blocks in order
         for (int w = 0; w < cnt; ++w) {
             const float4 *tl = reinterpret_cast<const float4 *>(terms + ((size_t)(buf * BW + w) * NPAIR + tid) * 8);
             const float4 v0 = tl[0], v1 = tl[1];
@@ -490,16 +499,30 @@ __global__ void __launch_bounds__(BW * 32, 3) gemv_batch_kernel(const __grid_con
             ch[2] = __fadd_rn(ch[2], v0.z); ch[3] = __fadd_rn(ch[3], v0.w);
             ch[4] = __fadd_rn(ch[4], v1.x); ch[5] = __fadd_rn(ch[5], v1.y);
             ch[6] = __fadd_rn(ch[6], v1.z); ch[7] = __fadd_rn(ch[7], v1.w);
-            if constexpr (NCH == 9)
-                ch[8] = __fadd_rn(ch[8], terms[TERMS_LANE_FLOATS + (size_t)(buf * BW + w) * NPAIR + tid]);
+            if (Q4) ch[8] = __fadd_rn(ch[8], terms[TERMS_LANE_FLOATS + (size_t)(buf * BW + w) * NPAIR + tid]);
         }
         if (r == R - 1) {
             // sumf (the dmin chain; Q6_K: 0) + sums[0..7] (src/kernels.c:408, 521)
-            float out = (T == T_Q4_K) ? ch[8] : 0.0f;
+            float out = Q4 ? ch[8] : 0.0f;
 #pragma unroll
             for (int l = 0; l < 8; ++l) out = __fadd_rn(out, ch[l]);
             const int row = row0 + (tid >> 3), tok = tid & 7;
             if (row < p.n_out[mat] && tok < p.m) p.y[mat][(size_t)tok * p.n_out[mat] + row] = out;
+        }
+        if (++s == S) {
+            s = 0;
+            sphase ^= 1u;
+        }
+        if (++r == R) {
+            r = 0;
+            tile += (int)gridDim.x;
+        }
+    }
+    if (failed) {
+        if (tid == 0) atomicOr(p.status, STATUS_WAIT_TIMEOUT);
+        // let copies still in flight land before the CTA's memory goes away
+        const uint64_t t0 = globaltimer_ns();
+        while (globaltimer_ns() - t0 < 2000000ull) {
         }
     }
 }
@@ -541,14 +564,14 @@ static int launch_batch_t(const BatchLaunch &L, cudaStream_t st) {
         while (((rs >> 4) & 7) < 2 || ((rs >> 4) & 7) > 6) rs += 16;
     p.rs = rs;
     const int stage = 16 * rs;
-    // three CTAs per SM with at least three stages each, else two; at most six
+    // three CTAs per SM with at least three stages each, else two; at most eight
     int per_sm = 3, stages = 0;
     for (; per_sm >= 2; --per_sm) {
         const int budget = L.smem_per_sm / per_sm - L.smem_reserved - 128 - TERMS_BYTES;
         stages = budget / stage;
         if (stages >= 3) break;
     }
-    if (stages > 6) stages = 6;
+    if (stages > 8) stages = 8;
     if (stages < 2) return -1;
     p.nstages = stages;
     const int smem = 128 + TERMS_BYTES + stages * stage;

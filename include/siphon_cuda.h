@@ -320,6 +320,14 @@ typedef struct sicu_prologue {
 SICU_API int sicu_gemv_fused(uint32_t wtype, int n_mats, const void *const *dw, const int64_t *n_out,
                              int64_t n_in, const float *dx, const sicu_prologue *pro, const int32_t *epi,
                              float *const *dy, sicu_ar *group, void *stream);
+/* sicu_gemv_fused with a bias per matrix: bias (NULL, or a host array of
+ * n_mats device vectors of n_out[i] floats, NULL entries allowed) is added to
+ * matrix i's outputs, y + b in f32, before its epilogue: the Q, K and V biases
+ * of Qwen2-architecture models, which the reference adds after those products
+ * (src/engine.c:320-334). */
+SICU_API int sicu_gemv_fused_ex(uint32_t wtype, int n_mats, const void *const *dw, const int64_t *n_out,
+                                int64_t n_in, const float *dx, const sicu_prologue *pro, const int32_t *epi,
+                                const float *const *bias, float *const *dy, sicu_ar *group, void *stream);
 /* The steps on their own, m rows of n floats (16-byte aligned rows, n a
  * multiple of 4): dy = rmsnorm(dx + dres) * dw with dsum = dx + dres (dres and
  * dsum per row, each NULL allowed), and dy = silu(dx) * dup. For prompts

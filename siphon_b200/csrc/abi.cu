@@ -840,6 +840,12 @@ extern "C" {
 int sicu_gemv_fused(uint32_t wtype, int n_mats, const void *const *dw, const int64_t *n_out, int64_t n_in,
                     const float *dx, const sicu_prologue *pro, const int32_t *epi, float *const *dy, sicu_ar *group,
                     void *stream) {
+    return sicu_gemv_fused_ex(wtype, n_mats, dw, n_out, n_in, dx, pro, epi, nullptr, dy, group, stream);
+}
+
+int sicu_gemv_fused_ex(uint32_t wtype, int n_mats, const void *const *dw, const int64_t *n_out, int64_t n_in,
+                       const float *dx, const sicu_prologue *pro, const int32_t *epi, const float *const *bias,
+                       float *const *dy, sicu_ar *group, void *stream) {
     if (n_mats < 1 || n_mats > MAX_MATS) return fail(SICU_EINVAL, "matvec fused: %d matrices (1..%d)", n_mats, MAX_MATS);
     if (!dw || !n_out || !dy) return fail(SICU_EINVAL, "matvec fused: null array");
     uint32_t pair;
@@ -860,6 +866,12 @@ int sicu_gemv_fused(uint32_t wtype, int n_mats, const void *const *dw, const int
             if (epi[i] == SICU_EPI_SILU) silu_mask |= 1ull << i;
             else if (epi[i] != SICU_EPI_NONE) return fail(SICU_EINVAL, "matvec fused: unknown epilogue %d", (int)epi[i]);
         }
+    const float *bs[MAX_MATS] = {};
+    if (bias)
+        for (int i = 0; i < n_mats; ++i) {
+            bs[i] = bias[i];
+            if (bs[i] && !aligned(bs[i], 4)) return fail(SICU_EINVAL, "matvec fused: bias %d misaligned", i);
+        }
     DevState *ds;
     const cudaStream_t st = (cudaStream_t)stream;
     if (group) {
@@ -874,6 +886,7 @@ int sicu_gemv_fused(uint32_t wtype, int n_mats, const void *const *dw, const int
         L.ar = group->d;
         L.pro = pd;
         L.epi_silu = silu_mask;
+        L.bias[0] = bs[0];
         return run_gemv(wtype, L, st);
     }
     if (int rc = current(ds)) return rc;
@@ -899,6 +912,7 @@ int sicu_gemv_fused(uint32_t wtype, int n_mats, const void *const *dw, const int
             GemvLaunch L = make_launch(*ds, dw[i], n_in, n_out[i], dy[i]);
             L.xf = x;
             if (int rc = run_gemv(wtype, L, st)) return rc;
+            if (bs[i] && launch_add_inplace(dy[i], bs[i], n_out[i], st)) return cuda_fail(cudaGetLastError(), "bias launch");
             if (((silu_mask >> i) & 1) && launch_silu_inplace(dy[i], n_out[i], st))
                 return cuda_fail(cudaGetLastError(), "silu launch");
         }
@@ -913,6 +927,7 @@ int sicu_gemv_fused(uint32_t wtype, int n_mats, const void *const *dw, const int
         L.wm[i] = dw[i];
         L.ym[i] = dy[i];
         L.n_outm[i] = n_out[i];
+        L.bias[i] = bs[i];
     }
     return run_gemv(wtype, L, st);
 }

@@ -92,6 +92,15 @@ __device__ __forceinline__ float chain_add(float a, const float *src, int n) {
     return a;
 }
 
+// Output epilogue of the STEPS kernels: the bias add the reference runs after
+// the Q, K and V products (src/engine.c:320-334: y + b, one f32 rounding),
+// then silu for a gate product with the SwiGLU epilogue.
+__device__ __forceinline__ float epilogue(const GemvParams &p, int mat, int64_t row, float v) {
+    if (p.bias[mat]) v = __fadd_rn(v, p.bias[mat][row]);
+    if ((p.epi_silu >> mat) & 1) v = silu_call(v);
+    return v;
+}
+
 __device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
@@ -284,7 +293,7 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 2) gemv_kernel(const GemvPara
                 // row-split product: the partial goes to every rank; y gets
                 // the sum after the loop
                 if (AR && ar_st[1]) ar_send(p.ar, ar_st[0], g.x + lane, r);
-                else if (STEPS && ((p.epi_silu >> mat) & 1)) p.y[mat][g.x + lane] = silu_call(r);
+                else if (STEPS) p.y[mat][g.x + lane] = epilogue(p, mat, g.x + lane, r);
                 else p.y[mat][g.x + lane] = r;
             }
         }
@@ -301,7 +310,7 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 2) gemv_kernel(const GemvPara
                 const int64_t row = (int64_t)t * p.rows_per_task + lane;
                 if (lane < p.rows_per_task && row < p.n_out[0]) {
                     const float v = ar_sum(p.ar, e, row, p.status, live);
-                    p.y[0][row] = (STEPS && (p.epi_silu & 1)) ? silu_call(v) : v;
+                    p.y[0][row] = STEPS ? epilogue(p, 0, row, v) : v;
                 }
             }
         }
@@ -512,7 +521,7 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32, 2) gemv_flat_kernel(const Gem
                 } else {
                     r = fin[lane];
                 }
-                p.y[mat][row0 + r_first + lane] = (STEPS && ((p.epi_silu >> mat) & 1)) ? silu_call(r) : r;
+                p.y[mat][row0 + r_first + lane] = STEPS ? epilogue(p, mat, row0 + r_first + lane, r) : r;
             }
             __syncwarp();
             if (++s == S) { s = 0; parity ^= 1u; }
@@ -603,6 +612,11 @@ static int launch_gemv_t(const GemvLaunch &L, cudaStream_t st) {
     // reduction scratch
     p.pro = L.pro;
     p.epi_silu = L.epi_silu;
+    bool any_bias = false;
+    for (int i = 0; i < L.nmat; ++i) {
+        p.bias[i] = L.bias[i];
+        any_bias = any_bias || L.bias[i] != nullptr;
+    }
     const bool rms = L.pro.kind == PRO_RMS_NORM;
     p.act_bytes = (ActView::bytes(p.nu) + (ar || rms ? 16 : 0) + (rms ? RMS_SCRATCH : 0) + 127) & ~127;
     // two CTAs per SM when each warp keeps >= 2 ring slots, with 8 warps per
@@ -625,7 +639,7 @@ static int launch_gemv_t(const GemvLaunch &L, cudaStream_t st) {
     p.nslots = slots;
     p.warp_bytes = (hdr + slots * p.slot_bytes + 127) & ~127;
     const int smem = p.act_bytes + warps * p.warp_bytes;
-    const bool steps = L.pro.kind != PRO_NONE || L.epi_silu != 0;
+    const bool steps = L.pro.kind != PRO_NONE || L.epi_silu != 0 || any_bias;
     auto kern = ar ? (steps ? gemv_kernel<T, true, true> : gemv_kernel<T, true, false>)
                    : (steps ? gemv_kernel<T, false, true> : gemv_kernel<T, false, false>);
     if constexpr (F::kind != 3) {

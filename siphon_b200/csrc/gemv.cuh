@@ -62,6 +62,7 @@ struct GemvParams {
     ArDev ar;              // n > 0: one row-split matrix; y = the group's sum of the partial outputs
     ProDev pro;            // activation step the quantizer applies to xf first (STEPS kernels)
     uint64_t epi_silu;     // bit i: write silu(y) for matrix i (STEPS kernels)
+    const float *bias[GEMV_MAX_MATS];   // add bias[i][row] to matrix i's outputs (STEPS kernels; null: none)
 };
 
 // ---------------------------------------------------------------------------

@@ -78,6 +78,7 @@ struct GemvLaunch {
     ArDev ar;             // n > 0: row-split product, y = the group's sum of the partial outputs
     ProDev pro;           // step applied to xf before quantizing (quantized types)
     uint64_t epi_silu;    // bit i: matrix i's outputs are written as silu(y)
+    const float *bias[MAX_MATS];   // matrix i's outputs get bias[i][row] added (null: none)
 };
 
 // quantized formats (K and classic); fails with -3 for other types
@@ -142,6 +143,8 @@ int launch_swiglu(const float *x, const float *up, int64_t n, int64_t m, float *
 int launch_mul(const float *x, const float *up, int64_t n, float *y, cudaStream_t st);
 // y = silu(y), n floats in place (F16 products with a silu epilogue)
 int launch_silu_inplace(float *y, int64_t n, cudaStream_t st);
+// y += b, n floats in place (F16 products with a bias epilogue)
+int launch_add_inplace(float *y, const float *b, int64_t n, cudaStream_t st);
 
 // the reference's attention softmax over m rows of n floats (row maximum
 // taken here); in place allowed

@@ -34,6 +34,11 @@ __global__ void __launch_bounds__(256) glu_kernel(const float *x, const float *u
         reinterpret_cast<float4 *>(y)[i] = ld(i);
 }
 
+__global__ void __launch_bounds__(256) add_kernel(float *y, const float *b, int64_t n) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        y[i] = __fadd_rn(y[i], b[i]);
+}
+
 __global__ void __launch_bounds__(256) silu_kernel(float *y, int64_t n) {
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
         y[i] = silu_ref(y[i]);
@@ -66,6 +71,12 @@ int launch_swiglu(const float *x, const float *up, int64_t n, int64_t m, float *
 
 int launch_mul(const float *x, const float *up, int64_t n, float *y, cudaStream_t st) {
     return launch_glu(x, up, n, true, y, st);
+}
+
+int launch_add_inplace(float *y, const float *b, int64_t n, cudaStream_t st) {
+    if (n <= 0) return 0;
+    add_kernel<<<grid_for(n), 256, 0, st>>>(y, b, n);
+    return cudaPeekAtLastError() == cudaSuccess ? 0 : -2;
 }
 
 int launch_silu_inplace(float *y, int64_t n, cudaStream_t st) {

@@ -151,43 +151,6 @@ __global__ void __launch_bounds__(256) softmax_kernel(const float *x, float *y, 
     softmax_row(x + off, y + off, n);
 }
 
-// The reference's f16 dot on the scalar path (si_dot_f16, src/kernels.c:
-// 189-195): exact f32 products of the f16 values added into a double in index
-// order, rounded to f32 at the end. stride_x: element spacing in x.
-__device__ __forceinline__ float dot_f16_seq(const uint16_t *x, int64_t stride_x, const uint16_t *y, int n) {
-    double s = 0.0;
-    for (int i = 0; i < n; ++i) s = __dadd_rn(s, (double)__fmul_rn(h2f(x[(int64_t)i * stride_x]), h2f(y[i])));
-    return __double2float_rn(s);
-}
-
-// One query head per CTA (src/engine.c:90-147, attn_head, on the scalar dot
-// path): q as f16, a score per cached position 0..pos against the head's K
-// rows, times kq_scale, the row's softmax, the probabilities as f16, and per
-// channel the f16 dot of the head's transposed V row with them. Dynamic
-// shared memory: n_score floats (scores, then probabilities) and n_score
-// halves.
-__global__ void __launch_bounds__(256) attention_kernel(const float *q, const uint16_t *kc, const uint16_t *vc,
-                                                        int n_head, int gqa, int hd, int n_ctx, int n_score,
-                                                        float ks, float *out) {
-    extern __shared__ __align__(16) uint8_t sm[];
-    float *sc = reinterpret_cast<float *>(sm);
-    uint16_t *p16 = reinterpret_cast<uint16_t *>(sc + n_score);
-    __shared__ uint16_t q16[1024];
-    const int h = blockIdx.x, hk = h / gqa;
-    for (int d = threadIdx.x; d < hd; d += blockDim.x) q16[d] = (uint16_t)f2h(q[(int64_t)h * hd + d]);
-    __syncthreads();
-    const uint16_t *kh = kc + (int64_t)hk * n_ctx * hd;
-    const uint16_t *vh = vc + (int64_t)hk * hd * n_ctx;
-    for (int j = threadIdx.x; j < n_score; j += blockDim.x)
-        sc[j] = __fmul_rn(dot_f16_seq(kh + (int64_t)j * hd, 1, q16, hd), ks);
-    __syncthreads();
-    softmax_row(sc, sc, n_score);
-    for (int j = threadIdx.x; j < n_score; j += blockDim.x) p16[j] = (uint16_t)f2h(sc[j]);
-    __syncthreads();
-    for (int c = threadIdx.x; c < hd; c += blockDim.x)
-        out[(int64_t)h * hd + c] = dot_f16_seq(vh + (int64_t)c * n_ctx, 1, p16, n_score);
-}
-
 // Eight f16 values x[0..7]: one 16-byte load when vec (x 16-byte aligned),
 // else eight 2-byte loads; the same bits either way. Lanes of a warp read
 // rows a whole row apart, so the wide load cuts the cache wavefronts of a
@@ -225,13 +188,264 @@ __device__ __forceinline__ float dot_f16_seq8(const uint16_t *x, const uint16_t 
     return __double2float_rn(s);
 }
 
+
+// ---- exactly parallel f16 dots ------------------------------------------------
+// The reference adds the exact f32 products of two f16 vectors into a double
+// in index order. Each product of f16 values a, b is a multiple of
+// 2^(qa + qb), q the weight of a value's last mantissa bit (2^-24 for the
+// smallest), so every partial sum is a multiple of 2^(qmin_a + qmin_b); a
+// double holds every such multiple below 2^(53 + qmin_a + qmin_b) exactly.
+// When sum |a_i b_i| <= max|a| * sum|b| stays below that, no addition rounds
+// in any order, and a parallel sum gives the sequential sum's bits. The
+// kernels below sum in parallel, check that bound for the head afterwards
+// (max|a| over everything they read, sum|b| and qmin_b of the fixed vector)
+// and redo the head sequentially when it fails.
+
+// weight of the last mantissa bit of a finite nonzero f16, as a power of 2
+__device__ __forceinline__ int h_quantum(uint32_t b) {
+    const int e = (int)((b >> 10) & 31u);
+    return e ? e - 25 : -24;
+}
+
+// CTA-wide reductions through shared memory (every thread calls)
+__device__ __forceinline__ uint32_t cta_max_u32(uint32_t v, uint32_t *scratch) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = max(v, __shfl_xor_sync(0xffffffffu, v, o));
+    if (threadIdx.x == 0) *scratch = 0u;
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) atomicMax(scratch, v);
+    __syncthreads();
+    const uint32_t r = *scratch;
+    __syncthreads();
+    return r;
+}
+
+// sum |x_i| (exact in double for f16 values) and the smallest last-bit
+// weight among the nonzero ones (+1000 when all are zero) of n f16 values
+__device__ __forceinline__ void h_abs_sum_qmin(const uint16_t *x, int n, double *sum_out, int *qmin_out,
+                                               double *dscratch, int *iscratch) {
+    double s = 0.0;
+    int qm = 1000;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const uint32_t b = x[i] & 0x7fffu;
+        s += (double)h2f(b);
+        if (b) qm = min(qm, h_quantum(b));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        s += __shfl_xor_sync(0xffffffffu, s, o);
+        qm = min(qm, __shfl_xor_sync(0xffffffffu, qm, o));
+    }
+    if (threadIdx.x == 0) {
+        *dscratch = 0.0;
+        *iscratch = 1000;
+    }
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) {
+        atomicAdd(dscratch, s);
+        atomicMin(iscratch, qm);
+    }
+    __syncthreads();
+    *sum_out = *dscratch;
+    *qmin_out = *iscratch;
+    __syncthreads();
+}
+
+// true when max|a| (as f16 bits) times sum|b| stays below 2^(29 + qmin_b):
+// the parallel sums are exact (qmin_a >= -24)
+__device__ __forceinline__ bool dots_exact(uint32_t amax_bits, double bsum, int bqmin) {
+    if (amax_bits >= 0x7c00u || !(bsum < 1e300)) return false;
+    if (bqmin >= 1000) return true;   // b all zero: every product is 0
+    return __dmul_ru((double)h2f(amax_bits), bsum) < ldexp(1.0, 29 + bqmin);
+}
+
+// 64 f16 values x[0..63] into eight 16-byte registers (x 16-byte aligned):
+// the eight loads are all in flight before any is used
+__device__ __forceinline__ void ld_h64(const uint16_t *x, uint4 r[8]) {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) r[k] = reinterpret_cast<const uint4 *>(x)[k];
+}
+__device__ __forceinline__ uint32_t h_of(const uint4 r[8], int i) {
+    const uint4 v = r[i >> 3];
+    const uint32_t w = ((i >> 1) & 3) == 0 ? v.x : ((i >> 1) & 3) == 1 ? v.y : ((i >> 1) & 3) == 2 ? v.z : v.w;
+    return (i & 1) ? (w >> 16) : (w & 0xffffu);
+}
+
+// Scores of positions 0..n_score-1 (row j of K at kh + j * hd; the row of
+// position `own` from krow_own when not null), times ks, into sc; q16 the
+// head's query as f16 in shared memory. Parallel sums (four accumulators per
+// dot), sequential when the exactness bound fails. A thread takes two
+// positions at a time and has all loads of a 64-element chunk of both rows in
+// flight before it uses them.
+__device__ void head_scores(const uint16_t *kh, const uint16_t *krow_own, int own, const uint16_t *q16, int hd,
+                            int n_score, float ks, float *sc, double *dscratch, int *iscratch, uint32_t *uscratch) {
+    double qsum;
+    int qqmin;
+    h_abs_sum_qmin(q16, hd, &qsum, &qqmin, dscratch, iscratch);
+    uint32_t kmax = 0;
+    const int nt = blockDim.x;
+    const bool vec = (reinterpret_cast<uintptr_t>(kh) & 15) == 0 && (hd & 63) == 0 &&
+                     (!krow_own || (reinterpret_cast<uintptr_t>(krow_own) & 15) == 0);
+    for (int j = threadIdx.x; j < n_score; j += 2 * nt) {
+        const int j2 = j + nt;
+        const bool two = j2 < n_score;
+        const uint16_t *ra = (krow_own && j == own) ? krow_own : kh + (int64_t)j * hd;
+        const uint16_t *rb = two ? ((krow_own && j2 == own) ? krow_own : kh + (int64_t)j2 * hd) : ra;
+        double a[4] = {0.0, 0.0, 0.0, 0.0}, b[4] = {0.0, 0.0, 0.0, 0.0};
+        if (vec) {
+            for (int d0 = 0; d0 < hd; d0 += 64) {
+                uint4 xa[8], xb[8];
+                ld_h64(ra + d0, xa);
+                if (two) ld_h64(rb + d0, xb);
+#pragma unroll
+                for (int i = 0; i < 64; ++i) {
+                    const float qv = h2f(q16[d0 + i]);
+                    const uint32_t ka = h_of(xa, i);
+                    kmax = max(kmax, ka & 0x7fffu);
+                    a[i & 3] = __dadd_rn(a[i & 3], (double)__fmul_rn(h2f(ka), qv));
+                    if (two) {
+                        const uint32_t kb = h_of(xb, i);
+                        kmax = max(kmax, kb & 0x7fffu);
+                        b[i & 3] = __dadd_rn(b[i & 3], (double)__fmul_rn(h2f(kb), qv));
+                    }
+                }
+            }
+        } else {
+            for (int d = 0; d < hd; ++d) {   // any order is exact under the bound checked below
+                const float qv = h2f(q16[d]);
+                kmax = max(kmax, (uint32_t)ra[d] & 0x7fffu);
+                a[0] = __dadd_rn(a[0], (double)__fmul_rn(h2f(ra[d]), qv));
+                if (two) {
+                    kmax = max(kmax, (uint32_t)rb[d] & 0x7fffu);
+                    b[0] = __dadd_rn(b[0], (double)__fmul_rn(h2f(rb[d]), qv));
+                }
+            }
+        }
+        sc[j] = __fmul_rn(__double2float_rn(__dadd_rn(__dadd_rn(a[0], a[1]), __dadd_rn(a[2], a[3]))), ks);
+        if (two) sc[j2] = __fmul_rn(__double2float_rn(__dadd_rn(__dadd_rn(b[0], b[1]), __dadd_rn(b[2], b[3]))), ks);
+    }
+    kmax = cta_max_u32(kmax, uscratch);
+    if (!dots_exact(kmax, qsum, qqmin)) {
+        for (int j = threadIdx.x; j < n_score; j += blockDim.x) {
+            const uint16_t *row = (krow_own && j == own) ? krow_own : kh + (int64_t)j * hd;
+            sc[j] = __fmul_rn(dot_f16_seq8(row, q16, hd), ks);
+        }
+    }
+    __syncthreads();
+}
+
+// out[c] = the f16 dot of V row c (vh + c * n_ctx, positions 0..n_score-1;
+// the value of position `own` from v_own[c] when v_own is not null) with the
+// probabilities p16, for c < hd. Threads split each row's positions into
+// blockDim / hd segments summed in parallel (two accumulators each),
+// sequential when the exactness bound fails. part: blockDim doubles.
+__device__ void head_values(const uint16_t *vh, int64_t n_ctx, const uint16_t *v_own, int own, const uint16_t *p16,
+                            int hd, int n_score, float *out, double *part, double *dscratch, int *iscratch,
+                            uint32_t *uscratch) {
+    double psum;
+    int pqmin;
+    h_abs_sum_qmin(p16, n_score, &psum, &pqmin, dscratch, iscratch);
+    const int segs = hd <= (int)blockDim.x ? (int)blockDim.x / hd : 1;
+    const int len = ((n_score + segs - 1) / segs + 7) & ~7;
+    uint32_t vmax = 0;
+    for (int task = threadIdx.x; task < hd * segs; task += blockDim.x) {
+        const int c = task % hd, sg = task / hd;
+        const uint16_t *row = vh + (int64_t)c * n_ctx;
+        const bool vec = (reinterpret_cast<uintptr_t>(row) & 15) == 0;
+        const int j0 = sg * len, j1 = min(n_score, j0 + len);
+        double a[2] = {0.0, 0.0};
+        int j = j0;
+        if (vec) {
+            // 64 positions at a time, every load in flight before use
+            for (; j + 64 <= j1; j += 64) {
+                uint4 x[8];
+                ld_h64(row + j, x);
+#pragma unroll
+                for (int k = 0; k < 64; ++k) {
+                    const uint32_t xv = (v_own && j + k == own) ? (uint32_t)v_own[c] : h_of(x, k);
+                    vmax = max(vmax, xv & 0x7fffu);
+                    a[k & 1] = __dadd_rn(a[k & 1], (double)__fmul_rn(h2f(xv), h2f(p16[j + k])));
+                }
+            }
+        }
+        for (; j + 8 <= j1; j += 8) {
+            uint16_t x[8];
+            if (v_own && own >= j && own < j + 8) {
+#pragma unroll
+                for (int k = 0; k < 8; ++k) x[k] = (j + k == own) ? v_own[c] : row[j + k];
+            } else {
+                ld_h8(row + j, vec, x);
+            }
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                vmax = max(vmax, (uint32_t)x[k] & 0x7fffu);
+                a[k & 1] = __dadd_rn(a[k & 1], (double)__fmul_rn(h2f(x[k]), h2f(p16[j + k])));
+            }
+        }
+        for (; j < j1; ++j) {
+            const uint16_t x = (v_own && j == own) ? v_own[c] : row[j];
+            vmax = max(vmax, (uint32_t)x & 0x7fffu);
+            a[0] = __dadd_rn(a[0], (double)__fmul_rn(h2f(x), h2f(p16[j])));
+        }
+        part[task] = __dadd_rn(a[0], a[1]);
+    }
+    vmax = cta_max_u32(vmax, uscratch);   // also orders the partials before their use
+    if (dots_exact(vmax, psum, pqmin)) {
+        for (int c = threadIdx.x; c < hd; c += blockDim.x) {
+            double sum = part[c];
+            for (int sg = 1; sg < segs; ++sg) sum = __dadd_rn(sum, part[sg * hd + c]);
+            out[c] = __double2float_rn(sum);
+        }
+    } else {
+        for (int c = threadIdx.x; c < hd; c += blockDim.x) {
+            const uint16_t *row = vh + (int64_t)c * n_ctx;
+            double sum = 0.0;
+            for (int j = 0; j < n_score; ++j) {
+                const uint16_t x = (v_own && j == own) ? v_own[c] : row[j];
+                sum = __dadd_rn(sum, (double)__fmul_rn(h2f(x), h2f(p16[j])));
+            }
+            out[c] = __double2float_rn(sum);
+        }
+    }
+}
+
+// One query head per CTA (src/engine.c:90-147, attn_head, on the scalar dot
+// path): q as f16, a score per cached position 0..pos against the head's K
+// rows, times kq_scale, the row's softmax, the probabilities as f16, and per
+// channel the f16 dot of the head's transposed V row with them. Dynamic
+// shared memory: n_score floats (scores, then probabilities) and n_score
+// halves.
+__global__ void __launch_bounds__(256) attention_kernel(const float *q, const uint16_t *kc, const uint16_t *vc,
+                                                        int n_head, int gqa, int hd, int n_ctx, int n_score,
+                                                        float ks, float *out) {
+    extern __shared__ __align__(16) uint8_t sm[];
+    float *sc = reinterpret_cast<float *>(sm);
+    uint16_t *p16 = reinterpret_cast<uint16_t *>(sc + n_score);
+    __shared__ __align__(16) uint16_t q16[1024];
+    __shared__ double part[1024], dscr;
+    __shared__ int iscr;
+    __shared__ uint32_t uscr;
+    const int h = blockIdx.x, hk = h / gqa;
+    for (int d = threadIdx.x; d < hd; d += blockDim.x) q16[d] = (uint16_t)f2h(q[(int64_t)h * hd + d]);
+    __syncthreads();
+    const uint16_t *kh = kc + (int64_t)hk * n_ctx * hd;
+    const uint16_t *vh = vc + (int64_t)hk * hd * n_ctx;
+    head_scores(kh, nullptr, -1, q16, hd, n_score, ks, sc, &dscr, &iscr, &uscr);
+    softmax_row(sc, sc, n_score);
+    for (int j = threadIdx.x; j < n_score; j += blockDim.x) p16[j] = (uint16_t)f2h(sc[j]);
+    __syncthreads();
+    head_values(vh, n_ctx, nullptr, -1, p16, hd, n_score, out + (int64_t)h * hd, part, &dscr, &iscr, &uscr);
+}
+
 // The attention step of one layer and position in one launch, one CTA per
 // query head: the head's q and its KV head's k rotated (the rotation of
 // rope_kernel) in shared memory, this position's K and V stored into the
 // caches (by the first CTA of each KV group; the others only read earlier
 // positions), the scores of positions 0..pos (this position's from the f16 k
 // in shared memory, the same bits the cache holds), softmax, f16
-// probabilities and the value dots (this position's V from shared memory).
+// probabilities and the value dots (this position's V from shared memory);
+// scores and value dots summed in parallel where that is exact (head_scores,
+// head_values).
 // Same results as rope_kernel + kv_store_kernel + attention_kernel. Launched
 // after the producing matvec has finished (launched early behind it, the
 // decode step measured slower: 3.0 ms per TinyLlama-shape token against 1.86),
@@ -247,6 +461,9 @@ __global__ void __launch_bounds__(256) attention_step_kernel(const float *q, con
     uint16_t *p16 = reinterpret_cast<uint16_t *>(sc + n_score);
     __shared__ __align__(16) float qf[1024], kf[1024];
     __shared__ __align__(16) uint16_t q16[1024], k16[1024], v16[1024];
+    __shared__ double part[1024], dscr;
+    __shared__ int iscr;
+    __shared__ uint32_t uscr;
     const int h = blockIdx.x, hk = h / gqa, tid = threadIdx.x;
     asm volatile("griddepcontrol.wait;" ::: "memory");
     for (int d = tid; d < hd; d += blockDim.x) {
@@ -285,32 +502,13 @@ __global__ void __launch_bounds__(256) attention_step_kernel(const float *q, con
         }
     }
     __syncthreads();
-    for (int j = tid; j < n_score; j += blockDim.x) {
-        const uint16_t *row = j == pos ? k16 : kh + (int64_t)j * hd;
-        sc[j] = __fmul_rn(dot_f16_seq8(row, q16, hd), ks);
-    }
-    __syncthreads();
+    // scores and value dots: this position's k and v from shared memory (the
+    // same bits the cache holds), positions 0..pos-1 from the cache
+    head_scores(kh, k16, pos, q16, hd, n_score, ks, sc, &dscr, &iscr, &uscr);
     softmax_row(sc, sc, n_score);
     for (int j = tid; j < n_score; j += blockDim.x) p16[j] = (uint16_t)f2h(sc[j]);
     __syncthreads();
-    for (int c = tid; c < hd; c += blockDim.x) {
-        // positions 0..pos-1 from the cache, then this position's v
-        const uint16_t *row = vh + (int64_t)c * n_ctx;
-        const bool vec = (reinterpret_cast<uintptr_t>(row) & 15) == 0;
-        double s = 0.0;
-        int j = 0;
-        for (; j + 8 <= pos; j += 8) {
-            uint16_t a[8], b[8];
-            ld_h8(row + j, vec, a);
-#pragma unroll
-            for (int t = 0; t < 8; ++t) b[t] = p16[j + t];
-#pragma unroll
-            for (int t = 0; t < 8; ++t) s = __dadd_rn(s, (double)__fmul_rn(h2f(a[t]), h2f(b[t])));
-        }
-        for (; j < pos; ++j) s = __dadd_rn(s, (double)__fmul_rn(h2f(row[j]), h2f(p16[j])));
-        s = __dadd_rn(s, (double)__fmul_rn(h2f(v16[c]), h2f(p16[pos])));
-        out[(int64_t)h * hd + c] = __double2float_rn(s);
-    }
+    head_values(vh, n_ctx, v16, pos, p16, hd, n_score, out + (int64_t)h * hd, part, &dscr, &iscr, &uscr);
 }
 
 // RoPE in place on n_heads heads of hd floats (src/engine.c:42-75): pairs

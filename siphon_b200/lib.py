@@ -61,6 +61,8 @@ SIGNATURES = {
     "sicu_gemv_ar": [_u32, _vp, _i64, _i64, _fp, _fp, _vp, _vp],
     "sicu_gemv_fused": [_u32, C.c_int, C.POINTER(C.c_void_p), C.POINTER(C.c_int64), _i64, _fp, _vp, _vp,
                         C.POINTER(C.c_void_p), _vp, _vp],
+    "sicu_gemv_fused_ex": [_u32, C.c_int, C.POINTER(C.c_void_p), C.POINTER(C.c_int64), _i64, _fp, _vp, _vp,
+                           C.POINTER(C.c_void_p), C.POINTER(C.c_void_p), _vp, _vp],
     "sicu_rms_norm": [_fp, _fp, _fp, _fp, _i64, _i64, C.c_float, _fp, _vp],
     "sicu_swiglu": [_fp, _fp, _i64, _i64, _fp, _vp],
     "sicu_softmax": [_fp, _fp, _i64, _i64, _vp],
@@ -225,8 +227,8 @@ class SiphonCuda:
 
     # -- activation steps ------------------------------------------------------------
     def gemv_fused(self, wtype: int, dws, n_outs, n_in: int, dx, step: Prologue | None, dys,
-                   group: "ArGroup | None" = None, stream=None, epi=None) -> None:
-        """sicu_gemv_fused: dys[i] = epi[i](W_i (step applied to dx)),
+                   group: "ArGroup | None" = None, stream=None, epi=None, bias=None) -> None:
+        """sicu_gemv_fused: dys[i] = epi[i](W_i (step applied to dx) [+ bias[i]]),
         optionally all-reduced over group (one matrix)."""
         n = len(dws)
         w_arr = (C.c_void_p * n)(*[_ptr(w) for w in dws])
@@ -234,8 +236,14 @@ class SiphonCuda:
         o_arr = (C.c_int64 * n)(*n_outs)
         e_arr = (C.c_int32 * n)(*epi) if epi is not None else None
         pro = C.byref(step) if step is not None else None
-        self.check(self.lib.sicu_gemv_fused(wtype, n, w_arr, o_arr, n_in, _ptr(dx), pro, e_arr, y_arr,
-                                            group.handle if group is not None else None, _ptr(stream)))
+        grp = group.handle if group is not None else None
+        if bias is None:
+            self.check(self.lib.sicu_gemv_fused(wtype, n, w_arr, o_arr, n_in, _ptr(dx), pro, e_arr, y_arr, grp,
+                                                _ptr(stream)))
+        else:
+            b_arr = (C.c_void_p * n)(*[_ptr(b) for b in bias])
+            self.check(self.lib.sicu_gemv_fused_ex(wtype, n, w_arr, o_arr, n_in, _ptr(dx), pro, e_arr, b_arr, y_arr,
+                                                   grp, _ptr(stream)))
 
     def rms_norm(self, dx, dw, n: int, m: int, eps: float, dy, dres=None, dsum=None, stream=None) -> None:
         self.check(self.lib.sicu_rms_norm(_ptr(dx), _ptr(dres), _ptr(dsum), _ptr(dw), n, m, eps, _ptr(dy),

@@ -16,8 +16,9 @@ With ``steps=True`` the decode step also runs the activation steps between
 the products the way the reference's forward pass does (engine.c:313-315,
 367-379, 387-389), each fused into the product that reads its result
 (sicu_gemv_fused): the residual add and RMS norm before Wq/Wk/Wv, before
-W_gate/W_up and before the output head, and SwiGLU split into a silu
-epilogue on W_gate's output and a multiply in W_down's prologue. The
+W_gate/W_up and before the output head, SwiGLU split into a silu epilogue on
+W_gate's output and a multiply in W_down's prologue, and for Qwen2-shaped
+models the Q/K/V bias adds as the QKV products' epilogue (engine.c:320-334). The
 residual stream starts from a fixed embedding row. Attention and RoPE are not
 part of this path: Wo reads a fixed activation in place of the attention
 output. Without ``steps`` each product reads a fixed activation buffer of its
@@ -232,6 +233,17 @@ class MatrixPath:
                 self.ffn_norm = [norm_w() for _ in range(sh.n_layer)]
                 self.out_norm = norm_w()
             self.resid = [torch.empty(sh.n_embd, device=device) for _ in range(2)]
+            # Qwen2-architecture Q/K/V biases, added after those products
+            # (synthetic: 0.02 N(0, 1), this rank's heads)
+            self.bias = None
+            if sh.qkv_bias:
+                def bias_vec(il, name, n):
+                    if reader is not None:
+                        return vec(f"blk.{il}.attn_{name}.bias")
+                    return 0.02 * torch.randn(n, device=device, generator=gen)
+                nq_, nkv_ = self.shapes["q"][0], self.shapes["k"][0]
+                self.bias = [{"q": bias_vec(il, "q", nq_), "k": bias_vec(il, "k", nkv_), "v": bias_vec(il, "v", nkv_)}
+                             for il in range(sh.n_layer)]
         if self.attention:
             # f16 caches per layer in the engine's layout (K [kv][n_ctx][hd],
             # V [kv][hd][n_ctx]), zero; the RoPE tables of every position as
@@ -372,12 +384,16 @@ class MatrixPath:
             (tq, wq), (tk, wk), (tv, wv) = lay["q"], lay["k"], lay["v"]
             out = self.resid[nxt]
             step = rms_norm_step(self.attn_norm[il], eps, res, out)
+            b = self.bias[il] if self.bias is not None else None
             if tv == tq:
-                s.gemv_fused(tq, [wq, wk, wv], [nq, nkv, nkv], d, cur, step, [y["q"], y["k"], y["v"]], stream=h)
+                s.gemv_fused(tq, [wq, wk, wv], [nq, nkv, nkv], d, cur, step, [y["q"], y["k"], y["v"]], stream=h,
+                             bias=[b["q"], b["k"], b["v"]] if b else None)
                 n += 1
             else:
-                s.gemv_fused(tq, [wq, wk], [nq, nkv], d, cur, step, [y["q"], y["k"]], stream=h)
-                s.gemv_fused(tv, [wv], [nkv], d, out, rms_norm_step(self.attn_norm[il], eps), [y["v"]], stream=h)
+                s.gemv_fused(tq, [wq, wk], [nq, nkv], d, cur, step, [y["q"], y["k"]], stream=h,
+                             bias=[b["q"], b["k"]] if b else None)
+                s.gemv_fused(tv, [wv], [nkv], d, out, rms_norm_step(self.attn_norm[il], eps), [y["v"]], stream=h,
+                             bias=[b["v"]] if b else None)
                 n += 2
             cur, nxt = out, 1 - nxt
             xa = self.x_attn[0]

@@ -93,3 +93,29 @@ def test_attention_step_equals_separate_launches(sicu, oracle, neox):
         assert_bits_equal(host(o1), host(o2), f"pos {pos} output")
         assert (host(kc1) == host(kc2)).all() and (host(vc1) == host(vc2)).all(), f"pos {pos} caches"
         assert_bits_equal(host(qd), q, "q left unrotated")
+
+
+@pytest.mark.parametrize("case", ["parallel", "values_fallback", "scores_fallback", "both_fallback"])
+def test_attention_exactness_bound_and_fallback(sicu, oracle, case):
+    """The scores and value dots are summed in parallel when no addition can
+    round (max|a| * sum|b| below 2^(53 + the smallest last-bit weights)) and
+    sequentially otherwise; both give the reference's bits. Large V values
+    (|v| ~ 100 against subnormal probabilities) and a subnormal query
+    component with large K values push the bound over."""
+    import torch
+    rng = np.random.default_rng(31)
+    n_head, nkv, hd, n_ctx, pos = 4, 2, 64, 256, 200
+    k, v = random_cache(rng, nkv, hd, n_ctx)
+    q = (rng.standard_normal(n_head * hd) * 2).astype(np.float32)
+    if case in ("values_fallback", "both_fallback"):
+        v = (v.view(np.float16).astype(np.float32) * 150).astype(np.float16).view(np.uint16)
+    if case in ("scores_fallback", "both_fallback"):
+        k = (k.view(np.float16).astype(np.float32) * 200).astype(np.float16).view(np.uint16)
+        q[::hd] = 3e-7                                   # a subnormal f16 component in every head
+        q = q * np.float32(0.02)                          # keep the scores' softmax spread
+    kd = torch.from_numpy(k.view(np.int16).reshape(-1).copy()).cuda()
+    vd = torch.from_numpy(v.view(np.int16).reshape(-1).copy()).cuda()
+    ks = float(np.float32(1.0 / np.sqrt(hd)))
+    out = empty_f32(n_head * hd)
+    sicu.attention(dev(q), kd, vd, n_head, nkv, hd, n_ctx, pos, ks, out)
+    assert_bits_equal(host(out), oracle.attention(q, k, v, n_head, nkv, hd, n_ctx, pos, ks), case)

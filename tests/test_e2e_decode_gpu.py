@@ -58,6 +58,13 @@ def small(tmp_path_factory):
 
 
 @pytest.fixture(scope="module")
+def small_qwen(tmp_path_factory):
+    """A small Qwen2-architecture model: Q/K/V biases, half-split RoPE."""
+    path = synth_model.write_llama(tmp_path_factory.mktemp("m") / "qwen.gguf", synth_model.SMALL_QWEN, seed=9)
+    return path, synth_model.SMALL_QWEN, _reference_run(path, synth_model.SMALL_QWEN, 17)
+
+
+@pytest.fixture(scope="module")
 def tinyllama(tmp_path_factory):
     sh = synth_model.TINYLLAMA
     path = synth_model.write_llama(tmp_path_factory.mktemp("m") / "tinyllama.gguf", sh, seed=7)
@@ -108,6 +115,16 @@ def test_reference_engine_cuda_backend_small(sicu, small):
 
 def test_device_resident_loop_small(sicu, small):
     _device_resident_loop(sicu, small)
+
+
+def test_reference_engine_cuda_backend_qwen2(sicu, small_qwen):
+    _reference_engine_on_cuda(small_qwen)
+
+
+def test_device_resident_loop_qwen2(sicu, small_qwen):
+    """Qwen2 architecture: the Q/K/V bias adds ride in the QKV product's
+    epilogue, RoPE in the half-split form."""
+    _device_resident_loop(sicu, small_qwen)
 
 
 def test_reference_engine_cuda_backend_tinyllama(sicu, tinyllama):

@@ -102,7 +102,8 @@ def test_gemv_fused_rms_norm(sicu, oracle, golden_dir, wt):
     gam = _gamma(256, 41)
     for i, x in enumerate(r256):
         y = empty_f32(n_out)
-        sicu.gemv_fused(wt, [dev(w)], [n_out], 256, dev(x), rms_norm_step(dev(gam), EPS), [y])
+        dw_, dx_, dg_ = dev(w), dev(x), dev(gam)      # held until the launch has run
+        sicu.gemv_fused(wt, [dw_], [n_out], 256, dx_, rms_norm_step(dg_, EPS), [y])
         want = _want(oracle, wt, w, 256, n_out, oracle.rms_norm(x, gam, EPS)[1])
         assert_bits_equal(host(y), want, f"{Q.NAMES[wt]} fused norm, row {i}")
     n_in = 4096
@@ -126,7 +127,8 @@ def test_gemv_fused_swiglu(sicu, oracle, wt):
     gate = (rng.standard_normal(n_in) * 6).astype(np.float32)
     up = rng.standard_normal(n_in).astype(np.float32)
     y = empty_f32(n_out)
-    sicu.gemv_fused(wt, [dev(w)], [n_out], n_in, dev(gate), swiglu_step(dev(up)), [y])
+    dw_, dgate, dup = dev(w), dev(gate), dev(up)     # held until the launch has run
+    sicu.gemv_fused(wt, [dw_], [n_out], n_in, dgate, swiglu_step(dup), [y])
     assert_bits_equal(host(y), _want(oracle, wt, w, n_in, n_out, oracle.swiglu(gate, up)), f"{Q.NAMES[wt]} swiglu")
     assert sicu.status() == 0
 
@@ -163,7 +165,8 @@ def test_gemv_fused_multi_large(sicu, oracle, wt):
     gam = _gamma(n_in, 63)
     ys = [empty_f32(n) for n in outs]
     h = empty_f32(n_in)
-    sicu.gemv_fused(wt, [dev(w) for w in ws], outs, n_in, dev(x), rms_norm_step(dev(gam), EPS, dev(res), h), ys,
+    dws, dx_, dg_, dres_ = [dev(w) for w in ws], dev(x), dev(gam), dev(res)   # held until the launch has run
+    sicu.gemv_fused(wt, dws, outs, n_in, dx_, rms_norm_step(dg_, EPS, dres_, h), ys,
                     epi=[EPI_SILU, EPI_NONE, EPI_NONE])
     hw, a = oracle.rms_norm(x, gam, EPS, res)
     assert_bits_equal(host(h), hw, "sum_out")
@@ -187,7 +190,8 @@ def test_gemv_fused_mul_long_rows(sicu, oracle, n_in):
     g = synth.activations(n_in, 1, seed=66)[0]
     u = synth.activations(n_in, 1, seed=67)[0]
     y = empty_f32(n_out)
-    sicu.gemv_fused(wt, [dev(w)], [n_out], n_in, dev(g), mul_step(dev(u)), [y])
+    dw_, dg_, du_ = dev(w), dev(g), dev(u)           # held until the launch has run
+    sicu.gemv_fused(wt, [dw_], [n_out], n_in, dg_, mul_step(du_), [y])
     assert_bits_equal(host(y), _want(oracle, wt, w, n_in, n_out, g * u), "mul step, long rows")
 
 
@@ -223,10 +227,11 @@ def test_gemv_fused_swiglu_with_allreduce(sicu, oracle, wt):
     g.open([g.local_handle])
     try:
         y = empty_f32(d)
-        sicu.gemv_fused(wt, [dev(w)], [d], n_in, dev(gate), swiglu_step(dev(up)), [y], group=g)
+        dw_, dgate, dup = dev(w), dev(gate), dev(up)     # held until the launches have run
+        sicu.gemv_fused(wt, [dw_], [d], n_in, dgate, swiglu_step(dup), [y], group=g)
         want = _want(oracle, wt, w, n_in, d, oracle.swiglu(gate, up))
         assert_bits_equal(host(y), want, "swiglu + all-reduce")
-        sicu.gemv_fused(wt, [dev(w)], [d], n_in, dev(gate), swiglu_step(dev(up)), [y], group=g, epi=[EPI_SILU])
+        sicu.gemv_fused(wt, [dw_], [d], n_in, dgate, swiglu_step(dup), [y], group=g, epi=[EPI_SILU])
         assert_bits_equal(host(y), oracle.silu_vec(want), "swiglu + all-reduce + silu of the sum")
         assert sicu.status() == 0
     finally:
@@ -245,3 +250,33 @@ def test_step_argument_checks(sicu):
         sicu.swiglu(x, x, 12, 1, y)
     with pytest.raises(SicuError):          # misaligned residual
         sicu.rms_norm(x, gam, n, 1, EPS, y, dres=x.data_ptr() + 4)
+
+
+@pytest.mark.parametrize("wt", ALL, ids=lambda t: Q.NAMES[t])
+def test_gemv_fused_bias_epilogue(sicu, oracle, wt):
+    """Q/K/V-style launch with per-matrix biases (sicu_gemv_fused_ex): every
+    output is the reference's product plus its bias, one f32 addition
+    (src/engine.c:320-334); a NULL entry leaves that matrix unbiased; a silu
+    epilogue applies after the bias. Covers whole-row, flattened-item and F16
+    kernels (5120-wide rows take the flattened path for K formats)."""
+    n_in = 5120 if wt in (Q.Q4_K, Q.Q6_K) else 1024
+    outs = [256, 64, 64]
+    ws = [synth.weights(wt, n, n_in, seed=40 + i) for i, n in enumerate(outs)]
+    x = synth.activations(n_in, 1, seed=41)[0]
+    g = _gamma(n_in, 42)
+    rng = np.random.default_rng(43)
+    bs = [(0.02 * rng.standard_normal(n)).astype(np.float32) for n in outs]
+    _, a = oracle.rms_norm(x, g, EPS)
+    ys = [empty_f32(n) for n in outs]
+    # device buffers held until the (asynchronous) launch has run: the step
+    # and the call keep only their addresses
+    dws, dx, dg, db0, db2 = [dev(w) for w in ws], dev(x), dev(g), dev(bs[0]), dev(bs[2])
+    sicu.gemv_fused(wt, dws, outs, n_in, dx, rms_norm_step(dg, EPS), ys, bias=[db0, None, db2],
+                    epi=[EPI_NONE, EPI_NONE, EPI_SILU])
+    for i, (w, n) in enumerate(zip(ws, outs)):
+        want = _want(oracle, wt, w, n_in, n, a)
+        if i != 1:
+            want = (want + bs[i]).astype(np.float32)        # one f32 addition per element
+        if i == 2:
+            want = oracle.silu_vec(want)
+        assert_bits_equal(host(ys[i]), want, f"{Q.NAMES[wt]} bias matrix {i}")

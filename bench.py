@@ -363,9 +363,11 @@ def model_decode(torch, s, shape, dev, stream, world, rank, group, reps, fused=F
 
 
 def model_prefill(torch, s, shape, dev, stream, world, rank, group, m_tok, reps) -> dict:
-    """Prefill tok/s of the matrix path of `shape` for an m_tok-token prompt."""
+    """Prefill tok/s of the matrix path of `shape` for an m_tok-token prompt,
+    from the prefill copies of the weights (sicu_prefill_pack, made at load
+    beside the raw blocks)."""
     from siphon_b200 import model_path as mp
-    m = mp.MatrixPath(s, shape, dev, world, rank, group, seed=5, max_tokens=m_tok)
+    m = mp.MatrixPath(s, shape, dev, world, rank, group, seed=5, max_tokens=m_tok, packed=True)
     with torch.cuda.stream(stream):
         m.prefill(stream, m_tok)          # sizes the workspace outside capture
     torch.cuda.synchronize()
@@ -387,8 +389,9 @@ def model_prefill(torch, s, shape, dev, stream, world, rank, group, m_tok, reps)
     out = {"tok_s": round(m_tok / sec, 1), "ms_per_prompt": round(sec * 1e3, 3), "prompt_tokens": m_tok,
            "TFLOPs": round(tflops, 1), "f16_tensor_frac": round(tflops / f16_peak, 4),
            "int8_tensor_frac_proxy": round(tflops / (2 * f16_peak), 4), "peak_kind": kind,
-           "note": "tensor-core kernel for Q4_K and Q6_K (kind::f16 MMAs on exact f16 (scale x quant) operands); "
-                   "int8 peak taken as 2x the measured bf16 dense peak"}
+           "pack_bytes_per_gpu": int(sum(t.numel() for t in m.pack.values())),
+           "note": "tensor-core kernel for Q4_K and Q6_K (kind::f16 MMAs on exact f16 (scale x quant) operands) "
+                   "reading the prefill copies of the weights; int8 peak taken as 2x the measured bf16 dense peak"}
     del m
     torch.cuda.empty_cache()
     return out
@@ -855,6 +858,7 @@ CASES = {
     "flat": "gemv_flat_kernel<Q4_K>: one sicu_gemv_multi launch over 4 copies of Q4_K 27648x5120, 4 times",
     "ar": "gemv_kernel<Q4_K, AR> (one-rank group) and the plain gemv_kernel<Q4_K> alternating, Q4_K 5120x13824",
     "prefill": "prefill_kernel<Q4_K>: 4096x4096, 512 tokens, twice",
+    "prefill_packed": "prefill_packed_kernel<Q4_K, 256>: 14336x4096 from its prefill copy, 512 tokens, twice",
     "steps": "Q4_K Wq/Wk/Wv of the 32B shape (5120 -> 5120+1024+1024): plain and with the residual add + "
              "RMS norm fused, alternating, 4 each",
     "decode_full": "three eager decode steps of the TinyLlama-1.1B shape with the steps and attention, "
@@ -904,6 +908,16 @@ def run_case(case: str, reps: int = 4) -> int:
         y = torch.empty(m, n, device=dev)
         for _ in range(2):
             s.gemm_prefill_f32(wt, w, n, n, x, m, y)
+    elif case == "prefill_packed":
+        wt, n_out, n_in, m = Q.Q4_K, 14336, 4096, 512
+        w = mp.device_weights(wt, n_out, n_in, 1, dev)
+        nb = s.prefill_pack_bytes(wt, n_in, n_out)
+        p = torch.empty(nb, dtype=torch.uint8, device=dev)
+        s.prefill_pack(wt, w, n_in, n_out, p, nb)
+        x = torch.randn(m, n_in, device=dev)
+        y = torch.empty(m, n_out, device=dev)
+        for _ in range(2):
+            s.gemm_prefill_packed_f32(wt, w, p, n_in, n_out, x, m, y)
     elif case == "steps":
         wt, n_in, outs = Q.Q4_K, 5120, [5120, 1024, 1024]
         ws = [mp.device_weights(wt, n, n_in, 1 + i, dev) for i, n in enumerate(outs)]

@@ -222,6 +222,33 @@ SICU_API int sicu_gemm_prefill(uint32_t wtype, const void *dw, int64_t n_in, int
 SICU_API int sicu_gemm_prefill_f32(uint32_t wtype, const void *dw, int64_t n_in, int64_t n_out,
                                    const float *dx, int64_t m, float *dy, void *stream);
 
+/* ---- prefill copies of the weights -----------------------------------------
+ * A second, re-tiled copy of a Q4_K or Q6_K matrix for prompt products, made
+ * once when the weights are loaded (the reference makes its tensor views at
+ * load, si_tensor_from_gguf, src/backend.c:144-176); the raw GGUF bytes stay
+ * on the device for decode. Per 128-row tile and super-block the copy holds
+ * the exact f16 (scale x quant) operands in the shared-memory layout the
+ * tensor cores read (128-byte swizzle), the mins operand and the row scales,
+ * so the prefill kernel streams it with bulk copies and converts nothing.
+ * Size: 4x64 KiB + 8.5 KiB per 128 rows and super-block for Q4_K (about 3.6x
+ * the raw bytes), 8x16 KiB + 0.5 KiB for Q6_K (about 4.9x).
+ * sicu_prefill_pack_bytes: the copy's size (SICU_ENOTSUP for other types).
+ * sicu_prefill_pack: writes the copy of device weights dw into dpack
+ * (pack_bytes >= that size, 16-byte aligned), asynchronously on stream.
+ * sicu_gemm_prefill_packed(_f32): sicu_gemm_prefill(_f32) with the copy
+ * (dpack may be null: then the same as without). Blocks of more than 32
+ * tokens run from the copy (128 rows x 128 or 256 tokens per CTA, both
+ * operands in shared memory); smaller ones read dw as before. Results are
+ * within the same tolerance as sicu_gemm_prefill, from the same exact integer
+ * sums per super-block; the float additions of super-blocks may differ. */
+SICU_API int sicu_prefill_pack_bytes(uint32_t wtype, int64_t n_in, int64_t n_out, size_t *bytes);
+SICU_API int sicu_prefill_pack(uint32_t wtype, const void *dw, int64_t n_in, int64_t n_out, void *dpack,
+                               size_t pack_bytes, void *stream);
+SICU_API int sicu_gemm_prefill_packed(uint32_t wtype, const void *dw, const void *dpack, int64_t n_in,
+                                      int64_t n_out, const void *dxq, int64_t m, float *dy, void *stream);
+SICU_API int sicu_gemm_prefill_packed_f32(uint32_t wtype, const void *dw, const void *dpack, int64_t n_in,
+                                          int64_t n_out, const float *dx, int64_t m, float *dy, void *stream);
+
 /* ---- tensor-parallel all-reduce fused into the matvec ------------------------
  * A row-split product (Wo, W_down split by input columns across a
  * tensor-parallel group) leaves a partial output vector on every rank that

@@ -546,7 +546,7 @@ static int batch_common(uint32_t wtype, int n_mats, const void *const *dw, const
 
 // xq: m rows of pair-format activation blocks (device), or null with xf set
 static int prefill_common(uint32_t wtype, const void *dw, int64_t n_in, int64_t n_out, const void *xq,
-                          const float *xf, int64_t m, float *dy, cudaStream_t st) {
+                          const float *xf, int64_t m, float *dy, cudaStream_t st, const void *pack = nullptr) {
     DevState *ds;
     if (int rc = current(ds)) return rc;
     uint32_t pair;
@@ -570,7 +570,8 @@ static int prefill_common(uint32_t wtype, const void *dw, int64_t n_in, int64_t 
         return SICU_OK;
     }
     const size_t qbytes = xq ? 0 : (((size_t)m * pair_row_bytes(pair, n_in) + 255) & ~size_t(255));
-    if (int rc = grow_prefill_ws(*ds, qbytes + prefill_workspace_bytes(wtype, n_in, n_out, m, ds->sms))) return rc;
+    if (int rc = grow_prefill_ws(*ds, qbytes + prefill_workspace_bytes(wtype, n_in, n_out, m, ds->sms, pack != nullptr)))
+        return rc;
     if (!xq) {
         if (launch_quantize(pair, xf, ds->pf_ws, n_in, m, st) != 0) return cuda_fail(cudaGetLastError(), "prefill quantize");
         xq = ds->pf_ws;
@@ -586,6 +587,7 @@ static int prefill_common(uint32_t wtype, const void *dw, int64_t n_in, int64_t 
     cudaGetDevice(&L.device);
     L.num_sms = ds->sms;
     L.status = ds->status;
+    L.pack = pack;
     const int rc = launch_prefill(wtype, L, st);
     if (rc == -4) return fail(SICU_EIO, "prefill: tensor map encoding failed");
     if (rc != 0) return cuda_fail(cudaGetLastError(), "prefill launch");
@@ -608,6 +610,67 @@ int sicu_gemm_prefill_f32(uint32_t wtype, const void *dw, int64_t n_in, int64_t 
     if (m == 0 || n_out == 0) return current_ok();
     if (!aligned(dx, 16)) return fail(SICU_EINVAL, "prefill: f32 activation must be 16-byte aligned");
     return prefill_common(wtype, dw, n_in, n_out, nullptr, dx, m, dy, (cudaStream_t)stream);
+}
+
+// ---- prefill copies of the weights ---------------------------------------------------
+static int check_pack_shape(const char *what, uint32_t wtype, int64_t n_in, int64_t n_out) {
+    if (!prefill_supported(wtype))
+        return fail(SICU_ENOTSUP, "%s: no tensor-core prefill kernel for %s (%u)", what, tname(wtype), wtype);
+    if (n_in <= 0 || n_out < 0 || n_in % QK_K || n_in > (int64_t)1 << 20 || n_out > (int64_t)1 << 30)
+        return fail(SICU_EINVAL, "%s: bad shape n_in=%lld n_out=%lld", what, (long long)n_in, (long long)n_out);
+    return SICU_OK;
+}
+
+int sicu_prefill_pack_bytes(uint32_t wtype, int64_t n_in, int64_t n_out, size_t *bytes) {
+    if (!bytes) return fail(SICU_EINVAL, "prefill pack: null bytes");
+    *bytes = 0;
+    if (int rc = check_pack_shape("prefill pack", wtype, n_in, n_out)) return rc;
+    *bytes = prefill_pack_bytes(wtype, n_in, n_out);
+    return SICU_OK;
+}
+
+int sicu_prefill_pack(uint32_t wtype, const void *dw, int64_t n_in, int64_t n_out, void *dpack, size_t pack_bytes,
+                      void *stream) {
+    if (int rc = check_pack_shape("prefill pack", wtype, n_in, n_out)) return rc;
+    const size_t need = prefill_pack_bytes(wtype, n_in, n_out);
+    if (pack_bytes < need)
+        return fail(SICU_EINVAL, "prefill pack: %zu bytes given, %zu needed", pack_bytes, need);
+    if (n_out == 0) return current_ok();
+    if (!dw || !dpack) return fail(SICU_EINVAL, "prefill pack: null pointer");
+    if (!aligned(dw, 16) || !aligned(dpack, 16)) return fail(SICU_EINVAL, "prefill pack: pointers must be 16-byte aligned");
+    DevState *ds;
+    if (int rc = current(ds)) return rc;
+    if (launch_prefill_pack(wtype, dw, n_in, n_out, dpack, (cudaStream_t)stream) != 0)
+        return cuda_fail(cudaGetLastError(), "prefill pack launch");
+    return SICU_OK;
+}
+
+static int check_packed(uint32_t wtype, const void *dpack) {
+    if (!dpack) return SICU_OK;
+    if (!prefill_supported(wtype))
+        return fail(SICU_EINVAL, "prefill: %s has no prefill copy (no tensor-core kernel)", tname(wtype));
+    if (!aligned(dpack, 16)) return fail(SICU_EINVAL, "prefill: packed copy must be 16-byte aligned");
+    return SICU_OK;
+}
+
+int sicu_gemm_prefill_packed(uint32_t wtype, const void *dw, const void *dpack, int64_t n_in, int64_t n_out,
+                             const void *dxq, int64_t m, float *dy, void *stream) {
+    uint32_t pair;
+    if (int rc = check_prefill(wtype, dw, n_in, n_out, dxq, m, dy, pair)) return rc;
+    if (int rc = check_packed(wtype, dpack)) return rc;
+    if (m == 0 || n_out == 0) return current_ok();
+    if (!aligned(dxq, pair == T_Q8_K ? 4 : 2)) return fail(SICU_EINVAL, "prefill: activation misaligned");
+    return prefill_common(wtype, dw, n_in, n_out, dxq, nullptr, m, dy, (cudaStream_t)stream, dpack);
+}
+
+int sicu_gemm_prefill_packed_f32(uint32_t wtype, const void *dw, const void *dpack, int64_t n_in, int64_t n_out,
+                                 const float *dx, int64_t m, float *dy, void *stream) {
+    uint32_t pair;
+    if (int rc = check_prefill(wtype, dw, n_in, n_out, dx, m, dy, pair)) return rc;
+    if (int rc = check_packed(wtype, dpack)) return rc;
+    if (m == 0 || n_out == 0) return current_ok();
+    if (!aligned(dx, 16)) return fail(SICU_EINVAL, "prefill: f32 activation must be 16-byte aligned");
+    return prefill_common(wtype, dw, n_in, n_out, nullptr, dx, m, dy, (cudaStream_t)stream, dpack);
 }
 
 int sicu_gemv_batch(uint32_t wtype, int n_mats, const void *const *dw, const int64_t *n_out, int64_t n_in,

@@ -100,13 +100,18 @@ struct PrefillLaunch {
     const void *xq;       // m rows of Q8_K blocks (device)
     int64_t m;
     float *y;             // [m][n_out] (device)
-    void *ws;             // prefill_workspace_bytes(wtype, n_in, n_out, m, num_sms) bytes, 256-byte aligned
+    void *ws;             // prefill_workspace_bytes(wtype, n_in, n_out, m, num_sms, pack != 0) bytes, 256-byte aligned
     int device;
     int num_sms;
     int *status;
+    const void *pack;     // the prefill copy of w (prefill_pack_bytes), or null
 };
 bool prefill_supported(uint32_t wtype);
-size_t prefill_workspace_bytes(uint32_t wtype, int64_t n_in, int64_t n_out, int64_t m, int num_sms);
+size_t prefill_workspace_bytes(uint32_t wtype, int64_t n_in, int64_t n_out, int64_t m, int num_sms, bool packed);
+// bytes of the prefill copy of an n_out x n_in matrix (0: no tensor-core kernel for the type)
+size_t prefill_pack_bytes(uint32_t wtype, int64_t n_in, int64_t n_out);
+// writes the prefill copy of the weight blocks w into pack; -3: unsupported type
+int launch_prefill_pack(uint32_t wtype, const void *w, int64_t n_in, int64_t n_out, void *pack, cudaStream_t st);
 // -3: no tensor-core kernel for the type; -4: tensor map encoding failed; -2: launch
 int launch_prefill(uint32_t wtype, const PrefillLaunch &L, cudaStream_t st);
 

@@ -198,6 +198,117 @@ __device__ __forceinline__ void span_words(uint32_t a, int head, uint32_t (&W)[N
     }
 }
 
+// Q4_K super-block header h (d, dmin, 12 bytes of packed scales and mins,
+// src/kernels.c:377-382): the exponent s of the row scale f = d 2^s, s >= 0
+// the smallest that keeps (dmin / f) * mn inside f16 range; keep_main is
+// false when d is zero or negligible (s > 14) and only the mins term is kept.
+__device__ __forceinline__ void q4k_scale_exp(const uint4 &h, int &sexp, bool &keep_main) {
+    const uint32_t mn_lo = h.z & 0x3f3f3f3fu;
+    const uint32_t mn_hi = ((h.w >> 4) & 0x0f0f0f0fu) | ((h.z >> 2) & 0x30303030u);
+    const float d = h2f(h.x & 0xffffu), dmin = h2f(h.x >> 16);
+    uint32_t mn_max = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) mn_max = max(mn_max, max(byte_at(mn_lo, j), byte_at(mn_hi, j)));
+    sexp = 0;
+    keep_main = d != 0.0f;
+    if (keep_main) {
+        const float ratio = fabsf(dmin) * (float)mn_max / (60000.0f * fabsf(d));
+        if (ratio > 1.0f) sexp = ilogbf(ratio) + 1;
+        if (sexp > 14) keep_main = false;
+    }
+}
+
+// The row scale f and the mins operand: 16 k (the bsums index i, mn[i / 2])
+// as -(hi + lo) of (dmin / f) mn, the hi parts in words 0-7, the lo parts in
+// 8-15, two equal f16 per word (k = 2j, 2j + 1).
+__device__ __forceinline__ void q4k_mins_words(const uint4 &h, int sexp, bool keep_main, bool valid, float &f,
+                                               uint32_t (&mw)[16]) {
+    const uint32_t mn_lo = h.z & 0x3f3f3f3fu;
+    const uint32_t mn_hi = ((h.w >> 4) & 0x0f0f0f0fu) | ((h.z >> 2) & 0x30303030u);
+    const float d = h2f(h.x & 0xffffu), dmin = h2f(h.x >> 16);
+    f = keep_main ? ldexpf(d, sexp) : ldexpf(dmin, -10);
+    const float mfac = f != 0.0f ? dmin / f : 0.0f;
+    if (!valid) f = 0.0f;
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+        const float mu = mfac * (float)byte_at(c < 4 ? mn_lo : mn_hi, c & 3);
+        const float hi = __half2float(__float2half_rn(mu));
+        mw[c] = valid ? half2_bits(-hi, -hi) : 0u;
+        mw[8 + c] = valid ? half2_bits(hi - mu, hi - mu) : 0u;
+    }
+}
+
+// K-step c of a Q4_K super-block (qs[32c..32c+31] in x: low nibbles =
+// sub-block 2c, high = 2c+1) as 64 f16 slots (sc q 2^-s): words 0-15 sub-block
+// 2c, 16-31 sub-block 2c+1; slot order inside each group of four elements:
+// 0, 2, 1, 3. on = false gives zeros.
+__device__ __forceinline__ void q4k_kstep_words(const uint4 &h, const uint32_t (&x)[8], int c, int sexp, bool on,
+                                                uint32_t (&w)[32]) {
+    const uint32_t sc_lo = h.y & 0x3f3f3f3fu;
+    const uint32_t sc_hi = (h.w & 0x0f0f0f0fu) | ((h.y >> 2) & 0x30303030u);
+    const uint32_t scw = c < 2 ? sc_lo : sc_hi;
+    const float s0 = on ? ldexpf((float)byte_at(scw, (2 * c) & 3), -sexp) : 0.0f;
+    const float s1 = on ? ldexpf((float)byte_at(scw, (2 * c + 1) & 3), -sexp) : 0.0f;
+    // (1024 + q) * sc - 1024 sc for the low nibbles, (1024 + 16 q) * sc/16 -
+    // 64 sc for the high ones: exact
+    const uint32_t mul0 = half2_bits(s0, s0), add0 = half2_bits(-1024.0f * s0, -1024.0f * s0);
+    const uint32_t mul1 = half2_bits(0.0625f * s1, 0.0625f * s1), add1 = half2_bits(-64.0f * s1, -64.0f * s1);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        w[2 * k] = nib_f16(x[k], 0x000f000fu, mul0, add0);
+        w[2 * k + 1] = nib_f16(x[k] >> 8, 0x000f000fu, mul0, add0);
+        w[16 + 2 * k] = nib_f16(x[k], 0x00f000f0u, mul1, add1);
+        w[16 + 2 * k + 1] = nib_f16(x[k] >> 8, 0x00f000f0u, mul1, add1);
+    }
+}
+
+// Quarter cq of a Q6_K super-block (src/kernels.c:480-523) as the two exact
+// f16 planes, (q - 32) lo (p0) and (q - 32) hi (p1) with sc = 16 hi + lo.
+// row: shared-memory address of the 16-byte aligned span holding the block
+// from byte `head` on; S: its scale words (bytes 192..211). Quarter cq (h =
+// cq / 2) element 32g + l (g = 0, 1; group G' = 2 (cq & 1) + g of half h):
+// ql[64h + 32g + l] (low nibble for even cq, high for odd), qh[32h + l] bits
+// 2G'..2G'+1, scale sc[4cq + 2g + l / 16].
+__device__ __forceinline__ void q6k_quarter_words(uint32_t row, int head, const uint32_t (&S)[5], bool valid,
+                                                  int cq, uint32_t (&p0)[32], uint32_t (&p1)[32]) {
+    const int h = cq >> 1;
+    const int nsh = (cq & 1) ? 4 : 0;
+    uint32_t QH[8];
+    span_words<8>(row + 128 + 32 * h, head, QH);
+#pragma unroll
+    for (int g = 0; g < 2; ++g) {
+        const int Gp = 2 * (cq & 1) + g;
+        uint32_t QL[8];
+        span_words<8>(row + 64 * h + 32 * g, head, QL);
+        // the two 16-element sub-blocks of these 32 elements
+        const int sbi = 4 * cq + 2 * g;
+        const int sa = (int)(int8_t)byte_at(S[sbi >> 2], sbi & 3);
+        const int sb2 = (int)(int8_t)byte_at(S[(sbi + 1) >> 2], (sbi + 1) & 3);
+        const int sv[2] = {valid ? sa : 0, valid ? sb2 : 0};
+        uint32_t mul0[2], add0[2], mul1[2], add1[2];
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            const float lo = (float)(sv[i] & 15), hi = (float)(sv[i] >> 4);   // sc = 16 hi + lo
+            mul0[i] = half2_bits(lo, lo);
+            add0[i] = half2_bits(-1056.0f * lo, -1056.0f * lo);              // (1024 + q) lo - 1056 lo
+            mul1[i] = half2_bits(hi, hi);
+            add1[i] = half2_bits(-1056.0f * hi, -1056.0f * hi);
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const int i = k >> 2;   // sub-block of word k
+            // 6-bit q of elements 4k..4k+3, one per byte
+            const uint32_t q = ((QL[k] >> nsh) & 0x0f0f0f0fu) | (((QH[k] >> (2 * Gp)) & 0x03030303u) << 4);
+            const uint32_t e02 = and_or(q, 0x00ff00ffu, 0x64006400u);
+            const uint32_t e13 = and_or(q >> 8, 0x00ff00ffu, 0x64006400u);
+            p0[16 * g + 2 * k] = hfma2_u32(e02, mul0[i], add0[i]);
+            p0[16 * g + 2 * k + 1] = hfma2_u32(e13, mul0[i], add0[i]);
+            p1[16 * g + 2 * k] = hfma2_u32(e02, mul1[i], add1[i]);
+            p1[16 * g + 2 * k + 1] = hfma2_u32(e13, mul1[i], add1[i]);
+        }
+    }
+}
+
 struct PfCtx {
     uint32_t sb0;
     uint8_t *smem;
@@ -217,38 +328,14 @@ __device__ __forceinline__ bool convert_q4k(const PfCtx &cx, uint32_t base, uint
     auto bar = [&](int i) { return barbase + 8u * (uint32_t)i; };
     const uint32_t raw = base + Lay::OFF_RAW + rb * Lay::RAW_BUF + r * B_Q4_K;
     const uint4 h = valid ? lds128(raw) : make_uint4(0, 0, 0, 0);
-    // 6-bit scales / mins (src/kernels.c:377-382)
-    const uint32_t sc_lo = h.y & 0x3f3f3f3fu;
-    const uint32_t sc_hi = (h.w & 0x0f0f0f0fu) | ((h.y >> 2) & 0x30303030u);
-    const uint32_t mn_lo = h.z & 0x3f3f3f3fu;
-    const uint32_t mn_hi = ((h.w >> 4) & 0x0f0f0f0fu) | ((h.z >> 2) & 0x30303030u);
-    const float d = h2f(h.x & 0xffffu), dmin = h2f(h.x >> 16);
-    uint32_t mn_max = 0;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) mn_max = max(mn_max, max(byte_at(mn_lo, j), byte_at(mn_hi, j)));
-    // f = d 2^s with the mins factor dmin / f * mn inside f16 range; a zero
-    // (or, past s = 14, negligible) d leaves only the mins term, exactly
-    int sexp = 0;
-    bool keep_main = d != 0.0f;
-    if (keep_main) {
-        const float ratio = fabsf(dmin) * (float)mn_max / (60000.0f * fabsf(d));
-        if (ratio > 1.0f) sexp = ilogbf(ratio) + 1;
-        if (sexp > 14) keep_main = false;
-    }
+    int sexp;
+    bool keep_main;
+    q4k_scale_exp(h, sexp, keep_main);
     if (G == 0) {
-        const float f = keep_main ? ldexpf(d, sexp) : ldexpf(dmin, -10);
-        const float mfac = f != 0.0f ? dmin / f : 0.0f;
-        reinterpret_cast<float *>(cx.smem + Lay::OFF_DW)[b4 * PF_BM + r] = valid ? f : 0.0f;
-        // mins operand: 16 k (the bsums index i, mn[i / 2]) as -(hi + lo), the
-        // hi parts in columns 0-7, the lo parts in 8-15, two f16 per column
+        float f;
         uint32_t mw[16];
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {
-            const float mu = mfac * (float)byte_at(c < 4 ? mn_lo : mn_hi, c & 3);
-            const float hi = __half2float(__float2half_rn(mu));
-            mw[c] = valid ? half2_bits(-hi, -hi) : 0u;
-            mw[8 + c] = valid ? half2_bits(hi - mu, hi - mu) : 0u;
-        }
+        q4k_mins_words(h, sexp, keep_main, valid, f, mw);
+        reinterpret_cast<float *>(cx.smem + Lay::OFF_DW)[b4 * PF_BM + r] = f;
         tc_fence_after();
         tmem_st16(tl + TM_MIN + 16 * b4, mw);
         tmem_wait_st();
@@ -262,23 +349,8 @@ __device__ __forceinline__ bool convert_q4k(const PfCtx &cx, uint32_t base, uint
             return false;
         const uint4 q0 = lds128(raw + 16 + 32 * c), q1 = lds128(raw + 32 + 32 * c);
         const uint32_t x[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
-        const uint32_t scw = c < 2 ? sc_lo : sc_hi;
-        const float s0 = (valid && keep_main) ? ldexpf((float)byte_at(scw, (2 * c) & 3), -sexp) : 0.0f;
-        const float s1 = (valid && keep_main) ? ldexpf((float)byte_at(scw, (2 * c + 1) & 3), -sexp) : 0.0f;
-        // (1024 + q) * sc - 1024 sc for the low nibbles, (1024 + 16 q) * sc/16 -
-        // 64 sc for the high ones: exact
-        const uint32_t mul0 = half2_bits(s0, s0), add0 = half2_bits(-1024.0f * s0, -1024.0f * s0);
-        const uint32_t mul1 = half2_bits(0.0625f * s1, 0.0625f * s1), add1 = half2_bits(-64.0f * s1, -64.0f * s1);
-        // columns 0-15: sub-block 2c, 16-31: 2c+1; slot order inside each group
-        // of four elements: 0, 2, 1, 3
         uint32_t w[32];
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-            w[2 * k] = nib_f16(x[k], 0x000f000fu, mul0, add0);
-            w[2 * k + 1] = nib_f16(x[k] >> 8, 0x000f000fu, mul0, add0);
-            w[16 + 2 * k] = nib_f16(x[k], 0x00f000f0u, mul1, add1);
-            w[16 + 2 * k + 1] = nib_f16(x[k] >> 8, 0x00f000f0u, mul1, add1);
-        }
+        q4k_kstep_words(h, x, c, sexp, valid && keep_main, w);
         tc_fence_after();
         tmem_st32(tl + TM_A + 32 * s, w);
         tmem_wait_st();
@@ -319,43 +391,8 @@ __device__ __forceinline__ bool convert_q6k(const PfCtx &cx, uint32_t base, uint
         if (!__all_sync(FULL, pf_wait(bar(BAR_ST_EMPTY + s0), use_of(t0) ^ 1, cx.abort_flag, cx.status) &&
                                   pf_wait(bar(BAR_ST_EMPTY + s1), use_of(t0 + 1) ^ 1, cx.abort_flag, cx.status)))
             return false;
-        const int h = cq >> 1;
-        const int nsh = (cq & 1) ? 4 : 0;
-        uint32_t QH[8];
-        span_words<8>(row + 128 + 32 * h, head, QH);
         uint32_t p0[32], p1[32];
-#pragma unroll
-        for (int g = 0; g < 2; ++g) {
-            const int Gp = 2 * (cq & 1) + g;
-            uint32_t QL[8];
-            span_words<8>(row + 64 * h + 32 * g, head, QL);
-            // the two 16-element sub-blocks of these 32 elements
-            const int sbi = 4 * cq + 2 * g;
-            const int sa = (int)(int8_t)byte_at(S[sbi >> 2], sbi & 3);
-            const int sb2 = (int)(int8_t)byte_at(S[(sbi + 1) >> 2], (sbi + 1) & 3);
-            const int sv[2] = {valid ? sa : 0, valid ? sb2 : 0};
-            uint32_t mul0[2], add0[2], mul1[2], add1[2];
-#pragma unroll
-            for (int i = 0; i < 2; ++i) {
-                const float lo = (float)(sv[i] & 15), hi = (float)(sv[i] >> 4);   // sc = 16 hi + lo
-                mul0[i] = half2_bits(lo, lo);
-                add0[i] = half2_bits(-1056.0f * lo, -1056.0f * lo);              // (1024 + q) lo - 1056 lo
-                mul1[i] = half2_bits(hi, hi);
-                add1[i] = half2_bits(-1056.0f * hi, -1056.0f * hi);
-            }
-#pragma unroll
-            for (int k = 0; k < 8; ++k) {
-                const int i = k >> 2;   // sub-block of word k
-                // 6-bit q of elements 4k..4k+3, one per byte
-                const uint32_t q = ((QL[k] >> nsh) & 0x0f0f0f0fu) | (((QH[k] >> (2 * Gp)) & 0x03030303u) << 4);
-                const uint32_t e02 = and_or(q, 0x00ff00ffu, 0x64006400u);
-                const uint32_t e13 = and_or(q >> 8, 0x00ff00ffu, 0x64006400u);
-                p0[16 * g + 2 * k] = hfma2_u32(e02, mul0[i], add0[i]);
-                p0[16 * g + 2 * k + 1] = hfma2_u32(e13, mul0[i], add0[i]);
-                p1[16 * g + 2 * k] = hfma2_u32(e02, mul1[i], add1[i]);
-                p1[16 * g + 2 * k + 1] = hfma2_u32(e13, mul1[i], add1[i]);
-            }
-        }
+        q6k_quarter_words(row, head, S, valid, cq, p0, p1);
         tc_fence_after();
         tmem_st32(tl + TM_A + 32 * s0, p0);
         tmem_st32(tl + TM_A + 32 * s1, p1);
@@ -601,6 +638,376 @@ prefill_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ 
     }
 }
 
+// ---- prefill copies of the weights ------------------------------------------------
+// Made once when the weights are uploaded, beside the raw GGUF bytes (which
+// the decode kernels keep reading): per 128-row tile and super-block one
+// contiguous chunk holding exactly the shared-memory image the MMAs read, so
+// the prefill kernel moves it with plain 1-D bulk copies and converts nothing:
+//   [KSTEPS][128 rows][64 f16]  A operand of each K-step (sc q 2^-s, or the two
+//                               Q6_K planes), K-major with the 128-byte swizzle
+//                               (16-byte unit j of row r stored at j ^ (r & 7))
+//   Q4_K: [2][128 rows][16 f16] the mins operand, hi then lo parts, K-major
+//                               with the 32-byte swizzle (unit j of row r at
+//                               j ^ ((r >> 2) & 1))
+//   [128] f32                   the row scale f (Q4_K: d 2^s; Q6_K: d)
+// Rows past n_out are zero. The values are those the converters of
+// prefill_kernel write into tensor memory.
+template <uint32_t T> struct PkFmt;
+template <> struct PkFmt<T_Q4_K> {
+    static constexpr int KSTEPS = 4, RAW_ROW = 144;
+    static constexpr bool MINS = true;
+};
+template <> struct PkFmt<T_Q6_K> {
+    static constexpr int KSTEPS = 8, RAW_ROW = 240;
+    static constexpr bool MINS = false;
+};
+constexpr int PK_ATILE = PF_BM * PF_KS * 2;   // 16 KB: one K-step of a 128-row tile
+constexpr int PK_MINT = PF_BM * 16 * 2;       // 4 KB: one half of the mins operand
+template <uint32_t T> __host__ __device__ constexpr int pk_off_min() { return PkFmt<T>::KSTEPS * PK_ATILE; }
+template <uint32_t T> __host__ __device__ constexpr int pk_off_f() {
+    return pk_off_min<T>() + (PkFmt<T>::MINS ? 2 * PK_MINT : 0);
+}
+template <uint32_t T> __host__ __device__ constexpr int pk_chunk() { return pk_off_f<T>() + PF_BM * 4; }
+
+// one CTA per (row tile, super-block); thread = tile row
+template <uint32_t T>
+__global__ void __launch_bounds__(PF_BM) prefill_pack_kernel(const uint8_t *w, int64_t row_bytes, int n_out, int nsb,
+                                                            uint8_t *pack) {
+    using P = PkFmt<T>;
+    __shared__ __align__(16) uint8_t raw[PF_BM * P::RAW_ROW];
+    const int rt = blockIdx.x, sb = blockIdx.y, r = threadIdx.x;
+    const int64_t row = (int64_t)rt * PF_BM + r;
+    const bool valid = row < n_out;
+    // this row's block into shared memory, 16-byte aligned (Q6_K blocks start
+    // at any even byte)
+    uint8_t *mine = raw + r * P::RAW_ROW;
+    if (T == T_Q4_K) {
+        const uint4 *src = reinterpret_cast<const uint4 *>(w + row * row_bytes + (int64_t)sb * B_Q4_K);
+#pragma unroll
+        for (int k = 0; k < B_Q4_K / 16; ++k)
+            reinterpret_cast<uint4 *>(mine)[k] = valid ? src[k] : make_uint4(0, 0, 0, 0);
+    } else {
+        const uint16_t *src = reinterpret_cast<const uint16_t *>(w + row * row_bytes + (int64_t)sb * B_Q6_K);
+        for (int k = 0; k < P::RAW_ROW / 2; ++k)
+            reinterpret_cast<uint16_t *>(mine)[k] = (valid && k < B_Q6_K / 2) ? src[k] : (uint16_t)0;
+    }
+    __syncwarp();
+    uint8_t *chunk = pack + ((size_t)rt * nsb + sb) * (size_t)pk_chunk<T>();
+    auto put_a = [&](int t, const uint32_t (&v)[32]) {
+        uint8_t *dst = chunk + (size_t)t * PK_ATILE + r * 128;
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+            reinterpret_cast<uint4 *>(dst)[j ^ (r & 7)] = make_uint4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+    };
+    float *fdst = reinterpret_cast<float *>(chunk + pk_off_f<T>());
+    const uint32_t a = smem_addr(mine);
+    if constexpr (T == T_Q4_K) {
+        const uint4 h = lds128(a);
+        int sexp;
+        bool keep_main;
+        q4k_scale_exp(h, sexp, keep_main);
+        float f;
+        uint32_t mw[16];
+        q4k_mins_words(h, sexp, keep_main, valid, f, mw);
+        fdst[r] = f;
+        for (int half = 0; half < 2; ++half) {
+            uint8_t *dst = chunk + pk_off_min<T>() + half * PK_MINT + r * 32;
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                const uint32_t *m4 = mw + 8 * half + 4 * j;
+                reinterpret_cast<uint4 *>(dst)[j ^ ((r >> 2) & 1)] = make_uint4(m4[0], m4[1], m4[2], m4[3]);
+            }
+        }
+        for (int c = 0; c < 4; ++c) {
+            const uint4 q0 = lds128(a + 16 + 32 * c), q1 = lds128(a + 32 + 32 * c);
+            const uint32_t x[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+            uint32_t v[32];
+            q4k_kstep_words(h, x, c, sexp, valid && keep_main, v);
+            put_a(c, v);
+        }
+    } else {
+        uint32_t S[5];
+        span_words<5>(a + 192, 0, S);
+        fdst[r] = valid ? h2f(S[4] & 0xffffu) : 0.0f;
+        for (int cq = 0; cq < 4; ++cq) {
+            uint32_t p0[32], p1[32];
+            q6k_quarter_words(a, 0, S, valid, cq, p0, p1);
+            put_a(2 * cq, p0);
+            put_a(2 * cq + 1, p1);
+        }
+    }
+}
+
+// ---- prefill from the packed copy ------------------------------------------------------
+// One CTA: 128 weight rows x BN tokens, one SM, 10 warps:
+//   warp 0     loads: per super-block the mins operand, row scales, bsums tile
+//              and token scales; per K-step the A chunk (bulk copy of 16 KB)
+//              and the token operand tile (TMA, 128-byte swizzle)
+//   warp 1     tensor-memory owner; lane 0 issues the MMAs, both operands
+//              from shared memory
+//   warps 2-9  epilogue as in prefill_kernel: per super-block the accumulator
+//              scaled by f * dA and added in registers (thread = row, BN / 2
+//              tokens)
+// Tensor memory: two BN-column accumulators.
+constexpr int PK_WARPS = 10, PK_EPI = 2, PK_NEPI = 8, PK_NSB = 2;
+template <uint32_t T, int BN> struct PkLayout {
+    using P = PkFmt<T>;
+    static constexpr int STAGE = PK_ATILE + stage_bytes(BN);
+    // per super-block buffer: mins hi / lo, bsums tile, row scales, token scales
+    static constexpr int META_MIN = P::MINS ? 2 * PK_MINT : 0;
+    static constexpr int META_B2 = P::MINS ? min_bytes(BN) : 0;
+    static constexpr int META = (META_MIN + META_B2 + PF_BM * 4 + BN * 4 + 1023) & ~1023;
+    static constexpr int BUDGET = 227 * 1024 - 2048;   // barriers, flags, alignment slack
+    static constexpr int STAGES = (BUDGET - PK_NSB * META) / STAGE > 6 ? 6 : (BUDGET - PK_NSB * META) / STAGE;
+    static constexpr int OFF_META = STAGES * STAGE;
+    static constexpr int OFF_BAR = OFF_META + PK_NSB * META;
+    static constexpr int OFF_FLAGS = OFF_BAR + 8 * 32;
+    static constexpr int SMEM = OFF_FLAGS + 16 + 1024;
+    static_assert(STAGES >= 2, "shared memory");
+    static_assert(SMEM <= 227 * 1024, "shared memory");
+};
+enum {
+    PB_FULL = 0,            // [6] A chunk + token tile landed (bytes)
+    PB_EMPTY = 6,           // [6] stage consumed by the MMAs (commit)
+    PB_META_FULL = 12,      // [2] super-block buffer landed (bytes)
+    PB_META_FREE = 14,      // [2] epilogue done with a super-block buffer (8 warps)
+    PB_ACC_FULL = 16,       // [2] accumulator of a super-block ready (commit)
+    PB_ACC_EMPTY = 18,      // [2] accumulator read (8 warps)
+    PB_DRAIN = 20,
+    PB_NBARS = 21,
+};
+
+struct PkParams {
+    const uint8_t *pack;
+    int n_out, nsb, nsplit, sb_per_split;
+    float *part;
+    const float *da;
+    float *y;
+    int m, m_pad, ntt;
+    int *status;
+};
+
+// 32 lanes x N consecutive 32-bit columns, waited for
+template <int N>
+__device__ __forceinline__ void tmem_ld32x(uint32_t taddr, uint32_t (&v)[N]);
+template <>
+__device__ __forceinline__ void tmem_ld32x<16>(uint32_t taddr, uint32_t (&v)[16]) {
+    tmem_ld16(taddr, v);
+    tmem_wait_ld(v);
+}
+template <>
+__device__ __forceinline__ void tmem_ld32x<32>(uint32_t taddr, uint32_t (&v)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]),
+          "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),
+          "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+        : "r"(taddr));
+    asm volatile(
+        "tcgen05.wait::ld.sync.aligned;"
+        : "+r"(v[0]), "+r"(v[1]), "+r"(v[2]), "+r"(v[3]), "+r"(v[4]), "+r"(v[5]), "+r"(v[6]), "+r"(v[7]),
+          "+r"(v[8]), "+r"(v[9]), "+r"(v[10]), "+r"(v[11]), "+r"(v[12]), "+r"(v[13]), "+r"(v[14]), "+r"(v[15]),
+          "+r"(v[16]), "+r"(v[17]), "+r"(v[18]), "+r"(v[19]), "+r"(v[20]), "+r"(v[21]), "+r"(v[22]), "+r"(v[23]),
+          "+r"(v[24]), "+r"(v[25]), "+r"(v[26]), "+r"(v[27]), "+r"(v[28]), "+r"(v[29]), "+r"(v[30]), "+r"(v[31])
+        :: "memory");
+}
+
+template <uint32_t T, int BN>
+__global__ void __launch_bounds__(PK_WARPS * 32, 1)
+prefill_packed_kernel(const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmS,
+                      const PkParams p) {
+    using P = PkFmt<T>;
+    using Lay = PkLayout<T, BN>;
+    constexpr int KST = P::KSTEPS, S = Lay::STAGES;
+    constexpr int EPI_COLS = BN / 2;
+    constexpr uint32_t FULL = 0xffffffffu;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const uint32_t sb0 = smem_addr(smem);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int ntiles = (int)(gridDim.x / (unsigned)p.nsplit);
+    const int split = blockIdx.x / ntiles, tile = blockIdx.x - split * ntiles;
+    const int rt = tile / p.ntt, tt = tile - rt * p.ntt;
+    const int row0 = rt * PF_BM, tok0 = tt * BN;
+    const int rows = min(PF_BM, p.n_out - row0);
+    const int sbb = split * p.sb_per_split;
+    const int nsb = min(p.sb_per_split, p.nsb - sbb);
+    float *const yout = p.nsplit > 1 ? p.part + (size_t)split * p.m * p.n_out : p.y;
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + Lay::OFF_FLAGS);
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + Lay::OFF_FLAGS + 4);
+    const uint32_t barbase = sb0 + Lay::OFF_BAR;
+    auto bar = [&](int i) { return barbase + 8u * (uint32_t)i; };
+    // shared-memory pieces
+    auto stage_a = [&](int s) { return sb0 + (uint32_t)(s * Lay::STAGE); };
+    auto stage_b = [&](int s) { return sb0 + (uint32_t)(s * Lay::STAGE + PK_ATILE); };
+    auto meta = [&](int b) { return (uint32_t)(Lay::OFF_META + b * Lay::META); };   // offset from smem
+    constexpr int M_MIN = 0, M_B2 = Lay::META_MIN, M_F = M_B2 + Lay::META_B2, M_DA = M_F + PF_BM * 4;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < S; ++i) {
+            mbar_init(bar(PB_FULL + i), 1);
+            mbar_init(bar(PB_EMPTY + i), 1);
+        }
+        for (int i = 0; i < PK_NSB; ++i) {
+            mbar_init(bar(PB_META_FULL + i), 1);
+            mbar_init(bar(PB_META_FREE + i), PK_NEPI);
+            mbar_init(bar(PB_ACC_FULL + i), 1);
+            mbar_init(bar(PB_ACC_EMPTY + i), PK_NEPI);
+        }
+        mbar_init(bar(PB_DRAIN), 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1) tmem_alloc(smem_addr(tmem_slot), 2 * BN);
+    if (warp == 0 && lane == 0) {
+        tma_prefetch_map(&tmB);
+        if constexpr (P::MINS) tma_prefetch_map(&tmS);
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        // ---- loads ----
+        if (lane == 0) {
+            const uint8_t *chunks = p.pack + ((size_t)rt * p.nsb + sbb) * (size_t)pk_chunk<T>();
+            int t_issued = 0, sb_issued = 0;
+            for (int sb = 0; sb < nsb; ++sb) {
+                const int b = sb % PK_NSB;
+                const uint8_t *ck = chunks + (size_t)sb * pk_chunk<T>();
+                if (!pf_wait(bar(PB_META_FREE + b), ((sb / PK_NSB) & 1) ^ 1, abort_flag, p.status)) break;
+                const uint32_t mb = sb0 + meta(b);
+                mbar_expect_tx(bar(PB_META_FULL + b), (uint32_t)(Lay::META_MIN + Lay::META_B2 + PF_BM * 4 + BN * 4));
+                if constexpr (P::MINS) {
+                    bulk_g2s(mb + M_MIN, ck + pk_off_min<T>(), 2 * PK_MINT, bar(PB_META_FULL + b));
+                    tma_load_2d(mb + M_B2, &tmS, 16 * (sbb + sb), tok0, bar(PB_META_FULL + b));
+                }
+                bulk_g2s(mb + M_F, ck + pk_off_f<T>(), PF_BM * 4, bar(PB_META_FULL + b));
+                bulk_g2s(mb + M_DA, p.da + (size_t)(sbb + sb) * p.m_pad + tok0, BN * 4, bar(PB_META_FULL + b));
+                sb_issued = sb + 1;
+                bool ok = true;
+                for (int c = 0; c < KST; ++c) {
+                    const int t = KST * sb + c, s = t % S;
+                    const uint32_t use = (uint32_t)(t / S) & 1u;
+                    if (!pf_wait(bar(PB_EMPTY + s), use ^ 1, abort_flag, p.status)) { ok = false; break; }
+                    mbar_expect_tx(bar(PB_FULL + s), (uint32_t)(PK_ATILE + stage_bytes(BN)));
+                    bulk_g2s(stage_a(s), ck + (size_t)c * PK_ATILE, PK_ATILE, bar(PB_FULL + s));
+                    tma_load_2d(stage_b(s), &tmB, PF_KS * (KST * sbb + t), tok0, bar(PB_FULL + s));
+                    t_issued = t + 1;
+                }
+                if (!ok) break;
+            }
+            if (*abort_flag) {
+                for (int t = max(0, t_issued - S); t < t_issued; ++t) pf_settle(bar(PB_FULL + t % S), (t / S) & 1);
+                for (int sb = max(0, sb_issued - PK_NSB); sb < sb_issued; ++sb)
+                    pf_settle(bar(PB_META_FULL + sb % PK_NSB), (sb / PK_NSB) & 1);
+            }
+        }
+    } else if (warp == 1) {
+        // ---- MMA issue ----
+        if (lane == 0) {
+            constexpr uint32_t idesc = idesc_f16_f32(PF_BM, BN);
+            for (int sb = 0; sb < nsb; ++sb) {
+                const int buf = sb & 1;
+                const uint32_t ph = (sb >> 1) & 1;
+                if (!pf_wait<true>(bar(PB_ACC_EMPTY + buf), ph ^ 1, abort_flag, p.status)) break;
+                tc_fence_after();
+                const uint32_t dacc = tmem + (uint32_t)(buf * BN);
+                bool ok = true;
+                for (int c = 0; c < KST; ++c) {
+                    const int t = KST * sb + c, s = t % S;
+                    if (!pf_wait<true>(bar(PB_FULL + s), (uint32_t)(t / S) & 1u, abort_flag, p.status)) { ok = false; break; }
+                    tc_fence_after();
+#pragma unroll
+                    for (int kk = 0; kk < PF_KS / 16; ++kk)
+                        tc_mma_f16(dacc, smem_desc(stage_a(s) + 32 * kk, 1024, SMEM_SWZ_128B),
+                                   smem_desc(stage_b(s) + 32 * kk, 1024, SMEM_SWZ_128B), idesc, (c | kk) != 0);
+                    tc_commit(bar(PB_EMPTY + s));
+                }
+                if (!ok) break;
+                const int b = sb % PK_NSB;
+                if (!pf_wait<true>(bar(PB_META_FULL + b), (uint32_t)(sb / PK_NSB) & 1u, abort_flag, p.status)) break;
+                if constexpr (P::MINS) {
+                    // the mins term, into the same accumulator: -(hi + lo) x bsums
+                    tc_fence_after();
+                    const uint32_t mb = sb0 + meta(b);
+                    const uint64_t bd = smem_desc(mb + M_B2, 256, SMEM_SWZ_32B);
+                    tc_mma_f16(dacc, smem_desc(mb + M_MIN, 256, SMEM_SWZ_32B), bd, idesc, 1);
+                    tc_mma_f16(dacc, smem_desc(mb + M_MIN + PK_MINT, 256, SMEM_SWZ_32B), bd, idesc, 1);
+                }
+                tc_commit(bar(PB_ACC_FULL + buf));
+            }
+            if (*abort_flag) {
+                tc_commit(bar(PB_DRAIN));
+                pf_settle(bar(PB_DRAIN), 0);
+            }
+        }
+    } else {
+        // ---- epilogue: thread = tile row (tensor-memory lane), BN / 2 token columns ----
+        const int q = warp & 3;
+        const int c0 = ((warp - PK_EPI) >> 2) * EPI_COLS;
+        const int r = 32 * q + lane;
+        float acc[EPI_COLS];
+#pragma unroll
+        for (int j = 0; j < EPI_COLS; ++j) acc[j] = 0.0f;
+        bool ok = true;
+        for (int sb = 0; sb < nsb && ok; ++sb) {
+            const int buf = sb & 1, b = sb % PK_NSB;
+            if (!__all_sync(FULL, pf_wait(bar(PB_ACC_FULL + buf), (uint32_t)(sb >> 1) & 1u, abort_flag, p.status) &&
+                                      pf_wait(bar(PB_META_FULL + b), (uint32_t)(sb / PK_NSB) & 1u, abort_flag,
+                                              p.status))) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            const uint8_t *mp = smem + meta(b);
+            const float fr = reinterpret_cast<const float *>(mp + M_F)[r];
+            const float4 *da4 = reinterpret_cast<const float4 *>(mp + M_DA + c0 * 4);
+            const uint32_t ta = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(buf * BN + c0);
+            // 10 warps leave 168 registers a thread: 128 accumulators load 16 columns at a time
+            constexpr int LD = EPI_COLS > 64 ? 16 : 32;
+#pragma unroll
+            for (int cc = 0; cc < EPI_COLS / LD; ++cc) {
+                uint32_t v[LD];
+                tmem_ld32x<LD>(ta + LD * cc, v);
+#pragma unroll
+                for (int g4 = 0; g4 < LD / 4; ++g4) {
+                    const float4 d = da4[(LD / 4) * cc + g4];
+                    const float dv[4] = {d.x, d.y, d.z, d.w};
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const int j = LD * cc + 4 * g4 + e;
+                        acc[j] = fmaf(dv[e], fr * __uint_as_float(v[4 * g4 + e]), acc[j]);
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(bar(PB_ACC_EMPTY + buf));
+                mbar_arrive(bar(PB_META_FREE + b));
+            }
+        }
+        if (ok && !*abort_flag && r < rows) {
+            float *yr = yout + row0 + r;
+#pragma unroll
+            for (int j = 0; j < EPI_COLS; ++j)
+                if (tok0 + c0 + j < p.m) yr[(int64_t)(tok0 + c0 + j) * p.n_out] = acc[j];
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 2 * BN);
+    }
+}
+
 // Q8_K rows -> token operand for the MMAs: f16 quants with the slots of each
 // group of four holding elements 0, 2, 1, 3 (the order the weight converters
 // produce); for two-plane formats (Q6_K) each 64-element quarter is followed by
@@ -696,12 +1103,11 @@ size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 // tile costing ~2.5 us per super-block and traffic at ~5 TB/s (measured
 // orders of magnitude; only the comparison matters). The split changes only
 // the float order in which super-blocks are added.
-int split_count(int64_t n_in, int64_t n_out, int64_t m, int num_sms) {
-    const int64_t bn = m <= PF_BN_SMALL ? PF_BN_SMALL : PF_BN;
+int split_count_bn(int64_t n_in, int64_t n_out, int64_t m, int num_sms, int64_t bn, double us_per_sb) {
     const int64_t tiles = (n_out + PF_BM - 1) / PF_BM * ((m + bn - 1) / bn);
     const int64_t nsb = n_in / QK_K;
     if (num_sms <= 0 || tiles <= 0) return 1;
-    const double tile_us = 2.5 * (double)nsb;
+    const double tile_us = us_per_sb * (double)nsb;
     auto cost = [&](int s) {
         const double waves = (double)((tiles * s + num_sms - 1) / num_sms) / s;
         const double traffic_us = s > 1 ? (double)s * m * n_out * 8.0 / 5e6 : 0.0;
@@ -718,20 +1124,29 @@ int split_count(int64_t n_in, int64_t n_out, int64_t m, int num_sms) {
     }
     return best;
 }
+int split_count(int64_t n_in, int64_t n_out, int64_t m, int num_sms) {
+    return split_count_bn(n_in, n_out, m, num_sms, m <= PF_BN_SMALL ? PF_BN_SMALL : PF_BN, 2.5);
+}
+// the packed kernel's token tile and its time per super-block (MMA time of a
+// 128 x bn x 256 tile at ~60 % of the f16 rate; only the comparison matters)
+int pk_bn(int64_t m) { return m > PF_BN ? 256 : PF_BN; }
+double pk_us_per_sb(uint32_t wtype, int64_t bn) { return (bn == 256 ? 1.8 : 0.9) * (wtype == T_Q6_K ? 2.0 : 1.0); }
 
 struct WsParts {
     size_t b, s, da, pad, part;
 };
-WsParts ws_parts(uint32_t wtype, int64_t n_in, int64_t n_out, int64_t m, int num_sms) {
-    const int64_t m_pad = (m + PF_BN - 1) / PF_BN * PF_BN;
+WsParts ws_parts(uint32_t wtype, int64_t n_in, int64_t n_out, int64_t m, int num_sms, bool packed = false) {
+    const int64_t bn = packed ? pk_bn(m) : PF_BN;
+    const int64_t m_pad = (m + bn - 1) / bn * bn;
     const int planes = wtype == T_Q6_K ? 2 : 1;
     WsParts w{};
     w.b = align256((size_t)m_pad * n_in * 2 * planes);
     w.s = wtype == T_Q4_K ? align256((size_t)m_pad * (n_in / 16) * 2) : 0;
     w.da = align256((size_t)(n_in / QK_K) * m_pad * 4);
     const int64_t rb = n_in / QK_K * B_Q6_K;
-    w.pad = (wtype == T_Q6_K && rb % 16) ? align256((size_t)n_out * ((rb + 15) & ~int64_t(15))) : 0;
-    const int ns = split_count(n_in, n_out, m, num_sms);
+    w.pad = (!packed && wtype == T_Q6_K && rb % 16) ? align256((size_t)n_out * ((rb + 15) & ~int64_t(15))) : 0;
+    const int ns = packed ? split_count_bn(n_in, n_out, m, num_sms, bn, pk_us_per_sb(wtype, bn))
+                          : split_count(n_in, n_out, m, num_sms);
     w.part = ns > 1 ? align256((size_t)ns * m * n_out * 4) : 0;
     return w;
 }
@@ -808,20 +1223,108 @@ int launch_tb(const PrefillLaunch &L, cudaStream_t st) {
     return 0;
 }
 
+template <uint32_t T, int BN>
+int launch_packed_tb(const PrefillLaunch &L, cudaStream_t st) {
+    using P = PkFmt<T>;
+    using Lay = PkLayout<T, BN>;
+    const int64_t K = L.n_in, nsb = K / QK_K;
+    const int64_t m_pad = (L.m + BN - 1) / BN * BN;
+    const WsParts parts = ws_parts(T, L.n_in, L.n_out, L.m, L.num_sms, true);
+    uint8_t *ws = static_cast<uint8_t *>(L.ws);
+    uint16_t *B = reinterpret_cast<uint16_t *>(ws);
+    uint16_t *S = P::MINS ? reinterpret_cast<uint16_t *>(ws + parts.b) : nullptr;
+    float *DA = reinterpret_cast<float *>(ws + parts.b + parts.s);
+    prefill_prep_q8k<P::KSTEPS / 4><<<dim3((unsigned)nsb, (unsigned)m_pad), 64, 0, st>>>(
+        static_cast<const uint8_t *>(L.xq), (int)L.m, (int)nsb, (int)m_pad, B, S, DA);
+    if (cudaGetLastError() != cudaSuccess) return -2;
+    CUtensorMap tmB, tmS;
+    if (!make_map(&tmB, B, (uint64_t)(K * P::KSTEPS / 4), (uint64_t)m_pad, (uint64_t)(K * P::KSTEPS / 4) * 2, PF_KS,
+                  BN, CU_TENSOR_MAP_SWIZZLE_128B, 2))
+        return -4;
+    if (P::MINS) {
+        if (!make_map(&tmS, S, (uint64_t)(K / 16), (uint64_t)m_pad, (uint64_t)(K / 16) * 2, 16, BN,
+                      CU_TENSOR_MAP_SWIZZLE_32B, 2))
+            return -4;
+    } else {
+        tmS = tmB;   // unused
+    }
+    static bool attr_set[64] = {};
+    const int dev = L.device & 63;
+    if (!attr_set[dev]) {
+        cudaFuncSetAttribute(prefill_packed_kernel<T, BN>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+        if (cudaFuncSetAttribute(prefill_packed_kernel<T, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 Lay::SMEM) != cudaSuccess)
+            return -2;
+        attr_set[dev] = true;
+    }
+    PkParams p{};
+    p.pack = static_cast<const uint8_t *>(L.pack);
+    p.n_out = (int)L.n_out;
+    p.nsb = (int)nsb;
+    p.da = DA;
+    p.y = L.y;
+    p.m = (int)L.m;
+    p.m_pad = (int)m_pad;
+    p.ntt = (int)(m_pad / BN);
+    p.status = L.status;
+    p.nsplit = split_count_bn(L.n_in, L.n_out, L.m, L.num_sms, BN, pk_us_per_sb(T, BN));
+    p.sb_per_split = (int)((nsb + p.nsplit - 1) / p.nsplit);
+    p.nsplit = (int)((nsb + p.sb_per_split - 1) / p.sb_per_split);   // no empty range
+    p.part = p.nsplit > 1 ? reinterpret_cast<float *>(ws + parts.b + parts.s + parts.da + parts.pad) : nullptr;
+    const int64_t tiles = (L.n_out + PF_BM - 1) / PF_BM * p.ntt;
+    prefill_packed_kernel<T, BN><<<(unsigned)(tiles * p.nsplit), PK_WARPS * 32, Lay::SMEM, st>>>(tmB, tmS, p);
+    if (cudaGetLastError() != cudaSuccess) return -2;
+    if (p.nsplit > 1) {
+        const int64_t n = L.m * L.n_out;
+        const int64_t blocks = (n + 255) / 256 < 4 * L.num_sms ? (n + 255) / 256 : 4 * L.num_sms;
+        prefill_sum_splits<<<(unsigned)blocks, 256, 0, st>>>(p.part, p.nsplit, n, L.y);
+        if (cudaGetLastError() != cudaSuccess) return -2;
+    }
+    return 0;
+}
+
 // blocks of up to 32 tokens (batched decode) use 32-token tiles: the weights
 // still stream once per token tile, with a quarter of the token-operand traffic
 template <uint32_t T>
 int launch_t(const PrefillLaunch &L, cudaStream_t st) {
+    if (L.pack && L.m > PF_BN_SMALL)
+        return pk_bn(L.m) == 256 ? launch_packed_tb<T, 256>(L, st) : launch_packed_tb<T, PF_BN>(L, st);
     return L.m <= PF_BN_SMALL ? launch_tb<T, PF_BN_SMALL>(L, st) : launch_tb<T, PF_BN>(L, st);
+}
+
+template <uint32_t T>
+int launch_pack_t(const void *w, int64_t n_in, int64_t n_out, void *pack, cudaStream_t st) {
+    const int64_t nsb = n_in / QK_K, nrt = (n_out + PF_BM - 1) / PF_BM;
+    const int64_t row_bytes = nsb * (T == T_Q4_K ? B_Q4_K : B_Q6_K);
+    prefill_pack_kernel<T><<<dim3((unsigned)nrt, (unsigned)nsb), PF_BM, 0, st>>>(
+        static_cast<const uint8_t *>(w), row_bytes, (int)n_out, (int)nsb, static_cast<uint8_t *>(pack));
+    return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }
 
 }  // namespace
 
 bool prefill_supported(uint32_t wtype) { return wtype == T_Q4_K || wtype == T_Q6_K; }
 
-size_t prefill_workspace_bytes(uint32_t wtype, int64_t n_in, int64_t n_out, int64_t m, int num_sms) {
-    const WsParts w = ws_parts(wtype, n_in, n_out, m, num_sms);
+size_t prefill_workspace_bytes(uint32_t wtype, int64_t n_in, int64_t n_out, int64_t m, int num_sms, bool packed) {
+    const WsParts w = ws_parts(wtype, n_in, n_out, m, num_sms, packed && m > PF_BN_SMALL);
     return w.b + w.s + w.da + w.pad + w.part;
+}
+
+size_t prefill_pack_bytes(uint32_t wtype, int64_t n_in, int64_t n_out) {
+    const int64_t nsb = n_in / QK_K, nrt = (n_out + PF_BM - 1) / PF_BM;
+    switch (wtype) {
+        case T_Q4_K: return (size_t)(nrt * nsb) * (size_t)pk_chunk<T_Q4_K>();
+        case T_Q6_K: return (size_t)(nrt * nsb) * (size_t)pk_chunk<T_Q6_K>();
+        default: return 0;
+    }
+}
+
+int launch_prefill_pack(uint32_t wtype, const void *w, int64_t n_in, int64_t n_out, void *pack, cudaStream_t st) {
+    switch (wtype) {
+        case T_Q4_K: return launch_pack_t<T_Q4_K>(w, n_in, n_out, pack, st);
+        case T_Q6_K: return launch_pack_t<T_Q6_K>(w, n_in, n_out, pack, st);
+        default: return -3;
+    }
 }
 
 int launch_prefill(uint32_t wtype, const PrefillLaunch &L, cudaStream_t st) {

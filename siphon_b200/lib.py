@@ -53,6 +53,10 @@ SIGNATURES = {
     "sicu_row_to_f32": [_u32, _vp, _i64, C.POINTER(C.c_int64), _i64, _fp, _vp],
     "sicu_gemm_prefill": [_u32, _vp, _i64, _i64, _vp, _i64, _fp, _vp],
     "sicu_gemm_prefill_f32": [_u32, _vp, _i64, _i64, _fp, _i64, _fp, _vp],
+    "sicu_prefill_pack_bytes": [_u32, _i64, _i64, C.POINTER(C.c_size_t)],
+    "sicu_prefill_pack": [_u32, _vp, _i64, _i64, _vp, C.c_size_t, _vp],
+    "sicu_gemm_prefill_packed": [_u32, _vp, _vp, _i64, _i64, _vp, _i64, _fp, _vp],
+    "sicu_gemm_prefill_packed_f32": [_u32, _vp, _vp, _i64, _i64, _fp, _i64, _fp, _vp],
     "sicu_ar_create": [C.c_int, C.c_int, _i64, C.POINTER(C.c_void_p), _vp],
     "sicu_ar_open": [_vp, _vp],
     "sicu_ar_set_timeout": [_vp, C.c_uint64],
@@ -215,6 +219,24 @@ class SiphonCuda:
 
     def gemm_prefill_f32(self, wtype: int, dw, n_in: int, n_out: int, dx, m: int, dy, stream=None) -> None:
         self.check(self.lib.sicu_gemm_prefill_f32(wtype, _ptr(dw), n_in, n_out, _ptr(dx), m, _ptr(dy), _ptr(stream)))
+
+    # -- prefill copies of the weights -------------------------------------------------
+    def prefill_pack_bytes(self, wtype: int, n_in: int, n_out: int) -> int:
+        n = C.c_size_t(0)
+        self.check(self.lib.sicu_prefill_pack_bytes(wtype, n_in, n_out, C.byref(n)))
+        return n.value
+
+    def prefill_pack(self, wtype: int, dw, n_in: int, n_out: int, dpack, pack_bytes: int, stream=None) -> None:
+        self.check(self.lib.sicu_prefill_pack(wtype, _ptr(dw), n_in, n_out, _ptr(dpack), pack_bytes, _ptr(stream)))
+
+    def gemm_prefill_packed(self, wtype: int, dw, dpack, n_in: int, n_out: int, dxq, m: int, dy, stream=None) -> None:
+        self.check(self.lib.sicu_gemm_prefill_packed(wtype, _ptr(dw), _ptr(dpack), n_in, n_out, _ptr(dxq), m,
+                                                     _ptr(dy), _ptr(stream)))
+
+    def gemm_prefill_packed_f32(self, wtype: int, dw, dpack, n_in: int, n_out: int, dx, m: int, dy,
+                                stream=None) -> None:
+        self.check(self.lib.sicu_gemm_prefill_packed_f32(wtype, _ptr(dw), _ptr(dpack), n_in, n_out, _ptr(dx), m,
+                                                         _ptr(dy), _ptr(stream)))
 
     # -- fused all-reduce groups ---------------------------------------------------
     def ar_create(self, n_ranks: int, rank: int, length: int) -> "ArGroup":

@@ -162,7 +162,7 @@ class MatrixPath:
 
     def __init__(self, sicu, sh: LlamaShape, device, world: int = 1, rank: int = 0, group=None, seed: int = 0,
                  max_tokens: int = 1, fused: bool = False, steps: bool = False, attention: bool = False,
-                 n_ctx: int = 256, embed: bool = False, gguf_path=None):
+                 n_ctx: int = 256, embed: bool = False, gguf_path=None, packed: bool = False):
         import numpy as np
         import torch
         self.s, self.sh, self.dev, self.world, self.group = sicu, sh, device, world, group
@@ -203,6 +203,21 @@ class MatrixPath:
             self.head = from_file("output.weight", n_out, n_in)
         else:
             self.head = (Q.Q6_K, device_weights(Q.Q6_K, n_out, n_in, seed * 7919 + 999 + 1000 * rank, device))
+        # prefill copies (sicu_prefill_pack) of the Q4_K / Q6_K matrices, made
+        # once here beside the raw blocks
+        self.pack = {}
+        if packed:
+            mats = [((il, name), lay[name]) for il, lay in enumerate(self.layers) for name in lay]
+            mats.append((("head",), self.head))
+            for key, (t, w) in mats:
+                if t not in (Q.Q4_K, Q.Q6_K):
+                    continue
+                n_out, n_in = self.shapes[key[-1]]
+                nb = sicu.prefill_pack_bytes(t, n_in, n_out)
+                buf = torch.empty(nb, dtype=torch.uint8, device=device)
+                sicu.prefill_pack(t, w, n_in, n_out, buf, nb)
+                self.pack[key] = buf
+            torch.cuda.synchronize(device)
         m = max_tokens
         gen = torch.Generator(device=device)
         gen.manual_seed(seed + 17)
@@ -471,13 +486,21 @@ class MatrixPath:
         s, h, y = self.s, stream.cuda_stream, self.y
         d = self.sh.n_embd
         nq, nkv, nff = self.shapes["q"][0], self.shapes["k"][0], self.shapes["gate"][0]
-        for lay in self.layers:
+        for il, lay in enumerate(self.layers):
             for name, n_in, xin in (("q", d, self.x_model), ("k", d, self.x_model), ("v", d, self.x_model),
                                     ("o", nq, self.x_attn), ("gate", d, self.x_model), ("up", d, self.x_model),
                                     ("down", nff, self.x_ff)):
                 t, w = lay[name]
-                s.gemm_prefill_f32(t, w, n_in, self.shapes[name][0], xin, m, y[name], stream=h)
+                pk = self.pack.get((il, name))
+                if pk is not None:
+                    s.gemm_prefill_packed_f32(t, w, pk, n_in, self.shapes[name][0], xin, m, y[name], stream=h)
+                else:
+                    s.gemm_prefill_f32(t, w, n_in, self.shapes[name][0], xin, m, y[name], stream=h)
                 if name in ("o", "down"):
                     self._allreduce(y[name][:m])
         th, wh = self.head
-        s.gemm_prefill_f32(th, wh, d, self.shapes["head"][0], self.x_model, m, y["head"], stream=h)
+        pk = self.pack.get(("head",))
+        if pk is not None:
+            s.gemm_prefill_packed_f32(th, wh, pk, d, self.shapes["head"][0], self.x_model, m, y["head"], stream=h)
+        else:
+            s.gemm_prefill_f32(th, wh, d, self.shapes["head"][0], self.x_model, m, y["head"], stream=h)

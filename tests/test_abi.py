@@ -149,3 +149,22 @@ def test_softmax_checks_run_on_host(so):
     assert "overlap" in so.last_error()
     assert so.lib.sicu_softmax(0x10000, 0x10000, 16, 1, None) == L.SICU_EINVAL     # in place: needs a device
     assert "sicu_init" in so.last_error()
+
+
+def test_prefill_copy_size_and_checks_run_on_host(so):
+    """The size of a prefill weight copy needs no GPU: per 128-row tile and
+    super-block 4 x 16 KiB of f16 operands + 8 KiB of mins + 512 B of row
+    scales (Q4_K), 8 x 16 KiB + 512 B (Q6_K)."""
+    assert so.prefill_pack_bytes(Q.Q4_K, 4096, 4096) == 32 * 16 * (4 * 16384 + 8192 + 512)
+    assert so.prefill_pack_bytes(Q.Q6_K, 1280, 130) == 2 * 5 * (8 * 16384 + 512)
+    assert so.prefill_pack_bytes(Q.Q4_K, 256, 0) == 0
+    n = C.c_size_t(7)
+    assert so.lib.sicu_prefill_pack_bytes(Q.Q8_0, 256, 128, C.byref(n)) == L.SICU_ENOTSUP and n.value == 0
+    assert so.lib.sicu_prefill_pack_bytes(Q.Q4_K, 300, 128, C.byref(n)) == L.SICU_EINVAL
+    need = so.prefill_pack_bytes(Q.Q4_K, 256, 128)
+    assert so.lib.sicu_prefill_pack(Q.Q4_K, 16, 256, 128, 32, need - 1, None) == L.SICU_EINVAL
+    assert so.lib.sicu_prefill_pack(Q.Q4_K, 24, 256, 128, 32, need, None) == L.SICU_EINVAL   # misaligned
+    assert so.lib.sicu_prefill_pack(Q.Q4_K, 16, 256, 128, 32, need, None) == L.SICU_EINVAL   # not initialised
+    assert "sicu_init" in so.last_error()
+    # a copy given for a type without one
+    assert so.lib.sicu_gemm_prefill_packed_f32(Q.Q8_0, 16, 32, 256, 128, 64, 64, 128, None) == L.SICU_EINVAL

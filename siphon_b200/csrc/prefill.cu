@@ -1008,6 +1008,280 @@ prefill_packed_kernel(const __grid_constant__ CUtensorMap tmB, const __grid_cons
     }
 }
 
+// ---- prefill from the packed copy on CTA pairs ------------------------------------------
+// A cluster of two CTAs (two SMs) computes a 256-row x BN-token tile with
+// M = 256 MMAs (cta_group::2): CTA r holds weight rows 128 r .. 128 r + 127 of
+// the tile (its own 128-row tile's chunks of the prefill copy: the A operand)
+// and tokens BN/2 r .. BN/2 r + BN/2 - 1 of the token operand (B); the MMAs
+// read both CTAs' shared memory and leave each CTA's 128 rows x BN tokens in
+// its own tensor memory. Per K-step an SM loads 16 KB of weights and BN x 64
+// bytes of tokens: half the token bytes of the one-CTA tile for the same MMA
+// work per SM, and shallower stages, so more of them fit.
+//   warp 0     K-step loads, in both CTAs: the A tile and B half of each
+//              K-step by TMA, completion counted on the leader's barrier (the
+//              leader expects both CTAs' bytes)
+//   warp 10    super-block loads, in both CTAs: the mins / bsums halves the
+//              same way; row scales and token scales into its own CTA for its
+//              epilogue (a separate warp, so the K-step ring never waits for
+//              an epilogue to free a super-block buffer)
+//   warp 1     tensor-memory owner in both; lane 0 of the leader (cluster
+//              rank 0) issues the MMAs and commits to both CTAs' barriers
+//   warps 2-9  epilogue in both, as in prefill_packed_kernel; the arrival
+//              that frees an accumulator goes to the leader
+// The loaders and the epilogue poll their barriers rather than suspending:
+// a suspended wait measured ~1 us late waking, longer than a K-step.
+// A pair whose second row tile lies past the matrix loads zeros for it (the
+// tensor map's fill) and stores nothing for those rows.
+constexpr int PP_NSB = 2, PP_WARPS = 11, PP_W_META = 10;
+template <uint32_t T, int BN> struct PpLayout {
+    using P = PkFmt<T>;
+    static constexpr int HB = BN / 2;                              // tokens per CTA in B
+    static constexpr int BHALF = HB * PF_KS * 2;                   // B bytes per CTA and K-step
+    static constexpr int STAGE = PK_ATILE + BHALF;
+    static constexpr int META_MIN = P::MINS ? 2 * PK_MINT : 0;     // mins operand hi + lo (A side)
+    static constexpr int META_B2 = P::MINS ? HB * 16 * 2 : 0;      // bsums half (B side)
+    static constexpr int META = (META_MIN + META_B2 + PF_BM * 4 + BN * 4 + 1023) & ~1023;
+    static constexpr int BUDGET = 227 * 1024 - 2048;               // barriers, flags, alignment slack
+    static constexpr int NS = (BUDGET - PP_NSB * META) / STAGE;
+    static constexpr int STAGES = NS > 8 ? 8 : NS;
+    static constexpr int OFF_META = STAGES * STAGE;
+    static constexpr int OFF_BAR = OFF_META + PP_NSB * META;
+    static constexpr int OFF_FLAGS = OFF_BAR + 8 * 32;
+    static constexpr int SMEM = OFF_FLAGS + 16 + 1024;
+    static_assert(STAGES >= 3, "shared memory");
+    static_assert(SMEM <= 227 * 1024, "shared memory");
+    static_assert(STAGE % 1024 == 0 && META % 1024 == 0, "swizzle atoms stay 1024-byte aligned");
+};
+enum {
+    PP_FULL = 0,           // [8] leader: A tiles + B halves of both CTAs landed (bytes)
+    PP_EMPTY = 8,          // [8] both: stage consumed by the pair's MMAs (multicast commit)
+    PP_MMETA = 16,         // [2] leader: mins + bsums halves of both CTAs landed (bytes)
+    PP_EMETA = 18,         // [2] own: row scales + token scales landed (bytes)
+    PP_META_FREE = 20,     // [2] own epilogue done with a super-block buffer (8 warps)
+    PP_ACC_FULL = 22,      // [2] both: accumulator of a super-block ready (multicast commit)
+    PP_ACC_EMPTY = 24,     // [2] leader: accumulator drained by both epilogues (16 warps)
+    PP_DRAIN = 26,
+    PP_NBARS = 27,
+};
+static_assert(PP_NBARS <= 32, "barrier area");
+
+template <uint32_t T, int BN>
+__global__ void __launch_bounds__(PP_WARPS * 32, 1)
+prefill_pair_kernel(const __grid_constant__ CUtensorMap tmP, const __grid_constant__ CUtensorMap tmM,
+                    const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmS,
+                    const PkParams p) {
+    using P = PkFmt<T>;
+    using Lay = PpLayout<T, BN>;
+    constexpr int KST = P::KSTEPS, S = Lay::STAGES, HB = Lay::HB;
+    constexpr int CH = pk_chunk<T>() / 128;   // 128-byte rows per chunk of the prefill copy
+    constexpr int EPI_COLS = BN / 2;
+    constexpr uint32_t FULL = 0xffffffffu;
+    static_assert(pk_chunk<T>() % 128 == 0, "chunks are whole 128-byte rows of the copy's tensor map");
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const uint32_t sb0 = smem_addr(smem);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_rank();
+    const bool leader = rank == 0;
+    const int pair = (int)(blockIdx.x >> 1);
+    const int ntiles = (int)(gridDim.x >> 1) / p.nsplit;
+    const int split = pair / ntiles, tile = pair - split * ntiles;
+    const int prt = tile / p.ntt, tt = tile - prt * p.ntt;
+    const int rt = 2 * prt + (int)rank;                  // this CTA's 128-row tile
+    const int nrt = (p.n_out + PF_BM - 1) / PF_BM;
+    const bool has_rows = rt < nrt;
+    const int row0 = rt * PF_BM, tok0 = tt * BN;
+    const int rows = has_rows ? min(PF_BM, p.n_out - row0) : 0;
+    const int sbb = split * p.sb_per_split;
+    const int nsb = min(p.sb_per_split, p.nsb - sbb);
+    float *const yout = p.nsplit > 1 ? p.part + (size_t)split * p.m * p.n_out : p.y;
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + Lay::OFF_FLAGS);
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + Lay::OFF_FLAGS + 4);
+    const uint32_t barbase = sb0 + Lay::OFF_BAR;
+    auto bar = [&](int i) { return barbase + 8u * (uint32_t)i; };
+    auto lbar = [&](int i) { return mapa(bar(i), 0); };   // the leader's barrier (shared::cluster)
+    auto stage_a = [&](int s) { return sb0 + (uint32_t)(s * Lay::STAGE); };
+    auto stage_b = [&](int s) { return sb0 + (uint32_t)(s * Lay::STAGE + PK_ATILE); };
+    auto meta = [&](int b) { return (uint32_t)(Lay::OFF_META + b * Lay::META); };   // offset from smem
+    constexpr int M_MIN = 0, M_B2 = Lay::META_MIN, M_F = M_B2 + Lay::META_B2, M_DA = M_F + PF_BM * 4;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < S; ++i) {
+            mbar_init(bar(PP_FULL + i), 1);
+            mbar_init(bar(PP_EMPTY + i), 1);
+        }
+        for (int i = 0; i < PP_NSB; ++i) {
+            mbar_init(bar(PP_MMETA + i), 1);
+            mbar_init(bar(PP_EMETA + i), 1);
+            mbar_init(bar(PP_META_FREE + i), PK_NEPI);
+            mbar_init(bar(PP_ACC_FULL + i), 1);
+            mbar_init(bar(PP_ACC_EMPTY + i), 2 * PK_NEPI);
+        }
+        mbar_init(bar(PP_DRAIN), 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1) tmem_alloc_pair(smem_addr(tmem_slot), 2 * BN);
+    if (warp == 0 && lane == 0) {
+        tma_prefetch_map(&tmP);
+        tma_prefetch_map(&tmB);
+        if constexpr (P::MINS) {
+            tma_prefetch_map(&tmM);
+            tma_prefetch_map(&tmS);
+        }
+    }
+    __syncwarp();
+    tc_fence_before();
+    cluster_sync();       // both CTAs' barriers initialised and tensor memory allocated
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        // ---- K-step loads (both CTAs) ----
+        if (lane == 0) {
+            const int64_t chunk0 = (int64_t)rt * p.nsb + sbb;    // this CTA's first chunk of the copy
+            for (int t = 0; t < KST * nsb; ++t) {
+                const int sb = t / KST, c = t - sb * KST, s = t % S;
+                // past the copy's end for a pair's missing row tile: zeros
+                const int crow = (int)((chunk0 + sb) * CH);
+                if (!pf_wait<true>(bar(PP_EMPTY + s), ((uint32_t)(t / S) & 1u) ^ 1u, abort_flag, p.status)) break;
+                if (leader) mbar_expect_tx(bar(PP_FULL + s), 2u * (uint32_t)Lay::STAGE);
+                tma_load_2d_pair(stage_a(s), &tmP, 0, crow + c * 128, lbar(PP_FULL + s));
+                tma_load_2d_pair(stage_b(s), &tmB, PF_KS * (KST * sbb + t), tok0 + (int)rank * HB, lbar(PP_FULL + s));
+            }
+        }
+    } else if (warp == PP_W_META) {
+        // ---- super-block loads (both CTAs) ----
+        if (lane == 0) {
+            const int64_t chunk0 = (int64_t)rt * p.nsb + sbb;
+            for (int sb = 0; sb < nsb; ++sb) {
+                const int b = sb % PP_NSB;
+                if (!pf_wait<true>(bar(PP_META_FREE + b), ((sb / PP_NSB) & 1) ^ 1, abort_flag, p.status)) break;
+                const uint32_t mb = sb0 + meta(b);
+                if constexpr (P::MINS) {
+                    const int crow = (int)((chunk0 + sb) * CH);
+                    if (leader) mbar_expect_tx(bar(PP_MMETA + b), 2u * (uint32_t)(Lay::META_MIN + Lay::META_B2));
+                    tma_load_2d_pair(mb + M_MIN, &tmM, 0, crow + KST * 128, lbar(PP_MMETA + b));
+                    tma_load_2d_pair(mb + M_B2, &tmS, 16 * (sbb + sb), tok0 + (int)rank * HB, lbar(PP_MMETA + b));
+                }
+                mbar_expect_tx(bar(PP_EMETA + b), (uint32_t)((has_rows ? PF_BM * 4 : 0) + BN * 4));
+                if (has_rows)
+                    bulk_g2s(mb + M_F, p.pack + (size_t)(chunk0 + sb) * pk_chunk<T>() + pk_off_f<T>(), PF_BM * 4,
+                             bar(PP_EMETA + b));
+                bulk_g2s(mb + M_DA, p.da + (size_t)(sbb + sb) * p.m_pad + tok0, BN * 4, bar(PP_EMETA + b));
+            }
+        }
+    } else if (warp == 1) {
+        // ---- MMA issue (leader) ----
+        if (leader && lane == 0) {
+            constexpr uint32_t idesc = idesc_f16_f32(2 * PF_BM, BN);
+            for (int sb = 0; sb < nsb; ++sb) {
+                const int buf = sb & 1;
+                if (!pf_wait<true>(bar(PP_ACC_EMPTY + buf), ((uint32_t)(sb >> 1) & 1u) ^ 1u, abort_flag, p.status))
+                    break;
+                tc_fence_after();
+                const uint32_t dacc = tmem + (uint32_t)(buf * BN);
+                bool ok = true;
+                for (int c = 0; c < KST; ++c) {
+                    const int t = KST * sb + c, s = t % S;
+                    if (!pf_wait<true>(bar(PP_FULL + s), (uint32_t)(t / S) & 1u, abort_flag, p.status)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+#pragma unroll
+                    for (int kk = 0; kk < PF_KS / 16; ++kk)
+                        tc_mma_f16_pair(dacc, smem_desc(stage_a(s) + 32 * kk, 1024, SMEM_SWZ_128B),
+                                        smem_desc(stage_b(s) + 32 * kk, 1024, SMEM_SWZ_128B), idesc, (c | kk) != 0);
+                    tc_commit_pair(bar(PP_EMPTY + s), 3);
+                }
+                if (!ok) break;
+                if constexpr (P::MINS) {
+                    // the mins term, into the same accumulator: -(hi + lo) x bsums
+                    const int b = sb % PP_NSB;
+                    if (!pf_wait<true>(bar(PP_MMETA + b), (uint32_t)(sb / PP_NSB) & 1u, abort_flag, p.status)) break;
+                    tc_fence_after();
+                    const uint32_t mb = sb0 + meta(b);
+                    const uint64_t bd = smem_desc(mb + M_B2, 256, SMEM_SWZ_32B);
+                    tc_mma_f16_pair(dacc, smem_desc(mb + M_MIN, 256, SMEM_SWZ_32B), bd, idesc, 1);
+                    tc_mma_f16_pair(dacc, smem_desc(mb + M_MIN + PK_MINT, 256, SMEM_SWZ_32B), bd, idesc, 1);
+                }
+                tc_commit_pair(bar(PP_ACC_FULL + buf), 3);
+            }
+            if (*abort_flag) {
+                tc_commit_pair(bar(PP_DRAIN), 1);
+                pf_settle(bar(PP_DRAIN), 0);
+            }
+        }
+    } else {
+        // ---- epilogue (both): thread = tile row (tensor-memory lane), BN / 2 token columns ----
+        const int q = warp & 3;
+        const int c0 = ((warp - PK_EPI) >> 2) * EPI_COLS;
+        const int r = 32 * q + lane;
+        float acc[EPI_COLS];
+#pragma unroll
+        for (int j = 0; j < EPI_COLS; ++j) acc[j] = 0.0f;
+        bool ok = true;
+        for (int sb = 0; sb < nsb && ok; ++sb) {
+            const int buf = sb & 1, b = sb % PP_NSB;
+            if (!__all_sync(FULL, pf_wait<true>(bar(PP_ACC_FULL + buf), (uint32_t)(sb >> 1) & 1u, abort_flag,
+                                                p.status) &&
+                                      pf_wait<true>(bar(PP_EMETA + b), (uint32_t)(sb / PP_NSB) & 1u, abort_flag,
+                                                    p.status))) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            const uint8_t *mp = smem + meta(b);
+            const float fr = reinterpret_cast<const float *>(mp + M_F)[r];
+            const float4 *da4 = reinterpret_cast<const float4 *>(mp + M_DA + c0 * 4);
+            const uint32_t ta = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(buf * BN + c0);
+            constexpr int LD = EPI_COLS > 64 ? 16 : 32;
+#pragma unroll
+            for (int cc = 0; cc < EPI_COLS / LD; ++cc) {
+                uint32_t v[LD];
+                tmem_ld32x<LD>(ta + LD * cc, v);
+#pragma unroll
+                for (int g4 = 0; g4 < LD / 4; ++g4) {
+                    const float4 d = da4[(LD / 4) * cc + g4];
+                    const float dv[4] = {d.x, d.y, d.z, d.w};
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const int j = LD * cc + 4 * g4 + e;
+                        acc[j] = fmaf(dv[e], fr * __uint_as_float(v[4 * g4 + e]), acc[j]);
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive_remote(lbar(PP_ACC_EMPTY + buf));
+                mbar_arrive(bar(PP_META_FREE + b));
+            }
+        }
+        if (ok && !*abort_flag && r < rows) {
+            float *yr = yout + row0 + r;
+#pragma unroll
+            for (int j = 0; j < EPI_COLS; ++j)
+                if (tok0 + c0 + j < p.m) yr[(int64_t)(tok0 + c0 + j) * p.n_out] = acc[j];
+        }
+    }
+
+    if (*abort_flag && (warp == 0 || warp == PP_W_META) && lane == 0) {
+        // let copies still in flight land before the CTA's shared memory goes away
+        const uint64_t t0 = globaltimer_ns();
+        while (globaltimer_ns() - t0 < 1000000ull) {
+        }
+    }
+    __syncwarp();
+    tc_fence_before();
+    cluster_sync();       // the pair's MMAs and remote arrivals are done
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc_pair(tmem, 2 * BN);
+    }
+}
+
 // Q8_K rows -> token operand for the MMAs: f16 quants with the slots of each
 // group of four holding elements 0, 2, 1, 3 (the order the weight converters
 // produce); for two-plane formats (Q6_K) each 64-element quarter is followed by
@@ -1103,13 +1377,11 @@ size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 // tile costing ~2.5 us per super-block and traffic at ~5 TB/s (measured
 // orders of magnitude; only the comparison matters). The split changes only
 // the float order in which super-blocks are added.
-int split_count_bn(int64_t n_in, int64_t n_out, int64_t m, int num_sms, int64_t bn, double us_per_sb) {
-    const int64_t tiles = (n_out + PF_BM - 1) / PF_BM * ((m + bn - 1) / bn);
-    const int64_t nsb = n_in / QK_K;
-    if (num_sms <= 0 || tiles <= 0) return 1;
+int split_count_tiles(int64_t tiles, int64_t nsb, int64_t m, int64_t n_out, int slots, double us_per_sb) {
+    if (slots <= 0 || tiles <= 0) return 1;
     const double tile_us = us_per_sb * (double)nsb;
     auto cost = [&](int s) {
-        const double waves = (double)((tiles * s + num_sms - 1) / num_sms) / s;
+        const double waves = (double)((tiles * s + slots - 1) / slots) / s;
         const double traffic_us = s > 1 ? (double)s * m * n_out * 8.0 / 5e6 : 0.0;
         return waves * tile_us + traffic_us;
     };
@@ -1124,6 +1396,10 @@ int split_count_bn(int64_t n_in, int64_t n_out, int64_t m, int num_sms, int64_t 
     }
     return best;
 }
+int split_count_bn(int64_t n_in, int64_t n_out, int64_t m, int num_sms, int64_t bn, double us_per_sb) {
+    const int64_t tiles = (n_out + PF_BM - 1) / PF_BM * ((m + bn - 1) / bn);
+    return split_count_tiles(tiles, n_in / QK_K, m, n_out, num_sms, us_per_sb);
+}
 int split_count(int64_t n_in, int64_t n_out, int64_t m, int num_sms) {
     return split_count_bn(n_in, n_out, m, num_sms, m <= PF_BN_SMALL ? PF_BN_SMALL : PF_BN, 2.5);
 }
@@ -1131,6 +1407,13 @@ int split_count(int64_t n_in, int64_t n_out, int64_t m, int num_sms) {
 // 128 x bn x 256 tile at ~60 % of the f16 rate; only the comparison matters)
 int pk_bn(int64_t m) { return m > PF_BN ? 256 : PF_BN; }
 double pk_us_per_sb(uint32_t wtype, int64_t bn) { return (bn == 256 ? 1.8 : 0.9) * (wtype == T_Q6_K ? 2.0 : 1.0); }
+// Products of at least two 128-row tiles run on CTA pairs (one 256-row tile
+// per pair, 2 SMs); a pair's time per super-block is the one-CTA tile's.
+bool use_pair(int64_t n_out) { return (n_out + PF_BM - 1) / PF_BM >= 2; }
+int pair_splits(uint32_t wtype, int64_t n_in, int64_t n_out, int64_t m, int num_sms, int64_t bn) {
+    const int64_t tiles = ((n_out + PF_BM - 1) / PF_BM + 1) / 2 * ((m + bn - 1) / bn);
+    return split_count_tiles(tiles, n_in / QK_K, m, n_out, num_sms / 2, pk_us_per_sb(wtype, bn));
+}
 
 struct WsParts {
     size_t b, s, da, pad, part;
@@ -1145,8 +1428,9 @@ WsParts ws_parts(uint32_t wtype, int64_t n_in, int64_t n_out, int64_t m, int num
     w.da = align256((size_t)(n_in / QK_K) * m_pad * 4);
     const int64_t rb = n_in / QK_K * B_Q6_K;
     w.pad = (!packed && wtype == T_Q6_K && rb % 16) ? align256((size_t)n_out * ((rb + 15) & ~int64_t(15))) : 0;
-    const int ns = packed ? split_count_bn(n_in, n_out, m, num_sms, bn, pk_us_per_sb(wtype, bn))
-                          : split_count(n_in, n_out, m, num_sms);
+    const int ns = !packed ? split_count(n_in, n_out, m, num_sms)
+                 : use_pair(n_out) ? pair_splits(wtype, n_in, n_out, m, num_sms, bn)
+                                   : split_count_bn(n_in, n_out, m, num_sms, bn, pk_us_per_sb(wtype, bn));
     w.part = ns > 1 ? align256((size_t)ns * m * n_out * 4) : 0;
     return w;
 }
@@ -1283,12 +1567,92 @@ int launch_packed_tb(const PrefillLaunch &L, cudaStream_t st) {
     return 0;
 }
 
+template <uint32_t T, int BN>
+int launch_pair_tb(const PrefillLaunch &L, cudaStream_t st) {
+    using P = PkFmt<T>;
+    using Lay = PpLayout<T, BN>;
+    const int64_t K = L.n_in, nsb = K / QK_K;
+    const int64_t m_pad = (L.m + BN - 1) / BN * BN;
+    const WsParts parts = ws_parts(T, L.n_in, L.n_out, L.m, L.num_sms, true);
+    uint8_t *ws = static_cast<uint8_t *>(L.ws);
+    uint16_t *B = reinterpret_cast<uint16_t *>(ws);
+    uint16_t *S = P::MINS ? reinterpret_cast<uint16_t *>(ws + parts.b) : nullptr;
+    float *DA = reinterpret_cast<float *>(ws + parts.b + parts.s);
+    prefill_prep_q8k<P::KSTEPS / 4><<<dim3((unsigned)nsb, (unsigned)m_pad), 64, 0, st>>>(
+        static_cast<const uint8_t *>(L.xq), (int)L.m, (int)nsb, (int)m_pad, B, S, DA);
+    if (cudaGetLastError() != cudaSuccess) return -2;
+    // the prefill copy as rows of 128 bytes: one K-step's A tile is 128 rows,
+    // the mins operand 64 (the copy is already in the shared-memory layout,
+    // so the maps do not swizzle)
+    const uint64_t copy_rows = prefill_pack_bytes(T, L.n_in, L.n_out) / 128;
+    CUtensorMap tmP, tmM, tmB, tmS;
+    if (!make_map(&tmP, L.pack, 64, copy_rows, 128, 64, PF_BM, CU_TENSOR_MAP_SWIZZLE_NONE, 2) ||
+        !make_map(&tmM, L.pack, 64, copy_rows, 128, 64, 64, CU_TENSOR_MAP_SWIZZLE_NONE, 2) ||
+        !make_map(&tmB, B, (uint64_t)(K * P::KSTEPS / 4), (uint64_t)m_pad, (uint64_t)(K * P::KSTEPS / 4) * 2, PF_KS,
+                  Lay::HB, CU_TENSOR_MAP_SWIZZLE_128B, 2))
+        return -4;
+    if (P::MINS) {
+        if (!make_map(&tmS, S, (uint64_t)(K / 16), (uint64_t)m_pad, (uint64_t)(K / 16) * 2, 16, Lay::HB,
+                      CU_TENSOR_MAP_SWIZZLE_32B, 2))
+            return -4;
+    } else {
+        tmS = tmB;   // unused
+    }
+    static bool attr_set[64] = {};
+    const int dev = L.device & 63;
+    if (!attr_set[dev]) {
+        cudaFuncSetAttribute(prefill_pair_kernel<T, BN>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+        if (cudaFuncSetAttribute(prefill_pair_kernel<T, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 Lay::SMEM) != cudaSuccess)
+            return -2;
+        attr_set[dev] = true;
+    }
+    PkParams p{};
+    p.pack = static_cast<const uint8_t *>(L.pack);
+    p.n_out = (int)L.n_out;
+    p.nsb = (int)nsb;
+    p.da = DA;
+    p.y = L.y;
+    p.m = (int)L.m;
+    p.m_pad = (int)m_pad;
+    p.ntt = (int)(m_pad / BN);
+    p.status = L.status;
+    p.nsplit = pair_splits(T, L.n_in, L.n_out, L.m, L.num_sms, BN);
+    p.sb_per_split = (int)((nsb + p.nsplit - 1) / p.nsplit);
+    p.nsplit = (int)((nsb + p.sb_per_split - 1) / p.sb_per_split);   // no empty range
+    p.part = p.nsplit > 1 ? reinterpret_cast<float *>(ws + parts.b + parts.s + parts.da + parts.pad) : nullptr;
+    const int64_t pair_tiles = ((L.n_out + PF_BM - 1) / PF_BM + 1) / 2 * p.ntt;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((unsigned)(2 * pair_tiles * p.nsplit));
+    cfg.blockDim = dim3(PP_WARPS * 32);
+    cfg.dynamicSmemBytes = Lay::SMEM;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, prefill_pair_kernel<T, BN>, tmP, tmM, tmB, tmS, p) != cudaSuccess) return -2;
+    if (p.nsplit > 1) {
+        const int64_t n = L.m * L.n_out;
+        const int64_t blocks = (n + 255) / 256 < 4 * L.num_sms ? (n + 255) / 256 : 4 * L.num_sms;
+        prefill_sum_splits<<<(unsigned)blocks, 256, 0, st>>>(p.part, p.nsplit, n, L.y);
+        if (cudaGetLastError() != cudaSuccess) return -2;
+    }
+    return 0;
+}
+
 // blocks of up to 32 tokens (batched decode) use 32-token tiles: the weights
 // still stream once per token tile, with a quarter of the token-operand traffic
 template <uint32_t T>
 int launch_t(const PrefillLaunch &L, cudaStream_t st) {
-    if (L.pack && L.m > PF_BN_SMALL)
+    if (L.pack && L.m > PF_BN_SMALL) {
+        if (use_pair(L.n_out))
+            return pk_bn(L.m) == 256 ? launch_pair_tb<T, 256>(L, st) : launch_pair_tb<T, PF_BN>(L, st);
         return pk_bn(L.m) == 256 ? launch_packed_tb<T, 256>(L, st) : launch_packed_tb<T, PF_BN>(L, st);
+    }
     return L.m <= PF_BN_SMALL ? launch_tb<T, PF_BN_SMALL>(L, st) : launch_tb<T, PF_BN>(L, st);
 }
 

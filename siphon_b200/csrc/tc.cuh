@@ -152,6 +152,54 @@ __device__ __forceinline__ void tma_prefetch_map(const CUtensorMap *map) {
     asm volatile("prefetch.tensormap [%0];" :: "l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
+// ---- CTA pairs (cta_group::2) ------------------------------------------------------------
+// A cluster of two CTAs on two SMs acts as one MMA unit: an M = 256 MMA takes
+// A rows 0..127 from the leader's (cluster rank 0) shared memory and 128..255
+// from the peer's, B's N rows split in halves the same way (each at the same
+// shared-memory offset in its CTA), and writes each CTA's 128 accumulator
+// rows into that CTA's tensor memory. Every tcgen05 operation of such a
+// kernel uses cta_group::2.
+__device__ __forceinline__ void tc_mma_f16_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                                uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+        :: "r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// One arrival on the barrier at offset `bar` of every CTA in `cta_mask`
+// once the pair's MMAs issued so far have completed.
+__device__ __forceinline__ void tc_commit_pair(uint32_t bar, uint16_t cta_mask) {
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;"
+        :: "r"(bar), "h"(cta_mask) : "memory");
+}
+// One warp in each CTA of the pair, same warp index and destination offset.
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t dst, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" :: "r"(dst), "r"(ncols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" :: "r"(taddr), "r"(ncols) : "memory");
+}
+// 2-D tile into this CTA's shared memory with its completion (bytes) counted
+// on a barrier of either CTA of the pair (`bar` a shared::cluster address).
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap *map, int x, int y, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3}], [%4];"
+        :: "r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+        : "memory");
+}
+// arrival on a barrier of another CTA of the cluster (shared::cluster
+// address), after tcgen05.fence::before_thread_sync when it releases tensor
+// memory the arriving threads have read (their tcgen05.wait::ld completed)
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t bar_cluster) {
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" :: "r"(bar_cluster) : "memory");
+}
+
 // ---- packed f16 ---------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t hfma2_u32(uint32_t a, uint32_t b, uint32_t c) {
     uint32_t d;

@@ -248,6 +248,21 @@ SICU_API int sicu_gemm_prefill_packed(uint32_t wtype, const void *dw, const void
                                       int64_t n_out, const void *dxq, int64_t m, float *dy, void *stream);
 SICU_API int sicu_gemm_prefill_packed_f32(uint32_t wtype, const void *dw, const void *dpack, int64_t n_in,
                                           int64_t n_out, const float *dx, int64_t m, float *dy, void *stream);
+/* dy_i = X W_i^T for n_mats (1..4) matrices of one type and row length that
+ * read the same m-token activation (dx: [m][n_in] f32, 16-byte aligned;
+ * dy[i]: [m][n_out[i]]), each with its prefill copy dpack[i]: the products
+ * the reference's forward pass runs one after another on one activation
+ * (src/engine.c:317-319 Wq/Wk/Wv, 375-376 W_gate/W_up), once per prompt
+ * token. The activation is quantized once and one launch covers every
+ * matrix's tiles, so products too small to fill the GPU alone share it.
+ * Each result is within the sicu_gemm_prefill tolerance (the same exact
+ * integer sums per super-block). dpack null (or any entry null), or at most
+ * 32 tokens: the products one after another as sicu_gemm_prefill_packed_f32
+ * (up to 8 tokens one batch launch for all matrices). dw, dpack, n_out and
+ * dy are host arrays. */
+SICU_API int sicu_gemm_prefill_multi_f32(uint32_t wtype, int n_mats, const void *const *dw,
+                                         const void *const *dpack, const int64_t *n_out, int64_t n_in,
+                                         const float *dx, int64_t m, float *const *dy, void *stream);
 
 /* ---- tensor-parallel all-reduce fused into the matvec ------------------------
  * A row-split product (Wo, W_down split by input columns across a

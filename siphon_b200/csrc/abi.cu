@@ -673,6 +673,64 @@ int sicu_gemm_prefill_packed_f32(uint32_t wtype, const void *dw, const void *dpa
     return prefill_common(wtype, dw, n_in, n_out, nullptr, dx, m, dy, (cudaStream_t)stream, dpack);
 }
 
+int sicu_gemm_prefill_multi_f32(uint32_t wtype, int n_mats, const void *const *dw, const void *const *dpack,
+                                const int64_t *n_out, int64_t n_in, const float *dx, int64_t m, float *const *dy,
+                                void *stream) {
+    if (n_mats < 1 || n_mats > PREFILL_MAXM)
+        return fail(SICU_EINVAL, "prefill multi: %d matrices (1..%d)", n_mats, PREFILL_MAXM);
+    if (!dw || !n_out || !dy) return fail(SICU_EINVAL, "prefill multi: null array");
+    uint32_t pair;
+    for (int i = 0; i < n_mats; ++i) {
+        if (int rc = check_prefill(wtype, dw[i], n_in, n_out[i], dx, m, dy[i], pair)) return rc;
+        if (dpack)
+            if (int rc = check_packed(wtype, dpack[i])) return rc;
+    }
+    if (m == 0) return current_ok();
+    if (!aligned(dx, 16)) return fail(SICU_EINVAL, "prefill multi: f32 activation must be 16-byte aligned");
+    const cudaStream_t st = (cudaStream_t)stream;
+    bool grouped = dpack && n_mats > 1 && m > PREFILL_PACKED_MIN_M && prefill_supported(wtype);
+    for (int i = 0; grouped && i < n_mats; ++i) grouped = dpack[i] && n_out[i] > 0;
+    if (!grouped) {
+        // the products one by one (a few tokens: one batch launch for all)
+        if (m <= BATCH_MAX && batch_supported(wtype))
+            return batch_common(wtype, n_mats, dw, n_out, n_in, dx, nullptr, m, dy, st);
+        for (int i = 0; i < n_mats; ++i)
+            if (n_out[i] > 0)
+                if (int rc = prefill_common(wtype, dw[i], n_in, n_out[i], nullptr, dx, m, dy[i], st,
+                                            dpack ? dpack[i] : nullptr))
+                    return rc;
+        return SICU_OK;
+    }
+    DevState *ds;
+    if (int rc = current(ds)) return rc;
+    const size_t qbytes = ((size_t)m * pair_row_bytes(pair, n_in) + 255) & ~size_t(255);
+    if (int rc = grow_prefill_ws(*ds, qbytes + prefill_group_workspace_bytes(wtype, n_in, n_mats, n_out, m, ds->sms)))
+        return rc;
+    if (launch_quantize(pair, dx, ds->pf_ws, n_in, m, st) != 0) return cuda_fail(cudaGetLastError(), "prefill quantize");
+    PrefillLaunch L{};
+    L.w = dw[0];
+    L.n_in = n_in;
+    L.n_out = n_out[0];
+    L.xq = ds->pf_ws;
+    L.m = m;
+    L.y = dy[0];
+    L.ws = static_cast<uint8_t *>(ds->pf_ws) + qbytes;
+    cudaGetDevice(&L.device);
+    L.num_sms = ds->sms;
+    L.status = ds->status;
+    L.pack = dpack[0];
+    L.nmat = n_mats;
+    for (int i = 0; i < n_mats; ++i) {
+        L.packm[i] = dpack[i];
+        L.n_outm[i] = n_out[i];
+        L.ym[i] = dy[i];
+    }
+    const int rc = launch_prefill(wtype, L, st);
+    if (rc == -4) return fail(SICU_EIO, "prefill multi: tensor map encoding failed");
+    if (rc != 0) return cuda_fail(cudaGetLastError(), "prefill multi launch");
+    return SICU_OK;
+}
+
 int sicu_gemv_batch(uint32_t wtype, int n_mats, const void *const *dw, const int64_t *n_out, int64_t n_in,
                     const float *dx, int64_t m, float *const *dy, void *stream) {
     if (n_mats < 1 || n_mats > 16) return fail(SICU_EINVAL, "batch matvec: %d matrices (1..16)", n_mats);

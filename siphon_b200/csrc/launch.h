@@ -94,6 +94,8 @@ int launch_host_copy(const float *src, float *dst, int64_t n, cudaStream_t st);
 int launch_quantize(uint32_t pair, const float *x, void *y, int64_t n, int64_t m, cudaStream_t st);
 
 // prefill matrix product on the tensor cores: y[t][r] for m tokens (Q8_K rows)
+constexpr int PREFILL_MAXM = 4;            // matrices per grouped prefill launch
+constexpr int PREFILL_PACKED_MIN_M = 32;   // blocks of more tokens than this read the prefill copies
 struct PrefillLaunch {
     const void *w;        // weight blocks (device)
     int64_t n_in, n_out;
@@ -105,9 +107,18 @@ struct PrefillLaunch {
     int num_sms;
     int *status;
     const void *pack;     // the prefill copy of w (prefill_pack_bytes), or null
+    // more matrices that read the same activation (prefill copies required):
+    // nmat > 1 lists every matrix of the group (entry 0 included) below
+    int nmat = 1;
+    const void *packm[PREFILL_MAXM];
+    int64_t n_outm[PREFILL_MAXM];
+    float *ym[PREFILL_MAXM];
 };
 bool prefill_supported(uint32_t wtype);
 size_t prefill_workspace_bytes(uint32_t wtype, int64_t n_in, int64_t n_out, int64_t m, int num_sms, bool packed);
+// a group of nmat matrices read from their prefill copies (m > 32)
+size_t prefill_group_workspace_bytes(uint32_t wtype, int64_t n_in, int nmat, const int64_t *n_out, int64_t m,
+                                     int num_sms);
 // bytes of the prefill copy of an n_out x n_in matrix (0: no tensor-core kernel for the type)
 size_t prefill_pack_bytes(uint32_t wtype, int64_t n_in, int64_t n_out);
 // writes the prefill copy of the weight blocks w into pack; -3: unsupported type

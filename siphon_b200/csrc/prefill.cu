@@ -45,6 +45,7 @@ namespace {
 constexpr int PF_BM = 128;        // weight rows per tile (MMA M)
 constexpr int PF_BN = 128;        // tokens per tile (MMA N) for prompts
 constexpr int PF_BN_SMALL = 32;   // tokens per tile for blocks of <= 32 tokens (batched decode)
+static_assert(PF_BN_SMALL == PREFILL_PACKED_MIN_M, "blocks above one small tile read the prefill copies");
 constexpr int PF_KS = 64;         // k slots per pipeline stage: one 128-byte swizzle atom of f16
 constexpr int PF_STAGES = 6;     // K-steps in flight (even: each stage belongs to one converter group)
 constexpr int PF_NSB = 4;         // per-super-block buffers: mins / bsums tiles, scales
@@ -1065,11 +1066,30 @@ enum {
 };
 static_assert(PP_NBARS <= 32, "barrier area");
 
+// A launch covers up to PP_MAXM matrices that read the same activation (the
+// products Wq / Wk / Wv, or W_gate / W_up, of a prompt), with one shared
+// token operand: pair tiles are numbered matrix by matrix.
+constexpr int PP_MAXM = PREFILL_MAXM;
+struct PpMaps {
+    CUtensorMap a[PP_MAXM];      // each matrix's prefill copy as 128-byte rows, 128-row boxes (A tiles)
+    CUtensorMap mins[PP_MAXM];   // the same, 64-row boxes (Q4_K mins operand)
+};
+struct PpParams {
+    const uint8_t *pack[PP_MAXM];
+    float *y[PP_MAXM];           // [m][n_out]
+    float *part[PP_MAXM];        // nsplit > 1: [nsplit][m][n_out] partial products
+    int n_out[PP_MAXM];
+    int tile_end[PP_MAXM];       // pair tiles of matrices 0..i (one split)
+    int nmat, nsb, nsplit, sb_per_split;
+    const float *da;             // [nsb][m_pad] token scales
+    int m, m_pad, ntt;
+    int *status;
+};
+
 template <uint32_t T, int BN>
 __global__ void __launch_bounds__(PP_WARPS * 32, 1)
-prefill_pair_kernel(const __grid_constant__ CUtensorMap tmP, const __grid_constant__ CUtensorMap tmM,
-                    const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmS,
-                    const PkParams p) {
+prefill_pair_kernel(const __grid_constant__ PpMaps maps, const __grid_constant__ CUtensorMap tmB,
+                    const __grid_constant__ CUtensorMap tmS, const PpParams p) {
     using P = PkFmt<T>;
     using Lay = PpLayout<T, BN>;
     constexpr int KST = P::KSTEPS, S = Lay::STAGES, HB = Lay::HB;
@@ -1084,17 +1104,24 @@ prefill_pair_kernel(const __grid_constant__ CUtensorMap tmP, const __grid_consta
     const uint32_t rank = cluster_rank();
     const bool leader = rank == 0;
     const int pair = (int)(blockIdx.x >> 1);
-    const int ntiles = (int)(gridDim.x >> 1) / p.nsplit;
-    const int split = pair / ntiles, tile = pair - split * ntiles;
+    const int ntiles = p.tile_end[p.nmat - 1];
+    const int split = pair / ntiles;
+    int tile = pair - split * ntiles, mi = 0;
+    while (mi + 1 < p.nmat && tile >= p.tile_end[mi]) ++mi;
+    if (mi > 0) tile -= p.tile_end[mi - 1];
+    const int n_out = p.n_out[mi];
+    const uint8_t *const pack = p.pack[mi];
+    const CUtensorMap *const tmP = &maps.a[mi];
+    const CUtensorMap *const tmM = &maps.mins[mi];
     const int prt = tile / p.ntt, tt = tile - prt * p.ntt;
     const int rt = 2 * prt + (int)rank;                  // this CTA's 128-row tile
-    const int nrt = (p.n_out + PF_BM - 1) / PF_BM;
+    const int nrt = (n_out + PF_BM - 1) / PF_BM;
     const bool has_rows = rt < nrt;
     const int row0 = rt * PF_BM, tok0 = tt * BN;
-    const int rows = has_rows ? min(PF_BM, p.n_out - row0) : 0;
+    const int rows = has_rows ? min(PF_BM, n_out - row0) : 0;
     const int sbb = split * p.sb_per_split;
     const int nsb = min(p.sb_per_split, p.nsb - sbb);
-    float *const yout = p.nsplit > 1 ? p.part + (size_t)split * p.m * p.n_out : p.y;
+    float *const yout = p.nsplit > 1 ? p.part[mi] + (size_t)split * p.m * n_out : p.y[mi];
     volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + Lay::OFF_FLAGS);
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + Lay::OFF_FLAGS + 4);
     const uint32_t barbase = sb0 + Lay::OFF_BAR;
@@ -1123,10 +1150,10 @@ prefill_pair_kernel(const __grid_constant__ CUtensorMap tmP, const __grid_consta
     }
     if (warp == 1) tmem_alloc_pair(smem_addr(tmem_slot), 2 * BN);
     if (warp == 0 && lane == 0) {
-        tma_prefetch_map(&tmP);
+        tma_prefetch_map(tmP);
         tma_prefetch_map(&tmB);
         if constexpr (P::MINS) {
-            tma_prefetch_map(&tmM);
+            tma_prefetch_map(tmM);
             tma_prefetch_map(&tmS);
         }
     }
@@ -1146,7 +1173,7 @@ prefill_pair_kernel(const __grid_constant__ CUtensorMap tmP, const __grid_consta
                 const int crow = (int)((chunk0 + sb) * CH);
                 if (!pf_wait<true>(bar(PP_EMPTY + s), ((uint32_t)(t / S) & 1u) ^ 1u, abort_flag, p.status)) break;
                 if (leader) mbar_expect_tx(bar(PP_FULL + s), 2u * (uint32_t)Lay::STAGE);
-                tma_load_2d_pair(stage_a(s), &tmP, 0, crow + c * 128, lbar(PP_FULL + s));
+                tma_load_2d_pair(stage_a(s), tmP, 0, crow + c * 128, lbar(PP_FULL + s));
                 tma_load_2d_pair(stage_b(s), &tmB, PF_KS * (KST * sbb + t), tok0 + (int)rank * HB, lbar(PP_FULL + s));
             }
         }
@@ -1161,12 +1188,12 @@ prefill_pair_kernel(const __grid_constant__ CUtensorMap tmP, const __grid_consta
                 if constexpr (P::MINS) {
                     const int crow = (int)((chunk0 + sb) * CH);
                     if (leader) mbar_expect_tx(bar(PP_MMETA + b), 2u * (uint32_t)(Lay::META_MIN + Lay::META_B2));
-                    tma_load_2d_pair(mb + M_MIN, &tmM, 0, crow + KST * 128, lbar(PP_MMETA + b));
+                    tma_load_2d_pair(mb + M_MIN, tmM, 0, crow + KST * 128, lbar(PP_MMETA + b));
                     tma_load_2d_pair(mb + M_B2, &tmS, 16 * (sbb + sb), tok0 + (int)rank * HB, lbar(PP_MMETA + b));
                 }
                 mbar_expect_tx(bar(PP_EMETA + b), (uint32_t)((has_rows ? PF_BM * 4 : 0) + BN * 4));
                 if (has_rows)
-                    bulk_g2s(mb + M_F, p.pack + (size_t)(chunk0 + sb) * pk_chunk<T>() + pk_off_f<T>(), PF_BM * 4,
+                    bulk_g2s(mb + M_F, pack + (size_t)(chunk0 + sb) * pk_chunk<T>() + pk_off_f<T>(), PF_BM * 4,
                              bar(PP_EMETA + b));
                 bulk_g2s(mb + M_DA, p.da + (size_t)(sbb + sb) * p.m_pad + tok0, BN * 4, bar(PP_EMETA + b));
             }
@@ -1263,7 +1290,7 @@ prefill_pair_kernel(const __grid_constant__ CUtensorMap tmP, const __grid_consta
             float *yr = yout + row0 + r;
 #pragma unroll
             for (int j = 0; j < EPI_COLS; ++j)
-                if (tok0 + c0 + j < p.m) yr[(int64_t)(tok0 + c0 + j) * p.n_out] = acc[j];
+                if (tok0 + c0 + j < p.m) yr[(int64_t)(tok0 + c0 + j) * n_out] = acc[j];
         }
     }
 
@@ -1407,12 +1434,26 @@ int split_count(int64_t n_in, int64_t n_out, int64_t m, int num_sms) {
 // 128 x bn x 256 tile at ~60 % of the f16 rate; only the comparison matters)
 int pk_bn(int64_t m) { return m > PF_BN ? 256 : PF_BN; }
 double pk_us_per_sb(uint32_t wtype, int64_t bn) { return (bn == 256 ? 1.8 : 0.9) * (wtype == T_Q6_K ? 2.0 : 1.0); }
-// Products of at least two 128-row tiles run on CTA pairs (one 256-row tile
-// per pair, 2 SMs); a pair's time per super-block is the one-CTA tile's.
+// Products of at least two 128-row tiles, and groups of products, run on CTA
+// pairs (one 256-row tile per pair, 2 SMs); a pair's time per super-block is
+// the one-CTA tile's.
 bool use_pair(int64_t n_out) { return (n_out + PF_BM - 1) / PF_BM >= 2; }
-int pair_splits(uint32_t wtype, int64_t n_in, int64_t n_out, int64_t m, int num_sms, int64_t bn) {
-    const int64_t tiles = ((n_out + PF_BM - 1) / PF_BM + 1) / 2 * ((m + bn - 1) / bn);
-    return split_count_tiles(tiles, n_in / QK_K, m, n_out, num_sms / 2, pk_us_per_sb(wtype, bn));
+struct PairPlan {
+    int64_t tiles;       // pair tiles of the group (one split)
+    int64_t sum_out;     // rows of the group
+    int nsplit, sb_per_split;
+};
+PairPlan pair_plan(uint32_t wtype, int64_t n_in, int nmat, const int64_t *n_out, int64_t m, int num_sms) {
+    const int64_t bn = pk_bn(m), ntt = (m + bn - 1) / bn, nsb = n_in / QK_K;
+    PairPlan pl{};
+    for (int i = 0; i < nmat; ++i) {
+        pl.tiles += ((n_out[i] + PF_BM - 1) / PF_BM + 1) / 2 * ntt;
+        pl.sum_out += n_out[i];
+    }
+    const int ns = split_count_tiles(pl.tiles, nsb, m, pl.sum_out, num_sms / 2, pk_us_per_sb(wtype, bn));
+    pl.sb_per_split = (int)((nsb + ns - 1) / ns);
+    pl.nsplit = (int)((nsb + pl.sb_per_split - 1) / pl.sb_per_split);   // no empty range
+    return pl;
 }
 
 struct WsParts {
@@ -1429,7 +1470,7 @@ WsParts ws_parts(uint32_t wtype, int64_t n_in, int64_t n_out, int64_t m, int num
     const int64_t rb = n_in / QK_K * B_Q6_K;
     w.pad = (!packed && wtype == T_Q6_K && rb % 16) ? align256((size_t)n_out * ((rb + 15) & ~int64_t(15))) : 0;
     const int ns = !packed ? split_count(n_in, n_out, m, num_sms)
-                 : use_pair(n_out) ? pair_splits(wtype, n_in, n_out, m, num_sms, bn)
+                 : use_pair(n_out) ? pair_plan(wtype, n_in, 1, &n_out, m, num_sms).nsplit
                                    : split_count_bn(n_in, n_out, m, num_sms, bn, pk_us_per_sb(wtype, bn));
     w.part = ns > 1 ? align256((size_t)ns * m * n_out * 4) : 0;
     return w;
@@ -1573,22 +1614,41 @@ int launch_pair_tb(const PrefillLaunch &L, cudaStream_t st) {
     using Lay = PpLayout<T, BN>;
     const int64_t K = L.n_in, nsb = K / QK_K;
     const int64_t m_pad = (L.m + BN - 1) / BN * BN;
-    const WsParts parts = ws_parts(T, L.n_in, L.n_out, L.m, L.num_sms, true);
+    const int nmat = L.nmat > 1 ? L.nmat : 1;
+    const int64_t *n_out = L.nmat > 1 ? L.n_outm : &L.n_out;
+    const PairPlan pl = pair_plan(T, L.n_in, nmat, n_out, L.m, L.num_sms);
+    const WsParts parts = ws_parts(T, L.n_in, L.n_out, L.m, L.num_sms, true);   // activation parts
     uint8_t *ws = static_cast<uint8_t *>(L.ws);
     uint16_t *B = reinterpret_cast<uint16_t *>(ws);
     uint16_t *S = P::MINS ? reinterpret_cast<uint16_t *>(ws + parts.b) : nullptr;
     float *DA = reinterpret_cast<float *>(ws + parts.b + parts.s);
+    float *part = reinterpret_cast<float *>(ws + parts.b + parts.s + parts.da);
     prefill_prep_q8k<P::KSTEPS / 4><<<dim3((unsigned)nsb, (unsigned)m_pad), 64, 0, st>>>(
         static_cast<const uint8_t *>(L.xq), (int)L.m, (int)nsb, (int)m_pad, B, S, DA);
     if (cudaGetLastError() != cudaSuccess) return -2;
-    // the prefill copy as rows of 128 bytes: one K-step's A tile is 128 rows,
-    // the mins operand 64 (the copy is already in the shared-memory layout,
-    // so the maps do not swizzle)
-    const uint64_t copy_rows = prefill_pack_bytes(T, L.n_in, L.n_out) / 128;
-    CUtensorMap tmP, tmM, tmB, tmS;
-    if (!make_map(&tmP, L.pack, 64, copy_rows, 128, 64, PF_BM, CU_TENSOR_MAP_SWIZZLE_NONE, 2) ||
-        !make_map(&tmM, L.pack, 64, copy_rows, 128, 64, 64, CU_TENSOR_MAP_SWIZZLE_NONE, 2) ||
-        !make_map(&tmB, B, (uint64_t)(K * P::KSTEPS / 4), (uint64_t)m_pad, (uint64_t)(K * P::KSTEPS / 4) * 2, PF_KS,
+    // each prefill copy as rows of 128 bytes: one K-step's A tile is 128 rows,
+    // the mins operand 64 (the copy is already in the shared-memory layout, so
+    // the maps do not swizzle)
+    PpMaps maps;
+    PpParams p{};
+    int64_t tiles = 0, rows_before = 0;
+    for (int i = 0; i < nmat; ++i) {
+        const void *pack = L.nmat > 1 ? L.packm[i] : L.pack;
+        const uint64_t copy_rows = prefill_pack_bytes(T, L.n_in, n_out[i]) / 128;
+        if (!make_map(&maps.a[i], pack, 64, copy_rows, 128, 64, PF_BM, CU_TENSOR_MAP_SWIZZLE_NONE, 2) ||
+            !make_map(&maps.mins[i], pack, 64, copy_rows, 128, 64, 64, CU_TENSOR_MAP_SWIZZLE_NONE, 2))
+            return -4;
+        p.pack[i] = static_cast<const uint8_t *>(pack);
+        p.y[i] = L.nmat > 1 ? L.ym[i] : L.y;
+        p.n_out[i] = (int)n_out[i];
+        p.part[i] = part + (size_t)pl.nsplit * L.m * rows_before;
+        tiles += ((n_out[i] + PF_BM - 1) / PF_BM + 1) / 2 * (m_pad / BN);
+        p.tile_end[i] = (int)tiles;
+        rows_before += n_out[i];
+    }
+    for (int i = nmat; i < PP_MAXM; ++i) maps.a[i] = maps.mins[i] = maps.a[0];
+    CUtensorMap tmB, tmS;
+    if (!make_map(&tmB, B, (uint64_t)(K * P::KSTEPS / 4), (uint64_t)m_pad, (uint64_t)(K * P::KSTEPS / 4) * 2, PF_KS,
                   Lay::HB, CU_TENSOR_MAP_SWIZZLE_128B, 2))
         return -4;
     if (P::MINS) {
@@ -1607,23 +1667,17 @@ int launch_pair_tb(const PrefillLaunch &L, cudaStream_t st) {
             return -2;
         attr_set[dev] = true;
     }
-    PkParams p{};
-    p.pack = static_cast<const uint8_t *>(L.pack);
-    p.n_out = (int)L.n_out;
+    p.nmat = nmat;
     p.nsb = (int)nsb;
+    p.nsplit = pl.nsplit;
+    p.sb_per_split = pl.sb_per_split;
     p.da = DA;
-    p.y = L.y;
     p.m = (int)L.m;
     p.m_pad = (int)m_pad;
     p.ntt = (int)(m_pad / BN);
     p.status = L.status;
-    p.nsplit = pair_splits(T, L.n_in, L.n_out, L.m, L.num_sms, BN);
-    p.sb_per_split = (int)((nsb + p.nsplit - 1) / p.nsplit);
-    p.nsplit = (int)((nsb + p.sb_per_split - 1) / p.sb_per_split);   // no empty range
-    p.part = p.nsplit > 1 ? reinterpret_cast<float *>(ws + parts.b + parts.s + parts.da + parts.pad) : nullptr;
-    const int64_t pair_tiles = ((L.n_out + PF_BM - 1) / PF_BM + 1) / 2 * p.ntt;
     cudaLaunchConfig_t cfg{};
-    cfg.gridDim = dim3((unsigned)(2 * pair_tiles * p.nsplit));
+    cfg.gridDim = dim3((unsigned)(2 * tiles * p.nsplit));
     cfg.blockDim = dim3(PP_WARPS * 32);
     cfg.dynamicSmemBytes = Lay::SMEM;
     cfg.stream = st;
@@ -1634,12 +1688,14 @@ int launch_pair_tb(const PrefillLaunch &L, cudaStream_t st) {
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    if (cudaLaunchKernelEx(&cfg, prefill_pair_kernel<T, BN>, tmP, tmM, tmB, tmS, p) != cudaSuccess) return -2;
+    if (cudaLaunchKernelEx(&cfg, prefill_pair_kernel<T, BN>, maps, tmB, tmS, p) != cudaSuccess) return -2;
     if (p.nsplit > 1) {
-        const int64_t n = L.m * L.n_out;
-        const int64_t blocks = (n + 255) / 256 < 4 * L.num_sms ? (n + 255) / 256 : 4 * L.num_sms;
-        prefill_sum_splits<<<(unsigned)blocks, 256, 0, st>>>(p.part, p.nsplit, n, L.y);
-        if (cudaGetLastError() != cudaSuccess) return -2;
+        for (int i = 0; i < nmat; ++i) {
+            const int64_t n = L.m * n_out[i];
+            const int64_t blocks = (n + 255) / 256 < 4 * L.num_sms ? (n + 255) / 256 : 4 * L.num_sms;
+            prefill_sum_splits<<<(unsigned)blocks, 256, 0, st>>>(p.part[i], p.nsplit, n, p.y[i]);
+            if (cudaGetLastError() != cudaSuccess) return -2;
+        }
     }
     return 0;
 }
@@ -1649,7 +1705,7 @@ int launch_pair_tb(const PrefillLaunch &L, cudaStream_t st) {
 template <uint32_t T>
 int launch_t(const PrefillLaunch &L, cudaStream_t st) {
     if (L.pack && L.m > PF_BN_SMALL) {
-        if (use_pair(L.n_out))
+        if (L.nmat > 1 || use_pair(L.n_out))
             return pk_bn(L.m) == 256 ? launch_pair_tb<T, 256>(L, st) : launch_pair_tb<T, PF_BN>(L, st);
         return pk_bn(L.m) == 256 ? launch_packed_tb<T, 256>(L, st) : launch_packed_tb<T, PF_BN>(L, st);
     }
@@ -1672,6 +1728,13 @@ bool prefill_supported(uint32_t wtype) { return wtype == T_Q4_K || wtype == T_Q6
 size_t prefill_workspace_bytes(uint32_t wtype, int64_t n_in, int64_t n_out, int64_t m, int num_sms, bool packed) {
     const WsParts w = ws_parts(wtype, n_in, n_out, m, num_sms, packed && m > PF_BN_SMALL);
     return w.b + w.s + w.da + w.pad + w.part;
+}
+
+size_t prefill_group_workspace_bytes(uint32_t wtype, int64_t n_in, int nmat, const int64_t *n_out, int64_t m,
+                                     int num_sms) {
+    const WsParts w = ws_parts(wtype, n_in, n_out[0], m, num_sms, true);
+    const PairPlan pl = pair_plan(wtype, n_in, nmat, n_out, m, num_sms);
+    return w.b + w.s + w.da + (pl.nsplit > 1 ? align256((size_t)pl.nsplit * m * pl.sum_out * 4) : 0);
 }
 
 size_t prefill_pack_bytes(uint32_t wtype, int64_t n_in, int64_t n_out) {

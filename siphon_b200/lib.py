@@ -57,6 +57,8 @@ SIGNATURES = {
     "sicu_prefill_pack": [_u32, _vp, _i64, _i64, _vp, C.c_size_t, _vp],
     "sicu_gemm_prefill_packed": [_u32, _vp, _vp, _i64, _i64, _vp, _i64, _fp, _vp],
     "sicu_gemm_prefill_packed_f32": [_u32, _vp, _vp, _i64, _i64, _fp, _i64, _fp, _vp],
+    "sicu_gemm_prefill_multi_f32": [_u32, C.c_int, C.POINTER(C.c_void_p), C.POINTER(C.c_void_p),
+                                    C.POINTER(C.c_int64), _i64, _fp, _i64, C.POINTER(C.c_void_p), _vp],
     "sicu_ar_create": [C.c_int, C.c_int, _i64, C.POINTER(C.c_void_p), _vp],
     "sicu_ar_open": [_vp, _vp],
     "sicu_ar_set_timeout": [_vp, C.c_uint64],
@@ -237,6 +239,19 @@ class SiphonCuda:
                                 stream=None) -> None:
         self.check(self.lib.sicu_gemm_prefill_packed_f32(wtype, _ptr(dw), _ptr(dpack), n_in, n_out, _ptr(dx), m,
                                                          _ptr(dy), _ptr(stream)))
+
+    def gemm_prefill_multi_f32(self, wtype: int, dws, dpacks, n_outs, n_in: int, dx, m: int, dys,
+                               stream=None) -> None:
+        """sicu_gemm_prefill_multi_f32: the products of several matrices that
+        read one m-token activation, from their prefill copies (dpacks may be
+        None, or hold None entries)."""
+        n = len(dws)
+        w_arr = (C.c_void_p * n)(*[_ptr(w) for w in dws])
+        p_arr = (C.c_void_p * n)(*[_ptr(p) for p in dpacks]) if dpacks is not None else None
+        o_arr = (C.c_int64 * n)(*n_outs)
+        y_arr = (C.c_void_p * n)(*[_ptr(y) for y in dys])
+        self.check(self.lib.sicu_gemm_prefill_multi_f32(wtype, n, w_arr, p_arr, o_arr, n_in, _ptr(dx), m, y_arr,
+                                                        _ptr(stream)))
 
     # -- fused all-reduce groups ---------------------------------------------------
     def ar_create(self, n_ranks: int, rank: int, length: int) -> "ArGroup":

@@ -487,17 +487,33 @@ class MatrixPath:
         d = self.sh.n_embd
         nq, nkv, nff = self.shapes["q"][0], self.shapes["k"][0], self.shapes["gate"][0]
         for il, lay in enumerate(self.layers):
-            for name, n_in, xin in (("q", d, self.x_model), ("k", d, self.x_model), ("v", d, self.x_model),
-                                    ("o", nq, self.x_attn), ("gate", d, self.x_model), ("up", d, self.x_model),
-                                    ("down", nff, self.x_ff)):
-                t, w = lay[name]
-                pk = self.pack.get((il, name))
-                if pk is not None:
-                    s.gemm_prefill_packed_f32(t, w, pk, n_in, self.shapes[name][0], xin, m, y[name], stream=h)
-                else:
-                    s.gemm_prefill_f32(t, w, n_in, self.shapes[name][0], xin, m, y[name], stream=h)
-                if name in ("o", "down"):
-                    self._allreduce(y[name][:m])
+            # products that read one activation with one weight type and have
+            # prefill copies run as one grouped launch (Wq/Wk[/Wv], W_gate/W_up)
+            for group, n_in, xin in ((("q", "k", "v"), d, self.x_model), (("o",), nq, self.x_attn),
+                                     (("gate", "up"), d, self.x_model), (("down",), nff, self.x_ff)):
+                runs = []
+                for name in group:
+                    t = lay[name][0]
+                    pk = self.pack.get((il, name))
+                    if runs and runs[-1][0] == t and pk is not None and runs[-1][1][-1][1] is not None:
+                        runs[-1][1].append((name, pk))
+                    else:
+                        runs.append((t, [(name, pk)]))
+                for t, members in runs:
+                    if len(members) > 1:
+                        names = [nm for nm, _ in members]
+                        s.gemm_prefill_multi_f32(t, [lay[nm][1] for nm in names], [pk for _, pk in members],
+                                                 [self.shapes[nm][0] for nm in names], n_in, xin, m,
+                                                 [y[nm] for nm in names], stream=h)
+                        continue
+                    name, pk = members[0]
+                    w = lay[name][1]
+                    if pk is not None:
+                        s.gemm_prefill_packed_f32(t, w, pk, n_in, self.shapes[name][0], xin, m, y[name], stream=h)
+                    else:
+                        s.gemm_prefill_f32(t, w, n_in, self.shapes[name][0], xin, m, y[name], stream=h)
+                if group[0] in ("o", "down"):
+                    self._allreduce(y[group[0]][:m])
         th, wh = self.head
         pk = self.pack.get(("head",))
         if pk is not None:

@@ -168,3 +168,26 @@ def test_prefill_copy_size_and_checks_run_on_host(so):
     assert "sicu_init" in so.last_error()
     # a copy given for a type without one
     assert so.lib.sicu_gemm_prefill_packed_f32(Q.Q8_0, 16, 32, 256, 128, 64, 64, 128, None) == L.SICU_EINVAL
+
+
+def test_prefill_multi_checks_run_on_host(so):
+    """The grouped prefill entry checks its arrays and every matrix before any
+    CUDA call: 1..4 matrices, null arrays, a copy for a type without one, a
+    misaligned copy."""
+    P = C.c_void_p
+    w = (P * 2)(16, 16)
+    ok_packs = (P * 2)(32, 48)
+    bad_packs = (P * 2)(32, 40)
+    n_out = (C.c_int64 * 2)(128, 128)
+    y = (P * 2)(64, 64)
+    f = so.lib.sicu_gemm_prefill_multi_f32
+    assert f(Q.Q4_K, 0, w, ok_packs, n_out, 256, 128, 64, y, None) == L.SICU_EINVAL
+    assert f(Q.Q4_K, 5, w, ok_packs, n_out, 256, 128, 64, y, None) == L.SICU_EINVAL
+    assert f(Q.Q4_K, 2, None, ok_packs, n_out, 256, 128, 64, y, None) == L.SICU_EINVAL
+    assert f(Q.Q4_K, 2, w, ok_packs, None, 256, 128, 64, y, None) == L.SICU_EINVAL
+    assert f(Q.Q4_K, 2, w, bad_packs, n_out, 256, 128, 64, y, None) == L.SICU_EINVAL     # misaligned copy
+    assert "aligned" in so.last_error()
+    assert f(Q.Q8_0, 2, w, ok_packs, n_out, 256, 128, 64, y, None) == L.SICU_EINVAL      # no copies for Q8_0
+    assert f(Q.Q4_K, 2, w, ok_packs, n_out, 300, 128, 64, y, None) == L.SICU_EINVAL      # not whole super-blocks
+    assert f(Q.Q4_K, 2, w, ok_packs, n_out, 256, 128, 64, y, None) == L.SICU_EINVAL      # not initialised
+    assert "sicu_init" in so.last_error()

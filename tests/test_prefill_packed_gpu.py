@@ -230,3 +230,60 @@ def test_pack_errors(sicu):
         sicu.gemm_prefill_packed_f32(Q.Q4_K, w, p[1:], 256, 128, x, 64, y)   # misaligned copy
     sicu.prefill_pack(Q.Q4_K, w, 256, 0, p, n)                     # no rows: nothing
     assert sicu.status() == 0
+
+
+@pytest.mark.parametrize("wt,n_outs,n_in,m", [
+    (Q.Q4_K, (640, 128, 128), 1024, 300),    # Wq/Wk/Wv-like: one-tile matrices leave half a pair idle
+    (Q.Q4_K, (1024, 1024), 4096, 512),       # W_gate/W_up-like
+    (Q.Q6_K, (256, 384), 1280, 77),          # 5 super-blocks, 128-token tiles
+    (Q.Q4_K, (200, 0, 130), 512, 64),        # a matrix without rows: the products one by one
+    (Q.Q4_K, (300, 100), 768, 20),           # at most 32 tokens: the raw blocks
+    (Q.Q6_K, (130, 260, 128, 64), 512, 6),   # a batch of decode steps: one batch launch
+])
+def test_packed_prefill_multi_vs_reference(sicu, oracle, wt, n_outs, n_in, m):
+    """sicu_gemm_prefill_multi_f32: several matrices on one activation, each
+    product within the prefill tolerance of the oracle's per-row dots, and
+    the same bits on a second call."""
+    x = synth.activations(n_in, m, seed=m + n_in)
+    xq = oracle.quantize_pair(wt, x)
+    ws, dws, dps, ys = [], [], [], []
+    for i, n_out in enumerate(n_outs):
+        w = synth.weights(wt, n_out, n_in, seed=10 * i + n_out + 1) if n_out else np.zeros(0, np.uint8)
+        ws.append(w)
+        if n_out:
+            dw, dp, _ = _pack(sicu, wt, w, n_in, n_out)
+        else:
+            import torch
+            dw = dp = torch.zeros(16, dtype=torch.uint8, device="cuda")
+        dws.append(dw)
+        dps.append(dp)
+        ys.append(empty_f32(m, max(n_out, 1)))
+    dx = dev(x)
+    sicu.gemm_prefill_multi_f32(wt, dws, dps, list(n_outs), n_in, dx, m, ys)
+    first = [host(y) for y in ys]
+    sicu.gemm_prefill_multi_f32(wt, dws, dps, list(n_outs), n_in, dx, m, ys)
+    xd = _dequant_q8k(xq, n_in)
+    for i, n_out in enumerate(n_outs):
+        if not n_out:
+            continue
+        got = host(ys[i])
+        assert_bits_equal(got, first[i], f"matrix {i} second call")
+        want = oracle.gemv_batch(wt, ws[i], n_in, n_out, xq)
+        l1 = np.abs(xd) @ np.abs(_dequant_w(oracle, wt, ws[i], n_in, n_out)).T
+        _check_tol(got, want, l1, f"{Q.NAMES[wt]} multi prefill matrix {i} {n_out}x{n_in} m={m}")
+        assert np.isfinite(got).all()
+    assert sicu.status() == 0
+
+
+def test_packed_prefill_multi_without_copies(sicu, oracle):
+    """No prefill copies: the products one by one from the raw blocks, the
+    same bits as single sicu_gemm_prefill_f32 calls."""
+    wt, n_outs, n_in, m = Q.Q4_K, (256, 128), 1024, 96
+    x = dev(synth.activations(n_in, m, seed=2))
+    ws = [dev(synth.weights(wt, n, n_in, seed=n)) for n in n_outs]
+    ys = [empty_f32(m, n) for n in n_outs]
+    sicu.gemm_prefill_multi_f32(wt, ws, None, list(n_outs), n_in, x, m, ys)
+    for w, n, y in zip(ws, n_outs, ys):
+        one = empty_f32(m, n)
+        sicu.gemm_prefill_f32(wt, w, n_in, n, x, m, one)
+        assert_bits_equal(host(y), host(one), f"{n} rows without copies")

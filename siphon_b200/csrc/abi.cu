@@ -569,21 +569,18 @@ static int prefill_common(uint32_t wtype, const void *dw, int64_t n_in, int64_t 
         }
         return SICU_OK;
     }
-    const size_t qbytes = xq ? 0 : (((size_t)m * pair_row_bytes(pair, n_in) + 255) & ~size_t(255));
-    if (int rc = grow_prefill_ws(*ds, qbytes + prefill_workspace_bytes(wtype, n_in, n_out, m, ds->sms, pack != nullptr)))
+    // f32 rows are quantized inside the launch, straight into the token operand
+    if (int rc = grow_prefill_ws(*ds, prefill_workspace_bytes(wtype, n_in, n_out, m, ds->sms, pack != nullptr)))
         return rc;
-    if (!xq) {
-        if (launch_quantize(pair, xf, ds->pf_ws, n_in, m, st) != 0) return cuda_fail(cudaGetLastError(), "prefill quantize");
-        xq = ds->pf_ws;
-    }
     PrefillLaunch L{};
     L.w = dw;
     L.n_in = n_in;
     L.n_out = n_out;
     L.xq = xq;
+    L.xf = xq ? nullptr : xf;
     L.m = m;
     L.y = dy;
-    L.ws = static_cast<uint8_t *>(ds->pf_ws) + qbytes;
+    L.ws = ds->pf_ws;
     cudaGetDevice(&L.device);
     L.num_sms = ds->sms;
     L.status = ds->status;
@@ -703,18 +700,16 @@ int sicu_gemm_prefill_multi_f32(uint32_t wtype, int n_mats, const void *const *d
     }
     DevState *ds;
     if (int rc = current(ds)) return rc;
-    const size_t qbytes = ((size_t)m * pair_row_bytes(pair, n_in) + 255) & ~size_t(255);
-    if (int rc = grow_prefill_ws(*ds, qbytes + prefill_group_workspace_bytes(wtype, n_in, n_mats, n_out, m, ds->sms)))
+    if (int rc = grow_prefill_ws(*ds, prefill_group_workspace_bytes(wtype, n_in, n_mats, n_out, m, ds->sms)))
         return rc;
-    if (launch_quantize(pair, dx, ds->pf_ws, n_in, m, st) != 0) return cuda_fail(cudaGetLastError(), "prefill quantize");
     PrefillLaunch L{};
     L.w = dw[0];
     L.n_in = n_in;
     L.n_out = n_out[0];
-    L.xq = ds->pf_ws;
+    L.xf = dx;
     L.m = m;
     L.y = dy[0];
-    L.ws = static_cast<uint8_t *>(ds->pf_ws) + qbytes;
+    L.ws = ds->pf_ws;
     cudaGetDevice(&L.device);
     L.num_sms = ds->sms;
     L.status = ds->status;

@@ -99,7 +99,8 @@ constexpr int PREFILL_PACKED_MIN_M = 32;   // blocks of more tokens than this re
 struct PrefillLaunch {
     const void *w;        // weight blocks (device)
     int64_t n_in, n_out;
-    const void *xq;       // m rows of Q8_K blocks (device)
+    const void *xq;       // m rows of Q8_K blocks (device), or null with xf set
+    const float *xf;      // m rows of f32 (device, 16-byte aligned), quantized inside the launch
     int64_t m;
     float *y;             // [m][n_out] (device)
     void *ws;             // prefill_workspace_bytes(wtype, n_in, n_out, m, num_sms, pack != 0) bytes, 256-byte aligned

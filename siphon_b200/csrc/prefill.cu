@@ -36,6 +36,7 @@
 #include <cudaTypedefs.h>
 
 #include "launch.h"
+#include "quantize.cuh"
 #include "tc.cuh"
 
 namespace sicu {
@@ -1345,6 +1346,57 @@ __global__ void prefill_prep_q8k(const uint8_t *xq, int m, int nsb, int m_pad, u
     }
 }
 
+// f32 rows straight into the token operand, the block sums and the block
+// scales, with the values and layout prefill_prep_q8k writes from the Q8_K
+// rows the quantizer would make of them (the same warp quantizer,
+// src/kernels.c:561-595): one warp per (token, super-block), lane L elements
+// 8L..8L+7. Tokens m..m_pad-1 are zero.
+template <int PLANES>
+__global__ void __launch_bounds__(256) prefill_prep_f32(const float *x, int m, int nsb, int m_pad, uint16_t *B,
+                                                        uint16_t *S, float *DA) {
+    const int64_t wid = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (wid >= (int64_t)m_pad * nsb) return;
+    const int t = (int)(wid / nsb), sb = (int)(wid - (int64_t)t * nsb);
+    const int64_t K = (int64_t)nsb * QK_K;
+    int q[8] = {0, 0, 0, 0, 0, 0, 0, 0}, bsum2 = 0;
+    float d = 0.0f;
+    if (t < m) q8k_quant_warp(x + t * K + (int64_t)sb * QK_K, lane, q, bsum2, d);
+    if (S && (lane & 1) == 0) S[(int64_t)t * (K / 16) + 16 * sb + (lane >> 1)] = __half_as_ushort(__float2half_rn((float)bsum2));
+    if (lane == 0) DA[(int64_t)sb * m_pad + t] = d;
+    float a[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) a[i] = (float)q[i];
+    // slots of each group of four hold elements 0, 2, 1, 3
+    uint16_t *row = B + (int64_t)t * K * PLANES + (int64_t)QK_K * PLANES * sb;
+    const uint4 v = make_uint4(half2_bits(a[0], a[2]), half2_bits(a[1], a[3]), half2_bits(a[4], a[6]),
+                               half2_bits(a[5], a[7]));
+    if (PLANES == 1) {
+        *reinterpret_cast<uint4 *>(row + 8 * lane) = v;
+    } else {
+        const int cq = lane >> 3, e64 = (8 * lane) & 63;
+        *reinterpret_cast<uint4 *>(row + 128 * cq + e64) = v;
+        *reinterpret_cast<uint4 *>(row + 128 * cq + 64 + e64) =
+            make_uint4(half2_bits(16.0f * a[0], 16.0f * a[2]), half2_bits(16.0f * a[1], 16.0f * a[3]),
+                       half2_bits(16.0f * a[4], 16.0f * a[6]), half2_bits(16.0f * a[5], 16.0f * a[7]));
+    }
+}
+
+// The token operand of a launch, from its f32 rows (L.xf) or its Q8_K rows.
+template <int PLANES>
+int launch_prep(const PrefillLaunch &L, int64_t nsb, int64_t m_pad, uint16_t *B, uint16_t *S, float *DA,
+                cudaStream_t st) {
+    if (L.xf) {
+        const int64_t warps = m_pad * nsb;
+        prefill_prep_f32<PLANES><<<(unsigned)((warps + 7) / 8), 256, 0, st>>>(L.xf, (int)L.m, (int)nsb, (int)m_pad, B,
+                                                                              S, DA);
+    } else {
+        prefill_prep_q8k<PLANES><<<dim3((unsigned)nsb, (unsigned)m_pad), 64, 0, st>>>(
+            static_cast<const uint8_t *>(L.xq), (int)L.m, (int)nsb, (int)m_pad, B, S, DA);
+    }
+    return cudaGetLastError() == cudaSuccess ? 0 : -2;
+}
+
 // Y = the splits' partial products added in split order (one f32 add per
 // split, the same order on every run)
 __global__ void prefill_sum_splits(const float *part, int nsplit, int64_t n, float *y) {
@@ -1487,9 +1539,7 @@ int launch_tb(const PrefillLaunch &L, cudaStream_t st) {
     uint16_t *B = reinterpret_cast<uint16_t *>(ws);
     uint16_t *S = F::MINS ? reinterpret_cast<uint16_t *>(ws + parts.b) : nullptr;
     float *DA = reinterpret_cast<float *>(ws + parts.b + parts.s);
-    prefill_prep_q8k<F::KSTEPS / 4><<<dim3((unsigned)nsb, (unsigned)m_pad), 64, 0, st>>>(
-        static_cast<const uint8_t *>(L.xq), (int)L.m, (int)nsb, (int)m_pad, B, S, DA);
-    if (cudaGetLastError() != cudaSuccess) return -2;
+    if (launch_prep<F::KSTEPS / 4>(L, nsb, m_pad, B, S, DA, st) != 0) return -2;
 
     const int64_t row_bytes = nsb * F::BLOCK;
     const void *w = L.w;
@@ -1559,9 +1609,7 @@ int launch_packed_tb(const PrefillLaunch &L, cudaStream_t st) {
     uint16_t *B = reinterpret_cast<uint16_t *>(ws);
     uint16_t *S = P::MINS ? reinterpret_cast<uint16_t *>(ws + parts.b) : nullptr;
     float *DA = reinterpret_cast<float *>(ws + parts.b + parts.s);
-    prefill_prep_q8k<P::KSTEPS / 4><<<dim3((unsigned)nsb, (unsigned)m_pad), 64, 0, st>>>(
-        static_cast<const uint8_t *>(L.xq), (int)L.m, (int)nsb, (int)m_pad, B, S, DA);
-    if (cudaGetLastError() != cudaSuccess) return -2;
+    if (launch_prep<P::KSTEPS / 4>(L, nsb, m_pad, B, S, DA, st) != 0) return -2;
     CUtensorMap tmB, tmS;
     if (!make_map(&tmB, B, (uint64_t)(K * P::KSTEPS / 4), (uint64_t)m_pad, (uint64_t)(K * P::KSTEPS / 4) * 2, PF_KS,
                   BN, CU_TENSOR_MAP_SWIZZLE_128B, 2))
@@ -1623,9 +1671,7 @@ int launch_pair_tb(const PrefillLaunch &L, cudaStream_t st) {
     uint16_t *S = P::MINS ? reinterpret_cast<uint16_t *>(ws + parts.b) : nullptr;
     float *DA = reinterpret_cast<float *>(ws + parts.b + parts.s);
     float *part = reinterpret_cast<float *>(ws + parts.b + parts.s + parts.da);
-    prefill_prep_q8k<P::KSTEPS / 4><<<dim3((unsigned)nsb, (unsigned)m_pad), 64, 0, st>>>(
-        static_cast<const uint8_t *>(L.xq), (int)L.m, (int)nsb, (int)m_pad, B, S, DA);
-    if (cudaGetLastError() != cudaSuccess) return -2;
+    if (launch_prep<P::KSTEPS / 4>(L, nsb, m_pad, B, S, DA, st) != 0) return -2;
     // each prefill copy as rows of 128 bytes: one K-step's A tile is 128 rows,
     // the mins operand 64 (the copy is already in the shared-memory layout, so
     // the maps do not swizzle)

@@ -10,11 +10,12 @@
 
 namespace sicu {
 
-// One warp quantizes one 256-element block into the raw 292-byte Q8_K layout
-// (d f32 @0, qs int8 @4, bsums int16 @260). Lane L owns elements 8L..8L+7.
-// x must be 16-byte aligned. An all-zero block writes d = 0, qs = 0 and
-// bsums = 0 (the reference leaves bsums untouched there).
-__device__ __forceinline__ void q8k_block_warp(const float *x, uint8_t *dst, int lane) {
+// One warp quantizes one 256-element block (src/kernels.c:561-595); lane L
+// owns elements 8L..8L+7 and gets their quants q[0..7], the sum of the 16
+// quants of lanes 2k and 2k+1 (bsum2: block sum k in lane 2k and 2k+1) and
+// the block scale d. An all-zero block gives d = 0 and zero quants and sums.
+// x must be 16-byte aligned.
+__device__ __forceinline__ void q8k_quant_warp(const float *x, int lane, int (&q)[8], int &bsum2, float &d) {
     const float4 v0 = reinterpret_cast<const float4 *>(x)[2 * lane];
     const float4 v1 = reinterpret_cast<const float4 *>(x)[2 * lane + 1];
     const float v[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
@@ -33,13 +34,11 @@ __device__ __forceinline__ void q8k_block_warp(const float *x, uint8_t *dst, int
         const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
         if (ob > best || (ob == best && oi < bi)) { best = ob; bi = oi; }
     }
-    uint32_t *qw = reinterpret_cast<uint32_t *>(dst + 4);
-    int16_t *bs = reinterpret_cast<int16_t *>(dst + 260);
     if (!(best > 0.0f)) {
-        qw[2 * lane] = 0u;
-        qw[2 * lane + 1] = 0u;
-        if (lane < 16) bs[lane] = 0;
-        if (lane == 0) *reinterpret_cast<float *>(dst) = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) q[i] = 0;
+        bsum2 = 0;
+        d = 0.0f;
         return;
     }
     float own = 0.0f;
@@ -47,26 +46,39 @@ __device__ __forceinline__ void q8k_block_warp(const float *x, uint8_t *dst, int
     for (int i = 0; i < 8; ++i) if ((bi & 7) == i) own = v[i];
     const float mx = __shfl_sync(0xffffffffu, own, bi >> 3);
     const float iscale = __fdiv_rn(-127.0f, mx);
-    uint32_t packed[2] = {0u, 0u};
     int sum = 0;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-        int q;
+        int qi;
         if (isnan(v[i])) {
             // the reference's magic-number rounding leaves a NaN's low payload bits
-            q = (int)(__float_as_uint(v[i]) & 0x3fffffu);
+            qi = (int)(__float_as_uint(v[i]) & 0x3fffffu);
         } else {
-            q = __float2int_rn(__fmul_rn(iscale, v[i]));
+            qi = __float2int_rn(__fmul_rn(iscale, v[i]));
         }
-        q = q < 127 ? q : 127;
-        sum += q;
-        packed[i / 4] |= ((uint32_t)q & 0xffu) << (8 * (i & 3));
+        q[i] = qi < 127 ? qi : 127;
+        sum += q[i];
     }
+    bsum2 = sum + __shfl_xor_sync(0xffffffffu, sum, 1);
+    d = __fdiv_rn(1.0f, iscale);
+}
+
+// One warp quantizes one 256-element block into the raw 292-byte Q8_K layout
+// (d f32 @0, qs int8 @4, bsums int16 @260). Lane L owns elements 8L..8L+7.
+// x must be 16-byte aligned. An all-zero block writes d = 0, qs = 0 and
+// bsums = 0 (the reference leaves bsums untouched there).
+__device__ __forceinline__ void q8k_block_warp(const float *x, uint8_t *dst, int lane) {
+    int q[8], bsum2;
+    float d;
+    q8k_quant_warp(x, lane, q, bsum2, d);
+    uint32_t packed[2] = {0u, 0u};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) packed[i / 4] |= ((uint32_t)q[i] & 0xffu) << (8 * (i & 3));
+    uint32_t *qw = reinterpret_cast<uint32_t *>(dst + 4);
     qw[2 * lane] = packed[0];
     qw[2 * lane + 1] = packed[1];
-    const int pair = sum + __shfl_xor_sync(0xffffffffu, sum, 1);
-    if ((lane & 1) == 0) bs[lane >> 1] = (int16_t)pair;
-    if (lane == 0) *reinterpret_cast<float *>(dst) = __fdiv_rn(1.0f, iscale);
+    if ((lane & 1) == 0) reinterpret_cast<int16_t *>(dst + 260)[lane >> 1] = (int16_t)bsum2;
+    if (lane == 0) *reinterpret_cast<float *>(dst) = d;
 }
 
 __device__ __forceinline__ float vmaxps(float a, float b) { return a > b ? a : b; }

@@ -140,16 +140,33 @@ def test_prefill_q4k_edge_rows(sicu, oracle):
     assert (got[3] == 0).all()
 
 
-def test_prefill_f32_entry_matches_quantized(sicu, oracle):
-    wt, n_out, n_in, m = Q.Q4_K, 256, 1024, 100
+@pytest.mark.parametrize("wt,n_out,n_in,m,packed", [
+    (Q.Q4_K, 256, 1024, 100, False),    # converter kernel
+    (Q.Q6_K, 200, 1280, 50, False),
+    (Q.Q4_K, 128, 512, 40, True),       # one row tile: one-CTA kernel from the copy
+    (Q.Q4_K, 640, 2048, 300, True),     # CTA pairs, 256-token tiles
+    (Q.Q6_K, 384, 1280, 77, True),      # CTA pairs, two planes per quarter
+])
+def test_prefill_f32_entry_matches_quantized(sicu, oracle, wt, n_out, n_in, m, packed):
+    """The f32 entries quantize inside the launch, straight into the token
+    operand: the same bits as quantizing with the reference's quantizer first
+    (zero rows and very large rows included)."""
     w = synth.weights(wt, n_out, n_in, seed=11)
     x = synth.activations(n_in, m, seed=12)
+    x[1] = 0.0
+    x[2] *= 3e4
     xq = oracle.quantize_pair(wt, x)
     dw = dev(w)
+    dp = None
+    if packed:
+        import torch
+        nb = sicu.prefill_pack_bytes(wt, n_in, n_out)
+        dp = torch.zeros(nb, dtype=torch.uint8, device="cuda")
+        sicu.prefill_pack(wt, dw, n_in, n_out, dp, nb)
     y1 = empty_f32(m, n_out)
-    sicu.gemm_prefill(wt, dw, n_in, n_out, dev(xq), m, y1)
+    sicu.gemm_prefill_packed(wt, dw, dp, n_in, n_out, dev(xq), m, y1)
     y2 = empty_f32(m, n_out)
-    sicu.gemm_prefill_f32(wt, dw, n_in, n_out, dev(x), m, y2)
+    sicu.gemm_prefill_packed_f32(wt, dw, dp, n_in, n_out, dev(x), m, y2)
     assert_bits_equal(host(y2), host(y1), "prefill f32 entry vs pre-quantized")
 
 

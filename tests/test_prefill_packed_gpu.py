@@ -287,3 +287,23 @@ def test_packed_prefill_multi_without_copies(sicu, oracle):
         one = empty_f32(m, n)
         sicu.gemm_prefill_f32(wt, w, n_in, n, x, m, one)
         assert_bits_equal(host(y), host(one), f"{n} rows without copies")
+
+
+def test_packed_prefill_many_pair_tiles(sicu, oracle):
+    """More 256-row x 256-token tiles than two waves of CTA pairs hold (150
+    on a 148-SM part), ragged tokens. Against the exact product, and the same
+    bits on a second call."""
+    wt, n_out, n_in, m = Q.Q4_K, 19200, 512, 300
+    w = synth.weights(wt, n_out, n_in, seed=21)
+    x = synth.activations(n_in, m, seed=22)
+    xq = oracle.quantize_pair(wt, x)
+    xd = _dequant_q8k(xq, n_in)
+    wd = _dequant_w(oracle, wt, w, n_in, n_out)
+    dw, dp, _ = _pack(sicu, wt, w, n_in, n_out)
+    y = empty_f32(m, n_out)
+    sicu.gemm_prefill_packed_f32(wt, dw, dp, n_in, n_out, dev(x), m, y)
+    got = host(y)
+    _check_tol(got, xd @ wd.T, np.abs(xd) @ np.abs(wd).T, "Q4_K packed prefill, 150 pair tiles")
+    y2 = empty_f32(m, n_out)
+    sicu.gemm_prefill_packed_f32(wt, dw, dp, n_in, n_out, dev(x), m, y2)
+    assert_bits_equal(host(y2), got, "second run")

@@ -37,8 +37,11 @@
 // Weights stream through a ring of shared-memory stages (16 rows x four
 // super-blocks) filled by 1-D bulk copies, one per row (rows that do not
 // start on a 16-byte boundary are copied from the boundary below and read
-// with funnel shifts). Every wait is bounded and reports through the status
-// word.
+// with funnel shifts), issued by a fifth warp that refills a stage once the
+// four compute warps have released it: issuing a stage's 16 copies takes
+// ~1 us, which in a compute warp held every round's barrier. The compute
+// warps' round barrier is a named barrier of their 128 threads. Every wait
+// is bounded and reports through the status word.
 #include "common.cuh"
 #include "launch.h"
 #include "quantize.cuh"
@@ -56,6 +59,7 @@ constexpr int BREC_BYTES = 4096 + 32;
 // the elements e, e+64, e+8, e+72 of lane class l
 
 __device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 __device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 __device__ __forceinline__ uint32_t f16x2_of_ints(int a, int b) {
@@ -106,7 +110,21 @@ __global__ void __launch_bounds__(256) batch_prep_kernel(const float *xf, const 
 }
 
 constexpr int BATCH_MATS = 16;
-constexpr int BW = 4;                   // warps per CTA = super-blocks per round
+constexpr int BW = 4;                   // compute warps per CTA = super-blocks per round
+constexpr int BT = (BW + 1) * 32;       // threads per CTA: the compute warps and the producer warp
+
+// barrier of the compute warps' BW * 32 threads (named barrier 1), true if
+// any of them passes true
+__device__ __forceinline__ bool compute_bar_or(bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred a, b;\n\t"
+        "setp.ne.u32 a, %1, 0;\n\t"
+        "bar.red.or.pred b, 1, %2, a;\n\t"
+        "selp.u32 %0, 1, 0, b;\n\t}"
+        : "=r"(r) : "r"((uint32_t)v), "n"(BW * 32) : "memory");
+    return r != 0;
+}
 constexpr int NPAIR = 16 * BATCH_MAX;   // (row, token) pairs of a tile
 // float terms of a round, double buffered: lane terms [buffer 2][warp][pair 128][8],
 // then the dmin terms [buffer 2][warp][pair 128]
@@ -350,13 +368,14 @@ __device__ __forceinline__ void batch_superblock(const uint8_t *b0, const uint8_
 }
 
 template <uint32_t T>
-__global__ void __launch_bounds__(BW * 32, 3) gemv_batch_kernel(const __grid_constant__ BatchParams p) {
+__global__ void __launch_bounds__(BT, 2) gemv_batch_kernel(const __grid_constant__ BatchParams p) {
     constexpr int UB = BFmt<T>::ub;
     constexpr bool Q4 = T == T_Q4_K;
     extern __shared__ __align__(128) uint8_t smem[];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
     const int S = p.nstages, R = p.rounds;
-    uint64_t *full = reinterpret_cast<uint64_t *>(smem);   // [S <= 8]
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem);        // [S <= 8] stage landed (bytes)
+    uint64_t *empty = reinterpret_cast<uint64_t *>(smem + 64);  // [S <= 8] stage released (BW warps)
     float *terms = reinterpret_cast<float *>(smem + 128);
     uint8_t *ring = smem + 128 + TERMS_BYTES;
     const int stage_bytes = 16 * p.rs;
@@ -364,7 +383,10 @@ __global__ void __launch_bounds__(BW * 32, 3) gemv_batch_kernel(const __grid_con
     const int Q = my_tiles * R;
 
     if (tid == 0) {
-        for (int i = 0; i < S; ++i) mbar_init(smem_addr(&full[i]), 16);
+        for (int i = 0; i < S; ++i) {
+            mbar_init(smem_addr(&full[i]), 16);
+            mbar_init(smem_addr(&empty[i]), BW);
+        }
         fence_mbar_init();
     }
     __syncthreads();
@@ -410,8 +432,23 @@ __global__ void __launch_bounds__(BW * 32, 3) gemv_batch_kernel(const __grid_con
         if (bulk > 0) bulk_g2s_hint(smem_addr(dst), al, (uint32_t)bulk, bar, policy);
     };
 
-    if (warp == 0)
-        for (int q = 0; q < Q && q < S; ++q) produce(q, q);   // weights never depend on earlier kernels
+    if (warp == BW) {
+        // producer: the first stages right away (weights never depend on
+        // earlier kernels), then each stage again once the compute warps have
+        // released it
+        for (int q = 0; q < Q; ++q) {
+            const int s = q % S;
+            if (q >= S) {
+                const bool ok = mbar_wait(smem_addr(&empty[s]), (uint32_t)((q / S - 1) & 1));
+                if (!__all_sync(0xffffffffu, ok)) {
+                    if (lane == 0) atomicOr(p.status, STATUS_WAIT_TIMEOUT);
+                    break;
+                }
+            }
+            produce(q, s);
+        }
+        return;
+    }
     grid_dep_wait();                                          // the activation records do
 
     // this warp's activation fragments for its next super-block
@@ -478,10 +515,14 @@ __global__ void __launch_bounds__(BW * 32, 3) gemv_batch_kernel(const __grid_con
                 failed = true;
             }
         }
-        // terms written and the stage consumed by every warp. No load of this
-        // thread is in flight here (a barrier waits for them), so the next
-        // round's loads are issued after it.
-        if (__syncthreads_or(failed)) {
+        // this warp is done with the stage (every compute warp releases it,
+        // with or without a super-block in it)
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_addr(&empty[s]));
+        // terms written by every compute warp. No load of this thread is in
+        // flight here (a barrier waits for them), so the next round's loads
+        // are issued after it.
+        if (compute_bar_or(failed)) {
             failed = true;
             break;
         }
@@ -490,7 +531,6 @@ __global__ void __launch_bounds__(BW * 32, 3) gemv_batch_kernel(const __grid_con
             const int un = rn * BW + warp;
             if (q + 1 < Q && un < p.nb) load_rec(un);
         }
-        if (warp == 0 && q + S < Q) produce(q + S, s);
         // chains: the round's super-blocks in order
         for (int w = 0; w < cnt; ++w) {
             const float4 *tl = reinterpret_cast<const float4 *>(terms + ((size_t)(buf * BW + w) * NPAIR + tid) * 8);
@@ -564,8 +604,10 @@ static int launch_batch_t(const BatchLaunch &L, cudaStream_t st) {
         while (((rs >> 4) & 7) < 2 || ((rs >> 4) & 7) > 6) rs += 16;
     p.rs = rs;
     const int stage = 16 * rs;
-    // three CTAs per SM with at least three stages each, else two; at most eight
-    int per_sm = 3, stages = 0;
+    // two CTAs per SM (the compute warps need ~168 registers: with the
+    // producer warp, three CTAs would leave them 128 and spill), at most
+    // eight stages each
+    int per_sm = 2, stages = 0;
     for (; per_sm >= 2; --per_sm) {
         const int budget = L.smem_per_sm / per_sm - L.smem_reserved - 128 - TERMS_BYTES;
         stages = budget / stage;
@@ -608,7 +650,7 @@ static int launch_batch_t(const BatchLaunch &L, cudaStream_t st) {
     }
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3((unsigned)grid);
-    cfg.blockDim = dim3(BW * 32);
+    cfg.blockDim = dim3(BT);
     cfg.dynamicSmemBytes = (size_t)smem;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];

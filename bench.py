@@ -390,8 +390,8 @@ def model_prefill(torch, s, shape, dev, stream, world, rank, group, m_tok, reps)
            "TFLOPs": round(tflops, 1), "f16_tensor_frac": round(tflops / f16_peak, 4),
            "int8_tensor_frac_proxy": round(tflops / (2 * f16_peak), 4), "peak_kind": kind,
            "pack_bytes_per_gpu": int(sum(t.numel() for t in m.pack.values())),
-           "note": "tensor-core kernel for Q4_K and Q6_K (kind::f16 MMAs on exact f16 (scale x quant) operands) "
-                   "reading the prefill copies of the weights; int8 peak taken as 2x the measured bf16 dense peak"}
+           "note": "tensor-core kernels (kind::f16 MMAs on exact f16 (scale x quant) operands) reading the "
+                   "prefill copies of the Q4_K and Q6_K weights; int8 peak taken as 2x the measured bf16 dense peak"}
     del m
     torch.cuda.empty_cache()
     return out
@@ -588,6 +588,54 @@ def per_format(torch, s, dev, stream, l2: int) -> dict:
     return out
 
 
+PREFILL_FORMAT_SHAPES = [(14336, 4096), (4096, 4096)]
+
+
+def prefill_per_format(torch, s, dev, stream, m_tok: int = 512) -> dict:
+    """Every K format's tensor-core prompt product from its prefill copy
+    (sicu_gemm_prefill_packed_f32, f32 prompt rows quantized inside the
+    launch): TFLOP/s = 2 m rows K / device time, against the measured f16
+    dense peak (the kernels run kind::f16 MMAs on exact f16 scale x quant)."""
+    try:
+        f16_peak = float(json.loads(PEAKS.read_text())["bf16_tflops"])
+        kind = "measured"
+    except Exception:
+        f16_peak, kind = 1590.0, "fallback"
+    out = {"prompt_tokens": m_tok, "f16_peak_TFLOPs": f16_peak, "peak_kind": kind}
+    h = stream.cuda_stream
+    x = torch.from_numpy(synth.activations(max(k for _, k in PREFILL_FORMAT_SHAPES), m_tok, seed=3)).to(dev)
+    for wt in (Q.Q4_K, Q.Q5_K, Q.Q6_K, Q.Q3_K, Q.Q2_K):
+        row = {}
+        for n_out, n_in in PREFILL_FORMAT_SHAPES:
+            w = bench_weights(wt, n_out, n_in, 31, dev)
+            nb = s.prefill_pack_bytes(wt, n_in, n_out)
+            pk = torch.empty(nb, dtype=torch.uint8, device=dev)
+            s.prefill_pack(wt, w, n_in, n_out, pk, nb, stream=h)
+            xi = x[:, :n_in].contiguous()
+            y = torch.empty(m_tok, n_out, device=dev)
+
+            def run():
+                s.gemm_prefill_packed_f32(wt, w, pk, n_in, n_out, xi, m_tok, y, stream=h)
+
+            with torch.cuda.stream(stream):
+                run()                      # sizes the workspace outside capture
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                for _ in range(4):
+                    run()
+            ms = _time_graph(torch, g, stream, 3, 1, dev) / 12
+            del g
+            tf = 2.0 * m_tok * n_out * n_in / (ms * 1e-3) / 1e12
+            row[f"{n_out}x{n_in}"] = {"us": round(ms * 1e3, 1), "TFLOPs": round(tf, 1),
+                                      "f16_frac": round(tf / f16_peak, 4)}
+            del w, pk, y
+        out[Q.NAMES[wt]] = row
+    torch.cuda.empty_cache()
+    assert s.status() == 0, "a prefill wait gave up"
+    return out
+
+
 TP_ROWS = ("decode_b1", "decode_b1_steps", "decode_b1_full", "decode_b1_nccl", "decode_b8", "prefill512")
 
 
@@ -658,6 +706,7 @@ def model_metrics(torch, s, dev, stream, world, rank, quick: bool) -> tuple[dict
                                              attention_ctx=512)}
         out["prefill"] = {"config": "configs[3] Llama-3-8B shape, 512-token prompt, matrix path",
                           **model_prefill(torch, s, sm.LLAMA3_8B, dev, stream, 1, 0, None, 512, max(2, reps // 2))}
+        out["prefill_per_format"] = prefill_per_format(torch, s, dev, stream)
     out["scope"] = ("every weight-matrix product of the forward pass (per layer Wq, Wk, Wv, Wo, W_gate, W_up, "
                     "W_down; then the output head) with synthetic Q4_K_M-style weights; the *_steps lines also run "
                     "the residual adds, RMS norms and SwiGLU between them, fused into the products (Wo reading a "

@@ -208,8 +208,12 @@ SICU_API int sicu_gemv_host_noalloc(uint32_t wtype, const void *dw, int64_t n_in
  * memory, the token operand loaded by TMA): the integer sums per super-block are exact
  * and the d / dmin scaling is applied per super-block, so each output agrees
  * with the reference's per-row dot (src/kernels.c:349-410) within a relative
- * 1e-5 of the L1 norm of its products, but is not bit-identical. Other types
- * run the decode matvec once per token (bit-identical to the reference).
+ * 1e-5 of the L1 norm of its products, but is not bit-identical. Q5_K, Q3_K
+ * and Q2_K (src/kernels.c:412-478, 289-347, 249-287) run on the same tensor
+ * cores for m > 32, from a prefill copy (below) that the call first writes
+ * into the workspace when the caller has none; at most 32 tokens, they and
+ * the other types run the decode matvec once per token (bit-identical to the
+ * reference).
  * The reference has no batched product: its prompt loop calls
  * si_engine_forward once per token (src/cmd_run.c:276), i.e. one backend gemv
  * per token and matrix. When a product has fewer 128-row x token tiles than
@@ -223,15 +227,17 @@ SICU_API int sicu_gemm_prefill_f32(uint32_t wtype, const void *dw, int64_t n_in,
                                    const float *dx, int64_t m, float *dy, void *stream);
 
 /* ---- prefill copies of the weights -----------------------------------------
- * A second, re-tiled copy of a Q4_K or Q6_K matrix for prompt products, made
+ * A second, re-tiled copy of a K-format (Q2_K ... Q6_K) matrix for prompt products, made
  * once when the weights are loaded (the reference makes its tensor views at
  * load, si_tensor_from_gguf, src/backend.c:144-176); the raw GGUF bytes stay
  * on the device for decode. Per 128-row tile and super-block the copy holds
  * the exact f16 (scale x quant) operands in the shared-memory layout the
  * tensor cores read (128-byte swizzle), the mins operand and the row scales,
  * so the prefill kernel streams it with bulk copies and converts nothing.
- * Size: 4x64 KiB + 8.5 KiB per 128 rows and super-block for Q4_K (about 3.6x
- * the raw bytes), 8x16 KiB + 0.5 KiB for Q6_K (about 4.9x).
+ * Size per 128 rows and super-block: 4x16 KiB + 8.5 KiB for Q4_K, Q5_K and
+ * Q2_K (about 3.6x, 3.3x and 6.9x the raw bytes), 4x16 KiB + 0.5 KiB for
+ * Q3_K (4.7x), 8x16 KiB + 0.5 KiB for Q6_K (4.9x). Q5_K, Q3_K and Q2_K have
+ * one exact f16 plane of scale x quant per K-step (|sc q| <= 1953, 128, 45).
  * sicu_prefill_pack_bytes: the copy's size (SICU_ENOTSUP for other types).
  * sicu_prefill_pack: writes the copy of device weights dw into dpack
  * (pack_bytes >= that size, 16-byte aligned), asynchronously on stream.

@@ -558,8 +558,12 @@ static int prefill_common(uint32_t wtype, const void *dw, int64_t n_in, int64_t 
         float *y1[1] = {dy};
         return batch_common(wtype, 1, w1, &n_out, n_in, xf, xq, m, y1, st);
     }
-    if (!prefill_supported(wtype)) {
-        // formats without a tensor-core kernel: the decode matvec per token
+    // Q2_K, Q3_K, Q5_K have tensor-core kernels only for the prefill copy:
+    // without a copy of the caller's, the product makes one in the workspace
+    const bool copy_only = !prefill_supported(wtype) && prefill_pack_supported(wtype);
+    if (!prefill_supported(wtype) && !(copy_only && m > PREFILL_PACKED_MIN_M)) {
+        // formats without a tensor-core kernel (and copy-only formats for
+        // blocks of at most 32 tokens): the decode matvec per token
         const int64_t prb = pair_row_bytes(pair, n_in);
         for (int64_t i = 0; i < m; ++i) {
             GemvLaunch L = make_launch(*ds, dw, n_in, n_out, dy + i * n_out);
@@ -570,8 +574,16 @@ static int prefill_common(uint32_t wtype, const void *dw, int64_t n_in, int64_t 
         return SICU_OK;
     }
     // f32 rows are quantized inside the launch, straight into the token operand
-    if (int rc = grow_prefill_ws(*ds, prefill_workspace_bytes(wtype, n_in, n_out, m, ds->sms, pack != nullptr)))
-        return rc;
+    size_t need = prefill_workspace_bytes(wtype, n_in, n_out, m, ds->sms, pack != nullptr || copy_only);
+    const size_t pack_off = (need + 255) & ~size_t(255);
+    const bool own_copy = copy_only && !pack;
+    if (own_copy) need = pack_off + prefill_pack_bytes(wtype, n_in, n_out);
+    if (int rc = grow_prefill_ws(*ds, need)) return rc;
+    if (own_copy) {
+        pack = static_cast<uint8_t *>(ds->pf_ws) + pack_off;
+        if (launch_prefill_pack(wtype, dw, n_in, n_out, const_cast<void *>(pack), st) != 0)
+            return cuda_fail(cudaGetLastError(), "prefill pack launch");
+    }
     PrefillLaunch L{};
     L.w = dw;
     L.n_in = n_in;
@@ -611,7 +623,7 @@ int sicu_gemm_prefill_f32(uint32_t wtype, const void *dw, int64_t n_in, int64_t 
 
 // ---- prefill copies of the weights ---------------------------------------------------
 static int check_pack_shape(const char *what, uint32_t wtype, int64_t n_in, int64_t n_out) {
-    if (!prefill_supported(wtype))
+    if (!prefill_pack_supported(wtype))
         return fail(SICU_ENOTSUP, "%s: no tensor-core prefill kernel for %s (%u)", what, tname(wtype), wtype);
     if (n_in <= 0 || n_out < 0 || n_in % QK_K || n_in > (int64_t)1 << 20 || n_out > (int64_t)1 << 30)
         return fail(SICU_EINVAL, "%s: bad shape n_in=%lld n_out=%lld", what, (long long)n_in, (long long)n_out);
@@ -644,7 +656,7 @@ int sicu_prefill_pack(uint32_t wtype, const void *dw, int64_t n_in, int64_t n_ou
 
 static int check_packed(uint32_t wtype, const void *dpack) {
     if (!dpack) return SICU_OK;
-    if (!prefill_supported(wtype))
+    if (!prefill_pack_supported(wtype))
         return fail(SICU_EINVAL, "prefill: %s has no prefill copy (no tensor-core kernel)", tname(wtype));
     if (!aligned(dpack, 16)) return fail(SICU_EINVAL, "prefill: packed copy must be 16-byte aligned");
     return SICU_OK;
@@ -685,7 +697,7 @@ int sicu_gemm_prefill_multi_f32(uint32_t wtype, int n_mats, const void *const *d
     if (m == 0) return current_ok();
     if (!aligned(dx, 16)) return fail(SICU_EINVAL, "prefill multi: f32 activation must be 16-byte aligned");
     const cudaStream_t st = (cudaStream_t)stream;
-    bool grouped = dpack && n_mats > 1 && m > PREFILL_PACKED_MIN_M && prefill_supported(wtype);
+    bool grouped = dpack && n_mats > 1 && m > PREFILL_PACKED_MIN_M && prefill_pack_supported(wtype);
     for (int i = 0; grouped && i < n_mats; ++i) grouped = dpack[i] && n_out[i] > 0;
     if (!grouped) {
         // the products one by one (a few tokens: one batch launch for all)

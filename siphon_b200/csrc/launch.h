@@ -115,7 +115,13 @@ struct PrefillLaunch {
     int64_t n_outm[PREFILL_MAXM];
     float *ym[PREFILL_MAXM];
 };
+// Q4_K, Q6_K: tensor-core kernels from the raw blocks (converters) and from
+// the prefill copies
 bool prefill_supported(uint32_t wtype);
+// Q2_K ... Q6_K: a prefill copy and the kernels that read it (m > 32 tokens);
+// Q2_K, Q3_K and Q5_K have no converter kernel, so without a copy of their own
+// a product first makes one in the workspace
+bool prefill_pack_supported(uint32_t wtype);
 size_t prefill_workspace_bytes(uint32_t wtype, int64_t n_in, int64_t n_out, int64_t m, int num_sms, bool packed);
 // a group of nmat matrices read from their prefill copies (m > 32)
 size_t prefill_group_workspace_bytes(uint32_t wtype, int64_t n_in, int nmat, const int64_t *n_out, int64_t m,
@@ -124,7 +130,8 @@ size_t prefill_group_workspace_bytes(uint32_t wtype, int64_t n_in, int nmat, con
 size_t prefill_pack_bytes(uint32_t wtype, int64_t n_in, int64_t n_out);
 // writes the prefill copy of the weight blocks w into pack; -3: unsupported type
 int launch_prefill_pack(uint32_t wtype, const void *w, int64_t n_in, int64_t n_out, void *pack, cudaStream_t st);
-// -3: no tensor-core kernel for the type; -4: tensor map encoding failed; -2: launch
+// -3: no tensor-core kernel for the type (or, for a type without converters,
+// no copy or m <= 32); -4: tensor map encoding failed; -2: launch
 int launch_prefill(uint32_t wtype, const PrefillLaunch &L, cudaStream_t st);
 
 // batch decode matvec on the tensor cores: y[i][t][r] = (W_i x_t)[r] for

@@ -663,6 +663,72 @@ template <> struct PkFmt<T_Q6_K> {
     static constexpr int KSTEPS = 8, RAW_ROW = 240;
     static constexpr bool MINS = false;
 };
+// Q5_K, Q3_K, Q2_K have a prefill copy but no converter kernel: their K-step
+// tiles hold one exact f16 plane of integer scale x quant, in the Q4_K slot
+// order, so they share the Q4_K token operand; Q5_K and Q2_K carry a mins
+// operand (Q2_K: one min per 16 elements, i.e. per bsums index).
+template <> struct PkFmt<T_Q5_K> {
+    static constexpr int KSTEPS = 4, RAW_ROW = 176;
+    static constexpr bool MINS = true;
+};
+template <> struct PkFmt<T_Q3_K> {
+    static constexpr int KSTEPS = 4, RAW_ROW = 112;
+    static constexpr bool MINS = false;
+};
+template <> struct PkFmt<T_Q2_K> {
+    static constexpr int KSTEPS = 4, RAW_ROW = 96;
+    static constexpr bool MINS = true;
+};
+
+// Integer main-term weight (sub-block scale x quant) of element e (0..255) of
+// one super-block, as the reference's dots form it:
+//   Q5_K src/kernels.c:412-478: sc (6-bit, src/kernels.c:648-656) x (nibble +
+//        16 x qh bit), qs[32c + l] low nibble = element 64c + l, high nibble
+//        = 64c + 32 + l, qh[l] bit 2c / 2c + 1;
+//   Q3_K src/kernels.c:289-347: (sc - 32) x ((qs[32n + l] >> 2j) & 3) - (4
+//        unless hmask[l] bit 4n + j), element 128n + 32j + l;
+//   Q2_K src/kernels.c:249-287: (scales[e / 16] & 15) x ((qs[32n + l] >> 2j)
+//        & 3), element 128n + 32j + l.
+// b: the block's bytes in shared memory.
+__device__ __forceinline__ int k4_scale6(const uint8_t *q, int j) {   // 6-bit scale j of the 12 packed bytes
+    return j < 4 ? (q[j] & 63) : ((q[j + 4] & 0xf) | ((q[j - 4] >> 6) << 4));
+}
+__device__ __forceinline__ int k4_min6(const uint8_t *q, int j) {     // 6-bit min j
+    return j < 4 ? (q[j + 4] & 63) : ((q[j + 4] >> 4) | ((q[j] >> 6) << 4));
+}
+template <uint32_t T>
+__device__ __forceinline__ int pk_int_weight(const uint8_t *b, int e) {
+    if constexpr (T == T_Q5_K) {
+        const int c = e >> 6, hi = (e >> 5) & 1, l = e & 31;
+        const int qs = b[48 + 32 * c + l];
+        const int q = (hi ? qs >> 4 : qs & 15) | (((b[16 + l] >> (2 * c + hi)) & 1) << 4);
+        return k4_scale6(b + 4, e >> 5) * q;
+    } else if constexpr (T == T_Q3_K) {
+        const int n = e >> 7, j = (e >> 5) & 3, l = e & 31;
+        const int q = ((b[32 + 32 * n + l] >> (2 * j)) & 3) - (((b[l] >> (4 * n + j)) & 1) ? 0 : 4);
+        const int s = e >> 4;   // 16 6-bit scales in 12 bytes (src/kernels.c:328-333)
+        const uint8_t *sc = b + 96;
+        const int lo = s < 8 ? (sc[s & 7] & 15) : (sc[s & 7] >> 4);
+        const int hi2 = (sc[8 + (s & 3)] >> (2 * (s >> 2))) & 3;
+        return ((lo | (hi2 << 4)) - 32) * q;
+    } else {
+        const int n = e >> 7, j = (e >> 5) & 3, l = e & 31;
+        return (b[e >> 4] & 15) * ((b[16 + 32 * n + l] >> (2 * j)) & 3);
+    }
+}
+
+// The exponent s of the row scale f = d 2^s (s >= 0 the smallest keeping
+// (dmin / f) x min inside f16 range), as q4k_scale_exp, for the given d, dmin
+// and largest min; keep_main is false when d is zero or negligible.
+__device__ __forceinline__ void pk_scale_exp(float d, float dmin, int mn_max, int &sexp, bool &keep_main) {
+    sexp = 0;
+    keep_main = d != 0.0f;
+    if (keep_main) {
+        const float ratio = fabsf(dmin) * (float)mn_max / (60000.0f * fabsf(d));
+        if (ratio > 1.0f) sexp = ilogbf(ratio) + 1;
+        if (sexp > 14) keep_main = false;
+    }
+}
 constexpr int PK_ATILE = PF_BM * PF_KS * 2;   // 16 KB: one K-step of a 128-row tile
 constexpr int PK_MINT = PF_BM * 16 * 2;       // 4 KB: one half of the mins operand
 template <uint32_t T> __host__ __device__ constexpr int pk_off_min() { return PkFmt<T>::KSTEPS * PK_ATILE; }
@@ -683,11 +749,18 @@ __global__ void __launch_bounds__(PF_BM) prefill_pack_kernel(const uint8_t *w, i
     // this row's block into shared memory, 16-byte aligned (Q6_K blocks start
     // at any even byte)
     uint8_t *mine = raw + r * P::RAW_ROW;
-    if (T == T_Q4_K) {
-        const uint4 *src = reinterpret_cast<const uint4 *>(w + row * row_bytes + (int64_t)sb * B_Q4_K);
+    if (T == T_Q4_K || T == T_Q5_K) {
+        constexpr int BLK = T == T_Q4_K ? B_Q4_K : B_Q5_K;
+        const uint4 *src = reinterpret_cast<const uint4 *>(w + row * row_bytes + (int64_t)sb * BLK);
 #pragma unroll
-        for (int k = 0; k < B_Q4_K / 16; ++k)
+        for (int k = 0; k < BLK / 16; ++k)
             reinterpret_cast<uint4 *>(mine)[k] = valid ? src[k] : make_uint4(0, 0, 0, 0);
+    } else if (T == T_Q3_K || T == T_Q2_K) {
+        // 110- and 84-byte blocks start at any even byte
+        constexpr int BLK = T == T_Q3_K ? B_Q3_K : B_Q2_K;
+        const uint16_t *src = reinterpret_cast<const uint16_t *>(w + row * row_bytes + (int64_t)sb * BLK);
+        for (int k = 0; k < P::RAW_ROW / 2; ++k)
+            reinterpret_cast<uint16_t *>(mine)[k] = (valid && k < BLK / 2) ? src[k] : (uint16_t)0;
     } else {
         const uint16_t *src = reinterpret_cast<const uint16_t *>(w + row * row_bytes + (int64_t)sb * B_Q6_K);
         for (int k = 0; k < P::RAW_ROW / 2; ++k)
@@ -727,7 +800,7 @@ __global__ void __launch_bounds__(PF_BM) prefill_pack_kernel(const uint8_t *w, i
             q4k_kstep_words(h, x, c, sexp, valid && keep_main, v);
             put_a(c, v);
         }
-    } else {
+    } else if constexpr (T == T_Q6_K) {
         uint32_t S[5];
         span_words<5>(a + 192, 0, S);
         fdst[r] = valid ? h2f(S[4] & 0xffffu) : 0.0f;
@@ -736,6 +809,65 @@ __global__ void __launch_bounds__(PF_BM) prefill_pack_kernel(const uint8_t *w, i
             q6k_quarter_words(a, 0, S, valid, cq, p0, p1);
             put_a(2 * cq, p0);
             put_a(2 * cq + 1, p1);
+        }
+    } else {
+        // Q5_K / Q3_K / Q2_K: made once at load, so plain per-element code.
+        // Main plane: (sc q) 2^-s, exact in f16 (|sc q| <= 1953, 128, 45);
+        // mins (Q5_K: mn[i / 2], Q2_K: m[i] for bsums index i): -(dmin / f)
+        // min as hi + lo f16 parts.
+        const uint8_t *b = mine;
+        float d = 0.0f, dmin = 0.0f;
+        int mins[16] = {};
+        int mn_max = 0;
+        if constexpr (T == T_Q5_K) {
+            d = h2f(b[0] | (b[1] << 8));
+            dmin = h2f(b[2] | (b[3] << 8));
+            for (int i = 0; i < 16; ++i) mins[i] = k4_min6(b + 4, i >> 1);
+        } else if constexpr (T == T_Q2_K) {
+            d = h2f(b[80] | (b[81] << 8));
+            dmin = h2f(b[82] | (b[83] << 8));
+            for (int i = 0; i < 16; ++i) mins[i] = b[i] >> 4;
+        } else {
+            d = h2f(b[108] | (b[109] << 8));
+        }
+        for (int i = 0; i < 16; ++i) mn_max = max(mn_max, mins[i]);
+        int sexp = 0;
+        bool keep_main = d != 0.0f;
+        if (P::MINS) pk_scale_exp(d, dmin, mn_max, sexp, keep_main);
+        const float f = !P::MINS ? d : keep_main ? ldexpf(d, sexp) : ldexpf(dmin, -10);
+        fdst[r] = valid ? f : 0.0f;
+        const bool on = valid && keep_main;
+        const float s2 = ldexpf(1.0f, -sexp);
+        for (int t = 0; t < 4; ++t) {
+            uint32_t v[32];
+#pragma unroll 4
+            for (int wi = 0; wi < 32; ++wi) {
+                // word wi: slots 2 wi, 2 wi + 1 = elements 4 (wi / 2) + (wi % 2) and that + 2
+                const int e0 = 64 * t + 4 * (wi >> 1) + (wi & 1);
+                const float v0 = on ? (float)pk_int_weight<T>(b, e0) * s2 : 0.0f;
+                const float v1 = on ? (float)pk_int_weight<T>(b, e0 + 2) * s2 : 0.0f;
+                v[wi] = half2_bits(v0, v1);
+            }
+            put_a(t, v);
+        }
+        if constexpr (P::MINS) {
+            const float mfac = f != 0.0f ? dmin / f : 0.0f;
+            uint32_t mw[16];
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+                const float m0 = mfac * (float)mins[2 * c], m1 = mfac * (float)mins[2 * c + 1];
+                const float h0 = __half2float(__float2half_rn(m0)), h1 = __half2float(__float2half_rn(m1));
+                mw[c] = valid ? half2_bits(-h0, -h1) : 0u;
+                mw[8 + c] = valid ? half2_bits(h0 - m0, h1 - m1) : 0u;
+            }
+            for (int half = 0; half < 2; ++half) {
+                uint8_t *dst = chunk + pk_off_min<T>() + half * PK_MINT + r * 32;
+#pragma unroll
+                for (int j = 0; j < 2; ++j) {
+                    const uint32_t *m4 = mw + 8 * half + 4 * j;
+                    reinterpret_cast<uint4 *>(dst)[j ^ ((r >> 2) & 1)] = make_uint4(m4[0], m4[1], m4[2], m4[3]);
+                }
+            }
         }
     }
 }
@@ -1515,9 +1647,10 @@ WsParts ws_parts(uint32_t wtype, int64_t n_in, int64_t n_out, int64_t m, int num
     const int64_t bn = packed ? pk_bn(m) : PF_BN;
     const int64_t m_pad = (m + bn - 1) / bn * bn;
     const int planes = wtype == T_Q6_K ? 2 : 1;
+    const bool mins = wtype == T_Q4_K || wtype == T_Q5_K || wtype == T_Q2_K;   // PkFmt<T>::MINS
     WsParts w{};
     w.b = align256((size_t)m_pad * n_in * 2 * planes);
-    w.s = wtype == T_Q4_K ? align256((size_t)m_pad * (n_in / 16) * 2) : 0;
+    w.s = mins ? align256((size_t)m_pad * (n_in / 16) * 2) : 0;
     w.da = align256((size_t)(n_in / QK_K) * m_pad * 4);
     const int64_t rb = n_in / QK_K * B_Q6_K;
     w.pad = (!packed && wtype == T_Q6_K && rb % 16) ? align256((size_t)n_out * ((rb + 15) & ~int64_t(15))) : 0;
@@ -1758,10 +1891,25 @@ int launch_t(const PrefillLaunch &L, cudaStream_t st) {
     return L.m <= PF_BN_SMALL ? launch_tb<T, PF_BN_SMALL>(L, st) : launch_tb<T, PF_BN>(L, st);
 }
 
+// formats with a prefill copy but no converter kernel: the copy only, and
+// blocks of more than PF_BN_SMALL tokens
+template <uint32_t T>
+int launch_pk_t(const PrefillLaunch &L, cudaStream_t st) {
+    if (!L.pack || L.m <= PF_BN_SMALL) return -3;
+    if (L.nmat > 1 || use_pair(L.n_out))
+        return pk_bn(L.m) == 256 ? launch_pair_tb<T, 256>(L, st) : launch_pair_tb<T, PF_BN>(L, st);
+    return pk_bn(L.m) == 256 ? launch_packed_tb<T, 256>(L, st) : launch_packed_tb<T, PF_BN>(L, st);
+}
+
+template <uint32_t T>
+constexpr int64_t block_bytes() {
+    return T == T_Q4_K ? B_Q4_K : T == T_Q5_K ? B_Q5_K : T == T_Q6_K ? B_Q6_K : T == T_Q3_K ? B_Q3_K : B_Q2_K;
+}
+
 template <uint32_t T>
 int launch_pack_t(const void *w, int64_t n_in, int64_t n_out, void *pack, cudaStream_t st) {
     const int64_t nsb = n_in / QK_K, nrt = (n_out + PF_BM - 1) / PF_BM;
-    const int64_t row_bytes = nsb * (T == T_Q4_K ? B_Q4_K : B_Q6_K);
+    const int64_t row_bytes = nsb * block_bytes<T>();
     prefill_pack_kernel<T><<<dim3((unsigned)nrt, (unsigned)nsb), PF_BM, 0, st>>>(
         static_cast<const uint8_t *>(w), row_bytes, (int)n_out, (int)nsb, static_cast<uint8_t *>(pack));
     return cudaGetLastError() == cudaSuccess ? 0 : -2;
@@ -1770,6 +1918,9 @@ int launch_pack_t(const void *w, int64_t n_in, int64_t n_out, void *pack, cudaSt
 }  // namespace
 
 bool prefill_supported(uint32_t wtype) { return wtype == T_Q4_K || wtype == T_Q6_K; }
+bool prefill_pack_supported(uint32_t wtype) {
+    return wtype == T_Q2_K || wtype == T_Q3_K || wtype == T_Q4_K || wtype == T_Q5_K || wtype == T_Q6_K;
+}
 
 size_t prefill_workspace_bytes(uint32_t wtype, int64_t n_in, int64_t n_out, int64_t m, int num_sms, bool packed) {
     const WsParts w = ws_parts(wtype, n_in, n_out, m, num_sms, packed && m > PF_BN_SMALL);
@@ -1788,6 +1939,9 @@ size_t prefill_pack_bytes(uint32_t wtype, int64_t n_in, int64_t n_out) {
     switch (wtype) {
         case T_Q4_K: return (size_t)(nrt * nsb) * (size_t)pk_chunk<T_Q4_K>();
         case T_Q6_K: return (size_t)(nrt * nsb) * (size_t)pk_chunk<T_Q6_K>();
+        case T_Q5_K: return (size_t)(nrt * nsb) * (size_t)pk_chunk<T_Q5_K>();
+        case T_Q3_K: return (size_t)(nrt * nsb) * (size_t)pk_chunk<T_Q3_K>();
+        case T_Q2_K: return (size_t)(nrt * nsb) * (size_t)pk_chunk<T_Q2_K>();
         default: return 0;
     }
 }
@@ -1796,6 +1950,9 @@ int launch_prefill_pack(uint32_t wtype, const void *w, int64_t n_in, int64_t n_o
     switch (wtype) {
         case T_Q4_K: return launch_pack_t<T_Q4_K>(w, n_in, n_out, pack, st);
         case T_Q6_K: return launch_pack_t<T_Q6_K>(w, n_in, n_out, pack, st);
+        case T_Q5_K: return launch_pack_t<T_Q5_K>(w, n_in, n_out, pack, st);
+        case T_Q3_K: return launch_pack_t<T_Q3_K>(w, n_in, n_out, pack, st);
+        case T_Q2_K: return launch_pack_t<T_Q2_K>(w, n_in, n_out, pack, st);
         default: return -3;
     }
 }
@@ -1804,6 +1961,9 @@ int launch_prefill(uint32_t wtype, const PrefillLaunch &L, cudaStream_t st) {
     switch (wtype) {
         case T_Q4_K: return launch_t<T_Q4_K>(L, st);
         case T_Q6_K: return launch_t<T_Q6_K>(L, st);
+        case T_Q5_K: return launch_pk_t<T_Q5_K>(L, st);
+        case T_Q3_K: return launch_pk_t<T_Q3_K>(L, st);
+        case T_Q2_K: return launch_pk_t<T_Q2_K>(L, st);
         default: return -3;
     }
 }

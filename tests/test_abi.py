@@ -158,6 +158,10 @@ def test_prefill_copy_size_and_checks_run_on_host(so):
     assert so.prefill_pack_bytes(Q.Q4_K, 4096, 4096) == 32 * 16 * (4 * 16384 + 8192 + 512)
     assert so.prefill_pack_bytes(Q.Q6_K, 1280, 130) == 2 * 5 * (8 * 16384 + 512)
     assert so.prefill_pack_bytes(Q.Q4_K, 256, 0) == 0
+    # one f16 plane per K-step; Q5_K and Q2_K with the mins operand
+    assert so.prefill_pack_bytes(Q.Q5_K, 4096, 4096) == 32 * 16 * (4 * 16384 + 8192 + 512)
+    assert so.prefill_pack_bytes(Q.Q2_K, 1024, 300) == 3 * 4 * (4 * 16384 + 8192 + 512)
+    assert so.prefill_pack_bytes(Q.Q3_K, 1280, 130) == 2 * 5 * (4 * 16384 + 512)
     n = C.c_size_t(7)
     assert so.lib.sicu_prefill_pack_bytes(Q.Q8_0, 256, 128, C.byref(n)) == L.SICU_ENOTSUP and n.value == 0
     assert so.lib.sicu_prefill_pack_bytes(Q.Q4_K, 300, 128, C.byref(n)) == L.SICU_EINVAL

@@ -1,6 +1,7 @@
 """Prefill from the re-tiled weight copy (sicu_prefill_pack,
 sicu_gemm_prefill_packed) against the oracle's scalar per-row dots of the
-reference (src/kernels.c:349-410 for Q4_K, 480-523 for Q6_K).
+reference (src/kernels.c:349-410 for Q4_K, 480-523 for Q6_K, 412-478 for
+Q5_K, 289-347 for Q3_K, 249-287 for Q2_K).
 
 The copy holds, per 128-row tile and super-block, the exact f16 operands the
 tensor cores multiply, so two things are checked: the copy itself (decoded
@@ -25,8 +26,24 @@ pytestmark = pytest.mark.gpu
 
 ATILE = 128 * 64 * 2         # one K-step of a 128-row tile
 MINT = 128 * 16 * 2          # one half of the Q4_K mins operand
-KSTEPS = {Q.Q4_K: 4, Q.Q6_K: 8}
+KSTEPS = {Q.Q4_K: 4, Q.Q6_K: 8, Q.Q5_K: 4, Q.Q3_K: 4, Q.Q2_K: 4}
+MINS = (Q.Q4_K, Q.Q5_K, Q.Q2_K)        # formats with a mins operand
+K_TYPES = (Q.Q4_K, Q.Q5_K, Q.Q6_K, Q.Q3_K, Q.Q2_K)
+COPY_ONLY = (Q.Q5_K, Q.Q3_K, Q.Q2_K)   # tensor-core kernels only from a prefill copy
 SLOT = np.array([0, 2, 1, 3])
+# byte offsets of d and dmin in a block, for the edge-row patches
+D_OFF = {Q.Q4_K: (0, 2), Q.Q5_K: (0, 2), Q.Q2_K: (80, 82), Q.Q3_K: (108, None)}
+
+
+def _zero_scales(wt, w, every_d=9, every_dmin=11):
+    """Some blocks with d = 0 and (K formats with mins) some with dmin = 0."""
+    w = w.copy()
+    blocks = w.reshape(-1, Q.row_bytes(wt, 256))
+    od, om = D_OFF[wt]
+    blocks[::every_d, od:od + 2] = 0
+    if om is not None:
+        blocks[4::every_dmin, om:om + 2] = 0
+    return w
 
 
 def _pack(sicu, wt, w, n_in, n_out):
@@ -52,13 +69,13 @@ def _decode_pack(wt, pack: np.ndarray, n_in: int, n_out: int) -> np.ndarray:
     """The weights a packed copy stands for: [n_out, n_in] float64."""
     nsb, nrt = n_in // 256, (n_out + 127) // 128
     kst = KSTEPS[wt]
-    chunk = kst * ATILE + (2 * MINT if wt == Q.Q4_K else 0) + 512
+    chunk = kst * ATILE + (2 * MINT if wt in MINS else 0) + 512
     assert pack.size == nrt * nsb * chunk
     out = np.zeros((nrt * 128, n_in))
     for rt in range(nrt):
         for sb in range(nsb):
             c = pack[(rt * nsb + sb) * chunk:(rt * nsb + sb + 1) * chunk]
-            f = c[kst * ATILE + (2 * MINT if wt == Q.Q4_K else 0):].view(np.float32).astype(np.float64)
+            f = c[kst * ATILE + (2 * MINT if wt in MINS else 0):].view(np.float32).astype(np.float64)
             # A tiles: 64 f16 per row, 16-byte unit j of row r at j ^ (r & 7)
             a = [_unswizzle(c[t * ATILE:(t + 1) * ATILE], 128, lambda r: r & 7).view(np.float16)
                  .astype(np.float64) for t in range(kst)]
@@ -66,12 +83,12 @@ def _decode_pack(wt, pack: np.ndarray, n_in: int, n_out: int) -> np.ndarray:
             for t in range(kst):
                 # slot s holds element 4 (s // 4) + (0, 2, 1, 3)[s % 4] of its 64
                 e = 4 * (np.arange(64) // 4) + SLOT[np.arange(64) % 4]
-                if wt == Q.Q4_K:
+                if wt != Q.Q6_K:    # one plane: sc q 2^-s
                     vals[:, 64 * t + e] = a[t]
                 else:   # two planes per quarter: (q - 32) lo + 16 (q - 32) hi
                     vals[:, 64 * (t // 2) + e] += a[t] * (16.0 if t % 2 else 1.0)
             vals *= f[:, None]
-            if wt == Q.Q4_K:
+            if wt in MINS:
                 mins = [_unswizzle(c[kst * ATILE + h * MINT:kst * ATILE + (h + 1) * MINT], 32,
                                    lambda r: (r >> 2) & 1).view(np.float16).astype(np.float64) for h in range(2)]
                 mterm = (mins[0] + mins[1]) * f[:, None]          # [128, 16]: per 16 elements
@@ -83,25 +100,26 @@ def _decode_pack(wt, pack: np.ndarray, n_in: int, n_out: int) -> np.ndarray:
 @pytest.mark.parametrize("wt,n_out,n_in", [
     (Q.Q4_K, 200, 768),
     (Q.Q6_K, 130, 1280),    # 5 super-blocks: rows that are not 16-byte multiples
+    (Q.Q5_K, 200, 768),
+    (Q.Q3_K, 130, 1280),    # 110-byte blocks at even offsets
+    (Q.Q2_K, 130, 1280),    # 84-byte blocks
 ])
 def test_pack_layout_gives_back_the_weights(sicu, oracle, wt, n_out, n_in):
     """Decoded from its layout, the copy is the reference's dequantized
     weights: exactly d sc q for the main term (f16 sc q 2^-s times f = d 2^s),
-    and the Q4_K mins term to the 22 bits of its hi + lo split."""
+    and the mins term (Q4_K, Q5_K, Q2_K) to the 22 bits of its hi + lo
+    split."""
     w = synth.weights(wt, n_out, n_in, seed=5)
-    if wt == Q.Q4_K:   # a few blocks with d = 0 or dmin = 0
-        w = w.copy()
-        blocks = w.reshape(-1, 144)
-        blocks[::9, 0:2] = 0
-        blocks[4::11, 2:4] = 0
+    if wt in D_OFF:   # a few blocks with d = 0 or dmin = 0
+        w = _zero_scales(wt, w)
     _, dp, _ = _pack(sicu, wt, w, n_in, n_out)
     got = _decode_pack(wt, host(dp), n_in, n_out)
     want = _dequant_w(oracle, wt, w, n_in, n_out)
     scale = np.abs(want).max()
     err = np.abs(got - want)
     assert err.max() <= 2e-6 * scale, f"max err {err.max():.3g} of {scale:.3g}"
-    if wt == Q.Q6_K:   # d (q - 32) sc exactly (zero products may differ in sign)
-        assert np.array_equal(got.astype(np.float32), want.astype(np.float32)), "Q6_K copy"
+    if wt in (Q.Q6_K, Q.Q3_K):   # d sc q exactly, no mins (zero products may differ in sign)
+        assert np.array_equal(got.astype(np.float32), want.astype(np.float32)), f"{Q.NAMES[wt]} copy"
     # the rows past n_out in the last tile are zero
     nrt, nsb = (n_out + 127) // 128, n_in // 256
     assert nrt * 128 > n_out
@@ -122,7 +140,7 @@ def _run_packed(sicu, oracle, wt, n_out, n_in, m, seed=0, patch=None, f32=False)
     return w, x, xq, dw, dp, host(y)
 
 
-@pytest.mark.parametrize("wt", [Q.Q4_K, Q.Q6_K])
+@pytest.mark.parametrize("wt", K_TYPES, ids=lambda t: Q.NAMES[t])
 @pytest.mark.parametrize("n_out,n_in,m", [
     (128, 256, 128),     # one tile, one super-block, 128-token tile
     (200, 512, 77),      # ragged rows and tokens
@@ -179,6 +197,9 @@ def test_packed_prefill_edge_rows(sicu, oracle):
 @pytest.mark.parametrize("wt,n_out,n_in,m", [
     (Q.Q4_K, 640, 4096, 300),    # few tiles: each row's super-blocks split over CTAs
     (Q.Q6_K, 256, 5632, 200),
+    (Q.Q5_K, 640, 4096, 300),
+    (Q.Q3_K, 256, 5632, 200),
+    (Q.Q2_K, 640, 4096, 130),
 ])
 def test_packed_prefill_split_rows_repeatable(sicu, oracle, wt, n_out, n_in, m):
     w, x, xq, dw, dp, got = _run_packed(sicu, oracle, wt, n_out, n_in, m, seed=n_in + m)
@@ -233,6 +254,10 @@ def test_pack_errors(sicu):
 
 
 @pytest.mark.parametrize("wt,n_outs,n_in,m", [
+    (Q.Q5_K, (640, 128), 1024, 300),
+    (Q.Q3_K, (200, 130), 1280, 64),
+    (Q.Q2_K, (256, 384, 128), 512, 77),
+    (Q.Q2_K, (300, 100), 768, 20),           # at most 32 tokens, a copy-only format: the matvec per token
     (Q.Q4_K, (640, 128, 128), 1024, 300),    # Wq/Wk/Wv-like: one-tile matrices leave half a pair idle
     (Q.Q4_K, (1024, 1024), 4096, 512),       # W_gate/W_up-like
     (Q.Q6_K, (256, 384), 1280, 77),          # 5 super-blocks, 128-token tiles
@@ -307,3 +332,53 @@ def test_packed_prefill_many_pair_tiles(sicu, oracle):
     y2 = empty_f32(m, n_out)
     sicu.gemm_prefill_packed_f32(wt, dw, dp, n_in, n_out, dev(x), m, y2)
     assert_bits_equal(host(y2), got, "second run")
+
+
+@pytest.mark.parametrize("wt", COPY_ONLY, ids=lambda t: Q.NAMES[t])
+def test_packed_prefill_edge_rows_copy_only(sicu, oracle, wt):
+    """Q5_K / Q3_K / Q2_K: blocks with d = 0 or dmin = 0, zero and large
+    activation rows."""
+    n_out, n_in, m = 260, 768, 96
+
+    def patch(w, x):
+        w = _zero_scales(wt, w, 5, 7)
+        x = x.copy()
+        x[3] = 0.0
+        x[10] *= 1e4
+        return w, x
+
+    w, x, xq, dw, dp, got = _run_packed(sicu, oracle, wt, n_out, n_in, m, seed=4, patch=patch)
+    want = oracle.gemv_batch(wt, w, n_in, n_out, xq)
+    l1 = np.abs(_dequant_q8k(xq, n_in)) @ np.abs(_dequant_w(oracle, wt, w, n_in, n_out)).T
+    _check_tol(got, want, l1, f"{Q.NAMES[wt]} packed prefill edge rows")
+    assert (got[3] == 0).all()
+
+
+@pytest.mark.parametrize("wt", COPY_ONLY, ids=lambda t: Q.NAMES[t])
+@pytest.mark.parametrize("n_out,n_in,m", [
+    (384, 1024, 100),    # CTA pairs, 128-token tiles
+    (128, 512, 40),      # one row tile: the one-CTA kernel
+    (130, 2048, 300),    # 256-token tiles, ragged rows
+])
+def test_copy_only_formats_without_a_copy(sicu, oracle, wt, n_out, n_in, m):
+    """sicu_gemm_prefill(_f32) of a format whose tensor-core kernels read only
+    the prefill copy: the call writes a copy into its workspace first. Within
+    the prefill tolerance of the oracle, and the same bits as the call with
+    the caller's own copy."""
+    w = synth.weights(wt, n_out, n_in, seed=n_out + m)
+    x = synth.activations(n_in, m, seed=n_in + m)
+    xq = oracle.quantize_pair(wt, x)
+    dw, dp, _ = _pack(sicu, wt, w, n_in, n_out)
+    y = empty_f32(m, n_out)
+    sicu.gemm_prefill(wt, dw, n_in, n_out, dev(xq), m, y)
+    got = host(y)
+    want = oracle.gemv_batch(wt, w, n_in, n_out, xq)
+    l1 = np.abs(_dequant_q8k(xq, n_in)) @ np.abs(_dequant_w(oracle, wt, w, n_in, n_out)).T
+    _check_tol(got, want, l1, f"{Q.NAMES[wt]} prefill without a copy {n_out}x{n_in} m={m}")
+    y2 = empty_f32(m, n_out)
+    sicu.gemm_prefill_packed(wt, dw, dp, n_in, n_out, dev(xq), m, y2)
+    assert_bits_equal(host(y2), got, "with the caller's copy")
+    y3 = empty_f32(m, n_out)
+    sicu.gemm_prefill_f32(wt, dw, n_in, n_out, dev(x), m, y3)
+    assert_bits_equal(host(y3), got, "f32 entry")
+    assert sicu.status() == 0

@@ -362,6 +362,31 @@ def model_decode(torch, s, shape, dev, stream, world, rank, group, reps, fused=F
     return out
 
 
+_TC_PEAKS: dict = {}
+
+
+def tensor_peaks(s, dev) -> dict:
+    """Dense tensor-core rates of this GPU from the library's own probe
+    (sicu_tc_peak: every SM issuing M = 128, N = 256 MMAs from shared memory,
+    about 30 ms per kind): kind::f16 (what the prefill kernels run) and
+    kind::i8, the int8 denominator of the prefill roofline. Measured once per
+    process."""
+    if not _TC_PEAKS:
+        import torch
+        from siphon_b200.lib import TC_F16, TC_I8
+        sms = torch.cuda.get_device_properties(dev).multi_processor_count
+        out = {}
+        for name, kind in (("f16_TFLOPs", TC_F16), ("i8_TOPs", TC_I8)):
+            s.tc_peak(kind, 200, sms)                       # warm-up
+            ms, tf = s.tc_peak(kind, 7000, sms)
+            out[name] = round(tf, 1)
+            out[name.split("_")[0] + "_ms"] = round(ms, 2)
+        out["source"] = ("sicu_tc_peak: one CTA per SM, back-to-back tcgen05.mma M=128 N=256 from shared memory, "
+                         "7000 rounds of 64 MMAs")
+        _TC_PEAKS.update(out)
+    return dict(_TC_PEAKS)
+
+
 def model_prefill(torch, s, shape, dev, stream, world, rank, group, m_tok, reps) -> dict:
     """Prefill tok/s of the matrix path of `shape` for an m_tok-token prompt,
     from the prefill copies of the weights (sicu_prefill_pack, made at load
@@ -386,12 +411,16 @@ def model_prefill(torch, s, shape, dev, stream, world, rank, group, m_tok, reps)
         kind = "measured"
     except Exception:
         f16_peak, kind = 1590.0, "fallback"
+    tc = tensor_peaks(s, dev)
     out = {"tok_s": round(m_tok / sec, 1), "ms_per_prompt": round(sec * 1e3, 3), "prompt_tokens": m_tok,
-           "TFLOPs": round(tflops, 1), "f16_tensor_frac": round(tflops / f16_peak, 4),
-           "int8_tensor_frac_proxy": round(tflops / (2 * f16_peak), 4), "peak_kind": kind,
+           "TFLOPs": round(tflops, 1), "f16_tensor_frac": round(tflops / f16_peak, 4), "peak_kind": kind,
+           "f16_probe_frac": round(tflops / tc["f16_TFLOPs"], 4), "int8_tensor_frac": round(tflops / tc["i8_TOPs"], 4),
+           "tensor_peaks_measured": tc,
            "pack_bytes_per_gpu": int(sum(t.numel() for t in m.pack.values())),
            "note": "tensor-core kernels (kind::f16 MMAs on exact f16 (scale x quant) operands) reading the "
-                   "prefill copies of the Q4_K and Q6_K weights; int8 peak taken as 2x the measured bf16 dense peak"}
+                   "prefill copies of the Q4_K and Q6_K weights; f16_tensor_frac against the measured cuBLAS bf16 "
+                   "peak, f16_probe_frac / int8_tensor_frac against this GPU's kind::f16 / kind::i8 MMA rates "
+                   "measured by sicu_tc_peak"}
     del m
     torch.cuda.empty_cache()
     return out
@@ -601,7 +630,9 @@ def prefill_per_format(torch, s, dev, stream, m_tok: int = 512) -> dict:
         kind = "measured"
     except Exception:
         f16_peak, kind = 1590.0, "fallback"
-    out = {"prompt_tokens": m_tok, "f16_peak_TFLOPs": f16_peak, "peak_kind": kind}
+    tc = tensor_peaks(s, dev)
+    out = {"prompt_tokens": m_tok, "f16_peak_TFLOPs": f16_peak, "peak_kind": kind,
+           "i8_peak_TOPs_measured": tc["i8_TOPs"]}
     h = stream.cuda_stream
     x = torch.from_numpy(synth.activations(max(k for _, k in PREFILL_FORMAT_SHAPES), m_tok, seed=3)).to(dev)
     for wt in (Q.Q4_K, Q.Q5_K, Q.Q6_K, Q.Q3_K, Q.Q2_K):
@@ -628,7 +659,7 @@ def prefill_per_format(torch, s, dev, stream, m_tok: int = 512) -> dict:
             del g
             tf = 2.0 * m_tok * n_out * n_in / (ms * 1e-3) / 1e12
             row[f"{n_out}x{n_in}"] = {"us": round(ms * 1e3, 1), "TFLOPs": round(tf, 1),
-                                      "f16_frac": round(tf / f16_peak, 4)}
+                                      "f16_frac": round(tf / f16_peak, 4), "int8_frac": round(tf / tc["i8_TOPs"], 4)}
             del w, pk, y
         out[Q.NAMES[wt]] = row
     torch.cuda.empty_cache()

@@ -89,6 +89,18 @@ SICU_API int sicu_status(int *flags);
  * launches. */
 SICU_API int sicu_set_overlap(int on);
 
+/* Tensor-core throughput probe for roofline denominators: one CTA on each of
+ * `sms` SMs issues `rounds` x 64 dense MMAs (M = 128, N = 256; K = 16 for
+ * SICU_TC_F16: f16 operands, f32 accumulation; K = 32 for SICU_TC_I8: int8
+ * operands, s32 accumulation) with both operands in shared memory, on the
+ * legacy default stream, and waits. *ms: device time; *tflops: 2 x
+ * multiply-adds / time, in 10^12 per second. Run it alone on the GPU: it
+ * holds every SM it is given. No counterpart in the reference, which has no
+ * tensor-core code. */
+#define SICU_TC_F16 0
+#define SICU_TC_I8  1
+SICU_API int sicu_tc_peak(int kind, int rounds, int sms, float *ms, double *tflops);
+
 /* ---- memory ------------------------------------------------------------- */
 
 SICU_API int sicu_malloc(void **dev, size_t bytes);

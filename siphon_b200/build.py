@@ -20,7 +20,7 @@ CSRC = PKG / "csrc"
 ROOT = PKG.parent
 LIB = PKG / "libsiphon_cuda.so"
 
-SOURCES = ["abi.cu", "gemv.cu", "gemv_batch.cu", "gemv_f16.cu", "quantize.cu", "noalloc.cu", "prefill.cu", "allreduce.cu", "prologue.cu", "softmax.cu"]
+SOURCES = ["abi.cu", "gemv.cu", "gemv_batch.cu", "gemv_f16.cu", "quantize.cu", "noalloc.cu", "prefill.cu", "allreduce.cu", "prologue.cu", "softmax.cu", "tcpeak.cu"]
 HEADERS = ["common.cuh", "gemv.cuh", "quantize.cuh", "launch.h", "tc.cuh", "allreduce.cuh", "prologue.cuh"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

@@ -29,6 +29,7 @@ SIGNATURES = {
     "sicu_shutdown": [],
     "sicu_last_error": [C.c_char_p, C.c_size_t],
     "sicu_status": [C.POINTER(C.c_int)],
+    "sicu_tc_peak": [C.c_int, C.c_int, C.c_int, C.POINTER(C.c_float), C.POINTER(C.c_double)],
     "sicu_set_overlap": [C.c_int],
     "sicu_malloc": [C.POINTER(C.c_void_p), C.c_size_t],
     "sicu_free": [_vp],
@@ -92,6 +93,7 @@ class Prologue(C.Structure):
     _fields_ = [("kind", C.c_int32), ("eps", C.c_float), ("weight", C.c_void_p), ("residual", C.c_void_p),
                 ("sum_out", C.c_void_p), ("up", C.c_void_p)]
 
+TC_F16, TC_I8 = 0, 1       # sicu_tc_peak kinds
 AR_HANDLE_BYTES = 64
 STATUS_WAIT_TIMEOUT, STATUS_AR_TIMEOUT, STATUS_BAD_ROW = 1, 2, 4
 
@@ -159,6 +161,12 @@ class SiphonCuda:
 
     def set_overlap(self, on: bool) -> None:
         self.check(self.lib.sicu_set_overlap(1 if on else 0))
+
+    def tc_peak(self, kind: int, rounds: int, sms: int) -> tuple[float, float]:
+        """(ms, TFLOP/s) of the tensor-core throughput probe (kind TC_F16 or TC_I8)."""
+        ms, tf = C.c_float(), C.c_double()
+        self.check(self.lib.sicu_tc_peak(kind, rounds, sms, C.byref(ms), C.byref(tf)))
+        return ms.value, tf.value
 
     def status(self) -> int:
         flags = C.c_int(0)

@@ -621,10 +621,11 @@ PREFILL_FORMAT_SHAPES = [(14336, 4096), (4096, 4096)]
 
 
 def prefill_per_format(torch, s, dev, stream, m_tok: int = 512) -> dict:
-    """Every K format's tensor-core prompt product from its prefill copy
-    (sicu_gemm_prefill_packed_f32, f32 prompt rows quantized inside the
+    """Every quantized format's tensor-core prompt product from its prefill
+    copy (sicu_gemm_prefill_packed_f32, f32 prompt rows quantized inside the
     launch): TFLOP/s = 2 m rows K / device time, against the measured f16
-    dense peak (the kernels run kind::f16 MMAs on exact f16 scale x quant)."""
+    dense peak (the K formats run kind::f16 MMAs on exact f16 scale x quant)
+    and the measured int8 rate (the classic formats run kind::i8 MMAs)."""
     try:
         f16_peak = float(json.loads(PEAKS.read_text())["bf16_tflops"])
         kind = "measured"
@@ -635,7 +636,7 @@ def prefill_per_format(torch, s, dev, stream, m_tok: int = 512) -> dict:
            "i8_peak_TOPs_measured": tc["i8_TOPs"]}
     h = stream.cuda_stream
     x = torch.from_numpy(synth.activations(max(k for _, k in PREFILL_FORMAT_SHAPES), m_tok, seed=3)).to(dev)
-    for wt in (Q.Q4_K, Q.Q5_K, Q.Q6_K, Q.Q3_K, Q.Q2_K):
+    for wt in (Q.Q4_K, Q.Q5_K, Q.Q6_K, Q.Q3_K, Q.Q2_K, Q.Q4_0, Q.Q5_0, Q.Q8_0):
         row = {}
         for n_out, n_in in PREFILL_FORMAT_SHAPES:
             w = bench_weights(wt, n_out, n_in, 31, dev)

@@ -223,9 +223,12 @@ SICU_API int sicu_gemv_host_noalloc(uint32_t wtype, const void *dw, int64_t n_in
  * 1e-5 of the L1 norm of its products, but is not bit-identical. Q5_K, Q3_K
  * and Q2_K (src/kernels.c:412-478, 289-347, 249-287) run on the same tensor
  * cores for m > 32, from a prefill copy (below) that the call first writes
- * into the workspace when the caller has none; at most 32 tokens, they and
- * the other types run the decode matvec once per token (bit-identical to the
- * reference).
+ * into the workspace when the caller has none. Q4_0, Q5_0 and Q8_0
+ * (src/kernels.c:197-247) run on int8 MMAs for m > 32 and n_in >= 128, one
+ * per 32-element block, with the reference's float operations per block in
+ * order: bit-identical to the reference (a copy made in the workspace the
+ * same way). Other cases (F16, at most 32 tokens) run the decode matvec once
+ * per token (bit-identical to the reference).
  * The reference has no batched product: its prompt loop calls
  * si_engine_forward once per token (src/cmd_run.c:276), i.e. one backend gemv
  * per token and matrix. When a product has fewer 128-row x token tiles than
@@ -239,7 +242,7 @@ SICU_API int sicu_gemm_prefill_f32(uint32_t wtype, const void *dw, int64_t n_in,
                                    const float *dx, int64_t m, float *dy, void *stream);
 
 /* ---- prefill copies of the weights -----------------------------------------
- * A second, re-tiled copy of a K-format (Q2_K ... Q6_K) matrix for prompt products, made
+ * A second, re-tiled copy of a quantized (Q2_K ... Q6_K, Q4_0, Q5_0, Q8_0) matrix for prompt products, made
  * once when the weights are loaded (the reference makes its tensor views at
  * load, si_tensor_from_gguf, src/backend.c:144-176); the raw GGUF bytes stay
  * on the device for decode. Per 128-row tile and super-block the copy holds
@@ -250,6 +253,8 @@ SICU_API int sicu_gemm_prefill_f32(uint32_t wtype, const void *dw, int64_t n_in,
  * Q2_K (about 3.6x, 3.3x and 6.9x the raw bytes), 4x16 KiB + 0.5 KiB for
  * Q3_K (4.7x), 8x16 KiB + 0.5 KiB for Q6_K (4.9x). Q5_K, Q3_K and Q2_K have
  * one exact f16 plane of scale x quant per K-step (|sc q| <= 1953, 128, 45).
+ * Q4_0, Q5_0, Q8_0: per 128 rows and K-step of four 32-blocks 16 KiB of int8
+ * quants + 2 KiB of block scales (n_in a multiple of 32, at least 128).
  * sicu_prefill_pack_bytes: the copy's size (SICU_ENOTSUP for other types).
  * sicu_prefill_pack: writes the copy of device weights dw into dpack
  * (pack_bytes >= that size, 16-byte aligned), asynchronously on stream.

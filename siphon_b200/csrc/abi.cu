@@ -560,7 +560,8 @@ static int prefill_common(uint32_t wtype, const void *dw, int64_t n_in, int64_t 
     }
     // Q2_K, Q3_K, Q5_K have tensor-core kernels only for the prefill copy:
     // without a copy of the caller's, the product makes one in the workspace
-    const bool copy_only = !prefill_supported(wtype) && prefill_pack_supported(wtype);
+    const bool copy_only = !prefill_supported(wtype) && prefill_pack_supported(wtype) &&
+                           !(is_classic(wtype) && n_in < 128);
     if (!prefill_supported(wtype) && !(copy_only && m > PREFILL_PACKED_MIN_M)) {
         // formats without a tensor-core kernel (and copy-only formats for
         // blocks of at most 32 tokens): the decode matvec per token
@@ -625,7 +626,9 @@ int sicu_gemm_prefill_f32(uint32_t wtype, const void *dw, int64_t n_in, int64_t 
 static int check_pack_shape(const char *what, uint32_t wtype, int64_t n_in, int64_t n_out) {
     if (!prefill_pack_supported(wtype))
         return fail(SICU_ENOTSUP, "%s: no tensor-core prefill kernel for %s (%u)", what, tname(wtype), wtype);
-    if (n_in <= 0 || n_out < 0 || n_in % QK_K || n_in > (int64_t)1 << 20 || n_out > (int64_t)1 << 30)
+    // K formats: whole super-blocks; classic formats: whole 32-blocks, at least one 128-element K-step
+    const bool shape_ok = is_classic(wtype) ? (n_in % 32 == 0 && n_in >= 128) : (n_in % QK_K == 0);
+    if (n_in <= 0 || n_out < 0 || !shape_ok || n_in > (int64_t)1 << 20 || n_out > (int64_t)1 << 30)
         return fail(SICU_EINVAL, "%s: bad shape n_in=%lld n_out=%lld", what, (long long)n_in, (long long)n_out);
     return SICU_OK;
 }
@@ -697,7 +700,7 @@ int sicu_gemm_prefill_multi_f32(uint32_t wtype, int n_mats, const void *const *d
     if (m == 0) return current_ok();
     if (!aligned(dx, 16)) return fail(SICU_EINVAL, "prefill multi: f32 activation must be 16-byte aligned");
     const cudaStream_t st = (cudaStream_t)stream;
-    bool grouped = dpack && n_mats > 1 && m > PREFILL_PACKED_MIN_M && prefill_pack_supported(wtype);
+    bool grouped = dpack && n_mats > 1 && m > PREFILL_PACKED_MIN_M && prefill_groupable(wtype);
     for (int i = 0; grouped && i < n_mats; ++i) grouped = dpack[i] && n_out[i] > 0;
     if (!grouped) {
         // the products one by one (a few tokens: one batch launch for all)

@@ -122,6 +122,11 @@ bool prefill_supported(uint32_t wtype);
 // Q2_K, Q3_K and Q5_K have no converter kernel, so without a copy of their own
 // a product first makes one in the workspace
 bool prefill_pack_supported(uint32_t wtype);
+// Q4_0, Q5_0, Q8_0: int8 tensor-core kernel from the prefill copy (m > 32,
+// n_in >= 128), bit-identical with the per-token matvec
+bool is_classic(uint32_t wtype);
+// formats whose copies several products on one activation can share a launch with
+bool prefill_groupable(uint32_t wtype);
 size_t prefill_workspace_bytes(uint32_t wtype, int64_t n_in, int64_t n_out, int64_t m, int num_sms, bool packed);
 // a group of nmat matrices read from their prefill copies (m > 32)
 size_t prefill_group_workspace_bytes(uint32_t wtype, int64_t n_in, int nmat, const int64_t *n_out, int64_t m,

@@ -1915,14 +1915,390 @@ int launch_pack_t(const void *w, int64_t n_in, int64_t n_out, void *pack, cudaSt
     return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }
 
+// ---- classic formats (Q4_0, Q5_0, Q8_0) on int8 MMAs -------------------------------
+// The reference's dots for these formats (src/kernels.c:197-247) form one
+// exact integer sum per 32-element block, then add one float term per block
+// into the row's running sum, in block order:
+//   Q4_0, Q5_0: sumf += sumi * dx * dy      ((sumi dx) dy, left to right)
+//   Q8_0:       sumf += sumi * (dx * dy)
+// with dx, dy the blocks' f16 scales. Every quant fits int8 (Q4_0 q - 8,
+// Q5_0 q - 16, Q8_0 q, the activation's Q8_0 quants), so one kind::i8 MMA of
+// K = 32 gives a block's integer sums for 128 rows x 128 tokens exactly, in
+// its own tensor-memory accumulator, and the epilogue replays the reference's
+// float operations per block in order: the outputs are the reference's bits.
+//
+// Prefill copy of a classic matrix: per 128-row tile and K-step of four
+// blocks (128 elements) one chunk of
+//   [128 rows][128] int8   the quants, K-major, 128-byte swizzle (16-byte
+//                          unit j of row r stored at j ^ (r & 7))
+//   [128 rows][4] f32      the blocks' weight scales dx (0 past the row's end)
+// Token operand: [m_pad][K] int8 (the activation's Q8_0 quants) and the
+// blocks' activation scales dy as [nblk][m_pad] f32.
+//
+// One CTA: 128 rows x 128 tokens, 10 warps: warp 0 loads (bulk copies of the
+// chunk and the scales, a TMA tile of the token quants), warp 1 owns tensor
+// memory and issues one MMA per block into a ring of four 128-column
+// accumulators, warps 2-9 are the epilogue (thread = row, 64 tokens, one
+// running sum each). The epilogue's five operations per (row, token, block)
+// bound the kernel, about ten times the MMA time.
+constexpr int I8_ATILE = PF_BM * 128;                // int8 quants of one K-step
+constexpr int I8_CHUNK = I8_ATILE + PF_BM * 4 * 4;   // + the four blocks' row scales
+constexpr int I8_BN = 128;                           // tokens per tile
+constexpr int I8_S = 4, I8_NSC = 4, I8_NACC = 4;     // stages, scale buffers, accumulators
+constexpr int I8_WARPS = 10, I8_NEPI = 8;
+constexpr int I8_STAGE = I8_ATILE + I8_BN * 128;
+constexpr int I8_SCBUF = PF_BM * 16 + 4 * I8_BN * 4;   // row scales [128][4], token scales [4][128]
+constexpr int I8_OFF_SC = I8_S * I8_STAGE, I8_OFF_BAR = I8_OFF_SC + I8_NSC * I8_SCBUF;
+constexpr int I8_SMEM = I8_OFF_BAR + 256 + 16 + 1024;
+enum {
+    I8B_FULL = 0, I8B_EMPTY = 4, I8B_SC_FULL = 8, I8B_SC_FREE = 12, I8B_ACC_FULL = 16, I8B_ACC_EMPTY = 20,
+    I8B_DRAIN = 24, I8B_NBARS = 25,
+};
+static_assert(I8B_NBARS * 8 <= 256, "barrier area");
+
+template <uint32_t T> struct I8Fmt;
+template <> struct I8Fmt<T_Q8_0> { static constexpr int BLOCK = B_Q8_0; static constexpr bool SCALES_FIRST = true; };
+template <> struct I8Fmt<T_Q4_0> { static constexpr int BLOCK = B_Q4_0; static constexpr bool SCALES_FIRST = false; };
+template <> struct I8Fmt<T_Q5_0> { static constexpr int BLOCK = B_Q5_0; static constexpr bool SCALES_FIRST = false; };
+
+// Instruction descriptor for kind::i8: signed int8 A and B, s32 accumulation,
+// both K-major: [4,6) D format (2 = s32), [7,10) / [10,13) A / B format (1 =
+// signed 8-bit), [17,23) N >> 3, [24,29) M >> 4.
+__host__ __device__ constexpr uint32_t idesc_s8(int m, int n) {
+    return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+// D[tmem] = A[smem] * B[smem]^T (the accumulator is overwritten); one thread issues
+__device__ __forceinline__ void tc_mma_s8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}"
+        :: "r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(0u)
+        : "memory");
+}
+
+// Quant e (0..31) of a classic block b (its bytes), as the reference's dots
+// form it (src/kernels.c:203-205, 222-225, 241).
+template <uint32_t T>
+__device__ __forceinline__ int classic_quant(const uint8_t *b, int e) {
+    if constexpr (T == T_Q8_0) {
+        return (int)(int8_t)b[2 + e];
+    } else if constexpr (T == T_Q4_0) {
+        const int q = b[2 + (e & 15)];
+        return (e < 16 ? (q & 15) : (q >> 4)) - 8;
+    } else {
+        const uint32_t qh = (uint32_t)b[2] | ((uint32_t)b[3] << 8) | ((uint32_t)b[4] << 16) | ((uint32_t)b[5] << 24);
+        const int q = b[6 + (e & 15)];
+        return (e < 16 ? ((q & 15) | (int)(((qh >> e) << 4) & 0x10u)) : ((q >> 4) | (int)((qh >> (e - 4)) & 0x10u))) - 16;
+    }
+}
+
+// one CTA per (row tile, K-step); thread = row
+template <uint32_t T>
+__global__ void __launch_bounds__(PF_BM) prefill_pack_i8_kernel(const uint8_t *w, int64_t row_bytes, int n_out,
+                                                               int nblk, uint8_t *pack) {
+    const int rt = blockIdx.x, ks = blockIdx.y, nks = gridDim.y, r = threadIdx.x;
+    const int64_t row = (int64_t)rt * PF_BM + r;
+    const bool valid = row < n_out;
+    uint8_t *chunk = pack + ((size_t)rt * nks + ks) * (size_t)I8_CHUNK;
+    float *dst_d = reinterpret_cast<float *>(chunk + I8_ATILE) + 4 * r;
+    uint32_t words[32];
+#pragma unroll
+    for (int bi = 0; bi < 4; ++bi) {
+        const int b = 4 * ks + bi;
+        const bool on = valid && b < nblk;
+        const uint8_t *blk = w + (on ? row * row_bytes + (int64_t)b * I8Fmt<T>::BLOCK : 0);
+        dst_d[bi] = on ? h2f((uint32_t)blk[0] | ((uint32_t)blk[1] << 8)) : 0.0f;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            uint32_t v = 0;
+            if (on)
+                for (int e = 0; e < 4; ++e) v |= (uint32_t)(classic_quant<T>(blk, 4 * k + e) & 0xff) << (8 * e);
+            words[8 * bi + k] = v;
+        }
+    }
+    uint8_t *dst = chunk + r * 128;
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+        reinterpret_cast<uint4 *>(dst)[j ^ (r & 7)] =
+            make_uint4(words[4 * j], words[4 * j + 1], words[4 * j + 2], words[4 * j + 3]);
+}
+
+// The token operand from f32 rows (the library's Q8_0 quantizer, the AVX2
+// form the decode matvec uses) or from Q8_0 rows: thread = (token, block).
+// Tokens m..m_pad-1 are zero.
+__global__ void prefill_prep_i8(const float *xf, const uint8_t *xq, int m, int nblk, int m_pad, uint8_t *B,
+                                float *DY) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (int64_t)m_pad * nblk) return;
+    const int t = (int)(i / nblk), b = (int)(i - (int64_t)t * nblk);
+    const int64_t K = 32 * (int64_t)nblk;
+    uint32_t q[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    float d = 0.0f;
+    if (t < m) {
+        if (xf) {
+            uint32_t d16;
+            q8_0_block(xf + t * K + 32 * (int64_t)b, d16, q);
+            d = h2f(d16);
+        } else {
+            const uint16_t *blk = reinterpret_cast<const uint16_t *>(xq + ((int64_t)t * nblk + b) * B_Q8_0);
+            d = h2f(blk[0]);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) q[k] = (uint32_t)blk[1 + 2 * k] | ((uint32_t)blk[2 + 2 * k] << 16);
+        }
+    }
+    uint4 *dst = reinterpret_cast<uint4 *>(B + t * K + 32 * (int64_t)b);
+    dst[0] = make_uint4(q[0], q[1], q[2], q[3]);
+    dst[1] = make_uint4(q[4], q[5], q[6], q[7]);
+    DY[(int64_t)b * m_pad + t] = d;
+}
+
+struct I8Params {
+    const uint8_t *pack;
+    const float *dy;
+    float *y;
+    int n_out, nblk, nks, m, m_pad, ntt;
+    int *status;
+};
+
+template <uint32_t T>
+__global__ void __launch_bounds__(I8_WARPS * 32, 1) prefill_i8_kernel(const __grid_constant__ CUtensorMap tmB,
+                                                                       const I8Params p) {
+    constexpr uint32_t FULL = 0xffffffffu;
+    constexpr int EPI_COLS = I8_BN / 2;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const uint32_t sb0 = smem_addr(smem);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int rt = blockIdx.x / p.ntt, tt = blockIdx.x - rt * p.ntt;
+    const int row0 = rt * PF_BM, tok0 = tt * I8_BN;
+    const int rows = min(PF_BM, p.n_out - row0);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + I8_OFF_BAR + 256);
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + I8_OFF_BAR + 256 + 4);
+    const uint32_t barbase = sb0 + I8_OFF_BAR;
+    auto bar = [&](int i) { return barbase + 8u * (uint32_t)i; };
+    auto stage_a = [&](int s) { return sb0 + (uint32_t)(s * I8_STAGE); };
+    auto stage_b = [&](int s) { return sb0 + (uint32_t)(s * I8_STAGE + I8_ATILE); };
+    auto scbuf = [&](int b) { return (uint32_t)(I8_OFF_SC + b * I8_SCBUF); };   // offset from smem
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < I8_S; ++i) {
+            mbar_init(bar(I8B_FULL + i), 1);
+            mbar_init(bar(I8B_EMPTY + i), 1);
+        }
+        for (int i = 0; i < I8_NSC; ++i) {
+            mbar_init(bar(I8B_SC_FULL + i), 1);
+            mbar_init(bar(I8B_SC_FREE + i), I8_NEPI);
+        }
+        for (int i = 0; i < I8_NACC; ++i) {
+            mbar_init(bar(I8B_ACC_FULL + i), 1);
+            mbar_init(bar(I8B_ACC_EMPTY + i), I8_NEPI);
+        }
+        mbar_init(bar(I8B_DRAIN), 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1) tmem_alloc(smem_addr(tmem_slot), I8_NACC * I8_BN);
+    if (warp == 0 && lane == 0) tma_prefetch_map(&tmB);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        // ---- loads: per K-step the scales (own ring) and the quant tiles ----
+        if (lane == 0) {
+            const uint8_t *chunks = p.pack + (size_t)rt * p.nks * (size_t)I8_CHUNK;
+            int k_issued = 0, sc_issued = 0;
+            for (int ks = 0; ks < p.nks; ++ks) {
+                const int nb = min(4, p.nblk - 4 * ks);
+                const uint8_t *ck = chunks + (size_t)ks * I8_CHUNK;
+                const int b = ks % I8_NSC;
+                if (!pf_wait(bar(I8B_SC_FREE + b), ((ks / I8_NSC) & 1) ^ 1, abort_flag, p.status)) break;
+                const uint32_t sc = sb0 + scbuf(b);
+                mbar_expect_tx(bar(I8B_SC_FULL + b), (uint32_t)(PF_BM * 16 + nb * I8_BN * 4));
+                bulk_g2s(sc, ck + I8_ATILE, PF_BM * 16, bar(I8B_SC_FULL + b));
+                for (int bi = 0; bi < nb; ++bi)
+                    bulk_g2s(sc + PF_BM * 16 + bi * I8_BN * 4, p.dy + (size_t)(4 * ks + bi) * p.m_pad + tok0,
+                             I8_BN * 4, bar(I8B_SC_FULL + b));
+                sc_issued = ks + 1;
+                const int s = ks % I8_S;
+                if (!pf_wait(bar(I8B_EMPTY + s), ((ks / I8_S) & 1) ^ 1, abort_flag, p.status)) break;
+                mbar_expect_tx(bar(I8B_FULL + s), (uint32_t)I8_STAGE);
+                bulk_g2s(stage_a(s), ck, I8_ATILE, bar(I8B_FULL + s));
+                tma_load_2d(stage_b(s), &tmB, 128 * ks, tok0, bar(I8B_FULL + s));
+                k_issued = ks + 1;
+            }
+            if (*abort_flag) {
+                for (int t = max(0, k_issued - I8_S); t < k_issued; ++t) pf_settle(bar(I8B_FULL + t % I8_S), (t / I8_S) & 1);
+                for (int t = max(0, sc_issued - I8_NSC); t < sc_issued; ++t)
+                    pf_settle(bar(I8B_SC_FULL + t % I8_NSC), (t / I8_NSC) & 1);
+            }
+        }
+    } else if (warp == 1) {
+        // ---- MMA issue: one K = 32 MMA per block into its own accumulator ----
+        if (lane == 0) {
+            constexpr uint32_t idesc = idesc_s8(PF_BM, I8_BN);
+            bool ok = true;
+            for (int ks = 0; ks < p.nks && ok; ++ks) {
+                const int nb = min(4, p.nblk - 4 * ks), s = ks % I8_S;
+                if (!pf_wait<true>(bar(I8B_FULL + s), (uint32_t)(ks / I8_S) & 1u, abort_flag, p.status)) break;
+                tc_fence_after();
+                for (int bi = 0; bi < nb; ++bi) {
+                    const int g = 4 * ks + bi, a = g % I8_NACC;
+                    if (!pf_wait<true>(bar(I8B_ACC_EMPTY + a), ((g / I8_NACC) & 1) ^ 1, abort_flag, p.status)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    // block bi: 32 bytes into the 128-byte swizzle atom of each row
+                    tc_mma_s8(tmem + (uint32_t)(a * I8_BN), smem_desc(stage_a(s) + 32 * bi, 1024, SMEM_SWZ_128B),
+                              smem_desc(stage_b(s) + 32 * bi, 1024, SMEM_SWZ_128B), idesc);
+                    tc_commit(bar(I8B_ACC_FULL + a));
+                }
+                tc_commit(bar(I8B_EMPTY + s));
+            }
+            if (*abort_flag) {
+                tc_commit(bar(I8B_DRAIN));
+                pf_settle(bar(I8B_DRAIN), 0);
+            }
+        }
+    } else {
+        // ---- epilogue: thread = row (tensor-memory lane), 64 tokens ----
+        const int q = warp & 3;
+        const int c0 = ((warp - 2) >> 2) * EPI_COLS;
+        const int r = 32 * q + lane;
+        float sum[EPI_COLS];
+#pragma unroll
+        for (int j = 0; j < EPI_COLS; ++j) sum[j] = 0.0f;
+        bool ok = true;
+        for (int ks = 0; ks < p.nks && ok; ++ks) {
+            const int nb = min(4, p.nblk - 4 * ks), b = ks % I8_NSC;
+            if (!__all_sync(FULL, pf_wait(bar(I8B_SC_FULL + b), (uint32_t)(ks / I8_NSC) & 1u, abort_flag, p.status))) {
+                ok = false;
+                break;
+            }
+            const uint8_t *scp = smem + scbuf(b);
+            const float4 dx4 = reinterpret_cast<const float4 *>(scp)[r];
+            const float dxs[4] = {dx4.x, dx4.y, dx4.z, dx4.w};
+            for (int bi = 0; bi < nb; ++bi) {
+                const int g = 4 * ks + bi, a = g % I8_NACC;
+                if (!__all_sync(FULL, pf_wait(bar(I8B_ACC_FULL + a), (uint32_t)(g / I8_NACC) & 1u, abort_flag,
+                                              p.status))) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                uint32_t v0[32], v1[32];
+                const uint32_t ta = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(a * I8_BN + c0);
+                tmem_ld32x<32>(ta, v0);
+                tmem_ld32x<32>(ta + 32, v1);
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(bar(I8B_ACC_EMPTY + a));
+                const float dx = dxs[bi];
+                const float4 *dy4 = reinterpret_cast<const float4 *>(scp + PF_BM * 16 + bi * I8_BN * 4 + c0 * 4);
+#pragma unroll
+                for (int g4 = 0; g4 < EPI_COLS / 4; ++g4) {
+                    const float4 dq = dy4[g4];
+                    const float dyv[4] = {dq.x, dq.y, dq.z, dq.w};
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const int j = 4 * g4 + e;
+                        const uint32_t raw = j < 32 ? v0[j] : v1[j - 32];
+                        // the block's integer sum (|sumi| < 2^20) to float, exactly
+                        const float si = __fsub_rn(__int_as_float((int)raw + 0x4b400000), 12582912.0f);
+                        const float t = I8Fmt<T>::SCALES_FIRST ? __fmul_rn(si, __fmul_rn(dx, dyv[e]))
+                                                              : __fmul_rn(__fmul_rn(si, dx), dyv[e]);
+                        sum[j] = __fadd_rn(sum[j], t);
+                    }
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar(I8B_SC_FREE + b));
+        }
+        if (ok && !*abort_flag && r < rows) {
+            float *yr = p.y + row0 + r;
+#pragma unroll
+            for (int j = 0; j < EPI_COLS; ++j)
+                if (tok0 + c0 + j < p.m) yr[(int64_t)(tok0 + c0 + j) * p.n_out] = sum[j];
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, I8_NACC * I8_BN);
+    }
+}
+
+size_t i8_ws_b(int64_t n_in, int64_t m) { return align256((size_t)((m + I8_BN - 1) / I8_BN * I8_BN) * n_in); }
+size_t i8_ws_bytes(int64_t n_in, int64_t m) {
+    const int64_t m_pad = (m + I8_BN - 1) / I8_BN * I8_BN;
+    return i8_ws_b(n_in, m) + align256((size_t)(n_in / 32) * m_pad * 4);
+}
+
+template <uint32_t T>
+int launch_i8_t(const PrefillLaunch &L, cudaStream_t st) {
+    if (!L.pack || L.m <= PF_BN_SMALL || L.nmat > 1 || L.n_in < 128) return -3;
+    const int64_t K = L.n_in, nblk = K / 32, nks = (nblk + 3) / 4;
+    const int64_t m_pad = (L.m + I8_BN - 1) / I8_BN * I8_BN;
+    uint8_t *ws = static_cast<uint8_t *>(L.ws);
+    uint8_t *B = ws;
+    float *DY = reinterpret_cast<float *>(ws + i8_ws_b(L.n_in, L.m));
+    const int64_t items = m_pad * nblk;
+    prefill_prep_i8<<<(unsigned)((items + 255) / 256), 256, 0, st>>>(L.xf, static_cast<const uint8_t *>(L.xq),
+                                                                      (int)L.m, (int)nblk, (int)m_pad, B, DY);
+    if (cudaGetLastError() != cudaSuccess) return -2;
+    CUtensorMap tmB;
+    if (!make_map(&tmB, B, (uint64_t)K, (uint64_t)m_pad, (uint64_t)K, 128, I8_BN, CU_TENSOR_MAP_SWIZZLE_128B, 1))
+        return -4;
+    static bool attr_set[64] = {};
+    const int dev = L.device & 63;
+    if (!attr_set[dev]) {
+        cudaFuncSetAttribute(prefill_i8_kernel<T>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+        if (cudaFuncSetAttribute(prefill_i8_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, I8_SMEM) !=
+            cudaSuccess)
+            return -2;
+        attr_set[dev] = true;
+    }
+    I8Params p{};
+    p.pack = static_cast<const uint8_t *>(L.pack);
+    p.dy = DY;
+    p.y = L.y;
+    p.n_out = (int)L.n_out;
+    p.nblk = (int)nblk;
+    p.nks = (int)nks;
+    p.m = (int)L.m;
+    p.m_pad = (int)m_pad;
+    p.ntt = (int)(m_pad / I8_BN);
+    p.status = L.status;
+    const int64_t tiles = (L.n_out + PF_BM - 1) / PF_BM * p.ntt;
+    prefill_i8_kernel<T><<<(unsigned)tiles, I8_WARPS * 32, I8_SMEM, st>>>(tmB, p);
+    return cudaGetLastError() == cudaSuccess ? 0 : -2;
+}
+
+template <uint32_t T>
+int launch_pack_i8_t(const void *w, int64_t n_in, int64_t n_out, void *pack, cudaStream_t st) {
+    const int64_t nblk = n_in / 32, nks = (nblk + 3) / 4, nrt = (n_out + PF_BM - 1) / PF_BM;
+    prefill_pack_i8_kernel<T><<<dim3((unsigned)nrt, (unsigned)nks), PF_BM, 0, st>>>(
+        static_cast<const uint8_t *>(w), nblk * I8Fmt<T>::BLOCK, (int)n_out, (int)nblk, static_cast<uint8_t *>(pack));
+    return cudaGetLastError() == cudaSuccess ? 0 : -2;
+}
+
 }  // namespace
 
 bool prefill_supported(uint32_t wtype) { return wtype == T_Q4_K || wtype == T_Q6_K; }
+bool is_classic(uint32_t wtype) { return wtype == T_Q4_0 || wtype == T_Q5_0 || wtype == T_Q8_0; }
 bool prefill_pack_supported(uint32_t wtype) {
-    return wtype == T_Q2_K || wtype == T_Q3_K || wtype == T_Q4_K || wtype == T_Q5_K || wtype == T_Q6_K;
+    return wtype == T_Q2_K || wtype == T_Q3_K || wtype == T_Q4_K || wtype == T_Q5_K || wtype == T_Q6_K ||
+           is_classic(wtype);
 }
+bool prefill_groupable(uint32_t wtype) { return prefill_pack_supported(wtype) && !is_classic(wtype); }
 
 size_t prefill_workspace_bytes(uint32_t wtype, int64_t n_in, int64_t n_out, int64_t m, int num_sms, bool packed) {
+    if (is_classic(wtype)) return i8_ws_bytes(n_in, m);
     const WsParts w = ws_parts(wtype, n_in, n_out, m, num_sms, packed && m > PF_BN_SMALL);
     return w.b + w.s + w.da + w.pad + w.part;
 }
@@ -1936,6 +2312,7 @@ size_t prefill_group_workspace_bytes(uint32_t wtype, int64_t n_in, int nmat, con
 
 size_t prefill_pack_bytes(uint32_t wtype, int64_t n_in, int64_t n_out) {
     const int64_t nsb = n_in / QK_K, nrt = (n_out + PF_BM - 1) / PF_BM;
+    if (is_classic(wtype)) return (size_t)(nrt * ((n_in / 32 + 3) / 4)) * (size_t)I8_CHUNK;
     switch (wtype) {
         case T_Q4_K: return (size_t)(nrt * nsb) * (size_t)pk_chunk<T_Q4_K>();
         case T_Q6_K: return (size_t)(nrt * nsb) * (size_t)pk_chunk<T_Q6_K>();
@@ -1953,6 +2330,9 @@ int launch_prefill_pack(uint32_t wtype, const void *w, int64_t n_in, int64_t n_o
         case T_Q5_K: return launch_pack_t<T_Q5_K>(w, n_in, n_out, pack, st);
         case T_Q3_K: return launch_pack_t<T_Q3_K>(w, n_in, n_out, pack, st);
         case T_Q2_K: return launch_pack_t<T_Q2_K>(w, n_in, n_out, pack, st);
+        case T_Q8_0: return launch_pack_i8_t<T_Q8_0>(w, n_in, n_out, pack, st);
+        case T_Q4_0: return launch_pack_i8_t<T_Q4_0>(w, n_in, n_out, pack, st);
+        case T_Q5_0: return launch_pack_i8_t<T_Q5_0>(w, n_in, n_out, pack, st);
         default: return -3;
     }
 }
@@ -1964,6 +2344,9 @@ int launch_prefill(uint32_t wtype, const PrefillLaunch &L, cudaStream_t st) {
         case T_Q5_K: return launch_pk_t<T_Q5_K>(L, st);
         case T_Q3_K: return launch_pk_t<T_Q3_K>(L, st);
         case T_Q2_K: return launch_pk_t<T_Q2_K>(L, st);
+        case T_Q8_0: return launch_i8_t<T_Q8_0>(L, st);
+        case T_Q4_0: return launch_i8_t<T_Q4_0>(L, st);
+        case T_Q5_0: return launch_i8_t<T_Q5_0>(L, st);
         default: return -3;
     }
 }

@@ -242,7 +242,7 @@ def test_pack_errors(sicu):
     with pytest.raises(SicuError):
         sicu.prefill_pack(Q.Q4_K, w, 256, 128, p, n - 16)          # too small
     with pytest.raises(SicuError):
-        sicu.prefill_pack(Q.Q8_0, w, 256, 128, p, n)               # no tensor-core kernel
+        sicu.prefill_pack(Q.F16, w, 256, 128, p, n)                # no prefill copy
     with pytest.raises(SicuError):
         sicu.prefill_pack(Q.Q4_K, w, 200, 128, p, n)               # not whole super-blocks
     x = torch.zeros(256, dtype=torch.float32, device="cuda")

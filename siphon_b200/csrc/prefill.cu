@@ -1935,17 +1935,17 @@ int launch_pack_t(const void *w, int64_t n_in, int64_t n_out, void *pack, cudaSt
 // Token operand: [m_pad][K] int8 (the activation's Q8_0 quants) and the
 // blocks' activation scales dy as [nblk][m_pad] f32.
 //
-// One CTA: 128 rows x 128 tokens, 10 warps: warp 0 loads (bulk copies of the
+// One CTA: 128 rows x 128 tokens, 18 warps: warp 0 loads (bulk copies of the
 // chunk and the scales, a TMA tile of the token quants), warp 1 owns tensor
 // memory and issues one MMA per block into a ring of four 128-column
-// accumulators, warps 2-9 are the epilogue (thread = row, 64 tokens, one
-// running sum each). The epilogue's five operations per (row, token, block)
+// accumulators, warps 2-17 are the epilogue (thread = row, 32 tokens, one
+// running sum each; four warps per 32-lane quarter of tensor memory). The epilogue's five operations per (row, token, block)
 // bound the kernel, about ten times the MMA time.
 constexpr int I8_ATILE = PF_BM * 128;                // int8 quants of one K-step
 constexpr int I8_CHUNK = I8_ATILE + PF_BM * 4 * 4;   // + the four blocks' row scales
 constexpr int I8_BN = 128;                           // tokens per tile
 constexpr int I8_S = 4, I8_NSC = 4, I8_NACC = 4;     // stages, scale buffers, accumulators
-constexpr int I8_WARPS = 10, I8_NEPI = 8;
+constexpr int I8_WARPS = 18, I8_NEPI = 16;   // loads, MMA, 16 epilogue warps (4 per lane quarter)
 constexpr int I8_STAGE = I8_ATILE + I8_BN * 128;
 constexpr int I8_SCBUF = PF_BM * 16 + 4 * I8_BN * 4;   // row scales [128][4], token scales [4][128]
 constexpr int I8_OFF_SC = I8_S * I8_STAGE, I8_OFF_BAR = I8_OFF_SC + I8_NSC * I8_SCBUF;
@@ -2065,7 +2065,7 @@ template <uint32_t T>
 __global__ void __launch_bounds__(I8_WARPS * 32, 1) prefill_i8_kernel(const __grid_constant__ CUtensorMap tmB,
                                                                        const I8Params p) {
     constexpr uint32_t FULL = 0xffffffffu;
-    constexpr int EPI_COLS = I8_BN / 2;
+    constexpr int EPI_COLS = I8_BN / (I8_NEPI / 4);
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const uint32_t sb0 = smem_addr(smem);
@@ -2164,7 +2164,7 @@ __global__ void __launch_bounds__(I8_WARPS * 32, 1) prefill_i8_kernel(const __gr
             }
         }
     } else {
-        // ---- epilogue: thread = row (tensor-memory lane), 64 tokens ----
+        // ---- epilogue: thread = row (tensor-memory lane), EPI_COLS tokens ----
         const int q = warp & 3;
         const int c0 = ((warp - 2) >> 2) * EPI_COLS;
         const int r = 32 * q + lane;
@@ -2189,10 +2189,9 @@ __global__ void __launch_bounds__(I8_WARPS * 32, 1) prefill_i8_kernel(const __gr
                     break;
                 }
                 tc_fence_after();
-                uint32_t v0[32], v1[32];
+                uint32_t v0[EPI_COLS];
                 const uint32_t ta = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(a * I8_BN + c0);
-                tmem_ld32x<32>(ta, v0);
-                tmem_ld32x<32>(ta + 32, v1);
+                tmem_ld32x<EPI_COLS>(ta, v0);
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(bar(I8B_ACC_EMPTY + a));
@@ -2205,7 +2204,7 @@ __global__ void __launch_bounds__(I8_WARPS * 32, 1) prefill_i8_kernel(const __gr
 #pragma unroll
                     for (int e = 0; e < 4; ++e) {
                         const int j = 4 * g4 + e;
-                        const uint32_t raw = j < 32 ? v0[j] : v1[j - 32];
+                        const uint32_t raw = v0[j];
                         // the block's integer sum (|sumi| < 2^20) to float, exactly
                         const float si = __fsub_rn(__int_as_float((int)raw + 0x4b400000), 12582912.0f);
                         const float t = I8Fmt<T>::SCALES_FIRST ? __fmul_rn(si, __fmul_rn(dx, dyv[e]))

@@ -636,7 +636,7 @@ def prefill_per_format(torch, s, dev, stream, m_tok: int = 512) -> dict:
            "i8_peak_TOPs_measured": tc["i8_TOPs"]}
     h = stream.cuda_stream
     x = torch.from_numpy(synth.activations(max(k for _, k in PREFILL_FORMAT_SHAPES), m_tok, seed=3)).to(dev)
-    for wt in (Q.Q4_K, Q.Q5_K, Q.Q6_K, Q.Q3_K, Q.Q2_K, Q.Q4_0, Q.Q5_0, Q.Q8_0):
+    for wt in (Q.Q4_K, Q.Q5_K, Q.Q6_K, Q.Q3_K, Q.Q2_K, Q.Q4_0, Q.Q5_0, Q.Q8_0, Q.F16):
         row = {}
         for n_out, n_in in PREFILL_FORMAT_SHAPES:
             w = bench_weights(wt, n_out, n_in, 31, dev)

@@ -227,8 +227,11 @@ SICU_API int sicu_gemv_host_noalloc(uint32_t wtype, const void *dw, int64_t n_in
  * (src/kernels.c:197-247) run on int8 MMAs for m > 32 and n_in >= 128, one
  * per 32-element block, with the reference's float operations per block in
  * order: bit-identical to the reference (a copy made in the workspace the
- * same way). Other cases (F16, at most 32 tokens) run the decode matvec once
- * per token (bit-identical to the reference).
+ * same way). F16 rows of whole 256-element chunks run on kind::f16 MMAs for
+ * m > 32 (the f16 weights re-tiled, within the same tolerance of the
+ * reference's double-accumulated dot, src/kernels.c:189-195). Other cases (at
+ * most 32 tokens, short F16 rows) run the decode matvec once per token
+ * (bit-identical to the reference).
  * The reference has no batched product: its prompt loop calls
  * si_engine_forward once per token (src/cmd_run.c:276), i.e. one backend gemv
  * per token and matrix. When a product has fewer 128-row x token tiles than
@@ -242,7 +245,7 @@ SICU_API int sicu_gemm_prefill_f32(uint32_t wtype, const void *dw, int64_t n_in,
                                    const float *dx, int64_t m, float *dy, void *stream);
 
 /* ---- prefill copies of the weights -----------------------------------------
- * A second, re-tiled copy of a quantized (Q2_K ... Q6_K, Q4_0, Q5_0, Q8_0) matrix for prompt products, made
+ * A second, re-tiled copy of a weight matrix (any format) for prompt products, made
  * once when the weights are loaded (the reference makes its tensor views at
  * load, si_tensor_from_gguf, src/backend.c:144-176); the raw GGUF bytes stay
  * on the device for decode. Per 128-row tile and super-block the copy holds
@@ -255,6 +258,7 @@ SICU_API int sicu_gemm_prefill_f32(uint32_t wtype, const void *dw, int64_t n_in,
  * one exact f16 plane of scale x quant per K-step (|sc q| <= 1953, 128, 45).
  * Q4_0, Q5_0, Q8_0: per 128 rows and K-step of four 32-blocks 16 KiB of int8
  * quants + 2 KiB of block scales (n_in a multiple of 32, at least 128).
+ * F16: per 128 rows and 256 elements 4x16 KiB of the re-tiled halves + 0.5 KiB.
  * sicu_prefill_pack_bytes: the copy's size (SICU_ENOTSUP for other types).
  * sicu_prefill_pack: writes the copy of device weights dw into dpack
  * (pack_bytes >= that size, 16-byte aligned), asynchronously on stream.

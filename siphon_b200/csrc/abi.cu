@@ -561,7 +561,7 @@ static int prefill_common(uint32_t wtype, const void *dw, int64_t n_in, int64_t 
     // Q2_K, Q3_K, Q5_K have tensor-core kernels only for the prefill copy:
     // without a copy of the caller's, the product makes one in the workspace
     const bool copy_only = !prefill_supported(wtype) && prefill_pack_supported(wtype) &&
-                           !(is_classic(wtype) && n_in < 128);
+                           !(is_classic(wtype) && n_in < 128) && !(wtype == T_F16 && n_in % QK_K);
     if (!prefill_supported(wtype) && !(copy_only && m > PREFILL_PACKED_MIN_M)) {
         // formats without a tensor-core kernel (and copy-only formats for
         // blocks of at most 32 tokens): the decode matvec per token

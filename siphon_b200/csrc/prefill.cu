@@ -679,6 +679,15 @@ template <> struct PkFmt<T_Q2_K> {
     static constexpr int KSTEPS = 4, RAW_ROW = 96;
     static constexpr bool MINS = true;
 };
+// F16: the weights themselves, re-tiled (no scale: row scale f = 1), against
+// the activation converted to f16 (the reference's F16 pair, src/backend.c:
+// 19-27) with token scale 1; 256-element chunks play the super-block's part,
+// so each chunk's sum is accumulated in tensor memory and the chunks are
+// added in the epilogue.
+template <> struct PkFmt<T_F16> {
+    static constexpr int KSTEPS = 4, RAW_ROW = 16;   // the pack kernel reads the row from global memory
+    static constexpr bool MINS = false;
+};
 
 // Integer main-term weight (sub-block scale x quant) of element e (0..255) of
 // one super-block, as the reference's dots form it:
@@ -749,6 +758,33 @@ __global__ void __launch_bounds__(PF_BM) prefill_pack_kernel(const uint8_t *w, i
     // this row's block into shared memory, 16-byte aligned (Q6_K blocks start
     // at any even byte)
     uint8_t *mine = raw + r * P::RAW_ROW;
+    if constexpr (T == T_F16) {
+        // 256 halves of the row straight from global memory (rows are 16-byte
+        // multiples: n_in is a multiple of 256), in the Q4_K slot order
+        uint8_t *chunk = pack + ((size_t)rt * nsb + sb) * (size_t)pk_chunk<T>();
+        reinterpret_cast<float *>(chunk + pk_off_f<T>())[r] = valid ? 1.0f : 0.0f;
+        const uint4 *src = reinterpret_cast<const uint4 *>(w + row * row_bytes + (int64_t)sb * 512);
+        for (int t = 0; t < 4; ++t) {
+            uint32_t h[32];   // halves 64t .. 64t + 63, two per word
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                const uint4 u = valid ? src[8 * t + k] : make_uint4(0, 0, 0, 0);
+                h[4 * k] = u.x; h[4 * k + 1] = u.y; h[4 * k + 2] = u.z; h[4 * k + 3] = u.w;
+            }
+            uint32_t v[32];
+#pragma unroll
+            for (int g = 0; g < 16; ++g) {   // elements 4g..4g+3 as slots (4g, 4g+2), (4g+1, 4g+3)
+                const uint32_t a = h[2 * g], b = h[2 * g + 1];
+                v[2 * g] = (a & 0xffffu) | (b << 16);
+                v[2 * g + 1] = (a >> 16) | (b & 0xffff0000u);
+            }
+            uint8_t *dst = chunk + (size_t)t * PK_ATILE + r * 128;
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+                reinterpret_cast<uint4 *>(dst)[j ^ (r & 7)] = make_uint4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+        }
+        return;
+    }
     if (T == T_Q4_K || T == T_Q5_K) {
         constexpr int BLK = T == T_Q4_K ? B_Q4_K : B_Q5_K;
         const uint4 *src = reinterpret_cast<const uint4 *>(w + row * row_bytes + (int64_t)sb * BLK);
@@ -1529,6 +1565,51 @@ int launch_prep(const PrefillLaunch &L, int64_t nsb, int64_t m_pad, uint16_t *B,
     return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }
 
+// The F16 token operand: the activation as f16 (the reference's RNE
+// conversion, src/kernels.c:98-176, from f32 rows, or the caller's f16 rows)
+// in the slot order of the copies, token scale 1: one warp per (token,
+// 256-element chunk), lane L elements 8L..8L+7. Tokens m..m_pad-1 are zero.
+__global__ void __launch_bounds__(256) prefill_prep_f16(const float *xf, const uint16_t *xh, int m, int nsb,
+                                                        int m_pad, uint16_t *B, float *DA) {
+    const int64_t wid = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (wid >= (int64_t)m_pad * nsb) return;
+    const int t = (int)(wid / nsb), sb = (int)(wid - (int64_t)t * nsb);
+    const int64_t K = (int64_t)nsb * QK_K;
+    uint32_t hv[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    if (t < m) {
+        const int64_t off = t * K + (int64_t)sb * QK_K + 8 * lane;
+        if (xf) {
+            const float4 a = reinterpret_cast<const float4 *>(xf + off)[0];
+            const float4 b = reinterpret_cast<const float4 *>(xf + off)[1];
+            const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+            for (int k = 0; k < 8; ++k) hv[k] = f2h(v[k]);
+        } else {
+#pragma unroll
+            for (int k = 0; k < 8; ++k) hv[k] = xh[off + k];
+        }
+    }
+    if (lane == 0) DA[(int64_t)sb * m_pad + t] = t < m ? 1.0f : 0.0f;
+    uint16_t *row = B + t * K + (int64_t)QK_K * sb;
+    *reinterpret_cast<uint4 *>(row + 8 * lane) =
+        make_uint4(hv[0] | (hv[2] << 16), hv[1] | (hv[3] << 16), hv[4] | (hv[6] << 16), hv[5] | (hv[7] << 16));
+}
+
+// The token operand of a copy-reading launch for weight type T.
+template <uint32_t T>
+int launch_prep_t(const PrefillLaunch &L, int64_t nsb, int64_t m_pad, uint16_t *B, uint16_t *S, float *DA,
+                  cudaStream_t st) {
+    if constexpr (T == T_F16) {
+        const int64_t warps = m_pad * nsb;
+        prefill_prep_f16<<<(unsigned)((warps + 7) / 8), 256, 0, st>>>(
+            L.xf, static_cast<const uint16_t *>(L.xq), (int)L.m, (int)nsb, (int)m_pad, B, DA);
+        return cudaGetLastError() == cudaSuccess ? 0 : -2;
+    } else {
+        return launch_prep<PkFmt<T>::KSTEPS / 4>(L, nsb, m_pad, B, S, DA, st);
+    }
+}
+
 // Y = the splits' partial products added in split order (one f32 add per
 // split, the same order on every run)
 __global__ void prefill_sum_splits(const float *part, int nsplit, int64_t n, float *y) {
@@ -1742,7 +1823,7 @@ int launch_packed_tb(const PrefillLaunch &L, cudaStream_t st) {
     uint16_t *B = reinterpret_cast<uint16_t *>(ws);
     uint16_t *S = P::MINS ? reinterpret_cast<uint16_t *>(ws + parts.b) : nullptr;
     float *DA = reinterpret_cast<float *>(ws + parts.b + parts.s);
-    if (launch_prep<P::KSTEPS / 4>(L, nsb, m_pad, B, S, DA, st) != 0) return -2;
+    if (launch_prep_t<T>(L, nsb, m_pad, B, S, DA, st) != 0) return -2;
     CUtensorMap tmB, tmS;
     if (!make_map(&tmB, B, (uint64_t)(K * P::KSTEPS / 4), (uint64_t)m_pad, (uint64_t)(K * P::KSTEPS / 4) * 2, PF_KS,
                   BN, CU_TENSOR_MAP_SWIZZLE_128B, 2))
@@ -1804,7 +1885,7 @@ int launch_pair_tb(const PrefillLaunch &L, cudaStream_t st) {
     uint16_t *S = P::MINS ? reinterpret_cast<uint16_t *>(ws + parts.b) : nullptr;
     float *DA = reinterpret_cast<float *>(ws + parts.b + parts.s);
     float *part = reinterpret_cast<float *>(ws + parts.b + parts.s + parts.da);
-    if (launch_prep<P::KSTEPS / 4>(L, nsb, m_pad, B, S, DA, st) != 0) return -2;
+    if (launch_prep_t<T>(L, nsb, m_pad, B, S, DA, st) != 0) return -2;
     // each prefill copy as rows of 128 bytes: one K-step's A tile is 128 rows,
     // the mins operand 64 (the copy is already in the shared-memory layout, so
     // the maps do not swizzle)
@@ -1903,7 +1984,8 @@ int launch_pk_t(const PrefillLaunch &L, cudaStream_t st) {
 
 template <uint32_t T>
 constexpr int64_t block_bytes() {
-    return T == T_Q4_K ? B_Q4_K : T == T_Q5_K ? B_Q5_K : T == T_Q6_K ? B_Q6_K : T == T_Q3_K ? B_Q3_K : B_Q2_K;
+    return T == T_Q4_K ? B_Q4_K : T == T_Q5_K ? B_Q5_K : T == T_Q6_K ? B_Q6_K : T == T_Q3_K ? B_Q3_K
+         : T == T_F16 ? 512 : B_Q2_K;
 }
 
 template <uint32_t T>
@@ -2292,7 +2374,7 @@ bool prefill_supported(uint32_t wtype) { return wtype == T_Q4_K || wtype == T_Q6
 bool is_classic(uint32_t wtype) { return wtype == T_Q4_0 || wtype == T_Q5_0 || wtype == T_Q8_0; }
 bool prefill_pack_supported(uint32_t wtype) {
     return wtype == T_Q2_K || wtype == T_Q3_K || wtype == T_Q4_K || wtype == T_Q5_K || wtype == T_Q6_K ||
-           is_classic(wtype);
+           wtype == T_F16 || is_classic(wtype);
 }
 bool prefill_groupable(uint32_t wtype) { return prefill_pack_supported(wtype) && !is_classic(wtype); }
 
@@ -2318,6 +2400,7 @@ size_t prefill_pack_bytes(uint32_t wtype, int64_t n_in, int64_t n_out) {
         case T_Q5_K: return (size_t)(nrt * nsb) * (size_t)pk_chunk<T_Q5_K>();
         case T_Q3_K: return (size_t)(nrt * nsb) * (size_t)pk_chunk<T_Q3_K>();
         case T_Q2_K: return (size_t)(nrt * nsb) * (size_t)pk_chunk<T_Q2_K>();
+        case T_F16: return (size_t)(nrt * nsb) * (size_t)pk_chunk<T_F16>();
         default: return 0;
     }
 }
@@ -2329,6 +2412,7 @@ int launch_prefill_pack(uint32_t wtype, const void *w, int64_t n_in, int64_t n_o
         case T_Q5_K: return launch_pack_t<T_Q5_K>(w, n_in, n_out, pack, st);
         case T_Q3_K: return launch_pack_t<T_Q3_K>(w, n_in, n_out, pack, st);
         case T_Q2_K: return launch_pack_t<T_Q2_K>(w, n_in, n_out, pack, st);
+        case T_F16: return launch_pack_t<T_F16>(w, n_in, n_out, pack, st);
         case T_Q8_0: return launch_pack_i8_t<T_Q8_0>(w, n_in, n_out, pack, st);
         case T_Q4_0: return launch_pack_i8_t<T_Q4_0>(w, n_in, n_out, pack, st);
         case T_Q5_0: return launch_pack_i8_t<T_Q5_0>(w, n_in, n_out, pack, st);
@@ -2343,6 +2427,7 @@ int launch_prefill(uint32_t wtype, const PrefillLaunch &L, cudaStream_t st) {
         case T_Q5_K: return launch_pk_t<T_Q5_K>(L, st);
         case T_Q3_K: return launch_pk_t<T_Q3_K>(L, st);
         case T_Q2_K: return launch_pk_t<T_Q2_K>(L, st);
+        case T_F16: return launch_pk_t<T_F16>(L, st);
         case T_Q8_0: return launch_i8_t<T_Q8_0>(L, st);
         case T_Q4_0: return launch_i8_t<T_Q4_0>(L, st);
         case T_Q5_0: return launch_i8_t<T_Q5_0>(L, st);

@@ -163,7 +163,8 @@ def test_prefill_copy_size_and_checks_run_on_host(so):
     assert so.prefill_pack_bytes(Q.Q2_K, 1024, 300) == 3 * 4 * (4 * 16384 + 8192 + 512)
     assert so.prefill_pack_bytes(Q.Q3_K, 1280, 130) == 2 * 5 * (4 * 16384 + 512)
     n = C.c_size_t(7)
-    assert so.lib.sicu_prefill_pack_bytes(Q.F16, 256, 128, C.byref(n)) == L.SICU_ENOTSUP and n.value == 0
+    assert so.lib.sicu_prefill_pack_bytes(Q.F32, 256, 128, C.byref(n)) == L.SICU_ENOTSUP and n.value == 0
+    assert so.prefill_pack_bytes(Q.F16, 512, 130) == 2 * 2 * (4 * 16384 + 512)   # the f16 weights re-tiled
     # classic formats: per 128-row tile and K-step of four 32-blocks, 16 KiB of
     # int8 quants + 2 KiB of row scales; at least one 128-element K-step
     assert so.prefill_pack_bytes(Q.Q8_0, 4096, 4096) == 32 * 32 * (16384 + 2048)
@@ -176,7 +177,7 @@ def test_prefill_copy_size_and_checks_run_on_host(so):
     assert so.lib.sicu_prefill_pack(Q.Q4_K, 16, 256, 128, 32, need, None) == L.SICU_EINVAL   # not initialised
     assert "sicu_init" in so.last_error()
     # a copy given for a type without one
-    assert so.lib.sicu_gemm_prefill_packed_f32(Q.F16, 16, 32, 256, 128, 64, 64, 128, None) == L.SICU_EINVAL
+    assert so.lib.sicu_gemm_prefill_packed_f32(Q.F32, 16, 32, 256, 128, 64, 64, 128, None) != L.SICU_OK
 
 
 def test_prefill_multi_checks_run_on_host(so):
@@ -196,7 +197,7 @@ def test_prefill_multi_checks_run_on_host(so):
     assert f(Q.Q4_K, 2, w, ok_packs, None, 256, 128, 64, y, None) == L.SICU_EINVAL
     assert f(Q.Q4_K, 2, w, bad_packs, n_out, 256, 128, 64, y, None) == L.SICU_EINVAL     # misaligned copy
     assert "aligned" in so.last_error()
-    assert f(Q.F16, 2, w, ok_packs, n_out, 256, 128, 64, y, None) == L.SICU_EINVAL       # no copies for F16
+    assert f(Q.F32, 2, w, ok_packs, n_out, 256, 128, 64, y, None) != L.SICU_OK          # no copies for F32
     assert f(Q.Q4_K, 2, w, ok_packs, n_out, 300, 128, 64, y, None) == L.SICU_EINVAL      # not whole super-blocks
     assert f(Q.Q4_K, 2, w, ok_packs, n_out, 256, 128, 64, y, None) == L.SICU_EINVAL      # not initialised
     assert "sicu_init" in so.last_error()

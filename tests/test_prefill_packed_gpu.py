@@ -242,7 +242,7 @@ def test_pack_errors(sicu):
     with pytest.raises(SicuError):
         sicu.prefill_pack(Q.Q4_K, w, 256, 128, p, n - 16)          # too small
     with pytest.raises(SicuError):
-        sicu.prefill_pack(Q.F16, w, 256, 128, p, n)                # no prefill copy
+        sicu.prefill_pack(Q.F32, w, 256, 128, p, n)                # no prefill copy
     with pytest.raises(SicuError):
         sicu.prefill_pack(Q.Q4_K, w, 200, 128, p, n)               # not whole super-blocks
     x = torch.zeros(256, dtype=torch.float32, device="cuda")
@@ -382,3 +382,54 @@ def test_copy_only_formats_without_a_copy(sicu, oracle, wt, n_out, n_in, m):
     sicu.gemm_prefill_f32(wt, dw, n_in, n_out, dev(x), m, y3)
     assert_bits_equal(host(y3), got, "f32 entry")
     assert sicu.status() == 0
+
+
+def _f16_l1(x, w, n_in, n_out):
+    """L1 = sum_k |x16_k| |w_k| of the F16 dot's products (x as the f16 the
+    reference converts it to)."""
+    xd = np.abs(x.astype(np.float16).astype(np.float64))
+    wd = np.abs(w.view(np.float16).astype(np.float64).reshape(n_out, n_in))
+    return xd @ wd.T
+
+
+@pytest.mark.parametrize("n_out,n_in,m", [
+    (128, 256, 64),      # one tile, one chunk
+    (200, 1024, 77),     # ragged rows and tokens, CTA pairs
+    (130, 4096, 300),    # long rows, 256-token tiles
+])
+def test_f16_prefill_vs_reference(sicu, oracle, n_out, n_in, m):
+    """F16 weights on the tensor cores: the f16 weights re-tiled (no scale)
+    against the activation converted to f16, 256-element chunks summed in
+    tensor memory and added in the epilogue; within the prefill tolerance of
+    the reference's F16 dot (src/kernels.c:189-195, exact products added into
+    a double). With and without the caller's copy, f32 and f16 entries."""
+    wt = Q.F16
+    w = synth.weights(wt, n_out, n_in, seed=n_out + m)
+    x = synth.activations(n_in, m, seed=n_in + m)
+    xq = oracle.quantize_pair(wt, x)
+    want = oracle.gemv_batch(wt, w, n_in, n_out, xq)
+    l1 = _f16_l1(x, w, n_in, n_out)
+    dw = dev(w)
+    y = empty_f32(m, n_out)
+    sicu.gemm_prefill_f32(wt, dw, n_in, n_out, dev(x), m, y)
+    got = host(y)
+    _check_tol(got, want, l1, f"F16 prefill {n_out}x{n_in} m={m}")
+    dp = sicu.prefill_pack_bytes(wt, n_in, n_out)
+    import torch
+    pk = torch.zeros(dp, dtype=torch.uint8, device="cuda")
+    sicu.prefill_pack(wt, dw, n_in, n_out, pk, dp)
+    y2 = empty_f32(m, n_out)
+    sicu.gemm_prefill_packed(wt, dw, pk, n_in, n_out, dev(xq), m, y2)
+    assert_bits_equal(host(y2), got, "F16 prefill: f16 rows with the caller's copy")
+    assert sicu.status() == 0
+
+
+def test_f16_prefill_rows_not_whole_chunks_use_the_matvec(sicu, oracle):
+    """F16 rows that are not whole 256-element chunks: the matvec per token,
+    bit-identical with the reference's F16 dot."""
+    wt, n_out, n_in, m = Q.F16, 96, 320, 40
+    w = synth.weights(wt, n_out, n_in, seed=1)
+    x = synth.activations(n_in, m, seed=2)
+    y = empty_f32(m, n_out)
+    sicu.gemm_prefill_f32(wt, dev(w), n_in, n_out, dev(x), m, y)
+    assert_bits_equal(host(y), oracle.gemv_batch(wt, w, n_in, n_out, oracle.quantize_pair(wt, x)), "F16 K=320")

@@ -952,6 +952,7 @@ CASES = {
     "decode_full": "three eager decode steps of the TinyLlama-1.1B shape with the steps and attention, "
                    "the token at position 511 of a 512-position context",
     "batch8": "the batch-8 decode matvec: Q4_K and Q6_K 5120x27648, 8 tokens, 4 times each",
+    "prefill_i8": "prefill_i8_kernel<Q8_0>: 4096x4096 from its int8 prefill copy, 512 f32 tokens, twice",
 }
 
 
@@ -989,6 +990,16 @@ def run_case(case: str, reps: int = 4) -> int:
             s.gemv_f32(wt, w, n_in, n_out, x, y)
         torch.cuda.synchronize()
         g.destroy()
+    elif case == "prefill_i8":
+        wt, n, m = Q.Q8_0, 4096, 512
+        w = bench_weights(wt, n, n, 1, dev)
+        nb = s.prefill_pack_bytes(wt, n, n)
+        pk = torch.empty(nb, dtype=torch.uint8, device=dev)
+        s.prefill_pack(wt, w, n, n, pk, nb)
+        x = torch.randn(m, n, device=dev)
+        y = torch.empty(m, n, device=dev)
+        for _ in range(2):
+            s.gemm_prefill_packed_f32(wt, w, pk, n, n, x, m, y)
     elif case == "prefill":
         wt, n, m = Q.Q4_K, 4096, 512
         w = mp.device_weights(wt, n, n, 1, dev)

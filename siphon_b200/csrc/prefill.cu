@@ -2059,6 +2059,27 @@ __device__ __forceinline__ void tc_mma_s8(uint32_t d_tmem, uint64_t adesc, uint6
         : "memory");
 }
 
+// Two f32 operations per instruction (sm_100 f32x2), each element rounded as
+// the scalar operation rounds it. The int8 epilogue uses them for the exact
+// integer-to-float conversion and the scale products; its running sums stay
+// scalar additions: with packed additions after the packed products, some
+// outputs differed from the reference by an ulp (measured), as a fused
+// multiply-add would.
+__device__ __forceinline__ float2 fmul2_rn(float2 a, float2 b) {
+    float2 r;
+    asm("{.reg .b64 a_, b_, d_;\n\tmov.b64 a_, {%2, %3};\n\tmov.b64 b_, {%4, %5};\n\t"
+        "mul.rn.f32x2 d_, a_, b_;\n\tmov.b64 {%0, %1}, d_;}"
+        : "=f"(r.x), "=f"(r.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return r;
+}
+__device__ __forceinline__ float2 fadd2_rn(float2 a, float2 b) {
+    float2 r;
+    asm("{.reg .b64 a_, b_, d_;\n\tmov.b64 a_, {%2, %3};\n\tmov.b64 b_, {%4, %5};\n\t"
+        "add.rn.f32x2 d_, a_, b_;\n\tmov.b64 {%0, %1}, d_;}"
+        : "=f"(r.x), "=f"(r.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return r;
+}
+
 // Quant e (0..31) of a classic block b (its bytes), as the reference's dots
 // form it (src/kernels.c:203-205, 222-225, 241).
 template <uint32_t T>
@@ -2282,16 +2303,19 @@ __global__ void __launch_bounds__(I8_WARPS * 32, 1) prefill_i8_kernel(const __gr
 #pragma unroll
                 for (int g4 = 0; g4 < EPI_COLS / 4; ++g4) {
                     const float4 dq = dy4[g4];
-                    const float dyv[4] = {dq.x, dq.y, dq.z, dq.w};
 #pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        const int j = 4 * g4 + e;
-                        const uint32_t raw = v0[j];
-                        // the block's integer sum (|sumi| < 2^20) to float, exactly
-                        const float si = __fsub_rn(__int_as_float((int)raw + 0x4b400000), 12582912.0f);
-                        const float t = I8Fmt<T>::SCALES_FIRST ? __fmul_rn(si, __fmul_rn(dx, dyv[e]))
-                                                              : __fmul_rn(__fmul_rn(si, dx), dyv[e]);
-                        sum[j] = __fadd_rn(sum[j], t);
+                    for (int e = 0; e < 2; ++e) {
+                        const int j = 4 * g4 + 2 * e;   // tokens j, j + 1
+                        // the blocks' integer sums (|sumi| < 2^20) to float, exactly
+                        const float2 si = fadd2_rn(make_float2(__int_as_float((int)v0[j] + 0x4b400000),
+                                                               __int_as_float((int)v0[j + 1] + 0x4b400000)),
+                                                   make_float2(-12582912.0f, -12582912.0f));
+                        const float2 dy = e ? make_float2(dq.z, dq.w) : make_float2(dq.x, dq.y);
+                        const float2 dx2 = make_float2(dx, dx);
+                        const float2 t = I8Fmt<T>::SCALES_FIRST ? fmul2_rn(si, fmul2_rn(dx2, dy))
+                                                               : fmul2_rn(fmul2_rn(si, dx2), dy);
+                        sum[j] = __fadd_rn(sum[j], t.x);
+                        sum[j + 1] = __fadd_rn(sum[j + 1], t.y);
                     }
                 }
             }

@@ -170,25 +170,6 @@ __device__ __forceinline__ void ld_h8(const uint16_t *x, bool vec, uint16_t a[8]
     }
 }
 
-// dot_f16_seq with x's elements 8 at a time: the loads of a chunk are
-// issued before its eight additions, which stay in index order.
-__device__ __forceinline__ float dot_f16_seq8(const uint16_t *x, const uint16_t *y, int n) {
-    double s = 0.0;
-    int i = 0;
-    const bool vec = (reinterpret_cast<uintptr_t>(x) & 15) == 0;
-    for (; i + 8 <= n; i += 8) {
-        uint16_t a[8], b[8];
-        ld_h8(x + i, vec, a);
-#pragma unroll
-        for (int k = 0; k < 8; ++k) b[k] = y[i + k];
-#pragma unroll
-        for (int k = 0; k < 8; ++k) s = __dadd_rn(s, (double)__fmul_rn(h2f(a[k]), h2f(b[k])));
-    }
-    for (; i < n; ++i) s = __dadd_rn(s, (double)__fmul_rn(h2f(x[i]), h2f(y[i])));
-    return __double2float_rn(s);
-}
-
-
 // ---- exactly parallel f16 dots ------------------------------------------------
 // The reference adds the exact f32 products of two f16 vectors into a double
 // in index order. Each product of f16 values a, b is a multiple of
@@ -196,8 +177,8 @@ __device__ __forceinline__ float dot_f16_seq8(const uint16_t *x, const uint16_t 
 // smallest), so every partial sum is a multiple of 2^(qmin_a + qmin_b); a
 // double holds every such multiple below 2^(53 + qmin_a + qmin_b) exactly.
 // When sum |a_i b_i| <= max|a| * sum|b| stays below that, no addition rounds
-// in any order, and a parallel sum gives the sequential sum's bits. The
-// kernels below sum in parallel, check that bound for the head afterwards
+// in any order, and a parallel sum gives the sequential sum's bits. The value
+// dots below sum in parallel, check that bound for the head afterwards
 // (max|a| over everything they read, sum|b| and qmin_b of the fixed vector)
 // and redo the head sequentially when it fails.
 
@@ -273,63 +254,45 @@ __device__ __forceinline__ uint32_t h_of(const uint4 r[8], int i) {
 
 // Scores of positions 0..n_score-1 (row j of K at kh + j * hd; the row of
 // position `own` from krow_own when not null), times ks, into sc; q16 the
-// head's query as f16 in shared memory. Parallel sums (four accumulators per
-// dot), sequential when the exactness bound fails. A thread takes two
-// positions at a time and has all loads of a 64-element chunk of both rows in
-// flight before it uses them.
+// head's query as f16 in shared memory. Each position's dot is the
+// reference's sequential double sum (src/kernels.c:189-195, index order); a
+// thread runs two positions' chains side by side, the eight loads of each
+// row's chunk issued before their additions. (A parallel sum, checked against
+// an exactness bound afterwards, measured no faster: both are bounded by the
+// f32 -> f64 widening of every product, and the bound failed for typical
+// queries, whose smallest components have small last-bit weights.)
 __device__ void head_scores(const uint16_t *kh, const uint16_t *krow_own, int own, const uint16_t *q16, int hd,
-                            int n_score, float ks, float *sc, double *dscratch, int *iscratch, uint32_t *uscratch) {
-    double qsum;
-    int qqmin;
-    h_abs_sum_qmin(q16, hd, &qsum, &qqmin, dscratch, iscratch);
-    uint32_t kmax = 0;
+                            int n_score, float ks, float *sc) {
     const int nt = blockDim.x;
-    const bool vec = (reinterpret_cast<uintptr_t>(kh) & 15) == 0 && (hd & 63) == 0 &&
+    const bool vec = (reinterpret_cast<uintptr_t>(kh) & 15) == 0 && (hd & 7) == 0 &&
                      (!krow_own || (reinterpret_cast<uintptr_t>(krow_own) & 15) == 0);
     for (int j = threadIdx.x; j < n_score; j += 2 * nt) {
         const int j2 = j + nt;
         const bool two = j2 < n_score;
         const uint16_t *ra = (krow_own && j == own) ? krow_own : kh + (int64_t)j * hd;
         const uint16_t *rb = two ? ((krow_own && j2 == own) ? krow_own : kh + (int64_t)j2 * hd) : ra;
-        double a[4] = {0.0, 0.0, 0.0, 0.0}, b[4] = {0.0, 0.0, 0.0, 0.0};
+        double a = 0.0, b = 0.0;
+        int d = 0;
         if (vec) {
-            for (int d0 = 0; d0 < hd; d0 += 64) {
-                uint4 xa[8], xb[8];
-                ld_h64(ra + d0, xa);
-                if (two) ld_h64(rb + d0, xb);
+            for (; d + 8 <= hd; d += 8) {
+                uint16_t xa[8], xb[8];
+                ld_h8(ra + d, true, xa);
+                ld_h8(rb + d, true, xb);
 #pragma unroll
-                for (int i = 0; i < 64; ++i) {
-                    const float qv = h2f(q16[d0 + i]);
-                    const uint32_t ka = h_of(xa, i);
-                    kmax = max(kmax, ka & 0x7fffu);
-                    a[i & 3] = __dadd_rn(a[i & 3], (double)__fmul_rn(h2f(ka), qv));
-                    if (two) {
-                        const uint32_t kb = h_of(xb, i);
-                        kmax = max(kmax, kb & 0x7fffu);
-                        b[i & 3] = __dadd_rn(b[i & 3], (double)__fmul_rn(h2f(kb), qv));
-                    }
-                }
-            }
-        } else {
-            for (int d = 0; d < hd; ++d) {   // any order is exact under the bound checked below
-                const float qv = h2f(q16[d]);
-                kmax = max(kmax, (uint32_t)ra[d] & 0x7fffu);
-                a[0] = __dadd_rn(a[0], (double)__fmul_rn(h2f(ra[d]), qv));
-                if (two) {
-                    kmax = max(kmax, (uint32_t)rb[d] & 0x7fffu);
-                    b[0] = __dadd_rn(b[0], (double)__fmul_rn(h2f(rb[d]), qv));
+                for (int k = 0; k < 8; ++k) {
+                    const float qv = h2f(q16[d + k]);
+                    a = __dadd_rn(a, (double)__fmul_rn(h2f(xa[k]), qv));
+                    b = __dadd_rn(b, (double)__fmul_rn(h2f(xb[k]), qv));
                 }
             }
         }
-        sc[j] = __fmul_rn(__double2float_rn(__dadd_rn(__dadd_rn(a[0], a[1]), __dadd_rn(a[2], a[3]))), ks);
-        if (two) sc[j2] = __fmul_rn(__double2float_rn(__dadd_rn(__dadd_rn(b[0], b[1]), __dadd_rn(b[2], b[3]))), ks);
-    }
-    kmax = cta_max_u32(kmax, uscratch);
-    if (!dots_exact(kmax, qsum, qqmin)) {
-        for (int j = threadIdx.x; j < n_score; j += blockDim.x) {
-            const uint16_t *row = (krow_own && j == own) ? krow_own : kh + (int64_t)j * hd;
-            sc[j] = __fmul_rn(dot_f16_seq8(row, q16, hd), ks);
+        for (; d < hd; ++d) {
+            const float qv = h2f(q16[d]);
+            a = __dadd_rn(a, (double)__fmul_rn(h2f(ra[d]), qv));
+            b = __dadd_rn(b, (double)__fmul_rn(h2f(rb[d]), qv));
         }
+        sc[j] = __fmul_rn(__double2float_rn(a), ks);
+        if (two) sc[j2] = __fmul_rn(__double2float_rn(b), ks);
     }
     __syncthreads();
 }
@@ -430,7 +393,7 @@ __global__ void __launch_bounds__(256) attention_kernel(const float *q, const ui
     __syncthreads();
     const uint16_t *kh = kc + (int64_t)hk * n_ctx * hd;
     const uint16_t *vh = vc + (int64_t)hk * hd * n_ctx;
-    head_scores(kh, nullptr, -1, q16, hd, n_score, ks, sc, &dscr, &iscr, &uscr);
+    head_scores(kh, nullptr, -1, q16, hd, n_score, ks, sc);
     softmax_row(sc, sc, n_score);
     for (int j = threadIdx.x; j < n_score; j += blockDim.x) p16[j] = (uint16_t)f2h(sc[j]);
     __syncthreads();
@@ -444,8 +407,8 @@ __global__ void __launch_bounds__(256) attention_kernel(const float *q, const ui
 // positions), the scores of positions 0..pos (this position's from the f16 k
 // in shared memory, the same bits the cache holds), softmax, f16
 // probabilities and the value dots (this position's V from shared memory);
-// scores and value dots summed in parallel where that is exact (head_scores,
-// head_values).
+// the scores as sequential chains in the reference's order (head_scores), the
+// value dots summed in parallel where that is exact (head_values).
 // Same results as rope_kernel + kv_store_kernel + attention_kernel. Launched
 // after the producing matvec has finished (launched early behind it, the
 // decode step measured slower: 3.0 ms per TinyLlama-shape token against 1.86),
@@ -504,7 +467,7 @@ __global__ void __launch_bounds__(256) attention_step_kernel(const float *q, con
     __syncthreads();
     // scores and value dots: this position's k and v from shared memory (the
     // same bits the cache holds), positions 0..pos-1 from the cache
-    head_scores(kh, k16, pos, q16, hd, n_score, ks, sc, &dscr, &iscr, &uscr);
+    head_scores(kh, k16, pos, q16, hd, n_score, ks, sc);
     softmax_row(sc, sc, n_score);
     for (int j = tid; j < n_score; j += blockDim.x) p16[j] = (uint16_t)f2h(sc[j]);
     __syncthreads();

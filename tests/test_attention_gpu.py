@@ -97,9 +97,10 @@ def test_attention_step_equals_separate_launches(sicu, oracle, neox):
 
 @pytest.mark.parametrize("case", ["parallel", "values_fallback", "scores_fallback", "both_fallback"])
 def test_attention_exactness_bound_and_fallback(sicu, oracle, case):
-    """The scores and value dots are summed in parallel when no addition can
-    round (max|a| * sum|b| below 2^(53 + the smallest last-bit weights)) and
-    sequentially otherwise; both give the reference's bits. Large V values
+    """The value dots are summed in parallel when no addition can round
+    (max|a| * sum|b| below 2^(53 + the smallest last-bit weights)) and
+    sequentially otherwise, the scores always sequentially; every form gives
+    the reference's bits. Large V values
     (|v| ~ 100 against subnormal probabilities) and a subnormal query
     component with large K values push the bound over."""
     import torch

@@ -283,10 +283,10 @@ SICU_API int sicu_gemm_prefill_packed_f32(uint32_t wtype, const void *dw, const 
  * token. The activation is quantized once and one launch covers every
  * matrix's tiles, so products too small to fill the GPU alone share it.
  * Each result is within the sicu_gemm_prefill tolerance (the same exact
- * integer sums per super-block). dpack null (or any entry null), or at most
- * 32 tokens: the products one after another as sicu_gemm_prefill_packed_f32
- * (up to 8 tokens one batch launch for all matrices). dw, dpack, n_out and
- * dy are host arrays. */
+ * integer sums per super-block). dpack null (or any entry null), at most
+ * 32 tokens, or Q4_0 / Q5_0 / Q8_0 weights: the products one after another as
+ * sicu_gemm_prefill_packed_f32 (up to 8 tokens one batch launch for all
+ * matrices). dw, dpack, n_out and dy are host arrays. */
 SICU_API int sicu_gemm_prefill_multi_f32(uint32_t wtype, int n_mats, const void *const *dw,
                                          const void *const *dpack, const int64_t *n_out, int64_t n_in,
                                          const float *dx, int64_t m, float *const *dy, void *stream);

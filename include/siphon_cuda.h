@@ -458,6 +458,22 @@ SICU_API int sicu_attention_step(const float *dq, const float *dk, const float *
                                  int64_t head_dim, int64_t n_rot, int neox, int64_t n_ctx, int64_t pos,
                                  float kq_scale, float *dout, void *stream);
 
+/* A prompt's attention: sicu_attention_step for the m consecutive positions
+ * pos0 .. pos0 + m - 1 in one call, as the engine's token-serial prompt loop
+ * (src/cmd_run.c:276) runs it one token at a time: dq [m][n_head * head_dim],
+ * dk and dv [m][n_head_kv * head_dim], dcos and dsin [m][n_rot / 2] (the
+ * tables of each token's position), dout [m][n_head * head_dim]. Every
+ * token's k (rotated) and v are stored into the caches first, then every
+ * (head, token) rotates its q and attends over positions 0 .. pos0 + t, which
+ * then hold exactly what the engine's cache held at that token: outputs and
+ * caches bit-identical to m sicu_attention_step calls. dq, dk, dv are left
+ * unrotated. pos0 + m <= min(n_ctx, 30000). No counterpart as one call in
+ * the reference. */
+SICU_API int sicu_attention_prompt(const float *dq, const float *dk, const float *dv, void *dk_cache,
+                                   void *dv_cache, const float *dcos, const float *dsin, int64_t n_head,
+                                   int64_t n_head_kv, int64_t head_dim, int64_t n_rot, int neox, int64_t n_ctx,
+                                   int64_t pos0, int64_t m, float kq_scale, float *dout, void *stream);
+
 /* ---- dequantisation --------------------------------------------------------
  * Rows rows[0..nrows) (host array) of W into dout[nrows][n_in] f32, reference
  * semantics. Replaces cpu_row_to_f32 (src/backend.c:122-131) with

@@ -1173,6 +1173,29 @@ int sicu_attention_step(const float *dq, const float *dk, const float *dv, void 
     return SICU_OK;
 }
 
+int sicu_attention_prompt(const float *dq, const float *dk, const float *dv, void *dk_cache, void *dv_cache,
+                          const float *dcos, const float *dsin, int64_t n_head, int64_t n_head_kv, int64_t head_dim,
+                          int64_t n_rot, int neox, int64_t n_ctx, int64_t pos0, int64_t m, float kq_scale,
+                          float *dout, void *stream) {
+    if (n_head <= 0 || n_head_kv <= 0 || n_head % n_head_kv || head_dim <= 0 || head_dim > 1024 || n_ctx <= 0 ||
+        n_ctx > INT32_MAX || pos0 < 0 || m < 0 || pos0 + m > n_ctx || n_head * head_dim > INT32_MAX || n_rot < 0 ||
+        n_rot > head_dim || n_rot % 2 || (neox && head_dim % 2) || n_head > 65535 || m > 65535)
+        return fail(SICU_EINVAL, "attention prompt: bad shape or positions");
+    if (pos0 + m > 30000) return fail(SICU_EINVAL, "attention prompt: at most 30000 positions per call");
+    if (m == 0) return current_ok();
+    if (!dq || !dk || !dv || !dk_cache || !dv_cache || !dout || (n_rot && (!dcos || !dsin)))
+        return fail(SICU_EINVAL, "attention prompt: null pointer");
+    if (!aligned(dk_cache, 2) || !aligned(dv_cache, 2))
+        return fail(SICU_EINVAL, "attention prompt: caches must be 2-byte aligned");
+    DevState *ds;
+    if (int rc = current(ds)) return rc;
+    if (launch_attention_prompt(dq, dk, dv, dk_cache, dv_cache, dcos, dsin, (int)n_head, (int)n_head_kv,
+                                (int)head_dim, (int)n_rot, neox ? 1 : 0, (int)n_ctx, (int)pos0, (int)m, kq_scale, dout,
+                                (cudaStream_t)stream))
+        return cuda_fail(cudaGetLastError(), "attention prompt launch");
+    return SICU_OK;
+}
+
 int sicu_row_to_f32_dev(uint32_t wtype, const void *dw, int64_t n_in, int64_t n_rows, const int64_t *drows,
                         int64_t nrows, float *dout, void *stream) {
     uint32_t blck, bytes;

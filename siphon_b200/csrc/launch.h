@@ -187,6 +187,11 @@ int launch_kv_store(const float *k, const float *v, void *kc, void *vc, int n_he
                     cudaStream_t st);
 // the three in one launch (overlap: unused; the launch always waits for the
 // previous kernel to finish)
+// a prompt's m consecutive positions pos0..pos0+m-1: RoPE, the K/V store and
+// every (head, token)'s attention over its prefix (two launches)
+int launch_attention_prompt(const float *q, const float *k, const float *v, void *kc, void *vc, const float *cs,
+                            const float *sn, int n_head, int n_head_kv, int hd, int n_rot, int neox, int n_ctx, int pos0,
+                            int m, float ks, float *out, cudaStream_t st);
 int launch_attention_step(const float *q, const float *k, const float *v, void *kc, void *vc, const float *cs,
                           const float *sn, int n_head, int n_head_kv, int hd, int n_rot, int neox, int n_ctx, int pos,
                           float ks, float *out, int overlap, cudaStream_t st);

@@ -510,6 +510,83 @@ __global__ void kv_store_kernel(const float *k, const float *v, uint16_t *kc, ui
     }
 }
 
+// ---- a prompt's attention: m consecutive positions in two launches -------------
+// The engine runs a prompt one token at a time (src/cmd_run.c:276): for token
+// t at position pos0 + t, RoPE of its q and k, k and v stored at that
+// position, then each head's attention over positions 0..pos0 + t
+// (src/engine.c:336-366, 90-147). Here every token's k and v are rotated and
+// stored first (one CTA per token), then one CTA per (head, token) rotates its
+// q and attends over its prefix, which by then holds exactly what the
+// token-serial engine's cache held at that token: the same computations, the
+// same bits, m tokens at once.
+
+// channel d of one head's vector after RoPE with tables c, s (n_rot / 2 pairs),
+// the rotation attention_step_kernel applies
+__device__ __forceinline__ float rope_channel(const float *x, int d, int hd, int n_rot, int neox, const float *c,
+                                              const float *s) {
+    if (!neox) {
+        const int j = d >> 1;
+        if (2 * j >= n_rot) return x[d];
+        const float x0 = x[2 * j], x1 = x[2 * j + 1];
+        return (d & 1) ? __fmaf_rn(x0, s[j], __fmul_rn(x1, c[j])) : __fmaf_rn(x0, c[j], -__fmul_rn(x1, s[j]));
+    }
+    const int half = hd / 2, j = d < half ? d : d - half;
+    if (j >= n_rot / 2) return x[d];
+    const float x0 = x[j], x1 = x[j + half];
+    return d < half ? __fsub_rn(__fmul_rn(x0, c[j]), __fmul_rn(x1, s[j]))
+                    : __fadd_rn(__fmul_rn(x0, s[j]), __fmul_rn(x1, c[j]));
+}
+
+// token t = blockIdx.x: its k rotated and stored (f16) at position pos0 + t
+// of the K cache, its v stored at that position of the V cache
+__global__ void prompt_kv_store_kernel(const float *k, const float *v, uint16_t *kc, uint16_t *vc, const float *cs,
+                                       const float *sn, int n_head_kv, int hd, int n_rot, int neox, int n_ctx,
+                                       int pos0) {
+    const int t = blockIdx.x, pos = pos0 + t;
+    const float *kt = k + (int64_t)t * n_head_kv * hd, *vt = v + (int64_t)t * n_head_kv * hd;
+    const float *c = cs + (int64_t)t * (n_rot / 2), *s = sn + (int64_t)t * (n_rot / 2);
+    for (int i = threadIdx.x; i < n_head_kv * hd; i += blockDim.x) {
+        const int hh = i / hd, d = i - hh * hd;
+        kc[((int64_t)hh * n_ctx + pos) * hd + d] = (uint16_t)f2h(rope_channel(kt + (int64_t)hh * hd, d, hd, n_rot,
+                                                                               neox, c, s));
+        vc[((int64_t)hh * hd + d) * n_ctx + pos] = (uint16_t)f2h(vt[i]);
+    }
+}
+
+// query head h = blockIdx.x of token t = blockIdx.y: its q rotated and made
+// f16, then the scores, softmax and value dots of attention_step_kernel over
+// positions 0..pos0 + t of the caches. Dynamic shared memory: (pos0 + m) x 6
+// bytes + 16.
+__global__ void __launch_bounds__(256) prompt_attention_kernel(const float *q, const uint16_t *kc, const uint16_t *vc,
+                                                               const float *cs, const float *sn, int n_head, int gqa,
+                                                               int hd, int n_rot, int neox, int n_ctx, int pos0,
+                                                               float ks, float *out) {
+    extern __shared__ __align__(16) uint8_t sm[];
+    const int h = blockIdx.x, t = blockIdx.y, hk = h / gqa, tid = threadIdx.x;
+    const int n_score = pos0 + t + 1;
+    float *sc = reinterpret_cast<float *>(sm);
+    uint16_t *p16 = reinterpret_cast<uint16_t *>(sc + n_score);
+    __shared__ __align__(16) float qf[1024];
+    __shared__ __align__(16) uint16_t q16[1024];
+    __shared__ double part[1024], dscr;
+    __shared__ int iscr;
+    __shared__ uint32_t uscr;
+    const float *qt = q + ((int64_t)t * n_head + h) * hd;
+    for (int d = tid; d < hd; d += blockDim.x) qf[d] = qt[d];
+    __syncthreads();
+    const float *c = cs + (int64_t)t * (n_rot / 2), *s = sn + (int64_t)t * (n_rot / 2);
+    for (int d = tid; d < hd; d += blockDim.x) q16[d] = (uint16_t)f2h(rope_channel(qf, d, hd, n_rot, neox, c, s));
+    __syncthreads();
+    const uint16_t *kh = kc + (int64_t)hk * n_ctx * hd;
+    const uint16_t *vh = vc + (int64_t)hk * hd * n_ctx;
+    head_scores(kh, nullptr, -1, q16, hd, n_score, ks, sc);
+    softmax_row(sc, sc, n_score);
+    for (int j = tid; j < n_score; j += blockDim.x) p16[j] = (uint16_t)f2h(sc[j]);
+    __syncthreads();
+    head_values(vh, n_ctx, nullptr, -1, p16, hd, n_score, out + ((int64_t)t * n_head + h) * hd, part, &dscr, &iscr,
+                &uscr);
+}
+
 }  // namespace
 
 int launch_attention(const float *q, const void *kc, const void *vc, int n_head, int n_head_kv, int hd, int n_ctx,
@@ -526,6 +603,28 @@ int launch_attention(const float *q, const void *kc, const void *vc, int n_head,
     }
     attention_kernel<<<n_head, 256, smem, st>>>(q, static_cast<const uint16_t *>(kc), static_cast<const uint16_t *>(vc),
                                                 n_head, n_head / n_head_kv, hd, n_ctx, n_score, ks, out);
+    return cudaPeekAtLastError() == cudaSuccess ? 0 : -2;
+}
+
+int launch_attention_prompt(const float *q, const float *k, const float *v, void *kc, void *vc, const float *cs,
+                            const float *sn, int n_head, int n_head_kv, int hd, int n_rot, int neox, int n_ctx, int pos0,
+                            int m, float ks, float *out, cudaStream_t st) {
+    static bool attr[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!attr[dev & 63]) {
+        if (cudaFuncSetAttribute(prompt_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 180 * 1024) !=
+            cudaSuccess)
+            return -2;
+        attr[dev & 63] = true;
+    }
+    prompt_kv_store_kernel<<<(unsigned)m, 256, 0, st>>>(k, v, static_cast<uint16_t *>(kc), static_cast<uint16_t *>(vc),
+                                                         cs, sn, n_head_kv, hd, n_rot, neox, n_ctx, pos0);
+    if (cudaPeekAtLastError() != cudaSuccess) return -2;
+    const size_t smem = (size_t)(pos0 + m) * 6 + 16;
+    prompt_attention_kernel<<<dim3((unsigned)n_head, (unsigned)m), 256, smem, st>>>(
+        q, static_cast<const uint16_t *>(kc), static_cast<const uint16_t *>(vc), cs, sn, n_head, n_head / n_head_kv, hd,
+        n_rot, neox, n_ctx, pos0, ks, out);
     return cudaPeekAtLastError() == cudaSuccess ? 0 : -2;
 }
 

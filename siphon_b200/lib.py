@@ -80,6 +80,8 @@ SIGNATURES = {
     "sicu_argmax": [_fp, _i64, _i64, _vp, _vp],
     "sicu_attention_step": [_fp, _fp, _fp, _vp, _vp, _fp, _fp, _i64, _i64, _i64, _i64, C.c_int, _i64, _i64,
                             C.c_float, _fp, _vp],
+    "sicu_attention_prompt": [_fp, _fp, _fp, _vp, _vp, _fp, _fp, _i64, _i64, _i64, _i64, C.c_int, _i64, _i64,
+                              _i64, C.c_float, _fp, _vp],
 }
 
 PRO_NONE, PRO_RMS_NORM, PRO_SWIGLU, PRO_MUL = 0, 1, 2, 3
@@ -321,6 +323,15 @@ class SiphonCuda:
         self.check(self.lib.sicu_attention_step(_ptr(dq), _ptr(dk), _ptr(dv), _ptr(dk_cache), _ptr(dv_cache),
                                                 _ptr(dcos), _ptr(dsin), n_head, n_head_kv, head_dim, n_rot,
                                                 1 if neox else 0, n_ctx, pos, kq_scale, _ptr(dout), _ptr(stream)))
+
+    def attention_prompt(self, dq, dk, dv, dk_cache, dv_cache, dcos, dsin, n_head: int, n_head_kv: int,
+                         head_dim: int, n_rot: int, n_ctx: int, pos0: int, m: int, kq_scale: float, dout,
+                         neox: bool = False, stream=None) -> None:
+        """attention_step for the m consecutive positions pos0 .. pos0 + m - 1 (a prompt)."""
+        self.check(self.lib.sicu_attention_prompt(_ptr(dq), _ptr(dk), _ptr(dv), _ptr(dk_cache), _ptr(dv_cache),
+                                                  _ptr(dcos), _ptr(dsin), n_head, n_head_kv, head_dim, n_rot,
+                                                  1 if neox else 0, n_ctx, pos0, m, kq_scale, _ptr(dout),
+                                                  _ptr(stream)))
 
     def row_to_f32_dev(self, wtype: int, dw, n_in: int, n_rows: int, drows, nrows: int, dout, stream=None) -> None:
         self.check(self.lib.sicu_row_to_f32_dev(wtype, _ptr(dw), n_in, n_rows, _ptr(drows), nrows, _ptr(dout),

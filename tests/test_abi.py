@@ -201,3 +201,23 @@ def test_prefill_multi_checks_run_on_host(so):
     assert f(Q.Q4_K, 2, w, ok_packs, n_out, 300, 128, 64, y, None) == L.SICU_EINVAL      # not whole super-blocks
     assert f(Q.Q4_K, 2, w, ok_packs, n_out, 256, 128, 64, y, None) == L.SICU_EINVAL      # not initialised
     assert "sicu_init" in so.last_error()
+
+
+def test_attention_prompt_checks_run_on_host(so):
+    """sicu_attention_prompt rejects bad shapes and positions before any
+    device work: a prompt past the cache, GQA that does not divide, an odd
+    or too large n_rot, null or misaligned buffers."""
+    f = so.lib.sicu_attention_prompt
+    p = 0x10000
+
+    def call(n_head=8, nkv=2, hd=64, n_rot=64, n_ctx=64, pos0=0, m=4, ptr=p, cache=p):
+        return f(ptr, ptr, ptr, cache, cache, ptr, ptr, n_head, nkv, hd, n_rot, 0, n_ctx, pos0, m, 0.125, ptr, None)
+    assert call(pos0=60, m=5) == L.SICU_EINVAL               # past the cache
+    assert call(nkv=3) == L.SICU_EINVAL                      # heads not a multiple of KV heads
+    assert call(n_rot=63) == L.SICU_EINVAL
+    assert call(n_rot=128) == L.SICU_EINVAL                  # more than the head
+    assert call(hd=2048, n_rot=64) == L.SICU_EINVAL          # head larger than 1024
+    assert call(m=-1) == L.SICU_EINVAL
+    assert call(ptr=None) == L.SICU_EINVAL
+    assert call(cache=p + 1) == L.SICU_EINVAL                # caches not 2-byte aligned
+    assert call(n_ctx=40000, pos0=29000, m=1001) == L.SICU_EINVAL   # more than 30000 positions

@@ -120,3 +120,44 @@ def test_attention_exactness_bound_and_fallback(sicu, oracle, case):
     out = empty_f32(n_head * hd)
     sicu.attention(dev(q), kd, vd, n_head, nkv, hd, n_ctx, pos, ks, out)
     assert_bits_equal(host(out), oracle.attention(q, k, v, n_head, nkv, hd, n_ctx, pos, ks), case)
+
+
+@pytest.mark.parametrize("neox,n_rot,pos0,m", [(False, 128, 0, 37), (True, 128, 20, 44), (False, 64, 5, 1)])
+def test_attention_prompt_equals_token_steps(sicu, oracle, neox, n_rot, pos0, m):
+    """sicu_attention_prompt (m consecutive positions in one call) against m
+    sicu_attention_step calls, the engine's token-serial order: the same
+    outputs and caches, bit for bit; the last token's heads also against the
+    oracle's attention over the final caches."""
+    import torch
+    rng = np.random.default_rng(pos0 * 100 + m)
+    n_head, nkv, hd, n_ctx = 8, 2, 128, 96
+    k0, v0 = random_cache(rng, nkv, hd, n_ctx)
+    theta = rng.uniform(-20, 20, (m, n_rot // 2))
+    c = np.cos(theta).astype(np.float32)
+    s = np.sin(theta).astype(np.float32)
+    ks = float(np.float32(1.0 / np.sqrt(hd)))
+    q = (rng.standard_normal((m, n_head * hd)) * 2).astype(np.float32)
+    k = (rng.standard_normal((m, nkv * hd)) * 2).astype(np.float32)
+    v = (rng.standard_normal((m, nkv * hd)) * 2).astype(np.float32)
+    kc1 = torch.from_numpy(k0.view(np.int16).reshape(-1).copy()).cuda()
+    vc1 = torch.from_numpy(v0.view(np.int16).reshape(-1).copy()).cuda()
+    kc2, vc2 = kc1.clone(), vc1.clone()
+    out1 = empty_f32(m, n_head * hd)
+    qd, kd, vd = dev(q), dev(k), dev(v)
+    sicu.attention_prompt(qd, kd, vd, kc1, vc1, dev(c), dev(s), n_head, nkv, hd, n_rot, n_ctx, pos0, m, ks, out1,
+                          neox=neox)
+    out2 = np.zeros((m, n_head * hd), np.float32)
+    for t in range(m):
+        o = empty_f32(n_head * hd)
+        sicu.attention_step(dev(q[t]), dev(k[t]), dev(v[t]), kc2, vc2, dev(c[t]), dev(s[t]), n_head, nkv, hd, n_rot,
+                            n_ctx, pos0 + t, ks, o, neox=neox)
+        out2[t] = host(o)
+    assert_bits_equal(host(out1), out2, f"prompt pos0={pos0} m={m} outputs")
+    assert (host(kc1) == host(kc2)).all() and (host(vc1) == host(vc2)).all(), "caches"
+    assert_bits_equal(host(qd), q, "q left unrotated")
+    # the last token's attention, with its q rotated on the host by the oracle
+    qr = oracle.rope(q[m - 1], n_head, hd, n_rot, c[m - 1], s[m - 1], neox=neox)
+    kf = host(kc1).view(np.uint16).reshape(nkv, n_ctx, hd)
+    vf = host(vc1).view(np.uint16).reshape(nkv, hd, n_ctx)
+    want = oracle.attention(qr, kf, vf, n_head, nkv, hd, n_ctx, pos0 + m - 1, ks)
+    assert_bits_equal(host(out1)[m - 1], want, "last token vs oracle")

@@ -426,6 +426,36 @@ def model_prefill(torch, s, shape, dev, stream, world, rank, group, m_tok, reps)
     return out
 
 
+def model_prompt(torch, s, shape, dev, stream, m_tok, reps) -> dict:
+    """A whole prompt's forward pass in one pass (MatrixPath.prompt_step, one
+    GPU): m_tok token ids in device memory -> the embedding rows, every
+    layer's norms, products (from the prefill copies), RoPE, KV-cache stores
+    and each token's attention over its prefix, SwiGLU, the head's logits of
+    every token and the greedy choice after the last. Graph-timed."""
+    from siphon_b200 import model_path as mp
+    m = mp.MatrixPath(s, shape, dev, seed=6, embed=True, n_ctx=m_tok, max_tokens=m_tok, packed=True)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(3)
+    m.tokens.copy_(torch.randint(0, shape.n_vocab, (m_tok,), device=dev, generator=gen))
+    with torch.cuda.stream(stream):
+        launches = m.prompt_step(stream, m_tok)     # sizes the workspace outside capture
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        m.prompt_step(stream, m_tok)
+    ms = _time_graph(torch, g, stream, reps, 1, dev)
+    del g
+    sec = ms * 1e-3 / reps
+    assert s.status() == 0, "a kernel of the prompt pass reported a device-side status"
+    out = {"tok_s": round(m_tok / sec, 1), "ms_per_prompt": round(sec * 1e3, 3), "prompt_tokens": m_tok,
+           "library_calls_per_prompt": launches,
+           "pack_bytes": int(sum(t.numel() for t in m.pack.values()))}
+    m.close()
+    del m
+    torch.cuda.empty_cache()
+    return out
+
+
 def model_batch_decode(torch, s, shape, dev, stream, world, rank, group, batch, reps) -> dict:
     """Decode tok/s of the matrix path for `batch` sequences per step (one
     token each): every weight product once per step for all of them, through
@@ -736,6 +766,12 @@ def model_metrics(torch, s, dev, stream, world, rank, quick: bool) -> tuple[dict
                                         "reference's forward pass but the embedding lookup",
                               **model_decode(torch, s, sm.TINYLLAMA, dev, stream, 1, 0, None, reps * 4,
                                              attention_ctx=512)}
+        out["prompt_full"] = {"config": "configs[2] TinyLlama-1.1B shape, a 512-token prompt's whole forward pass "
+                                        "in one pass: embedding, norms, products, RoPE, KV cache, each token's "
+                                        "attention over its prefix, SwiGLU, the logits of every token, the greedy "
+                                        "choice (MatrixPath.prompt_step); the reference engine runs a prompt "
+                                        "token by token (engine_cpu decode_tinyllama prompt_tok_s)",
+                              **model_prompt(torch, s, sm.TINYLLAMA, dev, stream, 512, max(2, reps // 2))}
         out["prefill"] = {"config": "configs[3] Llama-3-8B shape, 512-token prompt, matrix path",
                           **model_prefill(torch, s, sm.LLAMA3_8B, dev, stream, 1, 0, None, 512, max(2, reps // 2))}
         out["prefill_per_format"] = prefill_per_format(torch, s, dev, stream)
@@ -953,6 +989,8 @@ CASES = {
                    "the token at position 511 of a 512-position context",
     "batch8": "the batch-8 decode matvec: Q4_K and Q6_K 5120x27648, 8 tokens, 4 times each",
     "prefill_i8": "prefill_i8_kernel<Q8_0>: 4096x4096 from its int8 prefill copy, 512 f32 tokens, twice",
+    "prompt_full": "two eager whole-prompt passes (MatrixPath.prompt_step) of the TinyLlama-1.1B shape, "
+                   "512 tokens",
 }
 
 
@@ -1035,6 +1073,14 @@ def run_case(case: str, reps: int = 4) -> int:
         with torch.cuda.stream(st):
             for _ in range(3):
                 m.decode_step(st)
+        torch.cuda.synchronize()
+        m.close()
+    elif case == "prompt_full":
+        m = mp.MatrixPath(s, sm.TINYLLAMA, dev, seed=6, embed=True, n_ctx=512, max_tokens=512, packed=True)
+        st = torch.cuda.Stream(device=dev)
+        with torch.cuda.stream(st):
+            for _ in range(2):
+                m.prompt_step(st, 512)
         torch.cuda.synchronize()
         m.close()
     elif case == "batch8":

@@ -10,7 +10,15 @@ benchmark configs (synthetic Q4_K_M-style weights generated on the device):
 * ``decode_step``: one token (batch 1), sicu_gemv_multi for products that
   share an activation and type (Wq/Wk[/Wv], W_gate/W_up), sicu_gemv_f32 for
   the rest;
-* ``prefill``: m tokens at once through sicu_gemm_prefill_f32.
+* ``prefill``: m tokens at once through sicu_gemm_prefill_f32;
+* ``prompt_step`` (``embed=True``, ``max_tokens`` > 1, one GPU): a prompt's
+  whole forward pass, m tokens at once: the embedding rows, the RMS norms
+  with their residual adds (sicu_rms_norm), the products (sicu_gemm_prefill_*),
+  RoPE, the KV-cache stores and each token's attention over its prefix
+  (sicu_attention_prompt), SwiGLU (sicu_swiglu), the head's logits for every
+  token and the greedy choice after the last; the caches are left as the
+  token-serial engine leaves them (src/cmd_run.c:275-276), so decode_step
+  carries on at position pos + m.
 
 With ``steps=True`` the decode step also runs the activation steps between
 the products the way the reference's forward pass does (engine.c:313-315,
@@ -115,6 +123,17 @@ def rope_tables(sh: LlamaShape, n_ctx: int):
     return cos, sin
 
 
+def packable(wtype: int, n_in: int) -> bool:
+    """Whether sicu_prefill_pack makes a prefill copy of a matrix of this
+    type and row length: the K formats; the classic formats with rows of at
+    least one 128-element K-step; F16 rows of whole 256-element chunks."""
+    if wtype in (Q.Q2_K, Q.Q3_K, Q.Q4_K, Q.Q5_K, Q.Q6_K):
+        return True
+    if wtype in (Q.Q4_0, Q.Q5_0, Q.Q8_0):
+        return n_in >= 128
+    return wtype == Q.F16 and n_in % 256 == 0
+
+
 def shard_shapes(sh: LlamaShape, shard: Shard) -> dict:
     """(n_out, n_in) of every matrix one rank holds."""
     hd = sh.head_dim
@@ -203,16 +222,16 @@ class MatrixPath:
             self.head = from_file("output.weight", n_out, n_in)
         else:
             self.head = (Q.Q6_K, device_weights(Q.Q6_K, n_out, n_in, seed * 7919 + 999 + 1000 * rank, device))
-        # prefill copies (sicu_prefill_pack) of the Q4_K / Q6_K matrices, made
-        # once here beside the raw blocks
+        # prefill copies (sicu_prefill_pack) of the matrices, made once here
+        # beside the raw blocks
         self.pack = {}
         if packed:
             mats = [((il, name), lay[name]) for il, lay in enumerate(self.layers) for name in lay]
             mats.append((("head",), self.head))
             for key, (t, w) in mats:
-                if t not in (Q.Q4_K, Q.Q6_K):
-                    continue
                 n_out, n_in = self.shapes[key[-1]]
+                if not packable(t, n_in):
+                    continue
                 nb = sicu.prefill_pack_bytes(t, n_in, n_out)
                 buf = torch.empty(nb, dtype=torch.uint8, device=device)
                 sicu.prefill_pack(t, w, n_in, n_out, buf, nb)
@@ -288,6 +307,15 @@ class MatrixPath:
                 self.embd = device_weights(Q.Q4_K, sh.n_vocab, sh.n_embd, seed * 7919 + 555, device)
             self.token = torch.zeros(1, dtype=torch.int64, device=device)
             self.x_embed = torch.empty(sh.n_embd, device=device)
+            if m > 1:
+                # a prompt of up to m tokens (prompt_step): its token ids, two
+                # residual streams used in turn, the normed rows, the attention
+                # output and the SwiGLU rows
+                self.tokens = torch.zeros(m, dtype=torch.int64, device=device)
+                self.xp = [torch.empty(m, sh.n_embd, device=device) for _ in range(2)]
+                self.xn = torch.empty(m, sh.n_embd, device=device)
+                self.att = torch.empty(m, nq, device=device)
+                self.ffp = torch.empty(m, nff, device=device)
         if fused and world > 1:
             import torch.distributed as dist
             self.ar = sicu.ar_create(world, rank, sh.n_embd)
@@ -479,44 +507,103 @@ class MatrixPath:
         s.gemv_batch(th, [wh], [self.shapes["head"][0]], d, self.x_model, m, [y["head"]], stream=h)
         return n + 1
 
+    def _prompt_products(self, il: int, group, n_in: int, xin, m: int, h) -> int:
+        """The m-row products of layer il's matrices `group` (one activation
+        xin): those with one weight type and prefill copies as one grouped
+        launch (Wq/Wk[/Wv], W_gate/W_up), the rest one by one. Returns the
+        number of library calls."""
+        s, y, lay = self.s, self.y, self.layers[il]
+        runs = []
+        for name in group:
+            t = lay[name][0]
+            pk = self.pack.get((il, name))
+            if runs and runs[-1][0] == t and pk is not None and runs[-1][1][-1][1] is not None:
+                runs[-1][1].append((name, pk))
+            else:
+                runs.append((t, [(name, pk)]))
+        for t, members in runs:
+            if len(members) > 1:
+                names = [nm for nm, _ in members]
+                s.gemm_prefill_multi_f32(t, [lay[nm][1] for nm in names], [pk for _, pk in members],
+                                         [self.shapes[nm][0] for nm in names], n_in, xin, m,
+                                         [y[nm] for nm in names], stream=h)
+                continue
+            name, pk = members[0]
+            w = lay[name][1]
+            if pk is not None:
+                s.gemm_prefill_packed_f32(t, w, pk, n_in, self.shapes[name][0], xin, m, y[name], stream=h)
+            else:
+                s.gemm_prefill_f32(t, w, n_in, self.shapes[name][0], xin, m, y[name], stream=h)
+        return len(runs)
+
+    def _prompt_head(self, x, m: int, h) -> None:
+        s, d = self.s, self.sh.n_embd
+        th, wh = self.head
+        pk = self.pack.get(("head",))
+        if pk is not None:
+            s.gemm_prefill_packed_f32(th, wh, pk, d, self.shapes["head"][0], x, m, self.y["head"], stream=h)
+        else:
+            s.gemm_prefill_f32(th, wh, d, self.shapes["head"][0], x, m, self.y["head"], stream=h)
+
     def prefill(self, stream, m: int) -> None:
         """Launch the products of an m-token prompt on `stream` (or, with m
         up to the batch size, one decode step of a batch of m sequences:
         the same products, every weight matrix streamed once for all m)."""
-        s, h, y = self.s, stream.cuda_stream, self.y
+        h, y = stream.cuda_stream, self.y
         d = self.sh.n_embd
-        nq, nkv, nff = self.shapes["q"][0], self.shapes["k"][0], self.shapes["gate"][0]
-        for il, lay in enumerate(self.layers):
-            # products that read one activation with one weight type and have
-            # prefill copies run as one grouped launch (Wq/Wk[/Wv], W_gate/W_up)
+        nq, nff = self.shapes["q"][0], self.shapes["gate"][0]
+        for il in range(len(self.layers)):
             for group, n_in, xin in ((("q", "k", "v"), d, self.x_model), (("o",), nq, self.x_attn),
                                      (("gate", "up"), d, self.x_model), (("down",), nff, self.x_ff)):
-                runs = []
-                for name in group:
-                    t = lay[name][0]
-                    pk = self.pack.get((il, name))
-                    if runs and runs[-1][0] == t and pk is not None and runs[-1][1][-1][1] is not None:
-                        runs[-1][1].append((name, pk))
-                    else:
-                        runs.append((t, [(name, pk)]))
-                for t, members in runs:
-                    if len(members) > 1:
-                        names = [nm for nm, _ in members]
-                        s.gemm_prefill_multi_f32(t, [lay[nm][1] for nm in names], [pk for _, pk in members],
-                                                 [self.shapes[nm][0] for nm in names], n_in, xin, m,
-                                                 [y[nm] for nm in names], stream=h)
-                        continue
-                    name, pk = members[0]
-                    w = lay[name][1]
-                    if pk is not None:
-                        s.gemm_prefill_packed_f32(t, w, pk, n_in, self.shapes[name][0], xin, m, y[name], stream=h)
-                    else:
-                        s.gemm_prefill_f32(t, w, n_in, self.shapes[name][0], xin, m, y[name], stream=h)
+                self._prompt_products(il, group, n_in, xin, m, h)
                 if group[0] in ("o", "down"):
                     self._allreduce(y[group[0]][:m])
-        th, wh = self.head
-        pk = self.pack.get(("head",))
-        if pk is not None:
-            s.gemm_prefill_packed_f32(th, wh, pk, d, self.shapes["head"][0], self.x_model, m, y["head"], stream=h)
-        else:
-            s.gemm_prefill_f32(th, wh, d, self.shapes["head"][0], self.x_model, m, y["head"], stream=h)
+        self._prompt_head(self.x_model, m, h)
+
+    def prompt_step(self, stream, m: int) -> int:
+        """The forward pass of the m prompt tokens in self.tokens[:m] at
+        positions self.pos .. self.pos + m - 1, all tokens at once, in the
+        reference's per-token order of steps (src/engine.c:290-398):
+        embedding rows; per layer h += (previous W_down output) and its RMS
+        norm, Wq/Wk/Wv, RoPE + cache stores + each token's attention over
+        positions 0 .. its own, Wo, h += Wo output and its RMS norm,
+        W_gate/W_up, SwiGLU, W_down; the output norm and the head's logits of
+        every token (y["head"][:m]); the greedy choice after the last token
+        into self.token. Every step but the products repeats the reference's
+        arithmetic per row; the products are the prefill kernels' (bit-exact
+        for the classic formats and the matvec sizes, within 1e-5 of each
+        output's L1 norm for the K formats and F16 on tensor cores). Returns
+        the number of library calls."""
+        if not (self.embed and hasattr(self, "tokens")):
+            raise ValueError("prompt_step needs MatrixPath(embed=True, max_tokens > 1)")
+        if self.bias is not None:
+            raise ValueError("prompt_step: Q/K/V biases (Qwen2) are not supported")
+        if not 0 < m <= self.tokens.numel() or self.pos + m > self.n_ctx:
+            raise ValueError(f"prompt of {m} tokens at position {self.pos}: past the buffers or the context")
+        s, h, y, d, eps = self.s, stream.cuda_stream, self.y, self.sh.n_embd, self.sh.rms_eps
+        nq, nkv, nff = self.shapes["q"][0], self.shapes["k"][0], self.shapes["gate"][0]
+        hd, p = self.sh.head_dim, self.pos
+        xp, xn = self.xp, self.xn
+        s.row_to_f32_dev(self.embd_type, self.embd, d, self.sh.n_vocab, self.tokens, m, xp[0], stream=h)
+        cur, nxt, res, n = 0, 1, None, 1
+        for il in range(len(self.layers)):
+            if res is None:
+                s.rms_norm(xp[cur], self.attn_norm[il], d, m, eps, xn, stream=h)
+            else:
+                s.rms_norm(xp[cur], self.attn_norm[il], d, m, eps, xn, dres=res, dsum=xp[nxt], stream=h)
+                cur, nxt = nxt, cur
+            n += 1 + self._prompt_products(il, ("q", "k", "v"), d, xn, m, h)
+            s.attention_prompt(y["q"], y["k"], y["v"], self.kc[il], self.vc[il], self.rope_cos[p:],
+                               self.rope_sin[p:], nq // hd, nkv // hd, hd, hd, self.n_ctx, p, m, self.kq_scale,
+                               self.att, neox=self.sh.neox, stream=h)
+            n += 1 + self._prompt_products(il, ("o",), nq, self.att, m, h)
+            s.rms_norm(xp[cur], self.ffn_norm[il], d, m, eps, xn, dres=y["o"], dsum=xp[nxt], stream=h)
+            cur, nxt = nxt, cur
+            n += 1 + self._prompt_products(il, ("gate", "up"), d, xn, m, h)
+            s.swiglu(y["gate"], y["up"], nff, m, self.ffp, stream=h)
+            n += 1 + self._prompt_products(il, ("down",), nff, self.ffp, m, h)
+            res = y["down"]
+        s.rms_norm(xp[cur], self.out_norm, d, m, eps, xn, dres=res, dsum=xp[nxt], stream=h)
+        self._prompt_head(xn, m, h)
+        s.argmax(y["head"][m - 1], self.shapes["head"][0], 1, self.token, stream=h)
+        return n + 3

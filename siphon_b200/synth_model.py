@@ -82,17 +82,19 @@ GGUF_NAMES = {"q": "attn_q", "k": "attn_k", "v": "attn_v", "o": "attn_output", "
               "up": "ffn_up", "down": "ffn_down"}
 
 
-def matrices(sh: LlamaShape) -> list[tuple[str, int, int, int]]:
-    """(tensor name, ggml type, n_out, n_in) of every weight matrix."""
+def matrices(sh: LlamaShape, wtype: int | None = None) -> list[tuple[str, int, int, int]]:
+    """(tensor name, ggml type, n_out, n_in) of every weight matrix: the
+    Q4_K_M-style mix, or every matrix (embedding and head included) of one
+    type `wtype`."""
     kv = sh.n_head_kv * sh.head_dim
-    out = [("token_embd.weight", Q.Q4_K, sh.n_vocab, sh.n_embd),
-           ("output.weight", Q.Q6_K, sh.n_vocab, sh.n_embd)]
+    out = [("token_embd.weight", wtype or Q.Q4_K, sh.n_vocab, sh.n_embd),
+           ("output.weight", wtype or Q.Q6_K, sh.n_vocab, sh.n_embd)]
     shapes = {"q": (sh.n_embd, sh.n_embd), "k": (kv, sh.n_embd), "v": (kv, sh.n_embd), "o": (sh.n_embd, sh.n_embd),
               "gate": (sh.n_ff, sh.n_embd), "up": (sh.n_ff, sh.n_embd), "down": (sh.n_embd, sh.n_ff)}
     for il in range(sh.n_layer):
         t = layer_types(il)
         for k in ("q", "k", "v", "o", "gate", "up", "down"):
-            out.append((f"blk.{il}.{GGUF_NAMES[k]}.weight", t[k], *shapes[k]))
+            out.append((f"blk.{il}.{GGUF_NAMES[k]}.weight", wtype or t[k], *shapes[k]))
     return out
 
 
@@ -129,7 +131,7 @@ def _vector(name: str, n: int, seed: int) -> np.ndarray:
     return v.astype(np.float32)
 
 
-def write_llama(path: str | Path, sh: LlamaShape, seed: int = 0, blocks="quantized") -> Path:
+def write_llama(path: str | Path, sh: LlamaShape, seed: int = 0, blocks="quantized", wtype: int | None = None) -> Path:
     a = sh.arch
     kvs = [
         ("general.architecture", gguf.STRING, a),
@@ -144,7 +146,7 @@ def write_llama(path: str | Path, sh: LlamaShape, seed: int = 0, blocks="quantiz
         (f"{a}.rope.freq_base", gguf.F32, sh.rope_base),
     ]
     tensors = []
-    for name, wt, n_out, n_in in matrices(sh):
+    for name, wt, n_out, n_in in matrices(sh, wtype):
         key = [seed, zlib.crc32(name.encode())]
         if callable(blocks):
             fn = (lambda wt=wt, n_out=n_out, n_in=n_in, key=key: blocks(wt, n_out, n_in, key))

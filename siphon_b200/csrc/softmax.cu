@@ -587,6 +587,251 @@ __global__ void __launch_bounds__(256) prompt_attention_kernel(const float *q, c
                 &uscr);
 }
 
+// ---- the prompt's attention per KV group ---------------------------------------
+// The product of two f16 values is exact in f32 (22 significant bits) and in
+// double, so the reference's s += (double)(a * b) is fma(a, b, s) with a and
+// b widened to double: one rounding either way, the same bits. Widening each
+// f16 once and sharing it across the query heads of a KV group replaces the
+// per-product f32 -> f64 conversion (the bound of the per-head kernel) by
+// double fmas.
+
+// an f16 value as a double, exactly, with integer operations only
+// (subnormals normalised, infinities and NaNs kept)
+__device__ __forceinline__ double h2d_exact(uint32_t b) {
+    const uint32_t s = (b & 0x8000u) << 16, e = (b >> 10) & 31u, m = b & 1023u;
+    uint32_t hi;
+    if (e == 31u) {
+        hi = s | 0x7ff00000u | (m << 10);
+    } else if (e) {
+        hi = s | ((e + 1008u) << 20) | (m << 10);
+    } else if (m) {
+        const int p = 31 - __clz((int)m);          // leading bit of m, 0..9
+        hi = s | ((uint32_t)(p + 999) << 20) | (((m << (10 - p)) & 1023u) << 10);
+    } else {
+        hi = s;
+    }
+    return __hiloint2double((int)hi, 0);
+}
+
+// softmax_row by one warp (every lane calls; xr and yr may be the same row):
+// the same per-element arithmetic, the row's sum reduced across the lanes and
+// decided (or redone in the reference's order) by lane 0, as softmax_row does
+// across its CTA
+__device__ void softmax_row_warp(const float *xr, float *yr, int n) {
+    const int lane = threadIdx.x & 31;
+    float mx = -__int_as_float(0x7f800000);
+    for (int i = lane; i < n; i += 32) {
+        const float v = xr[i];
+        if (v > mx) mx = v;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float v = __shfl_xor_sync(0xffffffffu, mx, o);
+        if (v > mx) mx = v;
+    }
+    const int ng = n / 8, body = 8 * ng;
+    double s = 0.0;
+    for (int g = lane; g < ng; g += 32) {
+        float v[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) v[k] = expf_ref(__fsub_rn(xr[8 * g + k], mx));
+#pragma unroll
+        for (int k = 0; k < 8; ++k) yr[8 * g + k] = v[k];
+        s += (double)group_sum(v);
+    }
+    for (int i = body + lane; i < n; i += 32) {
+        const float v = expf_libm(__fsub_rn(xr[i], mx));
+        yr[i] = v;
+        s += (double)v;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_down_sync(0xffffffffu, s, o);
+    __syncwarp();
+    float scale = 0.0f;
+    if (lane == 0) {
+        const double nt = (double)(ng + (n - body));
+        const double q = __ddiv_rn(1.0, s);
+        const double w = nt * 0x1p-50 + 0x1p-49;
+        const float lo = __double2float_rn(__dmul_rd(q, 1.0 - w));
+        const float hi = __double2float_rn(__dmul_ru(q, 1.0 + w));
+        scale = lo;
+        if (!(lo == hi)) {
+            double t = 0.0;
+            for (int g = 0; g < ng; ++g) {
+                float v[8];
+#pragma unroll
+                for (int k = 0; k < 8; ++k) v[k] = yr[8 * g + k];
+                t = __dadd_rn(t, (double)group_sum(v));
+            }
+            for (int i = body; i < n; ++i) t = __dadd_rn(t, (double)yr[i]);
+            scale = __double2float_rn(__ddiv_rn(1.0, t));
+        }
+    }
+    scale = __shfl_sync(0xffffffffu, scale, 0);
+    for (int i = lane; i < n; i += 32) yr[i] = __fmul_rn(yr[i], scale);
+    __syncwarp();
+}
+
+constexpr int PA_CHUNK = 64;   // positions whose probabilities are widened at a time
+constexpr int PA_GROUP_SMEM_MAX = 200 * 1024;
+
+// KV head hk = blockIdx.x, token t = blockIdx.y, its G query heads at once
+// (256 threads): the queries rotated, made f16 and widened to double in
+// shared memory; a thread per position, its K row against all G queries
+// (G fma chains, in index order); one warp per head for the softmax;
+// the value dots as fma chains over positions in index order, a thread per
+// (channel, HPT heads). Dynamic shared memory: pa_group_smem.
+template <int G>
+__global__ void __launch_bounds__(256) prompt_attention_group_kernel(const float *q, const uint16_t *kc,
+                                                                     const uint16_t *vc, const float *cs,
+                                                                     const float *sn, int n_head, int hd, int n_rot,
+                                                                     int neox, int n_ctx, int pos0, int ns_max,
+                                                                     float ks, float *out) {
+    extern __shared__ __align__(16) uint8_t sm[];
+    double *qd = reinterpret_cast<double *>(sm);                       // [G][hd]
+    double *pd = qd + G * hd;                                          // [G][PA_CHUNK]
+    float *sc = reinterpret_cast<float *>(pd + G * PA_CHUNK);          // [G][n_score]
+    uint16_t *p16 = reinterpret_cast<uint16_t *>(sc + (size_t)G * ns_max);   // [G][n_score]
+    const int hk = blockIdx.x, t = blockIdx.y, tid = threadIdx.x;
+    const int n_score = pos0 + t + 1;
+    const float *c = cs + (int64_t)t * (n_rot / 2), *s = sn + (int64_t)t * (n_rot / 2);
+    for (int i = tid; i < G * hd; i += blockDim.x) {
+        const int g = i / hd, d = i - g * hd;
+        const float *qrow = q + ((int64_t)t * n_head + hk * G + g) * hd;
+        qd[i] = h2d_exact(f2h(rope_channel(qrow, d, hd, n_rot, neox, c, s)));
+    }
+    __syncthreads();
+    // scores: a position per thread at a time, its K row read 64 halves
+    // (eight 16-byte loads in flight) at a time
+    const uint16_t *kh = kc + (int64_t)hk * n_ctx * hd;
+    const bool kvec = (reinterpret_cast<uintptr_t>(kh) & 15) == 0 && (hd & 7) == 0;
+    for (int j = tid; j < n_score; j += blockDim.x) {
+        const uint16_t *row = kh + (int64_t)j * hd;
+        double a[G];
+#pragma unroll
+        for (int g = 0; g < G; ++g) a[g] = 0.0;
+        for (int d0 = 0; d0 < hd; d0 += 64) {
+            if (kvec && d0 + 64 <= hd) {
+                uint4 xr[8];
+                ld_h64(row + d0, xr);
+#pragma unroll
+                for (int k = 0; k < 64; ++k) {
+                    const double kd = h2d_exact(h_of(xr, k));
+#pragma unroll
+                    for (int g = 0; g < G; ++g) a[g] = __fma_rn(kd, qd[g * hd + d0 + k], a[g]);
+                }
+            } else {
+                for (int d = d0; d < min(hd, d0 + 64); d += 8) {
+                    uint16_t x[8];
+                    ld_h8(row + d, kvec, x);
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) {
+                        const double kd = h2d_exact(x[k]);
+#pragma unroll
+                        for (int g = 0; g < G; ++g) a[g] = __fma_rn(kd, qd[g * hd + d + k], a[g]);
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int g = 0; g < G; ++g) sc[(size_t)g * n_score + j] = __fmul_rn(__double2float_rn(a[g]), ks);
+    }
+    __syncthreads();
+    // softmax and f16 probabilities, one warp per head
+    const int warp = tid >> 5, lane = tid & 31;
+    for (int g = warp; g < G; g += (int)(blockDim.x >> 5)) {
+        float *row = sc + (size_t)g * n_score;
+        softmax_row_warp(row, row, n_score);
+        for (int j = lane; j < n_score; j += 32) p16[(size_t)g * n_score + j] = f2h(row[j]);
+    }
+    // value dots: task (channel cch, heads g0 .. g0 + hpt - 1), hpt the
+    // fewest heads per task that fit hd x ceil(G / hpt) tasks in the CTA
+    // (hd <= blockDim)
+    int hpt = 1;
+    while (hd * ((G + hpt - 1) / hpt) > (int)blockDim.x) ++hpt;
+    const int ngrp = (G + hpt - 1) / hpt;
+    const int cch = tid % hd, g0 = (tid / hd) * hpt;
+    const bool active = tid < hd * ngrp;
+    const uint16_t *vrow = vc + ((int64_t)hk * hd + cch) * n_ctx;
+    const bool vvec = (reinterpret_cast<uintptr_t>(vrow) & 15) == 0;   // j0 is a multiple of 64
+    double acc[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) acc[g] = 0.0;
+    for (int j0 = 0; j0 < n_score; j0 += PA_CHUNK) {
+        const int jn = min(PA_CHUNK, n_score - j0);
+        // a whole chunk of the V row in flight across the barriers below
+        const bool full = active && vvec && jn == PA_CHUNK;
+        uint4 xv[8];
+        if (full) ld_h64(vrow + j0, xv);
+        __syncthreads();   // the probabilities written; the previous chunk consumed
+        for (int i = tid; i < G * PA_CHUNK; i += blockDim.x) {
+            const int g = i / PA_CHUNK, jj = i - g * PA_CHUNK;
+            pd[i] = jj < jn ? h2d_exact(p16[(size_t)g * n_score + j0 + jj]) : 0.0;
+        }
+        __syncthreads();
+        if (full) {
+#pragma unroll
+            for (int k = 0; k < PA_CHUNK; ++k) {
+                const double vd = h2d_exact(h_of(xv, k));
+#pragma unroll
+                for (int hh = 0; hh < G; ++hh)
+                    if (hh < hpt && g0 + hh < G) acc[hh] = __fma_rn(vd, pd[(g0 + hh) * PA_CHUNK + k], acc[hh]);
+            }
+        } else if (active) {
+            const uint16_t *r = vrow + j0;
+            for (int jj = 0; jj < jn; jj += 8) {
+                uint16_t x[8];
+                if (jj + 8 <= jn) {
+                    ld_h8(r + jj, vvec, x);
+                } else {
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) x[k] = jj + k < jn ? r[jj + k] : (uint16_t)0;
+                }
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                    if (jj + k < jn) {
+                        const double vd = h2d_exact(x[k]);
+#pragma unroll
+                        for (int hh = 0; hh < G; ++hh)
+                            if (hh < hpt && g0 + hh < G)
+                                acc[hh] = __fma_rn(vd, pd[(g0 + hh) * PA_CHUNK + jj + k], acc[hh]);
+                    }
+                }
+            }
+        }
+    }
+    if (active) {
+#pragma unroll
+        for (int hh = 0; hh < G; ++hh)
+            if (hh < hpt && g0 + hh < G)
+                out[((int64_t)t * n_head + hk * G + g0 + hh) * hd + cch] = __double2float_rn(acc[hh]);
+    }
+}
+
+// dynamic shared memory of prompt_attention_group_kernel for G heads of hd
+// channels and at most ns_max positions
+size_t pa_group_smem(int G, int hd, int ns_max) {
+    return (size_t)G * hd * 8 + (size_t)G * PA_CHUNK * 8 + (size_t)G * ns_max * 6 + 16;
+}
+
+template <int G>
+int launch_pa_group(const float *q, const uint16_t *kc, const uint16_t *vc, const float *cs, const float *sn,
+                    int n_head, int n_head_kv, int hd, int n_rot, int neox, int n_ctx, int pos0, int m, float ks,
+                    float *out, size_t smem, cudaStream_t st) {
+    static bool attr[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!attr[dev & 63]) {
+        if (cudaFuncSetAttribute(prompt_attention_group_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 PA_GROUP_SMEM_MAX) != cudaSuccess)
+            return -2;
+        attr[dev & 63] = true;
+    }
+    prompt_attention_group_kernel<G><<<dim3((unsigned)n_head_kv, (unsigned)m), 256, smem, st>>>(
+        q, kc, vc, cs, sn, n_head, hd, n_rot, neox, n_ctx, pos0, pos0 + m, ks, out);
+    return cudaPeekAtLastError() == cudaSuccess ? 0 : -2;
+}
+
 }  // namespace
 
 int launch_attention(const float *q, const void *kc, const void *vc, int n_head, int n_head_kv, int hd, int n_ctx,
@@ -609,6 +854,23 @@ int launch_attention(const float *q, const void *kc, const void *vc, int n_head,
 int launch_attention_prompt(const float *q, const float *k, const float *v, void *kc, void *vc, const float *cs,
                             const float *sn, int n_head, int n_head_kv, int hd, int n_rot, int neox, int n_ctx, int pos0,
                             int m, float ks, float *out, cudaStream_t st) {
+    const int gqa = n_head / n_head_kv;
+    const size_t gsmem = pa_group_smem(gqa, hd, pos0 + m);
+    if (gqa <= 8 && hd <= 256 && hd % 8 == 0 && gsmem <= (size_t)PA_GROUP_SMEM_MAX) {
+        prompt_kv_store_kernel<<<(unsigned)m, 256, 0, st>>>(k, v, static_cast<uint16_t *>(kc),
+                                                             static_cast<uint16_t *>(vc), cs, sn, n_head_kv, hd, n_rot,
+                                                             neox, n_ctx, pos0);
+        if (cudaPeekAtLastError() != cudaSuccess) return -2;
+        const uint16_t *kcc = static_cast<const uint16_t *>(kc), *vcc = static_cast<const uint16_t *>(vc);
+        switch (gqa) {
+#define PA_G(G)                                                                                                        \
+    case G:                                                                                                            \
+        return launch_pa_group<G>(q, kcc, vcc, cs, sn, n_head, n_head_kv, hd, n_rot, neox, n_ctx, pos0, m, ks, out,   \
+                                  gsmem, st);
+            PA_G(1) PA_G(2) PA_G(3) PA_G(4) PA_G(5) PA_G(6) PA_G(7) PA_G(8)
+#undef PA_G
+        }
+    }
     static bool attr[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);

@@ -122,15 +122,25 @@ def test_attention_exactness_bound_and_fallback(sicu, oracle, case):
     assert_bits_equal(host(out), oracle.attention(q, k, v, n_head, nkv, hd, n_ctx, pos, ks), case)
 
 
-@pytest.mark.parametrize("neox,n_rot,pos0,m", [(False, 128, 0, 37), (True, 128, 20, 44), (False, 64, 5, 1)])
-def test_attention_prompt_equals_token_steps(sicu, oracle, neox, n_rot, pos0, m):
+@pytest.mark.parametrize("n_head,nkv,hd,n_ctx,neox,n_rot,pos0,m", [
+    (8, 2, 128, 96, False, 128, 0, 37),     # 4 heads per KV head
+    (8, 2, 128, 96, True, 128, 20, 44),
+    (8, 2, 128, 96, False, 64, 5, 1),       # partial rotation, one token
+    (32, 4, 64, 160, False, 64, 3, 70),     # TinyLlama's groups of 8
+    (10, 2, 128, 100, True, 128, 7, 40),    # groups of 5; V rows not 16-byte aligned
+    (4, 4, 64, 64, False, 64, 0, 33),       # no grouping
+    (16, 2, 96, 80, False, 96, 1, 30),      # head 96: 4 heads per value task
+    (16, 1, 64, 64, False, 64, 2, 20),      # 16 per KV head: the per-head kernel
+])
+def test_attention_prompt_equals_token_steps(sicu, oracle, n_head, nkv, hd, n_ctx, neox, n_rot, pos0, m):
     """sicu_attention_prompt (m consecutive positions in one call) against m
     sicu_attention_step calls, the engine's token-serial order: the same
     outputs and caches, bit for bit; the last token's heads also against the
-    oracle's attention over the final caches."""
+    oracle's attention over the final caches. Up to 8 query heads per KV head
+    run in the grouped kernel (fma chains over widened f16 values), more in
+    the per-head one."""
     import torch
     rng = np.random.default_rng(pos0 * 100 + m)
-    n_head, nkv, hd, n_ctx = 8, 2, 128, 96
     k0, v0 = random_cache(rng, nkv, hd, n_ctx)
     theta = rng.uniform(-20, 20, (m, n_rot // 2))
     c = np.cos(theta).astype(np.float32)

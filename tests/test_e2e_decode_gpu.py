@@ -283,6 +283,54 @@ def test_prompt_in_one_pass_k_formats_small(sicu, small):
 
 
 def test_prompt_in_one_pass_k_formats_tinyllama(sicu, tinyllama):
-    """configs[2] shape: the 32-token prompt in one pass, within twice the
-    reference's own dispatch-to-dispatch spread at this shape."""
-    _prompt_vs_reference(sicu, tinyllama, 1.25e-1)
+    """configs[2] shape: the 32-token prompt in one pass, within about three
+    times the reference's own dispatch-to-dispatch spread at this shape."""
+    _prompt_vs_reference(sicu, tinyllama, 2e-1)
+
+
+def _chunked_prompt_then_decode(sicu, model, chunk):
+    """The prompt through prompt_step in chunks of `chunk` tokens (positions
+    0, chunk, 2 chunk, ...: each chunk's attention reads the caches the
+    earlier chunks left), then the greedy decode on the device. With at most
+    8 tokens per chunk the K-format products take the batch kernel, which is
+    bit-identical to the per-token matvec, so every logit of the prompt and
+    of the 128 decode steps must equal the reference engine's token-serial
+    run bit for bit."""
+    import torch
+    from siphon_b200 import model_path as mp
+    path, sh, ref = model
+    m = mp.MatrixPath(sicu, sh, torch.device("cuda", 0), embed=True, n_ctx=N_CTX, gguf_path=path,
+                      max_tokens=chunk, packed=True)
+    stream = torch.cuda.Stream()
+    try:
+        for p0 in range(0, N_PROMPT, chunk):
+            n = min(chunk, N_PROMPT - p0)
+            m.tokens[:n].copy_(torch.tensor(ref["prompt"][p0:p0 + n], dtype=torch.int64))
+            m.pos = p0
+            with torch.cuda.stream(stream):
+                m.prompt_step(stream, n)
+            torch.cuda.synchronize()
+            got = m.y["head"][:n].cpu().numpy()
+            for i in range(n):
+                assert_bits_equal(got[i], ref["logits"][p0 + i], f"prompt logits of token {p0 + i}")
+        for step in range(N_PROMPT, N_PROMPT + N_GEN):
+            assert int(m.token.cpu()[0]) == ref["greedy"][step - 1]
+            m.pos = step
+            with torch.cuda.stream(stream):
+                m.decode_step(stream)
+            torch.cuda.synchronize()
+            assert_bits_equal(m.y["head"][0].cpu().numpy(), ref["logits"][step], f"logits at step {step}")
+        assert int(m.token.cpu()[0]) == ref["greedy"][-1]
+        assert sicu.status() == 0
+    finally:
+        m.close()
+
+
+def test_prompt_in_chunks_of_8_small_bit_exact(sicu, small):
+    _chunked_prompt_then_decode(sicu, small, 8)
+
+
+def test_prompt_in_chunks_of_8_tinyllama_bit_exact(sicu, tinyllama):
+    """configs[2] shape: the 32-token prompt as four 8-token passes, then 128
+    greedy tokens, every logit bit-identical to the reference engine."""
+    _chunked_prompt_then_decode(sicu, tinyllama, 8)

@@ -407,6 +407,11 @@ SICU_API int sicu_gemv_fused_ex(uint32_t wtype, int n_mats, const void *const *d
 SICU_API int sicu_rms_norm(const float *dx, const float *dres, float *dsum, const float *dw, int64_t n, int64_t m,
                            float eps, float *dy, void *stream);
 SICU_API int sicu_swiglu(const float *dx, const float *dup, int64_t n, int64_t m, float *dy, void *stream);
+/* dy_r += db for m rows of n floats, in place: the Q/K/V bias adds of
+ * Qwen2-architecture models (src/engine.c:319-333, one f32 addition per
+ * element) for a prompt's rows; a single token's adds ride in the QKV
+ * product's epilogue (sicu_gemv_fused_ex). */
+SICU_API int sicu_add_bias(float *dy, const float *db, int64_t n, int64_t m, void *stream);
 
 /* ---- attention softmax ------------------------------------------------------
  * dy_r = softmax(dx_r) for m rows of n floats, as the reference's attention

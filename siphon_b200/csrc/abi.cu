@@ -1082,6 +1082,19 @@ int sicu_rms_norm(const float *dx, const float *dres, float *dsum, const float *
     return SICU_OK;
 }
 
+int sicu_add_bias(float *dy, const float *db, int64_t n, int64_t m, void *stream) {
+    if (n <= 0 || m < 0 || n > INT64_MAX / (m > 0 ? m : 1))
+        return fail(SICU_EINVAL, "add bias: bad shape n=%lld m=%lld", (long long)n, (long long)m);
+    if (!dy || !db) return fail(SICU_EINVAL, "add bias: null pointer");
+    if (!aligned(dy, 4) || !aligned(db, 4)) return fail(SICU_EINVAL, "add bias: rows must be 4-byte aligned");
+    if (overlaps(dy, db, 4 * n * m, 4 * n)) return fail(SICU_EINVAL, "add bias: bias overlaps the rows");
+    DevState *ds;
+    if (int rc = current(ds)) return rc;
+    if (m == 0) return SICU_OK;
+    if (launch_add_rows(dy, db, n, m, (cudaStream_t)stream)) return cuda_fail(cudaGetLastError(), "add bias launch");
+    return SICU_OK;
+}
+
 int sicu_swiglu(const float *dx, const float *dup, int64_t n, int64_t m, float *dy, void *stream) {
     if (n <= 0 || m < 0) return fail(SICU_EINVAL, "swiglu: bad shape n=%lld m=%lld", (long long)n, (long long)m);
     if (!dx || !dy) return fail(SICU_EINVAL, "swiglu: null pointer");

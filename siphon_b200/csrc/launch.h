@@ -174,6 +174,8 @@ int launch_mul(const float *x, const float *up, int64_t n, float *y, cudaStream_
 int launch_silu_inplace(float *y, int64_t n, cudaStream_t st);
 // y += b, n floats in place (F16 products with a bias epilogue)
 int launch_add_inplace(float *y, const float *b, int64_t n, cudaStream_t st);
+// y_r += b for m rows of n floats (the Q/K/V bias adds of a prompt)
+int launch_add_rows(float *y, const float *b, int64_t n, int64_t m, cudaStream_t st);
 
 // the reference's attention softmax over m rows of n floats (row maximum
 // taken here); in place allowed

@@ -39,6 +39,12 @@ __global__ void __launch_bounds__(256) add_kernel(float *y, const float *b, int6
         y[i] = __fadd_rn(y[i], b[i]);
 }
 
+// y_r += b for m rows of n floats: y[i] + b[i mod n], one f32 addition each
+__global__ void __launch_bounds__(256) add_rows_kernel(float *y, const float *b, int64_t n, int64_t total) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x)
+        y[i] = __fadd_rn(y[i], b[i % n]);
+}
+
 __global__ void __launch_bounds__(256) silu_kernel(float *y, int64_t n) {
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
         y[i] = silu_ref(y[i]);
@@ -76,6 +82,12 @@ int launch_mul(const float *x, const float *up, int64_t n, float *y, cudaStream_
 int launch_add_inplace(float *y, const float *b, int64_t n, cudaStream_t st) {
     if (n <= 0) return 0;
     add_kernel<<<grid_for(n), 256, 0, st>>>(y, b, n);
+    return cudaPeekAtLastError() == cudaSuccess ? 0 : -2;
+}
+
+int launch_add_rows(float *y, const float *b, int64_t n, int64_t m, cudaStream_t st) {
+    if (n <= 0 || m <= 0) return 0;
+    add_rows_kernel<<<grid_for(n * m), 256, 0, st>>>(y, b, n, n * m);
     return cudaPeekAtLastError() == cudaSuccess ? 0 : -2;
 }
 

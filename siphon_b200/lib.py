@@ -72,6 +72,7 @@ SIGNATURES = {
                            C.POINTER(C.c_void_p), C.POINTER(C.c_void_p), _vp, _vp],
     "sicu_rms_norm": [_fp, _fp, _fp, _fp, _i64, _i64, C.c_float, _fp, _vp],
     "sicu_swiglu": [_fp, _fp, _i64, _i64, _fp, _vp],
+    "sicu_add_bias": [_fp, _fp, _i64, _i64, _vp],
     "sicu_softmax": [_fp, _fp, _i64, _i64, _vp],
     "sicu_rope": [_fp, _i64, _i64, _i64, _fp, _fp, C.c_int, _vp],
     "sicu_kv_store": [_fp, _fp, _vp, _vp, _i64, _i64, _i64, _i64, _vp],
@@ -298,6 +299,10 @@ class SiphonCuda:
 
     def swiglu(self, dx, dup, n: int, m: int, dy, stream=None) -> None:
         self.check(self.lib.sicu_swiglu(_ptr(dx), _ptr(dup), n, m, _ptr(dy), _ptr(stream)))
+
+    def add_bias(self, dy, db, n: int, m: int, stream=None) -> None:
+        """sicu_add_bias: dy_r += db for m rows of n floats."""
+        self.check(self.lib.sicu_add_bias(_ptr(dy), _ptr(db), n, m, _ptr(stream)))
 
     def softmax(self, dx, dy, n: int, m: int = 1, stream=None) -> None:
         """sicu_softmax: the reference's attention softmax over m rows."""

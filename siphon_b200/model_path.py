@@ -565,7 +565,8 @@ class MatrixPath:
         positions self.pos .. self.pos + m - 1, all tokens at once, in the
         reference's per-token order of steps (src/engine.c:290-398):
         embedding rows; per layer h += (previous W_down output) and its RMS
-        norm, Wq/Wk/Wv, RoPE + cache stores + each token's attention over
+        norm, Wq/Wk/Wv (and the Q/K/V bias adds of Qwen2 models), RoPE +
+        cache stores + each token's attention over
         positions 0 .. its own, Wo, h += Wo output and its RMS norm,
         W_gate/W_up, SwiGLU, W_down; the output norm and the head's logits of
         every token (y["head"][:m]); the greedy choice after the last token
@@ -576,8 +577,6 @@ class MatrixPath:
         the number of library calls."""
         if not (self.embed and hasattr(self, "tokens")):
             raise ValueError("prompt_step needs MatrixPath(embed=True, max_tokens > 1)")
-        if self.bias is not None:
-            raise ValueError("prompt_step: Q/K/V biases (Qwen2) are not supported")
         if not 0 < m <= self.tokens.numel() or self.pos + m > self.n_ctx:
             raise ValueError(f"prompt of {m} tokens at position {self.pos}: past the buffers or the context")
         s, h, y, d, eps = self.s, stream.cuda_stream, self.y, self.sh.n_embd, self.sh.rms_eps
@@ -593,6 +592,12 @@ class MatrixPath:
                 s.rms_norm(xp[cur], self.attn_norm[il], d, m, eps, xn, dres=res, dsum=xp[nxt], stream=h)
                 cur, nxt = nxt, cur
             n += 1 + self._prompt_products(il, ("q", "k", "v"), d, xn, m, h)
+            if self.bias is not None:
+                # Qwen2: the Q/K/V bias adds over the m rows (src/engine.c:319-333)
+                b = self.bias[il]
+                for name, width in (("q", nq), ("k", nkv), ("v", nkv)):
+                    s.add_bias(y[name], b[name], width, m, stream=h)
+                n += 3
             s.attention_prompt(y["q"], y["k"], y["v"], self.kc[il], self.vc[il], self.rope_cos[p:],
                                self.rope_sin[p:], nq // hd, nkv // hd, hd, hd, self.n_ctx, p, m, self.kq_scale,
                                self.att, neox=self.sh.neox, stream=h)

@@ -221,3 +221,13 @@ def test_attention_prompt_checks_run_on_host(so):
     assert call(ptr=None) == L.SICU_EINVAL
     assert call(cache=p + 1) == L.SICU_EINVAL                # caches not 2-byte aligned
     assert call(n_ctx=40000, pos0=29000, m=1001) == L.SICU_EINVAL   # more than 30000 positions
+
+
+def test_add_bias_checks_run_on_host(so):
+    f = so.lib.sicu_add_bias
+    p = 0x10000
+    assert f(p, p + 0x8000, 0, 4, None) == L.SICU_EINVAL          # no columns
+    assert f(p, p + 0x8000, 16, -1, None) == L.SICU_EINVAL
+    assert f(None, p, 16, 4, None) == L.SICU_EINVAL
+    assert f(p + 2, p + 0x8000, 16, 4, None) == L.SICU_EINVAL     # rows misaligned
+    assert f(p, p + 64, 16, 4, None) == L.SICU_EINVAL             # bias inside the rows

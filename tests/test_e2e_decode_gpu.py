@@ -330,6 +330,12 @@ def test_prompt_in_chunks_of_8_small_bit_exact(sicu, small):
     _chunked_prompt_then_decode(sicu, small, 8)
 
 
+def test_prompt_in_chunks_of_8_qwen2_bit_exact(sicu, small_qwen):
+    """Qwen2 architecture: the Q/K/V bias adds over the prompt's rows
+    (sicu_add_bias) and the half-split RoPE of the prompt attention."""
+    _chunked_prompt_then_decode(sicu, small_qwen, 8)
+
+
 def test_prompt_in_chunks_of_8_tinyllama_bit_exact(sicu, tinyllama):
     """configs[2] shape: the 32-token prompt as four 8-token passes, then 128
     greedy tokens, every logit bit-identical to the reference engine."""

@@ -280,3 +280,22 @@ def test_gemv_fused_bias_epilogue(sicu, oracle, wt):
         if i == 2:
             want = oracle.silu_vec(want)
         assert_bits_equal(host(ys[i]), want, f"{Q.NAMES[wt]} bias matrix {i}")
+
+
+def test_add_bias_rows(sicu):
+    """sicu_add_bias: m rows plus one bias row, one f32 addition per element
+    (the reference's q[i] + bq[i], src/engine.c:319-333), for a prompt's
+    Q/K/V rows; rows of odd widths, one row, and signed zeros."""
+    import torch
+    rng = np.random.default_rng(44)
+    for n, m in ((1000, 7), (256, 1), (5120, 33)):
+        y = (rng.standard_normal((m, n)) * 3).astype(np.float32)
+        b = (0.02 * rng.standard_normal(n)).astype(np.float32)
+        y[0, :4] = [0.0, -0.0, 0.0, -0.0]
+        b[:4] = [-0.0, -0.0, 0.0, 0.0]
+        dy = dev(y)
+        sicu.add_bias(dy, dev(b), n, m)
+        assert_bits_equal(host(dy), (y + b[None, :]).astype(np.float32), f"{m} rows of {n}")
+    d = torch.zeros(8, device="cuda")
+    with pytest.raises(SicuError):
+        sicu.add_bias(d, d[4:], 4, 2)        # the bias inside the rows

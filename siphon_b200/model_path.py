@@ -27,11 +27,14 @@ the products the way the reference's forward pass does (engine.c:313-315,
 W_gate/W_up and before the output head, SwiGLU split into a silu epilogue on
 W_gate's output and a multiply in W_down's prologue, and for Qwen2-shaped
 models the Q/K/V bias adds as the QKV products' epilogue (engine.c:320-334). The
-residual stream starts from a fixed embedding row. Attention and RoPE are not
-part of this path: Wo reads a fixed activation in place of the attention
-output. Without ``steps`` each product reads a fixed activation buffer of its
-input length, so a step is the matrix work of one token (or one prompt) and
-nothing else.
+residual stream starts from a fixed embedding row, and Wo reads a fixed
+activation in place of the attention output. ``attention=True`` adds RoPE,
+the f16 KV-cache store and the heads' attention (sicu_attention_step, one
+launch per layer), and ``embed=True`` the embedding lookup from a token id in
+device memory and the greedy choice after the head: every step of the
+reference's forward pass on the device. Without ``steps`` each product reads
+a fixed activation buffer of its input length, so a step is the matrix work
+of one token (or one prompt) and nothing else.
 
 Tensor parallelism (``world > 1``) follows the layout the 32B-class configs
 name: Wq/Wk/Wv, W_gate/W_up and the output head are split by output rows

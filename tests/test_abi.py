@@ -231,3 +231,17 @@ def test_add_bias_checks_run_on_host(so):
     assert f(None, p, 16, 4, None) == L.SICU_EINVAL
     assert f(p + 2, p + 0x8000, 16, 4, None) == L.SICU_EINVAL     # rows misaligned
     assert f(p, p + 64, 16, 4, None) == L.SICU_EINVAL             # bias inside the rows
+
+
+def test_model_path_packs_what_the_library_accepts(so):
+    """model_path.packable (which matrices get a prefill copy at load) agrees
+    with sicu_prefill_pack_bytes for every type and a spread of row lengths."""
+    from siphon_b200 import model_path as mp
+    for wt in Q.WEIGHT_TYPES + (Q.F32,):
+        blk = Q.GEOMETRY[wt][0]
+        for n_in in (32, 64, 96, 128, 160, 256, 512, 640, 4096, 5120):
+            if n_in % blk:
+                continue                      # not a whole row of blocks: no model matrix
+            n = C.c_size_t(0)
+            ok = so.lib.sicu_prefill_pack_bytes(wt, n_in, 256, C.byref(n)) == 0
+            assert ok == mp.packable(wt, n_in), (Q.NAMES[wt], n_in, ok)
